@@ -1,0 +1,230 @@
+/*
+ * woodcock_b200: C ABI of the B200-native speculative-decoding round.
+ *
+ * Drop-in boundary for the reference's C++ core (AtomicBot-ai/woodcock,
+ * include/woodcock/{ops,cache,model,drafter,sampling,spec}.h) and for its Python
+ * API (python/woodcock/{target,drafter,sampling,spec}.py). Every entry point is
+ * plain C: opaque handles, device or host pointers, sizes and a status code.
+ *
+ * Conventions
+ *  - One context per GPU; a context is not thread-safe. All work is enqueued on
+ *    the context's stream (set by wc_ctx_create / wc_ctx_set_stream).
+ *  - Activation buffers ("_dev" pointers) are caller-owned device memory, row-major
+ *    as in the reference (x[L][d], q[L][H][D], K/V[T][Hk][D], mask[L][T], 1 = visible).
+ *  - The library owns weights, KV arenas and workspaces behind its handles.
+ *  - No function aborts or throws: each returns wc_status; wc_last_error(ctx)
+ *    describes the most recent failure. Device-side failures (bounds, timeouts)
+ *    are raised through a device error word checked at the round's sync.
+ *  - dtype codes: WC_F32 = 0, WC_BF16 = 1.
+ */
+#ifndef WOODCOCK_B200_H_
+#define WOODCOCK_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define WC_API __attribute__((visibility("default")))
+#else
+#define WC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum {
+  WC_OK = 0,
+  WC_ERR_INVALID = 1,     /* bad argument: shape, dtype, token id, tap index, tree */
+  WC_ERR_IO = 2,          /* file missing / unreadable / malformed safetensors or JSON */
+  WC_ERR_CUDA = 3,        /* a CUDA runtime call failed */
+  WC_ERR_OOM = 4,         /* device allocation failed */
+  WC_ERR_CAPACITY = 5,    /* KV arena or workspace capacity exceeded */
+  WC_ERR_DEVICE = 6,      /* device-side error flag raised (bounds, bounded wait expired) */
+  WC_ERR_UNSUPPORTED = 7  /* configuration the reference also rejects, or not built yet */
+} wc_status;
+
+enum { WC_F32 = 0, WC_BF16 = 1 };
+
+typedef struct wc_ctx wc_ctx;
+typedef struct wc_weight wc_weight;
+typedef struct wc_kv wc_kv;
+typedef struct wc_target wc_target;
+typedef struct wc_drafter wc_drafter;
+typedef struct wc_decoder wc_decoder;
+
+/* ------------------------------------------------------------------ context */
+WC_API wc_status wc_ctx_create(int device, void* stream, wc_ctx** out);
+WC_API wc_status wc_ctx_set_stream(wc_ctx* ctx, void* stream);
+WC_API void wc_ctx_destroy(wc_ctx* ctx);
+WC_API const char* wc_last_error(const wc_ctx* ctx);
+WC_API wc_status wc_ctx_synchronize(wc_ctx* ctx);
+/* number of kernels this context launched since creation (graph replays count each kernel) */
+WC_API uint64_t wc_ctx_launch_count(const wc_ctx* ctx);
+
+/* ------------------------------------------------------------------ backend ops
+ * Device-pointer counterparts of woodcock::ops (include/woodcock/ops.h:11-22,
+ * src/backends/cpu_ops.cpp:45-115). A wc_weight replaces woodcock::Tensor
+ * (include/woodcock/weights.h:14-24): the library keeps it in its streaming layout. */
+
+/* W[out][in] row-major from `data` (host or device, src_dtype WC_F32/WC_BF16) stored as `dtype`. */
+WC_API wc_status wc_weight_create(wc_ctx* ctx, const void* data, int src_dtype, int data_on_device, int out_rows,
+                           int in_cols, int dtype, wc_weight** w);
+WC_API void wc_weight_destroy(wc_weight* w);
+/* ops.h:12  y[L][out] (+)= x[L][in] . W^T */
+WC_API wc_status wc_linear(wc_ctx* ctx, const float* x_dev, int L, int in, const wc_weight* W, float* y_dev, int accumulate);
+/* ops.h:14  y = x * rsqrt(mean(x^2) + eps) * w per row of length d; x and y may alias */
+WC_API wc_status wc_rmsnorm(wc_ctx* ctx, const float* x_dev, float* y_dev, int rows, int d, const float* w_dev, float eps);
+/* ops.h:16  rotate-half RoPE on x[L][heads][D] at positions[L] (device) */
+WC_API wc_status wc_rope(wc_ctx* ctx, float* x_dev, int L, int heads, int D, const int* positions_dev, float base);
+/* ops.h:18  gate = silu(gate) * up */
+WC_API wc_status wc_silu_mul(wc_ctx* ctx, float* gate_dev, const float* up_dev, int64_t n);
+/* ops.h:20  q[L][H][D]; K,V [T][Hk][D] of kv_dtype; mask[L][T] or NULL; out[L][H][D] */
+WC_API wc_status wc_attention(wc_ctx* ctx, const float* q_dev, int L, int H, int Hk, int D, const void* K_dev,
+                       const void* V_dev, int kv_dtype, int T, const uint8_t* mask_dev, float* out_dev, float scale);
+/* ops.h:22  in-place softmax of one row of n */
+WC_API wc_status wc_softmax(wc_ctx* ctx, float* x_dev, int n);
+/* first index of the maximum of each of `rows` rows of n (sampling.cpp:47) */
+WC_API wc_status wc_argmax_rows(wc_ctx* ctx, const float* x_dev, int rows, int n, int* out_dev);
+
+/* ------------------------------------------------------------------ KV cache
+ * include/woodcock/cache.h:9-28. Fixed capacity (no reallocation: rounds are
+ * graph-replayed); layout [layer][kv_head][capacity][head_dim] of `dtype`. */
+WC_API wc_status wc_kv_create(wc_ctx* ctx, int layers, int kv_heads, int head_dim, int capacity, int dtype, wc_kv** kv);
+WC_API void wc_kv_destroy(wc_kv* kv);
+WC_API int wc_kv_size(const wc_kv* kv);
+WC_API int wc_kv_capacity(const wc_kv* kv);
+/* cache.h:16  k, v: [L][kv_heads][head_dim] fp32 device rows, written at [size, size+L) of `layer` */
+WC_API wc_status wc_kv_append(wc_kv* kv, int layer, const float* k_dev, const float* v_dev, int L);
+WC_API wc_status wc_kv_commit(wc_kv* kv, int L);   /* cache.h:17 */
+WC_API wc_status wc_kv_trim_to(wc_kv* kv, int n);  /* cache.h:18 */
+/* cache.h:20  keep rows start+keep[i] contiguously at start+i (keep: host array, increasing) */
+WC_API wc_status wc_kv_compact(wc_kv* kv, int start, const int* keep, int n_keep);
+/* copy rows [0, T) of one layer out as [T][kv_heads][head_dim] fp32 (device) */
+WC_API wc_status wc_kv_read(const wc_kv* kv, int layer, int T, float* k_dev, float* v_dev);
+
+/* ------------------------------------------------------------------ target (Qwen3)
+ * include/woodcock/model.h:27-52; python/woodcock/target.py:42-116. */
+typedef struct {
+  int hidden, layers, heads, kv_heads, head_dim, intermediate, vocab;
+  float eps, rope_theta;
+  int tie_embeddings;
+} wc_qwen3_config;
+
+/* Loads HF config.json + *.safetensors from `dir`. taps: 3 block indices, or NULL for
+ * the reference default (2, L/2, L-3) (src/core/qwen3.cpp:57). dtype: storage/compute dtype. */
+WC_API wc_status wc_target_load(wc_ctx* ctx, const char* dir, const int* taps, int dtype, wc_target** out);
+/* Empty target of `cfg`; fill with wc_target_set_tensor (HF tensor names), then wc_target_finalize. */
+WC_API wc_status wc_target_create(wc_ctx* ctx, const wc_qwen3_config* cfg, const int* taps, int dtype, wc_target** out);
+WC_API wc_status wc_target_set_tensor(wc_target* t, const char* name, const void* data, int src_dtype, int on_device,
+                               const int64_t* shape, int ndim);
+WC_API wc_status wc_target_finalize(wc_target* t);
+WC_API void wc_target_destroy(wc_target* t);
+WC_API wc_status wc_target_config(const wc_target* t, wc_qwen3_config* cfg, int* taps3, int* dtype);
+/* KV cache shaped for this target (Qwen3::make_cache, model.h:38) */
+WC_API wc_status wc_target_make_cache(wc_target* t, int capacity, wc_kv** kv);
+/* model.h:37 Qwen3::forward. tokens[L] and positions[L] (NULL = cache size + i) are device
+ * int32; mask_dev is [L][size+L] uint8 or NULL (causal). Outputs (each optional, device):
+ * logits [L-logits_from][vocab] fp32, argmax [L-logits_from] int32, taps [3][L][hidden] fp32. */
+WC_API wc_status wc_target_forward(wc_target* t, wc_kv* cache, const int* tokens_dev, int L, const int* positions_dev,
+                            const uint8_t* mask_dev, int logits_from, float* logits_dev, int* argmax_dev,
+                            float* taps_dev);
+
+/* ------------------------------------------------------------------ drafter (EAGLE-3)
+ * include/woodcock/drafter.h:31-58; python/woodcock/drafter.py:134-229. */
+typedef struct {
+  int hidden, layers, heads, kv_heads, head_dim, intermediate, vocab, target_hidden, num_features;
+  float eps, rope_theta;
+  int post_norm, feature_norm, window;
+} wc_drafter_config;
+
+/* config.json + model.safetensors (drafter.cpp:18-73). Rejects what the reference rejects. */
+WC_API wc_status wc_drafter_load(wc_ctx* ctx, const char* dir, int dtype, wc_drafter** out);
+WC_API wc_status wc_drafter_create(wc_ctx* ctx, const wc_drafter_config* cfg, int dtype, wc_drafter** out);
+WC_API wc_status wc_drafter_set_tensor(wc_drafter* d, const char* name, const void* data, int src_dtype, int on_device,
+                                const int64_t* shape, int ndim);
+WC_API wc_status wc_drafter_finalize(wc_drafter* d);
+WC_API void wc_drafter_destroy(wc_drafter* d);
+WC_API wc_status wc_drafter_config_get(const wc_drafter* d, wc_drafter_config* cfg, int* dtype, int* head_rows);
+/* drafter.py:217-229 restrict_vocab: keep head rows ids[0..n) (host int32, ascending not required) */
+WC_API wc_status wc_drafter_restrict_vocab(wc_drafter* d, const int* ids, int n);
+WC_API wc_status wc_drafter_make_cache(wc_drafter* d, int capacity, wc_kv** kv);
+/* drafter.h:41 fuse: taps [num_features][L][target_hidden] -> g [L][hidden] (device fp32) */
+WC_API wc_status wc_drafter_fuse(wc_drafter* d, const float* taps_dev, int L, float* g_dev);
+/* drafter.h:43 forward: tokens[L], feat [L][hidden]; positions/mask as for the target.
+ * hidden_dev (un-normalised residual) and out_dev (RMSNorm(h)) are [L][hidden], each optional. */
+WC_API wc_status wc_drafter_forward(wc_drafter* d, wc_kv* cache, const int* tokens_dev, int L, const float* feat_dev,
+                             const int* positions_dev, const uint8_t* mask_dev, float* hidden_dev, float* out_dev);
+/* drafter.h:49 logits over the head rows (full vocabulary or the restricted rows) for `rows` rows */
+WC_API wc_status wc_drafter_logits(wc_drafter* d, const float* out_dev, int rows, float* z_dev);
+/* fused head + argmax; token ids are mapped back through the restricted vocabulary (drafter.py:213-215) */
+WC_API wc_status wc_drafter_head_argmax(wc_drafter* d, const float* out_dev, int rows, int* token_dev);
+
+/* ------------------------------------------------------------------ acceptance
+ * python/woodcock/sampling.py:60-177; src/sampling/sampling.cpp:85-141. Trees are
+ * flattened: parents[0] = -1, children in node order = draw order. */
+/* sampling.cpp:95-106 verify_tree_greedy on device: argmax[N], tokens[N], parents[N] device int32.
+ * out_path [N] (accepted node ids, excluding the root), out_n, out_next: device int32. */
+WC_API wc_status wc_accept_greedy(wc_ctx* ctx, const int* argmax_dev, const int* tokens_dev, const int* parents_dev, int N,
+                           int* out_path_dev, int* out_n_dev, int* out_next_dev);
+/* sampling.py:143-177 verify_tree_stochastic on device. p_dev [N][V] target probabilities, q_dev [N][V] draft
+ * distributions each node's children were drawn from (rows of leaves unused), fp64. Uniforms are the
+ * Philox4x32-10 stream (seed, counter offset): one per tested child with q > 0, one per final draw.
+ * out_used_dev receives the number of uniforms consumed. */
+WC_API wc_status wc_accept_stochastic(wc_ctx* ctx, const double* p_dev, const double* q_dev, int V, const int* tokens_dev,
+                               const int* parents_dev, int N, uint64_t seed, uint64_t offset, int* out_path_dev,
+                               int* out_n_dev, int* out_next_dev, int* out_used_dev);
+/* fp64 uniforms of the Philox stream, for the host side of tests and for draft sampling */
+WC_API wc_status wc_philox_uniforms(wc_ctx* ctx, uint64_t seed, uint64_t offset, int n, double* out_dev);
+
+/* ------------------------------------------------------------------ speculative decoder
+ * include/woodcock/spec.h:56-78; python/woodcock/spec.py:104-374. The round runs on the
+ * device from one CUDA graph per (mode, k): draft chain, verification, acceptance,
+ * KV compaction and the drafter update, with one host synchronisation. */
+typedef struct {
+  float temperature;  /* 0 = greedy */
+  int top_k;          /* 0 = off */
+  float top_p;        /* 1 = off */
+  uint64_t seed;
+} wc_sampling_params;
+
+typedef struct {
+  int prompt_tokens, new_tokens, rounds;
+  long accepted, verified;
+  double t_prefill, t_draft, t_verify, t_update, t_total;
+} wc_gen_stats;
+
+/* max_context: capacity of both KV arenas; max_k: largest chain length rounds may use */
+WC_API wc_status wc_decoder_create(wc_target* t, wc_drafter* d, int max_context, int max_k, wc_decoder** out);
+WC_API void wc_decoder_destroy(wc_decoder* dec);
+/* spec.py:129-141 prefill: prompt (host int32[n]); first token returned in *first */
+WC_API wc_status wc_decoder_prefill(wc_decoder* dec, const int* prompt, int n, const wc_sampling_params* sp, int* first);
+/* Oracle-drafter mode (tests/test_spec_model.py:59-92 pattern): when `forced` (host int32[k]) is
+ * non-NULL, draft token j is replaced by forced[j] after the drafter computed it. */
+WC_API wc_status wc_decoder_set_forced(wc_decoder* dec, const int* forced, int k);
+/* One greedy chain round of length k (spec.py:331-364). Writes the accepted tokens
+ * (d_1..d_a, next) to out_tokens (host, capacity k+1) and their count to *out_n. */
+WC_API wc_status wc_decoder_round(wc_decoder* dec, int k, int* out_tokens, int* out_n);
+/* spec.py:151-212 generate with a static chain policy of depth k (trees: WC_ERR_UNSUPPORTED until built).
+ * eos: host int32[n_eos]. out_tokens capacity max_new. */
+WC_API wc_status wc_decoder_generate(wc_decoder* dec, const int* prompt, int n, int max_new, int k,
+                              const wc_sampling_params* sp, const int* eos, int n_eos, int* out_tokens, int* out_n,
+                              wc_gen_stats* stats);
+/* spec.py:377-397 / spec.cpp:282-311 autoregressive baseline through the same target kernels */
+WC_API wc_status wc_generate_autoregressive(wc_target* t, const int* prompt, int n, int max_new,
+                                     const wc_sampling_params* sp, const int* eos, int n_eos, int max_context,
+                                     int* out_tokens, int* out_n, wc_gen_stats* stats);
+/* device-side state after the last round: committed length n (target cache size) and drafter cache size */
+WC_API wc_status wc_decoder_state(const wc_decoder* dec, int* n, int* drafter_len);
+/* copy the target KV cache of the decoder (for tests) */
+WC_API wc_kv* wc_decoder_target_cache(wc_decoder* dec);
+WC_API wc_kv* wc_decoder_drafter_cache(wc_decoder* dec);
+/* time the last captured round on the device (CUDA events around `iters` graph replays with the
+ * state restored between them is NOT done: callers time real rounds). Returns ms of last round. */
+WC_API wc_status wc_decoder_last_round_ms(const wc_decoder* dec, float* ms);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WOODCOCK_B200_H_ */

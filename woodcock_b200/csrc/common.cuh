@@ -1,0 +1,132 @@
+// Shared device helpers for the woodcock_b200 kernels (sm_100a).
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace wc {
+
+constexpr int kWarp = 32;
+
+// Device error word bits (raised with atomicOr, read by the host at the round's sync).
+enum DeviceError : int {
+  kErrTokenRange = 1,     // a token id outside [0, vocab)
+  kErrCapacity = 2,       // a KV write beyond the arena capacity
+  kErrRows = 4,           // a dynamic row count outside the sizes the launch was built for
+  kErrPosition = 8,       // a RoPE position beyond the precomputed table
+  kErrTree = 16,          // malformed tree (parent >= child)
+};
+
+__device__ __forceinline__ void raise_error(int* err, int bit) {
+  if (err) atomicOr(err, bit);
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ double warp_sum_d(double v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__device__ __forceinline__ float bf16_bits_to_f32(uint16_t b) { return __uint_as_float(uint32_t(b) << 16); }
+
+__device__ __forceinline__ uint16_t f32_to_bf16_bits(float f) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+
+// Two-term bf16 split: v ~= hi + lo with |v - hi - lo| <= 2^-16 |v|. Tensor-core
+// products of bf16 weights with (hi, lo) keep fp32-level accuracy on the activations.
+__device__ __forceinline__ void split_bf16(float v, uint16_t& hi, uint16_t& lo) {
+  hi = f32_to_bf16_bits(v);
+  lo = f32_to_bf16_bits(v - bf16_bits_to_f32(hi));
+}
+
+__device__ __forceinline__ uint32_t pack2(uint16_t lo_half, uint16_t hi_half) {
+  return uint32_t(lo_half) | (uint32_t(hi_half) << 16);
+}
+
+// D = A(16x16 bf16, row) * B(16x8 bf16, col) + D, fp32 accumulate.
+__device__ __forceinline__ void mma_bf16_16816(float (&d)[4], const uint4& a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a.x), "r"(a.y), "r"(a.z), "r"(a.w), "r"(b0), "r"(b1));
+}
+
+// Streaming 16-byte load: weights are read once per pass, keep L1 clean.
+__device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+__device__ __forceinline__ float4 ldg_stream_f4(const float4* p) {
+  float4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.f32 {%0,%1,%2,%3}, [%4];\n"
+               : "=f"(r.x), "=f"(r.y), "=f"(r.z), "=f"(r.w)
+               : "l"(p));
+  return r;
+}
+
+// Bulk prefetch of [p, p+bytes) into L2 (bytes multiple of 16, p 16-byte aligned).
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Orderable argmax key: larger value first, then the smaller index (first maximum,
+// like std::max_element / np.argmax). atomicMax over keys is order-independent.
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
+  uint32_t u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return (static_cast<unsigned long long>(u) << 32) | static_cast<unsigned long long>(0xFFFFFFFFu - idx);
+}
+__device__ __forceinline__ uint32_t argmax_key_index(unsigned long long k) {
+  return 0xFFFFFFFFu - static_cast<uint32_t>(k & 0xFFFFFFFFull);
+}
+__device__ __forceinline__ float argmax_key_value(unsigned long long k) {
+  uint32_t u = static_cast<uint32_t>(k >> 32);
+  u = (u & 0x80000000u) ? (u & 0x7FFFFFFFu) : ~u;
+  return __uint_as_float(u);
+}
+
+// Philox4x32-10 (Salmon, Moraes, Dror, Shaw, SC'11), counter (lo, hi, 0, 0), key = seed.
+__device__ __forceinline__ uint4 philox4x32_10(uint64_t counter, uint64_t seed) {
+  uint32_t c0 = uint32_t(counter), c1 = uint32_t(counter >> 32), c2 = 0, c3 = 0;
+  uint32_t k0 = uint32_t(seed), k1 = uint32_t(seed >> 32);
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t lo0 = 0xD2511F53u * c0, hi0 = __umulhi(0xD2511F53u, c0);
+    const uint32_t lo1 = 0xCD9E8D57u * c2, hi1 = __umulhi(0xCD9E8D57u, c2);
+    const uint32_t n0 = hi1 ^ c1 ^ k0, n2 = hi0 ^ c3 ^ k1;
+    c0 = n0;
+    c1 = lo1;
+    c2 = n2;
+    c3 = lo0;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  return make_uint4(c0, c1, c2, c3);
+}
+
+// fp64 uniform in [0, 1) from element `index` of the stream: 53 bits of words 0 and 1.
+__device__ __forceinline__ double philox_uniform(uint64_t seed, uint64_t index) {
+  const uint4 r = philox4x32_10(index, seed);
+  return (double(r.x >> 5) * 67108864.0 + double(r.y >> 6)) * (1.0 / 9007199254740992.0);
+}
+
+}  // namespace wc

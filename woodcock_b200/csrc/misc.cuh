@@ -1,0 +1,494 @@
+// Small kernels of the round and of the ops API: embedding gathers, row ops,
+// acceptance (greedy / stochastic), KV append / read / compaction and the device
+// bookkeeping that lets a whole round replay from one CUDA graph.
+#pragma once
+
+#include "common.cuh"
+
+namespace wc {
+
+constexpr int MAXK = 16;     // longest chain per round
+constexpr int MAXKEYS = 2 * MAXK + 2;
+constexpr int MAXTREE = 64;  // tree nodes per acceptance call
+
+// Device-resident decoder state (one per decoder). The host reads it only at the
+// round's single synchronisation.
+struct RoundState {
+  int n;        // committed tokens before x_n == target cache size
+  int dc_len;   // drafter cache size (real entries)
+  int x_n;      // newest committed token (not yet in the target cache)
+  int a;        // drafts accepted by the last round
+  int n_out;    // tokens emitted by the last round (a + 1)
+  int L_upd;    // rows of the drafter update (a + 1)
+  int err;      // device error word
+  int pad;
+  int tokens[MAXK + 1];   // verify input [x_n, d_1..d_K]
+  int acc[MAXK + 1];      // accepted tokens d_1..d_a, next
+  int forced[MAXK];       // oracle-drafter tokens (-1 = drafter's own)
+  unsigned long long keys[MAXKEYS];  // argmax keys: draft steps [0, K), verify rows [K, 2K+1)
+};
+
+// ----------------------------------------------------------------------------- embeddings
+
+// dst[l][d] = table[tok_l][d] (fp32 out); tokens from `tokens` or, when keys != nullptr,
+// row 0 from x0 and rows 1.. from the argmax keys (draft tokens, mapped + forced).
+__global__ void embed_rows_kernel(const void* table, int dtype, int vocab, int d, const int* tokens, int L,
+                                  const int* L_dev, float* dst, RoundState* st, const int* vocab_map, int K,
+                                  int* err) {
+  const int l = blockIdx.x;
+  const int Lr = L_dev ? *L_dev : L;
+  if (l >= Lr) return;
+  int tok;
+  if (st) {  // verify input: [x_n, d_1..d_K]
+    if (l == 0) {
+      tok = st->x_n;
+    } else if (st->forced[l - 1] >= 0) {
+      tok = st->forced[l - 1];
+    } else {
+      const uint32_t idx = argmax_key_index(st->keys[l - 1]);
+      tok = vocab_map ? vocab_map[idx] : int(idx);
+    }
+  } else {
+    tok = tokens[l];
+  }
+  if (tok < 0 || tok >= vocab) {
+    if (threadIdx.x == 0) raise_error(st ? &st->err : err, kErrTokenRange);
+    tok = 0;
+  }
+  if (st && threadIdx.x == 0) st->tokens[l] = tok;
+  const size_t base = size_t(tok) * d;
+  for (int i = threadIdx.x; i < d; i += blockDim.x)
+    dst[size_t(l) * d + i] = dtype == 1 ? bf16_bits_to_f32(static_cast<const uint16_t*>(table)[base + i])
+                                        : static_cast<const float*>(table)[base + i];
+}
+
+// ----------------------------------------------------------------------------- ops API row kernels
+
+// y = x * rsqrt(mean(x^2) + eps) * w with a double sum of squares (cpu_ops.cpp:50-59)
+__global__ void rmsnorm_rows_kernel(const float* x, float* y, int d, const float* w, float eps) {
+  const size_t r = blockIdx.x;
+  const float* xr = x + r * d;
+  float* yr = y + r * d;
+  __shared__ double red[32];
+  double ss = 0.0;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) ss += double(xr[i]) * double(xr[i]);
+  ss = warp_sum_d(ss);
+  if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    double v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.0;
+    v = warp_sum_d(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float inv = 1.f / sqrtf(float(red[0] / d) + eps);
+  __syncthreads();
+  for (int i = threadIdx.x; i < d; i += blockDim.x) yr[i] = xr[i] * inv * w[i];
+}
+
+// rotate-half RoPE on x[L][heads][D] with a host-built (cos, sin) table [max_pos][D/2]
+__global__ void rope_rows_kernel(float* x, int heads, int D, const int* positions, const float2* table, int max_pos,
+                                 int* err) {
+  const int l = blockIdx.x, half = D / 2;
+  int pos = positions[l];
+  if (pos < 0 || pos >= max_pos) {
+    if (threadIdx.x == 0) raise_error(err, kErrPosition);
+    return;
+  }
+  const float2* row = table + size_t(pos) * half;
+  for (int idx = threadIdx.x; idx < heads * half; idx += blockDim.x) {
+    const int h = idx / half, i = idx % half;
+    float* v = x + (size_t(l) * heads + h) * D;
+    const float x1 = v[i], x2 = v[i + half];
+    v[i] = x1 * row[i].x - x2 * row[i].y;
+    v[i + half] = x2 * row[i].x + x1 * row[i].y;
+  }
+}
+
+__global__ void silu_mul_kernel(float* g, const float* u, long long n) {
+  for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+    const float v = g[i];
+    g[i] = v / (1.f + expf(-v)) * u[i];
+  }
+}
+
+// one row in place; -inf -> 0; double sum (cpu_ops.cpp:86-96)
+__global__ void softmax_row_kernel(float* x, int n) {
+  __shared__ float fmax_s[32];
+  __shared__ double dsum_s[32];
+  const int tid = threadIdx.x, nw = blockDim.x / 32;
+  float m = -INFINITY;
+  for (int i = tid; i < n; i += blockDim.x) m = fmaxf(m, x[i]);
+  m = warp_max(m);
+  if (tid % 32 == 0) fmax_s[tid / 32] = m;
+  __syncthreads();
+  if (tid < 32) {
+    float v = tid < nw ? fmax_s[tid] : -INFINITY;
+    v = warp_max(v);
+    if (tid == 0) fmax_s[0] = v;
+  }
+  __syncthreads();
+  m = fmax_s[0];
+  double s = 0.0;
+  for (int i = tid; i < n; i += blockDim.x) {
+    const float v = x[i];
+    const float e = (isinf(v) && v < 0.f) ? 0.f : expf(v - m);
+    x[i] = e;
+    s += e;
+  }
+  s = warp_sum_d(s);
+  if (tid % 32 == 0) dsum_s[tid / 32] = s;
+  __syncthreads();
+  if (tid < 32) {
+    double v = tid < nw ? dsum_s[tid] : 0.0;
+    v = warp_sum_d(v);
+    if (tid == 0) dsum_s[0] = v;
+  }
+  __syncthreads();
+  const float inv = float(1.0 / dsum_s[0]);
+  for (int i = tid; i < n; i += blockDim.x) x[i] *= inv;
+}
+
+__global__ void argmax_rows_kernel(const float* x, int n, int* out) {
+  __shared__ unsigned long long best;
+  if (threadIdx.x == 0) best = 0ull;
+  __syncthreads();
+  const float* xr = x + size_t(blockIdx.x) * n;
+  unsigned long long k = 0ull;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const unsigned long long c = argmax_key(xr[i], uint32_t(i));
+    if (c > k) k = c;
+  }
+  atomicMax(&best, k);
+  __syncthreads();
+  if (threadIdx.x == 0) out[blockIdx.x] = int(argmax_key_index(best));
+}
+
+__global__ void keys_to_index_kernel(const unsigned long long* keys, int n, const int* vocab_map, int* out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) {
+    const uint32_t idx = argmax_key_index(keys[i]);
+    out[i] = vocab_map ? vocab_map[idx] : int(idx);
+  }
+}
+
+// ----------------------------------------------------------------------------- KV arena
+
+// k, v [L][Hk][D] fp32 -> arena rows [start, start+L) of one layer ([Hk][cap][D])
+__global__ void kv_append_kernel(void* K, void* V, int dtype, int Hk, int D, int cap, int start, const float* k,
+                                 const float* v, int L) {
+  const size_t total = size_t(L) * Hk * D;
+  for (size_t idx = blockIdx.x * size_t(blockDim.x) + threadIdx.x; idx < total; idx += size_t(gridDim.x) * blockDim.x) {
+    const int d = int(idx % D), h = int((idx / D) % Hk), l = int(idx / (size_t(D) * Hk));
+    const size_t dst = (size_t(h) * cap + start + l) * D + d;
+    if (dtype == 1) {
+      static_cast<uint16_t*>(K)[dst] = f32_to_bf16_bits(k[idx]);
+      static_cast<uint16_t*>(V)[dst] = f32_to_bf16_bits(v[idx]);
+    } else {
+      static_cast<float*>(K)[dst] = k[idx];
+      static_cast<float*>(V)[dst] = v[idx];
+    }
+  }
+}
+
+__global__ void kv_read_kernel(const void* K, const void* V, int dtype, int Hk, int D, int cap, int T, float* k,
+                               float* v) {
+  const size_t total = size_t(T) * Hk * D;
+  for (size_t idx = blockIdx.x * size_t(blockDim.x) + threadIdx.x; idx < total; idx += size_t(gridDim.x) * blockDim.x) {
+    const int d = int(idx % D), h = int((idx / D) % Hk), t = int(idx / (size_t(D) * Hk));
+    const size_t src = (size_t(h) * cap + t) * D + d;
+    if (dtype == 1) {
+      k[idx] = bf16_bits_to_f32(static_cast<const uint16_t*>(K)[src]);
+      v[idx] = bf16_bits_to_f32(static_cast<const uint16_t*>(V)[src]);
+    } else {
+      k[idx] = static_cast<const float*>(K)[src];
+      v[idx] = static_cast<const float*>(V)[src];
+    }
+  }
+}
+
+// In-place compaction: rows start+keep[i] -> start+i for every (layer, head, K|V) slab.
+// One block per slab stages all kept rows in shared memory before writing, so the
+// result equals the reference's increasing-order memmove (kv_cache.cpp:21-31) for any
+// keep list (dst <= src aliasing included).
+__global__ void kv_compact_kernel(void* K, void* V, int dtype, int D, int cap, int slabs, const int* keep, int n_keep,
+                                  int start) {
+  extern __shared__ float stage[];  // [n_keep][D]
+  const int slab = blockIdx.x;      // layer * Hk + head, K then V
+  const bool is_v = slab >= slabs;
+  void* base = is_v ? V : K;
+  const size_t slab_off = size_t(is_v ? slab - slabs : slab) * cap * D;
+  for (int idx = threadIdx.x; idx < n_keep * D; idx += blockDim.x) {
+    const int i = idx / D, d = idx % D;
+    const size_t src = slab_off + size_t(start + keep[i]) * D + d;
+    stage[idx] = dtype == 1 ? bf16_bits_to_f32(static_cast<const uint16_t*>(base)[src]) : static_cast<const float*>(base)[src];
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < n_keep * D; idx += blockDim.x) {
+    const int i = idx / D, d = idx % D;
+    const size_t dst = slab_off + size_t(start + i) * D + d;
+    if (dtype == 1) static_cast<uint16_t*>(base)[dst] = f32_to_bf16_bits(stage[idx]);
+    else static_cast<float*>(base)[dst] = stage[idx];
+  }
+}
+
+// ----------------------------------------------------------------------------- acceptance
+
+// verify_tree_greedy (sampling.cpp:95-106): from the root, follow the first child (in
+// node order = draw order) whose token equals the target argmax at the current node.
+__global__ void accept_greedy_tree_kernel(const int* am, const int* tokens, const int* parents, int N, int* out_path,
+                                          int* out_n, int* out_next, int* err) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  for (int v = 1; v < N; ++v)
+    if (parents[v] < 0 || parents[v] >= v) {
+      raise_error(err, kErrTree);
+      *out_n = 0;
+      *out_next = am[0];
+      return;
+    }
+  int v = 0, np = 0;
+  while (true) {
+    const int want = am[v];
+    int nxt = -1;
+    for (int c = v + 1; c < N; ++c)
+      if (parents[c] == v && tokens[c] == want) {
+        nxt = c;
+        break;
+      }
+    if (nxt < 0) {
+      *out_n = np;
+      *out_next = want;
+      return;
+    }
+    out_path[np++] = nxt;
+    v = nxt;
+  }
+}
+
+// Block-wide fp64 sum over n values (1024 threads).
+__device__ double block_sum_d(double v, double* red) {
+  v = warp_sum_d(v);
+  const int w = threadIdx.x / 32, lane = threadIdx.x % 32;
+  __syncthreads();
+  if (lane == 0) red[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    double x = lane < int(blockDim.x / 32) ? red[lane] : 0.0;
+    x = warp_sum_d(x);
+    if (lane == 0) red[32] = x;
+  }
+  __syncthreads();
+  return red[32];
+}
+
+// Inverse-CDF draw: first i with cumsum(p)[i] > u * sum(p) (np.searchsorted side="right"),
+// clipped to n-1 (sampling.py:190-193). Each thread owns a contiguous chunk; for n up
+// to 4096 thread 0 scans alone, so the cumsum is the reference's sequential one.
+__device__ int block_sample(const double* p, int n, double u, double* red, int* sel) {
+  const int tid = threadIdx.x, nt = blockDim.x;
+  if (n <= 4096) {
+    if (tid == 0) {
+      double tot = 0.0;
+      for (int i = 0; i < n; ++i) tot += p[i];
+      const double target = u * tot;
+      double c = 0.0;
+      int r = n - 1;
+      for (int i = 0; i < n; ++i) {
+        c += p[i];
+        if (c > target) {
+          r = i;
+          break;
+        }
+      }
+      *sel = r;
+    }
+    __syncthreads();
+    const int r = *sel;
+    __syncthreads();
+    return r;
+  }
+  const int chunk = (n + nt - 1) / nt;
+  const int i0 = min(n, tid * chunk), i1 = min(n, i0 + chunk);
+  double s = 0.0;
+  for (int i = i0; i < i1; ++i) s += p[i];
+  // exclusive prefix over chunk sums (in shared memory, sequential per warp leader)
+  __shared__ double chunk_sum[1024];
+  chunk_sum[tid] = s;
+  __syncthreads();
+  if (tid == 0) {
+    double c = 0.0;
+    for (int t = 0; t < nt; ++t) {
+      const double x = chunk_sum[t];
+      chunk_sum[t] = c;
+      c += x;
+    }
+    red[33] = c;  // total
+    *sel = n - 1;
+  }
+  __syncthreads();
+  const double target = u * red[33];
+  double c = chunk_sum[tid];
+  for (int i = i0; i < i1; ++i) {
+    c += p[i];
+    if (c > target) {
+      atomicMin(sel, i);
+      break;
+    }
+  }
+  __syncthreads();
+  const int r = *sel;
+  __syncthreads();
+  return r;
+}
+
+// verify_tree_stochastic (sampling.py:143-177) with Philox uniforms. Single block.
+// pw, qw: scratch [V] fp64 each.
+__global__ void __launch_bounds__(1024) accept_stochastic_tree_kernel(
+    const double* p, const double* q, int V, const int* tokens, const int* parents, int N, uint64_t seed,
+    uint64_t offset, double* pw, double* qw, int* out_path, int* out_n, int* out_next, int* out_used, int* err) {
+  __shared__ double red[40];
+  __shared__ int sel;
+  const int tid = threadIdx.x;
+  for (int v = 1; v < N; ++v)
+    if (parents[v] < 0 || parents[v] >= v) {
+      if (tid == 0) {
+        raise_error(err, kErrTree);
+        *out_n = 0;
+        *out_next = 0;
+        *out_used = 0;
+      }
+      return;
+    }
+  uint64_t ctr = offset;
+  int v = 0, np = 0;
+  while (true) {
+    for (int i = tid; i < V; i += blockDim.x) pw[i] = p[size_t(v) * V + i];
+    __syncthreads();
+    bool has_kids = false;
+    for (int c = v + 1; c < N; ++c) has_kids |= parents[c] == v;
+    if (!has_kids) {
+      const double u = philox_uniform(seed, ctr++);
+      const int r = block_sample(pw, V, u, red, &sel);
+      if (tid == 0) {
+        *out_n = np;
+        *out_next = r;
+        *out_used = int(ctr - offset);
+      }
+      return;
+    }
+    for (int i = tid; i < V; i += blockDim.x) qw[i] = q[size_t(v) * V + i];
+    __syncthreads();
+    int accepted = -1;
+    for (int c = v + 1; c < N; ++c) {
+      if (parents[c] != v) continue;
+      const int x = tokens[c];
+      const double qx = qw[x];
+      if (qx > 0) {
+        const double u = philox_uniform(seed, ctr++);
+        const double ratio = pw[x] / qx;
+        if (u < (ratio < 1.0 ? ratio : 1.0)) {
+          accepted = c;
+          break;
+        }
+      }
+      // p <- norm(max(p - q, 0)), or p / sum(p) when that mass is <= 1e-12
+      double s = 0.0;
+      for (int i = tid; i < V; i += blockDim.x) s += fmax(pw[i] - qw[i], 0.0);
+      s = block_sum_d(s, red);
+      if (s <= 1e-12) {
+        double tp = 0.0;
+        for (int i = tid; i < V; i += blockDim.x) tp += pw[i];
+        tp = block_sum_d(tp, red);
+        for (int i = tid; i < V; i += blockDim.x) pw[i] = pw[i] / tp;
+      } else {
+        for (int i = tid; i < V; i += blockDim.x) pw[i] = fmax(pw[i] - qw[i], 0.0) / s;
+      }
+      __syncthreads();
+      if (tid == 0) qw[x] = 0.0;
+      __syncthreads();
+      double sq = 0.0;
+      for (int i = tid; i < V; i += blockDim.x) sq += qw[i];
+      sq = block_sum_d(sq, red);
+      if (sq <= 0) break;
+      for (int i = tid; i < V; i += blockDim.x) qw[i] /= sq;
+      __syncthreads();
+    }
+    if (accepted < 0) {
+      const double u = philox_uniform(seed, ctr++);
+      const int r = block_sample(pw, V, u, red, &sel);
+      if (tid == 0) {
+        *out_n = np;
+        *out_next = r;
+        *out_used = int(ctr - offset);
+      }
+      return;
+    }
+    if (tid == 0) out_path[np] = accepted;
+    ++np;
+    v = accepted;
+    __syncthreads();
+  }
+}
+
+__global__ void philox_uniforms_kernel(uint64_t seed, uint64_t offset, int n, double* out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = philox_uniform(seed, offset + uint64_t(i));
+}
+
+// ----------------------------------------------------------------------------- round bookkeeping
+
+// Greedy chain acceptance (python/woodcock/spec.py:357-362): longest prefix of drafts
+// equal to the target argmax, plus the target token at the first mismatch. Chain
+// compaction keeps rows 0..a, i.e. the target cache size becomes n + a + 1 (no data
+// moves). Resets every argmax key for the next round.
+__global__ void accept_chain_kernel(RoundState* st, int K, const int* vocab_map_unused, int* out_host_view) {
+  if (threadIdx.x != 0) return;
+  int am[MAXK + 1];
+  for (int i = 0; i <= K; ++i) am[i] = int(argmax_key_index(st->keys[K + i]));
+  int a = 0;
+  while (a < K && st->tokens[a + 1] == am[a]) ++a;
+  const int next = am[a];
+  for (int i = 0; i < a; ++i) st->acc[i] = st->tokens[i + 1];
+  st->acc[a] = next;
+  st->a = a;
+  st->n_out = a + 1;
+  st->L_upd = a + 1;
+  st->n += a + 1;
+  st->x_n = next;
+  for (int i = 0; i < MAXKEYS; ++i) st->keys[i] = 0ull;
+  if (out_host_view) {
+    out_host_view[0] = a + 1;
+    for (int i = 0; i <= a; ++i) out_host_view[1 + i] = st->acc[i];
+  }
+  (void)vocab_map_unused;
+}
+
+// End of the drafter update: out = RMSNorm(h) for the last row (already written back by
+// the caller when needed), root_out / root_fb from row L-1, drafter cache grows by L.
+__global__ void finish_update_kernel(RoundState* st, const int* L_dev, int L_static, const float* h, int d,
+                                     const float* norm_w, float eps, int post_norm, float* root_out, float* root_fb,
+                                     int advance_dc) {
+  __shared__ float red[32];
+  const int L = L_dev ? *L_dev : L_static;
+  const float* hr = h + size_t(L - 1) * d;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < d; i += blockDim.x) ss = fmaf(hr[i], hr[i], ss);
+  ss = warp_sum(ss);
+  if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
+    v = warp_sum(v);
+    if (threadIdx.x == 0) red[0] = v;
+  }
+  __syncthreads();
+  const float inv = 1.f / sqrtf(red[0] / float(d) + eps);
+  for (int i = threadIdx.x; i < d; i += blockDim.x) {
+    const float o = hr[i] * inv * norm_w[i];
+    root_out[i] = o;
+    root_fb[i] = post_norm ? o : hr[i];
+  }
+  if (threadIdx.x == 0 && advance_dc) st->dc_len += L;
+}
+
+}  // namespace wc

@@ -1,0 +1,2246 @@
+// woodcock_b200 runtime: the C ABI of include/woodcock_b200.h.
+//
+// Host orchestration of the B200 decode round. Weights live on the device in their
+// streaming layouts (bf16 A-fragment tiles or fp32 rows); fused projections are
+// built at load: Q|K|V stacked, gate/up interleaved by 16-row blocks (SwiGLU
+// epilogue), the drafter's main and auxiliary Q/K/V side by side along K. A
+// decoder round (draft chain -> verify -> accept -> compact -> drafter update) is
+// captured once per chain length as a CUDA graph and replayed with one host
+// synchronisation per round; all round state lives in device memory.
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <filesystem>
+#include <functional>
+#include <map>
+#include <memory>
+#include <set>
+#include <string>
+#include <vector>
+
+#include "../../include/woodcock_b200.h"
+#include "attention.cuh"
+#include "common.cuh"
+#include "gemv.cuh"
+#include "host_io.h"
+#include "misc.cuh"
+
+using namespace wc;
+namespace fs = std::filesystem;
+
+// ============================================================================ errors
+
+namespace {
+
+struct WcError {
+  wc_status st;
+  std::string msg;
+};
+
+[[noreturn]] void fail(wc_status st, const std::string& msg) { throw WcError{st, msg}; }
+
+#define CUDA_TRY(x)                                                                                  \
+  do {                                                                                               \
+    cudaError_t e_ = (x);                                                                            \
+    if (e_ != cudaSuccess) fail(e_ == cudaErrorMemoryAllocation ? WC_ERR_OOM : WC_ERR_CUDA,          \
+                                std::string(#x) + ": " + cudaGetErrorString(e_));                    \
+  } while (0)
+
+double now_s() {
+  return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+}  // namespace
+
+// ============================================================================ context
+
+struct RopeTable {
+  float2* ptr = nullptr;
+  int max_pos = 0;
+};
+
+struct wc_ctx {
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  bool own_stream = false;
+  int num_sms = 148;
+  std::string err;
+  int* d_err = nullptr;  // device error word of the ops API
+  uint64_t launches = 0;
+  bool capturing = false;
+  uint64_t capture_launches = 0;
+  std::map<std::pair<int, uint32_t>, RopeTable> rope;
+  double* pw = nullptr;
+  double* qw = nullptr;
+  int pw_n = 0;
+  int occ_gemv[3] = {1, 1, 1};  // [0] fp32, [1] bf16 NT=1, [2] bf16 NT=2
+  size_t max_smem = 0;
+};
+
+namespace {
+
+template <class F>
+wc_status guard(wc_ctx* ctx, F&& f) {
+  try {
+    f();
+    return WC_OK;
+  } catch (const WcError& e) {
+    if (ctx) ctx->err = e.msg;
+    return e.st;
+  } catch (const std::bad_alloc&) {
+    if (ctx) ctx->err = "host allocation failed";
+    return WC_ERR_OOM;
+  } catch (const std::exception& e) {
+    if (ctx) ctx->err = e.what();
+    return WC_ERR_IO;
+  }
+}
+
+void count_launch(wc_ctx* ctx) {
+  if (ctx->capturing) ++ctx->capture_launches;
+  else ++ctx->launches;
+}
+
+void check_launch(wc_ctx* ctx, const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) fail(WC_ERR_CUDA, std::string("launch of ") + what + " failed: " + cudaGetErrorString(e));
+  count_launch(ctx);
+}
+
+void* dalloc(size_t bytes) {
+  if (bytes == 0) bytes = 16;
+  void* p = nullptr;
+  const cudaError_t e = cudaMalloc(&p, bytes);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    fail(WC_ERR_OOM, "cudaMalloc(" + std::to_string(bytes) + ") failed: " + cudaGetErrorString(e));
+  }
+  return p;
+}
+
+void dfree(void* p) {
+  if (p) cudaFree(p);
+}
+
+// Host-built rotate-half RoPE table [max_pos][D/2] of (cos, sin) computed with the
+// same float expressions as the reference (src/backends/cpu_ops.cpp:64-68).
+RopeTable& rope_table(wc_ctx* ctx, int D, float base, int need_pos) {
+  uint32_t bits;
+  std::memcpy(&bits, &base, 4);
+  auto& t = ctx->rope[{D, bits}];
+  if (t.max_pos >= need_pos) return t;
+  if (ctx->capturing) fail(WC_ERR_INVALID, "RoPE table growth during capture");
+  const int max_pos = std::max(need_pos, 32768);
+  const int half = D / 2;
+  std::vector<float> inv(half);
+  for (int i = 0; i < half; ++i) inv[i] = std::pow(base, -2.f * i / D);
+  std::vector<float2> host(size_t(max_pos) * half);
+  for (int p = 0; p < max_pos; ++p)
+    for (int i = 0; i < half; ++i) {
+      const float a = float(p) * inv[i];
+      host[size_t(p) * half + i] = make_float2(std::cos(a), std::sin(a));
+    }
+  if (t.ptr) {
+    CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    dfree(t.ptr);
+  }
+  t.ptr = static_cast<float2*>(dalloc(host.size() * sizeof(float2)));
+  CUDA_TRY(cudaMemcpy(t.ptr, host.data(), host.size() * sizeof(float2), cudaMemcpyHostToDevice));
+  t.max_pos = max_pos;
+  return t;
+}
+
+int dtype_size(int dt) { return dt == WC_BF16 ? 2 : 4; }
+
+int src_dtype_code(const std::string& s) {
+  if (s == "F32") return 0;
+  if (s == "BF16") return 1;
+  if (s == "F16") return 2;
+  return -1;
+}
+
+}  // namespace
+
+// ============================================================================ staged tensors / weights
+
+namespace {
+
+// A tensor uploaded to the device in its source dtype, waiting to be laid out.
+struct Staged {
+  void* ptr = nullptr;
+  int dtype = 0;  // 0 f32, 1 bf16 (f16 is converted to f32 on upload)
+  std::vector<int64_t> shape;
+  int64_t numel() const {
+    int64_t n = 1;
+    for (auto s : shape) n *= s;
+    return n;
+  }
+};
+
+__global__ void f16_to_f32_kernel(const uint16_t* src, float* dst, size_t n) {
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x)
+    dst[i] = __half2float(__ushort_as_half(src[i]));
+}
+
+__global__ void convert_kernel(const void* src, int src_dtype, void* dst, int dst_dtype, size_t n) {
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
+    const float v = src_dtype == 1 ? bf16_bits_to_f32(static_cast<const uint16_t*>(src)[i])
+                                   : static_cast<const float*>(src)[i];
+    if (dst_dtype == 1) static_cast<uint16_t*>(dst)[i] = f32_to_bf16_bits(v);
+    else static_cast<float*>(dst)[i] = v;
+  }
+}
+
+// Tiles a row-major part [N][K] into tile grid positions (rb * rb_stride + rbo, kt + kto)
+// of a bf16 A-fragment-tiled matrix with dst_KT k-tiles per row block.
+__global__ void tile_part_kernel(const void* src, int src_dtype, int N, int K, uint16_t* dst, int dst_KT,
+                                 int rb_stride, int rbo, int kto) {
+  const int NB = (N + 15) / 16, KB = (K + 15) / 16;
+  const size_t total = size_t(NB) * KB * 256;
+  for (size_t idx = blockIdx.x * size_t(blockDim.x) + threadIdx.x; idx < total; idx += size_t(gridDim.x) * blockDim.x) {
+    const size_t tile = idx / 256;
+    const int within = int(idx % 256);
+    const int rbp = int(tile / KB), ktp = int(tile % KB);
+    const int lane = within / 8, e = within % 8, g = lane / 4, t = lane % 4;
+    const int r = g + ((e & 2) ? 8 : 0);
+    const int c = 2 * t + (e & 1) + ((e & 4) ? 8 : 0);
+    const int row = rbp * 16 + r, col = ktp * 16 + c;
+    float v = 0.f;
+    if (row < N && col < K) {
+      const size_t s = size_t(row) * K + col;
+      v = src_dtype == 1 ? bf16_bits_to_f32(static_cast<const uint16_t*>(src)[s]) : static_cast<const float*>(src)[s];
+    }
+    const size_t dtile = size_t(rbp * rb_stride + rbo) * dst_KT + (ktp + kto);
+    dst[dtile * 256 + within] = f32_to_bf16_bits(v);
+  }
+}
+
+// Row-major fp32 part copy: dst[(r * row_stride + row_off) * ld + col_off + c] = src[r][c].
+__global__ void copy_part_f32_kernel(const void* src, int src_dtype, int N, int K, float* dst, int ld, int row_stride,
+                                     int row_off, int col_off) {
+  const size_t total = size_t(N) * K;
+  for (size_t idx = blockIdx.x * size_t(blockDim.x) + threadIdx.x; idx < total; idx += size_t(gridDim.x) * blockDim.x) {
+    const int r = int(idx / K), c = int(idx % K);
+    const float v = src_dtype == 1 ? bf16_bits_to_f32(static_cast<const uint16_t*>(src)[idx])
+                                   : static_cast<const float*>(src)[idx];
+    dst[size_t(r * row_stride + row_off) * ld + col_off + c] = v;
+  }
+}
+
+// Restricted head: new row i = old row ids[i], for the tiled bf16 layout.
+__global__ void gather_tiled_rows_kernel(const uint16_t* src, int KT, const int* ids, int n, uint16_t* dst) {
+  const int NB = (n + 15) / 16;
+  const size_t total = size_t(NB) * KT * 256;
+  for (size_t idx = blockIdx.x * size_t(blockDim.x) + threadIdx.x; idx < total; idx += size_t(gridDim.x) * blockDim.x) {
+    const size_t tile = idx / 256;
+    const int within = int(idx % 256);
+    const int rb = int(tile / KT), kt = int(tile % KT);
+    const int lane = within / 8, e = within % 8, g = lane / 4, t = lane % 4;
+    const int r = g + ((e & 2) ? 8 : 0);
+    const int c = 2 * t + (e & 1) + ((e & 4) ? 8 : 0);
+    const int row = rb * 16 + r;
+    uint16_t v = 0;
+    if (row < n) {
+      const int sr = ids[row];
+      const int sg = sr % 8, shalf = (sr % 16) / 8;
+      const int sc_t = (c % 8) / 2, sc_half = c / 8;
+      const int slane = sg * 4 + sc_t;
+      const int se = (c % 2) + shalf * 2 + sc_half * 4;
+      const size_t stile = size_t(sr / 16) * KT + kt;
+      v = src[stile * 256 + slane * 8 + se];
+    }
+    dst[idx] = v;
+  }
+}
+
+__global__ void gather_rows_f32_kernel(const float* src, int ld, const int* ids, int n, float* dst) {
+  const size_t total = size_t(n) * ld;
+  for (size_t idx = blockIdx.x * size_t(blockDim.x) + threadIdx.x; idx < total; idx += size_t(gridDim.x) * blockDim.x)
+    dst[idx] = src[size_t(ids[idx / ld]) * ld + idx % ld];
+}
+
+int grid_for(size_t n) { return int(std::min<size_t>((n + 255) / 256, 148 * 16)); }
+
+// One projection in its streaming layout. N = output features; for SwiGLU (group 2)
+// the stored matrix holds 2 * N rows (gate and up interleaved by 16-row blocks, or
+// rows 2n / 2n+1 in the fp32 layout).
+struct Lin {
+  void* w = nullptr;
+  int N = 0, Np = 0, K = 0, Kp = 0, dtype = 0, group = 1;
+  size_t bytes = 0;
+  bool owned = true;
+};
+
+Lin make_lin(int dtype, int N, int K, int group) {
+  Lin l;
+  l.dtype = dtype;
+  l.N = N;
+  l.K = K;
+  l.group = group;
+  if (dtype == WC_BF16) {
+    l.Np = ((N + 15) / 16) * 16 * group;
+    l.Kp = ((K + 15) / 16) * 16;
+    l.bytes = size_t(l.Np) * l.Kp * 2;
+  } else {
+    l.Np = N * group;
+    l.Kp = ((K + 3) / 4) * 4;
+    l.bytes = size_t(l.Np) * l.Kp * 4;
+  }
+  l.w = dalloc(l.bytes);
+  CUDA_TRY(cudaMemset(l.w, 0, l.bytes));
+  return l;
+}
+
+void free_lin(Lin& l) {
+  if (l.owned) dfree(l.w);
+  l.w = nullptr;
+}
+
+// Places a row-major part [rows][cols] at (row_off, col_off); `which` selects gate (0) /
+// up (1) for a SwiGLU projection.
+void lin_put(wc_ctx* ctx, Lin& l, const Staged& s, int rows, int cols, int row_off, int col_off, int which) {
+  if (l.dtype == WC_BF16) {
+    if (row_off % 16 || col_off % 16)
+      fail(WC_ERR_UNSUPPORTED, "projection parts must start on 16-row / 16-column boundaries");
+    const int KT = l.Kp / 16;
+    tile_part_kernel<<<grid_for(size_t(rows) * cols), 256, 0, ctx->stream>>>(
+        s.ptr, s.dtype, rows, cols, static_cast<uint16_t*>(l.w), KT, l.group, (row_off / 16) * l.group + which,
+        col_off / 16);
+  } else {
+    copy_part_f32_kernel<<<grid_for(size_t(rows) * cols), 256, 0, ctx->stream>>>(
+        s.ptr, s.dtype, rows, cols, static_cast<float*>(l.w), l.Kp, l.group, row_off * l.group + which, col_off);
+  }
+  check_launch(ctx, "weight layout");
+}
+
+}  // namespace
+
+struct wc_weight {
+  wc_ctx* ctx;
+  Lin lin;
+};
+
+// ============================================================================ GEMV launcher
+
+namespace {
+
+struct GemvPlan {
+  const Lin* W;
+  GemvParams p;
+};
+
+GemvParams gemv_params() {
+  GemvParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.eps = 1e-6f;
+  p.group = 1;
+  return p;
+}
+
+Seg seg_rows(const float* src, int ld, int len, const float* norm_w = nullptr, float* write_back = nullptr,
+             int ld_wb = 0) {
+  Seg s;
+  std::memset(&s, 0, sizeof(s));
+  s.src = src;
+  s.ld = ld;
+  s.len = len;
+  s.norm_w = norm_w;
+  s.write_back = write_back;
+  s.ld_wb = ld_wb;
+  return s;
+}
+
+Seg seg_embed(const void* table, int dtype, int len, const float* norm_w) {
+  Seg s;
+  std::memset(&s, 0, sizeof(s));
+  s.table = table;
+  s.table_dtype = dtype;
+  s.len = len;
+  s.norm_w = norm_w;
+  return s;
+}
+
+void launch_gemv(wc_ctx* ctx, const Lin& W, GemvParams p) {
+  p.w = W.w;
+  p.N = W.N;
+  p.Np = W.Np;
+  p.K = W.K;
+  p.Kp = W.Kp;
+  p.w_dtype = W.dtype;
+  p.group = W.group;
+  if (!p.err) p.err = ctx->d_err;
+  int klen = 0;
+  for (int s = 0; s < p.nseg; ++s) klen += p.seg[s].len;
+  if (klen != W.K) fail(WC_ERR_INVALID, "GEMV input width " + std::to_string(klen) + " != " + std::to_string(W.K));
+  if (p.L_max < 1 || p.L_max > GEMV_MAXL) fail(WC_ERR_INVALID, "GEMV rows outside 1..16");
+  if (W.dtype == WC_BF16) {
+    const int NT = p.L_max <= 8 ? 1 : 2;
+    const int nunits = W.Np / (16 * W.group);
+    const int grid = std::max(1, std::min(nunits, ctx->num_sms * ctx->occ_gemv[NT]));
+    if (NT == 1) gemv_bf16_kernel<1><<<grid, GEMV_THREADS, gemv_bf16_smem<1>(), ctx->stream>>>(p);
+    else gemv_bf16_kernel<2><<<grid, GEMV_THREADS, gemv_bf16_smem<2>(), ctx->stream>>>(p);
+  } else {
+    const size_t smem = gemv_f32_smem(p.L_max, W.Kp);
+    if (smem > ctx->max_smem) fail(WC_ERR_UNSUPPORTED, "fp32 projection too wide for shared memory");
+    const int grid = std::max(1, std::min((W.N + GEMV_WARPS - 1) / GEMV_WARPS, ctx->num_sms * 2));
+    gemv_f32_kernel<<<grid, GEMV_THREADS, smem, ctx->stream>>>(p);
+  }
+  check_launch(ctx, "gemv");
+}
+
+constexpr int ATT_CLUSTER = 8;
+
+void launch_attention(wc_ctx* ctx, AttnParams p) {
+  if (!p.err) p.err = ctx->d_err;
+  if (p.D > ATT_MAXD || p.D % 32) fail(WC_ERR_UNSUPPORTED, "head_dim must be a multiple of 32 up to 128");
+  if (p.H % p.Hk) fail(WC_ERR_INVALID, "heads must be a multiple of kv_heads");
+  const int rep = p.H / p.Hk;
+  if (p.L_max * rep > ATT_MAXR) fail(WC_ERR_UNSUPPORTED, "too many query rows per KV head in one launch");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ATT_CLUSTER, p.Hk, 1);
+  cfg.blockDim = dim3(ATT_THREADS, 1, 1);
+  cfg.dynamicSmemBytes = attention_smem(p.L_max);
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = ATT_CLUSTER;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, attention_kernel, p);
+  if (e != cudaSuccess) fail(WC_ERR_CUDA, std::string("attention launch: ") + cudaGetErrorString(e));
+  check_launch(ctx, "attention");
+}
+
+AttnParams attn_params() {
+  AttnParams p;
+  std::memset(&p, 0, sizeof(p));
+  return p;
+}
+
+}  // namespace
+
+// ============================================================================ C ABI: context
+
+extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
+  if (!out) return WC_ERR_INVALID;
+  auto* ctx = new wc_ctx();
+  const wc_status st = guard(ctx, [&] {
+    CUDA_TRY(cudaSetDevice(device));
+    ctx->device = device;
+    cudaDeviceProp prop;
+    CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+    if (prop.major < 10) fail(WC_ERR_UNSUPPORTED, "woodcock_b200 needs an sm_100 (Blackwell) GPU");
+    ctx->num_sms = prop.multiProcessorCount;
+    ctx->max_smem = prop.sharedMemPerBlockOptin;
+    if (stream) {
+      ctx->stream = static_cast<cudaStream_t>(stream);
+    } else {
+      CUDA_TRY(cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking));
+      ctx->own_stream = true;
+    }
+    ctx->d_err = static_cast<int*>(dalloc(sizeof(int)));
+    CUDA_TRY(cudaMemset(ctx->d_err, 0, sizeof(int)));
+    const int smax = int(ctx->max_smem);
+    CUDA_TRY(cudaFuncSetAttribute(gemv_bf16_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
+    CUDA_TRY(cudaFuncSetAttribute(gemv_bf16_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
+    CUDA_TRY(cudaFuncSetAttribute(gemv_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
+    CUDA_TRY(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
+    CUDA_TRY(cudaFuncSetAttribute(kv_compact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
+    int occ = 0;
+    CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_bf16_kernel<1>, GEMV_THREADS,
+                                                           gemv_bf16_smem<1>()));
+    ctx->occ_gemv[1] = std::max(1, occ);
+    CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_bf16_kernel<2>, GEMV_THREADS,
+                                                           gemv_bf16_smem<2>()));
+    ctx->occ_gemv[2] = std::max(1, occ);
+  });
+  if (st != WC_OK) {
+    // keep the context so the caller can read the error, but mark it unusable
+    *out = ctx;
+    return st;
+  }
+  *out = ctx;
+  return WC_OK;
+}
+
+extern "C" wc_status wc_ctx_set_stream(wc_ctx* ctx, void* stream) {
+  if (!ctx) return WC_ERR_INVALID;
+  return guard(ctx, [&] {
+    if (ctx->own_stream) {
+      CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+      cudaStreamDestroy(ctx->stream);
+      ctx->own_stream = false;
+    }
+    ctx->stream = static_cast<cudaStream_t>(stream);
+  });
+}
+
+extern "C" void wc_ctx_destroy(wc_ctx* ctx) {
+  if (!ctx) return;
+  cudaSetDevice(ctx->device);
+  if (ctx->stream) cudaStreamSynchronize(ctx->stream);
+  for (auto& kv : ctx->rope) dfree(kv.second.ptr);
+  dfree(ctx->d_err);
+  dfree(ctx->pw);
+  dfree(ctx->qw);
+  if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
+  delete ctx;
+}
+
+extern "C" const char* wc_last_error(const wc_ctx* ctx) { return ctx ? ctx->err.c_str() : "null context"; }
+
+extern "C" wc_status wc_ctx_synchronize(wc_ctx* ctx) {
+  if (!ctx) return WC_ERR_INVALID;
+  return guard(ctx, [&] {
+    CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    int e = 0;
+    CUDA_TRY(cudaMemcpy(&e, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (e) {
+      CUDA_TRY(cudaMemset(ctx->d_err, 0, sizeof(int)));
+      fail(WC_ERR_DEVICE, "device error flag " + std::to_string(e));
+    }
+  });
+}
+
+extern "C" uint64_t wc_ctx_launch_count(const wc_ctx* ctx) { return ctx ? ctx->launches : 0; }
+
+// ============================================================================ C ABI: ops
+
+extern "C" wc_status wc_weight_create(wc_ctx* ctx, const void* data, int src_dtype, int data_on_device, int out_rows,
+                                      int in_cols, int dtype, wc_weight** w) {
+  if (!ctx || !w || !data || out_rows <= 0 || in_cols <= 0) return WC_ERR_INVALID;
+  return guard(ctx, [&] {
+    if ((dtype != WC_F32 && dtype != WC_BF16) || (src_dtype != WC_F32 && src_dtype != WC_BF16))
+      fail(WC_ERR_INVALID, "dtype must be WC_F32 or WC_BF16");
+    Staged s;
+    const size_t bytes = size_t(out_rows) * in_cols * dtype_size(src_dtype);
+    s.dtype = src_dtype;
+    if (data_on_device) {
+      s.ptr = const_cast<void*>(data);
+    } else {
+      s.ptr = dalloc(bytes);
+      CUDA_TRY(cudaMemcpy(s.ptr, data, bytes, cudaMemcpyHostToDevice));
+    }
+    auto* out = new wc_weight{ctx, make_lin(dtype, out_rows, in_cols, 1)};
+    lin_put(ctx, out->lin, s, out_rows, in_cols, 0, 0, 0);
+    CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    if (!data_on_device) dfree(s.ptr);
+    *w = out;
+  });
+}
+
+extern "C" void wc_weight_destroy(wc_weight* w) {
+  if (!w) return;
+  free_lin(w->lin);
+  delete w;
+}
+
+extern "C" wc_status wc_linear(wc_ctx* ctx, const float* x, int L, int in, const wc_weight* W, float* y, int accumulate) {
+  if (!ctx || !x || !W || !y || L <= 0) return WC_ERR_INVALID;
+  return guard(ctx, [&] {
+    if (in != W->lin.K) fail(WC_ERR_INVALID, "linear: input width does not match the weight");
+    for (int r0 = 0; r0 < L; r0 += GEMV_MAXL) {
+      const int rows = std::min(GEMV_MAXL, L - r0);
+      GemvParams p = gemv_params();
+      p.L = rows;
+      p.L_max = rows;
+      p.nseg = 1;
+      p.seg[0] = seg_rows(x + size_t(r0) * in, in, in);
+      p.epi = accumulate ? EPI_ADD : EPI_STORE;
+      p.y = y + size_t(r0) * W->lin.N;
+      p.ldy = W->lin.N;
+      p.base = p.y;
+      p.ldb = W->lin.N;
+      launch_gemv(ctx, W->lin, p);
+    }
+  });
+}
+
+extern "C" wc_status wc_rmsnorm(wc_ctx* ctx, const float* x, float* y, int rows, int d, const float* w, float eps) {
+  if (!ctx || !x || !y || !w || rows <= 0 || d <= 0) return WC_ERR_INVALID;
+  return guard(ctx, [&] {
+    rmsnorm_rows_kernel<<<rows, 256, 0, ctx->stream>>>(x, y, d, w, eps);
+    check_launch(ctx, "rmsnorm");
+  });
+}
+
+extern "C" wc_status wc_rope(wc_ctx* ctx, float* x, int L, int heads, int D, const int* positions, float base) {
+  if (!ctx || !x || !positions || L <= 0 || heads <= 0 || D <= 0 || D % 2) return WC_ERR_INVALID;
+  return guard(ctx, [&] {
+    RopeTable& t = rope_table(ctx, D, base, 32768);
+    rope_rows_kernel<<<L, 256, 0, ctx->stream>>>(x, heads, D, positions, t.ptr, t.max_pos, ctx->d_err);
+    check_launch(ctx, "rope");
+  });
+}
+
+extern "C" wc_status wc_silu_mul(wc_ctx* ctx, float* gate, const float* up, int64_t n) {
+  if (!ctx || !gate || !up || n < 0) return WC_ERR_INVALID;
+  return guard(ctx, [&] {
+    if (n == 0) return;
+    silu_mul_kernel<<<grid_for(size_t(n)), 256, 0, ctx->stream>>>(gate, up, n);
+    check_launch(ctx, "silu_mul");
+  });
+}
+
+extern "C" wc_status wc_softmax(wc_ctx* ctx, float* x, int n) {
+  if (!ctx || !x || n <= 0) return WC_ERR_INVALID;
+  return guard(ctx, [&] {
+    softmax_row_kernel<<<1, 1024, 0, ctx->stream>>>(x, n);
+    check_launch(ctx, "softmax");
+  });
+}
+
+extern "C" wc_status wc_argmax_rows(wc_ctx* ctx, const float* x, int rows, int n, int* out) {
+  if (!ctx || !x || !out || rows <= 0 || n <= 0) return WC_ERR_INVALID;
+  return guard(ctx, [&] {
+    argmax_rows_kernel<<<rows, 1024, 0, ctx->stream>>>(x, n, out);
+    check_launch(ctx, "argmax");
+  });
+}
+
+extern "C" wc_status wc_attention(wc_ctx* ctx, const float* q, int L, int H, int Hk, int D, const void* K,
+                                  const void* V, int kv_dtype, int T, const uint8_t* mask, float* out, float scale) {
+  if (!ctx || !q || !K || !V || !out || L <= 0 || H <= 0 || Hk <= 0 || D <= 0 || T <= 0) return WC_ERR_INVALID;
+  return guard(ctx, [&] {
+    if (H % Hk) fail(WC_ERR_INVALID, "heads must be a multiple of kv_heads");
+    const int rep = H / Hk;
+    const int rows = std::max(1, ATT_MAXR / rep);
+    for (int r0 = 0; r0 < L; r0 += rows) {
+      const int n = std::min(rows, L - r0);
+      AttnParams p = attn_params();
+      p.q_ready = q + size_t(r0) * H * D;
+      p.L = n;
+      p.L_max = n;
+      p.T_full = T;
+      p.Kc = const_cast<void*>(K);
+      p.Vc = const_cast<void*>(V);
+      p.kv_dtype = kv_dtype;
+      p.stride_h = D;
+      p.stride_p = (long long)Hk * D;
+      p.cap = T;
+      p.H = H;
+      p.Hk = Hk;
+      p.D = D;
+      p.mask_full = mask ? mask + size_t(r0) * T : nullptr;
+      p.mask_ld = T;
+      p.scale = scale;
+      p.out = out + size_t(r0) * H * D;
+      p.ld_out = H * D;
+      p.max_pos = 1;
+      launch_attention(ctx, p);
+    }
+  });
+}
+
+extern "C" wc_status wc_philox_uniforms(wc_ctx* ctx, uint64_t seed, uint64_t offset, int n, double* out) {
+  if (!ctx || !out || n < 0) return WC_ERR_INVALID;
+  return guard(ctx, [&] {
+    if (n == 0) return;
+    philox_uniforms_kernel<<<(n + 255) / 256, 256, 0, ctx->stream>>>(seed, offset, n, out);
+    check_launch(ctx, "philox");
+  });
+}
+
+extern "C" wc_status wc_accept_greedy(wc_ctx* ctx, const int* am, const int* tokens, const int* parents, int N,
+                                      int* out_path, int* out_n, int* out_next) {
+  if (!ctx || !am || !tokens || !parents || !out_path || !out_n || !out_next || N <= 0) return WC_ERR_INVALID;
+  return guard(ctx, [&] {
+    accept_greedy_tree_kernel<<<1, 32, 0, ctx->stream>>>(am, tokens, parents, N, out_path, out_n, out_next,
+                                                         ctx->d_err);
+    check_launch(ctx, "accept_greedy");
+  });
+}
+
+extern "C" wc_status wc_accept_stochastic(wc_ctx* ctx, const double* p, const double* q, int V, const int* tokens,
+                                          const int* parents, int N, uint64_t seed, uint64_t offset, int* out_path,
+                                          int* out_n, int* out_next, int* out_used) {
+  if (!ctx || !p || !q || !tokens || !parents || !out_path || !out_n || !out_next || !out_used || N <= 0 || V <= 0)
+    return WC_ERR_INVALID;
+  return guard(ctx, [&] {
+    if (ctx->pw_n < V) {
+      CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+      dfree(ctx->pw);
+      dfree(ctx->qw);
+      ctx->pw = static_cast<double*>(dalloc(sizeof(double) * V));
+      ctx->qw = static_cast<double*>(dalloc(sizeof(double) * V));
+      ctx->pw_n = V;
+    }
+    accept_stochastic_tree_kernel<<<1, 1024, 0, ctx->stream>>>(p, q, V, tokens, parents, N, seed, offset, ctx->pw,
+                                                               ctx->qw, out_path, out_n, out_next, out_used,
+                                                               ctx->d_err);
+    check_launch(ctx, "accept_stochastic");
+  });
+}
+
+// ============================================================================ C ABI: KV cache
+
+struct wc_kv {
+  wc_ctx* ctx;
+  int layers, Hk, D, cap, dtype;
+  void* K;
+  void* V;
+  int n;  // host-side size for the ops / forward API
+  size_t layer_elems() const { return size_t(Hk) * cap * D; }
+  void* Kl(int l) const { return static_cast<char*>(K) + size_t(l) * layer_elems() * dtype_size(dtype); }
+  void* Vl(int l) const { return static_cast<char*>(V) + size_t(l) * layer_elems() * dtype_size(dtype); }
+};
+
+namespace {
+wc_kv* kv_new(wc_ctx* ctx, int layers, int Hk, int D, int cap, int dtype) {
+  if (layers <= 0 || Hk <= 0 || D <= 0 || cap <= 0) fail(WC_ERR_INVALID, "bad KV cache shape");
+  auto* kv = new wc_kv{ctx, layers, Hk, D, cap, dtype, nullptr, nullptr, 0};
+  const size_t bytes = size_t(layers) * kv->layer_elems() * dtype_size(dtype);
+  kv->K = dalloc(bytes);
+  kv->V = dalloc(bytes);
+  CUDA_TRY(cudaMemset(kv->K, 0, bytes));
+  CUDA_TRY(cudaMemset(kv->V, 0, bytes));
+  return kv;
+}
+}  // namespace
+
+extern "C" wc_status wc_kv_create(wc_ctx* ctx, int layers, int kv_heads, int head_dim, int capacity, int dtype,
+                                  wc_kv** kv) {
+  if (!ctx || !kv) return WC_ERR_INVALID;
+  return guard(ctx, [&] { *kv = kv_new(ctx, layers, kv_heads, head_dim, capacity, dtype); });
+}
+
+extern "C" void wc_kv_destroy(wc_kv* kv) {
+  if (!kv) return;
+  dfree(kv->K);
+  dfree(kv->V);
+  delete kv;
+}
+
+extern "C" int wc_kv_size(const wc_kv* kv) { return kv ? kv->n : -1; }
+extern "C" int wc_kv_capacity(const wc_kv* kv) { return kv ? kv->cap : -1; }
+
+extern "C" wc_status wc_kv_append(wc_kv* kv, int layer, const float* k, const float* v, int L) {
+  if (!kv || !k || !v || L < 0 || layer < 0 || layer >= kv->layers) return WC_ERR_INVALID;
+  return guard(kv->ctx, [&] {
+    if (kv->n + L > kv->cap) fail(WC_ERR_CAPACITY, "KV cache capacity exceeded");
+    if (L == 0) return;
+    kv_append_kernel<<<grid_for(size_t(L) * kv->Hk * kv->D), 256, 0, kv->ctx->stream>>>(
+        kv->Kl(layer), kv->Vl(layer), kv->dtype, kv->Hk, kv->D, kv->cap, kv->n, k, v, L);
+    check_launch(kv->ctx, "kv_append");
+  });
+}
+
+extern "C" wc_status wc_kv_commit(wc_kv* kv, int L) {
+  if (!kv || L < 0) return WC_ERR_INVALID;
+  return guard(kv->ctx, [&] {
+    if (kv->n + L > kv->cap) fail(WC_ERR_CAPACITY, "KV cache capacity exceeded");
+    kv->n += L;
+  });
+}
+
+extern "C" wc_status wc_kv_trim_to(wc_kv* kv, int n) {
+  if (!kv || n < 0 || n > kv->cap) return WC_ERR_INVALID;
+  kv->n = n;
+  return WC_OK;
+}
+
+namespace {
+void kv_compact_impl(wc_kv* kv, int start, const int* keep_host, int n_keep) {
+  if (start < 0 || n_keep < 0 || start + n_keep > kv->cap) fail(WC_ERR_INVALID, "bad compaction range");
+  for (int i = 0; i < n_keep; ++i) {
+    if (keep_host[i] < i || start + keep_host[i] >= kv->cap || (i && keep_host[i] <= keep_host[i - 1]))
+      fail(WC_ERR_INVALID, "keep list must be increasing, with keep[i] >= i");
+  }
+  bool identity = true;
+  for (int i = 0; i < n_keep; ++i) identity &= keep_host[i] == i;
+  if (!identity && n_keep > 0) {
+    if (n_keep > MAXTREE) fail(WC_ERR_UNSUPPORTED, "keep list longer than 64");
+    int* d_keep = static_cast<int*>(dalloc(sizeof(int) * n_keep));
+    CUDA_TRY(cudaMemcpyAsync(d_keep, keep_host, sizeof(int) * n_keep, cudaMemcpyHostToDevice, kv->ctx->stream));
+    const int slabs = kv->layers * kv->Hk;
+    kv_compact_kernel<<<2 * slabs, 256, size_t(n_keep) * kv->D * sizeof(float), kv->ctx->stream>>>(
+        kv->K, kv->V, kv->dtype, kv->D, kv->cap, slabs, d_keep, n_keep, start);
+    check_launch(kv->ctx, "kv_compact");
+    CUDA_TRY(cudaStreamSynchronize(kv->ctx->stream));
+    dfree(d_keep);
+  }
+  kv->n = start + n_keep;
+}
+}  // namespace
+
+extern "C" wc_status wc_kv_compact(wc_kv* kv, int start, const int* keep, int n_keep) {
+  if (!kv || (!keep && n_keep)) return WC_ERR_INVALID;
+  return guard(kv->ctx, [&] { kv_compact_impl(kv, start, keep, n_keep); });
+}
+
+extern "C" wc_status wc_kv_read(const wc_kv* kv, int layer, int T, float* k, float* v) {
+  if (!kv || !k || !v || layer < 0 || layer >= kv->layers || T < 0 || T > kv->cap) return WC_ERR_INVALID;
+  return guard(kv->ctx, [&] {
+    if (T == 0) return;
+    kv_read_kernel<<<grid_for(size_t(T) * kv->Hk * kv->D), 256, 0, kv->ctx->stream>>>(
+        kv->Kl(layer), kv->Vl(layer), kv->dtype, kv->Hk, kv->D, kv->cap, T, k, v);
+    check_launch(kv->ctx, "kv_read");
+  });
+}
+
+// ============================================================================ models: shared pieces
+
+namespace {
+
+struct Rows {
+  int L = 0;
+  const int* L_dev = nullptr;
+  int L_max = 0;
+  const int* n_dev = nullptr;
+  int n_add = 0;
+  const int* positions = nullptr;
+  const unsigned long long* newmask = nullptr;
+  const uint8_t* mask_full = nullptr;
+  int mask_ld = 0;
+};
+
+struct Stage {
+  std::map<std::string, Staged> t;
+  ~Stage() { clear(); }
+  void clear() {
+    for (auto& kv : t) dfree(kv.second.ptr);
+    t.clear();
+  }
+  const Staged& get(const std::string& name, std::vector<int64_t> shape) const {
+    auto it = t.find(name);
+    if (it == t.end()) fail(WC_ERR_IO, "missing tensor " + name);
+    if (it->second.shape != shape) {
+      std::string s = "tensor " + name + " has shape [";
+      for (size_t i = 0; i < it->second.shape.size(); ++i) s += (i ? "," : "") + std::to_string(it->second.shape[i]);
+      s += "], expected [";
+      for (size_t i = 0; i < shape.size(); ++i) s += (i ? "," : "") + std::to_string(shape[i]);
+      fail(WC_ERR_INVALID, s + "]");
+    }
+    return it->second;
+  }
+  bool has(const std::string& name) const { return t.count(name) > 0; }
+};
+
+void stage_put(wc_ctx* ctx, Stage& stg, const std::string& name, const void* data, int src_dtype, int on_device,
+               const int64_t* shape, int ndim) {
+  if (!data || !shape || ndim <= 0) fail(WC_ERR_INVALID, "bad tensor " + name);
+  Staged s;
+  s.shape.assign(shape, shape + ndim);
+  const int64_t n = s.numel();
+  if (n <= 0) fail(WC_ERR_INVALID, "empty tensor " + name);
+  if (src_dtype == 2) {  // f16 -> f32 on the device
+    void* tmp = dalloc(size_t(n) * 2);
+    CUDA_TRY(cudaMemcpy(tmp, data, size_t(n) * 2, on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice));
+    s.ptr = dalloc(size_t(n) * 4);
+    f16_to_f32_kernel<<<grid_for(size_t(n)), 256, 0, ctx->stream>>>(static_cast<uint16_t*>(tmp),
+                                                                   static_cast<float*>(s.ptr), size_t(n));
+    check_launch(ctx, "f16 convert");
+    CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    dfree(tmp);
+    s.dtype = 0;
+  } else if (src_dtype == 0 || src_dtype == 1) {
+    s.dtype = src_dtype;
+    const size_t bytes = size_t(n) * dtype_size(src_dtype);
+    s.ptr = dalloc(bytes);
+    CUDA_TRY(cudaMemcpy(s.ptr, data, bytes, on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice));
+  } else {
+    fail(WC_ERR_INVALID, "unsupported dtype for " + name);
+  }
+  auto it = stg.t.find(name);
+  if (it != stg.t.end()) dfree(it->second.ptr);
+  stg.t[name] = s;
+}
+
+float* to_f32_vec(wc_ctx* ctx, const Staged& s) {
+  const size_t n = size_t(s.numel());
+  float* out = static_cast<float*>(dalloc(n * 4));
+  convert_kernel<<<grid_for(n), 256, 0, ctx->stream>>>(s.ptr, s.dtype, out, 0, n);
+  check_launch(ctx, "convert");
+  return out;
+}
+
+void* to_dtype(wc_ctx* ctx, const Staged& s, int dtype) {
+  const size_t n = size_t(s.numel());
+  void* out = dalloc(n * dtype_size(dtype));
+  convert_kernel<<<grid_for(n), 256, 0, ctx->stream>>>(s.ptr, s.dtype, out, dtype, n);
+  check_launch(ctx, "convert");
+  return out;
+}
+
+void load_dir_tensors(const std::string& dir, const std::string& only_file,
+                      const std::function<void(const std::string&, const TensorView&)>& put) {
+  std::vector<std::string> files;
+  if (!only_file.empty()) {
+    files.push_back((fs::path(dir) / only_file).string());
+  } else {
+    if (!fs::is_directory(dir)) fail(WC_ERR_IO, "not a directory: " + dir);
+    for (auto& e : fs::directory_iterator(dir))
+      if (e.path().extension() == ".safetensors") files.push_back(e.path().string());
+    std::sort(files.begin(), files.end());
+  }
+  if (files.empty()) fail(WC_ERR_IO, "no .safetensors in " + dir);
+  for (auto& f : files) {
+    const std::string real = fs::is_symlink(f) ? fs::canonical(f).string() : f;
+    SafetensorsFile sf(real);
+    for (auto& kv : sf.tensors()) put(kv.first, kv.second);
+  }
+}
+
+}  // namespace
+
+// ============================================================================ target (Qwen3)
+
+namespace {
+struct TLayer {
+  Lin qkv, o, gu, down;
+  float *in_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+};
+}  // namespace
+
+struct wc_target {
+  wc_ctx* ctx;
+  wc_qwen3_config cfg;
+  int taps[3];
+  int dtype;
+  bool finalized = false;
+  Stage stage;
+  void* embed = nullptr;  // [V][H] in dtype
+  Lin head;
+  float* final_norm = nullptr;
+  std::vector<TLayer> layers;
+  RopeTable* rope = nullptr;
+  // workspace for up to GEMV_MAXL rows
+  float *ws_h = nullptr, *ws_qkv = nullptr, *ws_att = nullptr, *ws_act = nullptr;
+  unsigned long long* ws_keys = nullptr;
+  int* ws_tokens = nullptr;
+  int* ws_pos = nullptr;
+};
+
+namespace {
+
+void target_check_cfg(const wc_qwen3_config& c) {
+  if (c.hidden <= 0 || c.layers <= 0 || c.heads <= 0 || c.kv_heads <= 0 || c.head_dim <= 0 || c.intermediate <= 0 ||
+      c.vocab <= 0)
+    fail(WC_ERR_INVALID, "target config has non-positive sizes");
+  if (c.heads % c.kv_heads) fail(WC_ERR_INVALID, "heads must be a multiple of kv_heads");
+}
+
+void target_set_taps(wc_target* t, const int* taps) {
+  int tp[3];
+  if (taps) {
+    for (int i = 0; i < 3; ++i) tp[i] = taps[i];
+  } else {  // python default_feature_layers / src/core/qwen3.cpp:57
+    tp[0] = 2;
+    tp[1] = t->cfg.layers / 2;
+    tp[2] = t->cfg.layers - 3;
+  }
+  for (int i = 0; i < 3; ++i)
+    if (tp[i] < 0 || tp[i] >= t->cfg.layers) fail(WC_ERR_INVALID, "tap layer index out of range");
+  std::sort(tp, tp + 3);  // taps are emitted in ascending layer order (qwen3.cpp:103-104)
+  if (tp[0] == tp[1] || tp[1] == tp[2]) fail(WC_ERR_INVALID, "tap layers must be distinct");
+  for (int i = 0; i < 3; ++i) t->taps[i] = tp[i];
+}
+
+void target_finalize_impl(wc_target* t) {
+  wc_ctx* ctx = t->ctx;
+  const auto& c = t->cfg;
+  const int H = c.hidden, D = c.head_dim, Hq = c.heads * D, Hkv = c.kv_heads * D, I = c.intermediate;
+  const Stage& s = t->stage;
+  t->embed = to_dtype(ctx, s.get("model.embed_tokens.weight", {c.vocab, H}), t->dtype);
+  t->final_norm = to_f32_vec(ctx, s.get("model.norm.weight", {H}));
+  const bool tied = c.tie_embeddings || !s.has("lm_head.weight");
+  if (tied && t->dtype == WC_F32) {
+    t->head.w = t->embed;
+    t->head.owned = false;
+    t->head.dtype = WC_F32;
+    t->head.N = c.vocab;
+    t->head.Np = c.vocab;
+    t->head.K = H;
+    t->head.Kp = H;
+    t->head.group = 1;
+    if (H % 4) fail(WC_ERR_UNSUPPORTED, "fp32 hidden size must be a multiple of 4");
+  } else {
+    const Staged& hw = tied ? s.get("model.embed_tokens.weight", {c.vocab, H}) : s.get("lm_head.weight", {c.vocab, H});
+    t->head = make_lin(t->dtype, c.vocab, H, 1);
+    lin_put(ctx, t->head, hw, c.vocab, H, 0, 0, 0);
+  }
+  t->layers.resize(c.layers);
+  for (int i = 0; i < c.layers; ++i) {
+    const std::string p = "model.layers." + std::to_string(i) + ".";
+    TLayer& L = t->layers[i];
+    L.qkv = make_lin(t->dtype, Hq + 2 * Hkv, H, 1);
+    lin_put(ctx, L.qkv, s.get(p + "self_attn.q_proj.weight", {Hq, H}), Hq, H, 0, 0, 0);
+    lin_put(ctx, L.qkv, s.get(p + "self_attn.k_proj.weight", {Hkv, H}), Hkv, H, Hq, 0, 0);
+    lin_put(ctx, L.qkv, s.get(p + "self_attn.v_proj.weight", {Hkv, H}), Hkv, H, Hq + Hkv, 0, 0);
+    L.o = make_lin(t->dtype, H, Hq, 1);
+    lin_put(ctx, L.o, s.get(p + "self_attn.o_proj.weight", {H, Hq}), H, Hq, 0, 0, 0);
+    L.gu = make_lin(t->dtype, I, H, 2);
+    lin_put(ctx, L.gu, s.get(p + "mlp.gate_proj.weight", {I, H}), I, H, 0, 0, 0);
+    lin_put(ctx, L.gu, s.get(p + "mlp.up_proj.weight", {I, H}), I, H, 0, 0, 1);
+    L.down = make_lin(t->dtype, H, I, 1);
+    lin_put(ctx, L.down, s.get(p + "mlp.down_proj.weight", {H, I}), H, I, 0, 0, 0);
+    L.in_norm = to_f32_vec(ctx, s.get(p + "input_layernorm.weight", {H}));
+    L.post_norm = to_f32_vec(ctx, s.get(p + "post_attention_layernorm.weight", {H}));
+    L.q_norm = to_f32_vec(ctx, s.get(p + "self_attn.q_norm.weight", {D}));
+    L.k_norm = to_f32_vec(ctx, s.get(p + "self_attn.k_norm.weight", {D}));
+  }
+  t->rope = &rope_table(ctx, D, c.rope_theta, 32768);
+  const int M = GEMV_MAXL;
+  t->ws_h = static_cast<float*>(dalloc(sizeof(float) * M * H));
+  t->ws_qkv = static_cast<float*>(dalloc(sizeof(float) * M * (Hq + 2 * Hkv)));
+  t->ws_att = static_cast<float*>(dalloc(sizeof(float) * M * Hq));
+  t->ws_act = static_cast<float*>(dalloc(sizeof(float) * M * I));
+  t->ws_keys = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * M));
+  t->ws_tokens = static_cast<int*>(dalloc(sizeof(int) * 4096));
+  t->ws_pos = static_cast<int*>(dalloc(sizeof(int) * 4096));
+  CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  t->stage.clear();
+  t->finalized = true;
+}
+
+// The layer stack on h[L][H] in place (rows and prefix from `r`); taps (optional) receive
+// the block outputs of the three tap layers at taps + f * taps_stride.
+void target_layers(wc_target* t, wc_kv* kv, const Rows& r, float* h, float* taps, size_t taps_stride, int* err) {
+  wc_ctx* ctx = t->ctx;
+  const auto& c = t->cfg;
+  const int H = c.hidden, D = c.head_dim, Hq = c.heads * D, Hkv = c.kv_heads * D, I = c.intermediate;
+  const int ld_qkv = Hq + 2 * Hkv;
+  for (int li = 0; li < c.layers; ++li) {
+    const TLayer& Ly = t->layers[li];
+    {
+      GemvParams p = gemv_params();
+      p.L = r.L;
+      p.L_dev = r.L_dev;
+      p.L_max = r.L_max;
+      p.nseg = 1;
+      p.seg[0] = seg_rows(h, H, H, Ly.in_norm);
+      p.eps = c.eps;
+      p.epi = EPI_STORE;
+      p.y = t->ws_qkv;
+      p.ldy = ld_qkv;
+      p.err = err;
+      p.prefetch_next = Ly.o.w;
+      p.prefetch_bytes = (long long)Ly.o.bytes;
+      launch_gemv(ctx, Ly.qkv, p);
+    }
+    {
+      AttnParams a = attn_params();
+      a.qkv = t->ws_qkv;
+      a.ld_qkv = ld_qkv;
+      a.q_norm = Ly.q_norm;
+      a.k_norm = Ly.k_norm;
+      a.eps = c.eps;
+      a.rope = t->rope->ptr;
+      a.max_pos = t->rope->max_pos;
+      a.positions = r.positions;
+      a.n_dev = r.n_dev;
+      a.n_add = r.n_add;
+      a.L = r.L;
+      a.L_dev = r.L_dev;
+      a.L_max = r.L_max;
+      a.Kc = kv->Kl(li);
+      a.Vc = kv->Vl(li);
+      a.kv_dtype = kv->dtype;
+      a.stride_h = (long long)kv->cap * D;
+      a.stride_p = D;
+      a.cap = kv->cap;
+      a.H = c.heads;
+      a.Hk = c.kv_heads;
+      a.D = D;
+      a.newmask = r.newmask;
+      a.mask_full = r.mask_full;
+      a.mask_ld = r.mask_ld;
+      a.scale = 1.f / std::sqrt(float(D));
+      a.out = t->ws_att;
+      a.ld_out = Hq;
+      a.write_cache = 1;
+      a.err = err;
+      launch_attention(ctx, a);
+    }
+    {
+      GemvParams p = gemv_params();
+      p.L = r.L;
+      p.L_dev = r.L_dev;
+      p.L_max = r.L_max;
+      p.nseg = 1;
+      p.seg[0] = seg_rows(t->ws_att, Hq, Hq);
+      p.epi = EPI_ADD;
+      p.y = h;
+      p.ldy = H;
+      p.base = h;
+      p.ldb = H;
+      p.err = err;
+      p.prefetch_next = Ly.gu.w;
+      p.prefetch_bytes = std::min<long long>((long long)Ly.gu.bytes, 64ll << 20);
+      launch_gemv(ctx, Ly.o, p);
+    }
+    {
+      GemvParams p = gemv_params();
+      p.L = r.L;
+      p.L_dev = r.L_dev;
+      p.L_max = r.L_max;
+      p.nseg = 1;
+      p.seg[0] = seg_rows(h, H, H, Ly.post_norm);
+      p.eps = c.eps;
+      p.epi = EPI_SWIGLU;
+      p.y = t->ws_act;
+      p.ldy = I;
+      p.err = err;
+      p.prefetch_next = Ly.down.w;
+      p.prefetch_bytes = (long long)Ly.down.bytes;
+      launch_gemv(ctx, Ly.gu, p);
+    }
+    {
+      GemvParams p = gemv_params();
+      p.L = r.L;
+      p.L_dev = r.L_dev;
+      p.L_max = r.L_max;
+      p.nseg = 1;
+      p.seg[0] = seg_rows(t->ws_act, I, I);
+      p.epi = EPI_ADD;
+      p.y = h;
+      p.ldy = H;
+      p.base = h;
+      p.ldb = H;
+      p.err = err;
+      for (int f = 0; f < 3; ++f)
+        if (taps && t->taps[f] == li) {
+          p.y2 = taps + size_t(f) * taps_stride;
+          p.ldy2 = H;
+        }
+      if (li + 1 < c.layers) {
+        p.prefetch_next = t->layers[li + 1].qkv.w;
+        p.prefetch_bytes = (long long)t->layers[li + 1].qkv.bytes;
+      }
+      launch_gemv(ctx, Ly.down, p);
+    }
+  }
+}
+
+// Final norm + head on rows [0, L) of h: argmax keys and (optionally) logits [L][V].
+void target_head(wc_target* t, const float* h, int L, const int* L_dev, int L_max, unsigned long long* keys,
+                 float* logits, int* err) {
+  GemvParams p = gemv_params();
+  p.L = L;
+  p.L_dev = L_dev;
+  p.L_max = L_max;
+  p.nseg = 1;
+  p.seg[0] = seg_rows(h, t->cfg.hidden, t->cfg.hidden, t->final_norm);
+  p.eps = t->cfg.eps;
+  p.epi = EPI_ARGMAX;
+  p.y = logits;
+  p.ldy = t->cfg.vocab;
+  p.keys = keys;
+  p.err = err;
+  launch_gemv(t->ctx, t->head, p);
+}
+
+}  // namespace
+
+extern "C" wc_status wc_target_create(wc_ctx* ctx, const wc_qwen3_config* cfg, const int* taps, int dtype,
+                                      wc_target** out) {
+  if (!ctx || !cfg || !out) return WC_ERR_INVALID;
+  return guard(ctx, [&] {
+    if (dtype != WC_F32 && dtype != WC_BF16) fail(WC_ERR_INVALID, "dtype must be WC_F32 or WC_BF16");
+    target_check_cfg(*cfg);
+    auto t = std::make_unique<wc_target>();
+    t->ctx = ctx;
+    t->cfg = *cfg;
+    t->dtype = dtype;
+    target_set_taps(t.get(), taps);
+    *out = t.release();
+  });
+}
+
+extern "C" wc_status wc_target_set_tensor(wc_target* t, const char* name, const void* data, int src_dtype,
+                                          int on_device, const int64_t* shape, int ndim) {
+  if (!t || !name) return WC_ERR_INVALID;
+  return guard(t->ctx, [&] {
+    if (t->finalized) fail(WC_ERR_INVALID, "target already finalized");
+    stage_put(t->ctx, t->stage, name, data, src_dtype, on_device, shape, ndim);
+  });
+}
+
+extern "C" wc_status wc_target_finalize(wc_target* t) {
+  if (!t) return WC_ERR_INVALID;
+  return guard(t->ctx, [&] {
+    if (t->finalized) fail(WC_ERR_INVALID, "target already finalized");
+    target_finalize_impl(t);
+  });
+}
+
+namespace {
+wc_qwen3_config qwen3_config_from_json(const std::string& path) {
+  const JsonValue j = json_parse(read_file(path));
+  wc_qwen3_config c{};
+  c.hidden = int(j.at("hidden_size").num);
+  c.layers = int(j.at("num_hidden_layers").num);
+  c.heads = int(j.at("num_attention_heads").num);
+  c.kv_heads = int(j.at("num_key_value_heads").num);
+  c.head_dim = int(j.number_or("head_dim", double(c.hidden / std::max(1, c.heads))));
+  c.intermediate = int(j.at("intermediate_size").num);
+  c.vocab = int(j.at("vocab_size").num);
+  c.eps = float(j.number_or("rms_norm_eps", 1e-6));
+  c.rope_theta = float(j.number_or("rope_theta", 1e6));
+  c.tie_embeddings = j.bool_or("tie_word_embeddings", false) ? 1 : 0;
+  return c;
+}
+}  // namespace
+
+extern "C" wc_status wc_target_load(wc_ctx* ctx, const char* dir, const int* taps, int dtype, wc_target** out) {
+  if (!ctx || !dir || !out) return WC_ERR_INVALID;
+  return guard(ctx, [&] {
+    const wc_qwen3_config cfg = qwen3_config_from_json((fs::path(dir) / "config.json").string());
+    if (dtype != WC_F32 && dtype != WC_BF16) fail(WC_ERR_INVALID, "dtype must be WC_F32 or WC_BF16");
+    target_check_cfg(cfg);
+    auto t = std::make_unique<wc_target>();
+    t->ctx = ctx;
+    t->cfg = cfg;
+    t->dtype = dtype;
+    target_set_taps(t.get(), taps);
+    load_dir_tensors(dir, "", [&](const std::string& name, const TensorView& v) {
+      const int dt = src_dtype_code(v.dtype);
+      if (dt < 0) fail(WC_ERR_IO, "unsupported dtype " + v.dtype + " for " + name);
+      stage_put(ctx, t->stage, name, v.data, dt, 0, v.shape.data(), int(v.shape.size()));
+    });
+    target_finalize_impl(t.get());
+    *out = t.release();
+  });
+}
+
+extern "C" void wc_target_destroy(wc_target* t) {
+  if (!t) return;
+  cudaStreamSynchronize(t->ctx->stream);
+  dfree(t->embed);
+  free_lin(t->head);
+  dfree(t->final_norm);
+  for (auto& L : t->layers) {
+    free_lin(L.qkv);
+    free_lin(L.o);
+    free_lin(L.gu);
+    free_lin(L.down);
+    dfree(L.in_norm);
+    dfree(L.post_norm);
+    dfree(L.q_norm);
+    dfree(L.k_norm);
+  }
+  dfree(t->ws_h);
+  dfree(t->ws_qkv);
+  dfree(t->ws_att);
+  dfree(t->ws_act);
+  dfree(t->ws_keys);
+  dfree(t->ws_tokens);
+  dfree(t->ws_pos);
+  delete t;
+}
+
+extern "C" wc_status wc_target_config(const wc_target* t, wc_qwen3_config* cfg, int* taps3, int* dtype) {
+  if (!t) return WC_ERR_INVALID;
+  if (cfg) *cfg = t->cfg;
+  if (taps3)
+    for (int i = 0; i < 3; ++i) taps3[i] = t->taps[i];
+  if (dtype) *dtype = t->dtype;
+  return WC_OK;
+}
+
+extern "C" wc_status wc_target_make_cache(wc_target* t, int capacity, wc_kv** kv) {
+  if (!t || !kv) return WC_ERR_INVALID;
+  return guard(t->ctx, [&] {
+    *kv = kv_new(t->ctx, t->cfg.layers, t->cfg.kv_heads, t->cfg.head_dim, capacity, t->dtype);
+  });
+}
+
+extern "C" wc_status wc_target_forward(wc_target* t, wc_kv* cache, const int* tokens, int L, const int* positions,
+                                       const uint8_t* mask, int logits_from, float* logits, int* argmax,
+                                       float* taps) {
+  if (!t || !cache || !tokens || L <= 0) return WC_ERR_INVALID;
+  return guard(t->ctx, [&] {
+    if (!t->finalized) fail(WC_ERR_INVALID, "target not finalized");
+    const auto& c = t->cfg;
+    if (cache->layers != c.layers || cache->Hk != c.kv_heads || cache->D != c.head_dim || cache->dtype != t->dtype)
+      fail(WC_ERR_INVALID, "cache does not match the target");
+    if (logits_from < 0 || logits_from > L) fail(WC_ERR_INVALID, "logits_from out of range");
+    const int prefix = cache->n;
+    if (prefix + L > cache->cap) fail(WC_ERR_CAPACITY, "KV cache capacity exceeded");
+    wc_ctx* ctx = t->ctx;
+    const int H = c.hidden;
+    const size_t taps_stride = size_t(L) * H;
+    for (int r0 = 0; r0 < L; r0 += GEMV_MAXL) {
+      const int rows = std::min(GEMV_MAXL, L - r0);
+      embed_rows_kernel<<<rows, 256, 0, ctx->stream>>>(t->embed, t->dtype, c.vocab, H, tokens + r0, rows, nullptr,
+                                                       t->ws_h, nullptr, nullptr, 0, ctx->d_err);
+      check_launch(ctx, "embed");
+      Rows r;
+      r.L = rows;
+      r.L_max = rows;
+      r.n_add = prefix + r0;
+      r.positions = positions ? positions + r0 : nullptr;
+      r.mask_full = mask ? mask + size_t(r0) * (prefix + L) : nullptr;
+      r.mask_ld = prefix + L;
+      target_layers(t, cache, r, t->ws_h, taps ? taps + size_t(r0) * H : nullptr, taps_stride, ctx->d_err);
+      const int h0 = std::max(logits_from, r0);
+      if (h0 < r0 + rows && (logits || argmax)) {
+        const int hr = r0 + rows - h0;
+        CUDA_TRY(cudaMemsetAsync(t->ws_keys, 0, sizeof(unsigned long long) * GEMV_MAXL, ctx->stream));
+        target_head(t, t->ws_h + size_t(h0 - r0) * H, hr, nullptr, hr, t->ws_keys,
+                    logits ? logits + size_t(h0 - logits_from) * c.vocab : nullptr, ctx->d_err);
+        if (argmax) {
+          keys_to_index_kernel<<<1, 32, 0, ctx->stream>>>(t->ws_keys, hr, nullptr, argmax + (h0 - logits_from));
+          check_launch(ctx, "keys");
+        }
+      }
+    }
+    cache->n = prefix + L;
+  });
+}
+
+// ============================================================================ drafter (EAGLE-3)
+
+namespace {
+struct DLayer {
+  Lin qkv, o, gu, down;
+  float *in_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *aux_norm = nullptr;
+};
+}  // namespace
+
+struct wc_drafter {
+  wc_ctx* ctx;
+  wc_drafter_config cfg;
+  int dtype;
+  bool finalized = false;
+  Stage stage;
+  void* embed = nullptr;
+  Lin fc;
+  float* feature_norms[GEMV_MAXSEG] = {nullptr, nullptr, nullptr};
+  std::vector<DLayer> layers;
+  float* norm = nullptr;
+  Lin head;
+  int* vocab_map = nullptr;  // restricted head row -> token id
+  int head_rows = 0;
+  RopeTable* rope = nullptr;
+  float *ws_h = nullptr, *ws_qkv = nullptr, *ws_att = nullptr, *ws_act = nullptr, *ws_out = nullptr;
+  unsigned long long* ws_keys = nullptr;
+};
+
+namespace {
+
+void drafter_check_cfg(const wc_drafter_config& c) {
+  if (c.hidden <= 0 || c.layers <= 0 || c.heads <= 0 || c.kv_heads <= 0 || c.head_dim <= 0 || c.intermediate <= 0 ||
+      c.vocab <= 0 || c.target_hidden <= 0)
+    fail(WC_ERR_INVALID, "drafter config has non-positive sizes");
+  if (c.num_features < 1 || c.num_features > GEMV_MAXSEG)
+    fail(WC_ERR_UNSUPPORTED, "drafter num_features must be 1..3");
+  if (c.heads % c.kv_heads) fail(WC_ERR_INVALID, "heads must be a multiple of kv_heads");
+}
+
+void drafter_finalize_impl(wc_drafter* d) {
+  wc_ctx* ctx = d->ctx;
+  const auto& c = d->cfg;
+  const int H = c.hidden, D = c.head_dim, Hq = c.heads * D, Hkv = c.kv_heads * D, I = c.intermediate;
+  const Stage& s = d->stage;
+  d->embed = to_dtype(ctx, s.get("embed_tokens.weight", {c.vocab, H}), d->dtype);
+  const int F = c.num_features, Ht = c.target_hidden;
+  d->fc = make_lin(d->dtype, H, F * Ht, 1);
+  lin_put(ctx, d->fc, s.get("fc.weight", {H, F * Ht}), H, F * Ht, 0, 0, 0);
+  if (c.feature_norm)
+    for (int f = 0; f < F; ++f)
+      d->feature_norms[f] = to_f32_vec(ctx, s.get("feature_norms." + std::to_string(f) + ".weight", {Ht}));
+  d->layers.resize(c.layers);
+  for (int i = 0; i < c.layers; ++i) {
+    const std::string p = "layers." + std::to_string(i) + ".";
+    DLayer& L = d->layers[i];
+    const bool aux = i == 0;  // layer 0 is dual-stream (drafter.cpp:64-70)
+    L.qkv = make_lin(d->dtype, Hq + 2 * Hkv, aux ? 2 * H : H, 1);
+    lin_put(ctx, L.qkv, s.get(p + "self_attn.q_proj.weight", {Hq, H}), Hq, H, 0, 0, 0);
+    lin_put(ctx, L.qkv, s.get(p + "self_attn.k_proj.weight", {Hkv, H}), Hkv, H, Hq, 0, 0);
+    lin_put(ctx, L.qkv, s.get(p + "self_attn.v_proj.weight", {Hkv, H}), Hkv, H, Hq + Hkv, 0, 0);
+    if (aux) {
+      lin_put(ctx, L.qkv, s.get(p + "self_attn.aux_q.weight", {Hq, H}), Hq, H, 0, H, 0);
+      lin_put(ctx, L.qkv, s.get(p + "self_attn.aux_k.weight", {Hkv, H}), Hkv, H, Hq, H, 0);
+      lin_put(ctx, L.qkv, s.get(p + "self_attn.aux_v.weight", {Hkv, H}), Hkv, H, Hq + Hkv, H, 0);
+      L.aux_norm = to_f32_vec(ctx, s.get(p + "aux_norm.weight", {H}));
+    }
+    L.o = make_lin(d->dtype, H, Hq, 1);
+    lin_put(ctx, L.o, s.get(p + "self_attn.o_proj.weight", {H, Hq}), H, Hq, 0, 0, 0);
+    L.gu = make_lin(d->dtype, I, H, 2);
+    lin_put(ctx, L.gu, s.get(p + "mlp.gate_proj.weight", {I, H}), I, H, 0, 0, 0);
+    lin_put(ctx, L.gu, s.get(p + "mlp.up_proj.weight", {I, H}), I, H, 0, 0, 1);
+    L.down = make_lin(d->dtype, H, I, 1);
+    lin_put(ctx, L.down, s.get(p + "mlp.down_proj.weight", {H, I}), H, I, 0, 0, 0);
+    L.in_norm = to_f32_vec(ctx, s.get(p + "input_layernorm.weight", {H}));
+    L.post_norm = to_f32_vec(ctx, s.get(p + "post_attention_layernorm.weight", {H}));
+    L.q_norm = to_f32_vec(ctx, s.get(p + "self_attn.q_norm.weight", {D}));
+    L.k_norm = to_f32_vec(ctx, s.get(p + "self_attn.k_norm.weight", {D}));
+  }
+  d->norm = to_f32_vec(ctx, s.get("norm.weight", {H}));
+  d->head = make_lin(d->dtype, c.vocab, H, 1);
+  lin_put(ctx, d->head, s.get("lm_head.weight", {c.vocab, H}), c.vocab, H, 0, 0, 0);
+  d->head_rows = c.vocab;
+  d->rope = &rope_table(ctx, D, c.rope_theta, 32768);
+  const int M = GEMV_MAXL;
+  d->ws_h = static_cast<float*>(dalloc(sizeof(float) * M * H));
+  d->ws_out = static_cast<float*>(dalloc(sizeof(float) * M * H));
+  d->ws_qkv = static_cast<float*>(dalloc(sizeof(float) * M * (Hq + 2 * Hkv)));
+  d->ws_att = static_cast<float*>(dalloc(sizeof(float) * M * Hq));
+  d->ws_act = static_cast<float*>(dalloc(sizeof(float) * M * I));
+  d->ws_keys = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * M));
+  CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  d->stage.clear();
+  d->finalized = true;
+}
+
+// Drafter layer stack (drafter.cpp:91-136): feat [L][H] is the residual stream input,
+// layer 0 adds W_aux . aux_norm(embed(token)); the result lands in h_out [L][H].
+void drafter_layers(wc_drafter* d, wc_kv* kv, const Rows& r, const float* feat, const TokenSrc& tok, float* h_out,
+                    int* err) {
+  wc_ctx* ctx = d->ctx;
+  const auto& c = d->cfg;
+  const int H = c.hidden, D = c.head_dim, Hq = c.heads * D, Hkv = c.kv_heads * D, I = c.intermediate;
+  const int ld_qkv = Hq + 2 * Hkv;
+  for (int li = 0; li < c.layers; ++li) {
+    const DLayer& Ly = d->layers[li];
+    const float* hin = li == 0 ? feat : h_out;
+    {
+      GemvParams p = gemv_params();
+      p.L = r.L;
+      p.L_dev = r.L_dev;
+      p.L_max = r.L_max;
+      p.nseg = 1;
+      p.seg[0] = seg_rows(hin, H, H, Ly.in_norm);
+      if (Ly.aux_norm) {
+        p.nseg = 2;
+        p.seg[1] = seg_embed(d->embed, d->dtype, H, Ly.aux_norm);
+        p.tok = tok;
+        p.tok.vocab = c.vocab;
+      }
+      p.eps = c.eps;
+      p.epi = EPI_STORE;
+      p.y = d->ws_qkv;
+      p.ldy = ld_qkv;
+      p.err = err;
+      p.prefetch_next = Ly.o.w;
+      p.prefetch_bytes = (long long)Ly.o.bytes;
+      launch_gemv(ctx, Ly.qkv, p);
+    }
+    {
+      AttnParams a = attn_params();
+      a.qkv = d->ws_qkv;
+      a.ld_qkv = ld_qkv;
+      a.q_norm = Ly.q_norm;
+      a.k_norm = Ly.k_norm;
+      a.eps = c.eps;
+      a.rope = d->rope->ptr;
+      a.max_pos = d->rope->max_pos;
+      a.positions = r.positions;
+      a.n_dev = r.n_dev;
+      a.n_add = r.n_add;
+      a.L = r.L;
+      a.L_dev = r.L_dev;
+      a.L_max = r.L_max;
+      a.Kc = kv->Kl(li);
+      a.Vc = kv->Vl(li);
+      a.kv_dtype = kv->dtype;
+      a.stride_h = (long long)kv->cap * D;
+      a.stride_p = D;
+      a.cap = kv->cap;
+      a.H = c.heads;
+      a.Hk = c.kv_heads;
+      a.D = D;
+      a.newmask = r.newmask;
+      a.window = c.window;
+      a.mask_full = r.mask_full;
+      a.mask_ld = r.mask_ld;
+      a.scale = 1.f / std::sqrt(float(D));
+      a.out = d->ws_att;
+      a.ld_out = Hq;
+      a.write_cache = 1;
+      a.err = err;
+      launch_attention(ctx, a);
+    }
+    {
+      GemvParams p = gemv_params();
+      p.L = r.L;
+      p.L_dev = r.L_dev;
+      p.L_max = r.L_max;
+      p.nseg = 1;
+      p.seg[0] = seg_rows(d->ws_att, Hq, Hq);
+      p.epi = EPI_ADD;
+      p.y = h_out;
+      p.ldy = H;
+      p.base = hin;
+      p.ldb = H;
+      p.err = err;
+      p.prefetch_next = Ly.gu.w;
+      p.prefetch_bytes = std::min<long long>((long long)Ly.gu.bytes, 64ll << 20);
+      launch_gemv(ctx, Ly.o, p);
+    }
+    {
+      GemvParams p = gemv_params();
+      p.L = r.L;
+      p.L_dev = r.L_dev;
+      p.L_max = r.L_max;
+      p.nseg = 1;
+      p.seg[0] = seg_rows(h_out, H, H, Ly.post_norm);
+      p.eps = c.eps;
+      p.epi = EPI_SWIGLU;
+      p.y = d->ws_act;
+      p.ldy = I;
+      p.err = err;
+      p.prefetch_next = Ly.down.w;
+      p.prefetch_bytes = (long long)Ly.down.bytes;
+      launch_gemv(ctx, Ly.gu, p);
+    }
+    {
+      GemvParams p = gemv_params();
+      p.L = r.L;
+      p.L_dev = r.L_dev;
+      p.L_max = r.L_max;
+      p.nseg = 1;
+      p.seg[0] = seg_rows(d->ws_act, I, I);
+      p.epi = EPI_ADD;
+      p.y = h_out;
+      p.ldy = H;
+      p.base = h_out;
+      p.ldb = H;
+      p.err = err;
+      launch_gemv(ctx, Ly.down, p);
+    }
+  }
+}
+
+// fuse (drafter.cpp:75-89): per-tap RMSNorm, concatenated, through fc.
+void drafter_fuse_impl(wc_drafter* d, const float* taps, size_t tap_stride, int ld, int L, const int* L_dev, int L_max,
+                       float* g, int* err) {
+  const auto& c = d->cfg;
+  GemvParams p = gemv_params();
+  p.L = L;
+  p.L_dev = L_dev;
+  p.L_max = L_max;
+  p.nseg = c.num_features;
+  for (int f = 0; f < c.num_features; ++f)
+    p.seg[f] = seg_rows(taps + f * tap_stride, ld, c.target_hidden, c.feature_norm ? d->feature_norms[f] : nullptr);
+  p.eps = c.eps;
+  p.epi = EPI_STORE;
+  p.y = g;
+  p.ldy = c.hidden;
+  p.err = err;
+  launch_gemv(d->ctx, d->fc, p);
+}
+
+// head over `rows` rows of x (already normalised unless norm_w is given)
+void drafter_head(wc_drafter* d, const float* x, int rows, const float* norm_w, float* write_back,
+                  unsigned long long* keys, float* logits, int* err) {
+  GemvParams p = gemv_params();
+  p.L = rows;
+  p.L_max = rows;
+  p.nseg = 1;
+  p.seg[0] = seg_rows(x, d->cfg.hidden, d->cfg.hidden, norm_w, write_back, d->cfg.hidden);
+  p.eps = d->cfg.eps;
+  p.epi = EPI_ARGMAX;
+  p.y = logits;
+  p.ldy = d->head_rows;
+  p.keys = keys;
+  p.err = err;
+  launch_gemv(d->ctx, d->head, p);
+}
+
+wc_drafter_config drafter_config_from_json(const std::string& path) {
+  const JsonValue j = json_parse(read_file(path));
+  wc_drafter_config c{};
+  c.hidden = int(j.at("hidden_size").num);
+  c.layers = int(j.at("num_layers").num);
+  c.heads = int(j.at("num_heads").num);
+  c.kv_heads = int(j.at("num_kv_heads").num);
+  c.head_dim = int(j.at("head_dim").num);
+  c.intermediate = int(j.at("intermediate_size").num);
+  c.vocab = int(j.at("vocab_size").num);
+  c.target_hidden = int(j.at("target_hidden_size").num);
+  c.num_features = int(j.number_or("num_features", 3));
+  c.eps = float(j.number_or("rms_norm_eps", 1e-6));
+  c.rope_theta = float(j.number_or("rope_theta", 1e6));
+  // drafter.cpp:36, 41 and drafter.py:55-63 reject these configurations
+  if (j.str_or("residual", "feature") != "feature")
+    fail(WC_ERR_UNSUPPORTED, "unsupported drafter mode in " + path);
+  if (j.number_or("lowrank_rank", 0) != 0) fail(WC_ERR_UNSUPPORTED, "unsupported drafter configuration in " + path);
+  c.post_norm = j.bool_or("post_norm", true) ? 1 : 0;
+  c.feature_norm = j.bool_or("feature_norm", true) ? 1 : 0;
+  c.window = int(j.number_or("window", 0));
+  return c;
+}
+
+}  // namespace
+
+extern "C" wc_status wc_drafter_create(wc_ctx* ctx, const wc_drafter_config* cfg, int dtype, wc_drafter** out) {
+  if (!ctx || !cfg || !out) return WC_ERR_INVALID;
+  return guard(ctx, [&] {
+    if (dtype != WC_F32 && dtype != WC_BF16) fail(WC_ERR_INVALID, "dtype must be WC_F32 or WC_BF16");
+    drafter_check_cfg(*cfg);
+    auto d = std::make_unique<wc_drafter>();
+    d->ctx = ctx;
+    d->cfg = *cfg;
+    d->dtype = dtype;
+    *out = d.release();
+  });
+}
+
+extern "C" wc_status wc_drafter_set_tensor(wc_drafter* d, const char* name, const void* data, int src_dtype,
+                                           int on_device, const int64_t* shape, int ndim) {
+  if (!d || !name) return WC_ERR_INVALID;
+  return guard(d->ctx, [&] {
+    if (d->finalized) fail(WC_ERR_INVALID, "drafter already finalized");
+    stage_put(d->ctx, d->stage, name, data, src_dtype, on_device, shape, ndim);
+  });
+}
+
+extern "C" wc_status wc_drafter_finalize(wc_drafter* d) {
+  if (!d) return WC_ERR_INVALID;
+  return guard(d->ctx, [&] {
+    if (d->finalized) fail(WC_ERR_INVALID, "drafter already finalized");
+    drafter_finalize_impl(d);
+  });
+}
+
+extern "C" wc_status wc_drafter_load(wc_ctx* ctx, const char* dir, int dtype, wc_drafter** out) {
+  if (!ctx || !dir || !out) return WC_ERR_INVALID;
+  return guard(ctx, [&] {
+    const wc_drafter_config cfg = drafter_config_from_json((fs::path(dir) / "config.json").string());
+    if (dtype != WC_F32 && dtype != WC_BF16) fail(WC_ERR_INVALID, "dtype must be WC_F32 or WC_BF16");
+    drafter_check_cfg(cfg);
+    auto d = std::make_unique<wc_drafter>();
+    d->ctx = ctx;
+    d->cfg = cfg;
+    d->dtype = dtype;
+    load_dir_tensors(dir, "model.safetensors", [&](const std::string& name, const TensorView& v) {
+      const int dt = src_dtype_code(v.dtype);
+      if (dt < 0) fail(WC_ERR_IO, "unsupported dtype " + v.dtype + " for " + name);
+      stage_put(ctx, d->stage, name, v.data, dt, 0, v.shape.data(), int(v.shape.size()));
+    });
+    drafter_finalize_impl(d.get());
+    *out = d.release();
+  });
+}
+
+extern "C" void wc_drafter_destroy(wc_drafter* d) {
+  if (!d) return;
+  cudaStreamSynchronize(d->ctx->stream);
+  dfree(d->embed);
+  free_lin(d->fc);
+  for (auto* f : d->feature_norms) dfree(f);
+  for (auto& L : d->layers) {
+    free_lin(L.qkv);
+    free_lin(L.o);
+    free_lin(L.gu);
+    free_lin(L.down);
+    dfree(L.in_norm);
+    dfree(L.post_norm);
+    dfree(L.q_norm);
+    dfree(L.k_norm);
+    dfree(L.aux_norm);
+  }
+  dfree(d->norm);
+  free_lin(d->head);
+  dfree(d->vocab_map);
+  dfree(d->ws_h);
+  dfree(d->ws_out);
+  dfree(d->ws_qkv);
+  dfree(d->ws_att);
+  dfree(d->ws_act);
+  dfree(d->ws_keys);
+  delete d;
+}
+
+extern "C" wc_status wc_drafter_config_get(const wc_drafter* d, wc_drafter_config* cfg, int* dtype, int* head_rows) {
+  if (!d) return WC_ERR_INVALID;
+  if (cfg) *cfg = d->cfg;
+  if (dtype) *dtype = d->dtype;
+  if (head_rows) *head_rows = d->head_rows;
+  return WC_OK;
+}
+
+extern "C" wc_status wc_drafter_restrict_vocab(wc_drafter* d, const int* ids, int n) {
+  if (!d || !ids || n <= 0) return WC_ERR_INVALID;
+  return guard(d->ctx, [&] {
+    if (!d->finalized) fail(WC_ERR_INVALID, "drafter not finalized");
+    if (d->vocab_map) fail(WC_ERR_INVALID, "drafter vocabulary is already restricted");
+    for (int i = 0; i < n; ++i)
+      if (ids[i] < 0 || ids[i] >= d->cfg.vocab) fail(WC_ERR_INVALID, "vocabulary id out of range");
+    wc_ctx* ctx = d->ctx;
+    int* map = static_cast<int*>(dalloc(sizeof(int) * n));
+    CUDA_TRY(cudaMemcpy(map, ids, sizeof(int) * n, cudaMemcpyHostToDevice));
+    Lin nh;
+    if (d->dtype == WC_BF16) {
+      nh = make_lin(WC_BF16, n, d->cfg.hidden, 1);
+      const int KT = nh.Kp / 16;
+      gather_tiled_rows_kernel<<<grid_for(size_t(nh.Np) * nh.Kp), 256, 0, ctx->stream>>>(
+          static_cast<const uint16_t*>(d->head.w), KT, map, n, static_cast<uint16_t*>(nh.w));
+    } else {
+      nh = make_lin(WC_F32, n, d->cfg.hidden, 1);
+      gather_rows_f32_kernel<<<grid_for(size_t(n) * nh.Kp), 256, 0, ctx->stream>>>(
+          static_cast<const float*>(d->head.w), nh.Kp, map, n, static_cast<float*>(nh.w));
+    }
+    check_launch(ctx, "restrict_vocab");
+    CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    free_lin(d->head);  // the full head is dropped, as in drafter.py:217-229
+    d->head = nh;
+    d->vocab_map = map;
+    d->head_rows = n;
+  });
+}
+
+extern "C" wc_status wc_drafter_make_cache(wc_drafter* d, int capacity, wc_kv** kv) {
+  if (!d || !kv) return WC_ERR_INVALID;
+  return guard(d->ctx, [&] {
+    *kv = kv_new(d->ctx, d->cfg.layers, d->cfg.kv_heads, d->cfg.head_dim, capacity, d->dtype);
+  });
+}
+
+extern "C" wc_status wc_drafter_fuse(wc_drafter* d, const float* taps, int L, float* g) {
+  if (!d || !taps || !g || L <= 0) return WC_ERR_INVALID;
+  return guard(d->ctx, [&] {
+    const size_t stride = size_t(L) * d->cfg.target_hidden;
+    for (int r0 = 0; r0 < L; r0 += GEMV_MAXL) {
+      const int rows = std::min(GEMV_MAXL, L - r0);
+      drafter_fuse_impl(d, taps + size_t(r0) * d->cfg.target_hidden, stride, d->cfg.target_hidden, rows, nullptr,
+                        rows, g + size_t(r0) * d->cfg.hidden, d->ctx->d_err);
+    }
+  });
+}
+
+extern "C" wc_status wc_drafter_forward(wc_drafter* d, wc_kv* cache, const int* tokens, int L, const float* feat,
+                                        const int* positions, const uint8_t* mask, float* hidden, float* out) {
+  if (!d || !cache || !tokens || !feat || L <= 0) return WC_ERR_INVALID;
+  return guard(d->ctx, [&] {
+    const auto& c = d->cfg;
+    if (cache->layers != c.layers || cache->Hk != c.kv_heads || cache->D != c.head_dim || cache->dtype != d->dtype)
+      fail(WC_ERR_INVALID, "cache does not match the drafter");
+    const int prefix = cache->n;
+    if (prefix + L > cache->cap) fail(WC_ERR_CAPACITY, "KV cache capacity exceeded");
+    wc_ctx* ctx = d->ctx;
+    const int H = c.hidden;
+    for (int r0 = 0; r0 < L; r0 += GEMV_MAXL) {
+      const int rows = std::min(GEMV_MAXL, L - r0);
+      Rows r;
+      r.L = rows;
+      r.L_max = rows;
+      r.n_add = prefix + r0;
+      r.positions = positions ? positions + r0 : nullptr;
+      r.mask_full = mask ? mask + size_t(r0) * (prefix + L) : nullptr;
+      r.mask_ld = prefix + L;
+      TokenSrc tok;
+      std::memset(&tok, 0, sizeof(tok));
+      tok.tokens = tokens + r0;
+      tok.vocab = c.vocab;
+      drafter_layers(d, cache, r, feat + size_t(r0) * H, tok, d->ws_h, ctx->d_err);
+      if (hidden) CUDA_TRY(cudaMemcpyAsync(hidden + size_t(r0) * H, d->ws_h, sizeof(float) * rows * H,
+                                           cudaMemcpyDeviceToDevice, ctx->stream));
+      if (out) {
+        rmsnorm_rows_kernel<<<rows, 256, 0, ctx->stream>>>(d->ws_h, out + size_t(r0) * H, H, d->norm, c.eps);
+        check_launch(ctx, "rmsnorm");
+      }
+    }
+    cache->n = prefix + L;
+  });
+}
+
+extern "C" wc_status wc_drafter_logits(wc_drafter* d, const float* out, int rows, float* z) {
+  if (!d || !out || !z || rows <= 0) return WC_ERR_INVALID;
+  return guard(d->ctx, [&] {
+    for (int r0 = 0; r0 < rows; r0 += GEMV_MAXL) {
+      const int n = std::min(GEMV_MAXL, rows - r0);
+      CUDA_TRY(cudaMemsetAsync(d->ws_keys, 0, sizeof(unsigned long long) * GEMV_MAXL, d->ctx->stream));
+      drafter_head(d, out + size_t(r0) * d->cfg.hidden, n, nullptr, nullptr, d->ws_keys, z + size_t(r0) * d->head_rows,
+                   d->ctx->d_err);
+    }
+  });
+}
+
+extern "C" wc_status wc_drafter_head_argmax(wc_drafter* d, const float* out, int rows, int* token) {
+  if (!d || !out || !token || rows <= 0) return WC_ERR_INVALID;
+  return guard(d->ctx, [&] {
+    for (int r0 = 0; r0 < rows; r0 += GEMV_MAXL) {
+      const int n = std::min(GEMV_MAXL, rows - r0);
+      CUDA_TRY(cudaMemsetAsync(d->ws_keys, 0, sizeof(unsigned long long) * GEMV_MAXL, d->ctx->stream));
+      drafter_head(d, out + size_t(r0) * d->cfg.hidden, n, nullptr, nullptr, d->ws_keys, nullptr, d->ctx->d_err);
+      keys_to_index_kernel<<<1, 32, 0, d->ctx->stream>>>(d->ws_keys, n, d->vocab_map, token + r0);
+      check_launch(d->ctx, "keys");
+    }
+  });
+}
+
+// ============================================================================ decoder
+
+struct wc_decoder {
+  wc_ctx* ctx = nullptr;
+  wc_target* t = nullptr;
+  wc_drafter* d = nullptr;
+  int max_ctx = 0, max_k = 0;
+  wc_kv* tkv = nullptr;
+  wc_kv* dkv = nullptr;
+  RoundState* st = nullptr;
+  int* out_dev = nullptr;
+  int* out_host = nullptr;  // pinned: [n_out, tokens..., err]
+  float *root_out = nullptr, *root_fb = nullptr, *d_g = nullptr, *taps = nullptr, *t_h = nullptr;
+  std::map<int, std::pair<cudaGraphExec_t, uint64_t>> graphs;
+  int host_n = 0;  // committed length mirrored on the host
+  bool prefilled = false;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  float last_ms = 0.f;
+};
+
+namespace {
+
+void build_round(wc_decoder* dec, int K) {
+  wc_ctx* ctx = dec->ctx;
+  wc_target* t = dec->t;
+  wc_drafter* d = dec->d;
+  RoundState* st = dec->st;
+  int* err = &st->err;
+  const int H = d->cfg.hidden, Ht = t->cfg.hidden;
+  const bool post = d->cfg.post_norm != 0;
+  // ---- draft chain (spec.py:344-350): K heads, K-1 drafter layer passes
+  for (int k = 0; k < K; ++k) {
+    if (k == 0) drafter_head(d, dec->root_out, 1, nullptr, nullptr, st->keys + k, nullptr, err);
+    else drafter_head(d, d->ws_h, 1, d->norm, post ? d->ws_out : nullptr, st->keys + k, nullptr, err);
+    if (k < K - 1) {
+      const float* feat = k == 0 ? dec->root_fb : (post ? d->ws_out : d->ws_h);
+      Rows r;
+      r.L = 1;
+      r.L_max = 1;
+      r.n_dev = &st->dc_len;
+      r.n_add = k;
+      TokenSrc tok;
+      std::memset(&tok, 0, sizeof(tok));
+      tok.keys = st->keys + k;
+      tok.vocab_map = d->vocab_map;
+      tok.forced = st->forced + k;
+      tok.vocab = d->cfg.vocab;
+      drafter_layers(d, dec->dkv, r, feat, tok, d->ws_h, err);
+    }
+  }
+  // ---- verification of [x_n, d_1..d_K] (spec.py:353-355)
+  embed_rows_kernel<<<K + 1, 256, 0, ctx->stream>>>(t->embed, t->dtype, t->cfg.vocab, Ht, nullptr, K + 1, nullptr,
+                                                    dec->t_h, st, d->vocab_map, K, nullptr);
+  check_launch(ctx, "embed verify");
+  Rows rv;
+  rv.L = K + 1;
+  rv.L_max = K + 1;
+  rv.n_dev = &st->n;
+  target_layers(t, dec->tkv, rv, dec->t_h, dec->taps, size_t(dec->max_k + 1) * Ht, err);
+  target_head(t, dec->t_h, K + 1, nullptr, K + 1, st->keys + K, nullptr, err);
+  // ---- acceptance + chain compaction (spec.py:357-362)
+  accept_chain_kernel<<<1, 32, 0, ctx->stream>>>(st, K, nullptr, dec->out_dev);
+  check_launch(ctx, "accept");
+  // ---- drafter update on the accepted rows (spec.py:363, 366-374)
+  drafter_fuse_impl(d, dec->taps, size_t(dec->max_k + 1) * Ht, Ht, K + 1, &st->L_upd, K + 1, dec->d_g, err);
+  Rows ru;
+  ru.L = K + 1;
+  ru.L_dev = &st->L_upd;
+  ru.L_max = K + 1;
+  ru.n_dev = &st->dc_len;
+  TokenSrc tok;
+  std::memset(&tok, 0, sizeof(tok));
+  tok.tokens = st->acc;
+  tok.vocab = d->cfg.vocab;
+  drafter_layers(d, dec->dkv, ru, dec->d_g, tok, d->ws_h, err);
+  finish_update_kernel<<<1, 256, 0, ctx->stream>>>(st, &st->L_upd, K + 1, d->ws_h, H, d->norm, d->cfg.eps,
+                                                   d->cfg.post_norm, dec->root_out, dec->root_fb, 1);
+  check_launch(ctx, "finish update");
+}
+
+std::pair<cudaGraphExec_t, uint64_t>& round_graph(wc_decoder* dec, int K) {
+  auto it = dec->graphs.find(K);
+  if (it != dec->graphs.end()) return it->second;
+  wc_ctx* ctx = dec->ctx;
+  CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  cudaGraph_t g = nullptr;
+  CUDA_TRY(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+  ctx->capturing = true;
+  ctx->capture_launches = 0;
+  try {
+    build_round(dec, K);
+  } catch (...) {
+    ctx->capturing = false;
+    cudaStreamEndCapture(ctx->stream, &g);
+    if (g) cudaGraphDestroy(g);
+    cudaGetLastError();
+    throw;
+  }
+  ctx->capturing = false;
+  CUDA_TRY(cudaStreamEndCapture(ctx->stream, &g));
+  cudaGraphExec_t exec = nullptr;
+  const cudaError_t e = cudaGraphInstantiate(&exec, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) fail(WC_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+  dec->graphs[K] = {exec, ctx->capture_launches};
+  return dec->graphs[K];
+}
+
+void check_state_error(wc_decoder* dec) {
+  int e = 0;
+  CUDA_TRY(cudaMemcpy(&e, &dec->st->err, sizeof(int), cudaMemcpyDeviceToHost));
+  int ce = 0;
+  CUDA_TRY(cudaMemcpy(&ce, dec->ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+  if (e || ce) {
+    CUDA_TRY(cudaMemset(&dec->st->err, 0, sizeof(int)));
+    CUDA_TRY(cudaMemset(dec->ctx->d_err, 0, sizeof(int)));
+    fail(WC_ERR_DEVICE, "device error flag " + std::to_string(e | ce));
+  }
+}
+
+}  // namespace
+
+extern "C" wc_status wc_decoder_create(wc_target* t, wc_drafter* d, int max_context, int max_k, wc_decoder** out) {
+  if (!t || !d || !out) return WC_ERR_INVALID;
+  return guard(t->ctx, [&] {
+    if (t->ctx != d->ctx) fail(WC_ERR_INVALID, "target and drafter belong to different contexts");
+    if (!t->finalized || !d->finalized) fail(WC_ERR_INVALID, "models not finalized");
+    if (d->cfg.target_hidden != t->cfg.hidden) fail(WC_ERR_INVALID, "drafter target_hidden_size != target hidden");
+    if (d->cfg.num_features != 3) fail(WC_ERR_UNSUPPORTED, "the decoder fuses exactly three target taps");
+    if (max_k < 1 || max_k > MAXK || max_k + 1 > GEMV_MAXL) fail(WC_ERR_INVALID, "max_k must be in 1..15");
+    if (max_context < 2 || max_context > 32768 - MAXK) fail(WC_ERR_INVALID, "max_context out of range");
+    wc_ctx* ctx = t->ctx;
+    auto dec = std::make_unique<wc_decoder>();
+    dec->ctx = ctx;
+    dec->t = t;
+    dec->d = d;
+    dec->max_k = max_k;
+    dec->max_ctx = max_context;
+    const int cap = max_context + max_k + 1;
+    dec->tkv = kv_new(ctx, t->cfg.layers, t->cfg.kv_heads, t->cfg.head_dim, cap, t->dtype);
+    dec->dkv = kv_new(ctx, d->cfg.layers, d->cfg.kv_heads, d->cfg.head_dim, cap, d->dtype);
+    dec->st = static_cast<RoundState*>(dalloc(sizeof(RoundState)));
+    CUDA_TRY(cudaMemset(dec->st, 0, sizeof(RoundState)));
+    std::vector<int> neg(MAXK, -1);
+    CUDA_TRY(cudaMemcpy(dec->st->forced, neg.data(), sizeof(int) * MAXK, cudaMemcpyHostToDevice));
+    dec->out_dev = static_cast<int*>(dalloc(sizeof(int) * (MAXK + 4)));
+    CUDA_TRY(cudaMallocHost(&dec->out_host, sizeof(int) * (MAXK + 4)));
+    const int H = d->cfg.hidden, Ht = t->cfg.hidden;
+    dec->root_out = static_cast<float*>(dalloc(sizeof(float) * H));
+    dec->root_fb = static_cast<float*>(dalloc(sizeof(float) * H));
+    dec->d_g = static_cast<float*>(dalloc(sizeof(float) * GEMV_MAXL * H));
+    dec->taps = static_cast<float*>(dalloc(sizeof(float) * 3 * (max_k + 1) * Ht));
+    dec->t_h = static_cast<float*>(dalloc(sizeof(float) * GEMV_MAXL * Ht));
+    CUDA_TRY(cudaEventCreate(&dec->ev0));
+    CUDA_TRY(cudaEventCreate(&dec->ev1));
+    *out = dec.release();
+  });
+}
+
+extern "C" void wc_decoder_destroy(wc_decoder* dec) {
+  if (!dec) return;
+  cudaStreamSynchronize(dec->ctx->stream);
+  for (auto& g : dec->graphs) cudaGraphExecDestroy(g.second.first);
+  wc_kv_destroy(dec->tkv);
+  wc_kv_destroy(dec->dkv);
+  dfree(dec->st);
+  dfree(dec->out_dev);
+  if (dec->out_host) cudaFreeHost(dec->out_host);
+  dfree(dec->root_out);
+  dfree(dec->root_fb);
+  dfree(dec->d_g);
+  dfree(dec->taps);
+  dfree(dec->t_h);
+  if (dec->ev0) cudaEventDestroy(dec->ev0);
+  if (dec->ev1) cudaEventDestroy(dec->ev1);
+  delete dec;
+}
+
+namespace {
+
+// spec.py:129-141 / spec.cpp:61-84: target forward on the prompt (taps kept), first token,
+// drafter forward on prompt[1:] + [first] with the fused taps.
+int decoder_prefill_impl(wc_decoder* dec, const int* prompt, int n, const wc_sampling_params* sp) {
+  if (sp && sp->temperature > 0.f) fail(WC_ERR_UNSUPPORTED, "sampled decoding (temperature > 0) is not built yet");
+  if (n < 1) fail(WC_ERR_INVALID, "empty prompt");
+  if (n + dec->max_k + 1 > dec->tkv->cap) fail(WC_ERR_CAPACITY, "prompt longer than the decoder context");
+  wc_ctx* ctx = dec->ctx;
+  wc_target* t = dec->t;
+  wc_drafter* d = dec->d;
+  const int Ht = t->cfg.hidden, H = d->cfg.hidden;
+  for (int i = 0; i < n; ++i)
+    if (prompt[i] < 0 || prompt[i] >= t->cfg.vocab) fail(WC_ERR_INVALID, "prompt token id out of range");
+  int* d_tok = static_cast<int*>(dalloc(sizeof(int) * (n + 1)));
+  float* taps = static_cast<float*>(dalloc(sizeof(float) * 3 * size_t(n) * Ht));
+  float* g = static_cast<float*>(dalloc(sizeof(float) * GEMV_MAXL * H));
+  struct Free {
+    void* a[3];
+    ~Free() {
+      for (void* p : a) dfree(p);
+    }
+  } guard_free{{d_tok, taps, g}};
+  CUDA_TRY(cudaMemcpyAsync(d_tok, prompt, sizeof(int) * n, cudaMemcpyHostToDevice, ctx->stream));
+  CUDA_TRY(cudaMemsetAsync(dec->st, 0, offsetof(RoundState, forced), ctx->stream));
+  CUDA_TRY(cudaMemsetAsync(dec->st->keys, 0, sizeof(dec->st->keys), ctx->stream));
+  int* err = &dec->st->err;
+  const size_t tstride = size_t(n) * Ht;
+  for (int r0 = 0; r0 < n; r0 += GEMV_MAXL) {
+    const int rows = std::min(GEMV_MAXL, n - r0);
+    embed_rows_kernel<<<rows, 256, 0, ctx->stream>>>(t->embed, t->dtype, t->cfg.vocab, Ht, d_tok + r0, rows, nullptr,
+                                                     dec->t_h, nullptr, nullptr, 0, &dec->st->err);
+    check_launch(ctx, "embed");
+    Rows r;
+    r.L = rows;
+    r.L_max = rows;
+    r.n_add = r0;
+    target_layers(t, dec->tkv, r, dec->t_h, taps + size_t(r0) * Ht, tstride, err);
+    if (r0 + rows == n) target_head(t, dec->t_h + size_t(rows - 1) * Ht, 1, nullptr, 1, dec->st->keys, nullptr, err);
+  }
+  int first = 0;
+  {
+    unsigned long long key = 0;
+    CUDA_TRY(cudaMemcpyAsync(&key, dec->st->keys, sizeof(key), cudaMemcpyDeviceToHost, ctx->stream));
+    CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    first = int(0xFFFFFFFFu - uint32_t(key & 0xFFFFFFFFull));
+  }
+  // drafter entries e = (token x_{e+1}, feature at e) for e = 0..n-1
+  CUDA_TRY(cudaMemcpyAsync(d_tok, prompt + 1, sizeof(int) * (n - 1), cudaMemcpyHostToDevice, ctx->stream));
+  CUDA_TRY(cudaMemcpyAsync(d_tok + n - 1, &first, sizeof(int), cudaMemcpyHostToDevice, ctx->stream));
+  for (int r0 = 0; r0 < n; r0 += GEMV_MAXL) {
+    const int rows = std::min(GEMV_MAXL, n - r0);
+    drafter_fuse_impl(d, taps + size_t(r0) * Ht, tstride, Ht, rows, nullptr, rows, g, err);
+    Rows r;
+    r.L = rows;
+    r.L_max = rows;
+    r.n_add = r0;
+    TokenSrc tok;
+    std::memset(&tok, 0, sizeof(tok));
+    tok.tokens = d_tok + r0;
+    tok.vocab = d->cfg.vocab;
+    drafter_layers(d, dec->dkv, r, g, tok, d->ws_h, err);
+    if (r0 + rows == n) {
+      finish_update_kernel<<<1, 256, 0, ctx->stream>>>(dec->st, nullptr, rows, d->ws_h, H, d->norm, d->cfg.eps,
+                                                       d->cfg.post_norm, dec->root_out, dec->root_fb, 0);
+      check_launch(ctx, "finish prefill");
+    }
+  }
+  RoundState init{};
+  init.n = n;
+  init.dc_len = n;
+  init.x_n = first;
+  CUDA_TRY(cudaMemcpyAsync(dec->st, &init, offsetof(RoundState, forced), cudaMemcpyHostToDevice, ctx->stream));
+  CUDA_TRY(cudaMemsetAsync(dec->st->keys, 0, sizeof(dec->st->keys), ctx->stream));
+  CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  check_state_error(dec);
+  dec->host_n = n;
+  dec->prefilled = true;
+  return first;
+}
+
+int decoder_round_impl(wc_decoder* dec, int K, int* out_tokens) {
+  if (!dec->prefilled) fail(WC_ERR_INVALID, "prefill before the first round");
+  if (K < 1 || K > dec->max_k) fail(WC_ERR_INVALID, "chain length outside 1..max_k");
+  if (dec->host_n + K + 1 > dec->tkv->cap) fail(WC_ERR_CAPACITY, "decoder context exhausted");
+  wc_ctx* ctx = dec->ctx;
+  auto& g = round_graph(dec, K);
+  CUDA_TRY(cudaEventRecord(dec->ev0, ctx->stream));
+  CUDA_TRY(cudaGraphLaunch(g.first, ctx->stream));
+  CUDA_TRY(cudaEventRecord(dec->ev1, ctx->stream));
+  ctx->launches += g.second;
+  CUDA_TRY(cudaMemcpyAsync(dec->out_host, dec->out_dev, sizeof(int) * (K + 2), cudaMemcpyDeviceToHost, ctx->stream));
+  CUDA_TRY(cudaMemcpyAsync(dec->out_host + K + 2, &dec->st->err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+  CUDA_TRY(cudaStreamSynchronize(ctx->stream));  // the round's single host synchronisation
+  cudaEventElapsedTime(&dec->last_ms, dec->ev0, dec->ev1);
+  if (dec->out_host[K + 2]) check_state_error(dec);
+  const int m = dec->out_host[0];
+  if (m < 1 || m > K + 1) fail(WC_ERR_DEVICE, "round produced an invalid token count");
+  for (int i = 0; i < m; ++i) out_tokens[i] = dec->out_host[1 + i];
+  dec->host_n += m;
+  return m;
+}
+
+}  // namespace
+
+extern "C" wc_status wc_decoder_prefill(wc_decoder* dec, const int* prompt, int n, const wc_sampling_params* sp,
+                                        int* first) {
+  if (!dec || !prompt || !first) return WC_ERR_INVALID;
+  return guard(dec->ctx, [&] { *first = decoder_prefill_impl(dec, prompt, n, sp); });
+}
+
+extern "C" wc_status wc_decoder_set_forced(wc_decoder* dec, const int* forced, int k) {
+  if (!dec || k < 0 || k > MAXK) return WC_ERR_INVALID;
+  return guard(dec->ctx, [&] {
+    std::vector<int> f(MAXK, -1);
+    for (int i = 0; i < k && forced; ++i) f[i] = forced[i];
+    CUDA_TRY(cudaMemcpyAsync(dec->st->forced, f.data(), sizeof(int) * MAXK, cudaMemcpyHostToDevice, dec->ctx->stream));
+    CUDA_TRY(cudaStreamSynchronize(dec->ctx->stream));
+  });
+}
+
+extern "C" wc_status wc_decoder_round(wc_decoder* dec, int k, int* out_tokens, int* out_n) {
+  if (!dec || !out_tokens || !out_n) return WC_ERR_INVALID;
+  return guard(dec->ctx, [&] { *out_n = decoder_round_impl(dec, k, out_tokens); });
+}
+
+extern "C" wc_status wc_decoder_generate(wc_decoder* dec, const int* prompt, int n, int max_new, int k,
+                                         const wc_sampling_params* sp, const int* eos, int n_eos, int* out_tokens,
+                                         int* out_n, wc_gen_stats* stats) {
+  if (!dec || !prompt || !out_tokens || !out_n || max_new < 1) return WC_ERR_INVALID;
+  return guard(dec->ctx, [&] {
+    wc_gen_stats s{};
+    s.prompt_tokens = n;
+    std::set<int> eset(eos, eos + (eos ? n_eos : 0));
+    const double t0 = now_s();
+    int x = decoder_prefill_impl(dec, prompt, n, sp);
+    s.t_prefill = now_s() - t0;
+    int m = 0;
+    out_tokens[m++] = x;
+    int acc[MAXK + 1];
+    while (m < max_new && !eset.count(x)) {
+      if (dec->host_n + k + 1 > dec->tkv->cap) fail(WC_ERR_CAPACITY, "decoder context exhausted");
+      const double ta = now_s();
+      const int na = decoder_round_impl(dec, k, acc);
+      s.t_verify += now_s() - ta;
+      s.rounds += 1;
+      s.accepted += na - 1;
+      s.verified += k;
+      for (int i = 0; i < na; ++i) {
+        out_tokens[m++] = acc[i];
+        if (eset.count(acc[i]) || m >= max_new) break;
+      }
+      x = out_tokens[m - 1];
+    }
+    s.t_total = now_s() - t0;
+    s.new_tokens = m;
+    *out_n = m;
+    if (stats) *stats = s;
+  });
+}
+
+extern "C" wc_status wc_decoder_state(const wc_decoder* dec, int* n, int* drafter_len) {
+  if (!dec) return WC_ERR_INVALID;
+  RoundState s;
+  if (cudaMemcpy(&s, dec->st, offsetof(RoundState, tokens), cudaMemcpyDeviceToHost) != cudaSuccess) return WC_ERR_CUDA;
+  if (n) *n = s.n;
+  if (drafter_len) *drafter_len = s.dc_len;
+  return WC_OK;
+}
+
+extern "C" wc_kv* wc_decoder_target_cache(wc_decoder* dec) { return dec ? dec->tkv : nullptr; }
+extern "C" wc_kv* wc_decoder_drafter_cache(wc_decoder* dec) { return dec ? dec->dkv : nullptr; }
+
+extern "C" wc_status wc_decoder_last_round_ms(const wc_decoder* dec, float* ms) {
+  if (!dec || !ms) return WC_ERR_INVALID;
+  *ms = dec->last_ms;
+  return WC_OK;
+}
+
+// ============================================================================ autoregressive baseline
+
+namespace {
+__global__ void ar_advance_kernel(RoundState* st, int* out) {
+  if (threadIdx.x != 0) return;
+  const int tok = int(argmax_key_index(st->keys[0]));
+  st->x_n = tok;
+  st->n += 1;
+  st->keys[0] = 0ull;
+  out[0] = tok;
+}
+}  // namespace
+
+extern "C" wc_status wc_generate_autoregressive(wc_target* t, const int* prompt, int n, int max_new,
+                                                const wc_sampling_params* sp, const int* eos, int n_eos,
+                                                int max_context, int* out_tokens, int* out_n, wc_gen_stats* stats) {
+  if (!t || !prompt || !out_tokens || !out_n || n < 1 || max_new < 1) return WC_ERR_INVALID;
+  return guard(t->ctx, [&] {
+    if (sp && sp->temperature > 0.f) fail(WC_ERR_UNSUPPORTED, "sampled decoding (temperature > 0) is not built yet");
+    wc_ctx* ctx = t->ctx;
+    const int Ht = t->cfg.hidden;
+    const int cap = std::max(max_context, n + max_new + 1);
+    wc_gen_stats s{};
+    s.prompt_tokens = n;
+    std::set<int> eset(eos, eos + (eos ? n_eos : 0));
+    const double t0 = now_s();
+    std::unique_ptr<wc_kv, void (*)(wc_kv*)> kv(kv_new(ctx, t->cfg.layers, t->cfg.kv_heads, t->cfg.head_dim, cap,
+                                                      t->dtype),
+                                               wc_kv_destroy);
+    RoundState* st = static_cast<RoundState*>(dalloc(sizeof(RoundState)));
+    int* d_tok = static_cast<int*>(dalloc(sizeof(int) * n));
+    int* d_out = static_cast<int*>(dalloc(sizeof(int) * 4));
+    float* h = static_cast<float*>(dalloc(sizeof(float) * GEMV_MAXL * Ht));
+    cudaGraphExec_t exec = nullptr;
+    struct Free {
+      void* a[4];
+      cudaGraphExec_t* e;
+      ~Free() {
+        if (*e) cudaGraphExecDestroy(*e);
+        for (void* p : a) dfree(p);
+      }
+    } fr{{st, d_tok, d_out, h}, &exec};
+    CUDA_TRY(cudaMemsetAsync(st, 0, sizeof(RoundState), ctx->stream));
+    CUDA_TRY(cudaMemcpyAsync(d_tok, prompt, sizeof(int) * n, cudaMemcpyHostToDevice, ctx->stream));
+    for (int i = 0; i < n; ++i)
+      if (prompt[i] < 0 || prompt[i] >= t->cfg.vocab) fail(WC_ERR_INVALID, "prompt token id out of range");
+    for (int r0 = 0; r0 < n; r0 += GEMV_MAXL) {
+      const int rows = std::min(GEMV_MAXL, n - r0);
+      embed_rows_kernel<<<rows, 256, 0, ctx->stream>>>(t->embed, t->dtype, t->cfg.vocab, Ht, d_tok + r0, rows,
+                                                       nullptr, h, nullptr, nullptr, 0, &st->err);
+      check_launch(ctx, "embed");
+      Rows r;
+      r.L = rows;
+      r.L_max = rows;
+      r.n_add = r0;
+      target_layers(t, kv.get(), r, h, nullptr, 0, &st->err);
+      if (r0 + rows == n) target_head(t, h + size_t(rows - 1) * Ht, 1, nullptr, 1, st->keys, nullptr, &st->err);
+    }
+    // st->n = n - 1 so that the first advance makes it n while emitting the first token
+    RoundState init{};
+    init.n = n - 1;
+    CUDA_TRY(cudaMemcpyAsync(st, &init, offsetof(RoundState, err), cudaMemcpyHostToDevice, ctx->stream));
+    ar_advance_kernel<<<1, 32, 0, ctx->stream>>>(st, d_out);
+    check_launch(ctx, "ar advance");
+    int* hout = nullptr;
+    CUDA_TRY(cudaMallocHost(&hout, sizeof(int) * 2));
+    std::unique_ptr<int, cudaError_t (*)(void*)> hguard(hout, cudaFreeHost);
+    CUDA_TRY(cudaMemcpyAsync(hout, d_out, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+    CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    int x = hout[0];
+    s.t_prefill = now_s() - t0;
+    int m = 0;
+    out_tokens[m++] = x;
+    uint64_t per = 0;
+    while (m < max_new && !eset.count(x)) {
+      if (!exec) {
+        cudaGraph_t g = nullptr;
+        CUDA_TRY(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+        ctx->capturing = true;
+        ctx->capture_launches = 0;
+        try {
+          embed_rows_kernel<<<1, 256, 0, ctx->stream>>>(t->embed, t->dtype, t->cfg.vocab, Ht, nullptr, 1, nullptr, h,
+                                                        st, nullptr, 0, nullptr);
+          check_launch(ctx, "embed");
+          Rows r;
+          r.L = 1;
+          r.L_max = 1;
+          r.n_dev = &st->n;
+          target_layers(t, kv.get(), r, h, nullptr, 0, &st->err);
+          target_head(t, h, 1, nullptr, 1, st->keys, nullptr, &st->err);
+          ar_advance_kernel<<<1, 32, 0, ctx->stream>>>(st, d_out);
+          check_launch(ctx, "ar advance");
+        } catch (...) {
+          ctx->capturing = false;
+          cudaStreamEndCapture(ctx->stream, &g);
+          if (g) cudaGraphDestroy(g);
+          throw;
+        }
+        ctx->capturing = false;
+        CUDA_TRY(cudaStreamEndCapture(ctx->stream, &g));
+        const cudaError_t e = cudaGraphInstantiate(&exec, g, 0);
+        cudaGraphDestroy(g);
+        if (e != cudaSuccess) fail(WC_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+        per = ctx->capture_launches;
+      }
+      CUDA_TRY(cudaGraphLaunch(exec, ctx->stream));
+      ctx->launches += per;
+      CUDA_TRY(cudaMemcpyAsync(hout, d_out, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+      CUDA_TRY(cudaMemcpyAsync(hout + 1, &st->err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+      CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+      if (hout[1]) fail(WC_ERR_DEVICE, "device error flag " + std::to_string(hout[1]));
+      x = hout[0];
+      out_tokens[m++] = x;
+    }
+    s.t_total = now_s() - t0;
+    s.new_tokens = m;
+    s.rounds = m - 1;
+    *out_n = m;
+    if (stats) *stats = s;
+  });
+}
