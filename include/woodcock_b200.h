@@ -214,6 +214,12 @@ WC_API wc_status wc_decoder_generate(wc_decoder* dec, const int* prompt, int n, 
 WC_API wc_status wc_generate_autoregressive(wc_target* t, const int* prompt, int n, int max_new,
                                      const wc_sampling_params* sp, const int* eos, int n_eos, int max_context,
                                      int* out_tokens, int* out_n, wc_gen_stats* stats);
+/* A real round (as wc_decoder_round) replayed from a second graph that records CUDA events
+ * around kernels: ms_sum[i] / counts[i] is the mean device time of kernel class i, for
+ * i = 0 target QKV GEMV, 1 attention, 2 o-proj, 3 gate/up, 4 down-proj, 5 target head,
+ * 6 drafter head, 7 drafter layer pass (whole). Arrays of 8. */
+WC_API wc_status wc_decoder_profile_round(wc_decoder* dec, int k, int* out_tokens, int* out_n, float* ms_sum,
+                                          int* counts);
 /* device-side state after the last round: committed length n (target cache size) and drafter cache size */
 WC_API wc_status wc_decoder_state(const wc_decoder* dec, int* n, int* drafter_len);
 /* copy the target KV cache of the decoder (for tests) */

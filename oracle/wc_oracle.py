@@ -100,8 +100,11 @@ def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float) -> np.ndarray:
 
 
 def rope_inv_freq(D: int, base: float) -> np.ndarray:
+    """std::pow(base, -2.f * i / D) in float: the exponent is formed in float32 and the power
+    rounded once from double (glibc's powf is within 1 ulp of that)."""
     i = np.arange(D // 2, dtype=F32)
-    return np.power(F32(base), (F32(-2.0) * i / F32(D)).astype(F32)).astype(F32)
+    e = (F32(-2.0) * i / F32(D)).astype(F32)
+    return np.power(np.float64(F32(base)), e.astype(np.float64)).astype(F32)
 
 
 def rope(x: np.ndarray, positions, base: float) -> np.ndarray:
@@ -111,7 +114,10 @@ def rope(x: np.ndarray, positions, base: float) -> np.ndarray:
     half = D // 2
     inv = rope_inv_freq(D, base)
     a = (np.asarray(positions, F32)[:, None] * inv[None, :]).astype(F32)  # [L][half]
-    c, s = np.cos(a).astype(F32)[:, None, :], np.sin(a).astype(F32)[:, None, :]
+    # cosf / sinf of a float angle, rounded once from double (numpy's float32 cos/sin lose
+    # accuracy for angles in the thousands of radians; glibc's are correctly rounded)
+    a64 = a.astype(np.float64)
+    c, s = np.cos(a64).astype(F32)[:, None, :], np.sin(a64).astype(F32)[:, None, :]
     x1, x2 = x[..., :half], x[..., half:]
     return np.concatenate([x1 * c - x2 * s, x2 * c + x1 * s], axis=-1).astype(F32)
 
@@ -159,7 +165,8 @@ class KVCache:
     """Per-layer [pos][kv_head*head_dim] rows; append/commit/trim_to/compact
     (include/woodcock/cache.h:9-28, src/cache/kv_cache.cpp:8-31)."""
 
-    def __init__(self, layers: int, kv_heads: int, head_dim: int):
+    def __init__(self, layers: int, kv_heads: int, head_dim: int, bf16: bool = False):
+        self.bf16 = bf16  # store rows rounded to bf16, as a bf16 device cache does
         self.row = kv_heads * head_dim
         self.kv_heads, self.head_dim = kv_heads, head_dim
         self.k = [np.zeros((0, self.row), F32) for _ in range(layers)]
@@ -178,8 +185,11 @@ class KVCache:
                 a = np.zeros((grow, self.row), F32)
                 a[: arr[layer].shape[0]] = arr[layer]
                 arr[layer] = a
-        self.k[layer][self.n : need] = k.reshape(L, self.row)
-        self.v[layer][self.n : need] = v.reshape(L, self.row)
+        k, v = k.reshape(L, self.row), v.reshape(L, self.row)
+        if self.bf16:
+            k, v = _round_bf16(k), _round_bf16(v)
+        self.k[layer][self.n : need] = k
+        self.v[layer][self.n : need] = v
 
     def commit(self, L: int) -> None:
         self.n += L
@@ -201,6 +211,12 @@ class KVCache:
 
     def values(self, layer: int, T: int) -> np.ndarray:
         return self.v[layer][:T].reshape(T, self.kv_heads, self.head_dim)
+
+
+def _round_bf16(x: np.ndarray) -> np.ndarray:
+    u = np.ascontiguousarray(x, dtype=F32).view(np.uint32)
+    r = ((u + (((u >> 16) & 1) + np.uint32(0x7FFF))) >> 16) << 16
+    return r.astype(np.uint32).view(F32)
 
 
 def default_positions(start: int, L: int) -> list[int]:
@@ -249,6 +265,7 @@ class Qwen3:
         self.eps = float(cfg.get("rms_norm_eps", 1e-6))
         self.theta = float(cfg.get("rope_theta", 1e6))
         self.taps = list(taps) if taps is not None else [2, self.layers // 2, self.layers - 3]
+        self.kv_bf16 = False  # True: model a bf16 KV cache (rows rounded on append)
         self.w = w
         tied = bool(cfg.get("tie_word_embeddings", False)) or "lm_head.weight" not in w
         self.head = w["model.embed_tokens.weight"] if tied else w["lm_head.weight"]
@@ -259,7 +276,7 @@ class Qwen3:
         return cls(cfg, w, taps)
 
     def make_cache(self) -> KVCache:
-        return KVCache(self.layers, self.kv_heads, self.head_dim)
+        return KVCache(self.layers, self.kv_heads, self.head_dim, bf16=self.kv_bf16)
 
     def forward(self, tokens, cache: KVCache, positions=None, mask=None, logits=True, logits_from=0):
         """Returns (logits [rows][V] for rows >= logits_from, taps: list of [L][hidden])."""
@@ -315,6 +332,7 @@ class Drafter:
         self.post_norm = cfg.get("post_norm", True)
         self.feature_norm = cfg.get("feature_norm", True)
         self.window = cfg.get("window") or 0
+        self.kv_bf16 = False
         self.w = w
         self.head = w["lm_head.weight"]
         self.vocab_ids = None
@@ -336,7 +354,7 @@ class Drafter:
         return rows if self.vocab_ids is None else int(self.vocab_ids[rows])
 
     def make_cache(self) -> KVCache:
-        return KVCache(self.layers, self.kv_heads, self.head_dim)
+        return KVCache(self.layers, self.kv_heads, self.head_dim, bf16=self.kv_bf16)
 
     def fuse(self, taps: list[np.ndarray]) -> np.ndarray:
         w = self.w

@@ -160,23 +160,27 @@ def test_single_token_draft_vocab_maps_rows_to_token_ids(golden, tiny_models, gp
 
 
 def test_bf16_target_logits_within_tolerance(tmp_path):
-    """bf16 weights at Qwen3-1.7B widths (3 layers, full 151,936 vocabulary): logits vs the oracle
-    run in fp32 on the same bf16-rounded weights. Tolerance: |dz| <= 2e-3 * max|z| + 2e-3."""
-    from woodcock_b200 import Target
-    from woodcock_b200 import synthetic as syn
+    """bf16 weights at Qwen3-1.7B widths (3 layers, full 151,936 vocabulary), bf16 KV cache.
+    (a) vs the oracle in fp32 on the same bf16-rounded weights with bf16-rounded K/V rows:
+        |dz| <= 2e-3 * max|z| + 2e-3 (only summation order and the activation split differ);
+    (b) vs the oracle with an fp32 KV cache (the reference C++ core's arithmetic): the bf16
+        tolerance |dz| <= 1e-2 * max|z|, and the greedy argmax agrees on every row."""
     import dataclasses
 
-    # three distinct tap layers need three layers
-    ts = dataclasses.replace(syn.Q17_TARGET, layers=3, tie_embeddings=True)
+    from woodcock_b200 import Target
+    from woodcock_b200 import synthetic as syn
+
+    ts = dataclasses.replace(syn.Q17_TARGET, layers=3, tie_embeddings=True)  # three distinct taps
     w = syn.round_to_bf16(syn.generate_weights(syn.target_tensor_specs(ts), seed=0))
     t = Target.from_weights(ts.hf_config(), {k: torch.from_numpy(v).to(torch.bfloat16) for k, v in w.items()},
                             feature_layers=[0, 1, 2], dtype="bf16")
     prompt = syn.prompt_ids(24, ts.vocab, seed=1)
-    o = t(prompt, t.make_cache(64), logits_from=20)
-    z = o.logits[0].cpu().numpy()
+    z = t(prompt, t.make_cache(64), logits_from=20).logits[0].cpu().numpy()
     ot = O.Qwen3(ts.hf_config(), w, taps=[0, 1, 2])
-    zr, _ = ot.forward(prompt, ot.make_cache(), logits_from=20)
-    err = np.abs(z - zr).max()
-    assert err <= 2e-3 * np.abs(zr).max() + 2e-3, err
-    agree = (z.argmax(-1) == zr.argmax(-1)).mean()
-    assert agree >= 0.75, agree
+    ot.kv_bf16 = True
+    zb, _ = ot.forward(prompt, ot.make_cache(), logits_from=20)
+    assert np.abs(z - zb).max() <= 2e-3 * np.abs(zb).max() + 2e-3
+    ot.kv_bf16 = False
+    zf, _ = ot.forward(prompt, ot.make_cache(), logits_from=20)
+    assert np.abs(z - zf).max() <= 1e-2 * np.abs(zf).max()
+    assert (z.argmax(-1) == zf.argmax(-1)).all()

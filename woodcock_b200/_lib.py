@@ -112,6 +112,7 @@ SIGNATURES = {
                                 I32P, I32P, C.POINTER(GenStatsC)]),
     "wc_generate_autoregressive": (S, [P, I32P, C.c_int, C.c_int, C.POINTER(SamplingParamsC), I32P, C.c_int,
                                        C.c_int, I32P, I32P, C.POINTER(GenStatsC)]),
+    "wc_decoder_profile_round": (S, [P, C.c_int, I32P, I32P, C.POINTER(C.c_float), I32P]),
     "wc_decoder_state": (S, [P, I32P, I32P]),
     "wc_decoder_target_cache": (P, [P]),
     "wc_decoder_drafter_cache": (P, [P]),

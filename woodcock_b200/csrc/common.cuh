@@ -88,6 +88,14 @@ __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) 
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"(bytes) : "memory");
 }
 
+// Programmatic dependent launch: the next kernel in the stream may start once every block
+// of this one has called launch_dependents; it must call wait before reading anything this
+// kernel writes. Both are no-ops for kernels launched without the PDL attribute.
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
 // Orderable argmax key: larger value first, then the smaller index (first maximum,
 // like std::max_element / np.argmax). atomicMax over keys is order-independent.
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
@@ -127,6 +135,53 @@ __device__ __forceinline__ uint4 philox4x32_10(uint64_t counter, uint64_t seed) 
 __device__ __forceinline__ double philox_uniform(uint64_t seed, uint64_t index) {
   const uint4 r = philox4x32_10(index, seed);
   return (double(r.x >> 5) * 67108864.0 + double(r.y >> 6)) * (1.0 / 9007199254740992.0);
+}
+
+}  // namespace wc
+
+namespace wc {
+
+// ldmatrix: four 8x8 b16 matrices; thread i gives the address of row (i % 8) of matrix i / 8.
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* smem_row) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(smem_row));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(a));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* smem_row) {
+  const uint32_t a = static_cast<uint32_t>(__cvta_generic_to_shared(smem_row));
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(a));
+}
+
+// D = A(16x16 bf16, row) * B(16x8 bf16, col) + D with A given as four registers.
+__device__ __forceinline__ void mma_bf16_16816r(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// 16-byte global -> shared async copy; src_bytes < 16 zero-fills the rest (0 = all zeros).
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, int src_bytes) {
+  const uint32_t s = static_cast<uint32_t>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(src_bytes) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// bf16 hi/lo halves of two floats packed as (x0 in the low half, x1 in the high half)
+__device__ __forceinline__ void split2_bf16(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  uint16_t h0, l0, h1, l1;
+  split_bf16(x0, h0, l0);
+  split_bf16(x1, h1, l1);
+  hi = pack2(h0, h1);
+  lo = pack2(l0, l1);
 }
 
 }  // namespace wc

@@ -14,6 +14,12 @@
 // so every warp load is one fully coalesced 512-byte line. Activations are split
 // into bf16 hi + lo terms (two MMAs per tile), which keeps them at fp32-level accuracy.
 // fp32 weights: CUDA-core FMA, row-major [N][K].
+//
+// Latency hiding: each block owns a contiguous slice of row blocks. Before it waits
+// on the previous kernel (programmatic dependent launch) it bulk-prefetches the start
+// of its weight slice into L2, and keeps a prefetch window running ahead of the
+// consumption; the activation prologue uses 16-byte loads that are all in flight at
+// once, in two passes (RMSNorm statistics, then the bf16 hi/lo split into shared memory).
 #pragma once
 
 #include "common.cuh"
@@ -24,12 +30,13 @@ enum Epilogue : int { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3
 
 constexpr int GEMV_THREADS = 256;
 constexpr int GEMV_WARPS = GEMV_THREADS / kWarp;
-constexpr int GEMV_KC = 2048;                  // k per smem chunk
-constexpr int GEMV_KTC = GEMV_KC / 16;         // k-tiles per chunk
+constexpr int GEMV_KC = 2048;                    // k per shared-memory chunk
+constexpr int GEMV_KTC = GEMV_KC / 16;           // k-tiles per chunk
 constexpr int GEMV_TPW = GEMV_KTC / GEMV_WARPS;  // k-tiles per warp per chunk
-constexpr int GEMV_RBB = 2;                    // row blocks per reduction batch
-constexpr int GEMV_MAXL = 16;                  // rows per launch (2 n-tiles)
+constexpr int GEMV_RBB = 2;                      // row blocks per reduction batch
+constexpr int GEMV_MAXL = 16;                    // rows per launch (2 n-tiles)
 constexpr int GEMV_MAXSEG = 3;
+constexpr long long GEMV_PREFETCH_WINDOW = 384 * 1024;  // bytes of its slice a block keeps in flight
 
 struct Seg {
   const float* src;     // fp32 rows src + l*ld (when table == nullptr)
@@ -56,7 +63,7 @@ struct GemvParams {
   const void* w;
   int N;       // valid output rows
   int Np;      // padded rows (multiple of 16 * group for bf16)
-  int K;       // valid input columns
+  int K;       // valid input columns (a multiple of 4, segments too)
   int Kp;      // padded columns (multiple of 16 for bf16)
   int w_dtype;
   int L;
@@ -75,8 +82,6 @@ struct GemvParams {
   int ldy2;
   unsigned long long* keys;  // EPI_ARGMAX
   int group;          // row blocks per epilogue unit: 2 for SwiGLU (gate block, up block)
-  const void* prefetch_next;   // weights of the next launch: bulk-prefetched into L2
-  long long prefetch_bytes;
   int* err;
 };
 
@@ -106,70 +111,65 @@ __device__ __forceinline__ int resolve_token(const TokenSrc& t, int l, int* err)
   return tok;
 }
 
-__device__ __forceinline__ float seg_value(const Seg& s, int l, int i, const int* toks) {
+// 4 consecutive values (i multiple of 4) of row l of a segment.
+__device__ __forceinline__ float4 seg_load4(const Seg& s, int l, int i, const int* toks) {
   if (s.table) {
     const size_t off = size_t(toks[l]) * size_t(s.len) + size_t(i);
-    return s.table_dtype == 1 ? bf16_bits_to_f32(static_cast<const uint16_t*>(s.table)[off])
-                              : static_cast<const float*>(s.table)[off];
+    if (s.table_dtype == 1) {
+      const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(s.table) + off);
+      return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u), __uint_as_float(u.y << 16),
+                         __uint_as_float(u.y & 0xFFFF0000u));
+    }
+    return *reinterpret_cast<const float4*>(static_cast<const float*>(s.table) + off);
   }
-  return s.src[size_t(l) * size_t(s.ld) + size_t(i)];
+  return *reinterpret_cast<const float4*>(s.src + size_t(l) * size_t(s.ld) + size_t(i));
 }
 
-// Shared prologue: resolve tokens and compute the per-(row, segment) RMSNorm scale.
-__device__ void gemv_prologue_stats(const GemvParams& p, int L, int* s_tok, float* s_inv) {
+// Resolve tokens, then the per-(row, segment) RMSNorm scale: each thread owns columns
+// 4*c4 of every row, all of its loads in flight at once; fixed-order block reduction.
+__device__ void gemv_prologue_stats(const GemvParams& p, int L, int* s_tok, float* s_inv, float* s_red) {
   const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
+  bool need_tok = false;
+  for (int s = 0; s < p.nseg; ++s) need_tok |= p.seg[s].table != nullptr;
   if (tid < L) {
-    bool need = false;
-    for (int s = 0; s < p.nseg; ++s) need |= p.seg[s].table != nullptr;
-    const int t = need ? resolve_token(p.tok, tid, p.err) : 0;
+    const int t = need_tok ? resolve_token(p.tok, tid, p.err) : 0;
     s_tok[tid] = t;
-    if (need && p.tok.tok_out && blockIdx.x == 0) p.tok.tok_out[tid] = t;
+    if (need_tok && p.tok.tok_out && blockIdx.x == 0) p.tok.tok_out[tid] = t;
   }
   __syncthreads();
-  for (int item = warp; item < L * p.nseg; item += GEMV_WARPS) {
-    const int l = item / p.nseg, s = item % p.nseg;
+  for (int s = 0; s < p.nseg; ++s) {
     const Seg& sg = p.seg[s];
-    float inv = 1.f;
-    if (sg.norm_w) {
-      float ss = 0.f;
-      for (int i = lane; i < sg.len; i += kWarp) {
-        const float v = seg_value(sg, l, i, s_tok);
-        ss = fmaf(v, v, ss);
+    if (!sg.norm_w) {
+      if (tid < L) s_inv[tid * GEMV_MAXSEG + s] = 1.f;
+      continue;
+    }
+    const int len4 = sg.len / 4;
+    for (int l0 = 0; l0 < L; l0 += 4) {  // four rows at a time keeps the live registers small
+      float ss[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int c4 = tid; c4 < len4; c4 += GEMV_THREADS) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (l0 + u < L) v[u] = seg_load4(sg, l0 + u, c4 * 4, s_tok);
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (l0 + u < L) ss[u] += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
       }
-      ss = warp_sum(ss);
-      inv = 1.f / sqrtf(ss / float(sg.len) + p.eps);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (l0 + u < L) {
+          const float w = warp_sum(ss[u]);
+          if (lane == 0) s_red[warp * GEMV_MAXL + l0 + u] = w;
+        }
+      }
     }
-    if (lane == 0) s_inv[l * GEMV_MAXSEG + s] = inv;
-  }
-  __syncthreads();
-}
-
-// Value of input column k (global index) of row l after normalisation; 0 in padding.
-__device__ __forceinline__ float gemv_input(const GemvParams& p, int l, int k, const int* s_tok,
-                                            const float* s_inv) {
-  int off = 0;
-  for (int s = 0; s < p.nseg; ++s) {
-    const Seg& sg = p.seg[s];
-    if (k < off + sg.len) {
-      const int i = k - off;
-      float v = seg_value(sg, l, i, s_tok);
-      if (sg.norm_w) v = v * s_inv[l * GEMV_MAXSEG + s] * sg.norm_w[i];
-      return v;
+    __syncthreads();
+    if (tid < L) {
+      float tot = 0.f;
+      for (int w = 0; w < GEMV_WARPS; ++w) tot += s_red[w * GEMV_MAXL + tid];
+      s_inv[tid * GEMV_MAXSEG + s] = 1.f / sqrtf(tot / float(sg.len) + p.eps);
     }
-    off += sg.len;
-  }
-  return 0.f;
-}
-
-__device__ __forceinline__ void gemv_write_back(const GemvParams& p, int l, int k, float v) {
-  int off = 0;
-  for (int s = 0; s < p.nseg; ++s) {
-    const Seg& sg = p.seg[s];
-    if (k < off + sg.len) {
-      if (sg.write_back) sg.write_back[size_t(l) * sg.ld_wb + (k - off)] = v;
-      return;
-    }
-    off += sg.len;
+    __syncthreads();
   }
 }
 
@@ -181,86 +181,119 @@ __device__ __forceinline__ bool gemv_has_write_back(const GemvParams& p) {
 
 // Epilogue for one output element (row l of the activations, output feature n).
 __device__ __forceinline__ void gemv_store(const GemvParams& p, int l, int n, float v) {
-  if (p.epi == EPI_ADD) {
-    v += p.base[size_t(l) * p.ldb + n];
-  }
+  if (p.epi == EPI_ADD) v += p.base[size_t(l) * p.ldb + n];
   p.y[size_t(l) * p.ldy + n] = v;
   if (p.y2) p.y2[size_t(l) * p.ldy2 + n] = v;
 }
 
-__device__ __forceinline__ void gemv_prefetch_next(const GemvParams& p) {
-  if (!p.prefetch_next || p.prefetch_bytes <= 0) return;
-  // each block prefetches its share, in 64 KB bulk requests issued by one thread per warp
-  const long long per_block = ((p.prefetch_bytes + gridDim.x - 1) / gridDim.x + 15) & ~15LL;
-  const long long b0 = per_block * blockIdx.x;
-  long long b1 = b0 + per_block;
-  if (b1 > p.prefetch_bytes) b1 = p.prefetch_bytes;
+// Bulk L2 prefetch of bytes [b0, b1) of a block's weight slice, split over its warps.
+__device__ __forceinline__ void prefetch_slice(const char* slice, long long b0, long long b1) {
   const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
   if (lane != 0) return;
-  const char* base = static_cast<const char*>(p.prefetch_next);
-  for (long long o = b0 + (long long)warp * 65536; o < b1; o += (long long)GEMV_WARPS * 65536) {
-    long long n = b1 - o;
-    if (n > 65536) n = 65536;
-    n &= ~15LL;
-    if (n > 0) prefetch_l2_bulk(base + o, uint32_t(n));
+  constexpr long long piece = 32 * 1024;
+  for (long long o = b0 + (long long)warp * piece; o < b1; o += (long long)GEMV_WARPS * piece) {
+    const long long n = (b1 - o < piece ? b1 - o : piece) & ~15LL;
+    if (n > 0) prefetch_l2_bulk(slice + o, uint32_t(n));
   }
 }
 
 // ----------------------------------------------------------------------------- bf16 / mma path
 
-// smem B-fragment layout of one chunk: [nt][kt_local][lane] x uint4, where for lane (g, t) =
-// (lane / 4, lane % 4): .x = hi(x[g][2t], x[g][2t+1]), .y = hi(x[g][2t+8], x[g][2t+9]),
-// .z/.w = the lo terms, all relative to k-tile kt_local and n-tile nt.
+// Builds the B operand of chunk `chunk` in shared memory: [nt][kt_local][lane] x uint4 where,
+// for lane (g, t) = (lane / 4, lane % 4), .x = hi(x[g][2t], x[g][2t+1]), .y = hi(x[g][2t+8],
+// x[g][2t+9]), .z / .w the lo terms, relative to k-tile kt_local and n-tile nt. Rows >= L are
+// left unwritten: they only feed output columns that are never stored.
 template <int NT>
 __device__ void gemv_build_chunk(const GemvParams& p, int L, int chunk, uint4* xs, const int* s_tok,
                                  const float* s_inv, bool write_back) {
   uint32_t* xw = reinterpret_cast<uint32_t*>(xs);
   const int k0 = chunk * GEMV_KC;
-  const int kcount = min(GEMV_KC, p.Kp - k0);
-  const int pairs = kcount / 2;
-  for (int idx = threadIdx.x; idx < NT * 8 * pairs; idx += GEMV_THREADS) {
-    const int n = idx / pairs, pr = idx % pairs;
-    const int kl = pr * 2, k = k0 + kl;
-    float v0 = 0.f, v1 = 0.f;
-    if (n < L) {
-      if (k < p.K) v0 = gemv_input(p, n, k, s_tok, s_inv);
-      if (k + 1 < p.K) v1 = gemv_input(p, n, k + 1, s_tok, s_inv);
-      if (write_back) {
-        if (k < p.K) gemv_write_back(p, n, k, v0);
-        if (k + 1 < p.K) gemv_write_back(p, n, k + 1, v1);
+  const int kend = min(p.K, k0 + GEMV_KC);
+  // segments overlapping [k0, kend): each 4-column group belongs to exactly one segment
+  const int kc4 = (kend - k0) / 4;
+  const int total = L * kc4;
+  constexpr int U = 4;
+  for (int base = threadIdx.x; base < total; base += GEMV_THREADS * U) {
+    float4 v[U], w[U];
+    int segi[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int idx = base + u * GEMV_THREADS;
+      segi[u] = -1;
+      if (idx < total) {
+        const int n = idx / kc4, k = k0 + (idx % kc4) * 4;
+        int off = 0;
+        for (int s = 0; s < p.nseg; ++s) {
+          const Seg& sg = p.seg[s];
+          if (k < off + sg.len) {
+            segi[u] = s;
+            v[u] = seg_load4(sg, n, k - off, s_tok);
+            w[u] = sg.norm_w ? *reinterpret_cast<const float4*>(sg.norm_w + (k - off)) : make_float4(1.f, 1.f, 1.f, 1.f);
+            break;
+          }
+          off += sg.len;
+        }
       }
     }
-    uint16_t h0, l0, h1, l1;
-    split_bf16(v0, h0, l0);
-    split_bf16(v1, h1, l1);
-    const int ktl = kl / 16, kk = kl % 16, t = (kk % 8) / 2, half = kk / 8;
-    const int g = n % 8, nt = n / 8, lane = g * 4 + t;
-    const size_t word = ((size_t(nt) * GEMV_KTC + ktl) * kWarp + lane) * 4;
-    xw[word + half] = pack2(h0, h1);
-    xw[word + 2 + half] = pack2(l0, l1);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int idx = base + u * GEMV_THREADS;
+      if (segi[u] < 0) continue;
+      const int n = idx / kc4, k = k0 + (idx % kc4) * 4;
+      const float inv = s_inv[n * GEMV_MAXSEG + segi[u]];
+      const float x0 = v[u].x * inv * w[u].x, x1 = v[u].y * inv * w[u].y;
+      const float x2 = v[u].z * inv * w[u].z, x3 = v[u].w * inv * w[u].w;
+      if (write_back) {
+        int off = 0;
+        for (int s = 0; s < segi[u]; ++s) off += p.seg[s].len;
+        const Seg& sg = p.seg[segi[u]];
+        if (sg.write_back)
+          *reinterpret_cast<float4*>(sg.write_back + size_t(n) * sg.ld_wb + (k - off)) = make_float4(x0, x1, x2, x3);
+      }
+      uint16_t h0, l0, h1, l1, h2, l2, h3, l3;
+      split_bf16(x0, h0, l0);
+      split_bf16(x1, h1, l1);
+      split_bf16(x2, h2, l2);
+      split_bf16(x3, h3, l3);
+      const int kl = k - k0, ktl = kl >> 4, kk = kl & 15, t = (kk & 7) >> 1, half = kk >> 3;
+      const int lane = (n & 7) * 4 + t, nt = n >> 3;
+      const size_t word = ((size_t(nt) * GEMV_KTC + ktl) * kWarp + lane) * 4;
+      xw[word + half] = pack2(h0, h1);
+      xw[word + 2 + half] = pack2(l0, l1);
+      xw[word + 4 + half] = pack2(h2, h3);  // lane + 1 holds columns 2t+2, 2t+3
+      xw[word + 6 + half] = pack2(l2, l3);
+    }
   }
 }
 
 template <int NT>
-__global__ void __launch_bounds__(GEMV_THREADS) gemv_bf16_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_bf16_kernel(const GemvParams p) {
   extern __shared__ __align__(16) unsigned char smem[];
-  uint4* xs = reinterpret_cast<uint4*>(smem);                                   // NT * KTC * 32 uint4
+  uint4* xs = reinterpret_cast<uint4*>(smem);                                        // NT * KTC * 32 uint4
   float* red = reinterpret_cast<float*>(smem + size_t(NT) * GEMV_KTC * kWarp * 16);  // RBB*NT*W*32*4
-  float* s_inv = red + GEMV_RBB * NT * GEMV_WARPS * kWarp * 4;                 // MAXL * MAXSEG
-  int* s_tok = reinterpret_cast<int*>(s_inv + GEMV_MAXL * GEMV_MAXSEG);          // MAXL
-  unsigned long long* s_key = reinterpret_cast<unsigned long long*>(s_tok + GEMV_MAXL + 2);  // MAXL (8B aligned)
+  float* s_inv = red + GEMV_RBB * NT * GEMV_WARPS * kWarp * 4;                       // MAXL * MAXSEG
+  float* s_red = s_inv + GEMV_MAXL * GEMV_MAXSEG;                                    // WARPS * MAXL
+  int* s_tok = reinterpret_cast<int*>(s_red + GEMV_WARPS * GEMV_MAXL);               // MAXL
+  unsigned long long* s_key = reinterpret_cast<unsigned long long*>(s_tok + GEMV_MAXL);  // MAXL
 
-  gemv_prefetch_next(p);
-  const int L = gemv_rows(p);
-  const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
-  if (tid < GEMV_MAXL) s_key[tid] = 0ull;
-  gemv_prologue_stats(p, L, s_tok, s_inv);
-
+  pdl_launch_dependents();
   const int G = p.group;
   const int nunits = p.Np / (16 * G);
   const int u0 = int((long long)blockIdx.x * nunits / gridDim.x);
   const int u1 = int((long long)(blockIdx.x + 1) * nunits / gridDim.x);
   const int KT = p.Kp / 16;
+  const long long rb_bytes = (long long)KT * 512;
+  const char* slice = static_cast<const char*>(p.w) + (long long)u0 * G * rb_bytes;
+  const long long slice_bytes = (long long)(u1 - u0) * G * rb_bytes;
+  // weights do not depend on the previous kernel: start streaming them before waiting on it
+  prefetch_slice(slice, 0, slice_bytes < GEMV_PREFETCH_WINDOW ? slice_bytes : GEMV_PREFETCH_WINDOW);
+  pdl_wait();
+
+  const int L = gemv_rows(p);
+  const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
+  if (tid < GEMV_MAXL) s_key[tid] = 0ull;
+  gemv_prologue_stats(p, L, s_tok, s_inv, s_red);
+
   const int nchunks = (KT + GEMV_KTC - 1) / GEMV_KTC;
   const bool wb = blockIdx.x == 0 && gemv_has_write_back(p);
   if (nchunks == 1) {
@@ -273,6 +306,11 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_bf16_kernel(const GemvParam
   for (int ub = u0; ub < u1; ub += units_per_batch) {
     const int nrb = min(units_per_batch, u1 - ub) * G;  // row blocks in this batch
     const int rb0 = ub * G;
+    {  // keep the prefetch window running ahead of consumption
+      const long long done = (long long)(rb0 - u0 * G) * rb_bytes;
+      const long long a = done + GEMV_PREFETCH_WINDOW, b = a + (long long)nrb * rb_bytes;
+      if (ub > u0 && a < slice_bytes) prefetch_slice(slice, a, b < slice_bytes ? b : slice_bytes);
+    }
     float acc[GEMV_RBB][NT][4];
 #pragma unroll
     for (int j = 0; j < GEMV_RBB; ++j)
@@ -337,10 +375,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_bf16_kernel(const GemvParam
           us += red[(((ju * NT + nt) * GEMV_WARPS + w) * kWarp + ln) * 4 + e];
         }
         const int n = ((rb0 / 2) + jj) * 16 + r16;
-        if (n < p.N) {
-          const float v = gs / (1.f + expf(-gs)) * us;
-          p.y[size_t(l) * p.ldy + n] = v;
-        }
+        if (n < p.N) p.y[size_t(l) * p.ldy + n] = gs / (1.f + expf(-gs)) * us;
       } else {
         float s = 0.f;
 #pragma unroll
@@ -364,7 +399,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_bf16_kernel(const GemvParam
 template <int NT>
 size_t gemv_bf16_smem() {
   return size_t(NT) * GEMV_KTC * kWarp * 16 + size_t(GEMV_RBB) * NT * GEMV_WARPS * kWarp * 4 * 4 +
-         GEMV_MAXL * GEMV_MAXSEG * 4 + (GEMV_MAXL + 2) * 4 + GEMV_MAXL * 8 + 16;
+         GEMV_MAXL * GEMV_MAXSEG * 4 + GEMV_WARPS * GEMV_MAXL * 4 + GEMV_MAXL * 4 + GEMV_MAXL * 8 + 16;
 }
 
 // ----------------------------------------------------------------------------- fp32 / FMA path
@@ -372,26 +407,40 @@ size_t gemv_bf16_smem() {
 // x lives in smem as fp32 [L][Kp]; each warp computes whole output rows, lanes split K.
 __global__ void __launch_bounds__(GEMV_THREADS) gemv_f32_kernel(const GemvParams p) {
   extern __shared__ __align__(16) unsigned char smem[];
-  float* xs = reinterpret_cast<float*>(smem);                    // L_max * Kp
+  float* xs = reinterpret_cast<float*>(smem);  // L_max * Kp
   float* s_inv = xs + size_t(p.L_max) * p.Kp;
-  int* s_tok = reinterpret_cast<int*>(s_inv + GEMV_MAXL * GEMV_MAXSEG);
-  unsigned long long* s_key = reinterpret_cast<unsigned long long*>(s_tok + GEMV_MAXL + 2);
+  float* s_red = s_inv + GEMV_MAXL * GEMV_MAXSEG;
+  int* s_tok = reinterpret_cast<int*>(s_red + GEMV_WARPS * GEMV_MAXL);
+  unsigned long long* s_key = reinterpret_cast<unsigned long long*>(s_tok + GEMV_MAXL);
 
-  gemv_prefetch_next(p);
+  pdl_launch_dependents();
+  pdl_wait();
   const int L = gemv_rows(p);
   const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
   if (tid < GEMV_MAXL) s_key[tid] = 0ull;
-  gemv_prologue_stats(p, L, s_tok, s_inv);
+  gemv_prologue_stats(p, L, s_tok, s_inv, s_red);
   const bool wb = blockIdx.x == 0 && gemv_has_write_back(p);
-  for (int idx = tid; idx < L * p.Kp; idx += GEMV_THREADS) {
-    const int l = idx / p.Kp, k = idx % p.Kp;
-    float v = 0.f;
-    if (k < p.K) {
-      v = gemv_input(p, l, k, s_tok, s_inv);
-      if (wb) gemv_write_back(p, l, k, v);
+  const int kq = p.K / 4;
+  for (int idx = tid; idx < L * kq; idx += GEMV_THREADS) {
+    const int l = idx / kq, k = (idx % kq) * 4;
+    int off = 0;
+    for (int s = 0; s < p.nseg; ++s) {
+      const Seg& sg = p.seg[s];
+      if (k < off + sg.len) {
+        const float4 v = seg_load4(sg, l, k - off, s_tok);
+        const float inv = s_inv[l * GEMV_MAXSEG + s];
+        const float4 w = sg.norm_w ? *reinterpret_cast<const float4*>(sg.norm_w + (k - off))
+                                   : make_float4(1.f, 1.f, 1.f, 1.f);
+        const float4 x = make_float4(v.x * inv * w.x, v.y * inv * w.y, v.z * inv * w.z, v.w * inv * w.w);
+        *reinterpret_cast<float4*>(&xs[size_t(l) * p.Kp + k]) = x;
+        if (wb && sg.write_back) *reinterpret_cast<float4*>(sg.write_back + size_t(l) * sg.ld_wb + (k - off)) = x;
+        break;
+      }
+      off += sg.len;
     }
-    xs[idx] = v;
   }
+  for (int idx = tid; idx < L * (p.Kp - p.K); idx += GEMV_THREADS)
+    xs[size_t(idx / (p.Kp - p.K)) * p.Kp + p.K + idx % (p.Kp - p.K)] = 0.f;
   __syncthreads();
   const int rows_per_unit = p.group;  // SwiGLU: gate row n and up row n are rows 2n, 2n+1 (interleaved)
   const int nunits = p.N;             // one unit = one output feature (1 or 2 weight rows)
@@ -399,6 +448,7 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_f32_kernel(const GemvParams
   const int u1 = int((long long)(blockIdx.x + 1) * nunits / gridDim.x);
   const float* W = static_cast<const float*>(p.w);
   unsigned long long best[GEMV_MAXL];
+#pragma unroll
   for (int l = 0; l < GEMV_MAXL; ++l) best[l] = 0ull;
   for (int u = u0 + warp; u < u1; u += GEMV_WARPS) {
     float acc[2][GEMV_MAXL];
@@ -406,7 +456,9 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_f32_kernel(const GemvParams
     for (int r = 0; r < 2; ++r)
 #pragma unroll
       for (int l = 0; l < GEMV_MAXL; ++l) acc[r][l] = 0.f;
-    for (int r = 0; r < rows_per_unit; ++r) {
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      if (r >= rows_per_unit) break;
       const float* wr = W + size_t(u * rows_per_unit + r) * p.Kp;
       for (int k = lane * 4; k < p.Kp; k += kWarp * 4) {
         const float4 w4 = ldg_stream_f4(reinterpret_cast<const float4*>(wr + k));
@@ -439,67 +491,19 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_f32_kernel(const GemvParams
     }
   }
   if (p.epi == EPI_ARGMAX) {
-    if (lane == 0)
-      for (int l = 0; l < L; ++l)
-        if (best[l]) atomicMax(&s_key[l], best[l]);
+    if (lane == 0) {
+#pragma unroll
+      for (int l = 0; l < GEMV_MAXL; ++l)
+        if (l < L && best[l]) atomicMax(&s_key[l], best[l]);
+    }
     __syncthreads();
     if (tid < L && s_key[tid] != 0ull) atomicMax(&p.keys[tid], s_key[tid]);
   }
 }
 
 inline size_t gemv_f32_smem(int L_max, int Kp) {
-  return size_t(L_max) * Kp * 4 + GEMV_MAXL * GEMV_MAXSEG * 4 + (GEMV_MAXL + 2) * 4 + GEMV_MAXL * 8 + 16;
-}
-
-// ----------------------------------------------------------------------------- weight tiling
-
-// Row-major W[N][K] (fp32 or bf16 source) -> bf16 A-fragment tiles of [Np][Kp]; zero padding.
-// With interleave_rows = R > 0 (SwiGLU), row block 2j takes gate rows [16j, 16j+16) and row
-// block 2j+1 the up rows [16j, 16j+16), where the source holds gate rows [0, R) then up rows.
-__global__ void tile_bf16_kernel(const void* src, int src_dtype, int N, int K, int Np, int Kp, int interleave_rows,
-                                 uint16_t* dst) {
-  const size_t total = size_t(Np) * Kp;
-  for (size_t idx = size_t(blockIdx.x) * blockDim.x + threadIdx.x; idx < total; idx += size_t(gridDim.x) * blockDim.x) {
-    const size_t tile = idx / 256;
-    const int within = int(idx % 256);
-    const int KT = Kp / 16;
-    const int rb = int(tile / KT), kt = int(tile % KT);
-    const int lane = within / 8, e = within % 8;
-    const int g = lane / 4, t = lane % 4;
-    const int r = g + ((e & 2) ? 8 : 0);
-    const int c = 2 * t + (e & 1) + ((e & 4) ? 8 : 0);
-    int row = rb * 16 + r;
-    const int col = kt * 16 + c;
-    if (interleave_rows > 0) {
-      const int pair = rb / 2;
-      row = (rb % 2 == 0) ? pair * 16 + r : interleave_rows + pair * 16 + r;
-      if (pair * 16 + r >= interleave_rows) row = N;  // padding
-    }
-    float v = 0.f;
-    if (row < N && col < K) {
-      const size_t s = size_t(row) * K + col;
-      v = src_dtype == 1 ? bf16_bits_to_f32(static_cast<const uint16_t*>(src)[s]) : static_cast<const float*>(src)[s];
-    }
-    dst[idx] = f32_to_bf16_bits(v);
-  }
-}
-
-// Row-major fp32 copy with row padding (Kp) and optional gate/up interleave (row 2n = gate n,
-// row 2n+1 = up n).
-__global__ void copy_f32_rows_kernel(const void* src, int src_dtype, int N, int K, int Kp, int interleave_rows,
-                                     float* dst) {
-  const size_t total = size_t(N) * Kp;
-  for (size_t idx = size_t(blockIdx.x) * blockDim.x + threadIdx.x; idx < total; idx += size_t(gridDim.x) * blockDim.x) {
-    const int r = int(idx / Kp), c = int(idx % Kp);
-    int row = r;
-    if (interleave_rows > 0) row = (r % 2 == 0) ? r / 2 : interleave_rows + r / 2;
-    float v = 0.f;
-    if (c < K) {
-      const size_t s = size_t(row) * K + c;
-      v = src_dtype == 1 ? bf16_bits_to_f32(static_cast<const uint16_t*>(src)[s]) : static_cast<const float*>(src)[s];
-    }
-    dst[idx] = v;
-  }
+  return size_t(L_max) * Kp * 4 + GEMV_MAXL * GEMV_MAXSEG * 4 + GEMV_WARPS * GEMV_MAXL * 4 + GEMV_MAXL * 4 +
+         GEMV_MAXL * 8 + 16;
 }
 
 }  // namespace wc

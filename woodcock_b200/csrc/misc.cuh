@@ -350,7 +350,7 @@ __global__ void __launch_bounds__(1024) accept_stochastic_tree_kernel(
   __shared__ int sel;
   const int tid = threadIdx.x;
   for (int v = 1; v < N; ++v)
-    if (parents[v] < 0 || parents[v] >= v) {
+    if (parents[v] < 0 || parents[v] >= v || tokens[v] < 0 || tokens[v] >= V) {
       if (tid == 0) {
         raise_error(err, kErrTree);
         *out_n = 0;
@@ -470,6 +470,10 @@ __global__ void finish_update_kernel(RoundState* st, const int* L_dev, int L_sta
                                      int advance_dc) {
   __shared__ float red[32];
   const int L = L_dev ? *L_dev : L_static;
+  if (L < 1 || L > L_static) {
+    if (threadIdx.x == 0) raise_error(&st->err, kErrRows);
+    return;
+  }
   const float* hr = h + size_t(L - 1) * d;
   float ss = 0.f;
   for (int i = threadIdx.x; i < d; i += blockDim.x) ss = fmaf(hr[i], hr[i], ss);

@@ -11,6 +11,7 @@
 #include <chrono>
 #include <cmath>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <filesystem>
 #include <functional>
@@ -22,6 +23,7 @@
 
 #include "../../include/woodcock_b200.h"
 #include "attention.cuh"
+#include "attention_mma.cuh"
 #include "common.cuh"
 #include "gemv.cuh"
 #include "host_io.h"
@@ -61,6 +63,27 @@ struct RopeTable {
   int max_pos = 0;
 };
 
+// CUDA-event marks around kernels of a profiled round (a separate graph from the timed one).
+enum ProfKind { PK_QKV, PK_ATTN, PK_O, PK_GU, PK_DOWN, PK_HEAD, PK_DRAFT_HEAD, PK_DRAFT_LAYER, PK_COUNT };
+
+struct Profiler {
+  std::vector<cudaEvent_t> pool;
+  size_t next = 0;
+  std::vector<std::pair<int, std::pair<cudaEvent_t, cudaEvent_t>>> marks;
+  cudaEvent_t open[PK_COUNT] = {};
+  cudaEvent_t take() {
+    if (next == pool.size()) {
+      cudaEvent_t e;
+      cudaEventCreate(&e);
+      pool.push_back(e);
+    }
+    return pool[next++];
+  }
+  ~Profiler() {
+    for (auto e : pool) cudaEventDestroy(e);
+  }
+};
+
 struct wc_ctx {
   int device = 0;
   cudaStream_t stream = nullptr;
@@ -77,6 +100,10 @@ struct wc_ctx {
   int pw_n = 0;
   int occ_gemv[3] = {1, 1, 1};  // [0] fp32, [1] bf16 NT=1, [2] bf16 NT=2
   size_t max_smem = 0;
+  Profiler* prof = nullptr;  // set while a profiled round is being captured
+  bool pdl = true;           // programmatic dependent launch between round kernels
+  bool attn_mma = true;      // tensor-core attention for bf16 caches
+  int gemv_blocks_per_sm = 1;
 };
 
 namespace {
@@ -98,6 +125,22 @@ wc_status guard(wc_ctx* ctx, F&& f) {
   }
 }
 
+void prof_begin(wc_ctx* ctx, int kind) {
+  if (!ctx->prof) return;
+  cudaEvent_t e = ctx->prof->take();
+  // external event nodes: a plain record inside stream capture is only a dependency marker
+  cudaEventRecordWithFlags(e, ctx->stream, cudaEventRecordExternal);
+  ctx->prof->open[kind] = e;
+}
+
+void prof_end(wc_ctx* ctx, int kind) {
+  if (!ctx->prof || !ctx->prof->open[kind]) return;
+  cudaEvent_t e = ctx->prof->take();
+  cudaEventRecordWithFlags(e, ctx->stream, cudaEventRecordExternal);
+  ctx->prof->marks.push_back({kind, {ctx->prof->open[kind], e}});
+  ctx->prof->open[kind] = nullptr;
+}
+
 void count_launch(wc_ctx* ctx) {
   if (ctx->capturing) ++ctx->capture_launches;
   else ++ctx->launches;
@@ -106,6 +149,37 @@ void count_launch(wc_ctx* ctx) {
 void check_launch(wc_ctx* ctx, const char* what) {
   const cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) fail(WC_ERR_CUDA, std::string("launch of ") + what + " failed: " + cudaGetErrorString(e));
+  count_launch(ctx);
+}
+
+// Launch with optional programmatic dependent launch (the kernel must pdl_wait() before it
+// reads anything the previous kernel writes) and an optional cluster along x.
+template <typename... KArgs, typename... Args>
+void launch_ex(wc_ctx* ctx, const char* what, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, bool pdl,
+               int cluster_x, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[2];
+  int na = 0;
+  if (pdl && ctx->pdl) {
+    attr[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[na].val.programmaticStreamSerializationAllowed = 1;
+    ++na;
+  }
+  if (cluster_x > 1) {
+    attr[na].id = cudaLaunchAttributeClusterDimension;
+    attr[na].val.clusterDim.x = cluster_x;
+    attr[na].val.clusterDim.y = 1;
+    attr[na].val.clusterDim.z = 1;
+    ++na;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = na;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+  if (e != cudaSuccess) fail(WC_ERR_CUDA, std::string("launch of ") + what + ": " + cudaGetErrorString(e));
   count_launch(ctx);
 }
 
@@ -372,22 +446,31 @@ void launch_gemv(wc_ctx* ctx, const Lin& W, GemvParams p) {
   p.group = W.group;
   if (!p.err) p.err = ctx->d_err;
   int klen = 0;
-  for (int s = 0; s < p.nseg; ++s) klen += p.seg[s].len;
+  for (int s = 0; s < p.nseg; ++s) {
+    const Seg& sg = p.seg[s];
+    klen += sg.len;
+    // the prologue reads 4 columns at a time
+    if (sg.len % 4 || (!sg.table && (sg.ld % 4 || reinterpret_cast<uintptr_t>(sg.src) % 16)) ||
+        (sg.norm_w && reinterpret_cast<uintptr_t>(sg.norm_w) % 16) ||
+        (sg.write_back && (sg.ld_wb % 4 || reinterpret_cast<uintptr_t>(sg.write_back) % 16)))
+      fail(WC_ERR_INVALID, "GEMV inputs must be 16-byte aligned with widths and strides that are multiples of 4");
+  }
   if (klen != W.K) fail(WC_ERR_INVALID, "GEMV input width " + std::to_string(klen) + " != " + std::to_string(W.K));
   if (p.L_max < 1 || p.L_max > GEMV_MAXL) fail(WC_ERR_INVALID, "GEMV rows outside 1..16");
   if (W.dtype == WC_BF16) {
     const int NT = p.L_max <= 8 ? 1 : 2;
     const int nunits = W.Np / (16 * W.group);
-    const int grid = std::max(1, std::min(nunits, ctx->num_sms * ctx->occ_gemv[NT]));
-    if (NT == 1) gemv_bf16_kernel<1><<<grid, GEMV_THREADS, gemv_bf16_smem<1>(), ctx->stream>>>(p);
-    else gemv_bf16_kernel<2><<<grid, GEMV_THREADS, gemv_bf16_smem<2>(), ctx->stream>>>(p);
+    const int grid = std::max(1, std::min(nunits, ctx->num_sms * std::min(ctx->gemv_blocks_per_sm, ctx->occ_gemv[NT])));
+    if (NT == 1)
+      launch_ex(ctx, "gemv", gemv_bf16_kernel<1>, dim3(grid), dim3(GEMV_THREADS), gemv_bf16_smem<1>(), true, 1, p);
+    else
+      launch_ex(ctx, "gemv", gemv_bf16_kernel<2>, dim3(grid), dim3(GEMV_THREADS), gemv_bf16_smem<2>(), true, 1, p);
   } else {
     const size_t smem = gemv_f32_smem(p.L_max, W.Kp);
     if (smem > ctx->max_smem) fail(WC_ERR_UNSUPPORTED, "fp32 projection too wide for shared memory");
     const int grid = std::max(1, std::min((W.N + GEMV_WARPS - 1) / GEMV_WARPS, ctx->num_sms * 2));
-    gemv_f32_kernel<<<grid, GEMV_THREADS, smem, ctx->stream>>>(p);
+    launch_ex(ctx, "gemv", gemv_f32_kernel, dim3(grid), dim3(GEMV_THREADS), smem, true, 1, p);
   }
-  check_launch(ctx, "gemv");
 }
 
 constexpr int ATT_CLUSTER = 8;
@@ -398,21 +481,25 @@ void launch_attention(wc_ctx* ctx, AttnParams p) {
   if (p.H % p.Hk) fail(WC_ERR_INVALID, "heads must be a multiple of kv_heads");
   const int rep = p.H / p.Hk;
   if (p.L_max * rep > ATT_MAXR) fail(WC_ERR_UNSUPPORTED, "too many query rows per KV head in one launch");
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(ATT_CLUSTER, p.Hk, 1);
-  cfg.blockDim = dim3(ATT_THREADS, 1, 1);
-  cfg.dynamicSmemBytes = attention_smem(p.L_max);
-  cfg.stream = ctx->stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = ATT_CLUSTER;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, attention_kernel, p);
-  if (e != cudaSuccess) fail(WC_ERR_CUDA, std::string("attention launch: ") + cudaGetErrorString(e));
-  check_launch(ctx, "attention");
+  const uintptr_t al = reinterpret_cast<uintptr_t>(p.Kc) | reinterpret_cast<uintptr_t>(p.Vc) |
+                       reinterpret_cast<uintptr_t>(p.q_ready ? p.q_ready : p.qkv);
+  if (al % 16 || (p.stride_p * (p.kv_dtype == 1 ? 2 : 4)) % 16 || (p.stride_h * (p.kv_dtype == 1 ? 2 : 4)) % 16 ||
+      (!p.q_ready && p.ld_qkv % 4))
+    fail(WC_ERR_INVALID, "attention inputs must be 16-byte aligned with 16-byte row strides");
+  // tensor-core path: bf16 cache, rule-based visibility, new rows appended by the kernel
+  const bool mma_ok = !p.q_ready && !p.mask_full && p.kv_dtype == WC_BF16 && p.write_cache && ctx->attn_mma &&
+                      (p.D == 128 || p.D == 64) && p.L_max * rep <= AM_MAXR && p.stride_p == p.D;
+  if (mma_ok) {
+    if (p.D == 128)
+      launch_ex(ctx, "attention_mma", attention_mma_kernel<128>, dim3(AM_CLUSTER, p.Hk, 1), dim3(AM_THREADS),
+                attention_mma_smem<128>(p.L_max), true, AM_CLUSTER, p);
+    else
+      launch_ex(ctx, "attention_mma", attention_mma_kernel<64>, dim3(AM_CLUSTER, p.Hk, 1), dim3(AM_THREADS),
+                attention_mma_smem<64>(p.L_max), true, AM_CLUSTER, p);
+    return;
+  }
+  launch_ex(ctx, "attention", attention_kernel, dim3(ATT_CLUSTER, p.Hk, 1), dim3(ATT_THREADS),
+            attention_smem(p.L_max), true, ATT_CLUSTER, p);
 }
 
 AttnParams attn_params() {
@@ -442,6 +529,9 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
       CUDA_TRY(cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking));
       ctx->own_stream = true;
     }
+    if (const char* e = std::getenv("WC_PDL")) ctx->pdl = std::atoi(e) != 0;
+    if (const char* e = std::getenv("WC_GEMV_BLOCKS_PER_SM")) ctx->gemv_blocks_per_sm = std::max(1, std::atoi(e));
+    if (const char* e = std::getenv("WC_ATTN_MMA")) ctx->attn_mma = std::atoi(e) != 0;
     ctx->d_err = static_cast<int*>(dalloc(sizeof(int)));
     CUDA_TRY(cudaMemset(ctx->d_err, 0, sizeof(int)));
     const int smax = int(ctx->max_smem);
@@ -449,6 +539,8 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
     CUDA_TRY(cudaFuncSetAttribute(gemv_bf16_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(gemv_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
+    CUDA_TRY(cudaFuncSetAttribute(attention_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
+    CUDA_TRY(cudaFuncSetAttribute(attention_mma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(kv_compact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     int occ = 0;
     CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_bf16_kernel<1>, GEMV_THREADS,
@@ -1018,9 +1110,9 @@ void target_layers(wc_target* t, wc_kv* kv, const Rows& r, float* h, float* taps
       p.y = t->ws_qkv;
       p.ldy = ld_qkv;
       p.err = err;
-      p.prefetch_next = Ly.o.w;
-      p.prefetch_bytes = (long long)Ly.o.bytes;
+      prof_begin(ctx, PK_QKV);
       launch_gemv(ctx, Ly.qkv, p);
+      prof_end(ctx, PK_QKV);
     }
     {
       AttnParams a = attn_params();
@@ -1054,7 +1146,9 @@ void target_layers(wc_target* t, wc_kv* kv, const Rows& r, float* h, float* taps
       a.ld_out = Hq;
       a.write_cache = 1;
       a.err = err;
+      prof_begin(ctx, PK_ATTN);
       launch_attention(ctx, a);
+      prof_end(ctx, PK_ATTN);
     }
     {
       GemvParams p = gemv_params();
@@ -1069,9 +1163,9 @@ void target_layers(wc_target* t, wc_kv* kv, const Rows& r, float* h, float* taps
       p.base = h;
       p.ldb = H;
       p.err = err;
-      p.prefetch_next = Ly.gu.w;
-      p.prefetch_bytes = std::min<long long>((long long)Ly.gu.bytes, 64ll << 20);
+      prof_begin(ctx, PK_O);
       launch_gemv(ctx, Ly.o, p);
+      prof_end(ctx, PK_O);
     }
     {
       GemvParams p = gemv_params();
@@ -1085,9 +1179,9 @@ void target_layers(wc_target* t, wc_kv* kv, const Rows& r, float* h, float* taps
       p.y = t->ws_act;
       p.ldy = I;
       p.err = err;
-      p.prefetch_next = Ly.down.w;
-      p.prefetch_bytes = (long long)Ly.down.bytes;
+      prof_begin(ctx, PK_GU);
       launch_gemv(ctx, Ly.gu, p);
+      prof_end(ctx, PK_GU);
     }
     {
       GemvParams p = gemv_params();
@@ -1107,11 +1201,9 @@ void target_layers(wc_target* t, wc_kv* kv, const Rows& r, float* h, float* taps
           p.y2 = taps + size_t(f) * taps_stride;
           p.ldy2 = H;
         }
-      if (li + 1 < c.layers) {
-        p.prefetch_next = t->layers[li + 1].qkv.w;
-        p.prefetch_bytes = (long long)t->layers[li + 1].qkv.bytes;
-      }
+      prof_begin(ctx, PK_DOWN);
       launch_gemv(ctx, Ly.down, p);
+      prof_end(ctx, PK_DOWN);
     }
   }
 }
@@ -1131,7 +1223,9 @@ void target_head(wc_target* t, const float* h, int L, const int* L_dev, int L_ma
   p.ldy = t->cfg.vocab;
   p.keys = keys;
   p.err = err;
+  prof_begin(t->ctx, PK_HEAD);
   launch_gemv(t->ctx, t->head, p);
+  prof_end(t->ctx, PK_HEAD);
 }
 
 }  // namespace
@@ -1417,8 +1511,6 @@ void drafter_layers(wc_drafter* d, wc_kv* kv, const Rows& r, const float* feat, 
       p.y = d->ws_qkv;
       p.ldy = ld_qkv;
       p.err = err;
-      p.prefetch_next = Ly.o.w;
-      p.prefetch_bytes = (long long)Ly.o.bytes;
       launch_gemv(ctx, Ly.qkv, p);
     }
     {
@@ -1469,8 +1561,6 @@ void drafter_layers(wc_drafter* d, wc_kv* kv, const Rows& r, const float* feat, 
       p.base = hin;
       p.ldb = H;
       p.err = err;
-      p.prefetch_next = Ly.gu.w;
-      p.prefetch_bytes = std::min<long long>((long long)Ly.gu.bytes, 64ll << 20);
       launch_gemv(ctx, Ly.o, p);
     }
     {
@@ -1485,8 +1575,6 @@ void drafter_layers(wc_drafter* d, wc_kv* kv, const Rows& r, const float* feat, 
       p.y = d->ws_act;
       p.ldy = I;
       p.err = err;
-      p.prefetch_next = Ly.down.w;
-      p.prefetch_bytes = (long long)Ly.down.bytes;
       launch_gemv(ctx, Ly.gu, p);
     }
     {
@@ -1540,7 +1628,9 @@ void drafter_head(wc_drafter* d, const float* x, int rows, const float* norm_w, 
   p.ldy = d->head_rows;
   p.keys = keys;
   p.err = err;
+  prof_begin(d->ctx, PK_DRAFT_HEAD);
   launch_gemv(d->ctx, d->head, p);
+  prof_end(d->ctx, PK_DRAFT_HEAD);
 }
 
 wc_drafter_config drafter_config_from_json(const std::string& path) {
@@ -1780,6 +1870,8 @@ struct wc_decoder {
   int* out_host = nullptr;  // pinned: [n_out, tokens..., err]
   float *root_out = nullptr, *root_fb = nullptr, *d_g = nullptr, *taps = nullptr, *t_h = nullptr;
   std::map<int, std::pair<cudaGraphExec_t, uint64_t>> graphs;
+  std::map<int, std::pair<cudaGraphExec_t, uint64_t>> prof_graphs;
+  std::map<int, std::unique_ptr<Profiler>> profilers;
   int host_n = 0;  // committed length mirrored on the host
   bool prefilled = false;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
@@ -1813,7 +1905,9 @@ void build_round(wc_decoder* dec, int K) {
       tok.vocab_map = d->vocab_map;
       tok.forced = st->forced + k;
       tok.vocab = d->cfg.vocab;
+      prof_begin(ctx, PK_DRAFT_LAYER);
       drafter_layers(d, dec->dkv, r, feat, tok, d->ws_h, err);
+      prof_end(ctx, PK_DRAFT_LAYER);
     }
   }
   // ---- verification of [x_n, d_1..d_K] (spec.py:353-355)
@@ -1846,11 +1940,16 @@ void build_round(wc_decoder* dec, int K) {
   check_launch(ctx, "finish update");
 }
 
-std::pair<cudaGraphExec_t, uint64_t>& round_graph(wc_decoder* dec, int K) {
-  auto it = dec->graphs.find(K);
-  if (it != dec->graphs.end()) return it->second;
+std::pair<cudaGraphExec_t, uint64_t>& round_graph(wc_decoder* dec, int K, bool profiled = false) {
+  auto& store = profiled ? dec->prof_graphs : dec->graphs;
+  auto it = store.find(K);
+  if (it != store.end()) return it->second;
   wc_ctx* ctx = dec->ctx;
   CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  if (profiled) {
+    dec->profilers[K] = std::make_unique<Profiler>();
+    ctx->prof = dec->profilers[K].get();
+  }
   cudaGraph_t g = nullptr;
   CUDA_TRY(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
   ctx->capturing = true;
@@ -1859,19 +1958,21 @@ std::pair<cudaGraphExec_t, uint64_t>& round_graph(wc_decoder* dec, int K) {
     build_round(dec, K);
   } catch (...) {
     ctx->capturing = false;
+    ctx->prof = nullptr;
     cudaStreamEndCapture(ctx->stream, &g);
     if (g) cudaGraphDestroy(g);
     cudaGetLastError();
     throw;
   }
   ctx->capturing = false;
+  ctx->prof = nullptr;
   CUDA_TRY(cudaStreamEndCapture(ctx->stream, &g));
   cudaGraphExec_t exec = nullptr;
   const cudaError_t e = cudaGraphInstantiate(&exec, g, 0);
   cudaGraphDestroy(g);
   if (e != cudaSuccess) fail(WC_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
-  dec->graphs[K] = {exec, ctx->capture_launches};
-  return dec->graphs[K];
+  store[K] = {exec, ctx->capture_launches};
+  return store[K];
 }
 
 void check_state_error(wc_decoder* dec) {
@@ -1929,6 +2030,7 @@ extern "C" void wc_decoder_destroy(wc_decoder* dec) {
   if (!dec) return;
   cudaStreamSynchronize(dec->ctx->stream);
   for (auto& g : dec->graphs) cudaGraphExecDestroy(g.second.first);
+  for (auto& g : dec->prof_graphs) cudaGraphExecDestroy(g.second.first);
   wc_kv_destroy(dec->tkv);
   wc_kv_destroy(dec->dkv);
   dfree(dec->st);
@@ -2025,12 +2127,12 @@ int decoder_prefill_impl(wc_decoder* dec, const int* prompt, int n, const wc_sam
   return first;
 }
 
-int decoder_round_impl(wc_decoder* dec, int K, int* out_tokens) {
+int decoder_round_impl(wc_decoder* dec, int K, int* out_tokens, bool profiled = false) {
   if (!dec->prefilled) fail(WC_ERR_INVALID, "prefill before the first round");
   if (K < 1 || K > dec->max_k) fail(WC_ERR_INVALID, "chain length outside 1..max_k");
   if (dec->host_n + K + 1 > dec->tkv->cap) fail(WC_ERR_CAPACITY, "decoder context exhausted");
   wc_ctx* ctx = dec->ctx;
-  auto& g = round_graph(dec, K);
+  auto& g = round_graph(dec, K, profiled);
   CUDA_TRY(cudaEventRecord(dec->ev0, ctx->stream));
   CUDA_TRY(cudaGraphLaunch(g.first, ctx->stream));
   CUDA_TRY(cudaEventRecord(dec->ev1, ctx->stream));
@@ -2102,6 +2204,25 @@ extern "C" wc_status wc_decoder_generate(wc_decoder* dec, const int* prompt, int
     s.new_tokens = m;
     *out_n = m;
     if (stats) *stats = s;
+  });
+}
+
+extern "C" wc_status wc_decoder_profile_round(wc_decoder* dec, int k, int* out_tokens, int* out_n, float* ms_sum,
+                                             int* counts) {
+  if (!dec || !out_tokens || !out_n || !ms_sum || !counts) return WC_ERR_INVALID;
+  return guard(dec->ctx, [&] {
+    *out_n = decoder_round_impl(dec, k, out_tokens, true);
+    Profiler* pr = dec->profilers.at(k).get();
+    for (int i = 0; i < PK_COUNT; ++i) {
+      ms_sum[i] = 0.f;
+      counts[i] = 0;
+    }
+    for (auto& m : pr->marks) {
+      float ms = 0.f;
+      CUDA_TRY(cudaEventElapsedTime(&ms, m.second.first, m.second.second));
+      ms_sum[m.first] += ms;
+      counts[m.first] += 1;
+    }
   });
 }
 

@@ -59,7 +59,7 @@ class Drafter:
         h = C.c_void_p()
         ctx.check(lib().wc_drafter_create(ctx.h, C.byref(c), dtype_code(dtype), C.byref(h)))
         try:
-            for name, v in weights.items():
+            for name, v in (weights.items() if isinstance(weights, dict) else weights):
                 p, code, on_dev, keep = _tensor_arg(v)
                 shape = (C.c_int64 * keep.ndim)(*keep.shape)
                 if on_dev:

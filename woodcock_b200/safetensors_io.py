@@ -75,3 +75,28 @@ def to_f32(entry: tuple[str, np.ndarray]) -> np.ndarray:
     if dt == "BF16":
         return bf16_bits_to_f32(arr).reshape(arr.shape)
     return np.asarray(arr, dtype=np.float32)
+
+
+def save_streaming(path: str | Path, entries: list[tuple[str, str, tuple[int, ...]]], produce,
+                   metadata: dict | None = None) -> None:
+    """Writes tensors one at a time: `entries` lists (name, dtype tag, shape) in file order and
+    `produce(name)` returns each array (uint16 bits for BF16) when its turn comes."""
+    itemsize = {"F32": 4, "BF16": 2, "F16": 2, "I32": 4, "I64": 8}
+    header: dict = {}
+    if metadata:
+        header["__metadata__"] = {str(k): str(v) for k, v in metadata.items()}
+    off = 0
+    for name, dt, shape in entries:
+        nb = int(np.prod(shape)) * itemsize[dt]
+        header[name] = {"dtype": dt, "shape": list(shape), "data_offsets": [off, off + nb]}
+        off += nb
+    h = json.dumps(header, separators=(",", ":")).encode()
+    h += b" " * ((8 - len(h) % 8) % 8)
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(h)))
+        f.write(h)
+        for name, dt, shape in entries:
+            arr = np.ascontiguousarray(produce(name), dtype=_NP[dt])
+            if arr.shape != tuple(shape):
+                raise ValueError(f"{name}: produced shape {arr.shape}, declared {shape}")
+            f.write(arr.tobytes())

@@ -130,6 +130,20 @@ class SpeculativeDecoder:
         self.ctx.check(lib().wc_decoder_round(self.h, k, out, C.byref(n)))
         return list(out[: n.value])
 
+    PROFILE_KINDS = ("target_qkv", "attention", "target_o", "target_gate_up", "target_down", "target_head",
+                     "drafter_head", "drafter_layer")
+
+    def profile_round(self, k: int) -> tuple[list[int], dict]:
+        """A real round replayed from an instrumented graph: mean device ms per kernel class."""
+        out = (C.c_int * (k + 1))()
+        n = C.c_int()
+        ms = (C.c_float * 8)()
+        cnt = (C.c_int * 8)()
+        self.ctx.check(lib().wc_decoder_profile_round(self.h, k, out, C.byref(n), ms, cnt))
+        prof = {name: {"mean_ms": (ms[i] / cnt[i]) if cnt[i] else 0.0, "launches": cnt[i]}
+                for i, name in enumerate(self.PROFILE_KINDS)}
+        return list(out[: n.value]), prof
+
     def last_round_ms(self) -> float:
         ms = C.c_float()
         self.ctx.check(lib().wc_decoder_last_round_ms(self.h, C.byref(ms)))

@@ -232,3 +232,18 @@ def prompt_ids(n: int, vocab: int, seed: int = 0) -> list[int]:
 
 def spec_dict(x) -> dict:
     return asdict(x)
+
+
+def device_weight_stream(specs, seed: int, device="cuda", std: float = 0.02):
+    """(name, bf16 tensor on `device`) in spec order from a seeded torch generator on the device:
+    the fast path for the billion-parameter configs. Norm gains are ones. The same seed yields
+    the same tensors on every B200, so the reference's model files can be regenerated from it."""
+    import torch
+
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    for name, shape, is_norm in specs:
+        if is_norm:
+            yield name, torch.ones(shape, dtype=torch.bfloat16, device=device)
+        else:
+            yield name, (torch.randn(shape, generator=g, device=device, dtype=torch.float32) * std).to(torch.bfloat16)

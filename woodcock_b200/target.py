@@ -91,7 +91,8 @@ class Target:
 
     @classmethod
     def from_weights(cls, config: dict, weights: dict, feature_layers=None, dtype="bf16", device=0) -> "Target":
-        """HF-style config dict + {tensor name: torch tensor / numpy array (uint16 = bf16 bits)}."""
+        """HF-style config dict + {tensor name: torch tensor / numpy array (uint16 = bf16 bits)} or an
+        iterable of (name, tensor) pairs, consumed one at a time."""
         ctx = Context.get(device)
         c = Qwen3Config(hidden=config["hidden_size"], layers=config["num_hidden_layers"],
                         heads=config["num_attention_heads"], kv_heads=config["num_key_value_heads"],
@@ -104,7 +105,7 @@ class Target:
         ctx.check(lib().wc_target_create(ctx.h, C.byref(c), taps, dtype_code(dtype), C.byref(h)))
         t = cls.__new__(cls)
         try:
-            for name, v in weights.items():
+            for name, v in (weights.items() if isinstance(weights, dict) else weights):
                 p, code, on_dev, keep = _tensor_arg(v)
                 shape = (C.c_int64 * keep.ndim)(*keep.shape)
                 if on_dev:
