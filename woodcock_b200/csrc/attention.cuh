@@ -64,9 +64,20 @@ struct AttnParams {
   float scale;
   float* out;
   int ld_out;  // out row stride (floats); head h of row l at out + l*ld_out + h*D
+  uint32_t* xf_out;  // optional: the output as input fragments of the o-projection
+  int xf_width;      // their (padded) width, >= H*D
+  int xf_fp32;       // fp32 models: xf_out holds plain fp32 rows [16][H*D]
   int write_cache;
   int* err;
 };
+
+__device__ __forceinline__ void attn_emit(const AttnParams& p, int l, int col, float v) {
+  if (p.out) p.out[size_t(l) * p.ld_out + col] = v;
+  if (p.xf_out) {
+    if (p.xf_fp32) reinterpret_cast<float*>(p.xf_out)[size_t(l) * p.H * p.D + col] = v;
+    else xf_store(p.xf_out, p.xf_width, l, col, v);
+  }
+}
 
 __device__ __forceinline__ float kv_load(const void* base, int dtype, long long off) {
   return dtype == 1 ? bf16_bits_to_f32(static_cast<const uint16_t*>(base)[off]) : static_cast<const float*>(base)[off];
@@ -391,7 +402,7 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const AttnParams
     }
     if (tid < D) {
       const int l = r / rep, h = hk * rep + r % rep;
-      p.out[size_t(l) * p.ld_out + size_t(h) * D + tid] = o / lt;
+      attn_emit(p, l, h * D + tid, o / lt);
     }
   }
   cluster.sync();

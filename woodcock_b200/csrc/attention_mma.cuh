@@ -391,7 +391,7 @@ __global__ void __launch_bounds__(AM_THREADS) attention_mma_kernel(const AttnPar
     }
     if (tid < D) {
       const int l = r / rep, h = hk * rep + r % rep;
-      p.out[size_t(l) * p.ld_out + size_t(h) * D + tid] = acc / lt;
+      attn_emit(p, l, h * D + tid, acc / lt);
     }
   }
   cluster.sync();

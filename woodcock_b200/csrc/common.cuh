@@ -16,6 +16,7 @@ enum DeviceError : int {
   kErrRows = 4,           // a dynamic row count outside the sizes the launch was built for
   kErrPosition = 8,       // a RoPE position beyond the precomputed table
   kErrTree = 16,          // malformed tree (parent >= child)
+  kErrTimeout = 32,       // a bounded wait (mbarrier / pipeline) expired
 };
 
 __device__ __forceinline__ void raise_error(int* err, int bit) {
@@ -182,6 +183,71 @@ __device__ __forceinline__ void split2_bf16(float x0, float x1, uint32_t& hi, ui
   split_bf16(x1, h1, l1);
   hi = pack2(h0, h1);
   lo = pack2(l0, l1);
+}
+
+}  // namespace wc
+
+namespace wc {
+
+// ---- mbarrier + 1-D bulk (TMA) copies, CTA-local
+__device__ __forceinline__ uint32_t smem_addr(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory"); }
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_addr(bar)) : "memory");
+}
+// Bounded wait for the phase with the given parity; false when the bound expired.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t max_iters = 1u << 22) {
+  const uint32_t a = smem_addr(bar);
+  for (uint32_t i = 0; i < max_iters; ++i) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(a), "r"(parity)
+        : "memory");
+    if (done) return true;
+    if (i > 64) __nanosleep(32);
+  }
+  return false;
+}
+// global -> shared bulk copy completing on `bar` (addresses 16-byte aligned, bytes % 16 == 0)
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];\n" ::"r"(
+                   smem_addr(dst)),
+               "l"(src), "r"(bytes), "r"(smem_addr(bar))
+               : "memory");
+}
+// named barrier among `count` threads (warps 0 .. count/32-1)
+__device__ __forceinline__ void named_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(count) : "memory");
+}
+
+// ---- activation fragments: the B-operand layout of the bf16 GEMV, shared by producers and
+// consumers. Element (row l < 16, column k) of an input of width K lives in 32-bit word
+//   ((nt * (K / 16) + k / 16) * 32 + lane) * 4 + q,   nt = l / 8, lane = (l % 8) * 4 + t,
+//   t = (k % 8) / 2, q = (k % 16) / 8 (+2 for the lo term), half-word k % 2,
+// i.e. exactly what mma.m16n8k16 expects for B = x^T with hi / lo bf16 terms.
+constexpr int XF_NT = 2;  // rows 0..15
+
+__device__ __forceinline__ size_t xf_word(int K, int l, int k, bool lo) {
+  const int nt = l >> 3, g = l & 7, kt = k >> 4, kk = k & 15, t = (kk & 7) >> 1, q = kk >> 3;
+  return ((size_t(nt) * (K >> 4) + kt) * 32 + g * 4 + t) * 4 + q + (lo ? 2 : 0);
+}
+// write one element (hi and lo halves)
+__device__ __forceinline__ void xf_store(uint32_t* xf, int K, int l, int k, float v) {
+  uint16_t h, lo;
+  split_bf16(v, h, lo);
+  uint16_t* w16 = reinterpret_cast<uint16_t*>(xf);
+  w16[xf_word(K, l, k, false) * 2 + (k & 1)] = h;
+  w16[xf_word(K, l, k, true) * 2 + (k & 1)] = lo;
 }
 
 }  // namespace wc

@@ -1,25 +1,28 @@
-// Skinny GEMM ("GEMV" over L <= 16 rows) for the decode round: y[L][N] = x[L][K] . W[N][K]^T.
+// Skinny GEMM ("GEMV" over L <= 16 rows) for the decode round:
+//   y[L][N] = sum_s inv_s[l] * (x_s[L][K_s] . W_s[N][K_s]^T).
 //
-// Weights stream from HBM exactly once per launch. The input x is assembled in the
-// prologue from up to three segments, each a row source (fp32 activations or an
-// embedding-table gather by token id) with an optional RMSNorm; this fuses the
-// reference's rmsnorm -> linear pairs (src/core/qwen3.cpp:86-101,
-// src/core/drafter.cpp:106-128) and the drafter's feature fusion (drafter.cpp:75-89).
-// Epilogues: store, residual add (linear(..., accumulate=true)), SwiGLU
-// (silu(gate)*up, cpu_ops.cpp:79-84) and a fused argmax over the output rows.
+// Inputs arrive already in the GEMV's input form ("fragments", common.cuh): the producing
+// kernel wrote them pre-multiplied by this GEMV's RMSNorm gain, together with per-block
+// partial sums of squares of its rows. The per-row 1/rms (inv_s) is applied to the
+// accumulators, so a normalised input costs no prologue pass. This covers the reference's
+// rmsnorm -> linear pairs (src/core/qwen3.cpp:86-101, src/core/drafter.cpp:106-128) and
+// the drafter's per-tap RMSNorm + fc fusion (drafter.cpp:75-89). A segment can instead
+// gather embedding rows by token id (the drafter's auxiliary stream, drafter.cpp:110-116),
+// scaled by a per-token 1/rms table built at load time.
 //
-// bf16 weights: tensor-core mma.sync m16n8k16 with the weight as the A operand
-// (16 output rows) and the activations as B (8 rows per n-tile). Weights are stored
-// pre-tiled in A-fragment order (16x16 tile = 512 contiguous bytes, 16 bytes per lane),
-// so every warp load is one fully coalesced 512-byte line. Activations are split
-// into bf16 hi + lo terms (two MMAs per tile), which keeps them at fp32-level accuracy.
-// fp32 weights: CUDA-core FMA, row-major [N][K].
+// bf16 weights are pre-tiled in mma.m16n8k16 A-fragment order (16x16 tile = 512 contiguous
+// bytes) and stream through a 4-stage ring of 16 KB shared-memory slabs filled by 1-D bulk
+// (TMA) copies from a producer warp; the copies start before the kernel waits on its
+// predecessor (programmatic dependent launch), so the weight stream overlaps the previous
+// kernel's tail. Eight consumer warps split each slab's k-tiles and issue two MMAs per tile
+// and n-tile (activation hi and lo bf16 terms, fp32-level accuracy), then release the slot
+// through an mbarrier. Epilogues: store, residual add (linear(..., accumulate=true)),
+// SwiGLU (silu(gate)*up, cpu_ops.cpp:79-84, gate/up row blocks interleaved) and a fused
+// argmax. Stored results can also be emitted as fragments for up to two consumers (times
+// their norm gains) and as per-block partial sums of squares for their 1/rms.
 //
-// Latency hiding: each block owns a contiguous slice of row blocks. Before it waits
-// on the previous kernel (programmatic dependent launch) it bulk-prefetches the start
-// of its weight slice into L2, and keeps a prefetch window running ahead of the
-// consumption; the activation prologue uses 16-byte loads that are all in flight at
-// once, in two passes (RMSNorm statistics, then the bf16 hi/lo split into shared memory).
+// fp32 weights (row-major [N][Kp]) run the same interface on CUDA cores: fragments are
+// then plain fp32 rows [16][len].
 #pragma once
 
 #include "common.cuh"
@@ -28,26 +31,23 @@ namespace wc {
 
 enum Epilogue : int { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3 };
 
-constexpr int GEMV_THREADS = 256;
-constexpr int GEMV_WARPS = GEMV_THREADS / kWarp;
-constexpr int GEMV_KC = 2048;                    // k per shared-memory chunk
-constexpr int GEMV_KTC = GEMV_KC / 16;           // k-tiles per chunk
-constexpr int GEMV_TPW = GEMV_KTC / GEMV_WARPS;  // k-tiles per warp per chunk
-constexpr int GEMV_RBB = 2;                      // row blocks per reduction batch
-constexpr int GEMV_MAXL = 16;                    // rows per launch (2 n-tiles)
+constexpr int GEMV_MAXL = 16;  // rows per launch (2 n-tiles)
 constexpr int GEMV_MAXSEG = 3;
-constexpr long long GEMV_PREFETCH_WINDOW = 384 * 1024;  // bytes of its slice a block keeps in flight
+constexpr int GV_CWARPS = 8;                        // consumer warps
+constexpr int GV_CTHREADS = GV_CWARPS * kWarp;      // 256
+constexpr int GV_THREADS = GV_CTHREADS + kWarp;     // + one producer warp
+constexpr int GV_SLAB = 32;                         // k-tiles per ring stage: 512 columns
+constexpr int GV_COLS = GV_SLAB * 16;
+constexpr int GV_STAGE_BYTES = GV_SLAB * 512;       // 16 KB
+constexpr int GV_NSTAGE = 4;
+constexpr int GV_RBB = 2;                           // row blocks per reduction batch
+constexpr int GV_TPW = GV_SLAB / GV_CWARPS;         // k-tiles per warp per slab
+constexpr int GV_F32_THREADS = 256;
+constexpr int GV_F32_WARPS = GV_F32_THREADS / kWarp;
+constexpr int GV_SIDE_BLOCKS = 16;                  // blocks that run a head's side job
 
-struct Seg {
-  const float* src;     // fp32 rows src + l*ld (when table == nullptr)
-  const void* table;    // embedding table [vocab][len], row = resolved token of row l
-  int table_dtype;      // 0 fp32, 1 bf16
-  int ld;
-  int len;
-  const float* norm_w;  // RMSNorm gain or nullptr
-  float* write_back;    // block 0 stores the (normalised) segment rows here when set
-  int ld_wb;
-};
+// Fragment width of an input of K columns: bf16 models pad to whole ring slabs.
+__host__ __device__ inline int xf_width(bool bf16, int K) { return bf16 ? (K + GV_COLS - 1) / GV_COLS * GV_COLS : K; }
 
 // Per-row token ids for embedding segments: forced id (>= 0) > argmax key > plain id.
 struct TokenSrc {
@@ -59,37 +59,62 @@ struct TokenSrc {
   int vocab;
 };
 
+// One input segment: consecutive columns of the GEMV input.
+struct XSeg {
+  const uint32_t* xf;     // fragments (width lenp) or nullptr for an embedding segment
+  const float* ss;        // [nparts][16] partial sums of squares of the rows; nullptr = not normalised
+  int nparts;
+  int len;                // true width (RMSNorm mean, embedding row length)
+  int lenp;               // padded width: xf_width(len); the weight layout uses the same padding
+  float eps;
+  const void* table;      // embedding segment: [vocab][len] rows (bf16 or fp32 as the weights)
+  const float* norm_w;    //   times this gain
+  const float* row_inv;   //   times row_inv[token] (1/rms of the row), or 1 when nullptr
+};
+
+// Fragments of the stored result times w (the consumer's norm gain, or none).
+struct XOut {
+  uint32_t* xf;
+  const float* w;
+};
+
 struct GemvParams {
   const void* w;
-  int N;       // valid output rows
-  int Np;      // padded rows (multiple of 16 * group for bf16)
-  int K;       // valid input columns (a multiple of 4, segments too)
-  int Kp;      // padded columns (multiple of 16 for bf16)
-  int w_dtype;
+  int N, Np, Kp, group;  // group: row blocks per epilogue unit (2 for SwiGLU)
   int L;
-  const int* L_dev;  // dynamic row count (overrides L when set); rows <= L_max
+  const int* L_dev;      // dynamic row count (overrides L when set); rows <= L_max
   int L_max;
   int nseg;
-  Seg seg[GEMV_MAXSEG];
-  float eps;
+  XSeg seg[GEMV_MAXSEG];
   TokenSrc tok;
   int epi;
-  float* y;
+  float* y;              // fp32 result rows (optional except for argmax logits)
   int ldy;
-  const float* base;  // EPI_ADD: y = base + acc (base may equal y)
+  const float* base;     // EPI_ADD: y = base + acc (base may equal y)
   int ldb;
-  float* y2;          // optional copy of the stored result (tap capture)
+  float* y2;             // optional second copy of the stored result (tap capture)
   int ldy2;
-  unsigned long long* keys;  // EPI_ARGMAX
-  int group;          // row blocks per epilogue unit: 2 for SwiGLU (gate block, up block)
+  unsigned long long* keys;  // EPI_ARGMAX: per-row max keys (atomicMax)
+  int nout;
+  XOut out[2];
+  int out_width;         // fragment width of the outputs (xf_width(N))
+  float* ss_out;         // [gridDim.x][16]: this block's partial sum of y^2 per row
+  // side job of a drafter head, in blocks < side_blocks:
+  //   side_y = side_src * inv(seg 0) * side_w, the next chain step's feature
+  const float* side_src;
+  int side_len, side_width, side_blocks;
+  const float* side_w;
+  float* side_y;
+  XOut side_out;
+  float* side_ss;        // [side_blocks][16]
   int* err;
 };
 
-__device__ __forceinline__ int gemv_rows(const GemvParams& p) {
-  int L = p.L_dev ? *p.L_dev : p.L;
-  if (L < 0 || L > p.L_max) {
-    raise_error(p.err, kErrRows);
-    L = L < 0 ? 0 : p.L_max;
+__device__ __forceinline__ int gemv_rows(const int* L_dev, int L0, int L_max, int* err) {
+  int L = L_dev ? *L_dev : L0;
+  if (L < 0 || L > L_max) {
+    raise_error(err, kErrRows);
+    L = L < 0 ? 0 : L_max;
   }
   return L;
 }
@@ -111,346 +136,335 @@ __device__ __forceinline__ int resolve_token(const TokenSrc& t, int l, int* err)
   return tok;
 }
 
-// 4 consecutive values (i multiple of 4) of row l of a segment.
-__device__ __forceinline__ float4 seg_load4(const Seg& s, int l, int i, const int* toks) {
-  if (s.table) {
-    const size_t off = size_t(toks[l]) * size_t(s.len) + size_t(i);
-    if (s.table_dtype == 1) {
-      const uint2 u = *reinterpret_cast<const uint2*>(static_cast<const uint16_t*>(s.table) + off);
-      return make_float4(__uint_as_float(u.x << 16), __uint_as_float(u.x & 0xFFFF0000u), __uint_as_float(u.y << 16),
-                         __uint_as_float(u.y & 0xFFFF0000u));
-    }
-    return *reinterpret_cast<const float4*>(static_cast<const float*>(s.table) + off);
-  }
-  return *reinterpret_cast<const float4*>(s.src + size_t(l) * size_t(s.ld) + size_t(i));
-}
-
-// Resolve tokens, then the per-(row, segment) RMSNorm scale: each thread owns columns
-// 4*c4 of every row, all of its loads in flight at once; fixed-order block reduction.
-__device__ void gemv_prologue_stats(const GemvParams& p, int L, int* s_tok, float* s_inv, float* s_red) {
-  const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
+// Tokens, then s_inv[s * 16 + l] = the 1/rms of row l of segment s (0 for l >= L). The
+// partial sums are added in a fixed order: 16 part groups per row, then the groups.
+// Runs on 256 threads (named barrier 1); s_part holds 256 floats.
+__device__ void gemv_prologue(const GemvParams& p, int L, int* s_tok, float* s_inv, float* s_part) {
+  const int tid = threadIdx.x;
   bool need_tok = false;
-  for (int s = 0; s < p.nseg; ++s) need_tok |= p.seg[s].table != nullptr;
+  for (int s = 0; s < p.nseg; ++s) need_tok |= p.seg[s].xf == nullptr;
   if (tid < L) {
     const int t = need_tok ? resolve_token(p.tok, tid, p.err) : 0;
     s_tok[tid] = t;
     if (need_tok && p.tok.tok_out && blockIdx.x == 0) p.tok.tok_out[tid] = t;
   }
-  __syncthreads();
+  named_sync(1, 256);
+  const int l = tid & 15, g = tid >> 4;
   for (int s = 0; s < p.nseg; ++s) {
-    const Seg& sg = p.seg[s];
-    if (!sg.norm_w) {
-      if (tid < L) s_inv[tid * GEMV_MAXSEG + s] = 1.f;
-      continue;
-    }
-    const int len4 = sg.len / 4;
-    for (int l0 = 0; l0 < L; l0 += 4) {  // four rows at a time keeps the live registers small
-      float ss[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int c4 = tid; c4 < len4; c4 += GEMV_THREADS) {
-        float4 v[4];
+    const XSeg& sg = p.seg[s];
+    if (sg.xf && sg.ss) {
+      float a = 0.f;
+      for (int q = g; q < sg.nparts; q += 16) a += sg.ss[q * 16 + l];
+      s_part[g * 16 + l] = a;
+      named_sync(1, 256);
+      if (tid < 16) {
+        float t = 0.f;
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (l0 + u < L) v[u] = seg_load4(sg, l0 + u, c4 * 4, s_tok);
-#pragma unroll
-        for (int u = 0; u < 4; ++u)
-          if (l0 + u < L) ss[u] += v[u].x * v[u].x + v[u].y * v[u].y + v[u].z * v[u].z + v[u].w * v[u].w;
+        for (int q = 0; q < 16; ++q) t += s_part[q * 16 + tid];
+        s_inv[s * 16 + tid] = tid < L ? 1.f / sqrtf(t / float(sg.len) + sg.eps) : 0.f;
       }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        if (l0 + u < L) {
-          const float w = warp_sum(ss[u]);
-          if (lane == 0) s_red[warp * GEMV_MAXL + l0 + u] = w;
-        }
-      }
+      named_sync(1, 256);
+    } else if (tid < 16) {
+      s_inv[s * 16 + tid] = tid >= L ? 0.f : (!sg.xf && sg.row_inv) ? sg.row_inv[s_tok[tid]] : 1.f;
     }
-    __syncthreads();
-    if (tid < L) {
-      float tot = 0.f;
-      for (int w = 0; w < GEMV_WARPS; ++w) tot += s_red[w * GEMV_MAXL + tid];
-      s_inv[tid * GEMV_MAXSEG + s] = 1.f / sqrtf(tot / float(sg.len) + p.eps);
-    }
-    __syncthreads();
   }
+  named_sync(1, 256);
 }
 
-__device__ __forceinline__ bool gemv_has_write_back(const GemvParams& p) {
-  for (int s = 0; s < p.nseg; ++s)
-    if (p.seg[s].write_back) return true;
-  return false;
-}
-
-// Epilogue for one output element (row l of the activations, output feature n).
-__device__ __forceinline__ void gemv_store(const GemvParams& p, int l, int n, float v) {
-  if (p.epi == EPI_ADD) v += p.base[size_t(l) * p.ldb + n];
-  p.y[size_t(l) * p.ldy + n] = v;
-  if (p.y2) p.y2[size_t(l) * p.ldy2 + n] = v;
-}
-
-// Bulk L2 prefetch of bytes [b0, b1) of a block's weight slice, split over its warps.
-__device__ __forceinline__ void prefetch_slice(const char* slice, long long b0, long long b1) {
-  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
-  if (lane != 0) return;
-  constexpr long long piece = 32 * 1024;
-  for (long long o = b0 + (long long)warp * piece; o < b1; o += (long long)GEMV_WARPS * piece) {
-    const long long n = (b1 - o < piece ? b1 - o : piece) & ~15LL;
-    if (n > 0) prefetch_l2_bulk(slice + o, uint32_t(n));
+// B operand of one k-tile for this lane: {hi(2t), hi(2t+8), lo(2t), lo(2t+8)} of row nt*8 + g.
+__device__ __forceinline__ uint4 xseg_b(const XSeg& s, int kt_in_seg, int nt, int lane, int L, const int* s_tok) {
+  if (s.xf) {
+    const uint4* f = reinterpret_cast<const uint4*>(s.xf);
+    return __ldg(f + (size_t(nt) * (s.lenp >> 4) + kt_in_seg) * 32 + lane);
   }
+  const int g = lane >> 2, t = lane & 3, l = nt * 8 + g;
+  if (l >= L || kt_in_seg * 16 >= s.len) return make_uint4(0, 0, 0, 0);
+  const int c = kt_in_seg * 16 + 2 * t;
+  const uint16_t* row = static_cast<const uint16_t*>(s.table) + size_t(s_tok[l]) * s.len;
+  const uint32_t e0 = *reinterpret_cast<const uint32_t*>(row + c);
+  const uint32_t e1 = *reinterpret_cast<const uint32_t*>(row + c + 8);
+  const float2 w0 = *reinterpret_cast<const float2*>(s.norm_w + c);
+  const float2 w1 = *reinterpret_cast<const float2*>(s.norm_w + c + 8);
+  uint4 b;
+  split2_bf16(__uint_as_float(e0 << 16) * w0.x, __uint_as_float(e0 & 0xFFFF0000u) * w0.y, b.x, b.z);
+  split2_bf16(__uint_as_float(e1 << 16) * w1.x, __uint_as_float(e1 & 0xFFFF0000u) * w1.y, b.y, b.w);
+  return b;
 }
 
-// ----------------------------------------------------------------------------- bf16 / mma path
-
-// Builds the B operand of chunk `chunk` in shared memory: [nt][kt_local][lane] x uint4 where,
-// for lane (g, t) = (lane / 4, lane % 4), .x = hi(x[g][2t], x[g][2t+1]), .y = hi(x[g][2t+8],
-// x[g][2t+9]), .z / .w the lo terms, relative to k-tile kt_local and n-tile nt. Rows >= L are
-// left unwritten: they only feed output columns that are never stored.
-template <int NT>
-__device__ void gemv_build_chunk(const GemvParams& p, int L, int chunk, uint4* xs, const int* s_tok,
-                                 const float* s_inv, bool write_back) {
-  uint32_t* xw = reinterpret_cast<uint32_t*>(xs);
-  const int k0 = chunk * GEMV_KC;
-  const int kend = min(p.K, k0 + GEMV_KC);
-  // segments overlapping [k0, kend): each 4-column group belongs to exactly one segment
-  const int kc4 = (kend - k0) / 4;
-  const int total = L * kc4;
-  constexpr int U = 4;
-  for (int base = threadIdx.x; base < total; base += GEMV_THREADS * U) {
-    float4 v[U], w[U];
-    int segi[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int idx = base + u * GEMV_THREADS;
-      segi[u] = -1;
-      if (idx < total) {
-        const int n = idx / kc4, k = k0 + (idx % kc4) * 4;
-        int off = 0;
-        for (int s = 0; s < p.nseg; ++s) {
-          const Seg& sg = p.seg[s];
-          if (k < off + sg.len) {
-            segi[u] = s;
-            v[u] = seg_load4(sg, n, k - off, s_tok);
-            w[u] = sg.norm_w ? *reinterpret_cast<const float4*>(sg.norm_w + (k - off)) : make_float4(1.f, 1.f, 1.f, 1.f);
-            break;
-          }
-          off += sg.len;
-        }
+// The head's side job over this block's slice of the feature (s_inv[l] = seg 0's 1/rms).
+// `nthreads` threads take part (named barrier 1); s_red holds (nthreads / 32) * 16 floats.
+__device__ void gemv_side_job(const GemvParams& p, int L, const float* s_inv, float* s_red, int nthreads, bool bf16) {
+  const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
+  const int per = (p.side_len + p.side_blocks - 1) / p.side_blocks;
+  const int f0 = min(p.side_len, int(blockIdx.x) * per), f1 = min(p.side_len, f0 + per);
+  for (int l = 0; l < L; ++l) {
+    float a = 0.f;
+    for (int f = f0 + tid; f < f1; f += nthreads) {
+      const float o = p.side_src[size_t(l) * p.side_len + f] * s_inv[l] * p.side_w[f];
+      if (p.side_y) p.side_y[size_t(l) * p.side_len + f] = o;
+      if (p.side_out.xf) {
+        const float x = p.side_out.w ? o * p.side_out.w[f] : o;
+        if (bf16) xf_store(p.side_out.xf, p.side_width, l, f, x);
+        else reinterpret_cast<float*>(p.side_out.xf)[size_t(l) * p.side_len + f] = x;
       }
+      a = fmaf(o, o, a);
     }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int idx = base + u * GEMV_THREADS;
-      if (segi[u] < 0) continue;
-      const int n = idx / kc4, k = k0 + (idx % kc4) * 4;
-      const float inv = s_inv[n * GEMV_MAXSEG + segi[u]];
-      const float x0 = v[u].x * inv * w[u].x, x1 = v[u].y * inv * w[u].y;
-      const float x2 = v[u].z * inv * w[u].z, x3 = v[u].w * inv * w[u].w;
-      if (write_back) {
-        int off = 0;
-        for (int s = 0; s < segi[u]; ++s) off += p.seg[s].len;
-        const Seg& sg = p.seg[segi[u]];
-        if (sg.write_back)
-          *reinterpret_cast<float4*>(sg.write_back + size_t(n) * sg.ld_wb + (k - off)) = make_float4(x0, x1, x2, x3);
-      }
-      uint16_t h0, l0, h1, l1, h2, l2, h3, l3;
-      split_bf16(x0, h0, l0);
-      split_bf16(x1, h1, l1);
-      split_bf16(x2, h2, l2);
-      split_bf16(x3, h3, l3);
-      const int kl = k - k0, ktl = kl >> 4, kk = kl & 15, t = (kk & 7) >> 1, half = kk >> 3;
-      const int lane = (n & 7) * 4 + t, nt = n >> 3;
-      const size_t word = ((size_t(nt) * GEMV_KTC + ktl) * kWarp + lane) * 4;
-      xw[word + half] = pack2(h0, h1);
-      xw[word + 2 + half] = pack2(l0, l1);
-      xw[word + 4 + half] = pack2(h2, h3);  // lane + 1 holds columns 2t+2, 2t+3
-      xw[word + 6 + half] = pack2(l2, l3);
-    }
+    a = warp_sum(a);
+    if (lane == 0) s_red[warp * 16 + l] = a;
+  }
+  named_sync(1, nthreads);
+  if (p.side_ss && tid < 16) {
+    float a = 0.f;
+    if (tid < L)
+      for (int w = 0; w < nthreads / kWarp; ++w) a += s_red[w * 16 + tid];
+    p.side_ss[blockIdx.x * 16 + tid] = a;
   }
 }
 
 template <int NT>
-__global__ void __launch_bounds__(GEMV_THREADS, 2) gemv_bf16_kernel(const GemvParams p) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  uint4* xs = reinterpret_cast<uint4*>(smem);                                        // NT * KTC * 32 uint4
-  float* red = reinterpret_cast<float*>(smem + size_t(NT) * GEMV_KTC * kWarp * 16);  // RBB*NT*W*32*4
-  float* s_inv = red + GEMV_RBB * NT * GEMV_WARPS * kWarp * 4;                       // MAXL * MAXSEG
-  float* s_red = s_inv + GEMV_MAXL * GEMV_MAXSEG;                                    // WARPS * MAXL
-  int* s_tok = reinterpret_cast<int*>(s_red + GEMV_WARPS * GEMV_MAXL);               // MAXL
-  unsigned long long* s_key = reinterpret_cast<unsigned long long*>(s_tok + GEMV_MAXL);  // MAXL
+__global__ void __launch_bounds__(GV_THREADS, 2) gemv_bf16_kernel(const GemvParams p) {
+  extern __shared__ __align__(128) unsigned char gv_smem[];
+  unsigned char* smem = gv_smem;
+  unsigned char* ring = smem;                                                         // NSTAGE x 16 KB
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + GV_NSTAGE * GV_STAGE_BYTES);    // [NSTAGE]
+  uint64_t* empty = full + GV_NSTAGE;                                                 // [NSTAGE]
+  float* red = reinterpret_cast<float*>(empty + GV_NSTAGE);                           // [RBB][NT][W][32][4]
+  float* s_inv = red + GV_RBB * NT * GV_CWARPS * kWarp * 4;                           // [3][16]
+  float* s_sq = s_inv + GEMV_MAXSEG * 16;                                             // [RBB*16][16]
+  float* s_ss = s_sq + GV_RBB * 16 * 16;                                              // [16]
+  int* s_tok = reinterpret_cast<int*>(s_ss + 16);                                     // [16]
+  unsigned long long* s_key = reinterpret_cast<unsigned long long*>(s_tok + 16);      // [16]
 
-  pdl_launch_dependents();
+  const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
   const int G = p.group;
   const int nunits = p.Np / (16 * G);
   const int u0 = int((long long)blockIdx.x * nunits / gridDim.x);
   const int u1 = int((long long)(blockIdx.x + 1) * nunits / gridDim.x);
-  const int KT = p.Kp / 16;
-  const long long rb_bytes = (long long)KT * 512;
-  const char* slice = static_cast<const char*>(p.w) + (long long)u0 * G * rb_bytes;
-  const long long slice_bytes = (long long)(u1 - u0) * G * rb_bytes;
-  // weights do not depend on the previous kernel: start streaming them before waiting on it
-  prefetch_slice(slice, 0, slice_bytes < GEMV_PREFETCH_WINDOW ? slice_bytes : GEMV_PREFETCH_WINDOW);
-  pdl_wait();
-
-  const int L = gemv_rows(p);
-  const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
-  if (tid < GEMV_MAXL) s_key[tid] = 0ull;
-  gemv_prologue_stats(p, L, s_tok, s_inv, s_red);
-
-  const int nchunks = (KT + GEMV_KTC - 1) / GEMV_KTC;
-  const bool wb = blockIdx.x == 0 && gemv_has_write_back(p);
-  if (nchunks == 1) {
-    gemv_build_chunk<NT>(p, L, 0, xs, s_tok, s_inv, wb);
-    __syncthreads();
-  }
-  const uint4* W = static_cast<const uint4*>(p.w);
-  const int units_per_batch = GEMV_RBB / G;
-
-  for (int ub = u0; ub < u1; ub += units_per_batch) {
-    const int nrb = min(units_per_batch, u1 - ub) * G;  // row blocks in this batch
-    const int rb0 = ub * G;
-    {  // keep the prefetch window running ahead of consumption
-      const long long done = (long long)(rb0 - u0 * G) * rb_bytes;
-      const long long a = done + GEMV_PREFETCH_WINDOW, b = a + (long long)nrb * rb_bytes;
-      if (ub > u0 && a < slice_bytes) prefetch_slice(slice, a, b < slice_bytes ? b : slice_bytes);
+  const int KT = p.Kp >> 4;
+  const int nslab = KT / GV_SLAB;
+  const int rb_first = u0 * G, nrb = (u1 - u0) * G;
+  const int total = nrb * nslab;  // ring stages: row-block major, slab minor
+  if (tid == 0) {
+    for (int s = 0; s < GV_NSTAGE; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, GV_CWARPS);
     }
-    float acc[GEMV_RBB][NT][4];
+    mbar_fence_init();
+  }
+  __syncthreads();
+  pdl_launch_dependents();
+
+  if (warp == GV_CWARPS) {  // ---- producer: the weights do not depend on the previous kernel
+    if (lane == 0) {
+      const char* wbase = static_cast<const char*>(p.w) + size_t(rb_first) * KT * 512;
+      int issued = 0;
+      for (int q = 0; q < total; ++q) {
+        const int s = q % GV_NSTAGE;
+        // the first refill waits for the consumers, i.e. for the previous kernel: a long bound
+        if (q >= GV_NSTAGE && !mbar_wait(empty + s, ((q / GV_NSTAGE) - 1) & 1, 1u << 26)) {
+          raise_error(p.err, kErrTimeout);
+          break;
+        }
+        mbar_arrive_expect_tx(full + s, GV_STAGE_BYTES);
+        bulk_g2s(ring + s * GV_STAGE_BYTES, wbase + size_t(q) * GV_STAGE_BYTES, GV_STAGE_BYTES, full + s);
+        ++issued;
+      }
+      // the block's shared memory must outlive every copy issued into it, also when the
+      // consumers gave up on a wait: wait (bounded) for the last copy of each slot
+      for (int q = max(0, issued - GV_NSTAGE); q < issued; ++q)
+        if (!mbar_wait(full + q % GV_NSTAGE, (q / GV_NSTAGE) & 1)) raise_error(p.err, kErrTimeout);
+    }
+    return;
+  }
+
+  // ---- consumers
+  pdl_wait();
+  const int L = gemv_rows(p.L_dev, p.L, p.L_max, p.err);
+  if (tid < 16) {
+    s_key[tid] = 0ull;
+    s_ss[tid] = 0.f;
+  }
+  gemv_prologue(p, L, s_tok, s_inv, s_sq);
+
+  bool ok = true;
+  for (int b0 = 0; b0 < nrb; b0 += GV_RBB) {
+    const int nb = min(GV_RBB, nrb - b0);
+    float tot[GV_RBB][NT][4];
 #pragma unroll
-    for (int j = 0; j < GEMV_RBB; ++j)
+    for (int j = 0; j < GV_RBB; ++j)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc[j][nt][e] = 0.f;
-
-    for (int c = 0; c < nchunks; ++c) {
-      if (nchunks > 1) {
-        __syncthreads();
-        gemv_build_chunk<NT>(p, L, c, xs, s_tok, s_inv, wb && ub == u0);
-        __syncthreads();
-      }
-      const int kt0 = c * GEMV_KTC;
-      const int ktn = min(GEMV_KTC, KT - kt0);
+        for (int e = 0; e < 4; ++e) tot[j][nt][e] = 0.f;
 #pragma unroll
-      for (int j = 0; j < GEMV_RBB; ++j) {
-        if (j >= nrb) break;
-        const uint4* wt = W + (size_t(rb0 + j) * KT + kt0) * kWarp + lane;
-        uint4 a[GEMV_TPW];
+    for (int j = 0; j < GV_RBB; ++j) {
+      if (j >= nb) break;
+      float acc[NT][4];
 #pragma unroll
-        for (int i = 0; i < GEMV_TPW; ++i) {
-          const int kl = warp + i * GEMV_WARPS;
-          if (kl < ktn) a[i] = ldg_stream(wt + size_t(kl) * kWarp);
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+      int seg = 0, seg_k0 = 0, seg_end = p.seg[0].lenp / GV_COLS;  // segment and its first / end slab
+      for (int slab = 0; slab < nslab; ++slab) {
+        const int q = (b0 + j) * nslab + slab, s = q % GV_NSTAGE;
+        if (ok && !mbar_wait(full + s, (q / GV_NSTAGE) & 1)) {
+          raise_error(p.err, kErrTimeout);
+          ok = false;
         }
+        if (ok) {
+          const uint4* A = reinterpret_cast<const uint4*>(ring + s * GV_STAGE_BYTES);
+          const XSeg& sg = p.seg[seg];
 #pragma unroll
-        for (int i = 0; i < GEMV_TPW; ++i) {
-          const int kl = warp + i * GEMV_WARPS;
-          if (kl < ktn) {
+          for (int i = 0; i < GV_TPW; ++i) {
+            const int kl = warp + i * GV_CWARPS;
+            const uint4 a = A[kl * kWarp + lane];
+            const int kt_in_seg = slab * GV_SLAB + kl - seg_k0;
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-              const uint4 b = xs[(size_t(nt) * GEMV_KTC + kl) * kWarp + lane];
-              mma_bf16_16816(acc[j][nt], a[i], b.x, b.y);
-              mma_bf16_16816(acc[j][nt], a[i], b.z, b.w);
+              const uint4 b = xseg_b(sg, kt_in_seg, nt, lane, L, s_tok);
+              mma_bf16_16816(acc[nt], a, b.x, b.y);
+              mma_bf16_16816(acc[nt], a, b.z, b.w);
             }
           }
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty + s);
+        if (slab + 1 == seg_end) {  // fold the segment with its 1/rms per activation row
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const int l = nt * 8 + 2 * (lane & 3) + (e & 1);
+              tot[j][nt][e] += acc[nt][e] * s_inv[seg * 16 + l];
+              acc[nt][e] = 0.f;
+            }
+          seg_k0 = seg_end * GV_SLAB;
+          ++seg;
+          if (seg < p.nseg) seg_end += p.seg[seg].lenp / GV_COLS;
+        }
       }
     }
-    // cross-warp reduction of the split-K partials
+    // ---- cross-warp reduction and epilogue
 #pragma unroll
-    for (int j = 0; j < GEMV_RBB; ++j)
+    for (int j = 0; j < GV_RBB; ++j)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
-        *reinterpret_cast<float4*>(&red[(((j * NT + nt) * GEMV_WARPS + warp) * kWarp + lane) * 4]) =
-            make_float4(acc[j][nt][0], acc[j][nt][1], acc[j][nt][2], acc[j][nt][3]);
-    __syncthreads();
-    const int jcount = (p.epi == EPI_SWIGLU) ? nrb / 2 : nrb;
-    for (int idx = tid; idx < jcount * NT * kWarp * 4; idx += GEMV_THREADS) {
+        *reinterpret_cast<float4*>(&red[(((j * NT + nt) * GV_CWARPS + warp) * kWarp + lane) * 4]) =
+            make_float4(tot[j][nt][0], tot[j][nt][1], tot[j][nt][2], tot[j][nt][3]);
+    named_sync(1, GV_CTHREADS);
+    const int rb0 = rb_first + b0;
+    const bool swiglu = p.epi == EPI_SWIGLU;
+    const int jcount = swiglu ? nb / 2 : nb;
+    for (int idx = tid; idx < jcount * NT * kWarp * 4; idx += GV_CTHREADS) {
       const int e = idx % 4, ln = (idx / 4) % kWarp, nt = (idx / (4 * kWarp)) % NT, jj = idx / (4 * kWarp * NT);
       const int g = ln / 4, t = ln % 4;
       const int l = nt * 8 + 2 * t + (e & 1);
       const int r16 = g + ((e & 2) ? 8 : 0);
-      if (l >= L) continue;
-      if (p.epi == EPI_SWIGLU) {
-        const int jg = jj * 2, ju = jj * 2 + 1;
+      float v = 0.f;
+      int n;
+      if (swiglu) {
         float gs = 0.f, us = 0.f;
 #pragma unroll
-        for (int w = 0; w < GEMV_WARPS; ++w) {
-          gs += red[(((jg * NT + nt) * GEMV_WARPS + w) * kWarp + ln) * 4 + e];
-          us += red[(((ju * NT + nt) * GEMV_WARPS + w) * kWarp + ln) * 4 + e];
+        for (int w = 0; w < GV_CWARPS; ++w) {
+          gs += red[((((2 * jj) * NT + nt) * GV_CWARPS + w) * kWarp + ln) * 4 + e];
+          us += red[((((2 * jj + 1) * NT + nt) * GV_CWARPS + w) * kWarp + ln) * 4 + e];
         }
-        const int n = ((rb0 / 2) + jj) * 16 + r16;
-        if (n < p.N) p.y[size_t(l) * p.ldy + n] = gs / (1.f + expf(-gs)) * us;
+        n = ((rb0 / 2) + jj) * 16 + r16;
+        v = gs / (1.f + expf(-gs)) * us;
       } else {
-        float s = 0.f;
 #pragma unroll
-        for (int w = 0; w < GEMV_WARPS; ++w) s += red[(((jj * NT + nt) * GEMV_WARPS + w) * kWarp + ln) * 4 + e];
-        const int n = (rb0 + jj) * 16 + r16;
-        if (n < p.N) {
-          if (p.epi == EPI_ARGMAX) {
-            if (p.y) p.y[size_t(l) * p.ldy + n] = s;
-            atomicMax(&s_key[l], argmax_key(s, uint32_t(n)));
-          } else {
-            gemv_store(p, l, n, s);
-          }
+        for (int w = 0; w < GV_CWARPS; ++w) v += red[(((jj * NT + nt) * GV_CWARPS + w) * kWarp + ln) * 4 + e];
+        n = (rb0 + jj) * 16 + r16;
+      }
+      float sq = 0.f;
+      if (l < L && n < p.N) {
+        if (p.epi == EPI_ARGMAX) {
+          if (p.y) p.y[size_t(l) * p.ldy + n] = v;
+          atomicMax(&s_key[l], argmax_key(v, uint32_t(n)));
+        } else {
+          if (p.epi == EPI_ADD) v += p.base[size_t(l) * p.ldb + n];
+          if (p.y) p.y[size_t(l) * p.ldy + n] = v;
+          if (p.y2) p.y2[size_t(l) * p.ldy2 + n] = v;
+          for (int o = 0; o < p.nout; ++o)
+            xf_store(p.out[o].xf, p.out_width, l, n, p.out[o].w ? v * p.out[o].w[n] : v);
+          sq = v * v;
         }
       }
+      if (p.ss_out) s_sq[(jj * 16 + r16) * 16 + l] = sq;  // every (feature, row) slot written once
     }
-    __syncthreads();
+    named_sync(1, GV_CTHREADS);
+    if (p.ss_out && tid < L) {  // fixed-order per-row sum over this batch's features
+      float a = 0.f;
+      for (int f = 0; f < jcount * 16; ++f) a += s_sq[f * 16 + tid];
+      s_ss[tid] += a;
+    }
   }
   if (p.epi == EPI_ARGMAX && tid < L && s_key[tid] != 0ull) atomicMax(&p.keys[tid], s_key[tid]);
+  if (p.ss_out && tid < 16) p.ss_out[blockIdx.x * 16 + tid] = tid < L ? s_ss[tid] : 0.f;
+  if (p.side_src && int(blockIdx.x) < p.side_blocks) {
+    named_sync(1, GV_CTHREADS);
+    gemv_side_job(p, L, s_inv, s_sq, GV_CTHREADS, true);
+  }
 }
 
 template <int NT>
-size_t gemv_bf16_smem() {
-  return size_t(NT) * GEMV_KTC * kWarp * 16 + size_t(GEMV_RBB) * NT * GEMV_WARPS * kWarp * 4 * 4 +
-         GEMV_MAXL * GEMV_MAXSEG * 4 + GEMV_WARPS * GEMV_MAXL * 4 + GEMV_MAXL * 4 + GEMV_MAXL * 8 + 16;
+constexpr size_t gemv_bf16_smem() {
+  return size_t(GV_NSTAGE) * GV_STAGE_BYTES + 2 * GV_NSTAGE * 8 + size_t(GV_RBB) * NT * GV_CWARPS * kWarp * 4 * 4 +
+         GEMV_MAXSEG * 16 * 4 + GV_RBB * 16 * 16 * 4 + 16 * 4 + 16 * 4 + 16 * 8 + 128;
 }
 
-// ----------------------------------------------------------------------------- fp32 / FMA path
-
-// x lives in smem as fp32 [L][Kp]; each warp computes whole output rows, lanes split K.
-__global__ void __launch_bounds__(GEMV_THREADS) gemv_f32_kernel(const GemvParams p) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  float* xs = reinterpret_cast<float*>(smem);  // L_max * Kp
-  float* s_inv = xs + size_t(p.L_max) * p.Kp;
-  float* s_red = s_inv + GEMV_MAXL * GEMV_MAXSEG;
-  int* s_tok = reinterpret_cast<int*>(s_red + GEMV_WARPS * GEMV_MAXL);
-  unsigned long long* s_key = reinterpret_cast<unsigned long long*>(s_tok + GEMV_MAXL);
+// ----------------------------------------------------------------------------- fp32 models
+// Inputs are staged in shared memory with their 1/rms applied, then one warp per output
+// feature (or gate/up pair) runs CUDA-core FMA over the fp32 row; same epilogues.
+__global__ void __launch_bounds__(GV_F32_THREADS) gemv_f32_kernel(const GemvParams p) {
+  extern __shared__ __align__(16) unsigned char gf_smem[];
+  float* xs = reinterpret_cast<float*>(gf_smem);  // [L_max][Kp]
+  float* s_inv = xs + size_t(p.L_max) * p.Kp;   // [3][16]
+  float* s_part = s_inv + GEMV_MAXSEG * 16;     // [256]
+  float* s_ss = s_part + 256;                   // [16]
+  int* s_tok = reinterpret_cast<int*>(s_ss + 16);
+  unsigned long long* s_key = reinterpret_cast<unsigned long long*>(s_tok + 16);
 
   pdl_launch_dependents();
   pdl_wait();
-  const int L = gemv_rows(p);
+  const int L = gemv_rows(p.L_dev, p.L, p.L_max, p.err);
   const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
-  if (tid < GEMV_MAXL) s_key[tid] = 0ull;
-  gemv_prologue_stats(p, L, s_tok, s_inv, s_red);
-  const bool wb = blockIdx.x == 0 && gemv_has_write_back(p);
-  const int kq = p.K / 4;
-  for (int idx = tid; idx < L * kq; idx += GEMV_THREADS) {
-    const int l = idx / kq, k = (idx % kq) * 4;
+  if (tid < 16) {
+    s_key[tid] = 0ull;
+    s_ss[tid] = 0.f;
+  }
+  gemv_prologue(p, L, s_tok, s_inv, s_part);
+  for (int idx = tid; idx < L * p.Kp; idx += GV_F32_THREADS) {
+    const int l = idx / p.Kp, k = idx % p.Kp;
+    float v = 0.f;
     int off = 0;
     for (int s = 0; s < p.nseg; ++s) {
-      const Seg& sg = p.seg[s];
+      const XSeg& sg = p.seg[s];
       if (k < off + sg.len) {
-        const float4 v = seg_load4(sg, l, k - off, s_tok);
-        const float inv = s_inv[l * GEMV_MAXSEG + s];
-        const float4 w = sg.norm_w ? *reinterpret_cast<const float4*>(sg.norm_w + (k - off))
-                                   : make_float4(1.f, 1.f, 1.f, 1.f);
-        const float4 x = make_float4(v.x * inv * w.x, v.y * inv * w.y, v.z * inv * w.z, v.w * inv * w.w);
-        *reinterpret_cast<float4*>(&xs[size_t(l) * p.Kp + k]) = x;
-        if (wb && sg.write_back) *reinterpret_cast<float4*>(sg.write_back + size_t(l) * sg.ld_wb + (k - off)) = x;
+        const int i = k - off;
+        v = sg.xf ? reinterpret_cast<const float*>(sg.xf)[size_t(l) * sg.len + i]
+                  : static_cast<const float*>(sg.table)[size_t(s_tok[l]) * sg.len + i] * sg.norm_w[i];
+        v *= s_inv[s * 16 + l];
         break;
       }
       off += sg.len;
     }
+    xs[idx] = v;
   }
-  for (int idx = tid; idx < L * (p.Kp - p.K); idx += GEMV_THREADS)
-    xs[size_t(idx / (p.Kp - p.K)) * p.Kp + p.K + idx % (p.Kp - p.K)] = 0.f;
   __syncthreads();
-  const int rows_per_unit = p.group;  // SwiGLU: gate row n and up row n are rows 2n, 2n+1 (interleaved)
-  const int nunits = p.N;             // one unit = one output feature (1 or 2 weight rows)
+  const int G = p.group;
+  const int nunits = p.N;
   const int u0 = int((long long)blockIdx.x * nunits / gridDim.x);
   const int u1 = int((long long)(blockIdx.x + 1) * nunits / gridDim.x);
   const float* W = static_cast<const float*>(p.w);
   unsigned long long best[GEMV_MAXL];
+  float ssl[GEMV_MAXL];
 #pragma unroll
-  for (int l = 0; l < GEMV_MAXL; ++l) best[l] = 0ull;
-  for (int u = u0 + warp; u < u1; u += GEMV_WARPS) {
+  for (int l = 0; l < GEMV_MAXL; ++l) {
+    best[l] = 0ull;
+    ssl[l] = 0.f;
+  }
+  for (int u = u0 + warp; u < u1; u += GV_F32_WARPS) {
     float acc[2][GEMV_MAXL];
 #pragma unroll
     for (int r = 0; r < 2; ++r)
@@ -458,8 +472,8 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_f32_kernel(const GemvParams
       for (int l = 0; l < GEMV_MAXL; ++l) acc[r][l] = 0.f;
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
-      if (r >= rows_per_unit) break;
-      const float* wr = W + size_t(u * rows_per_unit + r) * p.Kp;
+      if (r >= G) break;
+      const float* wr = W + size_t(u * G + r) * p.Kp;
       for (int k = lane * 4; k < p.Kp; k += kWarp * 4) {
         const float4 w4 = ldg_stream_f4(reinterpret_cast<const float4*>(wr + k));
 #pragma unroll
@@ -475,16 +489,20 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_f32_kernel(const GemvParams
     for (int l = 0; l < GEMV_MAXL; ++l) {
       if (l < L) {
         const float s0 = warp_sum(acc[0][l]);
-        const float s1 = rows_per_unit == 2 ? warp_sum(acc[1][l]) : 0.f;
+        const float s1 = G == 2 ? warp_sum(acc[1][l]) : 0.f;
         if (lane == 0) {
-          if (p.epi == EPI_SWIGLU) {
-            p.y[size_t(l) * p.ldy + u] = s0 / (1.f + expf(-s0)) * s1;
-          } else if (p.epi == EPI_ARGMAX) {
+          if (p.epi == EPI_ARGMAX) {
             if (p.y) p.y[size_t(l) * p.ldy + u] = s0;
             const unsigned long long k = argmax_key(s0, uint32_t(u));
             if (k > best[l]) best[l] = k;
           } else {
-            gemv_store(p, l, u, s0);
+            float v = (p.epi == EPI_SWIGLU) ? s0 / (1.f + expf(-s0)) * s1 : s0;
+            if (p.epi == EPI_ADD) v += p.base[size_t(l) * p.ldb + u];
+            if (p.y) p.y[size_t(l) * p.ldy + u] = v;
+            if (p.y2) p.y2[size_t(l) * p.ldy2 + u] = v;
+            for (int o = 0; o < p.nout; ++o)
+              reinterpret_cast<float*>(p.out[o].xf)[size_t(l) * p.N + u] = p.out[o].w ? v * p.out[o].w[u] : v;
+            ssl[l] = fmaf(v, v, ssl[l]);
           }
         }
       }
@@ -499,11 +517,27 @@ __global__ void __launch_bounds__(GEMV_THREADS) gemv_f32_kernel(const GemvParams
     __syncthreads();
     if (tid < L && s_key[tid] != 0ull) atomicMax(&p.keys[tid], s_key[tid]);
   }
+  if (p.ss_out) {  // fixed order: lane 0 of each warp holds its features' partials
+    if (lane == 0) {
+#pragma unroll
+      for (int l = 0; l < GEMV_MAXL; ++l) s_part[warp * 16 + l] = ssl[l];
+    }
+    __syncthreads();
+    if (tid < 16) {
+      float a = 0.f;
+      if (tid < L)
+        for (int w = 0; w < GV_F32_WARPS; ++w) a += s_part[w * 16 + tid];
+      p.ss_out[blockIdx.x * 16 + tid] = a;
+    }
+  }
+  if (p.side_src && int(blockIdx.x) < p.side_blocks) {
+    __syncthreads();
+    gemv_side_job(p, L, s_inv, s_part, GV_F32_THREADS, false);
+  }
 }
 
 inline size_t gemv_f32_smem(int L_max, int Kp) {
-  return size_t(L_max) * Kp * 4 + GEMV_MAXL * GEMV_MAXSEG * 4 + GEMV_WARPS * GEMV_MAXL * 4 + GEMV_MAXL * 4 +
-         GEMV_MAXL * 8 + 16;
+  return size_t(L_max) * Kp * 4 + GEMV_MAXSEG * 16 * 4 + 256 * 4 + 16 * 4 + 16 * 4 + 16 * 8 + 64;
 }
 
 }  // namespace wc

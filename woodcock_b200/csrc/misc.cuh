@@ -28,38 +28,103 @@ struct RoundState {
   unsigned long long keys[MAXKEYS];  // argmax keys: draft steps [0, K), verify rows [K, 2K+1)
 };
 
-// ----------------------------------------------------------------------------- embeddings
+// ----------------------------------------------------------------------------- activation packing
 
-// dst[l][d] = table[tok_l][d] (fp32 out); tokens from `tokens` or, when keys != nullptr,
-// row 0 from x0 and rows 1.. from the argmax keys (draft tokens, mapped + forced).
-__global__ void embed_rows_kernel(const void* table, int dtype, int vocab, int d, const int* tokens, int L,
-                                  const int* L_dev, float* dst, RoundState* st, const int* vocab_map, int K,
-                                  int* err) {
+// Writes the GEMV input form of L rows (one block per row): fragments of x * w (bf16 models)
+// or fp32 rows x * w [16][K] (fp32 models), the row's sum of squares of x into ss[l]
+// (a single-part statistic), and optionally an fp32 copy of x. Rows come from fp32
+// activations (src + l * ld) or from an embedding table gathered by token id; for the
+// verify input the tokens are [x_n, d_1..d_K] resolved from the round state.
+struct PackParams {
+  const float* src;
+  int ld;
+  const void* table;   // [vocab][K] of table_dtype (when src == nullptr)
+  int table_dtype;
+  const int* tokens;
+  RoundState* st;      // tokens from the round state (verify input)
+  const int* vocab_map;
+  int vocab;
+  int K;
+  int L;
+  const int* L_dev;
+  const float* w;      // scale written into the fragments (norm gain) or nullptr
+  uint32_t* xf;        // rows in the model's fragment format
+  int xf_width;        // fragment width (bf16: K padded to whole slabs)
+  int xf_fp32;
+  float* ss;           // [16] or nullptr
+  float* copy;         // [L][K] fp32 copy of x or nullptr
+  int* err;
+};
+
+__global__ void pack_rows_kernel(const PackParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int l = blockIdx.x;
-  const int Lr = L_dev ? *L_dev : L;
-  if (l >= Lr) return;
-  int tok;
-  if (st) {  // verify input: [x_n, d_1..d_K]
-    if (l == 0) {
-      tok = st->x_n;
-    } else if (st->forced[l - 1] >= 0) {
-      tok = st->forced[l - 1];
-    } else {
-      const uint32_t idx = argmax_key_index(st->keys[l - 1]);
-      tok = vocab_map ? vocab_map[idx] : int(idx);
+  const int L = p.L_dev ? *p.L_dev : p.L;
+  if (l >= L) return;
+  __shared__ int s_tok;
+  __shared__ float red[32];
+  if (threadIdx.x == 0) {
+    int tok = 0;
+    if (!p.src) {
+      if (p.st) {
+        if (l == 0) tok = p.st->x_n;
+        else if (p.st->forced[l - 1] >= 0) tok = p.st->forced[l - 1];
+        else {
+          const uint32_t idx = argmax_key_index(p.st->keys[l - 1]);
+          tok = p.vocab_map ? p.vocab_map[idx] : int(idx);
+        }
+      } else {
+        tok = p.tokens[l];
+      }
+      if (tok < 0 || tok >= p.vocab) {
+        raise_error(p.st ? &p.st->err : p.err, kErrTokenRange);
+        tok = 0;
+      }
+      if (p.st) p.st->tokens[l] = tok;
     }
-  } else {
-    tok = tokens[l];
+    s_tok = tok;
   }
-  if (tok < 0 || tok >= vocab) {
-    if (threadIdx.x == 0) raise_error(st ? &st->err : err, kErrTokenRange);
-    tok = 0;
+  __syncthreads();
+  float ss = 0.f;
+  for (int k = threadIdx.x; k < p.K; k += blockDim.x) {
+    float v;
+    if (p.src) v = p.src[size_t(l) * p.ld + k];
+    else {
+      const size_t o = size_t(s_tok) * p.K + k;
+      v = p.table_dtype == 1 ? bf16_bits_to_f32(static_cast<const uint16_t*>(p.table)[o])
+                             : static_cast<const float*>(p.table)[o];
+    }
+    ss = fmaf(v, v, ss);
+    if (p.copy) p.copy[size_t(l) * p.K + k] = v;
+    const float x = p.w ? v * p.w[k] : v;
+    if (p.xf_fp32) reinterpret_cast<float*>(p.xf)[size_t(l) * p.K + k] = x;
+    else xf_store(p.xf, p.xf_width, l, k, x);
   }
-  if (st && threadIdx.x == 0) st->tokens[l] = tok;
-  const size_t base = size_t(tok) * d;
-  for (int i = threadIdx.x; i < d; i += blockDim.x)
-    dst[size_t(l) * d + i] = dtype == 1 ? bf16_bits_to_f32(static_cast<const uint16_t*>(table)[base + i])
-                                        : static_cast<const float*>(table)[base + i];
+  if (p.ss) {
+    ss = warp_sum(ss);
+    if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = ss;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float a = 0.f;
+      for (int w = 0; w < int(blockDim.x / 32); ++w) a += red[w];
+      p.ss[l] = a;
+    }
+  }
+}
+
+// 1/rms of every row of an embedding table (the drafter's auxiliary-stream norm per token)
+__global__ void row_inv_kernel(const void* table, int dtype, int rows, int K, float eps, float* out) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) / 32, lane = threadIdx.x % 32;
+  if (warp >= rows) return;
+  double ss = 0.0;
+  for (int k = lane; k < K; k += 32) {
+    const size_t o = size_t(warp) * K + k;
+    const float v = dtype == 1 ? bf16_bits_to_f32(static_cast<const uint16_t*>(table)[o]) : static_cast<const float*>(table)[o];
+    ss += double(v) * double(v);
+  }
+  ss = warp_sum_d(ss);
+  if (lane == 0) out[warp] = 1.f / sqrtf(float(ss / K) + eps);
 }
 
 // ----------------------------------------------------------------------------- ops API row kernels
@@ -442,6 +507,8 @@ __global__ void philox_uniforms_kernel(uint64_t seed, uint64_t offset, int n, do
 // compaction keeps rows 0..a, i.e. the target cache size becomes n + a + 1 (no data
 // moves). Resets every argmax key for the next round.
 __global__ void accept_chain_kernel(RoundState* st, int K, const int* vocab_map_unused, int* out_host_view) {
+  pdl_launch_dependents();
+  pdl_wait();
   if (threadIdx.x != 0) return;
   int am[MAXK + 1];
   for (int i = 0; i <= K; ++i) am[i] = int(argmax_key_index(st->keys[K + i]));
@@ -463,36 +530,78 @@ __global__ void accept_chain_kernel(RoundState* st, int K, const int* vocab_map_
   (void)vocab_map_unused;
 }
 
-// End of the drafter update: out = RMSNorm(h) for the last row (already written back by
-// the caller when needed), root_out / root_fb from row L-1, drafter cache grows by L.
-__global__ void finish_update_kernel(RoundState* st, const int* L_dev, int L_static, const float* h, int d,
-                                     const float* norm_w, float eps, int post_norm, float* root_out, float* root_fb,
-                                     int advance_dc) {
+// End of the drafter update (and of the drafter prefill): out = RMSNorm(h[L-1]) with the
+// drafter's final norm; root_out (head input of the next round's first draft step) and
+// root_fb (feature of its first drafter pass: out with post_norm, else h) as fp32 rows and
+// as GEMV input fragments (root_fb times the layer-0 input norm gain, with its sum of
+// squares); with advance_dc the drafter cache grows by L.
+struct FinishParams {
+  RoundState* st;
+  const int* L_dev;
+  int L_static;
+  const float* h;
+  int d;
+  const float* norm_w;
+  float eps;
+  int post_norm;
+  float* root_out;
+  float* root_fb;
+  uint32_t* xf_out;   // fragments of root_out (no scale)
+  uint32_t* xf_fb;    // fragments of root_fb * in_norm0
+  const float* in_norm0;
+  float* ss_fb;       // [16]: row 0 = sum of root_fb^2
+  int xf_width;       // fragment width (bf16: d padded to whole slabs)
+  int xf_fp32;
+  int advance_dc;
+};
+
+__global__ void finish_update_kernel(const FinishParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
   __shared__ float red[32];
-  const int L = L_dev ? *L_dev : L_static;
-  if (L < 1 || L > L_static) {
-    if (threadIdx.x == 0) raise_error(&st->err, kErrRows);
+  __shared__ float s_inv;
+  const int L = p.L_dev ? *p.L_dev : p.L_static;
+  if (L < 1 || L > p.L_static) {
+    if (threadIdx.x == 0) raise_error(&p.st->err, kErrRows);
     return;
   }
-  const float* hr = h + size_t(L - 1) * d;
+  const float* hr = p.h + size_t(L - 1) * p.d;
   float ss = 0.f;
-  for (int i = threadIdx.x; i < d; i += blockDim.x) ss = fmaf(hr[i], hr[i], ss);
+  for (int i = threadIdx.x; i < p.d; i += blockDim.x) ss = fmaf(hr[i], hr[i], ss);
   ss = warp_sum(ss);
   if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = ss;
   __syncthreads();
-  if (threadIdx.x < 32) {
-    float v = threadIdx.x < blockDim.x / 32 ? red[threadIdx.x] : 0.f;
-    v = warp_sum(v);
-    if (threadIdx.x == 0) red[0] = v;
+  if (threadIdx.x == 0) {
+    float a = 0.f;
+    for (int w = 0; w < int(blockDim.x / 32); ++w) a += red[w];
+    s_inv = 1.f / sqrtf(a / float(p.d) + p.eps);
   }
   __syncthreads();
-  const float inv = 1.f / sqrtf(red[0] / float(d) + eps);
-  for (int i = threadIdx.x; i < d; i += blockDim.x) {
-    const float o = hr[i] * inv * norm_w[i];
-    root_out[i] = o;
-    root_fb[i] = post_norm ? o : hr[i];
+  float sf = 0.f;
+  for (int i = threadIdx.x; i < p.d; i += blockDim.x) {
+    const float o = hr[i] * s_inv * p.norm_w[i];
+    const float fb = p.post_norm ? o : hr[i];
+    p.root_out[i] = o;
+    p.root_fb[i] = fb;
+    sf = fmaf(fb, fb, sf);
+    if (p.xf_fp32) {
+      reinterpret_cast<float*>(p.xf_out)[i] = o;
+      reinterpret_cast<float*>(p.xf_fb)[i] = fb * p.in_norm0[i];
+    } else {
+      xf_store(p.xf_out, p.xf_width, 0, i, o);
+      xf_store(p.xf_fb, p.xf_width, 0, i, fb * p.in_norm0[i]);
+    }
   }
-  if (threadIdx.x == 0 && advance_dc) st->dc_len += L;
+  sf = warp_sum(sf);
+  __syncthreads();
+  if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = sf;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float a = 0.f;
+    for (int w = 0; w < int(blockDim.x / 32); ++w) a += red[w];
+    p.ss_fb[0] = a;
+    if (p.advance_dc) p.st->dc_len += L;
+  }
 }
 
 }  // namespace wc

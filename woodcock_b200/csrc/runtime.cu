@@ -103,7 +103,10 @@ struct wc_ctx {
   Profiler* prof = nullptr;  // set while a profiled round is being captured
   bool pdl = true;           // programmatic dependent launch between round kernels
   bool attn_mma = true;      // tensor-core attention for bf16 caches
-  int gemv_blocks_per_sm = 1;
+  int gemv_blocks_per_sm = 2;
+  uint32_t* lin_xf = nullptr;  // input fragments of the ops-API linear
+  int lin_xf_k = 0;
+  bool lin_xf_bf16 = false;
 };
 
 namespace {
@@ -339,27 +342,42 @@ int grid_for(size_t n) { return int(std::min<size_t>((n + 255) / 256, 148 * 16))
 
 // One projection in its streaming layout. N = output features; for SwiGLU (group 2)
 // the stored matrix holds 2 * N rows (gate and up interleaved by 16-row blocks, or
-// rows 2n / 2n+1 in the fp32 layout).
+// rows 2n / 2n+1 in the fp32 layout). The input is one to three segments side by side;
+// in the bf16 layout each segment starts on a whole ring slab (512 columns) and its
+// padding columns are zero.
 struct Lin {
   void* w = nullptr;
   int N = 0, Np = 0, K = 0, Kp = 0, dtype = 0, group = 1;
+  int nseg = 1;
+  int seg_len[GEMV_MAXSEG] = {0, 0, 0};
+  int seg_off[GEMV_MAXSEG] = {0, 0, 0};
   size_t bytes = 0;
   bool owned = true;
 };
 
-Lin make_lin(int dtype, int N, int K, int group) {
+Lin make_lin(int dtype, int N, std::initializer_list<int> segs, int group) {
   Lin l;
   l.dtype = dtype;
   l.N = N;
-  l.K = K;
   l.group = group;
-  if (dtype == WC_BF16) {
+  const bool bf16 = dtype == WC_BF16;
+  int off = 0;
+  l.nseg = 0;
+  for (int s : segs) {
+    if (l.nseg == GEMV_MAXSEG) fail(WC_ERR_INVALID, "too many input segments");
+    l.seg_len[l.nseg] = s;
+    l.seg_off[l.nseg] = off;
+    off += xf_width(bf16, s);
+    l.K += s;
+    ++l.nseg;
+  }
+  if (bf16) {
     l.Np = ((N + 15) / 16) * 16 * group;
-    l.Kp = ((K + 15) / 16) * 16;
+    l.Kp = off;
     l.bytes = size_t(l.Np) * l.Kp * 2;
   } else {
     l.Np = N * group;
-    l.Kp = ((K + 3) / 4) * 4;
+    l.Kp = ((off + 3) / 4) * 4;
     l.bytes = size_t(l.Np) * l.Kp * 4;
   }
   l.w = dalloc(l.bytes);
@@ -372,12 +390,13 @@ void free_lin(Lin& l) {
   l.w = nullptr;
 }
 
-// Places a row-major part [rows][cols] at (row_off, col_off); `which` selects gate (0) /
-// up (1) for a SwiGLU projection.
-void lin_put(wc_ctx* ctx, Lin& l, const Staged& s, int rows, int cols, int row_off, int col_off, int which) {
+// Places a row-major part [rows][cols] at output row row_off of input segment `seg`;
+// `which` selects gate (0) / up (1) for a SwiGLU projection.
+void lin_put(wc_ctx* ctx, Lin& l, const Staged& s, int rows, int cols, int row_off, int seg, int which) {
+  if (seg < 0 || seg >= l.nseg || cols != l.seg_len[seg]) fail(WC_ERR_INVALID, "projection part does not fit");
+  const int col_off = l.seg_off[seg];
   if (l.dtype == WC_BF16) {
-    if (row_off % 16 || col_off % 16)
-      fail(WC_ERR_UNSUPPORTED, "projection parts must start on 16-row / 16-column boundaries");
+    if (row_off % 16) fail(WC_ERR_UNSUPPORTED, "projection parts must start on 16-row boundaries");
     const int KT = l.Kp / 16;
     tile_part_kernel<<<grid_for(size_t(rows) * cols), 256, 0, ctx->stream>>>(
         s.ptr, s.dtype, rows, cols, static_cast<uint16_t*>(l.w), KT, l.group, (row_off / 16) * l.group + which,
@@ -396,81 +415,128 @@ struct wc_weight {
   Lin lin;
 };
 
-// ============================================================================ GEMV launcher
+// ============================================================================ GEMV / attention launchers
 
 namespace {
 
-struct GemvPlan {
-  const Lin* W;
-  GemvParams p;
+// A GEMV input held as fragments (common.cuh) with the partial sums of squares of its
+// rows ([nparts][16], nullptr when the consumer does not normalise it).
+struct XIn {
+  const uint32_t* xf = nullptr;
+  const float* ss = nullptr;
+  int nparts = 0;
 };
+
+int max_parts(const wc_ctx* ctx) { return ctx->num_sms * 4; }
+
+uint32_t* xf_alloc(bool bf16, int K) {
+  const size_t bytes = size_t(GEMV_MAXL) * xf_width(bf16, K) * 4;
+  auto* p = static_cast<uint32_t*>(dalloc(bytes));
+  CUDA_TRY(cudaMemset(p, 0, bytes));  // padding columns and unused rows stay finite
+  return p;
+}
+
+float* ss_alloc(const wc_ctx* ctx) {
+  const size_t bytes = sizeof(float) * max_parts(ctx) * 16;
+  auto* p = static_cast<float*>(dalloc(bytes));
+  CUDA_TRY(cudaMemset(p, 0, bytes));
+  return p;
+}
 
 GemvParams gemv_params() {
   GemvParams p;
   std::memset(&p, 0, sizeof(p));
-  p.eps = 1e-6f;
   p.group = 1;
   return p;
 }
 
-Seg seg_rows(const float* src, int ld, int len, const float* norm_w = nullptr, float* write_back = nullptr,
-             int ld_wb = 0) {
-  Seg s;
+XSeg xs_frag(const XIn& x, int len, bool bf16, float eps = 0.f) {
+  XSeg s;
   std::memset(&s, 0, sizeof(s));
-  s.src = src;
-  s.ld = ld;
+  s.xf = x.xf;
+  s.ss = x.ss;
+  s.nparts = x.nparts;
   s.len = len;
-  s.norm_w = norm_w;
-  s.write_back = write_back;
-  s.ld_wb = ld_wb;
+  s.lenp = xf_width(bf16, len);
+  s.eps = eps;
   return s;
 }
 
-Seg seg_embed(const void* table, int dtype, int len, const float* norm_w) {
-  Seg s;
+XSeg xs_embed(const void* table, int len, bool bf16, const float* norm_w, const float* row_inv) {
+  XSeg s;
   std::memset(&s, 0, sizeof(s));
   s.table = table;
-  s.table_dtype = dtype;
   s.len = len;
+  s.lenp = xf_width(bf16, len);
   s.norm_w = norm_w;
+  s.row_inv = row_inv;
   return s;
 }
 
+// Blocks of a GEMV launch over W with up to L_max rows: the part count of its ss_out.
+int gemv_grid(const wc_ctx* ctx, const Lin& W, int L_max) {
+  if (W.dtype == WC_BF16) {
+    const int NT = L_max <= 8 ? 1 : 2;
+    const int nunits = W.Np / (16 * W.group);
+    return std::max(1, std::min(nunits, ctx->num_sms * std::min(ctx->gemv_blocks_per_sm, ctx->occ_gemv[NT])));
+  }
+  return std::max(1, std::min((W.N + GV_F32_WARPS - 1) / GV_F32_WARPS, ctx->num_sms * 2));
+}
+
+// Part count of a head's side-job sums of squares.
+int side_parts(const wc_ctx* ctx, const Lin& W, int L_max) { return std::min(GV_SIDE_BLOCKS, gemv_grid(ctx, W, L_max)); }
+
 void launch_gemv(wc_ctx* ctx, const Lin& W, GemvParams p) {
+  const bool bf16 = W.dtype == WC_BF16;
   p.w = W.w;
   p.N = W.N;
   p.Np = W.Np;
-  p.K = W.K;
   p.Kp = W.Kp;
-  p.w_dtype = W.dtype;
   p.group = W.group;
   if (!p.err) p.err = ctx->d_err;
-  int klen = 0;
+  if (p.nseg != W.nseg) fail(WC_ERR_INVALID, "GEMV input segments do not match the weight");
   for (int s = 0; s < p.nseg; ++s) {
-    const Seg& sg = p.seg[s];
-    klen += sg.len;
-    // the prologue reads 4 columns at a time
-    if (sg.len % 4 || (!sg.table && (sg.ld % 4 || reinterpret_cast<uintptr_t>(sg.src) % 16)) ||
-        (sg.norm_w && reinterpret_cast<uintptr_t>(sg.norm_w) % 16) ||
-        (sg.write_back && (sg.ld_wb % 4 || reinterpret_cast<uintptr_t>(sg.write_back) % 16)))
-      fail(WC_ERR_INVALID, "GEMV inputs must be 16-byte aligned with widths and strides that are multiples of 4");
+    const XSeg& sg = p.seg[s];
+    if (sg.len != W.seg_len[s] || sg.lenp != xf_width(bf16, sg.len))
+      fail(WC_ERR_INVALID, "GEMV input width " + std::to_string(sg.len) + " != " + std::to_string(W.seg_len[s]));
+    if (sg.xf && sg.ss && (sg.nparts < 1 || sg.nparts > max_parts(ctx)))
+      fail(WC_ERR_INVALID, "GEMV input statistics have a bad part count");
+    if (!sg.xf && (!sg.table || !sg.norm_w || (bf16 && sg.len % 16)))
+      fail(WC_ERR_INVALID, "embedding segments need a table, a gain and a width that is a multiple of 16");
   }
-  if (klen != W.K) fail(WC_ERR_INVALID, "GEMV input width " + std::to_string(klen) + " != " + std::to_string(W.K));
   if (p.L_max < 1 || p.L_max > GEMV_MAXL) fail(WC_ERR_INVALID, "GEMV rows outside 1..16");
-  if (W.dtype == WC_BF16) {
-    const int NT = p.L_max <= 8 ? 1 : 2;
-    const int nunits = W.Np / (16 * W.group);
-    const int grid = std::max(1, std::min(nunits, ctx->num_sms * std::min(ctx->gemv_blocks_per_sm, ctx->occ_gemv[NT])));
-    if (NT == 1)
-      launch_ex(ctx, "gemv", gemv_bf16_kernel<1>, dim3(grid), dim3(GEMV_THREADS), gemv_bf16_smem<1>(), true, 1, p);
+  if (p.nout > 2 || (p.nout > 0 && p.epi == EPI_ARGMAX)) fail(WC_ERR_INVALID, "bad GEMV outputs");
+  p.out_width = xf_width(bf16, W.N);
+  const int grid = gemv_grid(ctx, W, p.L_max);
+  if (grid > max_parts(ctx)) fail(WC_ERR_INVALID, "GEMV grid above the statistics buffers");
+  if (p.side_src) {
+    p.side_width = xf_width(bf16, p.side_len);
+    p.side_blocks = std::min(GV_SIDE_BLOCKS, grid);
+  }
+  if (bf16) {
+    if (p.L_max <= 8)
+      launch_ex(ctx, "gemv", gemv_bf16_kernel<1>, dim3(grid), dim3(GV_THREADS), gemv_bf16_smem<1>(), true, 1, p);
     else
-      launch_ex(ctx, "gemv", gemv_bf16_kernel<2>, dim3(grid), dim3(GEMV_THREADS), gemv_bf16_smem<2>(), true, 1, p);
+      launch_ex(ctx, "gemv", gemv_bf16_kernel<2>, dim3(grid), dim3(GV_THREADS), gemv_bf16_smem<2>(), true, 1, p);
   } else {
     const size_t smem = gemv_f32_smem(p.L_max, W.Kp);
     if (smem > ctx->max_smem) fail(WC_ERR_UNSUPPORTED, "fp32 projection too wide for shared memory");
-    const int grid = std::max(1, std::min((W.N + GEMV_WARPS - 1) / GEMV_WARPS, ctx->num_sms * 2));
-    launch_ex(ctx, "gemv", gemv_f32_kernel, dim3(grid), dim3(GEMV_THREADS), smem, true, 1, p);
+    launch_ex(ctx, "gemv", gemv_f32_kernel, dim3(grid), dim3(GV_F32_THREADS), smem, true, 1, p);
   }
+}
+
+PackParams pack_params() {
+  PackParams p;
+  std::memset(&p, 0, sizeof(p));
+  return p;
+}
+
+// Rows -> GEMV input fragments (+ sums of squares, + fp32 copy); one block per row.
+void launch_pack(wc_ctx* ctx, PackParams p, bool bf16, int L_max) {
+  if (!p.err) p.err = ctx->d_err;
+  p.xf_width = xf_width(bf16, p.K);
+  p.xf_fp32 = bf16 ? 0 : 1;
+  launch_ex(ctx, "pack", pack_rows_kernel, dim3(L_max), dim3(256), 0, true, 1, p);
 }
 
 constexpr int ATT_CLUSTER = 8;
@@ -486,6 +552,7 @@ void launch_attention(wc_ctx* ctx, AttnParams p) {
   if (al % 16 || (p.stride_p * (p.kv_dtype == 1 ? 2 : 4)) % 16 || (p.stride_h * (p.kv_dtype == 1 ? 2 : 4)) % 16 ||
       (!p.q_ready && p.ld_qkv % 4))
     fail(WC_ERR_INVALID, "attention inputs must be 16-byte aligned with 16-byte row strides");
+  if (p.xf_out) p.xf_width = xf_width(!p.xf_fp32, p.H * p.D);
   // tensor-core path: bf16 cache, rule-based visibility, new rows appended by the kernel
   const bool mma_ok = !p.q_ready && !p.mask_full && p.kv_dtype == WC_BF16 && p.write_cache && ctx->attn_mma &&
                       (p.D == 128 || p.D == 64) && p.L_max * rep <= AM_MAXR && p.stride_p == p.D;
@@ -543,10 +610,10 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
     CUDA_TRY(cudaFuncSetAttribute(attention_mma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(kv_compact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     int occ = 0;
-    CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_bf16_kernel<1>, GEMV_THREADS,
+    CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_bf16_kernel<1>, GV_THREADS,
                                                            gemv_bf16_smem<1>()));
     ctx->occ_gemv[1] = std::max(1, occ);
-    CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_bf16_kernel<2>, GEMV_THREADS,
+    CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_bf16_kernel<2>, GV_THREADS,
                                                            gemv_bf16_smem<2>()));
     ctx->occ_gemv[2] = std::max(1, occ);
   });
@@ -579,6 +646,7 @@ extern "C" void wc_ctx_destroy(wc_ctx* ctx) {
   dfree(ctx->d_err);
   dfree(ctx->pw);
   dfree(ctx->qw);
+  dfree(ctx->lin_xf);
   if (ctx->own_stream && ctx->stream) cudaStreamDestroy(ctx->stream);
   delete ctx;
 }
@@ -617,7 +685,7 @@ extern "C" wc_status wc_weight_create(wc_ctx* ctx, const void* data, int src_dty
       s.ptr = dalloc(bytes);
       CUDA_TRY(cudaMemcpy(s.ptr, data, bytes, cudaMemcpyHostToDevice));
     }
-    auto* out = new wc_weight{ctx, make_lin(dtype, out_rows, in_cols, 1)};
+    auto* out = new wc_weight{ctx, make_lin(dtype, out_rows, {in_cols}, 1)};
     lin_put(ctx, out->lin, s, out_rows, in_cols, 0, 0, 0);
     CUDA_TRY(cudaStreamSynchronize(ctx->stream));
     if (!data_on_device) dfree(s.ptr);
@@ -634,20 +702,39 @@ extern "C" void wc_weight_destroy(wc_weight* w) {
 extern "C" wc_status wc_linear(wc_ctx* ctx, const float* x, int L, int in, const wc_weight* W, float* y, int accumulate) {
   if (!ctx || !x || !W || !y || L <= 0) return WC_ERR_INVALID;
   return guard(ctx, [&] {
-    if (in != W->lin.K) fail(WC_ERR_INVALID, "linear: input width does not match the weight");
+    const Lin& lin = W->lin;
+    if (in != lin.K) fail(WC_ERR_INVALID, "linear: input width does not match the weight");
+    const bool bf16 = lin.dtype == WC_BF16;
+    if (!ctx->lin_xf || ctx->lin_xf_k < in || ctx->lin_xf_bf16 != bf16) {
+      CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+      dfree(ctx->lin_xf);
+      ctx->lin_xf = xf_alloc(bf16, in);
+      ctx->lin_xf_k = in;
+      ctx->lin_xf_bf16 = bf16;
+    } else {
+      // the padding columns of a narrower input must be zero again
+      CUDA_TRY(cudaMemsetAsync(ctx->lin_xf, 0, size_t(GEMV_MAXL) * xf_width(bf16, ctx->lin_xf_k) * 4, ctx->stream));
+    }
     for (int r0 = 0; r0 < L; r0 += GEMV_MAXL) {
       const int rows = std::min(GEMV_MAXL, L - r0);
+      PackParams pk = pack_params();
+      pk.src = x + size_t(r0) * in;
+      pk.ld = in;
+      pk.K = in;
+      pk.L = rows;
+      pk.xf = ctx->lin_xf;
+      launch_pack(ctx, pk, bf16, rows);
       GemvParams p = gemv_params();
       p.L = rows;
       p.L_max = rows;
       p.nseg = 1;
-      p.seg[0] = seg_rows(x + size_t(r0) * in, in, in);
+      p.seg[0] = xs_frag(XIn{ctx->lin_xf, nullptr, 0}, in, bf16);
       p.epi = accumulate ? EPI_ADD : EPI_STORE;
-      p.y = y + size_t(r0) * W->lin.N;
-      p.ldy = W->lin.N;
+      p.y = y + size_t(r0) * lin.N;
+      p.ldy = lin.N;
       p.base = p.y;
-      p.ldb = W->lin.N;
-      launch_gemv(ctx, W->lin, p);
+      p.ldb = lin.N;
+      launch_gemv(ctx, lin, p);
     }
   });
 }
@@ -985,6 +1072,16 @@ namespace {
 struct TLayer {
   Lin qkv, o, gu, down;
   float *in_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+  float *ss_o = nullptr, *ss_d = nullptr;  // sums of squares of h after the o / down projections
+};
+
+// Where the three tap layers' outputs go: fp32 rows (taps + f * stride) and / or
+// fragments times a gain (the drafter's feature norms).
+struct TapOut {
+  float* rows = nullptr;
+  size_t stride = 0;
+  uint32_t* xf[3] = {nullptr, nullptr, nullptr};
+  const float* w[3] = {nullptr, nullptr, nullptr};
 };
 }  // namespace
 
@@ -1001,19 +1098,23 @@ struct wc_target {
   std::vector<TLayer> layers;
   RopeTable* rope = nullptr;
   // workspace for up to GEMV_MAXL rows
-  float *ws_h = nullptr, *ws_qkv = nullptr, *ws_att = nullptr, *ws_act = nullptr;
+  float *ws_h = nullptr, *ws_qkv = nullptr;
+  uint32_t *xf_in = nullptr, *xf_post = nullptr, *xf_att = nullptr, *xf_act = nullptr, *xf_tmp = nullptr;
+  float *ss_pack = nullptr, *ss_tmp = nullptr;
   unsigned long long* ws_keys = nullptr;
   int* ws_tokens = nullptr;
-  int* ws_pos = nullptr;
 };
 
 namespace {
+
+bool is_bf16(int dtype) { return dtype == WC_BF16; }
 
 void target_check_cfg(const wc_qwen3_config& c) {
   if (c.hidden <= 0 || c.layers <= 0 || c.heads <= 0 || c.kv_heads <= 0 || c.head_dim <= 0 || c.intermediate <= 0 ||
       c.vocab <= 0)
     fail(WC_ERR_INVALID, "target config has non-positive sizes");
   if (c.heads % c.kv_heads) fail(WC_ERR_INVALID, "heads must be a multiple of kv_heads");
+  if (c.hidden % 16 || c.head_dim % 32) fail(WC_ERR_UNSUPPORTED, "hidden must be a multiple of 16, head_dim of 32");
 }
 
 void target_set_taps(wc_target* t, const int* taps) {
@@ -1036,11 +1137,13 @@ void target_finalize_impl(wc_target* t) {
   wc_ctx* ctx = t->ctx;
   const auto& c = t->cfg;
   const int H = c.hidden, D = c.head_dim, Hq = c.heads * D, Hkv = c.kv_heads * D, I = c.intermediate;
+  const bool bf16 = is_bf16(t->dtype);
   const Stage& s = t->stage;
   t->embed = to_dtype(ctx, s.get("model.embed_tokens.weight", {c.vocab, H}), t->dtype);
   t->final_norm = to_f32_vec(ctx, s.get("model.norm.weight", {H}));
   const bool tied = c.tie_embeddings || !s.has("lm_head.weight");
-  if (tied && t->dtype == WC_F32) {
+  if (tied && !bf16) {
+    if (H % 4) fail(WC_ERR_UNSUPPORTED, "fp32 hidden size must be a multiple of 4");
     t->head.w = t->embed;
     t->head.owned = false;
     t->head.dtype = WC_F32;
@@ -1049,53 +1152,87 @@ void target_finalize_impl(wc_target* t) {
     t->head.K = H;
     t->head.Kp = H;
     t->head.group = 1;
-    if (H % 4) fail(WC_ERR_UNSUPPORTED, "fp32 hidden size must be a multiple of 4");
+    t->head.nseg = 1;
+    t->head.seg_len[0] = H;
   } else {
     const Staged& hw = tied ? s.get("model.embed_tokens.weight", {c.vocab, H}) : s.get("lm_head.weight", {c.vocab, H});
-    t->head = make_lin(t->dtype, c.vocab, H, 1);
+    t->head = make_lin(t->dtype, c.vocab, {H}, 1);
     lin_put(ctx, t->head, hw, c.vocab, H, 0, 0, 0);
   }
   t->layers.resize(c.layers);
   for (int i = 0; i < c.layers; ++i) {
     const std::string p = "model.layers." + std::to_string(i) + ".";
     TLayer& L = t->layers[i];
-    L.qkv = make_lin(t->dtype, Hq + 2 * Hkv, H, 1);
+    L.qkv = make_lin(t->dtype, Hq + 2 * Hkv, {H}, 1);
     lin_put(ctx, L.qkv, s.get(p + "self_attn.q_proj.weight", {Hq, H}), Hq, H, 0, 0, 0);
     lin_put(ctx, L.qkv, s.get(p + "self_attn.k_proj.weight", {Hkv, H}), Hkv, H, Hq, 0, 0);
     lin_put(ctx, L.qkv, s.get(p + "self_attn.v_proj.weight", {Hkv, H}), Hkv, H, Hq + Hkv, 0, 0);
-    L.o = make_lin(t->dtype, H, Hq, 1);
+    L.o = make_lin(t->dtype, H, {Hq}, 1);
     lin_put(ctx, L.o, s.get(p + "self_attn.o_proj.weight", {H, Hq}), H, Hq, 0, 0, 0);
-    L.gu = make_lin(t->dtype, I, H, 2);
+    L.gu = make_lin(t->dtype, I, {H}, 2);
     lin_put(ctx, L.gu, s.get(p + "mlp.gate_proj.weight", {I, H}), I, H, 0, 0, 0);
     lin_put(ctx, L.gu, s.get(p + "mlp.up_proj.weight", {I, H}), I, H, 0, 0, 1);
-    L.down = make_lin(t->dtype, H, I, 1);
+    L.down = make_lin(t->dtype, H, {I}, 1);
     lin_put(ctx, L.down, s.get(p + "mlp.down_proj.weight", {H, I}), H, I, 0, 0, 0);
     L.in_norm = to_f32_vec(ctx, s.get(p + "input_layernorm.weight", {H}));
     L.post_norm = to_f32_vec(ctx, s.get(p + "post_attention_layernorm.weight", {H}));
     L.q_norm = to_f32_vec(ctx, s.get(p + "self_attn.q_norm.weight", {D}));
     L.k_norm = to_f32_vec(ctx, s.get(p + "self_attn.k_norm.weight", {D}));
+    L.ss_o = ss_alloc(ctx);
+    L.ss_d = ss_alloc(ctx);
   }
   t->rope = &rope_table(ctx, D, c.rope_theta, 32768);
   const int M = GEMV_MAXL;
   t->ws_h = static_cast<float*>(dalloc(sizeof(float) * M * H));
   t->ws_qkv = static_cast<float*>(dalloc(sizeof(float) * M * (Hq + 2 * Hkv)));
-  t->ws_att = static_cast<float*>(dalloc(sizeof(float) * M * Hq));
-  t->ws_act = static_cast<float*>(dalloc(sizeof(float) * M * I));
+  t->xf_in = xf_alloc(bf16, H);
+  t->xf_post = xf_alloc(bf16, H);
+  t->xf_att = xf_alloc(bf16, Hq);
+  t->xf_act = xf_alloc(bf16, I);
+  t->xf_tmp = xf_alloc(bf16, H);
+  t->ss_pack = ss_alloc(ctx);
+  t->ss_tmp = ss_alloc(ctx);
   t->ws_keys = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * M));
   t->ws_tokens = static_cast<int*>(dalloc(sizeof(int) * 4096));
-  t->ws_pos = static_cast<int*>(dalloc(sizeof(int) * 4096));
   CUDA_TRY(cudaStreamSynchronize(ctx->stream));
   t->stage.clear();
   t->finalized = true;
 }
 
-// The layer stack on h[L][H] in place (rows and prefix from `r`); taps (optional) receive
-// the block outputs of the three tap layers at taps + f * taps_stride.
-void target_layers(wc_target* t, wc_kv* kv, const Rows& r, float* h, float* taps, size_t taps_stride, int* err) {
+// Embedding rows -> the residual stream h (fp32) and the first layer's input fragments
+// (times its input norm gain) with their sums of squares. Tokens from `tokens`, or the
+// verify input [x_n, d_1..d_K] of the round state `st`.
+XIn target_embed(wc_target* t, const Rows& r, const int* tokens, RoundState* st, const int* vocab_map, float* h,
+                 int* err) {
+  PackParams p = pack_params();
+  p.table = t->embed;
+  p.table_dtype = t->dtype == WC_BF16 ? 1 : 0;
+  p.tokens = tokens;
+  p.st = st;
+  p.vocab_map = vocab_map;
+  p.vocab = t->cfg.vocab;
+  p.K = t->cfg.hidden;
+  p.L = r.L;
+  p.L_dev = r.L_dev;
+  p.w = t->layers[0].in_norm;
+  p.xf = t->xf_in;
+  p.ss = t->ss_pack;
+  p.copy = h;
+  p.err = err;
+  launch_pack(t->ctx, p, is_bf16(t->dtype), r.L_max);
+  return XIn{t->xf_in, t->ss_pack, 1};
+}
+
+// The layer stack on the residual stream h[L][H] in place (rows and prefix from `r`),
+// starting from `in0` (layer 0's input fragments). Returns the head input: fragments of
+// h times the final norm gain with the last layer's sums of squares.
+XIn target_layers(wc_target* t, wc_kv* kv, const Rows& r, XIn in0, float* h, const TapOut* taps, int* err) {
   wc_ctx* ctx = t->ctx;
   const auto& c = t->cfg;
   const int H = c.hidden, D = c.head_dim, Hq = c.heads * D, Hkv = c.kv_heads * D, I = c.intermediate;
   const int ld_qkv = Hq + 2 * Hkv;
+  const bool bf16 = is_bf16(t->dtype);
+  XIn x = in0;
   for (int li = 0; li < c.layers; ++li) {
     const TLayer& Ly = t->layers[li];
     {
@@ -1104,8 +1241,7 @@ void target_layers(wc_target* t, wc_kv* kv, const Rows& r, float* h, float* taps
       p.L_dev = r.L_dev;
       p.L_max = r.L_max;
       p.nseg = 1;
-      p.seg[0] = seg_rows(h, H, H, Ly.in_norm);
-      p.eps = c.eps;
+      p.seg[0] = xs_frag(x, H, bf16, c.eps);
       p.epi = EPI_STORE;
       p.y = t->ws_qkv;
       p.ldy = ld_qkv;
@@ -1142,8 +1278,8 @@ void target_layers(wc_target* t, wc_kv* kv, const Rows& r, float* h, float* taps
       a.mask_full = r.mask_full;
       a.mask_ld = r.mask_ld;
       a.scale = 1.f / std::sqrt(float(D));
-      a.out = t->ws_att;
-      a.ld_out = Hq;
+      a.xf_out = t->xf_att;
+      a.xf_fp32 = bf16 ? 0 : 1;
       a.write_cache = 1;
       a.err = err;
       prof_begin(ctx, PK_ATTN);
@@ -1156,12 +1292,15 @@ void target_layers(wc_target* t, wc_kv* kv, const Rows& r, float* h, float* taps
       p.L_dev = r.L_dev;
       p.L_max = r.L_max;
       p.nseg = 1;
-      p.seg[0] = seg_rows(t->ws_att, Hq, Hq);
+      p.seg[0] = xs_frag(XIn{t->xf_att, nullptr, 0}, Hq, bf16);
       p.epi = EPI_ADD;
       p.y = h;
       p.ldy = H;
       p.base = h;
       p.ldb = H;
+      p.nout = 1;
+      p.out[0] = XOut{t->xf_post, Ly.post_norm};
+      p.ss_out = Ly.ss_o;
       p.err = err;
       prof_begin(ctx, PK_O);
       launch_gemv(ctx, Ly.o, p);
@@ -1173,11 +1312,10 @@ void target_layers(wc_target* t, wc_kv* kv, const Rows& r, float* h, float* taps
       p.L_dev = r.L_dev;
       p.L_max = r.L_max;
       p.nseg = 1;
-      p.seg[0] = seg_rows(h, H, H, Ly.post_norm);
-      p.eps = c.eps;
+      p.seg[0] = xs_frag(XIn{t->xf_post, Ly.ss_o, gemv_grid(ctx, Ly.o, r.L_max)}, H, bf16, c.eps);
       p.epi = EPI_SWIGLU;
-      p.y = t->ws_act;
-      p.ldy = I;
+      p.nout = 1;
+      p.out[0] = XOut{t->xf_act, nullptr};
       p.err = err;
       prof_begin(ctx, PK_GU);
       launch_gemv(ctx, Ly.gu, p);
@@ -1189,35 +1327,49 @@ void target_layers(wc_target* t, wc_kv* kv, const Rows& r, float* h, float* taps
       p.L_dev = r.L_dev;
       p.L_max = r.L_max;
       p.nseg = 1;
-      p.seg[0] = seg_rows(t->ws_act, I, I);
+      p.seg[0] = xs_frag(XIn{t->xf_act, nullptr, 0}, I, bf16);
       p.epi = EPI_ADD;
       p.y = h;
       p.ldy = H;
       p.base = h;
       p.ldb = H;
-      p.err = err;
+      p.nout = 1;
+      p.out[0] = XOut{t->xf_in, li + 1 < c.layers ? t->layers[li + 1].in_norm : t->final_norm};
+      p.ss_out = Ly.ss_d;
       for (int f = 0; f < 3; ++f)
         if (taps && t->taps[f] == li) {
-          p.y2 = taps + size_t(f) * taps_stride;
-          p.ldy2 = H;
+          if (taps->rows) {
+            p.y2 = taps->rows + size_t(f) * taps->stride;
+            p.ldy2 = H;
+          }
+          if (taps->xf[f]) p.out[p.nout++] = XOut{taps->xf[f], taps->w[f]};
         }
+      p.err = err;
       prof_begin(ctx, PK_DOWN);
       launch_gemv(ctx, Ly.down, p);
       prof_end(ctx, PK_DOWN);
     }
+    x = XIn{t->xf_in, Ly.ss_d, gemv_grid(ctx, Ly.down, r.L_max)};
   }
+  return x;
 }
 
-// Final norm + head on rows [0, L) of h: argmax keys and (optionally) logits [L][V].
-void target_head(wc_target* t, const float* h, int L, const int* L_dev, int L_max, unsigned long long* keys,
-                 float* logits, int* err) {
+// Sums of squares of a tap layer's output, as the fuse reads them.
+XIn target_tap_stats(const wc_target* t, int f, const uint32_t* xf, int L_max) {
+  const TLayer& Ly = t->layers[t->taps[f]];
+  return XIn{xf, Ly.ss_d, gemv_grid(t->ctx, Ly.down, L_max)};
+}
+
+// Head over `rows` rows given as fragments (times the final norm): argmax keys and,
+// optionally, logits [rows][V].
+void target_head(wc_target* t, XIn x, int rows, const int* L_dev, int L_max, unsigned long long* keys, float* logits,
+                 int* err) {
   GemvParams p = gemv_params();
-  p.L = L;
+  p.L = rows;
   p.L_dev = L_dev;
   p.L_max = L_max;
   p.nseg = 1;
-  p.seg[0] = seg_rows(h, t->cfg.hidden, t->cfg.hidden, t->final_norm);
-  p.eps = t->cfg.eps;
+  p.seg[0] = xs_frag(x, t->cfg.hidden, is_bf16(t->dtype), t->cfg.eps);
   p.epi = EPI_ARGMAX;
   p.y = logits;
   p.ldy = t->cfg.vocab;
@@ -1226,6 +1378,21 @@ void target_head(wc_target* t, const float* h, int L, const int* L_dev, int L_ma
   prof_begin(t->ctx, PK_HEAD);
   launch_gemv(t->ctx, t->head, p);
   prof_end(t->ctx, PK_HEAD);
+}
+
+// Head over fp32 residual rows h[rows][H] (any row offset): re-packs them first.
+void target_head_rows(wc_target* t, const float* h, int rows, unsigned long long* keys, float* logits, int* err) {
+  PackParams p = pack_params();
+  p.src = h;
+  p.ld = t->cfg.hidden;
+  p.K = t->cfg.hidden;
+  p.L = rows;
+  p.w = t->final_norm;
+  p.xf = t->xf_tmp;
+  p.ss = t->ss_tmp;
+  p.err = err;
+  launch_pack(t->ctx, p, is_bf16(t->dtype), rows);
+  target_head(t, XIn{t->xf_tmp, t->ss_tmp, 1}, rows, nullptr, rows, keys, logits, err);
 }
 
 }  // namespace
@@ -1316,14 +1483,13 @@ extern "C" void wc_target_destroy(wc_target* t) {
     dfree(L.post_norm);
     dfree(L.q_norm);
     dfree(L.k_norm);
+    dfree(L.ss_o);
+    dfree(L.ss_d);
   }
-  dfree(t->ws_h);
-  dfree(t->ws_qkv);
-  dfree(t->ws_att);
-  dfree(t->ws_act);
-  dfree(t->ws_keys);
-  dfree(t->ws_tokens);
-  dfree(t->ws_pos);
+  for (void* p : {(void*)t->ws_h, (void*)t->ws_qkv, (void*)t->xf_in, (void*)t->xf_post, (void*)t->xf_att,
+                  (void*)t->xf_act, (void*)t->xf_tmp, (void*)t->ss_pack, (void*)t->ss_tmp, (void*)t->ws_keys,
+                  (void*)t->ws_tokens})
+    dfree(p);
   delete t;
 }
 
@@ -1357,12 +1523,11 @@ extern "C" wc_status wc_target_forward(wc_target* t, wc_kv* cache, const int* to
     if (prefix + L > cache->cap) fail(WC_ERR_CAPACITY, "KV cache capacity exceeded");
     wc_ctx* ctx = t->ctx;
     const int H = c.hidden;
-    const size_t taps_stride = size_t(L) * H;
+    TapOut to;
+    to.rows = taps;
+    to.stride = size_t(L) * H;
     for (int r0 = 0; r0 < L; r0 += GEMV_MAXL) {
       const int rows = std::min(GEMV_MAXL, L - r0);
-      embed_rows_kernel<<<rows, 256, 0, ctx->stream>>>(t->embed, t->dtype, c.vocab, H, tokens + r0, rows, nullptr,
-                                                       t->ws_h, nullptr, nullptr, 0, ctx->d_err);
-      check_launch(ctx, "embed");
       Rows r;
       r.L = rows;
       r.L_max = rows;
@@ -1370,13 +1535,17 @@ extern "C" wc_status wc_target_forward(wc_target* t, wc_kv* cache, const int* to
       r.positions = positions ? positions + r0 : nullptr;
       r.mask_full = mask ? mask + size_t(r0) * (prefix + L) : nullptr;
       r.mask_ld = prefix + L;
-      target_layers(t, cache, r, t->ws_h, taps ? taps + size_t(r0) * H : nullptr, taps_stride, ctx->d_err);
+      const XIn in0 = target_embed(t, r, tokens + r0, nullptr, nullptr, t->ws_h, ctx->d_err);
+      TapOut tc = to;
+      if (taps) tc.rows = taps + size_t(r0) * H;
+      const XIn hx = target_layers(t, cache, r, in0, t->ws_h, taps ? &tc : nullptr, ctx->d_err);
       const int h0 = std::max(logits_from, r0);
       if (h0 < r0 + rows && (logits || argmax)) {
         const int hr = r0 + rows - h0;
+        float* lg = logits ? logits + size_t(h0 - logits_from) * c.vocab : nullptr;
         CUDA_TRY(cudaMemsetAsync(t->ws_keys, 0, sizeof(unsigned long long) * GEMV_MAXL, ctx->stream));
-        target_head(t, t->ws_h + size_t(h0 - r0) * H, hr, nullptr, hr, t->ws_keys,
-                    logits ? logits + size_t(h0 - logits_from) * c.vocab : nullptr, ctx->d_err);
+        if (h0 == r0) target_head(t, hx, hr, nullptr, hr, t->ws_keys, lg, ctx->d_err);
+        else target_head_rows(t, t->ws_h + size_t(h0 - r0) * H, hr, t->ws_keys, lg, ctx->d_err);
         if (argmax) {
           keys_to_index_kernel<<<1, 32, 0, ctx->stream>>>(t->ws_keys, hr, nullptr, argmax + (h0 - logits_from));
           check_launch(ctx, "keys");
@@ -1393,6 +1562,7 @@ namespace {
 struct DLayer {
   Lin qkv, o, gu, down;
   float *in_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *aux_norm = nullptr;
+  float *ss_o = nullptr, *ss_d = nullptr;
 };
 }  // namespace
 
@@ -1403,6 +1573,7 @@ struct wc_drafter {
   bool finalized = false;
   Stage stage;
   void* embed = nullptr;
+  float* aux_inv = nullptr;  // [vocab]: 1/rms of each embedding row with the drafter eps (aux_norm)
   Lin fc;
   float* feature_norms[GEMV_MAXSEG] = {nullptr, nullptr, nullptr};
   std::vector<DLayer> layers;
@@ -1411,7 +1582,12 @@ struct wc_drafter {
   int* vocab_map = nullptr;  // restricted head row -> token id
   int head_rows = 0;
   RopeTable* rope = nullptr;
-  float *ws_h = nullptr, *ws_qkv = nullptr, *ws_att = nullptr, *ws_act = nullptr, *ws_out = nullptr;
+  // workspace for up to GEMV_MAXL rows
+  float *ws_h = nullptr, *ws_feat = nullptr, *ws_g = nullptr, *ws_qkv = nullptr;
+  uint32_t *xf_feat = nullptr, *xf_post = nullptr, *xf_att = nullptr, *xf_act = nullptr, *xf_out = nullptr;
+  uint32_t* xf_tap[3] = {nullptr, nullptr, nullptr};
+  float *ss_feat = nullptr, *ss_g = nullptr, *ss_pack = nullptr;
+  float* ss_tap[3] = {nullptr, nullptr, nullptr};
   unsigned long long* ws_keys = nullptr;
 };
 
@@ -1424,17 +1600,36 @@ void drafter_check_cfg(const wc_drafter_config& c) {
   if (c.num_features < 1 || c.num_features > GEMV_MAXSEG)
     fail(WC_ERR_UNSUPPORTED, "drafter num_features must be 1..3");
   if (c.heads % c.kv_heads) fail(WC_ERR_INVALID, "heads must be a multiple of kv_heads");
+  if (c.hidden % 16 || c.head_dim % 32) fail(WC_ERR_UNSUPPORTED, "hidden must be a multiple of 16, head_dim of 32");
 }
 
 void drafter_finalize_impl(wc_drafter* d) {
   wc_ctx* ctx = d->ctx;
   const auto& c = d->cfg;
   const int H = c.hidden, D = c.head_dim, Hq = c.heads * D, Hkv = c.kv_heads * D, I = c.intermediate;
+  const bool bf16 = is_bf16(d->dtype);
   const Stage& s = d->stage;
   d->embed = to_dtype(ctx, s.get("embed_tokens.weight", {c.vocab, H}), d->dtype);
   const int F = c.num_features, Ht = c.target_hidden;
-  d->fc = make_lin(d->dtype, H, F * Ht, 1);
-  lin_put(ctx, d->fc, s.get("fc.weight", {H, F * Ht}), H, F * Ht, 0, 0, 0);
+  if (F == 1) d->fc = make_lin(d->dtype, H, {Ht}, 1);
+  else if (F == 2) d->fc = make_lin(d->dtype, H, {Ht, Ht}, 1);
+  else d->fc = make_lin(d->dtype, H, {Ht, Ht, Ht}, 1);
+  {
+    // fc.weight [H][F*Ht]: split into one part per tap column block
+    const Staged& fw = s.get("fc.weight", {H, F * Ht});
+    for (int f = 0; f < F; ++f) {
+      Staged part;
+      part.dtype = fw.dtype;
+      part.shape = {H, Ht};
+      const size_t es = size_t(dtype_size(fw.dtype));
+      part.ptr = dalloc(size_t(H) * Ht * es);
+      CUDA_TRY(cudaMemcpy2DAsync(part.ptr, Ht * es, static_cast<const char*>(fw.ptr) + f * Ht * es, size_t(F) * Ht * es,
+                                 Ht * es, H, cudaMemcpyDeviceToDevice, ctx->stream));
+      lin_put(ctx, d->fc, part, H, Ht, 0, f, 0);
+      CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+      dfree(part.ptr);
+    }
+  }
   if (c.feature_norm)
     for (int f = 0; f < F; ++f)
       d->feature_norms[f] = to_f32_vec(ctx, s.get("feature_norms." + std::to_string(f) + ".weight", {Ht}));
@@ -1443,70 +1638,90 @@ void drafter_finalize_impl(wc_drafter* d) {
     const std::string p = "layers." + std::to_string(i) + ".";
     DLayer& L = d->layers[i];
     const bool aux = i == 0;  // layer 0 is dual-stream (drafter.cpp:64-70)
-    L.qkv = make_lin(d->dtype, Hq + 2 * Hkv, aux ? 2 * H : H, 1);
+    L.qkv = aux ? make_lin(d->dtype, Hq + 2 * Hkv, {H, H}, 1) : make_lin(d->dtype, Hq + 2 * Hkv, {H}, 1);
     lin_put(ctx, L.qkv, s.get(p + "self_attn.q_proj.weight", {Hq, H}), Hq, H, 0, 0, 0);
     lin_put(ctx, L.qkv, s.get(p + "self_attn.k_proj.weight", {Hkv, H}), Hkv, H, Hq, 0, 0);
     lin_put(ctx, L.qkv, s.get(p + "self_attn.v_proj.weight", {Hkv, H}), Hkv, H, Hq + Hkv, 0, 0);
     if (aux) {
-      lin_put(ctx, L.qkv, s.get(p + "self_attn.aux_q.weight", {Hq, H}), Hq, H, 0, H, 0);
-      lin_put(ctx, L.qkv, s.get(p + "self_attn.aux_k.weight", {Hkv, H}), Hkv, H, Hq, H, 0);
-      lin_put(ctx, L.qkv, s.get(p + "self_attn.aux_v.weight", {Hkv, H}), Hkv, H, Hq + Hkv, H, 0);
+      lin_put(ctx, L.qkv, s.get(p + "self_attn.aux_q.weight", {Hq, H}), Hq, H, 0, 1, 0);
+      lin_put(ctx, L.qkv, s.get(p + "self_attn.aux_k.weight", {Hkv, H}), Hkv, H, Hq, 1, 0);
+      lin_put(ctx, L.qkv, s.get(p + "self_attn.aux_v.weight", {Hkv, H}), Hkv, H, Hq + Hkv, 1, 0);
       L.aux_norm = to_f32_vec(ctx, s.get(p + "aux_norm.weight", {H}));
     }
-    L.o = make_lin(d->dtype, H, Hq, 1);
+    L.o = make_lin(d->dtype, H, {Hq}, 1);
     lin_put(ctx, L.o, s.get(p + "self_attn.o_proj.weight", {H, Hq}), H, Hq, 0, 0, 0);
-    L.gu = make_lin(d->dtype, I, H, 2);
+    L.gu = make_lin(d->dtype, I, {H}, 2);
     lin_put(ctx, L.gu, s.get(p + "mlp.gate_proj.weight", {I, H}), I, H, 0, 0, 0);
     lin_put(ctx, L.gu, s.get(p + "mlp.up_proj.weight", {I, H}), I, H, 0, 0, 1);
-    L.down = make_lin(d->dtype, H, I, 1);
+    L.down = make_lin(d->dtype, H, {I}, 1);
     lin_put(ctx, L.down, s.get(p + "mlp.down_proj.weight", {H, I}), H, I, 0, 0, 0);
     L.in_norm = to_f32_vec(ctx, s.get(p + "input_layernorm.weight", {H}));
     L.post_norm = to_f32_vec(ctx, s.get(p + "post_attention_layernorm.weight", {H}));
     L.q_norm = to_f32_vec(ctx, s.get(p + "self_attn.q_norm.weight", {D}));
     L.k_norm = to_f32_vec(ctx, s.get(p + "self_attn.k_norm.weight", {D}));
+    L.ss_o = ss_alloc(ctx);
+    L.ss_d = ss_alloc(ctx);
   }
+  d->aux_inv = static_cast<float*>(dalloc(sizeof(float) * c.vocab));
+  row_inv_kernel<<<(c.vocab + 7) / 8, 256, 0, ctx->stream>>>(d->embed, d->dtype == WC_BF16 ? 1 : 0, c.vocab, H, c.eps,
+                                                             d->aux_inv);
+  check_launch(ctx, "row_inv");
   d->norm = to_f32_vec(ctx, s.get("norm.weight", {H}));
-  d->head = make_lin(d->dtype, c.vocab, H, 1);
+  d->head = make_lin(d->dtype, c.vocab, {H}, 1);
   lin_put(ctx, d->head, s.get("lm_head.weight", {c.vocab, H}), c.vocab, H, 0, 0, 0);
   d->head_rows = c.vocab;
   d->rope = &rope_table(ctx, D, c.rope_theta, 32768);
   const int M = GEMV_MAXL;
   d->ws_h = static_cast<float*>(dalloc(sizeof(float) * M * H));
-  d->ws_out = static_cast<float*>(dalloc(sizeof(float) * M * H));
+  d->ws_feat = static_cast<float*>(dalloc(sizeof(float) * M * H));
+  d->ws_g = static_cast<float*>(dalloc(sizeof(float) * M * H));
   d->ws_qkv = static_cast<float*>(dalloc(sizeof(float) * M * (Hq + 2 * Hkv)));
-  d->ws_att = static_cast<float*>(dalloc(sizeof(float) * M * Hq));
-  d->ws_act = static_cast<float*>(dalloc(sizeof(float) * M * I));
+  d->xf_feat = xf_alloc(bf16, H);
+  d->xf_post = xf_alloc(bf16, H);
+  d->xf_att = xf_alloc(bf16, Hq);
+  d->xf_act = xf_alloc(bf16, I);
+  d->xf_out = xf_alloc(bf16, H);
+  for (int f = 0; f < 3; ++f) {
+    d->xf_tap[f] = xf_alloc(bf16, Ht);
+    d->ss_tap[f] = ss_alloc(ctx);
+  }
+  d->ss_feat = ss_alloc(ctx);
+  d->ss_g = ss_alloc(ctx);
+  d->ss_pack = ss_alloc(ctx);
   d->ws_keys = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * M));
   CUDA_TRY(cudaStreamSynchronize(ctx->stream));
   d->stage.clear();
   d->finalized = true;
 }
 
-// Drafter layer stack (drafter.cpp:91-136): feat [L][H] is the residual stream input,
-// layer 0 adds W_aux . aux_norm(embed(token)); the result lands in h_out [L][H].
-void drafter_layers(wc_drafter* d, wc_kv* kv, const Rows& r, const float* feat, const TokenSrc& tok, float* h_out,
-                    int* err) {
+// Drafter layer stack (drafter.cpp:91-136). `feat` [L][H] is the residual stream input
+// (fp32) and `feat_in` its fragments times layer 0's input norm gain; layer 0 adds
+// W_aux . aux_norm(embed(token)). The result h lands in h_out [L][H]. `extra` (optional)
+// receives fragments of h as well (the next chain step's feature without post-norm).
+// Returns the head input: fragments of h times the final norm gain, with h's sums of squares.
+XIn drafter_layers(wc_drafter* d, wc_kv* kv, const Rows& r, XIn feat_in, const float* feat, const TokenSrc& tok,
+                   float* h_out, const XOut* extra, int* err) {
   wc_ctx* ctx = d->ctx;
   const auto& c = d->cfg;
   const int H = c.hidden, D = c.head_dim, Hq = c.heads * D, Hkv = c.kv_heads * D, I = c.intermediate;
   const int ld_qkv = Hq + 2 * Hkv;
+  const bool bf16 = is_bf16(d->dtype);
+  XIn x = feat_in;
   for (int li = 0; li < c.layers; ++li) {
     const DLayer& Ly = d->layers[li];
-    const float* hin = li == 0 ? feat : h_out;
     {
       GemvParams p = gemv_params();
       p.L = r.L;
       p.L_dev = r.L_dev;
       p.L_max = r.L_max;
       p.nseg = 1;
-      p.seg[0] = seg_rows(hin, H, H, Ly.in_norm);
+      p.seg[0] = xs_frag(x, H, bf16, c.eps);
       if (Ly.aux_norm) {
         p.nseg = 2;
-        p.seg[1] = seg_embed(d->embed, d->dtype, H, Ly.aux_norm);
+        p.seg[1] = xs_embed(d->embed, H, bf16, Ly.aux_norm, d->aux_inv);
         p.tok = tok;
         p.tok.vocab = c.vocab;
       }
-      p.eps = c.eps;
       p.epi = EPI_STORE;
       p.y = d->ws_qkv;
       p.ldy = ld_qkv;
@@ -1542,8 +1757,8 @@ void drafter_layers(wc_drafter* d, wc_kv* kv, const Rows& r, const float* feat, 
       a.mask_full = r.mask_full;
       a.mask_ld = r.mask_ld;
       a.scale = 1.f / std::sqrt(float(D));
-      a.out = d->ws_att;
-      a.ld_out = Hq;
+      a.xf_out = d->xf_att;
+      a.xf_fp32 = bf16 ? 0 : 1;
       a.write_cache = 1;
       a.err = err;
       launch_attention(ctx, a);
@@ -1554,12 +1769,15 @@ void drafter_layers(wc_drafter* d, wc_kv* kv, const Rows& r, const float* feat, 
       p.L_dev = r.L_dev;
       p.L_max = r.L_max;
       p.nseg = 1;
-      p.seg[0] = seg_rows(d->ws_att, Hq, Hq);
+      p.seg[0] = xs_frag(XIn{d->xf_att, nullptr, 0}, Hq, bf16);
       p.epi = EPI_ADD;
       p.y = h_out;
       p.ldy = H;
-      p.base = hin;
+      p.base = li == 0 ? feat : h_out;
       p.ldb = H;
+      p.nout = 1;
+      p.out[0] = XOut{d->xf_post, Ly.post_norm};
+      p.ss_out = Ly.ss_o;
       p.err = err;
       launch_gemv(ctx, Ly.o, p);
     }
@@ -1569,64 +1787,122 @@ void drafter_layers(wc_drafter* d, wc_kv* kv, const Rows& r, const float* feat, 
       p.L_dev = r.L_dev;
       p.L_max = r.L_max;
       p.nseg = 1;
-      p.seg[0] = seg_rows(h_out, H, H, Ly.post_norm);
-      p.eps = c.eps;
+      p.seg[0] = xs_frag(XIn{d->xf_post, Ly.ss_o, gemv_grid(ctx, Ly.o, r.L_max)}, H, bf16, c.eps);
       p.epi = EPI_SWIGLU;
-      p.y = d->ws_act;
-      p.ldy = I;
+      p.nout = 1;
+      p.out[0] = XOut{d->xf_act, nullptr};
       p.err = err;
       launch_gemv(ctx, Ly.gu, p);
     }
     {
+      const bool last = li + 1 == c.layers;
       GemvParams p = gemv_params();
       p.L = r.L;
       p.L_dev = r.L_dev;
       p.L_max = r.L_max;
       p.nseg = 1;
-      p.seg[0] = seg_rows(d->ws_act, I, I);
+      p.seg[0] = xs_frag(XIn{d->xf_act, nullptr, 0}, I, bf16);
       p.epi = EPI_ADD;
       p.y = h_out;
       p.ldy = H;
       p.base = h_out;
       p.ldb = H;
+      p.nout = 1;
+      p.out[0] = XOut{d->xf_out, last ? d->norm : d->layers[li + 1].in_norm};
+      if (last && extra) p.out[p.nout++] = *extra;
+      p.ss_out = Ly.ss_d;
       p.err = err;
       launch_gemv(ctx, Ly.down, p);
     }
+    x = XIn{d->xf_out, Ly.ss_d, gemv_grid(ctx, Ly.down, r.L_max)};
   }
+  return x;
 }
 
-// fuse (drafter.cpp:75-89): per-tap RMSNorm, concatenated, through fc.
-void drafter_fuse_impl(wc_drafter* d, const float* taps, size_t tap_stride, int ld, int L, const int* L_dev, int L_max,
-                       float* g, int* err) {
+// fuse (drafter.cpp:75-89): per-tap RMSNorm (the tap fragments are already times the
+// feature norm gains), concatenated, through fc. Writes g [L][H] (fp32, the layer-0
+// residual input) and its fragments times layer 0's input norm gain with sums of squares;
+// returns them as the layer-0 input.
+XIn drafter_fuse_impl(wc_drafter* d, const XIn* taps, int L, const int* L_dev, int L_max, float* g, int* err) {
   const auto& c = d->cfg;
+  const bool bf16 = is_bf16(d->dtype);
   GemvParams p = gemv_params();
   p.L = L;
   p.L_dev = L_dev;
   p.L_max = L_max;
   p.nseg = c.num_features;
-  for (int f = 0; f < c.num_features; ++f)
-    p.seg[f] = seg_rows(taps + f * tap_stride, ld, c.target_hidden, c.feature_norm ? d->feature_norms[f] : nullptr);
-  p.eps = c.eps;
+  for (int f = 0; f < c.num_features; ++f) {
+    XIn tf = taps[f];
+    if (!c.feature_norm) tf.ss = nullptr;
+    p.seg[f] = xs_frag(tf, c.target_hidden, bf16, c.eps);
+  }
   p.epi = EPI_STORE;
   p.y = g;
   p.ldy = c.hidden;
+  p.nout = 1;
+  p.out[0] = XOut{d->xf_feat, d->layers[0].in_norm};
+  p.ss_out = d->ss_g;
   p.err = err;
   launch_gemv(d->ctx, d->fc, p);
+  return XIn{d->xf_feat, d->ss_g, gemv_grid(d->ctx, d->fc, L_max)};
 }
 
-// head over `rows` rows of x (already normalised unless norm_w is given)
-void drafter_head(wc_drafter* d, const float* x, int rows, const float* norm_w, float* write_back,
-                  unsigned long long* keys, float* logits, int* err) {
+// Tap rows [L][Ht] (fp32, row stride ld, tap f at + f * stride) -> tap fragments times
+// the feature norm gains with their sums of squares.
+void drafter_pack_taps(wc_drafter* d, const float* taps, size_t stride, int ld, int L, XIn* out, int* err) {
+  for (int f = 0; f < d->cfg.num_features; ++f) {
+    PackParams p = pack_params();
+    p.src = taps + f * stride;
+    p.ld = ld;
+    p.K = d->cfg.target_hidden;
+    p.L = L;
+    p.w = d->cfg.feature_norm ? d->feature_norms[f] : nullptr;
+    p.xf = d->xf_tap[f];
+    p.ss = d->ss_tap[f];
+    p.err = err;
+    launch_pack(d->ctx, p, is_bf16(d->dtype), L);
+    out[f] = XIn{d->xf_tap[f], d->ss_tap[f], 1};
+  }
+}
+
+// fp32 rows [L][H] -> fragments times `w` (+ sums of squares) in xf / ss.
+XIn drafter_pack_rows(wc_drafter* d, const float* x, int L, const float* w, uint32_t* xf, float* ss, int* err) {
+  PackParams p = pack_params();
+  p.src = x;
+  p.ld = d->cfg.hidden;
+  p.K = d->cfg.hidden;
+  p.L = L;
+  p.w = w;
+  p.xf = xf;
+  p.ss = ss;
+  p.err = err;
+  launch_pack(d->ctx, p, is_bf16(d->dtype), L);
+  return XIn{xf, ss, 1};
+}
+
+// Head over `rows` rows of fragments `x` (seg 0; normalised by x.ss when set); the side
+// job (when side_y is set) writes the next chain feature RMSNorm(h) * norm as fp32 rows and
+// as fragments times layer 0's input gain, with sums of squares in ss_feat.
+void drafter_head(wc_drafter* d, XIn x, int rows, unsigned long long* keys, float* logits, const float* side_src,
+                  float* side_y, int* err) {
+  const bool bf16 = is_bf16(d->dtype);
   GemvParams p = gemv_params();
   p.L = rows;
   p.L_max = rows;
   p.nseg = 1;
-  p.seg[0] = seg_rows(x, d->cfg.hidden, d->cfg.hidden, norm_w, write_back, d->cfg.hidden);
-  p.eps = d->cfg.eps;
+  p.seg[0] = xs_frag(x, d->cfg.hidden, bf16, d->cfg.eps);
   p.epi = EPI_ARGMAX;
   p.y = logits;
   p.ldy = d->head_rows;
   p.keys = keys;
+  if (side_y) {
+    p.side_src = side_src;
+    p.side_len = d->cfg.hidden;
+    p.side_w = d->norm;
+    p.side_y = side_y;
+    p.side_out = XOut{d->xf_feat, d->layers[0].in_norm};
+    p.side_ss = d->ss_feat;
+  }
   p.err = err;
   prof_begin(d->ctx, PK_DRAFT_HEAD);
   launch_gemv(d->ctx, d->head, p);
@@ -1713,6 +1989,7 @@ extern "C" void wc_drafter_destroy(wc_drafter* d) {
   if (!d) return;
   cudaStreamSynchronize(d->ctx->stream);
   dfree(d->embed);
+  dfree(d->aux_inv);
   free_lin(d->fc);
   for (auto* f : d->feature_norms) dfree(f);
   for (auto& L : d->layers) {
@@ -1725,16 +2002,20 @@ extern "C" void wc_drafter_destroy(wc_drafter* d) {
     dfree(L.q_norm);
     dfree(L.k_norm);
     dfree(L.aux_norm);
+    dfree(L.ss_o);
+    dfree(L.ss_d);
   }
   dfree(d->norm);
   free_lin(d->head);
   dfree(d->vocab_map);
-  dfree(d->ws_h);
-  dfree(d->ws_out);
-  dfree(d->ws_qkv);
-  dfree(d->ws_att);
-  dfree(d->ws_act);
-  dfree(d->ws_keys);
+  for (void* p : {(void*)d->ws_h, (void*)d->ws_feat, (void*)d->ws_g, (void*)d->ws_qkv, (void*)d->xf_feat,
+                  (void*)d->xf_post, (void*)d->xf_att, (void*)d->xf_act, (void*)d->xf_out, (void*)d->ss_feat,
+                  (void*)d->ss_g, (void*)d->ss_pack, (void*)d->ws_keys})
+    dfree(p);
+  for (int f = 0; f < 3; ++f) {
+    dfree(d->xf_tap[f]);
+    dfree(d->ss_tap[f]);
+  }
   delete d;
 }
 
@@ -1756,14 +2037,12 @@ extern "C" wc_status wc_drafter_restrict_vocab(wc_drafter* d, const int* ids, in
     wc_ctx* ctx = d->ctx;
     int* map = static_cast<int*>(dalloc(sizeof(int) * n));
     CUDA_TRY(cudaMemcpy(map, ids, sizeof(int) * n, cudaMemcpyHostToDevice));
-    Lin nh;
+    Lin nh = make_lin(d->dtype, n, {d->cfg.hidden}, 1);
     if (d->dtype == WC_BF16) {
-      nh = make_lin(WC_BF16, n, d->cfg.hidden, 1);
       const int KT = nh.Kp / 16;
       gather_tiled_rows_kernel<<<grid_for(size_t(nh.Np) * nh.Kp), 256, 0, ctx->stream>>>(
           static_cast<const uint16_t*>(d->head.w), KT, map, n, static_cast<uint16_t*>(nh.w));
     } else {
-      nh = make_lin(WC_F32, n, d->cfg.hidden, 1);
       gather_rows_f32_kernel<<<grid_for(size_t(n) * nh.Kp), 256, 0, ctx->stream>>>(
           static_cast<const float*>(d->head.w), nh.Kp, map, n, static_cast<float*>(nh.w));
     }
@@ -1786,11 +2065,13 @@ extern "C" wc_status wc_drafter_make_cache(wc_drafter* d, int capacity, wc_kv** 
 extern "C" wc_status wc_drafter_fuse(wc_drafter* d, const float* taps, int L, float* g) {
   if (!d || !taps || !g || L <= 0) return WC_ERR_INVALID;
   return guard(d->ctx, [&] {
-    const size_t stride = size_t(L) * d->cfg.target_hidden;
+    const int Ht = d->cfg.target_hidden;
+    const size_t stride = size_t(L) * Ht;
     for (int r0 = 0; r0 < L; r0 += GEMV_MAXL) {
       const int rows = std::min(GEMV_MAXL, L - r0);
-      drafter_fuse_impl(d, taps + size_t(r0) * d->cfg.target_hidden, stride, d->cfg.target_hidden, rows, nullptr,
-                        rows, g + size_t(r0) * d->cfg.hidden, d->ctx->d_err);
+      XIn tx[3];
+      drafter_pack_taps(d, taps + size_t(r0) * Ht, stride, Ht, rows, tx, d->ctx->d_err);
+      drafter_fuse_impl(d, tx, rows, nullptr, rows, g + size_t(r0) * d->cfg.hidden, d->ctx->d_err);
     }
   });
 }
@@ -1819,7 +2100,9 @@ extern "C" wc_status wc_drafter_forward(wc_drafter* d, wc_kv* cache, const int* 
       std::memset(&tok, 0, sizeof(tok));
       tok.tokens = tokens + r0;
       tok.vocab = c.vocab;
-      drafter_layers(d, cache, r, feat + size_t(r0) * H, tok, d->ws_h, ctx->d_err);
+      const float* f = feat + size_t(r0) * H;
+      const XIn fin = drafter_pack_rows(d, f, rows, d->layers[0].in_norm, d->xf_feat, d->ss_pack, ctx->d_err);
+      drafter_layers(d, cache, r, fin, f, tok, d->ws_h, nullptr, ctx->d_err);
       if (hidden) CUDA_TRY(cudaMemcpyAsync(hidden + size_t(r0) * H, d->ws_h, sizeof(float) * rows * H,
                                            cudaMemcpyDeviceToDevice, ctx->stream));
       if (out) {
@@ -1837,8 +2120,9 @@ extern "C" wc_status wc_drafter_logits(wc_drafter* d, const float* out, int rows
     for (int r0 = 0; r0 < rows; r0 += GEMV_MAXL) {
       const int n = std::min(GEMV_MAXL, rows - r0);
       CUDA_TRY(cudaMemsetAsync(d->ws_keys, 0, sizeof(unsigned long long) * GEMV_MAXL, d->ctx->stream));
-      drafter_head(d, out + size_t(r0) * d->cfg.hidden, n, nullptr, nullptr, d->ws_keys, z + size_t(r0) * d->head_rows,
-                   d->ctx->d_err);
+      const XIn x = drafter_pack_rows(d, out + size_t(r0) * d->cfg.hidden, n, nullptr, d->xf_out, nullptr,
+                                      d->ctx->d_err);
+      drafter_head(d, x, n, d->ws_keys, z + size_t(r0) * d->head_rows, nullptr, nullptr, d->ctx->d_err);
     }
   });
 }
@@ -1849,7 +2133,9 @@ extern "C" wc_status wc_drafter_head_argmax(wc_drafter* d, const float* out, int
     for (int r0 = 0; r0 < rows; r0 += GEMV_MAXL) {
       const int n = std::min(GEMV_MAXL, rows - r0);
       CUDA_TRY(cudaMemsetAsync(d->ws_keys, 0, sizeof(unsigned long long) * GEMV_MAXL, d->ctx->stream));
-      drafter_head(d, out + size_t(r0) * d->cfg.hidden, n, nullptr, nullptr, d->ws_keys, nullptr, d->ctx->d_err);
+      const XIn x = drafter_pack_rows(d, out + size_t(r0) * d->cfg.hidden, n, nullptr, d->xf_out, nullptr,
+                                      d->ctx->d_err);
+      drafter_head(d, x, n, d->ws_keys, nullptr, nullptr, nullptr, d->ctx->d_err);
       keys_to_index_kernel<<<1, 32, 0, d->ctx->stream>>>(d->ws_keys, n, d->vocab_map, token + r0);
       check_launch(d->ctx, "keys");
     }
@@ -1868,7 +2154,12 @@ struct wc_decoder {
   RoundState* st = nullptr;
   int* out_dev = nullptr;
   int* out_host = nullptr;  // pinned: [n_out, tokens..., err]
-  float *root_out = nullptr, *root_fb = nullptr, *d_g = nullptr, *taps = nullptr, *t_h = nullptr;
+  // the next round's chain root: head input and first drafter feature (fp32 + fragments)
+  float *root_out = nullptr, *root_fb = nullptr;
+  uint32_t *xf_root = nullptr, *xf_fb = nullptr;
+  float* ss_fb = nullptr;
+  float* taps = nullptr;  // prefill taps [3][n][Ht]
+  int taps_n = 0;
   std::map<int, std::pair<cudaGraphExec_t, uint64_t>> graphs;
   std::map<int, std::pair<cudaGraphExec_t, uint64_t>> prof_graphs;
   std::map<int, std::unique_ptr<Profiler>> profilers;
@@ -1880,51 +2171,94 @@ struct wc_decoder {
 
 namespace {
 
+void launch_finish(wc_decoder* dec, const int* L_dev, int L_static, bool advance) {
+  wc_drafter* d = dec->d;
+  FinishParams f;
+  std::memset(&f, 0, sizeof(f));
+  f.st = dec->st;
+  f.L_dev = L_dev;
+  f.L_static = L_static;
+  f.h = d->ws_h;
+  f.d = d->cfg.hidden;
+  f.norm_w = d->norm;
+  f.eps = d->cfg.eps;
+  f.post_norm = d->cfg.post_norm;
+  f.root_out = dec->root_out;
+  f.root_fb = dec->root_fb;
+  f.xf_out = dec->xf_root;
+  f.xf_fb = dec->xf_fb;
+  f.in_norm0 = d->layers[0].in_norm;
+  f.ss_fb = dec->ss_fb;
+  f.xf_width = xf_width(is_bf16(d->dtype), d->cfg.hidden);
+  f.xf_fp32 = is_bf16(d->dtype) ? 0 : 1;
+  f.advance_dc = advance ? 1 : 0;
+  launch_ex(dec->ctx, "finish update", finish_update_kernel, dim3(1), dim3(256), 0, true, 1, f);
+}
+
 void build_round(wc_decoder* dec, int K) {
   wc_ctx* ctx = dec->ctx;
   wc_target* t = dec->t;
   wc_drafter* d = dec->d;
   RoundState* st = dec->st;
   int* err = &st->err;
-  const int H = d->cfg.hidden, Ht = t->cfg.hidden;
   const bool post = d->cfg.post_norm != 0;
   // ---- draft chain (spec.py:344-350): K heads, K-1 drafter layer passes
+  XIn head_in{dec->xf_root, nullptr, 0};  // root_out is already normalised
+  const Lin& ld = d->layers.back().down;
   for (int k = 0; k < K; ++k) {
-    if (k == 0) drafter_head(d, dec->root_out, 1, nullptr, nullptr, st->keys + k, nullptr, err);
-    else drafter_head(d, d->ws_h, 1, d->norm, post ? d->ws_out : nullptr, st->keys + k, nullptr, err);
-    if (k < K - 1) {
-      const float* feat = k == 0 ? dec->root_fb : (post ? d->ws_out : d->ws_h);
-      Rows r;
-      r.L = 1;
-      r.L_max = 1;
-      r.n_dev = &st->dc_len;
-      r.n_add = k;
-      TokenSrc tok;
-      std::memset(&tok, 0, sizeof(tok));
-      tok.keys = st->keys + k;
-      tok.vocab_map = d->vocab_map;
-      tok.forced = st->forced + k;
-      tok.vocab = d->cfg.vocab;
-      prof_begin(ctx, PK_DRAFT_LAYER);
-      drafter_layers(d, dec->dkv, r, feat, tok, d->ws_h, err);
-      prof_end(ctx, PK_DRAFT_LAYER);
+    const bool more = k < K - 1;
+    // with post-norm the next feature is RMSNorm(h) * norm: the head's side job makes it
+    drafter_head(d, head_in, 1, st->keys + k, nullptr, (k > 0 && post && more) ? d->ws_h : nullptr,
+                 (k > 0 && post && more) ? d->ws_feat : nullptr, err);
+    if (!more) break;
+    XIn fin;
+    const float* feat;
+    if (k == 0) {
+      fin = XIn{dec->xf_fb, dec->ss_fb, 1};
+      feat = dec->root_fb;
+    } else if (post) {
+      fin = XIn{d->xf_feat, d->ss_feat, side_parts(ctx, d->head, 1)};
+      feat = d->ws_feat;
+    } else {
+      fin = XIn{d->xf_feat, d->layers.back().ss_d, gemv_grid(ctx, ld, 1)};
+      feat = d->ws_h;
     }
+    Rows r;
+    r.L = 1;
+    r.L_max = 1;
+    r.n_dev = &st->dc_len;
+    r.n_add = k;
+    TokenSrc tok;
+    std::memset(&tok, 0, sizeof(tok));
+    tok.keys = st->keys + k;
+    tok.vocab_map = d->vocab_map;
+    tok.forced = st->forced + k;
+    tok.vocab = d->cfg.vocab;
+    const XOut extra{d->xf_feat, d->layers[0].in_norm};
+    prof_begin(ctx, PK_DRAFT_LAYER);
+    head_in = drafter_layers(d, dec->dkv, r, fin, feat, tok, d->ws_h, post ? nullptr : &extra, err);
+    prof_end(ctx, PK_DRAFT_LAYER);
   }
   // ---- verification of [x_n, d_1..d_K] (spec.py:353-355)
-  embed_rows_kernel<<<K + 1, 256, 0, ctx->stream>>>(t->embed, t->dtype, t->cfg.vocab, Ht, nullptr, K + 1, nullptr,
-                                                    dec->t_h, st, d->vocab_map, K, nullptr);
-  check_launch(ctx, "embed verify");
   Rows rv;
   rv.L = K + 1;
   rv.L_max = K + 1;
   rv.n_dev = &st->n;
-  target_layers(t, dec->tkv, rv, dec->t_h, dec->taps, size_t(dec->max_k + 1) * Ht, err);
-  target_head(t, dec->t_h, K + 1, nullptr, K + 1, st->keys + K, nullptr, err);
+  const XIn in0 = target_embed(t, rv, nullptr, st, d->vocab_map, t->ws_h, err);
+  TapOut to;
+  for (int f = 0; f < 3; ++f) {
+    to.xf[f] = d->xf_tap[f];
+    to.w[f] = d->cfg.feature_norm ? d->feature_norms[f] : nullptr;
+  }
+  const XIn hx = target_layers(t, dec->tkv, rv, in0, t->ws_h, &to, err);
+  target_head(t, hx, K + 1, nullptr, K + 1, st->keys + K, nullptr, err);
   // ---- acceptance + chain compaction (spec.py:357-362)
-  accept_chain_kernel<<<1, 32, 0, ctx->stream>>>(st, K, nullptr, dec->out_dev);
-  check_launch(ctx, "accept");
+  launch_ex(ctx, "accept", accept_chain_kernel, dim3(1), dim3(32), 0, true, 1, st, K, (const int*)nullptr,
+            dec->out_dev);
   // ---- drafter update on the accepted rows (spec.py:363, 366-374)
-  drafter_fuse_impl(d, dec->taps, size_t(dec->max_k + 1) * Ht, Ht, K + 1, &st->L_upd, K + 1, dec->d_g, err);
+  XIn tx[3];
+  for (int f = 0; f < 3; ++f) tx[f] = target_tap_stats(t, f, d->xf_tap[f], K + 1);
+  const XIn gin = drafter_fuse_impl(d, tx, K + 1, &st->L_upd, K + 1, d->ws_g, err);
   Rows ru;
   ru.L = K + 1;
   ru.L_dev = &st->L_upd;
@@ -1934,10 +2268,8 @@ void build_round(wc_decoder* dec, int K) {
   std::memset(&tok, 0, sizeof(tok));
   tok.tokens = st->acc;
   tok.vocab = d->cfg.vocab;
-  drafter_layers(d, dec->dkv, ru, dec->d_g, tok, d->ws_h, err);
-  finish_update_kernel<<<1, 256, 0, ctx->stream>>>(st, &st->L_upd, K + 1, d->ws_h, H, d->norm, d->cfg.eps,
-                                                   d->cfg.post_norm, dec->root_out, dec->root_fb, 1);
-  check_launch(ctx, "finish update");
+  drafter_layers(d, dec->dkv, ru, gin, d->ws_g, tok, d->ws_h, nullptr, err);
+  launch_finish(dec, &st->L_upd, K + 1, true);
 }
 
 std::pair<cudaGraphExec_t, uint64_t>& round_graph(wc_decoder* dec, int K, bool profiled = false) {
@@ -1996,6 +2328,7 @@ extern "C" wc_status wc_decoder_create(wc_target* t, wc_drafter* d, int max_cont
     if (!t->finalized || !d->finalized) fail(WC_ERR_INVALID, "models not finalized");
     if (d->cfg.target_hidden != t->cfg.hidden) fail(WC_ERR_INVALID, "drafter target_hidden_size != target hidden");
     if (d->cfg.num_features != 3) fail(WC_ERR_UNSUPPORTED, "the decoder fuses exactly three target taps");
+    if (t->dtype != d->dtype) fail(WC_ERR_UNSUPPORTED, "target and drafter must use the same dtype");
     if (max_k < 1 || max_k > MAXK || max_k + 1 > GEMV_MAXL) fail(WC_ERR_INVALID, "max_k must be in 1..15");
     if (max_context < 2 || max_context > 32768 - MAXK) fail(WC_ERR_INVALID, "max_context out of range");
     wc_ctx* ctx = t->ctx;
@@ -2014,12 +2347,13 @@ extern "C" wc_status wc_decoder_create(wc_target* t, wc_drafter* d, int max_cont
     CUDA_TRY(cudaMemcpy(dec->st->forced, neg.data(), sizeof(int) * MAXK, cudaMemcpyHostToDevice));
     dec->out_dev = static_cast<int*>(dalloc(sizeof(int) * (MAXK + 4)));
     CUDA_TRY(cudaMallocHost(&dec->out_host, sizeof(int) * (MAXK + 4)));
-    const int H = d->cfg.hidden, Ht = t->cfg.hidden;
+    const int H = d->cfg.hidden;
+    const bool bf16 = is_bf16(d->dtype);
     dec->root_out = static_cast<float*>(dalloc(sizeof(float) * H));
     dec->root_fb = static_cast<float*>(dalloc(sizeof(float) * H));
-    dec->d_g = static_cast<float*>(dalloc(sizeof(float) * GEMV_MAXL * H));
-    dec->taps = static_cast<float*>(dalloc(sizeof(float) * 3 * (max_k + 1) * Ht));
-    dec->t_h = static_cast<float*>(dalloc(sizeof(float) * GEMV_MAXL * Ht));
+    dec->xf_root = xf_alloc(bf16, H);
+    dec->xf_fb = xf_alloc(bf16, H);
+    dec->ss_fb = ss_alloc(ctx);
     CUDA_TRY(cudaEventCreate(&dec->ev0));
     CUDA_TRY(cudaEventCreate(&dec->ev1));
     *out = dec.release();
@@ -2036,11 +2370,9 @@ extern "C" void wc_decoder_destroy(wc_decoder* dec) {
   dfree(dec->st);
   dfree(dec->out_dev);
   if (dec->out_host) cudaFreeHost(dec->out_host);
-  dfree(dec->root_out);
-  dfree(dec->root_fb);
-  dfree(dec->d_g);
-  dfree(dec->taps);
-  dfree(dec->t_h);
+  for (void* p : {(void*)dec->root_out, (void*)dec->root_fb, (void*)dec->xf_root, (void*)dec->xf_fb,
+                  (void*)dec->ss_fb, (void*)dec->taps})
+    dfree(p);
   if (dec->ev0) cudaEventDestroy(dec->ev0);
   if (dec->ev1) cudaEventDestroy(dec->ev1);
   delete dec;
@@ -2057,18 +2389,20 @@ int decoder_prefill_impl(wc_decoder* dec, const int* prompt, int n, const wc_sam
   wc_ctx* ctx = dec->ctx;
   wc_target* t = dec->t;
   wc_drafter* d = dec->d;
-  const int Ht = t->cfg.hidden, H = d->cfg.hidden;
+  const int Ht = t->cfg.hidden;
   for (int i = 0; i < n; ++i)
     if (prompt[i] < 0 || prompt[i] >= t->cfg.vocab) fail(WC_ERR_INVALID, "prompt token id out of range");
+  if (dec->taps_n < n) {
+    CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    dfree(dec->taps);
+    dec->taps = static_cast<float*>(dalloc(sizeof(float) * 3 * size_t(n) * Ht));
+    dec->taps_n = n;
+  }
   int* d_tok = static_cast<int*>(dalloc(sizeof(int) * (n + 1)));
-  float* taps = static_cast<float*>(dalloc(sizeof(float) * 3 * size_t(n) * Ht));
-  float* g = static_cast<float*>(dalloc(sizeof(float) * GEMV_MAXL * H));
   struct Free {
-    void* a[3];
-    ~Free() {
-      for (void* p : a) dfree(p);
-    }
-  } guard_free{{d_tok, taps, g}};
+    void* p;
+    ~Free() { dfree(p); }
+  } guard_free{d_tok};
   CUDA_TRY(cudaMemcpyAsync(d_tok, prompt, sizeof(int) * n, cudaMemcpyHostToDevice, ctx->stream));
   CUDA_TRY(cudaMemsetAsync(dec->st, 0, offsetof(RoundState, forced), ctx->stream));
   CUDA_TRY(cudaMemsetAsync(dec->st->keys, 0, sizeof(dec->st->keys), ctx->stream));
@@ -2076,15 +2410,16 @@ int decoder_prefill_impl(wc_decoder* dec, const int* prompt, int n, const wc_sam
   const size_t tstride = size_t(n) * Ht;
   for (int r0 = 0; r0 < n; r0 += GEMV_MAXL) {
     const int rows = std::min(GEMV_MAXL, n - r0);
-    embed_rows_kernel<<<rows, 256, 0, ctx->stream>>>(t->embed, t->dtype, t->cfg.vocab, Ht, d_tok + r0, rows, nullptr,
-                                                     dec->t_h, nullptr, nullptr, 0, &dec->st->err);
-    check_launch(ctx, "embed");
     Rows r;
     r.L = rows;
     r.L_max = rows;
     r.n_add = r0;
-    target_layers(t, dec->tkv, r, dec->t_h, taps + size_t(r0) * Ht, tstride, err);
-    if (r0 + rows == n) target_head(t, dec->t_h + size_t(rows - 1) * Ht, 1, nullptr, 1, dec->st->keys, nullptr, err);
+    const XIn in0 = target_embed(t, r, d_tok + r0, nullptr, nullptr, t->ws_h, err);
+    TapOut to;
+    to.rows = dec->taps + size_t(r0) * Ht;
+    to.stride = tstride;
+    target_layers(t, dec->tkv, r, in0, t->ws_h, &to, err);
+    if (r0 + rows == n) target_head_rows(t, t->ws_h + size_t(rows - 1) * Ht, 1, dec->st->keys, nullptr, err);
   }
   int first = 0;
   {
@@ -2098,7 +2433,9 @@ int decoder_prefill_impl(wc_decoder* dec, const int* prompt, int n, const wc_sam
   CUDA_TRY(cudaMemcpyAsync(d_tok + n - 1, &first, sizeof(int), cudaMemcpyHostToDevice, ctx->stream));
   for (int r0 = 0; r0 < n; r0 += GEMV_MAXL) {
     const int rows = std::min(GEMV_MAXL, n - r0);
-    drafter_fuse_impl(d, taps + size_t(r0) * Ht, tstride, Ht, rows, nullptr, rows, g, err);
+    XIn tx[3];
+    drafter_pack_taps(d, dec->taps + size_t(r0) * Ht, tstride, Ht, rows, tx, err);
+    const XIn gin = drafter_fuse_impl(d, tx, rows, nullptr, rows, d->ws_g, err);
     Rows r;
     r.L = rows;
     r.L_max = rows;
@@ -2107,12 +2444,8 @@ int decoder_prefill_impl(wc_decoder* dec, const int* prompt, int n, const wc_sam
     std::memset(&tok, 0, sizeof(tok));
     tok.tokens = d_tok + r0;
     tok.vocab = d->cfg.vocab;
-    drafter_layers(d, dec->dkv, r, g, tok, d->ws_h, err);
-    if (r0 + rows == n) {
-      finish_update_kernel<<<1, 256, 0, ctx->stream>>>(dec->st, nullptr, rows, d->ws_h, H, d->norm, d->cfg.eps,
-                                                       d->cfg.post_norm, dec->root_out, dec->root_fb, 0);
-      check_launch(ctx, "finish prefill");
-    }
+    drafter_layers(d, dec->dkv, r, gin, d->ws_g, tok, d->ws_h, nullptr, err);
+    if (r0 + rows == n) launch_finish(dec, nullptr, rows, false);
   }
   RoundState init{};
   init.n = n;
@@ -2292,15 +2625,13 @@ extern "C" wc_status wc_generate_autoregressive(wc_target* t, const int* prompt,
       if (prompt[i] < 0 || prompt[i] >= t->cfg.vocab) fail(WC_ERR_INVALID, "prompt token id out of range");
     for (int r0 = 0; r0 < n; r0 += GEMV_MAXL) {
       const int rows = std::min(GEMV_MAXL, n - r0);
-      embed_rows_kernel<<<rows, 256, 0, ctx->stream>>>(t->embed, t->dtype, t->cfg.vocab, Ht, d_tok + r0, rows,
-                                                       nullptr, h, nullptr, nullptr, 0, &st->err);
-      check_launch(ctx, "embed");
       Rows r;
       r.L = rows;
       r.L_max = rows;
       r.n_add = r0;
-      target_layers(t, kv.get(), r, h, nullptr, 0, &st->err);
-      if (r0 + rows == n) target_head(t, h + size_t(rows - 1) * Ht, 1, nullptr, 1, st->keys, nullptr, &st->err);
+      const XIn in0 = target_embed(t, r, d_tok + r0, nullptr, nullptr, h, &st->err);
+      target_layers(t, kv.get(), r, in0, h, nullptr, &st->err);
+      if (r0 + rows == n) target_head_rows(t, h + size_t(rows - 1) * Ht, 1, st->keys, nullptr, &st->err);
     }
     // st->n = n - 1 so that the first advance makes it n while emitting the first token
     RoundState init{};
@@ -2325,15 +2656,13 @@ extern "C" wc_status wc_generate_autoregressive(wc_target* t, const int* prompt,
         ctx->capturing = true;
         ctx->capture_launches = 0;
         try {
-          embed_rows_kernel<<<1, 256, 0, ctx->stream>>>(t->embed, t->dtype, t->cfg.vocab, Ht, nullptr, 1, nullptr, h,
-                                                        st, nullptr, 0, nullptr);
-          check_launch(ctx, "embed");
           Rows r;
           r.L = 1;
           r.L_max = 1;
           r.n_dev = &st->n;
-          target_layers(t, kv.get(), r, h, nullptr, 0, &st->err);
-          target_head(t, h, 1, nullptr, 1, st->keys, nullptr, &st->err);
+          const XIn in0 = target_embed(t, r, nullptr, st, nullptr, h, &st->err);
+          const XIn hx = target_layers(t, kv.get(), r, in0, h, nullptr, &st->err);
+          target_head(t, hx, 1, nullptr, 1, st->keys, nullptr, &st->err);
           ar_advance_kernel<<<1, 32, 0, ctx->stream>>>(st, d_out);
           check_launch(ctx, "ar advance");
         } catch (...) {
