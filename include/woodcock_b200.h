@@ -174,6 +174,28 @@ WC_API wc_status wc_accept_greedy(wc_ctx* ctx, const int* argmax_dev, const int*
 WC_API wc_status wc_accept_stochastic(wc_ctx* ctx, const double* p_dev, const double* q_dev, int V, const int* tokens_dev,
                                const int* parents_dev, int N, uint64_t seed, uint64_t offset, int* out_path_dev,
                                int* out_n_dev, int* out_next_dev, int* out_used_dev);
+/* The same decision as wc_accept_stochastic (same arguments, same results), for callers that must
+ * not allocate device memory while they verify. No counterpart in the reference, whose sampling
+ * runs on the host (python/woodcock/sampling.py, src/core/sampling.cpp).
+ * wc_accept_stochastic keeps two scratch rows of V doubles per context and grows them with
+ * cudaMalloc / cudaFree on its first call and whenever V grows. cudaFree waits for the whole
+ * device, which a caller that keeps other streams busy cannot accept, and a caller that runs
+ * under a device-memory budget fixed at start-up cannot let a library allocate behind its back.
+ * This entry allocates nothing: its scratch is one array compiled into the library, two rows of
+ * WC_ACCEPT_NOALLOC_MAX_V doubles (2.5 MiB of device memory per GPU).
+ *  - V > WC_ACCEPT_NOALLOC_MAX_V returns WC_ERR_CAPACITY and launches nothing.
+ *  - Nothing in the scratch has to start at zero: each call writes the rows before it reads them.
+ *  - The first call on a device looks up the array's device address (cudaGetSymbolAddress), with
+ *    the context's device current (otherwise WC_ERR_INVALID). Make that first call before any
+ *    stream capture begins.
+ *  - Every call on one device uses the same array. Two calls that can run at the same time
+ *    (different streams, or different contexts on that device) race on it: order them on one
+ *    stream, or use wc_accept_stochastic. */
+#define WC_ACCEPT_NOALLOC_MAX_V 163840
+WC_API wc_status wc_accept_stochastic_noalloc(wc_ctx* ctx, const double* p_dev, const double* q_dev, int V,
+                                       const int* tokens_dev, const int* parents_dev, int N, uint64_t seed,
+                                       uint64_t offset, int* out_path_dev, int* out_n_dev, int* out_next_dev,
+                                       int* out_used_dev);
 /* fp64 uniforms of the Philox stream, for the host side of tests and for draft sampling */
 WC_API wc_status wc_philox_uniforms(wc_ctx* ctx, uint64_t seed, uint64_t offset, int n, double* out_dev);
 

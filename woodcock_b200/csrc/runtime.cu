@@ -17,6 +17,7 @@
 #include <functional>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <set>
 #include <string>
 #include <vector>
@@ -852,6 +853,52 @@ extern "C" wc_status wc_accept_stochastic(wc_ctx* ctx, const double* p, const do
                                                                ctx->qw, out_path, out_n, out_next, out_used,
                                                                ctx->d_err);
     check_launch(ctx, "accept_stochastic");
+  });
+}
+
+// ---- wc_accept_stochastic_noalloc: the same kernel with scratch compiled into the library,
+// for callers that cannot let a verify step allocate (or free, which waits for the device).
+// Two rows of WC_ACCEPT_NOALLOC_MAX_V doubles (p residual, q); each call overwrites what it reads.
+static __device__ __align__(256) double g_accept_scratch[2 * WC_ACCEPT_NOALLOC_MAX_V];
+
+namespace {
+constexpr int kMaxDevices = 256;
+std::mutex g_scratch_mu;
+double* g_scratch_addr[kMaxDevices] = {};  // device address of g_accept_scratch per ordinal
+}  // namespace
+
+extern "C" wc_status wc_accept_stochastic_noalloc(wc_ctx* ctx, const double* p, const double* q, int V,
+                                                  const int* tokens, const int* parents, int N, uint64_t seed,
+                                                  uint64_t offset, int* out_path, int* out_n, int* out_next,
+                                                  int* out_used) {
+  if (!ctx || !p || !q || !tokens || !parents || !out_path || !out_n || !out_next || !out_used || N <= 0 || V <= 0)
+    return WC_ERR_INVALID;
+  return guard(ctx, [&] {
+    if (V > WC_ACCEPT_NOALLOC_MAX_V)
+      fail(WC_ERR_CAPACITY, "wc_accept_stochastic_noalloc: V = " + std::to_string(V) +
+                                " exceeds WC_ACCEPT_NOALLOC_MAX_V = " + std::to_string(WC_ACCEPT_NOALLOC_MAX_V));
+    int cur = -1;
+    CUDA_TRY(cudaGetDevice(&cur));
+    if (cur != ctx->device)
+      fail(WC_ERR_INVALID, "wc_accept_stochastic_noalloc: make the context's device current first");
+    if (cur < 0 || cur >= kMaxDevices) fail(WC_ERR_UNSUPPORTED, "device ordinal out of range");
+    double* scratch = nullptr;
+    {
+      // one-time set-up per device, with that device current
+      std::lock_guard<std::mutex> lock(g_scratch_mu);
+      if (!g_scratch_addr[cur]) {
+        void* a = nullptr;
+        const cudaError_t e = cudaGetSymbolAddress(&a, g_accept_scratch);
+        if (e != cudaSuccess || !a)
+          fail(WC_ERR_CUDA, std::string("cudaGetSymbolAddress(scratch): ") + cudaGetErrorString(e));
+        g_scratch_addr[cur] = static_cast<double*>(a);
+      }
+      scratch = g_scratch_addr[cur];
+    }
+    accept_stochastic_tree_kernel<<<1, 1024, 0, ctx->stream>>>(p, q, V, tokens, parents, N, seed, offset, scratch,
+                                                               scratch + WC_ACCEPT_NOALLOC_MAX_V, out_path, out_n,
+                                                               out_next, out_used, ctx->d_err);
+    check_launch(ctx, "accept_stochastic_noalloc");
   });
 }
 
