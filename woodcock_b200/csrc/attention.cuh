@@ -68,6 +68,9 @@ struct AttnParams {
   int xf_width;      // their (padded) width, >= H*D
   int xf_fp32;       // fp32 models: xf_out holds plain fp32 rows [16][H*D]
   int write_cache;
+  int stable_prefix;  // n_dev and the cache rows below it were written by completed work
+                      // (not by a kernel that may still run): they may be read before the
+                      // dependency wait
   int* err;
 };
 
@@ -90,7 +93,7 @@ __device__ __forceinline__ void kv_store(void* base, int dtype, long long off, f
   else static_cast<float*>(base)[off] = v;
 }
 
-__global__ void __launch_bounds__(ATT_THREADS) attention_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(ATT_THREADS) attention_kernel(__grid_constant__ const AttnParams p) {
   extern __shared__ __align__(16) unsigned char smem[];
   cg::cluster_group cluster = cg::this_cluster();
   const int S = int(cluster.num_blocks());

@@ -44,7 +44,7 @@ inline size_t attention_mma_smem(int L_max) {
 }
 
 template <int D>
-__global__ void __launch_bounds__(AM_THREADS) attention_mma_kernel(const AttnParams p) {
+__global__ void __launch_bounds__(AM_THREADS) attention_mma_kernel(__grid_constant__ const AttnParams p) {
   using Lay = AmLayout<D>;
   constexpr int LD = Lay::LD;
   constexpr int NDT = D / 8;  // 8-wide output tiles

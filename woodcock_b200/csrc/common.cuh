@@ -97,6 +97,20 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
 
+// Kernel parameters live in a per-launch constant buffer, so the first use of each of its
+// lines misses, and spread along a kernel those misses add up one after another. A kernel
+// with a large parameter block copies it into shared memory at entry (one parallel load,
+// before the dependency wait) and reads every field from there. The parameter must be
+// declared __grid_constant__ so that its address refers to it; call from all threads,
+// followed by a barrier.
+template <typename P>
+__device__ __forceinline__ void params_to_smem(const P& p, P* dst) {
+  static_assert(sizeof(P) % 4 == 0, "parameter block size");
+  const uint32_t* src = reinterpret_cast<const uint32_t*>(&p);
+  uint32_t* d = reinterpret_cast<uint32_t*>(dst);
+  for (unsigned i = threadIdx.x; i < sizeof(P) / 4; i += blockDim.x) d[i] = src[i];
+}
+
 // Orderable argmax key: larger value first, then the smaller index (first maximum,
 // like std::max_element / np.argmax). atomicMax over keys is order-independent.
 __device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t idx) {
@@ -224,6 +238,20 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
                    smem_addr(dst)),
                "l"(src), "r"(bytes), "r"(smem_addr(bar))
                : "memory");
+}
+// L2 policy for data read once (streamed weights): evicted before other lines.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;\n" : "=l"(pol));
+  return pol;
+}
+// bulk_g2s with an L2 cache policy
+__device__ __forceinline__ void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;\n" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(pol)
+      : "memory");
 }
 // named barrier among `count` threads (warps 0 .. count/32-1)
 __device__ __forceinline__ void named_sync(int id, int count) {

@@ -2,24 +2,30 @@
 //   y[L][N] = sum_s inv_s[l] * (x_s[L][K_s] . W_s[N][K_s]^T).
 //
 // Inputs arrive already in the GEMV's input form ("fragments", common.cuh): the producing
-// kernel wrote them pre-multiplied by this GEMV's RMSNorm gain, together with per-block
-// partial sums of squares of its rows. The per-row 1/rms (inv_s) is applied to the
-// accumulators, so a normalised input costs no prologue pass. This covers the reference's
-// rmsnorm -> linear pairs (src/core/qwen3.cpp:86-101, src/core/drafter.cpp:106-128) and
-// the drafter's per-tap RMSNorm + fc fusion (drafter.cpp:75-89). A segment can instead
-// gather embedding rows by token id (the drafter's auxiliary stream, drafter.cpp:110-116),
-// scaled by a per-token 1/rms table built at load time.
+// kernel wrote them pre-multiplied by this GEMV's RMSNorm gain, together with partial sums
+// of squares of its rows. The per-row 1/rms (inv_s) is applied to the accumulators, so a
+// normalised input costs no prologue pass. This covers the reference's rmsnorm -> linear
+// pairs (src/core/qwen3.cpp:86-101, src/core/drafter.cpp:106-128) and the drafter's per-tap
+// RMSNorm + fc fusion (drafter.cpp:75-89). A segment can instead gather embedding rows by
+// token id (the drafter's auxiliary stream, drafter.cpp:110-116), scaled by a per-token
+// 1/rms table built at load time.
 //
 // bf16 weights are pre-tiled in mma.m16n8k16 A-fragment order (16x16 tile = 512 contiguous
-// bytes) and stream through a 4-stage ring of 16 KB shared-memory slabs filled by 1-D bulk
-// (TMA) copies from a producer warp; the copies start before the kernel waits on its
-// predecessor (programmatic dependent launch), so the weight stream overlaps the previous
-// kernel's tail. Eight consumer warps split each slab's k-tiles and issue two MMAs per tile
-// and n-tile (activation hi and lo bf16 terms, fp32-level accuracy), then release the slot
-// through an mbarrier. Epilogues: store, residual add (linear(..., accumulate=true)),
-// SwiGLU (silu(gate)*up, cpu_ops.cpp:79-84, gate/up row blocks interleaved) and a fused
-// argmax. Stored results can also be emitted as fragments for up to two consumers (times
-// their norm gains) and as per-block partial sums of squares for their 1/rms.
+// bytes). One block per SM: a producer warp streams the block's weights through a 4-stage
+// ring of 16 KB shared-memory slabs with 1-D bulk (TMA) copies marked L2 evict-first; the
+// first stages are issued before the kernel waits on its predecessor (programmatic
+// dependent launch). After the wait the producer bulk-copies the activation fragments of
+// the block's K-chunk into shared memory once, so the MMA loop reads only shared memory.
+// Eight consumer warps split each slab's k-tiles and issue two MMAs per tile and n-tile
+// (activation hi and lo bf16 terms, fp32-level accuracy), then release the slot through an
+// mbarrier. When K exceeds the activation buffer, K is split into chunks: the blocks of one
+// row range write fp32 partials and the last of them to arrive (one fence and one atomic
+// per block) adds them in chunk order and runs the epilogue, so results do not depend on
+// arrival order. Epilogues: store, residual add (linear(..., accumulate=true)), SwiGLU
+// (silu(gate)*up, cpu_ops.cpp:79-84, gate/up row blocks interleaved) and a fused argmax;
+// stored results can also be emitted as fragments for up to two consumers (times their norm
+// gains) and as per-unit sums of squares for their 1/rms. As its own stream ends, each block
+// prefetches its share of the next GEMV's weights into L2.
 //
 // fp32 weights (row-major [N][Kp]) run the same interface on CUDA cores: fragments are
 // then plain fp32 rows [16][len].
@@ -40,11 +46,14 @@ constexpr int GV_SLAB = 32;                         // k-tiles per ring stage: 5
 constexpr int GV_COLS = GV_SLAB * 16;
 constexpr int GV_STAGE_BYTES = GV_SLAB * 512;       // 16 KB
 constexpr int GV_NSTAGE = 4;
-constexpr int GV_RBB = 2;                           // row blocks per reduction batch
+constexpr int GV_ACT_BYTES = 64 * 1024;             // activation chunk buffer
 constexpr int GV_TPW = GV_SLAB / GV_CWARPS;         // k-tiles per warp per slab
 constexpr int GV_F32_THREADS = 256;
 constexpr int GV_F32_WARPS = GV_F32_THREADS / kWarp;
 constexpr int GV_SIDE_BLOCKS = 16;                  // blocks that run a head's side job
+
+// Slabs of K per activation chunk: 4 (2048 columns) for 8 rows, 2 for 16 rows.
+__host__ __device__ constexpr int gv_chunk_slabs(int NT) { return GV_ACT_BYTES / (GV_STAGE_BYTES * NT); }
 
 // Fragment width of an input of K columns: bf16 models pad to whole ring slabs.
 __host__ __device__ inline int xf_width(bool bf16, int K) { return bf16 ? (K + GV_COLS - 1) / GV_COLS * GV_COLS : K; }
@@ -98,7 +107,15 @@ struct GemvParams {
   int nout;
   XOut out[2];
   int out_width;         // fragment width of the outputs (xf_width(N))
-  float* ss_out;         // [gridDim.x][16]: this block's partial sum of y^2 per row
+  float* ss_out;         // bf16: [units][16] sum of y^2 per row over each unit's features;
+                         // fp32: [gridDim.x][16] per block
+  // bf16 work split: gridDim.x = nkc * gpk; block b owns K-chunk b % nkc (kc_slabs slabs)
+  // and the (b / nkc)-th of gpk contiguous unit ranges
+  int nkc, kc_slabs, gpk;
+  float* partial;        // nkc > 1: [nkc][Np / 16][16 features][16 rows] fp32 partial sums
+  int* counters;         // nkc > 1: [gpk] arrivals per unit range (left at zero)
+  const void* pf;        // L2 prefetch of the next GEMV's weights, split over the blocks
+  size_t pf_bytes;
   // side job of a drafter head, in blocks < side_blocks:
   //   side_y = side_src * inv(seg 0) * side_w, the next chain step's feature
   const float* side_src;
@@ -171,12 +188,9 @@ __device__ void gemv_prologue(const GemvParams& p, int L, int* s_tok, float* s_i
   named_sync(1, 256);
 }
 
-// B operand of one k-tile for this lane: {hi(2t), hi(2t+8), lo(2t), lo(2t+8)} of row nt*8 + g.
-__device__ __forceinline__ uint4 xseg_b(const XSeg& s, int kt_in_seg, int nt, int lane, int L, const int* s_tok) {
-  if (s.xf) {
-    const uint4* f = reinterpret_cast<const uint4*>(s.xf);
-    return __ldg(f + (size_t(nt) * (s.lenp >> 4) + kt_in_seg) * 32 + lane);
-  }
+// B operand of one k-tile of an embedding segment for this lane: {hi(2t), hi(2t+8), lo(2t),
+// lo(2t+8)} of row nt*8 + g, i.e. table[tok] * norm_w in fragment form (zero past L or len).
+__device__ __forceinline__ uint4 xseg_table_b(const XSeg& s, int kt_in_seg, int nt, int lane, int L, const int* s_tok) {
   const int g = lane >> 2, t = lane & 3, l = nt * 8 + g;
   if (l >= L || kt_in_seg * 16 >= s.len) return make_uint4(0, 0, 0, 0);
   const int c = kt_in_seg * 16 + 2 * t;
@@ -189,6 +203,21 @@ __device__ __forceinline__ uint4 xseg_b(const XSeg& s, int kt_in_seg, int nt, in
   split2_bf16(__uint_as_float(e0 << 16) * w0.x, __uint_as_float(e0 & 0xFFFF0000u) * w0.y, b.x, b.z);
   split2_bf16(__uint_as_float(e1 << 16) * w1.x, __uint_as_float(e1 & 0xFFFF0000u) * w1.y, b.y, b.w);
   return b;
+}
+
+// Segment holding global slab `slab` (slabs of 512 padded columns); *first = its first slab.
+__device__ __forceinline__ int gemv_seg_of(const GemvParams& p, int slab, int* first) {
+  int f = 0;
+  for (int s = 0; s < p.nseg; ++s) {
+    const int n = p.seg[s].lenp / GV_COLS;
+    if (slab < f + n || s + 1 == p.nseg) {
+      *first = f;
+      return s;
+    }
+    f += n;
+  }
+  *first = 0;
+  return 0;
 }
 
 // The head's side job over this block's slice of the feature (s_inv[l] = seg 0's 1/rms).
@@ -221,58 +250,119 @@ __device__ void gemv_side_job(const GemvParams& p, int L, const float* s_inv, fl
   }
 }
 
+// Epilogue of one output element: feature n of unit u (row r16 of its block), row l; v0 the
+// sum (SwiGLU: gate), v1 the up sum. Writes y / y2 / fragments, returns y^2 for the unit's
+// sum of squares; argmax goes to the block key.
+__device__ __forceinline__ float gemv_epilogue(const GemvParams& p, int n, int l, float v0, float v1,
+                                               unsigned long long* s_key) {
+  float v = v0;
+  if (p.epi == EPI_ARGMAX) {
+    if (p.y) p.y[size_t(l) * p.ldy + n] = v;
+    atomicMax(&s_key[l], argmax_key(v, uint32_t(n)));
+    return 0.f;
+  }
+  if (p.epi == EPI_SWIGLU) v = v0 / (1.f + expf(-v0)) * v1;
+  if (p.epi == EPI_ADD) v += p.base[size_t(l) * p.ldb + n];
+  if (p.y) p.y[size_t(l) * p.ldy + n] = v;
+  if (p.y2) p.y2[size_t(l) * p.ldy2 + n] = v;
+  for (int o = 0; o < p.nout; ++o) xf_store(p.out[o].xf, p.out_width, l, n, p.out[o].w ? v * p.out[o].w[n] : v);
+  return v * v;
+}
+
 template <int NT>
-__global__ void __launch_bounds__(GV_THREADS, 2) gemv_bf16_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constant__ const GemvParams pk) {
+  constexpr int CHS = gv_chunk_slabs(NT);
   extern __shared__ __align__(128) unsigned char gv_smem[];
-  unsigned char* smem = gv_smem;
-  unsigned char* ring = smem;                                                         // NSTAGE x 16 KB
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + GV_NSTAGE * GV_STAGE_BYTES);    // [NSTAGE]
-  uint64_t* empty = full + GV_NSTAGE;                                                 // [NSTAGE]
-  float* red = reinterpret_cast<float*>(empty + GV_NSTAGE);                           // [RBB][NT][W][32][4]
-  float* s_inv = red + GV_RBB * NT * GV_CWARPS * kWarp * 4;                           // [3][16]
-  float* s_sq = s_inv + GEMV_MAXSEG * 16;                                             // [RBB*16][16]
-  float* s_ss = s_sq + GV_RBB * 16 * 16;                                              // [16]
-  int* s_tok = reinterpret_cast<int*>(s_ss + 16);                                     // [16]
-  unsigned long long* s_key = reinterpret_cast<unsigned long long*>(s_tok + 16);      // [16]
+  unsigned char* ring = gv_smem;                                              // NSTAGE x 16 KB
+  unsigned char* act = ring + GV_NSTAGE * GV_STAGE_BYTES;                     // [NT][CHS][32 kt][32 lanes] uint4
+  uint64_t* full = reinterpret_cast<uint64_t*>(act + GV_ACT_BYTES);           // [NSTAGE]
+  uint64_t* empty = full + GV_NSTAGE;                                         // [NSTAGE]
+  uint64_t* act_bar = empty + GV_NSTAGE;                                      // [1]
+  float* red = reinterpret_cast<float*>(act_bar + 2);                         // [2][NT][W][32][4]
+  float* s_inv = red + 2 * NT * GV_CWARPS * kWarp * 4;                        // [3][16]
+  float* s_part = s_inv + GEMV_MAXSEG * 16;                                   // [256]
+  float* s_sq = s_part + 256;                                                 // [16 features][16 rows]
+  int* s_tok = reinterpret_cast<int*>(s_sq + 256);                            // [16]
+  int* s_flag = s_tok + 16;                                                   // [4]
+  unsigned long long* s_key = reinterpret_cast<unsigned long long*>(s_flag + 4);  // [16]
+  const uint4* act4 = reinterpret_cast<const uint4*>(act);
+  GemvParams* s_params = reinterpret_cast<GemvParams*>(s_key + 16);
+  params_to_smem(pk, s_params);
+  __syncthreads();
+  const GemvParams& p = *s_params;
 
   const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
   const int G = p.group;
   const int nunits = p.Np / (16 * G);
-  const int u0 = int((long long)blockIdx.x * nunits / gridDim.x);
-  const int u1 = int((long long)(blockIdx.x + 1) * nunits / gridDim.x);
   const int KT = p.Kp >> 4;
   const int nslab = KT / GV_SLAB;
-  const int rb_first = u0 * G, nrb = (u1 - u0) * G;
-  const int total = nrb * nslab;  // ring stages: row-block major, slab minor
+  const int kc = int(blockIdx.x) % p.nkc, gi = int(blockIdx.x) / p.nkc;
+  const int u0 = int((long long)gi * nunits / p.gpk), u1 = int((long long)(gi + 1) * nunits / p.gpk);
+  const int s0 = kc * p.kc_slabs, s1 = min(nslab, s0 + p.kc_slabs), ns = s1 - s0;
+  const int total = (u1 - u0) * G * ns;  // ring stages: unit, row block of the unit, slab
   if (tid == 0) {
     for (int s = 0; s < GV_NSTAGE; ++s) {
       mbar_init(full + s, 1);
       mbar_init(empty + s, GV_CWARPS);
     }
+    mbar_init(act_bar, 1);
     mbar_fence_init();
   }
   __syncthreads();
   pdl_launch_dependents();
 
-  if (warp == GV_CWARPS) {  // ---- producer: the weights do not depend on the previous kernel
+  if (warp == GV_CWARPS) {  // ---- producer
     if (lane == 0) {
-      const char* wbase = static_cast<const char*>(p.w) + size_t(rb_first) * KT * 512;
+      const uint64_t pol = l2_evict_first_policy();
+      const char* w = static_cast<const char*>(p.w);
+      auto issue = [&](int q) {
+        const int st = q % GV_NSTAGE, rbl = q / ns, si = q % ns;
+        const size_t rb = size_t(u0) * G + rbl;
+        mbar_arrive_expect_tx(full + st, GV_STAGE_BYTES);
+        bulk_g2s_hint(ring + st * GV_STAGE_BYTES, w + (rb * KT + size_t(s0 + si) * GV_SLAB) * 512, GV_STAGE_BYTES,
+                      full + st, pol);
+      };
       int issued = 0;
-      for (int q = 0; q < total; ++q) {
-        const int s = q % GV_NSTAGE;
-        // the first refill waits for the consumers, i.e. for the previous kernel: a long bound
-        if (q >= GV_NSTAGE && !mbar_wait(empty + s, ((q / GV_NSTAGE) - 1) & 1, 1u << 26)) {
+      // weights do not depend on the previous kernel: fill the ring before waiting on it
+      for (; issued < min(total, GV_NSTAGE); ++issued) issue(issued);
+      pdl_wait();
+      uint32_t act_bytes = 0;
+      for (int sl = s0; sl < s1; ++sl) {
+        int f0;
+        if (p.seg[gemv_seg_of(p, sl, &f0)].xf) act_bytes += NT * GV_STAGE_BYTES;
+      }
+      mbar_arrive_expect_tx(act_bar, act_bytes);
+      for (int sl = s0; sl < s1; ++sl) {
+        int f0;
+        const XSeg& sg = p.seg[gemv_seg_of(p, sl, &f0)];
+        if (!sg.xf) continue;
+        for (int nt = 0; nt < NT; ++nt)
+          bulk_g2s(act + (nt * CHS + (sl - s0)) * GV_STAGE_BYTES,
+                   reinterpret_cast<const char*>(sg.xf) + (size_t(nt) * (sg.lenp >> 4) + size_t(sl - f0) * GV_SLAB) * 512,
+                   GV_STAGE_BYTES, act_bar);
+      }
+      bool ok = true;
+      for (; issued < total; ++issued) {
+        const int st = issued % GV_NSTAGE;
+        if (!mbar_wait(empty + st, ((issued / GV_NSTAGE) - 1) & 1, 1u << 26)) {
           raise_error(p.err, kErrTimeout);
+          ok = false;
           break;
         }
-        mbar_arrive_expect_tx(full + s, GV_STAGE_BYTES);
-        bulk_g2s(ring + s * GV_STAGE_BYTES, wbase + size_t(q) * GV_STAGE_BYTES, GV_STAGE_BYTES, full + s);
-        ++issued;
+        issue(issued);
+      }
+      // the HBM stream of this block is issued: fetch our share of the next GEMV's weights
+      if (ok && p.pf && p.pf_bytes >= 16) {
+        const size_t per = ((p.pf_bytes / gridDim.x) + 15) & ~size_t(15);
+        const size_t b0 = per * blockIdx.x, b1 = min(p.pf_bytes & ~size_t(15), b0 + per);
+        for (size_t o = b0; o < b1; o += (1u << 20))
+          prefetch_l2_bulk(static_cast<const char*>(p.pf) + o, uint32_t(min(size_t(1u << 20), b1 - o)));
       }
       // the block's shared memory must outlive every copy issued into it, also when the
       // consumers gave up on a wait: wait (bounded) for the last copy of each slot
       for (int q = max(0, issued - GV_NSTAGE); q < issued; ++q)
         if (!mbar_wait(full + q % GV_NSTAGE, (q / GV_NSTAGE) & 1)) raise_error(p.err, kErrTimeout);
+      if (!mbar_wait(act_bar, 0)) raise_error(p.err, kErrTimeout);
     }
     return;
   }
@@ -280,143 +370,190 @@ __global__ void __launch_bounds__(GV_THREADS, 2) gemv_bf16_kernel(const GemvPara
   // ---- consumers
   pdl_wait();
   const int L = gemv_rows(p.L_dev, p.L, p.L_max, p.err);
-  if (tid < 16) {
-    s_key[tid] = 0ull;
-    s_ss[tid] = 0.f;
+  if (tid < 16) s_key[tid] = 0ull;
+  gemv_prologue(p, L, s_tok, s_inv, s_part);
+  // embedding segments of this chunk: built from the table straight into the buffer
+  bool table = false;
+  for (int sl = s0; sl < s1; ++sl) {
+    int f0;
+    const XSeg& sg = p.seg[gemv_seg_of(p, sl, &f0)];
+    if (sg.xf) continue;
+    table = true;
+    for (int idx = tid; idx < NT * GV_SLAB * kWarp; idx += GV_CTHREADS) {
+      const int nt = idx / (GV_SLAB * kWarp), kt = (idx / kWarp) % GV_SLAB, ln = idx % kWarp;
+      reinterpret_cast<uint4*>(act)[((nt * CHS + (sl - s0)) * GV_SLAB + kt) * kWarp + ln] =
+          xseg_table_b(sg, (sl - f0) * GV_SLAB + kt, nt, ln, L, s_tok);
+    }
   }
-  gemv_prologue(p, L, s_tok, s_inv, s_sq);
-
+  if (table) named_sync(1, GV_CTHREADS);
   bool ok = true;
-  for (int b0 = 0; b0 < nrb; b0 += GV_RBB) {
-    const int nb = min(GV_RBB, nrb - b0);
-    float tot[GV_RBB][NT][4];
+  if (!mbar_wait(act_bar, 0)) {
+    raise_error(p.err, kErrTimeout);
+    ok = false;
+  }
+  int seg_first0;
+  const int seg0 = gemv_seg_of(p, s0, &seg_first0);
+  const int seg_end0 = seg_first0 + p.seg[seg0].lenp / GV_COLS;
+  int q = 0;
+  for (int u = u0; u < u1; ++u) {
+    float tot[2][NT][4];
 #pragma unroll
-    for (int j = 0; j < GV_RBB; ++j)
+    for (int r = 0; r < 2; ++r)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) tot[j][nt][e] = 0.f;
+        for (int e = 0; e < 4; ++e) tot[r][nt][e] = 0.f;
 #pragma unroll
-    for (int j = 0; j < GV_RBB; ++j) {
-      if (j >= nb) break;
+    for (int r = 0; r < 2; ++r) {
+      if (r >= G) break;
       float acc[NT][4];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
-      int seg = 0, seg_k0 = 0, seg_end = p.seg[0].lenp / GV_COLS;  // segment and its first / end slab
-      for (int slab = 0; slab < nslab; ++slab) {
-        const int q = (b0 + j) * nslab + slab, s = q % GV_NSTAGE;
-        if (ok && !mbar_wait(full + s, (q / GV_NSTAGE) & 1)) {
+      int seg = seg0, seg_end = seg_end0;
+      for (int si = 0; si < ns; ++si, ++q) {
+        const int st = q % GV_NSTAGE;
+        if (ok && !mbar_wait(full + st, (q / GV_NSTAGE) & 1)) {
           raise_error(p.err, kErrTimeout);
           ok = false;
         }
         if (ok) {
-          const uint4* A = reinterpret_cast<const uint4*>(ring + s * GV_STAGE_BYTES);
-          const XSeg& sg = p.seg[seg];
+          const uint4* A = reinterpret_cast<const uint4*>(ring + st * GV_STAGE_BYTES);
 #pragma unroll
           for (int i = 0; i < GV_TPW; ++i) {
             const int kl = warp + i * GV_CWARPS;
             const uint4 a = A[kl * kWarp + lane];
-            const int kt_in_seg = slab * GV_SLAB + kl - seg_k0;
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-              const uint4 b = xseg_b(sg, kt_in_seg, nt, lane, L, s_tok);
+              const uint4 b = act4[((nt * CHS + si) * GV_SLAB + kl) * kWarp + lane];
               mma_bf16_16816(acc[nt], a, b.x, b.y);
               mma_bf16_16816(acc[nt], a, b.z, b.w);
             }
           }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(empty + s);
-        if (slab + 1 == seg_end) {  // fold the segment with its 1/rms per activation row
+        if (lane == 0) mbar_arrive(empty + st);
+        const int gs = s0 + si;
+        if (gs + 1 == seg_end || si + 1 == ns) {  // fold with the segment's 1/rms per activation row
 #pragma unroll
           for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const int l = nt * 8 + 2 * (lane & 3) + (e & 1);
-              tot[j][nt][e] += acc[nt][e] * s_inv[seg * 16 + l];
+              tot[r][nt][e] += acc[nt][e] * s_inv[seg * 16 + l];
               acc[nt][e] = 0.f;
             }
-          seg_k0 = seg_end * GV_SLAB;
-          ++seg;
-          if (seg < p.nseg) seg_end += p.seg[seg].lenp / GV_COLS;
+          if (gs + 1 == seg_end && seg + 1 < p.nseg) {
+            ++seg;
+            seg_end += p.seg[seg].lenp / GV_COLS;
+          }
         }
       }
     }
-    // ---- cross-warp reduction and epilogue
+    // ---- cross-warp reduction of the unit
 #pragma unroll
-    for (int j = 0; j < GV_RBB; ++j)
+    for (int r = 0; r < 2; ++r)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
-        *reinterpret_cast<float4*>(&red[(((j * NT + nt) * GV_CWARPS + warp) * kWarp + lane) * 4]) =
-            make_float4(tot[j][nt][0], tot[j][nt][1], tot[j][nt][2], tot[j][nt][3]);
+        if (r < G)
+          *reinterpret_cast<float4*>(&red[(((r * NT + nt) * GV_CWARPS + warp) * kWarp + lane) * 4]) =
+              make_float4(tot[r][nt][0], tot[r][nt][1], tot[r][nt][2], tot[r][nt][3]);
     named_sync(1, GV_CTHREADS);
-    const int rb0 = rb_first + b0;
-    const bool swiglu = p.epi == EPI_SWIGLU;
-    const int jcount = swiglu ? nb / 2 : nb;
-    for (int idx = tid; idx < jcount * NT * kWarp * 4; idx += GV_CTHREADS) {
-      const int e = idx % 4, ln = (idx / 4) % kWarp, nt = (idx / (4 * kWarp)) % NT, jj = idx / (4 * kWarp * NT);
-      const int g = ln / 4, t = ln % 4;
-      const int l = nt * 8 + 2 * t + (e & 1);
-      const int r16 = g + ((e & 2) ? 8 : 0);
-      float v = 0.f;
-      int n;
-      if (swiglu) {
-        float gs = 0.f, us = 0.f;
+    if (tid < NT * kWarp * 4) {
+      const int e = tid % 4, ln = (tid / 4) % kWarp, nt = tid / (4 * kWarp);
+      const int l = nt * 8 + 2 * (ln % 4) + (e & 1), r16 = ln / 4 + ((e & 2) ? 8 : 0);
+      float v[2] = {0.f, 0.f};
 #pragma unroll
-        for (int w = 0; w < GV_CWARPS; ++w) {
-          gs += red[((((2 * jj) * NT + nt) * GV_CWARPS + w) * kWarp + ln) * 4 + e];
-          us += red[((((2 * jj + 1) * NT + nt) * GV_CWARPS + w) * kWarp + ln) * 4 + e];
-        }
-        n = ((rb0 / 2) + jj) * 16 + r16;
-        v = gs / (1.f + expf(-gs)) * us;
+      for (int r = 0; r < 2; ++r)
+        if (r < G)
+#pragma unroll
+          for (int w = 0; w < GV_CWARPS; ++w) v[r] += red[(((r * NT + nt) * GV_CWARPS + w) * kWarp + ln) * 4 + e];
+      if (p.nkc > 1) {  // this chunk's share, reduced below by the last block of the range
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+          if (r < G) p.partial[((size_t(kc) * (p.Np >> 4) + size_t(u) * G + r) * 16 + r16) * 16 + l] = v[r];
       } else {
-#pragma unroll
-        for (int w = 0; w < GV_CWARPS; ++w) v += red[(((jj * NT + nt) * GV_CWARPS + w) * kWarp + ln) * 4 + e];
-        n = (rb0 + jj) * 16 + r16;
+        float sq = 0.f;
+        if (l < L && u * 16 + r16 < p.N)
+          sq = gemv_epilogue(p, u * 16 + r16, l, v[0], v[1], s_key);
+        s_sq[r16 * 16 + l] = sq;
       }
-      float sq = 0.f;
-      if (l < L && n < p.N) {
-        if (p.epi == EPI_ARGMAX) {
-          if (p.y) p.y[size_t(l) * p.ldy + n] = v;
-          atomicMax(&s_key[l], argmax_key(v, uint32_t(n)));
-        } else {
-          if (p.epi == EPI_ADD) v += p.base[size_t(l) * p.ldb + n];
-          if (p.y) p.y[size_t(l) * p.ldy + n] = v;
-          if (p.y2) p.y2[size_t(l) * p.ldy2 + n] = v;
-          for (int o = 0; o < p.nout; ++o)
-            xf_store(p.out[o].xf, p.out_width, l, n, p.out[o].w ? v * p.out[o].w[n] : v);
-          sq = v * v;
-        }
-      }
-      if (p.ss_out) s_sq[(jj * 16 + r16) * 16 + l] = sq;  // every (feature, row) slot written once
     }
     named_sync(1, GV_CTHREADS);
-    if (p.ss_out && tid < L) {  // fixed-order per-row sum over this batch's features
+    if (p.nkc == 1 && p.ss_out && tid < 16) {  // fixed-order sum over the unit's 16 features
       float a = 0.f;
-      for (int f = 0; f < jcount * 16; ++f) a += s_sq[f * 16 + tid];
-      s_ss[tid] += a;
+      if (tid < L)
+        for (int f = 0; f < 16; ++f) a += s_sq[f * 16 + tid];
+      p.ss_out[size_t(u) * 16 + tid] = a;
     }
   }
-  if (p.epi == EPI_ARGMAX && tid < L && s_key[tid] != 0ull) atomicMax(&p.keys[tid], s_key[tid]);
-  if (p.ss_out && tid < 16) p.ss_out[blockIdx.x * 16 + tid] = tid < L ? s_ss[tid] : 0.f;
-  if (p.side_src && int(blockIdx.x) < p.side_blocks) {
+  if (p.nkc > 1) {
+    // ---- split K: the last block of this unit range adds the chunks in order
+    __threadfence();
     named_sync(1, GV_CTHREADS);
-    gemv_side_job(p, L, s_inv, s_sq, GV_CTHREADS, true);
+    if (tid == 0) s_flag[0] = atomicAdd(&p.counters[gi], 1) == p.nkc - 1;
+    named_sync(1, GV_CTHREADS);
+    if (s_flag[0]) {
+      __threadfence();
+      // up to 8 units at a time: every partial load of the group in flight together
+      constexpr int FU = 8;
+      float* s_sq8 = red;  // [FU][16 features][16 rows]
+      for (int ub = u0; ub < u1; ub += FU) {
+        const int nu = min(FU, u1 - ub), per = 16 * L, items = nu * per;
+        float v0[FU], v1[FU];
+#pragma unroll
+        for (int i = 0; i < FU; ++i) v0[i] = v1[i] = 0.f;
+        for (int c = 0; c < p.nkc; ++c) {
+#pragma unroll
+          for (int i = 0; i < FU; ++i) {
+            const int it = tid + i * GV_CTHREADS;
+            if (it < items) {
+              const int uu = it / per, r16 = (it % per) / L, l = it % L;
+              const float* src = &p.partial[((size_t(c) * (p.Np >> 4) + size_t(ub + uu) * G) * 16 + r16) * 16 + l];
+              v0[i] += __ldcg(src);
+              if (G == 2) v1[i] += __ldcg(src + 256);
+            }
+          }
+        }
+#pragma unroll
+        for (int i = 0; i < FU; ++i) {
+          const int it = tid + i * GV_CTHREADS;
+          if (it < items) {
+            const int uu = it / per, r16 = (it % per) / L, l = it % L;
+            const int n = (ub + uu) * 16 + r16;
+            s_sq8[(uu * 16 + r16) * 16 + l] = n < p.N ? gemv_epilogue(p, n, l, v0[i], v1[i], s_key) : 0.f;
+          }
+        }
+        named_sync(1, GV_CTHREADS);
+        if (p.ss_out && tid < nu * 16) {  // fixed-order sum over each unit's 16 features
+          const int uu = tid / 16, l = tid % 16;
+          float a = 0.f;
+          if (l < L)
+            for (int f = 0; f < 16; ++f) a += s_sq8[(uu * 16 + f) * 16 + l];
+          p.ss_out[size_t(ub + uu) * 16 + l] = a;
+        }
+        named_sync(1, GV_CTHREADS);
+      }
+      if (tid == 0) p.counters[gi] = 0;  // ready for the next launch
+    }
   }
+  named_sync(1, GV_CTHREADS);
+  if (p.epi == EPI_ARGMAX && tid < L && s_key[tid] != 0ull) atomicMax(&p.keys[tid], s_key[tid]);
+  if (p.side_src && int(blockIdx.x) < p.side_blocks) gemv_side_job(p, L, s_inv, s_part, GV_CTHREADS, true);
 }
 
 template <int NT>
 constexpr size_t gemv_bf16_smem() {
-  return size_t(GV_NSTAGE) * GV_STAGE_BYTES + 2 * GV_NSTAGE * 8 + size_t(GV_RBB) * NT * GV_CWARPS * kWarp * 4 * 4 +
-         GEMV_MAXSEG * 16 * 4 + GV_RBB * 16 * 16 * 4 + 16 * 4 + 16 * 4 + 16 * 8 + 128;
+  return size_t(GV_NSTAGE) * GV_STAGE_BYTES + GV_ACT_BYTES + (2 * GV_NSTAGE + 2) * 8 +
+         size_t(2) * NT * GV_CWARPS * kWarp * 4 * 4 + GEMV_MAXSEG * 16 * 4 + 256 * 4 + 256 * 4 + 16 * 4 + 4 * 4 +
+         16 * 8 + sizeof(GemvParams) + 128;
 }
 
 // ----------------------------------------------------------------------------- fp32 models
 // Inputs are staged in shared memory with their 1/rms applied, then one warp per output
 // feature (or gate/up pair) runs CUDA-core FMA over the fp32 row; same epilogues.
-__global__ void __launch_bounds__(GV_F32_THREADS) gemv_f32_kernel(const GemvParams p) {
+__global__ void __launch_bounds__(GV_F32_THREADS) gemv_f32_kernel(__grid_constant__ const GemvParams p) {
   extern __shared__ __align__(16) unsigned char gf_smem[];
   float* xs = reinterpret_cast<float*>(gf_smem);  // [L_max][Kp]
   float* s_inv = xs + size_t(p.L_max) * p.Kp;   // [3][16]

@@ -56,7 +56,7 @@ struct PackParams {
   int* err;
 };
 
-__global__ void pack_rows_kernel(const PackParams p) {
+__global__ void pack_rows_kernel(__grid_constant__ const PackParams p) {
   pdl_launch_dependents();
   pdl_wait();
   const int l = blockIdx.x;
@@ -555,7 +555,7 @@ struct FinishParams {
   int advance_dc;
 };
 
-__global__ void finish_update_kernel(const FinishParams p) {
+__global__ void finish_update_kernel(__grid_constant__ const FinishParams p) {
   pdl_launch_dependents();
   pdl_wait();
   __shared__ float red[32];

@@ -24,6 +24,7 @@
 
 #include "../../include/woodcock_b200.h"
 #include "attention.cuh"
+#include "attention_dec.cuh"
 #include "attention_mma.cuh"
 #include "common.cuh"
 #include "gemv.cuh"
@@ -103,8 +104,14 @@ struct wc_ctx {
   size_t max_smem = 0;
   Profiler* prof = nullptr;  // set while a profiled round is being captured
   bool pdl = true;           // programmatic dependent launch between round kernels
-  bool attn_mma = true;      // tensor-core attention for bf16 caches
-  int gemv_blocks_per_sm = 2;
+  int attn_mode = 2;         // bf16 caches: 2 decode kernel, 1 split-KV mma kernel, 0 CUDA cores
+  int gemv_blocks_per_sm = 1;
+  bool gemv_prefetch = true;             // L2 prefetch of the next GEMV's weights
+  size_t gemv_prefetch_cap = 64u << 20;  // bytes prefetched at most
+  float* gv_partial = nullptr;           // split-K partial sums
+  size_t gv_partial_n = 0;               // floats
+  int* gv_counters = nullptr;            // split-K arrival counters (zero between launches)
+  int gv_counters_n = 0;
   uint32_t* lin_xf = nullptr;  // input fragments of the ops-API linear
   int lin_xf_k = 0;
   bool lin_xf_bf16 = false;
@@ -428,7 +435,7 @@ struct XIn {
   int nparts = 0;
 };
 
-int max_parts(const wc_ctx* ctx) { return ctx->num_sms * 4; }
+int max_parts(const wc_ctx*) { return 4096; }
 
 uint32_t* xf_alloc(bool bf16, int K) {
   const size_t bytes = size_t(GEMV_MAXL) * xf_width(bf16, K) * 4;
@@ -474,18 +481,47 @@ XSeg xs_embed(const void* table, int len, bool bf16, const float* norm_w, const 
   return s;
 }
 
-// Blocks of a GEMV launch over W with up to L_max rows: the part count of its ss_out.
-int gemv_grid(const wc_ctx* ctx, const Lin& W, int L_max) {
-  if (W.dtype == WC_BF16) {
-    const int NT = L_max <= 8 ? 1 : 2;
-    const int nunits = W.Np / (16 * W.group);
-    return std::max(1, std::min(nunits, ctx->num_sms * std::min(ctx->gemv_blocks_per_sm, ctx->occ_gemv[NT])));
+// Work split of a bf16 GEMV launch: K-chunks that fit the activation buffer, and blocks
+// per chunk so that one block runs per SM.
+struct GemvPlan {
+  int grid = 1, nkc = 1, kc_slabs = 1, gpk = 1;
+};
+
+GemvPlan gemv_plan(const wc_ctx* ctx, const Lin& W, int L_max) {
+  GemvPlan g;
+  if (W.dtype != WC_BF16) {
+    g.grid = std::max(1, std::min((W.N + GV_F32_WARPS - 1) / GV_F32_WARPS, ctx->num_sms * 2));
+    return g;
   }
-  return std::max(1, std::min((W.N + GV_F32_WARPS - 1) / GV_F32_WARPS, ctx->num_sms * 2));
+  const int NT = L_max <= 8 ? 1 : 2;
+  const int chs = gv_chunk_slabs(NT);
+  const int nslab = W.Kp / GV_COLS;
+  const int nunits = W.Np / (16 * W.group);
+  g.nkc = (nslab + chs - 1) / chs;
+  g.kc_slabs = (nslab + g.nkc - 1) / g.nkc;
+  const int target = ctx->num_sms * std::min(ctx->gemv_blocks_per_sm, ctx->occ_gemv[NT]);
+  g.gpk = std::max(1, std::min(nunits, target / g.nkc));
+  g.grid = g.nkc * g.gpk;
+  return g;
+}
+
+// Blocks of a GEMV launch (the part count of an fp32 GEMV's ss_out and of side jobs).
+int gemv_grid(const wc_ctx* ctx, const Lin& W, int L_max) { return gemv_plan(ctx, W, L_max).grid; }
+
+// Part count of a GEMV's ss_out: one per epilogue unit (bf16) or per block (fp32).
+int gemv_parts(const wc_ctx* ctx, const Lin& W, int L_max) {
+  return W.dtype == WC_BF16 ? W.Np / (16 * W.group) : gemv_grid(ctx, W, L_max);
 }
 
 // Part count of a head's side-job sums of squares.
 int side_parts(const wc_ctx* ctx, const Lin& W, int L_max) { return std::min(GV_SIDE_BLOCKS, gemv_grid(ctx, W, L_max)); }
+
+// Bytes of `next` to prefetch into L2 while the current GEMV ends (0 = off).
+void gemv_prefetch(const wc_ctx* ctx, GemvParams& p, const Lin* next) {
+  if (!next || !ctx->gemv_prefetch || next->dtype != WC_BF16) return;
+  p.pf = next->w;
+  p.pf_bytes = std::min(next->bytes, ctx->gemv_prefetch_cap);
+}
 
 void launch_gemv(wc_ctx* ctx, const Lin& W, GemvParams p) {
   const bool bf16 = W.dtype == WC_BF16;
@@ -508,21 +544,32 @@ void launch_gemv(wc_ctx* ctx, const Lin& W, GemvParams p) {
   if (p.L_max < 1 || p.L_max > GEMV_MAXL) fail(WC_ERR_INVALID, "GEMV rows outside 1..16");
   if (p.nout > 2 || (p.nout > 0 && p.epi == EPI_ARGMAX)) fail(WC_ERR_INVALID, "bad GEMV outputs");
   p.out_width = xf_width(bf16, W.N);
-  const int grid = gemv_grid(ctx, W, p.L_max);
-  if (grid > max_parts(ctx)) fail(WC_ERR_INVALID, "GEMV grid above the statistics buffers");
+  const GemvPlan g = gemv_plan(ctx, W, p.L_max);
+  if (p.ss_out && gemv_parts(ctx, W, p.L_max) > max_parts(ctx))
+    fail(WC_ERR_INVALID, "GEMV output statistics above the buffer size");
   if (p.side_src) {
     p.side_width = xf_width(bf16, p.side_len);
-    p.side_blocks = std::min(GV_SIDE_BLOCKS, grid);
+    p.side_blocks = std::min(GV_SIDE_BLOCKS, g.grid);
   }
   if (bf16) {
+    p.nkc = g.nkc;
+    p.kc_slabs = g.kc_slabs;
+    p.gpk = g.gpk;
+    if (g.kc_slabs > gv_chunk_slabs(p.L_max <= 8 ? 1 : 2)) fail(WC_ERR_INVALID, "GEMV chunk above the buffer");
+    if (g.nkc > 1) {
+      if (size_t(g.nkc) * (W.Np / 16) * 256 > ctx->gv_partial_n || g.gpk > ctx->gv_counters_n)
+        fail(WC_ERR_UNSUPPORTED, "GEMV split-K scratch too small for this projection");
+      p.partial = ctx->gv_partial;
+      p.counters = ctx->gv_counters;
+    }
     if (p.L_max <= 8)
-      launch_ex(ctx, "gemv", gemv_bf16_kernel<1>, dim3(grid), dim3(GV_THREADS), gemv_bf16_smem<1>(), true, 1, p);
+      launch_ex(ctx, "gemv", gemv_bf16_kernel<1>, dim3(g.grid), dim3(GV_THREADS), gemv_bf16_smem<1>(), true, 1, p);
     else
-      launch_ex(ctx, "gemv", gemv_bf16_kernel<2>, dim3(grid), dim3(GV_THREADS), gemv_bf16_smem<2>(), true, 1, p);
+      launch_ex(ctx, "gemv", gemv_bf16_kernel<2>, dim3(g.grid), dim3(GV_THREADS), gemv_bf16_smem<2>(), true, 1, p);
   } else {
     const size_t smem = gemv_f32_smem(p.L_max, W.Kp);
     if (smem > ctx->max_smem) fail(WC_ERR_UNSUPPORTED, "fp32 projection too wide for shared memory");
-    launch_ex(ctx, "gemv", gemv_f32_kernel, dim3(grid), dim3(GV_F32_THREADS), smem, true, 1, p);
+    launch_ex(ctx, "gemv", gemv_f32_kernel, dim3(g.grid), dim3(GV_F32_THREADS), smem, true, 1, p);
   }
 }
 
@@ -554,10 +601,29 @@ void launch_attention(wc_ctx* ctx, AttnParams p) {
       (!p.q_ready && p.ld_qkv % 4))
     fail(WC_ERR_INVALID, "attention inputs must be 16-byte aligned with 16-byte row strides");
   if (p.xf_out) p.xf_width = xf_width(!p.xf_fp32, p.H * p.D);
-  // tensor-core path: bf16 cache, rule-based visibility, new rows appended by the kernel
-  const bool mma_ok = !p.q_ready && !p.mask_full && p.kv_dtype == WC_BF16 && p.write_cache && ctx->attn_mma &&
-                      (p.D == 128 || p.D == 64) && p.L_max * rep <= AM_MAXR && p.stride_p == p.D;
-  if (mma_ok) {
+  // tensor-core paths: bf16 cache, rule-based visibility, new rows appended by the kernel
+  const bool tc_ok = !p.q_ready && !p.mask_full && p.kv_dtype == WC_BF16 && p.write_cache &&
+                     (p.D == 128 || p.D == 64) && p.L_max * rep <= AM_MAXR && p.stride_p == p.D;
+  if (tc_ok && ctx->attn_mode == 2 && p.L_max <= AD_MAXL && p.L_max * rep <= AD_MAXR) {
+    const bool mt2 = p.L_max * rep > 16;
+    if (p.D == 128) {
+      if (mt2)
+        launch_ex(ctx, "attention_dec", attention_dec_kernel<128, 2>, dim3(AD_CLUSTER, p.Hk, 1), dim3(AD_THREADS),
+                  attention_dec_smem<128>(), true, AD_CLUSTER, p);
+      else
+        launch_ex(ctx, "attention_dec", attention_dec_kernel<128, 1>, dim3(AD_CLUSTER, p.Hk, 1), dim3(AD_THREADS),
+                  attention_dec_smem<128>(), true, AD_CLUSTER, p);
+    } else {
+      if (mt2)
+        launch_ex(ctx, "attention_dec", attention_dec_kernel<64, 2>, dim3(AD_CLUSTER, p.Hk, 1), dim3(AD_THREADS),
+                  attention_dec_smem<64>(), true, AD_CLUSTER, p);
+      else
+        launch_ex(ctx, "attention_dec", attention_dec_kernel<64, 1>, dim3(AD_CLUSTER, p.Hk, 1), dim3(AD_THREADS),
+                  attention_dec_smem<64>(), true, AD_CLUSTER, p);
+    }
+    return;
+  }
+  if (tc_ok && ctx->attn_mode >= 1) {
     if (p.D == 128)
       launch_ex(ctx, "attention_mma", attention_mma_kernel<128>, dim3(AM_CLUSTER, p.Hk, 1), dim3(AM_THREADS),
                 attention_mma_smem<128>(p.L_max), true, AM_CLUSTER, p);
@@ -599,9 +665,15 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
     }
     if (const char* e = std::getenv("WC_PDL")) ctx->pdl = std::atoi(e) != 0;
     if (const char* e = std::getenv("WC_GEMV_BLOCKS_PER_SM")) ctx->gemv_blocks_per_sm = std::max(1, std::atoi(e));
-    if (const char* e = std::getenv("WC_ATTN_MMA")) ctx->attn_mma = std::atoi(e) != 0;
+    if (const char* e = std::getenv("WC_ATTN")) ctx->attn_mode = std::atoi(e);
+    if (const char* e = std::getenv("WC_GEMV_PREFETCH")) ctx->gemv_prefetch = std::atoi(e) != 0;
     ctx->d_err = static_cast<int*>(dalloc(sizeof(int)));
     CUDA_TRY(cudaMemset(ctx->d_err, 0, sizeof(int)));
+    ctx->gv_partial_n = size_t(8) << 20;  // 32 MB of split-K partials
+    ctx->gv_partial = static_cast<float*>(dalloc(sizeof(float) * ctx->gv_partial_n));
+    ctx->gv_counters_n = 8192;
+    ctx->gv_counters = static_cast<int*>(dalloc(sizeof(int) * ctx->gv_counters_n));
+    CUDA_TRY(cudaMemset(ctx->gv_counters, 0, sizeof(int) * ctx->gv_counters_n));
     const int smax = int(ctx->max_smem);
     CUDA_TRY(cudaFuncSetAttribute(gemv_bf16_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(gemv_bf16_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
@@ -609,6 +681,10 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
     CUDA_TRY(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(attention_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(attention_mma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
+    CUDA_TRY(cudaFuncSetAttribute(attention_dec_kernel<128, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
+    CUDA_TRY(cudaFuncSetAttribute(attention_dec_kernel<128, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
+    CUDA_TRY(cudaFuncSetAttribute(attention_dec_kernel<64, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
+    CUDA_TRY(cudaFuncSetAttribute(attention_dec_kernel<64, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(kv_compact_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     int occ = 0;
     CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, gemv_bf16_kernel<1>, GV_THREADS,
@@ -645,6 +721,8 @@ extern "C" void wc_ctx_destroy(wc_ctx* ctx) {
   if (ctx->stream) cudaStreamSynchronize(ctx->stream);
   for (auto& kv : ctx->rope) dfree(kv.second.ptr);
   dfree(ctx->d_err);
+  dfree(ctx->gv_partial);
+  dfree(ctx->gv_counters);
   dfree(ctx->pw);
   dfree(ctx->qw);
   dfree(ctx->lin_xf);
@@ -662,6 +740,7 @@ extern "C" wc_status wc_ctx_synchronize(wc_ctx* ctx) {
     CUDA_TRY(cudaMemcpy(&e, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
     if (e) {
       CUDA_TRY(cudaMemset(ctx->d_err, 0, sizeof(int)));
+      CUDA_TRY(cudaMemset(ctx->gv_counters, 0, sizeof(int) * ctx->gv_counters_n));
       fail(WC_ERR_DEVICE, "device error flag " + std::to_string(e));
     }
   });
@@ -1013,6 +1092,7 @@ extern "C" wc_status wc_kv_read(const wc_kv* kv, int layer, int T, float* k, flo
 namespace {
 
 struct Rows {
+  bool stable = false;  // n_dev and the cache below it were written by completed work (round graphs)
   int L = 0;
   const int* L_dev = nullptr;
   int L_max = 0;
@@ -1293,6 +1373,7 @@ XIn target_layers(wc_target* t, wc_kv* kv, const Rows& r, XIn in0, float* h, con
       p.y = t->ws_qkv;
       p.ldy = ld_qkv;
       p.err = err;
+      gemv_prefetch(ctx, p, &Ly.o);
       prof_begin(ctx, PK_QKV);
       launch_gemv(ctx, Ly.qkv, p);
       prof_end(ctx, PK_QKV);
@@ -1328,6 +1409,7 @@ XIn target_layers(wc_target* t, wc_kv* kv, const Rows& r, XIn in0, float* h, con
       a.xf_out = t->xf_att;
       a.xf_fp32 = bf16 ? 0 : 1;
       a.write_cache = 1;
+      a.stable_prefix = r.stable ? 1 : 0;
       a.err = err;
       prof_begin(ctx, PK_ATTN);
       launch_attention(ctx, a);
@@ -1349,6 +1431,7 @@ XIn target_layers(wc_target* t, wc_kv* kv, const Rows& r, XIn in0, float* h, con
       p.out[0] = XOut{t->xf_post, Ly.post_norm};
       p.ss_out = Ly.ss_o;
       p.err = err;
+      gemv_prefetch(ctx, p, &Ly.gu);
       prof_begin(ctx, PK_O);
       launch_gemv(ctx, Ly.o, p);
       prof_end(ctx, PK_O);
@@ -1359,11 +1442,12 @@ XIn target_layers(wc_target* t, wc_kv* kv, const Rows& r, XIn in0, float* h, con
       p.L_dev = r.L_dev;
       p.L_max = r.L_max;
       p.nseg = 1;
-      p.seg[0] = xs_frag(XIn{t->xf_post, Ly.ss_o, gemv_grid(ctx, Ly.o, r.L_max)}, H, bf16, c.eps);
+      p.seg[0] = xs_frag(XIn{t->xf_post, Ly.ss_o, gemv_parts(ctx, Ly.o, r.L_max)}, H, bf16, c.eps);
       p.epi = EPI_SWIGLU;
       p.nout = 1;
       p.out[0] = XOut{t->xf_act, nullptr};
       p.err = err;
+      gemv_prefetch(ctx, p, &Ly.down);
       prof_begin(ctx, PK_GU);
       launch_gemv(ctx, Ly.gu, p);
       prof_end(ctx, PK_GU);
@@ -1392,11 +1476,12 @@ XIn target_layers(wc_target* t, wc_kv* kv, const Rows& r, XIn in0, float* h, con
           if (taps->xf[f]) p.out[p.nout++] = XOut{taps->xf[f], taps->w[f]};
         }
       p.err = err;
+      gemv_prefetch(ctx, p, li + 1 < c.layers ? &t->layers[li + 1].qkv : &t->head);
       prof_begin(ctx, PK_DOWN);
       launch_gemv(ctx, Ly.down, p);
       prof_end(ctx, PK_DOWN);
     }
-    x = XIn{t->xf_in, Ly.ss_d, gemv_grid(ctx, Ly.down, r.L_max)};
+    x = XIn{t->xf_in, Ly.ss_d, gemv_parts(ctx, Ly.down, r.L_max)};
   }
   return x;
 }
@@ -1404,7 +1489,7 @@ XIn target_layers(wc_target* t, wc_kv* kv, const Rows& r, XIn in0, float* h, con
 // Sums of squares of a tap layer's output, as the fuse reads them.
 XIn target_tap_stats(const wc_target* t, int f, const uint32_t* xf, int L_max) {
   const TLayer& Ly = t->layers[t->taps[f]];
-  return XIn{xf, Ly.ss_d, gemv_grid(t->ctx, Ly.down, L_max)};
+  return XIn{xf, Ly.ss_d, gemv_parts(t->ctx, Ly.down, L_max)};
 }
 
 // Head over `rows` rows given as fragments (times the final norm): argmax keys and,
@@ -1773,6 +1858,7 @@ XIn drafter_layers(wc_drafter* d, wc_kv* kv, const Rows& r, XIn feat_in, const f
       p.y = d->ws_qkv;
       p.ldy = ld_qkv;
       p.err = err;
+      gemv_prefetch(ctx, p, &Ly.o);
       launch_gemv(ctx, Ly.qkv, p);
     }
     {
@@ -1807,6 +1893,7 @@ XIn drafter_layers(wc_drafter* d, wc_kv* kv, const Rows& r, XIn feat_in, const f
       a.xf_out = d->xf_att;
       a.xf_fp32 = bf16 ? 0 : 1;
       a.write_cache = 1;
+      a.stable_prefix = r.stable ? 1 : 0;
       a.err = err;
       launch_attention(ctx, a);
     }
@@ -1826,6 +1913,7 @@ XIn drafter_layers(wc_drafter* d, wc_kv* kv, const Rows& r, XIn feat_in, const f
       p.out[0] = XOut{d->xf_post, Ly.post_norm};
       p.ss_out = Ly.ss_o;
       p.err = err;
+      gemv_prefetch(ctx, p, &Ly.gu);
       launch_gemv(ctx, Ly.o, p);
     }
     {
@@ -1834,11 +1922,12 @@ XIn drafter_layers(wc_drafter* d, wc_kv* kv, const Rows& r, XIn feat_in, const f
       p.L_dev = r.L_dev;
       p.L_max = r.L_max;
       p.nseg = 1;
-      p.seg[0] = xs_frag(XIn{d->xf_post, Ly.ss_o, gemv_grid(ctx, Ly.o, r.L_max)}, H, bf16, c.eps);
+      p.seg[0] = xs_frag(XIn{d->xf_post, Ly.ss_o, gemv_parts(ctx, Ly.o, r.L_max)}, H, bf16, c.eps);
       p.epi = EPI_SWIGLU;
       p.nout = 1;
       p.out[0] = XOut{d->xf_act, nullptr};
       p.err = err;
+      gemv_prefetch(ctx, p, &Ly.down);
       launch_gemv(ctx, Ly.gu, p);
     }
     {
@@ -1859,9 +1948,10 @@ XIn drafter_layers(wc_drafter* d, wc_kv* kv, const Rows& r, XIn feat_in, const f
       if (last && extra) p.out[p.nout++] = *extra;
       p.ss_out = Ly.ss_d;
       p.err = err;
+      gemv_prefetch(ctx, p, last ? &d->head : &d->layers[li + 1].qkv);
       launch_gemv(ctx, Ly.down, p);
     }
-    x = XIn{d->xf_out, Ly.ss_d, gemv_grid(ctx, Ly.down, r.L_max)};
+    x = XIn{d->xf_out, Ly.ss_d, gemv_parts(ctx, Ly.down, r.L_max)};
   }
   return x;
 }
@@ -1890,8 +1980,9 @@ XIn drafter_fuse_impl(wc_drafter* d, const XIn* taps, int L, const int* L_dev, i
   p.out[0] = XOut{d->xf_feat, d->layers[0].in_norm};
   p.ss_out = d->ss_g;
   p.err = err;
+  gemv_prefetch(d->ctx, p, &d->layers[0].qkv);
   launch_gemv(d->ctx, d->fc, p);
-  return XIn{d->xf_feat, d->ss_g, gemv_grid(d->ctx, d->fc, L_max)};
+  return XIn{d->xf_feat, d->ss_g, gemv_parts(d->ctx, d->fc, L_max)};
 }
 
 // Tap rows [L][Ht] (fp32, row stride ld, tap f at + f * stride) -> tap fragments times
@@ -1951,6 +2042,7 @@ void drafter_head(wc_drafter* d, XIn x, int rows, unsigned long long* keys, floa
     p.side_ss = d->ss_feat;
   }
   p.err = err;
+  gemv_prefetch(d->ctx, p, &d->layers[0].qkv);
   prof_begin(d->ctx, PK_DRAFT_HEAD);
   launch_gemv(d->ctx, d->head, p);
   prof_end(d->ctx, PK_DRAFT_HEAD);
@@ -2267,10 +2359,11 @@ void build_round(wc_decoder* dec, int K) {
       fin = XIn{d->xf_feat, d->ss_feat, side_parts(ctx, d->head, 1)};
       feat = d->ws_feat;
     } else {
-      fin = XIn{d->xf_feat, d->layers.back().ss_d, gemv_grid(ctx, ld, 1)};
+      fin = XIn{d->xf_feat, d->layers.back().ss_d, gemv_parts(ctx, ld, 1)};
       feat = d->ws_h;
     }
     Rows r;
+    r.stable = true;
     r.L = 1;
     r.L_max = 1;
     r.n_dev = &st->dc_len;
@@ -2288,6 +2381,7 @@ void build_round(wc_decoder* dec, int K) {
   }
   // ---- verification of [x_n, d_1..d_K] (spec.py:353-355)
   Rows rv;
+  rv.stable = true;
   rv.L = K + 1;
   rv.L_max = K + 1;
   rv.n_dev = &st->n;
@@ -2307,6 +2401,7 @@ void build_round(wc_decoder* dec, int K) {
   for (int f = 0; f < 3; ++f) tx[f] = target_tap_stats(t, f, d->xf_tap[f], K + 1);
   const XIn gin = drafter_fuse_impl(d, tx, K + 1, &st->L_upd, K + 1, d->ws_g, err);
   Rows ru;
+  ru.stable = true;
   ru.L = K + 1;
   ru.L_dev = &st->L_upd;
   ru.L_max = K + 1;
@@ -2362,6 +2457,7 @@ void check_state_error(wc_decoder* dec) {
   if (e || ce) {
     CUDA_TRY(cudaMemset(&dec->st->err, 0, sizeof(int)));
     CUDA_TRY(cudaMemset(dec->ctx->d_err, 0, sizeof(int)));
+    CUDA_TRY(cudaMemset(dec->ctx->gv_counters, 0, sizeof(int) * dec->ctx->gv_counters_n));
     fail(WC_ERR_DEVICE, "device error flag " + std::to_string(e | ce));
   }
 }
@@ -2704,6 +2800,7 @@ extern "C" wc_status wc_generate_autoregressive(wc_target* t, const int* prompt,
         ctx->capture_launches = 0;
         try {
           Rows r;
+          r.stable = true;
           r.L = 1;
           r.L_max = 1;
           r.n_dev = &st->n;
@@ -2730,7 +2827,10 @@ extern "C" wc_status wc_generate_autoregressive(wc_target* t, const int* prompt,
       CUDA_TRY(cudaMemcpyAsync(hout, d_out, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
       CUDA_TRY(cudaMemcpyAsync(hout + 1, &st->err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
       CUDA_TRY(cudaStreamSynchronize(ctx->stream));
-      if (hout[1]) fail(WC_ERR_DEVICE, "device error flag " + std::to_string(hout[1]));
+      if (hout[1]) {
+        CUDA_TRY(cudaMemset(ctx->gv_counters, 0, sizeof(int) * ctx->gv_counters_n));
+        fail(WC_ERR_DEVICE, "device error flag " + std::to_string(hout[1]));
+      }
       x = hout[0];
       out_tokens[m++] = x;
     }
