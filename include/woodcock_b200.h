@@ -239,7 +239,8 @@ WC_API wc_status wc_generate_autoregressive(wc_target* t, const int* prompt, int
 /* A real round (as wc_decoder_round) replayed from a second graph that records CUDA events
  * around kernels: ms_sum[i] / counts[i] is the mean device time of kernel class i, for
  * i = 0 target QKV GEMV, 1 attention, 2 o-proj, 3 gate/up, 4 down-proj, 5 target head,
- * 6 drafter head, 7 drafter layer pass (whole). Arrays of 8. */
+ * 6 drafter head, 7 drafter layer pass (whole), 8 target layer stack (the persistent kernel
+ * that replaces classes 0-4 in the verify pass when it is used). Arrays of 16. */
 WC_API wc_status wc_decoder_profile_round(wc_decoder* dec, int k, int* out_tokens, int* out_n, float* ms_sum,
                                           int* counts);
 /* device-side state after the last round: committed length n (target cache size) and drafter cache size */

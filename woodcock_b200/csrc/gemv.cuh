@@ -45,7 +45,7 @@ constexpr int GV_THREADS = GV_CTHREADS + kWarp;     // + one producer warp
 constexpr int GV_SLAB = 32;                         // k-tiles per ring stage: 512 columns
 constexpr int GV_COLS = GV_SLAB * 16;
 constexpr int GV_STAGE_BYTES = GV_SLAB * 512;       // 16 KB
-constexpr int GV_NSTAGE = 4;
+constexpr int GV_NSTAGE = 8;
 constexpr int GV_ACT_BYTES = 64 * 1024;             // activation chunk buffer
 constexpr int GV_TPW = GV_SLAB / GV_CWARPS;         // k-tiles per warp per slab
 constexpr int GV_F32_THREADS = 256;
@@ -114,8 +114,10 @@ struct GemvParams {
   int nkc, kc_slabs, gpk;
   float* partial;        // nkc > 1: [nkc][Np / 16][16 features][16 rows] fp32 partial sums
   int* counters;         // nkc > 1: [gpk] arrivals per unit range (left at zero)
-  const void* pf;        // L2 prefetch of the next GEMV's weights, split over the blocks
+  const void* pf;        // L2 prefetch of upcoming weights (up to two regions), split over the blocks
   size_t pf_bytes;
+  const void* pf2;
+  size_t pf2_bytes;
   // side job of a drafter head, in blocks < side_blocks:
   //   side_y = side_src * inv(seg 0) * side_w, the next chain step's feature
   const float* side_src;
@@ -352,11 +354,13 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
         issue(issued);
       }
       // the HBM stream of this block is issued: fetch our share of the next GEMV's weights
-      if (ok && p.pf && p.pf_bytes >= 16) {
-        const size_t per = ((p.pf_bytes / gridDim.x) + 15) & ~size_t(15);
-        const size_t b0 = per * blockIdx.x, b1 = min(p.pf_bytes & ~size_t(15), b0 + per);
-        for (size_t o = b0; o < b1; o += (1u << 20))
-          prefetch_l2_bulk(static_cast<const char*>(p.pf) + o, uint32_t(min(size_t(1u << 20), b1 - o)));
+      for (int rgn = 0; rgn < 2 && ok; ++rgn) {
+        const char* pfp = static_cast<const char*>(rgn ? p.pf2 : p.pf);
+        const size_t pfb = rgn ? p.pf2_bytes : p.pf_bytes;
+        if (!pfp || pfb < 16) continue;
+        const size_t per = ((pfb / gridDim.x) + 15) & ~size_t(15);
+        const size_t b0 = per * blockIdx.x, b1 = min(pfb & ~size_t(15), b0 + per);
+        for (size_t o = b0; o < b1; o += (1u << 20)) prefetch_l2_bulk(pfp + o, uint32_t(min(size_t(1u << 20), b1 - o)));
       }
       // the block's shared memory must outlive every copy issued into it, also when the
       // consumers gave up on a wait: wait (bounded) for the last copy of each slot
@@ -406,11 +410,16 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
 #pragma unroll
     for (int r = 0; r < 2; ++r) {
       if (r >= G) break;
-      float acc[NT][4];
+      // independent accumulators per k-tile and hi / lo term: the MMAs of a slab do not wait
+      // on one another (a single accumulator chains them at the MMA latency)
+      constexpr int NA = 2 * GV_TPW;
+      float acc[NT][NA][4];
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) acc[nt][e] = 0.f;
+        for (int c = 0; c < NA; ++c)
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[nt][c][e] = 0.f;
       int seg = seg0, seg_end = seg_end0;
       for (int si = 0; si < ns; ++si, ++q) {
         const int st = q % GV_NSTAGE;
@@ -427,8 +436,8 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
               const uint4 b = act4[((nt * CHS + si) * GV_SLAB + kl) * kWarp + lane];
-              mma_bf16_16816(acc[nt], a, b.x, b.y);
-              mma_bf16_16816(acc[nt], a, b.z, b.w);
+              mma_bf16_16816(acc[nt][2 * i], a, b.x, b.y);
+              mma_bf16_16816(acc[nt][2 * i + 1], a, b.z, b.w);
             }
           }
         }
@@ -441,8 +450,13 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
 #pragma unroll
             for (int e = 0; e < 4; ++e) {
               const int l = nt * 8 + 2 * (lane & 3) + (e & 1);
-              tot[r][nt][e] += acc[nt][e] * s_inv[seg * 16 + l];
-              acc[nt][e] = 0.f;
+              float a = 0.f;
+#pragma unroll
+              for (int c = 0; c < NA; ++c) {
+                a += acc[nt][c][e];
+                acc[nt][c][e] = 0.f;
+              }
+              tot[r][nt][e] += a * s_inv[seg * 16 + l];
             }
           if (gs + 1 == seg_end && seg + 1 < p.nseg) {
             ++seg;

@@ -30,6 +30,7 @@
 #include "gemv.cuh"
 #include "host_io.h"
 #include "misc.cuh"
+#include "stack.cuh"
 
 using namespace wc;
 namespace fs = std::filesystem;
@@ -66,7 +67,8 @@ struct RopeTable {
 };
 
 // CUDA-event marks around kernels of a profiled round (a separate graph from the timed one).
-enum ProfKind { PK_QKV, PK_ATTN, PK_O, PK_GU, PK_DOWN, PK_HEAD, PK_DRAFT_HEAD, PK_DRAFT_LAYER, PK_COUNT };
+enum ProfKind { PK_QKV, PK_ATTN, PK_O, PK_GU, PK_DOWN, PK_HEAD, PK_DRAFT_HEAD, PK_DRAFT_LAYER, PK_STACK, PK_COUNT };
+constexpr int PK_SLOTS = 16;  // entries of the profile arrays in the C ABI
 
 struct Profiler {
   std::vector<cudaEvent_t> pool;
@@ -112,6 +114,10 @@ struct wc_ctx {
   size_t gv_partial_n = 0;               // floats
   int* gv_counters = nullptr;            // split-K arrival counters (zero between launches)
   int gv_counters_n = 0;
+  bool stack = false;                    // persistent layer-stack kernel for the verify pass (opt-in: WC_STACK=1)
+  int occ_stack = 0;                     // its blocks per SM (0: unavailable)
+  float* sk_part = nullptr;              // its attention partial states
+  int* sk_counters = nullptr;            // its per-head arrival counters (zero between launches)
   uint32_t* lin_xf = nullptr;  // input fragments of the ops-API linear
   int lin_xf_k = 0;
   bool lin_xf_bf16 = false;
@@ -517,10 +523,16 @@ int gemv_parts(const wc_ctx* ctx, const Lin& W, int L_max) {
 int side_parts(const wc_ctx* ctx, const Lin& W, int L_max) { return std::min(GV_SIDE_BLOCKS, gemv_grid(ctx, W, L_max)); }
 
 // Bytes of `next` to prefetch into L2 while the current GEMV ends (0 = off).
-void gemv_prefetch(const wc_ctx* ctx, GemvParams& p, const Lin* next) {
-  if (!next || !ctx->gemv_prefetch || next->dtype != WC_BF16) return;
-  p.pf = next->w;
-  p.pf_bytes = std::min(next->bytes, ctx->gemv_prefetch_cap);
+void gemv_prefetch(const wc_ctx* ctx, GemvParams& p, const Lin* next, const Lin* next2 = nullptr) {
+  if (!ctx->gemv_prefetch) return;
+  if (next && next->dtype == WC_BF16) {
+    p.pf = next->w;
+    p.pf_bytes = std::min(next->bytes, ctx->gemv_prefetch_cap);
+  }
+  if (next2 && next2->dtype == WC_BF16) {
+    p.pf2 = next2->w;
+    p.pf2_bytes = std::min(next2->bytes, ctx->gemv_prefetch_cap);
+  }
 }
 
 void launch_gemv(wc_ctx* ctx, const Lin& W, GemvParams p) {
@@ -674,6 +686,18 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
     ctx->gv_counters_n = 8192;
     ctx->gv_counters = static_cast<int*>(dalloc(sizeof(int) * ctx->gv_counters_n));
     CUDA_TRY(cudaMemset(ctx->gv_counters, 0, sizeof(int) * ctx->gv_counters_n));
+    if (const char* e = std::getenv("WC_STACK")) ctx->stack = std::atoi(e) != 0;
+    ctx->sk_part = static_cast<float*>(dalloc(sizeof(float) * 16 * SK_MAXS * SK_MAXR * (SK_D + 2)));
+    ctx->sk_counters = static_cast<int*>(dalloc(sizeof(int) * 64));
+    CUDA_TRY(cudaMemset(ctx->sk_counters, 0, sizeof(int) * 64));
+    CUDA_TRY(cudaFuncSetAttribute(stack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(stack_smem())));
+    {
+      int occ_s = 0;
+      if (stack_smem() <= ctx->max_smem &&
+          cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_s, stack_kernel, SK_THREADS, stack_smem()) == cudaSuccess)
+        ctx->occ_stack = occ_s;
+      cudaGetLastError();
+    }
     const int smax = int(ctx->max_smem);
     CUDA_TRY(cudaFuncSetAttribute(gemv_bf16_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(gemv_bf16_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
@@ -723,6 +747,8 @@ extern "C" void wc_ctx_destroy(wc_ctx* ctx) {
   dfree(ctx->d_err);
   dfree(ctx->gv_partial);
   dfree(ctx->gv_counters);
+  dfree(ctx->sk_part);
+  dfree(ctx->sk_counters);
   dfree(ctx->pw);
   dfree(ctx->qw);
   dfree(ctx->lin_xf);
@@ -741,6 +767,7 @@ extern "C" wc_status wc_ctx_synchronize(wc_ctx* ctx) {
     if (e) {
       CUDA_TRY(cudaMemset(ctx->d_err, 0, sizeof(int)));
       CUDA_TRY(cudaMemset(ctx->gv_counters, 0, sizeof(int) * ctx->gv_counters_n));
+      CUDA_TRY(cudaMemset(ctx->sk_counters, 0, sizeof(int) * 64));
       fail(WC_ERR_DEVICE, "device error flag " + std::to_string(e));
     }
   });
@@ -1373,7 +1400,7 @@ XIn target_layers(wc_target* t, wc_kv* kv, const Rows& r, XIn in0, float* h, con
       p.y = t->ws_qkv;
       p.ldy = ld_qkv;
       p.err = err;
-      gemv_prefetch(ctx, p, &Ly.o);
+      gemv_prefetch(ctx, p, &Ly.o, &Ly.gu);  // both land while attention runs
       prof_begin(ctx, PK_QKV);
       launch_gemv(ctx, Ly.qkv, p);
       prof_end(ctx, PK_QKV);
@@ -1431,7 +1458,6 @@ XIn target_layers(wc_target* t, wc_kv* kv, const Rows& r, XIn in0, float* h, con
       p.out[0] = XOut{t->xf_post, Ly.post_norm};
       p.ss_out = Ly.ss_o;
       p.err = err;
-      gemv_prefetch(ctx, p, &Ly.gu);
       prof_begin(ctx, PK_O);
       launch_gemv(ctx, Ly.o, p);
       prof_end(ctx, PK_O);
@@ -1490,6 +1516,228 @@ XIn target_layers(wc_target* t, wc_kv* kv, const Rows& r, XIn in0, float* h, con
 XIn target_tap_stats(const wc_target* t, int f, const uint32_t* xf, int L_max) {
   const TLayer& Ly = t->layers[t->taps[f]];
   return XIn{xf, Ly.ss_d, gemv_parts(t->ctx, Ly.down, L_max)};
+}
+
+// ---- persistent layer stack (stack.cuh): the same layer program as target_layers, as jobs
+
+struct StackPlan {
+  bool ready = false;
+  Job* dev = nullptr;
+  int njobs = 0;
+  unsigned* bar = nullptr;
+  int last_down_parts = 0;
+  ~StackPlan() {
+    dfree(dev);
+    dfree(bar);
+  }
+};
+
+bool target_stack_ok(const wc_target* t, const Rows& r) {
+  const wc_ctx* ctx = t->ctx;
+  const auto& c = t->cfg;
+  return ctx->stack && ctx->occ_stack >= 1 && t->dtype == WC_BF16 && c.head_dim == SK_D && c.kv_heads <= 16 &&
+         r.L_max <= SK_MAXL && r.L_max * (c.heads / c.kv_heads) <= SK_MAXR && !r.mask_full && !r.positions &&
+         r.stable;
+}
+
+// GEMV job parameters for the stack grid (one CTA per SM, 8-row fragments)
+GemvParams stack_gemv(wc_ctx* ctx, const Lin& W, GemvParams p) {
+  const bool bf16 = W.dtype == WC_BF16;
+  if (!bf16 || p.L_max > 8) fail(WC_ERR_INVALID, "stack GEMV needs bf16 weights and <= 8 rows");
+  p.w = W.w;
+  p.N = W.N;
+  p.Np = W.Np;
+  p.Kp = W.Kp;
+  p.group = W.group;
+  if (!p.err) p.err = ctx->d_err;
+  if (p.nseg != W.nseg) fail(WC_ERR_INVALID, "GEMV input segments do not match the weight");
+  for (int i = 0; i < p.nseg; ++i)
+    if (p.seg[i].len != W.seg_len[i] || p.seg[i].lenp != xf_width(true, p.seg[i].len))
+      fail(WC_ERR_INVALID, "GEMV input width does not match the weight");
+  p.out_width = xf_width(true, W.N);
+  const int chs = SK_ACT_BYTES / GV_STAGE_BYTES;
+  const int nslab = W.Kp / GV_COLS, nunits = W.Np / (16 * W.group);
+  p.nkc = (nslab + chs - 1) / chs;
+  p.kc_slabs = (nslab + p.nkc - 1) / p.nkc;
+  p.gpk = std::max(1, std::min(nunits, ctx->num_sms / p.nkc));
+  if (p.nkc > 1) {
+    if (size_t(p.nkc) * (W.Np / 16) * 256 > ctx->gv_partial_n) fail(WC_ERR_UNSUPPORTED, "stack split-K scratch");
+    p.partial = ctx->gv_partial;
+  }
+  if (p.ss_out && nunits > max_parts(ctx)) fail(WC_ERR_INVALID, "GEMV output statistics above the buffer size");
+  return p;
+}
+
+// Builds and uploads the verify's job list (outside stream capture).
+void target_stack_build(wc_target* t, wc_kv* kv, const Rows& r, XIn in0, float* h, const TapOut* taps, int* err,
+                        StackPlan& plan) {
+  wc_ctx* ctx = t->ctx;
+  const auto& c = t->cfg;
+  const int H = c.hidden, D = c.head_dim, Hq = c.heads * D, Hkv = c.kv_heads * D, I = c.intermediate;
+  const int ld_qkv = Hq + 2 * Hkv;
+  std::vector<Job> jobs;
+  auto gemv_job = [&](const Lin& W, const GemvParams& p) {
+    Job j;
+    std::memset(&j, 0, sizeof(j));
+    j.type = JOB_GEMV;
+    j.g = stack_gemv(ctx, W, p);
+    jobs.push_back(j);
+    if (j.g.nkc > 1) {  // partials only; the finalize job runs the epilogue
+      jobs.back().g.ss_out = nullptr;
+      Job f = j;
+      f.type = JOB_FIN;
+      jobs.push_back(f);
+    }
+  };
+  const int S = std::max(1, std::min(SK_MAXS, ctx->num_sms / c.kv_heads));
+  XIn x = in0;
+  for (int li = 0; li < c.layers; ++li) {
+    const TLayer& Ly = t->layers[li];
+    {
+      GemvParams p = gemv_params();
+      p.L = r.L;
+      p.L_dev = r.L_dev;
+      p.L_max = r.L_max;
+      p.nseg = 1;
+      p.seg[0] = xs_frag(x, H, true, c.eps);
+      p.epi = EPI_STORE;
+      p.y = t->ws_qkv;
+      p.ldy = ld_qkv;
+      p.err = err;
+      gemv_job(Ly.qkv, p);
+    }
+    {
+      Job j;
+      std::memset(&j, 0, sizeof(j));
+      j.type = JOB_ATTN;
+      AttnParams& a = j.at.a;
+      a.qkv = t->ws_qkv;
+      a.ld_qkv = ld_qkv;
+      a.q_norm = Ly.q_norm;
+      a.k_norm = Ly.k_norm;
+      a.eps = c.eps;
+      a.rope = t->rope->ptr;
+      a.max_pos = t->rope->max_pos;
+      a.n_dev = r.n_dev;
+      a.n_add = r.n_add;
+      a.L = r.L;
+      a.L_dev = r.L_dev;
+      a.L_max = r.L_max;
+      a.Kc = kv->Kl(li);
+      a.Vc = kv->Vl(li);
+      a.kv_dtype = kv->dtype;
+      a.stride_h = (long long)kv->cap * D;
+      a.stride_p = D;
+      a.cap = kv->cap;
+      a.H = c.heads;
+      a.Hk = c.kv_heads;
+      a.D = D;
+      a.newmask = r.newmask;
+      a.scale = 1.f / std::sqrt(float(D));
+      a.xf_out = t->xf_att;
+      a.xf_width = xf_width(true, Hq);
+      a.write_cache = 1;
+      a.err = err;
+      j.at.part = ctx->sk_part;
+      j.at.counters = ctx->sk_counters;
+      j.at.S = S;
+      jobs.push_back(j);
+    }
+    {
+      GemvParams p = gemv_params();
+      p.L = r.L;
+      p.L_dev = r.L_dev;
+      p.L_max = r.L_max;
+      p.nseg = 1;
+      p.seg[0] = xs_frag(XIn{t->xf_att, nullptr, 0}, Hq, true);
+      p.epi = EPI_ADD;
+      p.y = h;
+      p.ldy = H;
+      p.base = h;
+      p.ldb = H;
+      p.nout = 1;
+      p.out[0] = XOut{t->xf_post, Ly.post_norm};
+      p.ss_out = Ly.ss_o;
+      p.err = err;
+      gemv_job(Ly.o, p);
+    }
+    {
+      GemvParams p = gemv_params();
+      p.L = r.L;
+      p.L_dev = r.L_dev;
+      p.L_max = r.L_max;
+      p.nseg = 1;
+      p.seg[0] = xs_frag(XIn{t->xf_post, Ly.ss_o, gemv_parts(ctx, Ly.o, r.L_max)}, H, true, c.eps);
+      p.epi = EPI_SWIGLU;
+      p.nout = 1;
+      p.out[0] = XOut{t->xf_act, nullptr};
+      p.err = err;
+      gemv_job(Ly.gu, p);
+    }
+    {
+      GemvParams p = gemv_params();
+      p.L = r.L;
+      p.L_dev = r.L_dev;
+      p.L_max = r.L_max;
+      p.nseg = 1;
+      p.seg[0] = xs_frag(XIn{t->xf_act, nullptr, 0}, I, true);
+      p.epi = EPI_ADD;
+      p.y = h;
+      p.ldy = H;
+      p.base = h;
+      p.ldb = H;
+      p.nout = 1;
+      p.out[0] = XOut{t->xf_in, li + 1 < c.layers ? t->layers[li + 1].in_norm : t->final_norm};
+      p.ss_out = Ly.ss_d;
+      for (int f = 0; f < 3; ++f)
+        if (taps && t->taps[f] == li) {
+          if (taps->rows) {
+            p.y2 = taps->rows + size_t(f) * taps->stride;
+            p.ldy2 = H;
+          }
+          if (taps->xf[f]) p.out[p.nout++] = XOut{taps->xf[f], taps->w[f]};
+        }
+      p.err = err;
+      gemv_job(Ly.down, p);
+    }
+    x = XIn{t->xf_in, Ly.ss_d, gemv_parts(ctx, Ly.down, r.L_max)};
+  }
+  plan.last_down_parts = x.nparts;
+  dfree(plan.dev);
+  plan.dev = static_cast<Job*>(dalloc(sizeof(Job) * jobs.size()));
+  CUDA_TRY(cudaMemcpy(plan.dev, jobs.data(), sizeof(Job) * jobs.size(), cudaMemcpyHostToDevice));
+  if (!plan.bar) plan.bar = static_cast<unsigned*>(dalloc(sizeof(unsigned) * 4));
+  plan.njobs = int(jobs.size());
+  plan.ready = true;
+}
+
+// Runs a built stack; returns the head input (fragments times the final norm gain).
+XIn target_stack_launch(wc_target* t, StackPlan& plan, int* err) {
+  wc_ctx* ctx = t->ctx;
+  if (!plan.ready) fail(WC_ERR_INVALID, "layer stack not built");
+  CUDA_TRY(cudaMemsetAsync(plan.bar, 0, sizeof(unsigned) * 4, ctx->stream));
+  StackParams sp;
+  std::memset(&sp, 0, sizeof(sp));
+  sp.jobs = plan.dev;
+  sp.njobs = plan.njobs;
+  sp.bar = plan.bar;
+  sp.err = err;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ctx->num_sms);
+  cfg.blockDim = dim3(SK_THREADS);
+  cfg.dynamicSmemBytes = stack_smem();
+  cfg.stream = ctx->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  prof_begin(ctx, PK_STACK);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, stack_kernel, sp);
+  if (e != cudaSuccess) fail(WC_ERR_CUDA, std::string("launch of stack_kernel: ") + cudaGetErrorString(e));
+  count_launch(ctx);
+  prof_end(ctx, PK_STACK);
+  return XIn{t->xf_in, t->layers.back().ss_d, plan.last_down_parts};
 }
 
 // Head over `rows` rows given as fragments (times the final norm): argmax keys and,
@@ -1858,7 +2106,7 @@ XIn drafter_layers(wc_drafter* d, wc_kv* kv, const Rows& r, XIn feat_in, const f
       p.y = d->ws_qkv;
       p.ldy = ld_qkv;
       p.err = err;
-      gemv_prefetch(ctx, p, &Ly.o);
+      gemv_prefetch(ctx, p, &Ly.o, &Ly.gu);  // both land while attention runs
       launch_gemv(ctx, Ly.qkv, p);
     }
     {
@@ -1913,7 +2161,6 @@ XIn drafter_layers(wc_drafter* d, wc_kv* kv, const Rows& r, XIn feat_in, const f
       p.out[0] = XOut{d->xf_post, Ly.post_norm};
       p.ss_out = Ly.ss_o;
       p.err = err;
-      gemv_prefetch(ctx, p, &Ly.gu);
       launch_gemv(ctx, Ly.o, p);
     }
     {
@@ -2306,6 +2553,7 @@ struct wc_decoder {
   bool prefilled = false;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   float last_ms = 0.f;
+  std::map<int, std::unique_ptr<StackPlan>> stack_plans;  // verify layer stacks per chain length
 };
 
 namespace {
@@ -2391,7 +2639,10 @@ void build_round(wc_decoder* dec, int K) {
     to.xf[f] = d->xf_tap[f];
     to.w[f] = d->cfg.feature_norm ? d->feature_norms[f] : nullptr;
   }
-  const XIn hx = target_layers(t, dec->tkv, rv, in0, t->ws_h, &to, err);
+  auto sp_it = dec->stack_plans.find(K);
+  const XIn hx = (sp_it != dec->stack_plans.end() && sp_it->second->ready)
+                     ? target_stack_launch(t, *sp_it->second, err)
+                     : target_layers(t, dec->tkv, rv, in0, t->ws_h, &to, err);
   target_head(t, hx, K + 1, nullptr, K + 1, st->keys + K, nullptr, err);
   // ---- acceptance + chain compaction (spec.py:357-362)
   launch_ex(ctx, "accept", accept_chain_kernel, dim3(1), dim3(32), 0, true, 1, st, K, (const int*)nullptr,
@@ -2423,6 +2674,25 @@ std::pair<cudaGraphExec_t, uint64_t>& round_graph(wc_decoder* dec, int K, bool p
   if (profiled) {
     dec->profilers[K] = std::make_unique<Profiler>();
     ctx->prof = dec->profilers[K].get();
+  }
+  {  // the verify's layer stack is built and uploaded before capture
+    wc_target* t = dec->t;
+    wc_drafter* d = dec->d;
+    Rows rv;
+    rv.stable = true;
+    rv.L = K + 1;
+    rv.L_max = K + 1;
+    rv.n_dev = &dec->st->n;
+    if (!dec->stack_plans.count(K) && target_stack_ok(t, rv)) {
+      TapOut to;
+      for (int f = 0; f < 3; ++f) {
+        to.xf[f] = d->xf_tap[f];
+        to.w[f] = d->cfg.feature_norm ? d->feature_norms[f] : nullptr;
+      }
+      auto plan = std::make_unique<StackPlan>();
+      target_stack_build(t, dec->tkv, rv, XIn{t->xf_in, t->ss_pack, 1}, t->ws_h, &to, &dec->st->err, *plan);
+      dec->stack_plans[K] = std::move(plan);
+    }
   }
   cudaGraph_t g = nullptr;
   CUDA_TRY(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
@@ -2458,6 +2728,7 @@ void check_state_error(wc_decoder* dec) {
     CUDA_TRY(cudaMemset(&dec->st->err, 0, sizeof(int)));
     CUDA_TRY(cudaMemset(dec->ctx->d_err, 0, sizeof(int)));
     CUDA_TRY(cudaMemset(dec->ctx->gv_counters, 0, sizeof(int) * dec->ctx->gv_counters_n));
+    CUDA_TRY(cudaMemset(dec->ctx->sk_counters, 0, sizeof(int) * 64));
     fail(WC_ERR_DEVICE, "device error flag " + std::to_string(e | ce));
   }
 }
@@ -2689,7 +2960,7 @@ extern "C" wc_status wc_decoder_profile_round(wc_decoder* dec, int k, int* out_t
   return guard(dec->ctx, [&] {
     *out_n = decoder_round_impl(dec, k, out_tokens, true);
     Profiler* pr = dec->profilers.at(k).get();
-    for (int i = 0; i < PK_COUNT; ++i) {
+    for (int i = 0; i < PK_SLOTS; ++i) {
       ms_sum[i] = 0.f;
       counts[i] = 0;
     }

@@ -131,14 +131,14 @@ class SpeculativeDecoder:
         return list(out[: n.value])
 
     PROFILE_KINDS = ("target_qkv", "attention", "target_o", "target_gate_up", "target_down", "target_head",
-                     "drafter_head", "drafter_layer")
+                     "drafter_head", "drafter_layer", "target_stack")
 
     def profile_round(self, k: int) -> tuple[list[int], dict]:
         """A real round replayed from an instrumented graph: mean device ms per kernel class."""
         out = (C.c_int * (k + 1))()
         n = C.c_int()
-        ms = (C.c_float * 8)()
-        cnt = (C.c_int * 8)()
+        ms = (C.c_float * 16)()
+        cnt = (C.c_int * 16)()
         self.ctx.check(lib().wc_decoder_profile_round(self.h, k, out, C.byref(n), ms, cnt))
         prof = {name: {"mean_ms": (ms[i] / cnt[i]) if cnt[i] else 0.0, "launches": cnt[i]}
                 for i, name in enumerate(self.PROFILE_KINDS)}
