@@ -224,8 +224,14 @@ WC_API wc_status wc_decoder_prefill(wc_decoder* dec, const int* prompt, int n, c
 /* Oracle-drafter mode (tests/test_spec_model.py:59-92 pattern): when `forced` (host int32[k]) is
  * non-NULL, draft token j is replaced by forced[j] after the drafter computed it. */
 WC_API wc_status wc_decoder_set_forced(wc_decoder* dec, const int* forced, int k);
-/* One greedy chain round of length k (spec.py:331-364). Writes the accepted tokens
- * (d_1..d_a, next) to out_tokens (host, capacity k+1) and their count to *out_n. */
+/* One chain round of length k (spec.py:331-364). Writes the accepted tokens (d_1..d_a, next)
+ * to out_tokens (host, capacity k+1) and their count to *out_n. After a prefill with
+ * temperature > 0 the round is sampled (spec.py:216-324 on a chain): draft d_i is drawn from
+ * the drafter's softmax(z_i / T) over its head rows, the target's p = softmax(z / T) verifies
+ * with verify_tree_stochastic's chain rule (sampling.py:143-187) and the next token is drawn
+ * from the residual or from the bonus row. Random numbers: Philox4x32-10 keyed by sp->seed;
+ * each round consumes one counter block of 2^26 (streams of 2^21: draft step i, the
+ * acceptance uniforms, the residual's Gumbel noise). top_k / top_p: WC_ERR_UNSUPPORTED. */
 WC_API wc_status wc_decoder_round(wc_decoder* dec, int k, int* out_tokens, int* out_n);
 /* spec.py:151-212 generate with a static chain policy of depth k (trees: WC_ERR_UNSUPPORTED until built).
  * eos: host int32[n_eos]. out_tokens capacity max_new. */
@@ -236,6 +242,17 @@ WC_API wc_status wc_decoder_generate(wc_decoder* dec, const int* prompt, int n, 
 WC_API wc_status wc_generate_autoregressive(wc_target* t, const int* prompt, int n, int max_new,
                                      const wc_sampling_params* sp, const int* eos, int n_eos, int max_context,
                                      int* out_tokens, int* out_n, wc_gen_stats* stats);
+/* Test and measurement support, no counterpart in the reference. save_state snapshots the
+ * decoder's device state (round state, chain root) after a prefill or a round; restore_state
+ * puts it back (cache rows past the snapshot are scratch and get rewritten) but keeps the
+ * current random counter, so rounds replayed from one snapshot draw fresh numbers. */
+WC_API wc_status wc_decoder_save_state(wc_decoder* dec);
+WC_API wc_status wc_decoder_restore_state(wc_decoder* dec);
+/* The last sampled round of length k: target logits [k+1][V] at [x_n, d_1..d_k], draft
+ * logits [k][head_rows], the verify tokens [x_n, d_1..d_k] and rng = {seed, counter base
+ * of that round}. Host buffers; any may be NULL. */
+WC_API wc_status wc_decoder_round_logits(wc_decoder* dec, int k, float* zt, float* zd, int* tokens,
+                                         unsigned long long* rng);
 /* A real round (as wc_decoder_round) replayed from a second graph that records CUDA events
  * around kernels: ms_sum[i] / counts[i] is the mean device time of kernel class i, for
  * i = 0 target QKV GEMV, 1 attention, 2 o-proj, 3 gate/up, 4 down-proj, 5 target head,

@@ -82,6 +82,118 @@ class Tape:
         return float(u[0]) if size is None else u.reshape(size)
 
 
+# ----------------------------------------------------------------------------- sampled device rounds
+# The CUDA path draws with the same rules as the reference (sampling.py:39-55, 69-82,
+# 143-203) but from Philox counters instead of numpy's Generator: a draw from softmax(z / T)
+# is the Gumbel-max argmax_j (z_j / T + g_j), and the residual / bonus draw is the Gumbel-max
+# over log r_j. Layout per round (or autoregressive step): RNG_STREAMS streams of
+# RNG_STREAM_LEN counters from the round's base; stream i < 16 = draft step i (element = head
+# row), RNG_ACCEPT_STREAM = acceptance uniforms (element = draft index), RNG_RESIDUAL_STREAM =
+# residual / bonus noise (element = token id). Keys are ranked as float32, as on the device.
+
+RNG_STREAM_LEN = 1 << 21
+RNG_STREAMS = 32
+RNG_ROUND_STRIDE = RNG_STREAM_LEN * RNG_STREAMS
+RNG_ACCEPT_STREAM = 16
+RNG_RESIDUAL_STREAM = 17
+
+
+def _philox_words(seed: int, start: int, n: int):
+    idx = np.arange(start, start + n, dtype=np.uint64)
+    return philox4x32_10((idx & np.uint64(0xFFFFFFFF)).astype(np.uint32), (idx >> np.uint64(32)).astype(np.uint32),
+                         seed)
+
+
+def philox_gumbel_f32(seed: int, start: int, n: int) -> np.ndarray:
+    """float32 Gumbel noise, u = (24 bits of word 0 + 1/2) / 2^24 on (0, 1)."""
+    r0, _, _, _ = _philox_words(seed, start, n)
+    u = ((r0 >> np.uint32(8)).astype(F32) + F32(0.5)) * F32(1.0 / 16777216.0)
+    return (-np.log(-np.log(u))).astype(F32)
+
+
+def philox_gumbel_f64(seed: int, start: int, n: int) -> np.ndarray:
+    """float64 Gumbel noise, u = (53 bits of words 0 and 1 + 1/2) / 2^53 on (0, 1)."""
+    r0, r1, _, _ = _philox_words(seed, start, n)
+    u = ((r0 >> np.uint32(5)).astype(np.float64) * 67108864.0 + (r1 >> np.uint32(6)).astype(np.float64) + 0.5) / \
+        9007199254740992.0
+    return -np.log(-np.log(u))
+
+
+def gumbel_draw(z: np.ndarray, T: float, seed: int, base: int, stream: int) -> int:
+    """Draft draw of one head row: argmax of float32 z / T + Gumbel noise (element = row)."""
+    g = philox_gumbel_f32(seed, base + stream * RNG_STREAM_LEN, len(z))
+    key = (np.asarray(z, F32) / F32(T)).astype(F32) + g
+    return int(np.argmax(key))  # first maximum, as the device's key packing breaks ties
+
+
+def sampled_chain_accept(zt: np.ndarray, zd: np.ndarray, tokens: list[int], T: float, seed: int, base: int,
+                         vocab_ids: np.ndarray | None = None, skip_residual: bool = False) -> tuple[int, int]:
+    """Acceptance of one sampled chain round from its logits: zt [K+1][V] target rows at
+    [x_n, d_1..d_K], zd [K][Vd] draft rows (head row r is token vocab_ids[r]). p_i =
+    softmax(zt_i / T), q_i = softmax(zd_i / T) scattered to token ids (spec.py:239-249);
+    the chain case of verify_tree_stochastic (sampling.py:143-187). `skip_residual` plants
+    the mistake a negative control must catch: a rejection draws from p instead."""
+    K = len(tokens) - 1
+    V = zt.shape[1]
+
+    def probs(z):
+        x = (np.asarray(z, F32) / F32(T)).astype(np.float64)
+        e = np.exp(x - x.max())
+        return e / e.sum()
+
+    def q_full(i):
+        qd = probs(zd[i])
+        q = np.zeros(V)
+        if vocab_ids is None:
+            q[: len(qd)] = qd
+        else:
+            q[np.asarray(vocab_ids)] = qd
+        return q
+
+    a = 0
+    while a < K:
+        x = tokens[a + 1]
+        q = q_full(a)
+        qx = q[x]
+        if not qx > 0:
+            break
+        px = probs(zt[a])[x]
+        u = philox_uniforms(seed, base + RNG_ACCEPT_STREAM * RNG_STREAM_LEN + a, 1)[0]
+        if not u < min(1.0, px / qx):
+            break
+        a += 1
+    p = probs(zt[a])
+    if a < K and not skip_residual:
+        r = np.maximum(p - q_full(a), 0.0)
+        if not r.sum() > 1e-12:
+            r = p
+    else:
+        r = p
+    g = philox_gumbel_f64(seed, base + RNG_RESIDUAL_STREAM * RNG_STREAM_LEN, V)
+    with np.errstate(divide="ignore"):
+        key = np.where(r > 0, (np.log(r) + g).astype(F32), -np.inf)
+    return a, int(np.argmax(key))
+
+
+def chi2_equal_mass(counts: np.ndarray, p: np.ndarray, bins: int = 1000) -> tuple[float, int, float]:
+    """Pearson chi-square of token counts against the law p, on `bins` groups of consecutive
+    token ids with (near) equal expected mass (the binning the reference's test uses where one
+    token per cell would leave expected counts under 5, tests/test_sampling.py:73-76).
+    Returns (statistic, degrees of freedom, p-value)."""
+    from scipy.stats import chi2
+    n = counts.sum()
+    c = np.cumsum(p) / p.sum()
+    edges = np.searchsorted(c, np.arange(1, bins) / bins, side="left")
+    b = np.concatenate([[0], edges + 1, [len(p)]])
+    b = np.unique(np.clip(b, 0, len(p)))
+    obs = np.add.reduceat(counts, b[:-1])
+    exp = np.add.reduceat(p / p.sum(), b[:-1]) * n
+    keep = exp > 0
+    stat = float(((obs[keep] - exp[keep]) ** 2 / exp[keep]).sum())
+    dof = int(keep.sum()) - 1
+    return stat, dof, float(chi2.sf(stat, dof))
+
+
 # ----------------------------------------------------------------------------- ops (cpu_ops.cpp)
 
 

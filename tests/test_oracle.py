@@ -256,3 +256,59 @@ def test_negative_control_skipping_the_residual_is_biased():
         return [int(rng.choice(V, p=P[prev]))]
 
     assert _pvalue(_run(gen)) < 1e-6
+
+
+# ------------------------------------------------------------------ the device's sampled-round protocol
+
+def _device_chain_round(K, Qm=Q, skip_residual=False):
+    """One sampled chain round as the CUDA path draws it (Gumbel-max drafts from Philox
+    stream i, acceptance uniforms and residual noise from their streams), on log-probabilities
+    as logits at T = 1; each round takes the next counter block."""
+    state = {"base": 0}
+
+    def gen(prev, rng):
+        base = state["base"]
+        state["base"] += O.RNG_ROUND_STRIDE
+        with np.errstate(divide="ignore"):
+            toks, zd, zt, cur = [prev], [], [np.log(P[prev])], prev
+            for i in range(K):
+                z = np.log(Qm[cur]).astype(np.float32)
+                cur = O.gumbel_draw(z, 1.0, 77, base, i)
+                toks.append(cur)
+                zd.append(z)
+                zt.append(np.log(P[cur]))
+        a, nxt = O.sampled_chain_accept(np.array(zt, np.float32), np.array(zd, np.float32), toks, 1.0, 77, base,
+                                        skip_residual=skip_residual)
+        return toks[1:a + 1] + [nxt]
+
+    return gen
+
+
+DEVICE_TRIALS = 5000  # numpy Philox per draw is slow; the planted mistake is still caught by far
+
+
+def test_device_protocol_preserves_target():
+    assert _pvalue(_run(_device_chain_round(3, Q_TRUNC), trials=DEVICE_TRIALS)) > 1e-3
+
+
+def test_device_protocol_negative_control_skipping_the_residual_is_biased():
+    assert _pvalue(_run(_device_chain_round(3, Q_TRUNC, skip_residual=True), trials=DEVICE_TRIALS)) < 1e-6
+
+
+def test_device_protocol_decisions_equal_the_reference_rule_on_its_uniforms():
+    """The accept count of sampled_chain_accept equals verify_chain_stochastic (pinned to the
+    reference above) fed the acceptance stream as its uniform tape."""
+    rng = np.random.default_rng(5)
+    Vs, K = 64, 4
+    for trial in range(200):
+        zt = rng.normal(0, 1.5, (K + 1, Vs)).astype(np.float32)
+        zd = rng.normal(0, 1.5, (K, Vs)).astype(np.float32)
+        toks = [0] + [int(x) for x in rng.integers(0, Vs, K)]
+        base = trial * O.RNG_ROUND_STRIDE
+        a, _ = O.sampled_chain_accept(zt, zd, toks, 0.7, 9, base)
+        sm = lambda z: (lambda e: e / e.sum())(np.exp((z / np.float32(0.7)).astype(np.float64) -
+                                                      (z / np.float32(0.7)).max()))
+        p = np.array([sm(r) for r in zt])
+        q = np.array([sm(r) for r in zd])
+        ref_a, _ = O.verify_chain_stochastic(p, q, toks[1:], O.Tape(9, base + O.RNG_ACCEPT_STREAM * O.RNG_STREAM_LEN))
+        assert a == ref_a, trial

@@ -118,6 +118,9 @@ SIGNATURES = {
     "wc_decoder_target_cache": (P, [P]),
     "wc_decoder_drafter_cache": (P, [P]),
     "wc_decoder_last_round_ms": (S, [P, C.POINTER(C.c_float)]),
+    "wc_decoder_save_state": (S, [P]),
+    "wc_decoder_restore_state": (S, [P]),
+    "wc_decoder_round_logits": (S, [P, C.c_int, P, P, I32P, C.POINTER(C.c_uint64)]),
 }
 
 _lib = None

@@ -17,6 +17,7 @@ enum DeviceError : int {
   kErrPosition = 8,       // a RoPE position beyond the precomputed table
   kErrTree = 16,          // malformed tree (parent >= child)
   kErrTimeout = 32,       // a bounded wait (mbarrier / pipeline) expired
+  kErrSample = 64,        // a sampled draw found no token with positive probability
 };
 
 __device__ __forceinline__ void raise_error(int* err, int bit) {
@@ -151,6 +152,34 @@ __device__ __forceinline__ double philox_uniform(uint64_t seed, uint64_t index) 
   const uint4 r = philox4x32_10(index, seed);
   return (double(r.x >> 5) * 67108864.0 + double(r.y >> 6)) * (1.0 / 9007199254740992.0);
 }
+
+// Gumbel(0, 1) noise from element `index` of the stream, -log(-log(u)) with u on the open
+// interval (0, 1): argmax_j (z_j / T + g_j) is a draw from softmax(z / T) (the Gumbel-max
+// identity; Gumbel 1954, as used for sampling by Maddison, Tarlow & Minka 2014).
+// fp32 from 24 bits of word 0, for the fused head epilogues:
+__device__ __forceinline__ float philox_gumbel_f(uint64_t seed, uint64_t index) {
+  const uint4 r = philox4x32_10(index, seed);
+  const float u = (float(r.x >> 8) + 0.5f) * (1.0f / 16777216.0f);
+  return -logf(-logf(u));
+}
+// fp64 from 53 bits of words 0 and 1, for the residual draw:
+__device__ __forceinline__ double philox_gumbel_d(uint64_t seed, uint64_t index) {
+  const uint4 r = philox4x32_10(index, seed);
+  const double u = (double(r.x >> 5) * 67108864.0 + double(r.y >> 6) + 0.5) * (1.0 / 9007199254740992.0);
+  return -log(-log(u));
+}
+
+// Random-number layout of sampled decoding. The device keeps (seed, counter base); a
+// round (or an autoregressive step, or the prefill's first token) owns kRngStreams
+// streams of kRngStreamLen elements from its base, then advances the base by
+// kRngRoundStride. Streams 0..15: draft step i / head row l (element = vocabulary row);
+// kRngAcceptStream: the acceptance uniform of draft i (element i); kRngResidualStream:
+// the Gumbel noise of the residual or bonus draw (element = token id).
+constexpr uint64_t kRngStreamLen = 1ull << 21;
+constexpr int kRngStreams = 32;
+constexpr uint64_t kRngRoundStride = kRngStreamLen * kRngStreams;
+constexpr int kRngAcceptStream = 16;
+constexpr int kRngResidualStream = 17;
 
 }  // namespace wc
 

@@ -104,6 +104,13 @@ struct GemvParams {
   float* y2;             // optional second copy of the stored result (tap capture)
   int ldy2;
   unsigned long long* keys;  // EPI_ARGMAX: per-row max keys (atomicMax)
+  // EPI_ARGMAX with `temperature` set (T on the device, > 0): the key of row l is a draw from
+  // softmax(v / T), the argmax of v / T + Gumbel noise (element n of stream rng_stream + l
+  // from rng = [seed, counter base] on the device); the stored logits stay v
+  const float* temperature;
+  const unsigned long long* rng;
+  int rng_stream;
+  int pad_rng;
   int nout;
   XOut out[2];
   int out_width;         // fragment width of the outputs (xf_width(N))
@@ -255,12 +262,19 @@ __device__ void gemv_side_job(const GemvParams& p, int L, const float* s_inv, fl
 // Epilogue of one output element: feature n of unit u (row r16 of its block), row l; v0 the
 // sum (SwiGLU: gate), v1 the up sum. Writes y / y2 / fragments, returns y^2 for the unit's
 // sum of squares; argmax goes to the block key.
+// the value an EPI_ARGMAX key ranks: the logit, or with a temperature the perturbed logit
+__device__ __forceinline__ float gemv_pick_value(const GemvParams& p, int l, int n, float v) {
+  if (!p.temperature) return v;
+  return v / *p.temperature +
+         philox_gumbel_f(p.rng[0], p.rng[1] + uint64_t(p.rng_stream + l) * kRngStreamLen + uint64_t(n));
+}
+
 __device__ __forceinline__ float gemv_epilogue(const GemvParams& p, int n, int l, float v0, float v1,
                                                unsigned long long* s_key) {
   float v = v0;
   if (p.epi == EPI_ARGMAX) {
     if (p.y) p.y[size_t(l) * p.ldy + n] = v;
-    atomicMax(&s_key[l], argmax_key(v, uint32_t(n)));
+    atomicMax(&s_key[l], argmax_key(gemv_pick_value(p, l, n, v), uint32_t(n)));
     return 0.f;
   }
   if (p.epi == EPI_SWIGLU) v = v0 / (1.f + expf(-v0)) * v1;
@@ -644,7 +658,7 @@ __global__ void __launch_bounds__(GV_F32_THREADS) gemv_f32_kernel(__grid_constan
         if (lane == 0) {
           if (p.epi == EPI_ARGMAX) {
             if (p.y) p.y[size_t(l) * p.ldy + u] = s0;
-            const unsigned long long k = argmax_key(s0, uint32_t(u));
+            const unsigned long long k = argmax_key(gemv_pick_value(p, l, u, s0), uint32_t(u));
             if (k > best[l]) best[l] = k;
           } else {
             float v = (p.epi == EPI_SWIGLU) ? s0 / (1.f + expf(-s0)) * s1 : s0;

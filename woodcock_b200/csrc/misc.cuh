@@ -26,6 +26,9 @@ struct RoundState {
   int acc[MAXK + 1];      // accepted tokens d_1..d_a, next
   int forced[MAXK];       // oracle-drafter tokens (-1 = drafter's own)
   unsigned long long keys[MAXKEYS];  // argmax keys: draft steps [0, K), verify rows [K, 2K+1)
+  unsigned long long rng[2];         // sampled decoding: Philox seed, counter base of the next round
+  float temperature;                 // sampled decoding: T (0 = greedy)
+  int pad2;
 };
 
 // ----------------------------------------------------------------------------- activation packing
@@ -528,6 +531,219 @@ __global__ void accept_chain_kernel(RoundState* st, int K, const int* vocab_map_
     for (int i = 0; i <= a; ++i) out_host_view[1 + i] = st->acc[i];
   }
   (void)vocab_map_unused;
+}
+
+// ----------------------------------------------------------------------------- sampled rounds
+// Softmax statistics of logit rows at temperature T, in slices: block b of a row's nb blocks
+// writes (max of z / T, sum of exp(z / T - max)) over its slice. Rows [0, R1) are z1 (length
+// V1, row stride V1), then rows [R1, R1 + R2) are z2 (length V2).
+struct StatsParams {
+  const float* z1;
+  int R1, V1, nb1;
+  const float* z2;
+  int R2, V2, nb2;
+  const float* temperature;  // T on the device
+  float2* out;               // [R1 * nb1 + R2 * nb2]
+};
+
+__global__ void __launch_bounds__(256) logit_stats_kernel(__grid_constant__ const StatsParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
+  __shared__ float red[32];
+  const int b = blockIdx.x;
+  const float* z;
+  int V, nb, i;
+  if (b < p.R1 * p.nb1) {
+    z = p.z1 + size_t(b / p.nb1) * p.V1;
+    V = p.V1;
+    nb = p.nb1;
+    i = b % p.nb1;
+  } else {
+    const int b2 = b - p.R1 * p.nb1;
+    z = p.z2 + size_t(b2 / p.nb2) * p.V2;
+    V = p.V2;
+    nb = p.nb2;
+    i = b2 % p.nb2;
+  }
+  const int chunk = (V + nb - 1) / nb, j0 = min(V, i * chunk), j1 = min(V, j0 + chunk);
+  const float T = *p.temperature;
+  float m = -INFINITY;
+  for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x) m = fmaxf(m, z[j] / T);
+  m = warp_max(m);
+  if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = m;
+  __syncthreads();
+  float M = -INFINITY;
+  for (int w = 0; w < int(blockDim.x / 32); ++w) M = fmaxf(M, red[w]);
+  __syncthreads();
+  float e = 0.f;
+  if (M != -INFINITY)
+    for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x) e += expf(z[j] / T - M);
+  e = warp_sum(e);
+  if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = e;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float S = 0.f;
+    for (int w = 0; w < int(blockDim.x / 32); ++w) S += red[w];
+    p.out[b] = make_float2(M, S);
+  }
+}
+
+// Stochastic chain acceptance (sampling.py:69-82, the chain case of verify_tree_stochastic,
+// sampling.py:143-177, with _residual 182-187) on the round's logits: target rows zt [K+1][V]
+// at [x_n, d_1..d_K], draft rows zd [K][Vd] (the drafter head's rows; token j is row
+// vocab_inv[j], or j without a restricted head). With p_i = softmax(zt_i / T) and
+// q_i = softmax(zd_i / T): draft d_{i+1} is accepted when q_i(x) > 0 and u_i < min(1,
+// p_i(x) / q_i(x)); at the first rejection (row a) the next token is drawn from
+// norm(max(p_a - q_a, 0)) (from p_a when that mass is <= 1e-12), after K acceptances from p_K.
+// The draw is the Gumbel-max over the token ids, sliced across the grid; every block repeats
+// the (K-step) decision, and the last block to finish reduces the slices in block order and
+// commits the round as accept_chain_kernel does, advancing the random counter base.
+struct SampleAcceptParams {
+  RoundState* st;
+  int K;
+  const float* zt;
+  int V;
+  const float* zd;
+  int Vd;
+  const int* vocab_inv;  // [V] or nullptr
+  const float2* stats;   // logit_stats_kernel: target rows (nbt each), then draft rows (nbd each)
+  int nbt, nbd;
+  double* part;          // [gridDim][3]: residual mass, residual key, p key (bits)
+  unsigned* counter;     // zero at launch; left at zero
+  int* out_host_view;
+};
+
+__device__ __forceinline__ int sample_row_of(const SampleAcceptParams& p, int tok) {
+  if (tok < 0 || tok >= p.V) return -1;
+  if (p.vocab_inv) return p.vocab_inv[tok];
+  return tok < p.Vd ? tok : -1;
+}
+
+__global__ void __launch_bounds__(256) accept_sampled_kernel(__grid_constant__ const SampleAcceptParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
+  __shared__ double sM[MAXK + 1], sS[MAXK + 1], dM[MAXK], dS[MAXK];
+  __shared__ int s_a;
+  __shared__ double red_d[32];
+  __shared__ unsigned long long s_kr, s_kp;
+  __shared__ bool s_last;
+  RoundState* st = p.st;
+  const int K = p.K, tid = threadIdx.x;
+  const float T = st->temperature;
+  const uint64_t seed = st->rng[0], base = st->rng[1];
+  // ---- per-row statistics from the slices, in slice order
+  if (tid < 2 * K + 1) {
+    const bool tgt = tid <= K;
+    const int r = tgt ? tid : tid - K - 1, nb = tgt ? p.nbt : p.nbd;
+    const float2* s = p.stats + (tgt ? size_t(r) * p.nbt : size_t(K + 1) * p.nbt + size_t(r) * p.nbd);
+    double M = -INFINITY;
+    for (int b = 0; b < nb; ++b) M = fmax(M, double(s[b].x));
+    double S = 0.0;
+    for (int b = 0; b < nb; ++b)
+      if (s[b].x != -INFINITY) S += double(s[b].y) * exp(double(s[b].x) - M);
+    if (tgt) {
+      sM[r] = M;
+      sS[r] = S;
+    } else {
+      dM[r] = M;
+      dS[r] = S;
+    }
+  }
+  if (tid == 0) {
+    s_kr = 0ull;
+    s_kp = 0ull;
+  }
+  __syncthreads();
+  // ---- the decisions (identical in every block)
+  if (tid == 0) {
+    int a = 0;
+    for (; a < K; ++a) {
+      const int x = st->tokens[a + 1];
+      const int row = sample_row_of(p, x);
+      const double qx = row >= 0 ? exp(double(p.zd[size_t(a) * p.Vd + row] / T) - dM[a]) / dS[a] : 0.0;
+      if (!(qx > 0.0)) break;
+      const double px = exp(double(p.zt[size_t(a) * p.V + x] / T) - sM[a]) / sS[a];
+      const double u = philox_uniform(seed, base + uint64_t(kRngAcceptStream) * kRngStreamLen + uint64_t(a));
+      const double ratio = px / qx;
+      if (!(u < (ratio < 1.0 ? ratio : 1.0))) break;
+    }
+    s_a = a;
+  }
+  __syncthreads();
+  const int a = s_a;
+  // ---- this block's slice of the residual (a < K) or bonus (a == K) draw
+  const int chunk = (p.V + gridDim.x - 1) / gridDim.x;
+  const int j0 = min(p.V, int(blockIdx.x) * chunk), j1 = min(p.V, j0 + chunk);
+  const float* zr = p.zt + size_t(a) * p.V;
+  const float* qr = a < K ? p.zd + size_t(a) * p.Vd : nullptr;
+  double mass = 0.0;
+  unsigned long long kr = 0ull, kp = 0ull;
+  for (int j = j0 + tid; j < j1; j += blockDim.x) {
+    const double pj = exp(double(zr[j] / T) - sM[a]) / sS[a];
+    double rj = pj;
+    if (qr) {
+      const int row = sample_row_of(p, j);
+      const double qj = row >= 0 ? exp(double(qr[row] / T) - dM[a]) / dS[a] : 0.0;
+      rj = fmax(pj - qj, 0.0);
+    }
+    mass += rj;
+    const double g = philox_gumbel_d(seed, base + uint64_t(kRngResidualStream) * kRngStreamLen + uint64_t(j));
+    if (rj > 0.0) {
+      const unsigned long long k = argmax_key(float(log(rj) + g), uint32_t(j));
+      if (k > kr) kr = k;
+    }
+    if (pj > 0.0) {
+      const unsigned long long k = argmax_key(float(log(pj) + g), uint32_t(j));
+      if (k > kp) kp = k;
+    }
+  }
+  mass = warp_sum_d(mass);
+  if (tid % 32 == 0) red_d[tid / 32] = mass;
+  if (kr) atomicMax(&s_kr, kr);
+  if (kp) atomicMax(&s_kp, kp);
+  __syncthreads();
+  if (tid == 0) {
+    double m2 = 0.0;
+    for (int w = 0; w < int(blockDim.x / 32); ++w) m2 += red_d[w];
+    double* pp = p.part + size_t(blockIdx.x) * 3;
+    pp[0] = m2;
+    pp[1] = __longlong_as_double((long long)s_kr);
+    pp[2] = __longlong_as_double((long long)s_kp);
+    __threadfence();
+    s_last = atomicAdd(p.counter, 1u) == gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!s_last || tid != 0) return;
+  // ---- last block: reduce the slices in block order and commit
+  __threadfence();
+  double m_all = 0.0;
+  unsigned long long kr_all = 0ull, kp_all = 0ull;
+  for (int b = 0; b < int(gridDim.x); ++b) {
+    const double* pp = p.part + size_t(b) * 3;
+    m_all += __ldcg(pp);
+    const unsigned long long k1 = (unsigned long long)__double_as_longlong(__ldcg(pp + 1));
+    const unsigned long long k2 = (unsigned long long)__double_as_longlong(__ldcg(pp + 2));
+    if (k1 > kr_all) kr_all = k1;
+    if (k2 > kp_all) kp_all = k2;
+  }
+  const bool use_p = a < K && !(m_all > 1e-12);
+  const unsigned long long key = use_p ? kp_all : kr_all;
+  int next = key ? int(argmax_key_index(key)) : 0;
+  if (!key) raise_error(&st->err, kErrSample);
+  for (int i = 0; i < a; ++i) st->acc[i] = st->tokens[i + 1];
+  st->acc[a] = next;
+  st->a = a;
+  st->n_out = a + 1;
+  st->L_upd = a + 1;
+  st->n += a + 1;
+  st->x_n = next;
+  for (int i = 0; i < MAXKEYS; ++i) st->keys[i] = 0ull;
+  st->rng[1] = base + kRngRoundStride;
+  *p.counter = 0u;
+  if (p.out_host_view) {
+    p.out_host_view[0] = a + 1;
+    for (int i = 0; i <= a; ++i) p.out_host_view[1 + i] = st->acc[i];
+  }
 }
 
 // End of the drafter update (and of the drafter prefill): out = RMSNorm(h[L-1]) with the

@@ -464,6 +464,21 @@ GemvParams gemv_params() {
   return p;
 }
 
+// A sampled head (sampled decoding): the argmax key of row l becomes a draw from
+// softmax(z / T), T read from the device, Gumbel noise from stream `stream` + l.
+struct Pick {
+  const float* temperature = nullptr;
+  const unsigned long long* rng = nullptr;  // [seed, counter base] on the device
+  int stream = 0;
+};
+
+void apply_pick(GemvParams& p, const Pick* pk) {
+  if (!pk || !pk->temperature) return;
+  p.temperature = pk->temperature;
+  p.rng = pk->rng;
+  p.rng_stream = pk->stream;
+}
+
 XSeg xs_frag(const XIn& x, int len, bool bf16, float eps = 0.f) {
   XSeg s;
   std::memset(&s, 0, sizeof(s));
@@ -1743,7 +1758,7 @@ XIn target_stack_launch(wc_target* t, StackPlan& plan, int* err) {
 // Head over `rows` rows given as fragments (times the final norm): argmax keys and,
 // optionally, logits [rows][V].
 void target_head(wc_target* t, XIn x, int rows, const int* L_dev, int L_max, unsigned long long* keys, float* logits,
-                 int* err) {
+                 int* err, const Pick* pick = nullptr) {
   GemvParams p = gemv_params();
   p.L = rows;
   p.L_dev = L_dev;
@@ -1755,13 +1770,15 @@ void target_head(wc_target* t, XIn x, int rows, const int* L_dev, int L_max, uns
   p.ldy = t->cfg.vocab;
   p.keys = keys;
   p.err = err;
+  apply_pick(p, pick);
   prof_begin(t->ctx, PK_HEAD);
   launch_gemv(t->ctx, t->head, p);
   prof_end(t->ctx, PK_HEAD);
 }
 
 // Head over fp32 residual rows h[rows][H] (any row offset): re-packs them first.
-void target_head_rows(wc_target* t, const float* h, int rows, unsigned long long* keys, float* logits, int* err) {
+void target_head_rows(wc_target* t, const float* h, int rows, unsigned long long* keys, float* logits, int* err,
+                      const Pick* pick = nullptr) {
   PackParams p = pack_params();
   p.src = h;
   p.ld = t->cfg.hidden;
@@ -1772,7 +1789,7 @@ void target_head_rows(wc_target* t, const float* h, int rows, unsigned long long
   p.ss = t->ss_tmp;
   p.err = err;
   launch_pack(t->ctx, p, is_bf16(t->dtype), rows);
-  target_head(t, XIn{t->xf_tmp, t->ss_tmp, 1}, rows, nullptr, rows, keys, logits, err);
+  target_head(t, XIn{t->xf_tmp, t->ss_tmp, 1}, rows, nullptr, rows, keys, logits, err, pick);
 }
 
 }  // namespace
@@ -1960,6 +1977,7 @@ struct wc_drafter {
   float* norm = nullptr;
   Lin head;
   int* vocab_map = nullptr;  // restricted head row -> token id
+  int* vocab_inv = nullptr;  // token id -> restricted head row or -1 (sampled decoding)
   int head_rows = 0;
   RopeTable* rope = nullptr;
   // workspace for up to GEMV_MAXL rows
@@ -2269,7 +2287,7 @@ XIn drafter_pack_rows(wc_drafter* d, const float* x, int L, const float* w, uint
 // job (when side_y is set) writes the next chain feature RMSNorm(h) * norm as fp32 rows and
 // as fragments times layer 0's input gain, with sums of squares in ss_feat.
 void drafter_head(wc_drafter* d, XIn x, int rows, unsigned long long* keys, float* logits, const float* side_src,
-                  float* side_y, int* err) {
+                  float* side_y, int* err, const Pick* pick = nullptr) {
   const bool bf16 = is_bf16(d->dtype);
   GemvParams p = gemv_params();
   p.L = rows;
@@ -2289,6 +2307,7 @@ void drafter_head(wc_drafter* d, XIn x, int rows, unsigned long long* keys, floa
     p.side_ss = d->ss_feat;
   }
   p.err = err;
+  apply_pick(p, pick);
   gemv_prefetch(d->ctx, p, &d->layers[0].qkv);
   prof_begin(d->ctx, PK_DRAFT_HEAD);
   launch_gemv(d->ctx, d->head, p);
@@ -2394,6 +2413,7 @@ extern "C" void wc_drafter_destroy(wc_drafter* d) {
   dfree(d->norm);
   free_lin(d->head);
   dfree(d->vocab_map);
+  dfree(d->vocab_inv);
   for (void* p : {(void*)d->ws_h, (void*)d->ws_feat, (void*)d->ws_g, (void*)d->ws_qkv, (void*)d->xf_feat,
                   (void*)d->xf_post, (void*)d->xf_att, (void*)d->xf_act, (void*)d->xf_out, (void*)d->ss_feat,
                   (void*)d->ss_g, (void*)d->ss_pack, (void*)d->ws_keys})
@@ -2423,6 +2443,11 @@ extern "C" wc_status wc_drafter_restrict_vocab(wc_drafter* d, const int* ids, in
     wc_ctx* ctx = d->ctx;
     int* map = static_cast<int*>(dalloc(sizeof(int) * n));
     CUDA_TRY(cudaMemcpy(map, ids, sizeof(int) * n, cudaMemcpyHostToDevice));
+    // token -> row (the scatter of spec.py:239-249; a repeated id keeps its last row)
+    std::vector<int> inv(size_t(d->cfg.vocab), -1);
+    for (int i = 0; i < n; ++i) inv[size_t(ids[i])] = i;
+    int* dinv = static_cast<int*>(dalloc(sizeof(int) * inv.size()));
+    CUDA_TRY(cudaMemcpy(dinv, inv.data(), sizeof(int) * inv.size(), cudaMemcpyHostToDevice));
     Lin nh = make_lin(d->dtype, n, {d->cfg.hidden}, 1);
     if (d->dtype == WC_BF16) {
       const int KT = nh.Kp / 16;
@@ -2437,6 +2462,7 @@ extern "C" wc_status wc_drafter_restrict_vocab(wc_drafter* d, const int* ids, in
     free_lin(d->head);  // the full head is dropped, as in drafter.py:217-229
     d->head = nh;
     d->vocab_map = map;
+    d->vocab_inv = dinv;
     d->head_rows = n;
   });
 }
@@ -2528,6 +2554,32 @@ extern "C" wc_status wc_drafter_head_argmax(wc_drafter* d, const float* out, int
   });
 }
 
+// ============================================================================ sampled decoding
+
+namespace {
+
+// probs_from_logits (sampling.py:39-55) on the device covers the temperature; top-k and
+// top-p warping are refused rather than silently ignored.
+bool sampling_on(const wc_sampling_params* sp) {
+  if (!sp || !(sp->temperature > 0.f)) return false;
+  if (sp->top_k > 0) fail(WC_ERR_UNSUPPORTED, "sampled decoding on the device: top_k is not supported yet");
+  if (sp->top_p < 1.f) fail(WC_ERR_UNSUPPORTED, "sampled decoding on the device: top_p is not supported yet");
+  return true;
+}
+
+// RoundState's random state and temperature: seed, counter base 0 (the first token's draw)
+void seed_rounds(wc_ctx* ctx, RoundState* st, const wc_sampling_params* sp, bool on) {
+  struct {
+    unsigned long long rng[2];
+    float temperature;
+    int pad;
+  } v{{on ? (unsigned long long)sp->seed : 0ull, 0ull}, on ? sp->temperature : 0.f, 0};
+  static_assert(sizeof(v) == sizeof(RoundState) - offsetof(RoundState, rng), "RoundState tail layout");
+  CUDA_TRY(cudaMemcpyAsync(st->rng, &v, sizeof(v), cudaMemcpyHostToDevice, ctx->stream));
+}
+
+}  // namespace
+
 // ============================================================================ decoder
 
 struct wc_decoder {
@@ -2554,9 +2606,28 @@ struct wc_decoder {
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   float last_ms = 0.f;
   std::map<int, std::unique_ptr<StackPlan>> stack_plans;  // verify layer stacks per chain length
+  // sampled decoding (temperature > 0, set by the prefill): the round's logits, their softmax
+  // slices and the acceptance kernel's partials
+  bool sampled = false;
+  float* zt = nullptr;       // [max_k + 1][V] target logits of the verify rows
+  float* zd = nullptr;       // [max_k][head rows] draft logits
+  float2* zstats = nullptr;  // logit_stats_kernel output
+  double* apart = nullptr;   // [kAcceptBlocks][3]
+  unsigned* acount = nullptr;
+  int nbt = 0, nbd = 0;      // softmax slices per target / draft row
+  int zd_rows = 0;           // draft head rows zd was sized for
+  // wc_decoder_save_state snapshot
+  RoundState* saved_st = nullptr;
+  unsigned char* saved_root = nullptr;
+  size_t root_bytes[5] = {};
+  int saved_host_n = -1;
 };
 
 namespace {
+
+constexpr int kAcceptBlocks = 148;      // acceptance draw: one slice of the vocabulary per SM
+constexpr int kStatsSlice = 4096;       // logits per softmax slice
+constexpr int kSampledGraphKey = 1000;  // graph key offset of sampled rounds
 
 void launch_finish(wc_decoder* dec, const int* L_dev, int L_static, bool advance) {
   wc_drafter* d = dec->d;
@@ -2589,14 +2660,21 @@ void build_round(wc_decoder* dec, int K) {
   RoundState* st = dec->st;
   int* err = &st->err;
   const bool post = d->cfg.post_norm != 0;
-  // ---- draft chain (spec.py:344-350): K heads, K-1 drafter layer passes
+  const bool smp = dec->sampled;
+  Pick pick;
+  pick.temperature = &st->temperature;
+  pick.rng = st->rng;
+  // ---- draft chain (spec.py:344-350): K heads, K-1 drafter layer passes; sampled rounds
+  // draw d_k from softmax(z_k / T) in the head's epilogue and keep z_k for the acceptance
   XIn head_in{dec->xf_root, nullptr, 0};  // root_out is already normalised
   const Lin& ld = d->layers.back().down;
   for (int k = 0; k < K; ++k) {
     const bool more = k < K - 1;
+    pick.stream = k;
     // with post-norm the next feature is RMSNorm(h) * norm: the head's side job makes it
-    drafter_head(d, head_in, 1, st->keys + k, nullptr, (k > 0 && post && more) ? d->ws_h : nullptr,
-                 (k > 0 && post && more) ? d->ws_feat : nullptr, err);
+    drafter_head(d, head_in, 1, st->keys + k, smp ? dec->zd + size_t(k) * d->head_rows : nullptr,
+                 (k > 0 && post && more) ? d->ws_h : nullptr, (k > 0 && post && more) ? d->ws_feat : nullptr, err,
+                 smp ? &pick : nullptr);
     if (!more) break;
     XIn fin;
     const float* feat;
@@ -2643,10 +2721,42 @@ void build_round(wc_decoder* dec, int K) {
   const XIn hx = (sp_it != dec->stack_plans.end() && sp_it->second->ready)
                      ? target_stack_launch(t, *sp_it->second, err)
                      : target_layers(t, dec->tkv, rv, in0, t->ws_h, &to, err);
-  target_head(t, hx, K + 1, nullptr, K + 1, st->keys + K, nullptr, err);
-  // ---- acceptance + chain compaction (spec.py:357-362)
-  launch_ex(ctx, "accept", accept_chain_kernel, dim3(1), dim3(32), 0, true, 1, st, K, (const int*)nullptr,
-            dec->out_dev);
+  target_head(t, hx, K + 1, nullptr, K + 1, st->keys + K, smp ? dec->zt : nullptr, err);
+  // ---- acceptance + chain compaction (spec.py:357-362; sampled: spec.py:321-324 with
+  // verify_tree_stochastic on the chain)
+  if (smp) {
+    StatsParams sp;
+    sp.z1 = dec->zt;
+    sp.R1 = K + 1;
+    sp.V1 = t->cfg.vocab;
+    sp.nb1 = dec->nbt;
+    sp.z2 = dec->zd;
+    sp.R2 = K;
+    sp.V2 = d->head_rows;
+    sp.nb2 = dec->nbd;
+    sp.temperature = &st->temperature;
+    sp.out = dec->zstats;
+    launch_ex(ctx, "logit stats", logit_stats_kernel, dim3((K + 1) * dec->nbt + K * dec->nbd), dim3(256), 0, true, 1,
+              sp);
+    SampleAcceptParams ap;
+    ap.st = st;
+    ap.K = K;
+    ap.zt = dec->zt;
+    ap.V = t->cfg.vocab;
+    ap.zd = dec->zd;
+    ap.Vd = d->head_rows;
+    ap.vocab_inv = d->vocab_inv;
+    ap.stats = dec->zstats;
+    ap.nbt = dec->nbt;
+    ap.nbd = dec->nbd;
+    ap.part = dec->apart;
+    ap.counter = dec->acount;
+    ap.out_host_view = dec->out_dev;
+    launch_ex(ctx, "accept sampled", accept_sampled_kernel, dim3(kAcceptBlocks), dim3(256), 0, true, 1, ap);
+  } else {
+    launch_ex(ctx, "accept", accept_chain_kernel, dim3(1), dim3(32), 0, true, 1, st, K, (const int*)nullptr,
+              dec->out_dev);
+  }
   // ---- drafter update on the accepted rows (spec.py:363, 366-374)
   XIn tx[3];
   for (int f = 0; f < 3; ++f) tx[f] = target_tap_stats(t, f, d->xf_tap[f], K + 1);
@@ -2665,15 +2775,18 @@ void build_round(wc_decoder* dec, int K) {
   launch_finish(dec, &st->L_upd, K + 1, true);
 }
 
+int graph_key(const wc_decoder* dec, int K) { return K + (dec->sampled ? kSampledGraphKey : 0); }
+
 std::pair<cudaGraphExec_t, uint64_t>& round_graph(wc_decoder* dec, int K, bool profiled = false) {
   auto& store = profiled ? dec->prof_graphs : dec->graphs;
-  auto it = store.find(K);
+  const int gk = graph_key(dec, K);
+  auto it = store.find(gk);
   if (it != store.end()) return it->second;
   wc_ctx* ctx = dec->ctx;
   CUDA_TRY(cudaStreamSynchronize(ctx->stream));
   if (profiled) {
-    dec->profilers[K] = std::make_unique<Profiler>();
-    ctx->prof = dec->profilers[K].get();
+    dec->profilers[gk] = std::make_unique<Profiler>();
+    ctx->prof = dec->profilers[gk].get();
   }
   {  // the verify's layer stack is built and uploaded before capture
     wc_target* t = dec->t;
@@ -2715,8 +2828,8 @@ std::pair<cudaGraphExec_t, uint64_t>& round_graph(wc_decoder* dec, int K, bool p
   const cudaError_t e = cudaGraphInstantiate(&exec, g, 0);
   cudaGraphDestroy(g);
   if (e != cudaSuccess) fail(WC_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
-  store[K] = {exec, ctx->capture_launches};
-  return store[K];
+  store[gk] = {exec, ctx->capture_launches};
+  return store[gk];
 }
 
 void check_state_error(wc_decoder* dec) {
@@ -2768,6 +2881,23 @@ extern "C" wc_status wc_decoder_create(wc_target* t, wc_drafter* d, int max_cont
     dec->xf_root = xf_alloc(bf16, H);
     dec->xf_fb = xf_alloc(bf16, H);
     dec->ss_fb = ss_alloc(ctx);
+    dec->root_bytes[0] = sizeof(float) * H;
+    dec->root_bytes[1] = sizeof(float) * H;
+    dec->root_bytes[2] = size_t(GEMV_MAXL) * xf_width(bf16, H) * 4;
+    dec->root_bytes[3] = dec->root_bytes[2];
+    dec->root_bytes[4] = sizeof(float) * max_parts(ctx) * 16;
+    {  // sampled decoding buffers
+      const int V = t->cfg.vocab, Vd = d->head_rows;
+      dec->nbt = (V + kStatsSlice - 1) / kStatsSlice;
+      dec->nbd = (Vd + kStatsSlice - 1) / kStatsSlice;
+      dec->zd_rows = Vd;
+      dec->zt = static_cast<float*>(dalloc(sizeof(float) * size_t(max_k + 1) * V));
+      dec->zd = static_cast<float*>(dalloc(sizeof(float) * size_t(max_k) * Vd));
+      dec->zstats = static_cast<float2*>(dalloc(sizeof(float2) * size_t((max_k + 1) * dec->nbt + max_k * dec->nbd)));
+      dec->apart = static_cast<double*>(dalloc(sizeof(double) * 3 * kAcceptBlocks));
+      dec->acount = static_cast<unsigned*>(dalloc(sizeof(unsigned)));
+      CUDA_TRY(cudaMemset(dec->acount, 0, sizeof(unsigned)));
+    }
     CUDA_TRY(cudaEventCreate(&dec->ev0));
     CUDA_TRY(cudaEventCreate(&dec->ev1));
     *out = dec.release();
@@ -2785,7 +2915,8 @@ extern "C" void wc_decoder_destroy(wc_decoder* dec) {
   dfree(dec->out_dev);
   if (dec->out_host) cudaFreeHost(dec->out_host);
   for (void* p : {(void*)dec->root_out, (void*)dec->root_fb, (void*)dec->xf_root, (void*)dec->xf_fb,
-                  (void*)dec->ss_fb, (void*)dec->taps})
+                  (void*)dec->ss_fb, (void*)dec->taps, (void*)dec->zt, (void*)dec->zd, (void*)dec->zstats,
+                  (void*)dec->apart, (void*)dec->acount, (void*)dec->saved_st, (void*)dec->saved_root})
     dfree(p);
   if (dec->ev0) cudaEventDestroy(dec->ev0);
   if (dec->ev1) cudaEventDestroy(dec->ev1);
@@ -2797,7 +2928,11 @@ namespace {
 // spec.py:129-141 / spec.cpp:61-84: target forward on the prompt (taps kept), first token,
 // drafter forward on prompt[1:] + [first] with the fused taps.
 int decoder_prefill_impl(wc_decoder* dec, const int* prompt, int n, const wc_sampling_params* sp) {
-  if (sp && sp->temperature > 0.f) fail(WC_ERR_UNSUPPORTED, "sampled decoding (temperature > 0) is not built yet");
+  const bool smp = sampling_on(sp);
+  if (smp && dec->d->cfg.vocab != dec->t->cfg.vocab)
+    fail(WC_ERR_UNSUPPORTED, "sampled decoding needs the drafter and target vocabularies to match");
+  if (dec->d->head_rows != dec->zd_rows)
+    fail(WC_ERR_INVALID, "the drafter head changed after the decoder was created (restrict the vocabulary first)");
   if (n < 1) fail(WC_ERR_INVALID, "empty prompt");
   if (n + dec->max_k + 1 > dec->tkv->cap) fail(WC_ERR_CAPACITY, "prompt longer than the decoder context");
   wc_ctx* ctx = dec->ctx;
@@ -2820,8 +2955,12 @@ int decoder_prefill_impl(wc_decoder* dec, const int* prompt, int n, const wc_sam
   CUDA_TRY(cudaMemcpyAsync(d_tok, prompt, sizeof(int) * n, cudaMemcpyHostToDevice, ctx->stream));
   CUDA_TRY(cudaMemsetAsync(dec->st, 0, offsetof(RoundState, forced), ctx->stream));
   CUDA_TRY(cudaMemsetAsync(dec->st->keys, 0, sizeof(dec->st->keys), ctx->stream));
+  seed_rounds(ctx, dec->st, sp, smp);
   int* err = &dec->st->err;
   const size_t tstride = size_t(n) * Ht;
+  Pick pick;  // _sample_target (spec.py:143-147) of the first token
+  pick.temperature = &dec->st->temperature;
+  pick.rng = dec->st->rng;
   for (int r0 = 0; r0 < n; r0 += GEMV_MAXL) {
     const int rows = std::min(GEMV_MAXL, n - r0);
     Rows r;
@@ -2833,7 +2972,8 @@ int decoder_prefill_impl(wc_decoder* dec, const int* prompt, int n, const wc_sam
     to.rows = dec->taps + size_t(r0) * Ht;
     to.stride = tstride;
     target_layers(t, dec->tkv, r, in0, t->ws_h, &to, err);
-    if (r0 + rows == n) target_head_rows(t, t->ws_h + size_t(rows - 1) * Ht, 1, dec->st->keys, nullptr, err);
+    if (r0 + rows == n)
+      target_head_rows(t, t->ws_h + size_t(rows - 1) * Ht, 1, dec->st->keys, nullptr, err, smp ? &pick : nullptr);
   }
   int first = 0;
   {
@@ -2867,10 +3007,15 @@ int decoder_prefill_impl(wc_decoder* dec, const int* prompt, int n, const wc_sam
   init.x_n = first;
   CUDA_TRY(cudaMemcpyAsync(dec->st, &init, offsetof(RoundState, forced), cudaMemcpyHostToDevice, ctx->stream));
   CUDA_TRY(cudaMemsetAsync(dec->st->keys, 0, sizeof(dec->st->keys), ctx->stream));
+  if (smp) {  // rounds draw from the next counter block
+    const unsigned long long base = kRngRoundStride;
+    CUDA_TRY(cudaMemcpyAsync(&dec->st->rng[1], &base, sizeof(base), cudaMemcpyHostToDevice, ctx->stream));
+  }
   CUDA_TRY(cudaStreamSynchronize(ctx->stream));
   check_state_error(dec);
   dec->host_n = n;
   dec->prefilled = true;
+  dec->sampled = smp;
   return first;
 }
 
@@ -2959,7 +3104,7 @@ extern "C" wc_status wc_decoder_profile_round(wc_decoder* dec, int k, int* out_t
   if (!dec || !out_tokens || !out_n || !ms_sum || !counts) return WC_ERR_INVALID;
   return guard(dec->ctx, [&] {
     *out_n = decoder_round_impl(dec, k, out_tokens, true);
-    Profiler* pr = dec->profilers.at(k).get();
+    Profiler* pr = dec->profilers.at(graph_key(dec, k)).get();
     for (int i = 0; i < PK_SLOTS; ++i) {
       ms_sum[i] = 0.f;
       counts[i] = 0;
@@ -2991,6 +3136,74 @@ extern "C" wc_status wc_decoder_last_round_ms(const wc_decoder* dec, float* ms) 
   return WC_OK;
 }
 
+// ---- test and measurement support: device-state snapshots and the last sampled round's logits
+namespace {
+void* root_buf(wc_decoder* dec, int i) {
+  void* b[5] = {dec->root_out, dec->root_fb, dec->xf_root, dec->xf_fb, dec->ss_fb};
+  return b[i];
+}
+}  // namespace
+
+extern "C" wc_status wc_decoder_save_state(wc_decoder* dec) {
+  if (!dec) return WC_ERR_INVALID;
+  return guard(dec->ctx, [&] {
+    if (!dec->prefilled) fail(WC_ERR_INVALID, "prefill before saving the decoder state");
+    wc_ctx* ctx = dec->ctx;
+    size_t total = 0;
+    for (size_t b : dec->root_bytes) total += b;
+    if (!dec->saved_st) {
+      dec->saved_st = static_cast<RoundState*>(dalloc(sizeof(RoundState)));
+      dec->saved_root = static_cast<unsigned char*>(dalloc(total));
+    }
+    CUDA_TRY(cudaMemcpyAsync(dec->saved_st, dec->st, sizeof(RoundState), cudaMemcpyDeviceToDevice, ctx->stream));
+    size_t off = 0;
+    for (int i = 0; i < 5; ++i) {
+      CUDA_TRY(cudaMemcpyAsync(dec->saved_root + off, root_buf(dec, i), dec->root_bytes[i], cudaMemcpyDeviceToDevice,
+                               ctx->stream));
+      off += dec->root_bytes[i];
+    }
+    CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    dec->saved_host_n = dec->host_n;
+  });
+}
+
+extern "C" wc_status wc_decoder_restore_state(wc_decoder* dec) {
+  if (!dec) return WC_ERR_INVALID;
+  return guard(dec->ctx, [&] {
+    if (dec->saved_host_n < 0) fail(WC_ERR_INVALID, "no saved decoder state");
+    wc_ctx* ctx = dec->ctx;
+    // everything up to the random state; the counter base keeps running
+    CUDA_TRY(cudaMemcpyAsync(dec->st, dec->saved_st, offsetof(RoundState, rng), cudaMemcpyDeviceToDevice,
+                             ctx->stream));
+    size_t off = 0;
+    for (int i = 0; i < 5; ++i) {
+      CUDA_TRY(cudaMemcpyAsync(root_buf(dec, i), dec->saved_root + off, dec->root_bytes[i], cudaMemcpyDeviceToDevice,
+                               ctx->stream));
+      off += dec->root_bytes[i];
+    }
+    CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    dec->host_n = dec->saved_host_n;
+  });
+}
+
+extern "C" wc_status wc_decoder_round_logits(wc_decoder* dec, int k, float* zt, float* zd, int* tokens,
+                                             unsigned long long* rng) {
+  if (!dec) return WC_ERR_INVALID;
+  return guard(dec->ctx, [&] {
+    if (!dec->sampled) fail(WC_ERR_INVALID, "the last rounds were not sampled");
+    if (k < 1 || k > dec->max_k) fail(WC_ERR_INVALID, "chain length outside 1..max_k");
+    wc_ctx* ctx = dec->ctx;
+    CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    if (zt) CUDA_TRY(cudaMemcpy(zt, dec->zt, sizeof(float) * size_t(k + 1) * dec->t->cfg.vocab, cudaMemcpyDeviceToHost));
+    if (zd) CUDA_TRY(cudaMemcpy(zd, dec->zd, sizeof(float) * size_t(k) * dec->d->head_rows, cudaMemcpyDeviceToHost));
+    if (tokens) CUDA_TRY(cudaMemcpy(tokens, dec->st->tokens, sizeof(int) * (k + 1), cudaMemcpyDeviceToHost));
+    if (rng) {
+      CUDA_TRY(cudaMemcpy(rng, dec->st->rng, sizeof(unsigned long long) * 2, cudaMemcpyDeviceToHost));
+      rng[1] -= kRngRoundStride;  // the base the last round drew from
+    }
+  });
+}
+
 // ============================================================================ autoregressive baseline
 
 namespace {
@@ -3000,6 +3213,7 @@ __global__ void ar_advance_kernel(RoundState* st, int* out) {
   st->x_n = tok;
   st->n += 1;
   st->keys[0] = 0ull;
+  st->rng[1] += kRngRoundStride;  // sampled steps: the next step's counter block
   out[0] = tok;
 }
 }  // namespace
@@ -3009,7 +3223,7 @@ extern "C" wc_status wc_generate_autoregressive(wc_target* t, const int* prompt,
                                                 int max_context, int* out_tokens, int* out_n, wc_gen_stats* stats) {
   if (!t || !prompt || !out_tokens || !out_n || n < 1 || max_new < 1) return WC_ERR_INVALID;
   return guard(t->ctx, [&] {
-    if (sp && sp->temperature > 0.f) fail(WC_ERR_UNSUPPORTED, "sampled decoding (temperature > 0) is not built yet");
+    const bool smp = sampling_on(sp);
     wc_ctx* ctx = t->ctx;
     const int Ht = t->cfg.hidden;
     const int cap = std::max(max_context, n + max_new + 1);
@@ -3034,6 +3248,10 @@ extern "C" wc_status wc_generate_autoregressive(wc_target* t, const int* prompt,
       }
     } fr{{st, d_tok, d_out, h}, &exec};
     CUDA_TRY(cudaMemsetAsync(st, 0, sizeof(RoundState), ctx->stream));
+    seed_rounds(ctx, st, sp, smp);
+    Pick pick;  // spec.py:377-397 samples each step from probs_from_logits
+    pick.temperature = &st->temperature;
+    pick.rng = st->rng;
     CUDA_TRY(cudaMemcpyAsync(d_tok, prompt, sizeof(int) * n, cudaMemcpyHostToDevice, ctx->stream));
     for (int i = 0; i < n; ++i)
       if (prompt[i] < 0 || prompt[i] >= t->cfg.vocab) fail(WC_ERR_INVALID, "prompt token id out of range");
@@ -3045,7 +3263,8 @@ extern "C" wc_status wc_generate_autoregressive(wc_target* t, const int* prompt,
       r.n_add = r0;
       const XIn in0 = target_embed(t, r, d_tok + r0, nullptr, nullptr, h, &st->err);
       target_layers(t, kv.get(), r, in0, h, nullptr, &st->err);
-      if (r0 + rows == n) target_head_rows(t, h + size_t(rows - 1) * Ht, 1, st->keys, nullptr, &st->err);
+      if (r0 + rows == n)
+        target_head_rows(t, h + size_t(rows - 1) * Ht, 1, st->keys, nullptr, &st->err, smp ? &pick : nullptr);
     }
     // st->n = n - 1 so that the first advance makes it n while emitting the first token
     RoundState init{};
@@ -3077,7 +3296,7 @@ extern "C" wc_status wc_generate_autoregressive(wc_target* t, const int* prompt,
           r.n_dev = &st->n;
           const XIn in0 = target_embed(t, r, nullptr, st, nullptr, h, &st->err);
           const XIn hx = target_layers(t, kv.get(), r, in0, h, nullptr, &st->err);
-          target_head(t, hx, 1, nullptr, 1, st->keys, nullptr, &st->err);
+          target_head(t, hx, 1, nullptr, 1, st->keys, nullptr, &st->err, smp ? &pick : nullptr);
           ar_advance_kernel<<<1, 32, 0, ctx->stream>>>(st, d_out);
           check_launch(ctx, "ar advance");
         } catch (...) {

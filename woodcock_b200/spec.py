@@ -3,7 +3,7 @@ include/woodcock/spec.h; src/core/spec.cpp:235-311).
 
 State between rounds lives on the device (n = committed tokens before x_n = target
 cache size; drafter cache of real entries 0..n-1; the root drafter output). One
-greedy chain round is one CUDA-graph replay:
+chain round is one CUDA-graph replay:
 
   K drafter heads (fused argmax, rows mapped to token ids) and K-1 drafter layer
   passes -> target verification of [x_n, d_1..d_K] with tap capture -> acceptance
@@ -11,6 +11,11 @@ greedy chain round is one CUDA-graph replay:
   drafter update on the accepted rows,
 
 followed by the round's single host synchronisation, which returns the emitted tokens.
+With temperature > 0 (SamplingParams given to the prefill / generate) the same graph
+shape samples: each head draws its draft from softmax(z / T) (Gumbel-max in the
+epilogue, Philox noise) and keeps its logits; verification keeps the target logits and
+the acceptance kernel applies verify_tree_stochastic's chain rule (sampling.py:143-187)
+with a Gumbel-max draw from the residual or the bonus row.
 """
 
 from __future__ import annotations
@@ -124,7 +129,7 @@ class SpeculativeDecoder:
         self.ctx.check(lib().wc_decoder_set_forced(self.h, int_array(toks) if toks else None, len(toks)))
 
     def round(self, k: int) -> list[int]:
-        """One fused greedy chain round; returns d_1..d_a, next."""
+        """One fused chain round (sampled after a prefill with temperature > 0); returns d_1..d_a, next."""
         out = (C.c_int * (k + 1))()
         n = C.c_int()
         self.ctx.check(lib().wc_decoder_round(self.h, k, out, C.byref(n)))
@@ -144,6 +149,27 @@ class SpeculativeDecoder:
                 for i, name in enumerate(self.PROFILE_KINDS)}
         return list(out[: n.value]), prof
 
+    # ---------------------------------------------------------------- test / measurement support
+    def save_state(self) -> None:
+        """Snapshot the device state (round state, chain root) after a prefill or round."""
+        self.ctx.check(lib().wc_decoder_save_state(self.h))
+
+    def restore_state(self) -> None:
+        """Back to the snapshot; the random counter keeps running, so replays draw afresh."""
+        self.ctx.check(lib().wc_decoder_restore_state(self.h))
+
+    def round_logits(self, k: int) -> dict:
+        """The last sampled round's target logits [k+1][V], draft logits [k][head rows], verify
+        tokens [x_n, d_1..d_k] and (seed, counter base)."""
+        V = self.t.cfg.vocab
+        Vd = self.d.head_rows
+        zt = np.empty((k + 1, V), dtype=np.float32)
+        zd = np.empty((k, Vd), dtype=np.float32)
+        toks = (C.c_int * (k + 1))()
+        rng = (C.c_uint64 * 2)()
+        self.ctx.check(lib().wc_decoder_round_logits(self.h, k, zt.ctypes.data, zd.ctypes.data, toks, rng))
+        return {"zt": zt, "zd": zd, "tokens": list(toks), "seed": int(rng[0]), "base": int(rng[1])}
+
     def last_round_ms(self) -> float:
         ms = C.c_float()
         self.ctx.check(lib().wc_decoder_last_round_ms(self.h, C.byref(ms)))
@@ -154,8 +180,8 @@ class SpeculativeDecoder:
                  stop_on_eos: bool = True) -> tuple[list[int], GenStats]:
         """spec.py:151-212: returns (tokens, GenStats)."""
         chain = isinstance(self.policy, StaticPolicy) and self.policy.width == 1
-        if not sp.greedy or not chain:
-            raise WcValueError(WC_ERR_UNSUPPORTED, "only greedy chain policies run on the device round so far")
+        if not chain:
+            raise WcValueError(WC_ERR_UNSUPPORTED, "only chain policies run on the device round so far")
         st = GenStats(prompt_tokens=len(prompt), fused=True)
         eos = self.t.eos_token_ids if stop_on_eos else set()
         t0 = time.perf_counter()
@@ -167,7 +193,7 @@ class SpeculativeDecoder:
         forced_active = False
         while len(out) < max_new_tokens and x_n not in eos:
             ta = time.perf_counter()
-            k = self.policy.plan(context_len=n, stochastic=False).max_depth
+            k = self.policy.plan(context_len=n, stochastic=not sp.greedy).max_depth
             if self.forced is not None:
                 self.set_forced(self.forced(st.rounds, k, len(out)))
                 forced_active = True
