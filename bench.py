@@ -51,8 +51,9 @@ def parse():
     ap.add_argument("--accept", type=int, default=2, help="drafts accepted per round (oracle-drafter mode)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--out", default=None, help="also write the JSON line here")
-    ap.add_argument("--workload", choices=["c3", "c4"], default="c3",
-                    help="c3: the headline greedy round (default); c4: Qwen3-4B sampled round at T = 1.0")
+    ap.add_argument("--workload", choices=["c3", "c4", "c5"], default="c3",
+                    help="c3: the headline greedy round (default); c4: Qwen3-4B sampled round at T = 1.0; "
+                         "c5: batched tree verification + compaction, 64 requests x 4096 context")
     ap.add_argument("--chi2", type=int, default=0,
                     help="c4: also draw this many first tokens from one replayed state and test their law")
     ap.add_argument("--profile-rounds", type=int, default=0,
@@ -68,8 +69,10 @@ def peaks() -> dict:
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
         d = json.loads(p.read_text())
-        return {"hbm_gbs": float(d["hbm_gbs"]), "source": "measured (MEASURED_PEAKS.json)"}
-    return {"hbm_gbs": 6650.0, "source": "fallback"}
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d.get("bf16_tflops", 1590.0)),
+                "bf16_tflops_sustained": float(d.get("bf16_tflops_sustained", 1400.0)),
+                "source": "measured (MEASURED_PEAKS.json)"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -585,6 +588,180 @@ def bench_c4(a):
             Path(a.out).write_text(s + "\n")
 
 
+# ----------------------------------------------------------------------------- C5: batched tree verify
+
+C5_LEVELS = [1, 4, 8, 8, 6, 3, 2]  # nodes per depth: 32 nodes, depth 6
+
+
+def c5_tree(rng, vocab):
+    """A 32-node depth-6 draft tree: each level's nodes hang under seeded parents of the level
+    above (the shape of top-k branching); tokens seeded uniform ids."""
+    parents, levels, nid = [-1], [[0]], 1
+    for cnt in C5_LEVELS[1:]:
+        prev = levels[-1]
+        lv = []
+        for j in range(cnt):
+            parents.append(prev[j % len(prev)] if j < len(prev) else int(rng.choice(prev)))
+            lv.append(nid)
+            nid += 1
+        levels.append(lv)
+    tokens = [int(x) for x in rng.integers(0, vocab, len(parents))]
+    return tokens, parents
+
+
+def c5_path(rng, parents, mean_len=3.0):
+    """Accepted path: length ~ Geometric(1 / mean) capped by the tree, descending through seeded
+    children from the root; returns keep = [0] + path."""
+    children = [[] for _ in parents]
+    for v, p in enumerate(parents):
+        if p >= 0:
+            children[p].append(v)
+    want = int(rng.geometric(1.0 / mean_len))
+    keep, v = [0], 0
+    while len(keep) <= want and children[v]:
+        v = int(rng.choice(children[v]))
+        keep.append(v)
+    return keep
+
+
+def bench_c5(a):
+    """Qwen3-1.7B architecture bf16, 64 independent requests per GPU, each with
+    4096 committed context rows (seeded synthetic K/V) and a 32-node depth-6 draft tree per round;
+    one batched verify (tcgen05 GEMMs, tree-masked attention), accepted paths drawn from a seeded
+    geometric distribution (mean 3) and compacted in place in the target and drafter caches.
+    value = emitted tokens (accepted + 1 per request) / device time of verify + commit."""
+    import numpy as np
+    import torch
+
+    from woodcock_b200 import Target
+    from woodcock_b200 import synthetic as syn
+    from woodcock_b200.batch import BatchVerifier
+
+    rank, world, local = dist_info()
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+
+        dist.init_process_group("gloo", timeout=timedelta(seconds=900))
+    torch.cuda.set_device(local)
+    ts = syn.Q17_TARGET
+    nreq, ctx0, nodes = 64, 4096, sum(C5_LEVELS)
+    t0 = time.time()
+    dev = f"cuda:{local}"
+    t = Target.from_weights(ts.hf_config(), syn.device_weight_stream(syn.target_tensor_specs(ts), 0, dev),
+                            feature_layers=[2, 14, 26], dtype="bf16", device=local)
+    rounds_total = a.warmup + a.steps + 2
+    cap = ctx0 + nodes + 8 * rounds_total
+    bv = BatchVerifier(t, nreq, nodes, cap, drafter_cache=(1, ts.kv_heads, ts.head_dim))
+    bv.fill_synthetic(nreq, ctx0, seed=1234 + rank)
+    setup_s = time.time() - t0
+    rng = np.random.default_rng(100 + rank)
+    stream = t.ctx.stream
+
+    def one_round(timed):
+        trees = [c5_tree(rng, ts.vocab) for _ in range(nreq)]
+        tok = np.array([x[0] for x in trees], dtype=np.int32)
+        par = np.array([x[1] for x in trees], dtype=np.int32)
+        keeps = [c5_path(rng, x[1]) for x in trees]
+        lens = bv.lens(nreq)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        w0 = time.perf_counter()
+        e0.record(stream)
+        bv.verify(tok, par)
+        bv.commit(keeps)
+        e1.record(stream)
+        e1.synchronize()
+        wall = time.perf_counter() - w0
+        return e0.elapsed_time(e1), wall, sum(len(k) for k in keeps), lens
+
+    for _ in range(a.warmup):
+        one_round(False)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ms, walls, toks, bytes_total = [], [], 0, 0.0
+    kvrow = ts.layers * 2 * ts.kv_heads * ts.head_dim * 2
+    from woodcock_b200 import roofline as rl
+
+    tp = rl._target_params(ts)
+    wbytes = (tp["layers"] + tp["head"]) * 2
+    with ClockSampler(local) as clk:
+        for _ in range(a.steps):
+            m_, w_, k_, lens = one_round(True)
+            ms.append(m_)
+            walls.append(w_)
+            toks += k_
+            bytes_total += wbytes + sum(n + nodes for n in lens) * kvrow
+        torch.cuda.synchronize()
+    timed_ms, wall_s, tok_total = float(sum(ms)), float(sum(walls)), float(toks)
+    if world > 1:
+        x = torch.tensor([timed_ms, wall_s], dtype=torch.float64)
+        dist.all_reduce(x, op=dist.ReduceOp.MAX)
+        timed_ms, wall_s = float(x[0]), float(x[1])
+        y = torch.tensor([tok_total], dtype=torch.float64)
+        dist.all_reduce(y, op=dist.ReduceOp.SUM)
+        tok_total = float(y[0])
+    # kernel classes of one more round, timed one by one
+    trees = [c5_tree(rng, ts.vocab) for _ in range(nreq)]
+    _, prof = bv.verify_profiled(np.array([x[0] for x in trees]), np.array([x[1] for x in trees]))
+    bv.commit([[0] for _ in range(nreq)])
+    M = nreq * nodes
+    H, I, Dq = ts.hidden, ts.intermediate, ts.heads * ts.head_dim
+    flops = {"qkv_gemm": 2 * M * H * (ts.heads + 2 * ts.kv_heads) * ts.head_dim * ts.layers,
+             "o_gemm": 2 * M * Dq * H * ts.layers, "gate_up_gemm": 2 * M * H * 2 * I * ts.layers,
+             "down_gemm": 2 * M * I * H * ts.layers, "head_gemm": 2 * M * H * ts.vocab}
+    pk = peaks()
+    kernels = {}
+    for k, v in prof.items():
+        e = {"total_ms": v["total_ms"], "launches": v["launches"]}
+        if k in flops and v["total_ms"] > 0:
+            e["tflops"] = flops[k] / (v["total_ms"] / 1e3) / 1e12
+            e["frac_of_bf16_peak"] = e["tflops"] / pk["bf16_tflops"] if pk.get("bf16_tflops") else None
+        if k == "tree_attention" and v["total_ms"] > 0:
+            kv_bytes = sum(n + nodes for n in bv.lens(nreq)) * kvrow
+            e["gbs"] = kv_bytes / (v["total_ms"] / 1e3) / 1e9
+            e["frac_of_hbm_peak"] = e["gbs"] / pk["hbm_gbs"]
+        kernels[k] = e
+    top = max(kernels, key=lambda k: kernels[k]["total_ms"])
+    te = kernels[top]
+    if "gbs" in te:
+        roof = {"bound": "hbm", "kernel": top, "achieved": te["gbs"], "peak": pk["hbm_gbs"], "unit": "GB/s",
+                "frac": te["frac_of_hbm_peak"], "traffic": None}
+    else:
+        roof = {"bound": "tensor", "kernel": top, "achieved": te["tflops"], "peak": pk["bf16_tflops"],
+                "unit": "TFLOP/s", "frac": te.get("frac_of_bf16_peak"), "traffic": None}
+    gemm_flops = sum(flops.values())
+    ideal_ms = max(gemm_flops / (pk.get("bf16_tflops", 1590) * 1e12), 0) * 1e3 + \
+        (bytes_total / a.steps) / (pk["hbm_gbs"] * 1e9) * 1e3
+    line = {"metric": "batched tree-verify tok/s (C5)", "value": tok_total / (timed_ms / 1e3), "unit": "tok/s",
+            "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": timed_ms / a.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded random-init Qwen3-1.7B-architecture weights, seeded N(0,1) K/V prefixes, "
+                    "seeded trees and geometric accepted paths",
+            "config": {"workload": "C5: 64 requests x 4096 context, 32-node depth-6 trees, batched verify + "
+                                   "compaction (target and drafter caches)", "requests": nreq, "context": ctx0,
+                       "tree_nodes": nodes, "mean_path": 3, "tokens_per_round": toks / a.steps,
+                       "l2": "inputs larger than L2: ~34 GB of weights + KV per round"},
+            "round_ms": {"mean": statistics.mean(ms), "median": statistics.median(ms)},
+            "kernels": kernels, "roofline": roof,
+            "round_ideal_ms": ideal_ms,
+            "round_frac_of_sequential_ideal": ideal_ms / statistics.mean(ms),
+            "e2e": {"value": tok_total / wall_s, "unit": "tok/s",
+                    "h2d_bytes_per_step": nreq * nodes * 4 * 3 + nreq * 8 * 4,
+                    "d2h_bytes_per_step": nreq * nodes * 4},
+            "setup_s": setup_s}
+    if rank == 0:
+        line["clocks"] = clk.summary()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        s_ = json.dumps(line)
+        print(s_, flush=True)
+        if a.out:
+            Path(a.out).write_text(s_ + "\n")
+
+
 def main():
     a = parse()
     if a.profile_rounds:
@@ -593,6 +770,8 @@ def main():
         bench_reference(a)
     elif a.workload == "c4":
         bench_c4(a)
+    elif a.workload == "c5":
+        bench_c5(a)
     else:
         bench_ours(a)
 

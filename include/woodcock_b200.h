@@ -269,6 +269,47 @@ WC_API wc_kv* wc_decoder_drafter_cache(wc_decoder* dec);
  * state restored between them is NOT done: callers time real rounds). Returns ms of last round. */
 WC_API wc_status wc_decoder_last_round_ms(const wc_decoder* dec, float* ms);
 
+/* ------------------------------------------------------------------ batched tree verification
+ * BASELINE config C5 (no counterpart in the reference, whose decoder runs one request): B
+ * independent requests, each verifying a draft token tree against its own KV arena, then
+ * compacting the accepted path in place (sampling.py:118-140 tree mask and greedy rule;
+ * src/cache/kv_cache.cpp:21-31 compaction). Rows are request-major; the projections are
+ * tcgen05 GEMMs (bf16 in, fp32 accumulate), attention is the tree-masked prefix attention.
+ * bf16 targets with head_dim 64 or 128; nodes x (heads / kv_heads) <= 64. */
+typedef struct wc_batch wc_batch;
+/* Row-major GEMM copies of the target's weights are made here (their bytes again). The
+ * drafter cache (drafter_layers = 0: none) is only compacted alongside the target's. */
+WC_API wc_status wc_batch_create(wc_target* t, int max_requests, int max_nodes, int capacity, int drafter_layers,
+                                 int drafter_kv_heads, int drafter_head_dim, wc_batch** out);
+WC_API void wc_batch_destroy(wc_batch* b);
+/* Request r's committed prefix: rows [0, n) of a single-request bf16 target cache. */
+WC_API wc_status wc_batch_set_prefix(wc_batch* b, int r, const wc_kv* src, int n);
+/* Requests [0, nreq): n committed rows of seeded N(0, 1) bf16 K/V (timing workloads). */
+WC_API wc_status wc_batch_fill_synthetic(wc_batch* b, int nreq, int n, uint64_t seed);
+/* Verify trees of `nodes` nodes for requests [0, nreq): tokens / parents host int32
+ * [nreq][nodes] (node 0 = the request's newest committed token, parents[0] = -1, parents[i] < i),
+ * positions lens[r] + depth. Appends every node's K/V at rows lens[r] + i and writes the
+ * target's argmax per node (host int32 [nreq][nodes]); out_logits (host fp32 [nreq * nodes][V])
+ * may be NULL. */
+WC_API wc_status wc_batch_verify(wc_batch* b, int nreq, int nodes, const int* tokens, const int* parents,
+                                 int* out_argmax, float* out_logits);
+/* wc_batch_verify with CUDA events around kernel classes (no logits): ms_sum[i] / counts[i]
+ * as wc_decoder_profile_round (0 QKV GEMM, 1 tree attention, 2 O GEMM, 3 gate/up GEMM,
+ * 4 down GEMM, 5 head GEMM); arrays of 16. */
+WC_API wc_status wc_batch_verify_profiled(wc_batch* b, int nreq, int nodes, const int* tokens, const int* parents,
+                                          int* out_argmax, float* ms_sum, int* counts);
+/* Keep lists (host int32 [nreq][maxkeep], keep[r][0] = 0, increasing) with counts n_keep[r]:
+ * rows lens[r] + keep[r][i] -> lens[r] + i in the target (and drafter) caches, lens[r] += n_keep[r]. */
+WC_API wc_status wc_batch_commit(wc_batch* b, int nreq, const int* keep, const int* n_keep, int maxkeep);
+WC_API wc_status wc_batch_lens(const wc_batch* b, int nreq, int* lens);
+/* Rows [0, n) of request r's target cache at `layer` as bf16 [n][kv_heads][head_dim] (host; the arena itself
+ * is head-major, [layer][request][kv_head][capacity][head_dim]). */
+WC_API wc_status wc_batch_read_kv(wc_batch* b, int r, int layer, int n, void* k_out, void* v_out);
+/* C[M][N] (+)= A[M][K] . B[N][K]^T on the tensor cores (tcgen05): A, B bf16 row-major device
+ * pointers (16-byte aligned, K a multiple of 64), C fp32; residual (may equal C) added when set. */
+WC_API wc_status wc_gemm_bf16(wc_ctx* ctx, const void* A, const void* B, float* C, int M, int N, int K,
+                              const float* residual);
+
 #ifdef __cplusplus
 }
 #endif

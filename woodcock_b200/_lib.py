@@ -118,6 +118,16 @@ SIGNATURES = {
     "wc_decoder_target_cache": (P, [P]),
     "wc_decoder_drafter_cache": (P, [P]),
     "wc_decoder_last_round_ms": (S, [P, C.POINTER(C.c_float)]),
+    "wc_batch_create": (S, [P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(P)]),
+    "wc_batch_destroy": (None, [P]),
+    "wc_batch_set_prefix": (S, [P, C.c_int, P, C.c_int]),
+    "wc_batch_fill_synthetic": (S, [P, C.c_int, C.c_int, C.c_uint64]),
+    "wc_batch_verify": (S, [P, C.c_int, C.c_int, P, P, P, P]),
+    "wc_batch_verify_profiled": (S, [P, C.c_int, C.c_int, P, P, P, P, P]),
+    "wc_batch_commit": (S, [P, C.c_int, P, P, C.c_int]),
+    "wc_batch_lens": (S, [P, C.c_int, P]),
+    "wc_batch_read_kv": (S, [P, C.c_int, C.c_int, C.c_int, P, P]),
+    "wc_gemm_bf16": (S, [P, P, P, P, C.c_int, C.c_int, C.c_int, P]),
     "wc_decoder_save_state": (S, [P]),
     "wc_decoder_restore_state": (S, [P]),
     "wc_decoder_round_logits": (S, [P, C.c_int, P, P, I32P, C.POINTER(C.c_uint64)]),

@@ -26,6 +26,7 @@
 #include "attention.cuh"
 #include "attention_dec.cuh"
 #include "attention_mma.cuh"
+#include "batch.cuh"
 #include "common.cuh"
 #include "gemv.cuh"
 #include "host_io.h"
@@ -3329,5 +3330,585 @@ extern "C" wc_status wc_generate_autoregressive(wc_target* t, const int* prompt,
     s.rounds = m - 1;
     *out_n = m;
     if (stats) *stats = s;
+  });
+}
+
+// ============================================================================ batched tree verification
+
+namespace {
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no libcuda link).
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_tiled() {
+  static EncodeTiledFn fn = nullptr;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    const cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (e != cudaSuccess || !p || q != cudaDriverEntryPointSuccess)
+      fail(WC_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
+}
+
+// 2-D bf16 row-major [rows][K] operand, box of `box_rows` rows x 64 columns, 128-byte swizzle.
+CUtensorMap tmap_bf16(const void* base, int rows, int K, int box_rows) {
+  if (reinterpret_cast<uintptr_t>(base) % 16 || K % 8 || rows < 1 || K < 1)
+    fail(WC_ERR_INVALID, "GEMM operand: 16-byte aligned base and K a multiple of 8 required");
+  CUtensorMap m;
+  const cuuint64_t dims[2] = {cuuint64_t(K), cuuint64_t(rows)};
+  const cuuint64_t strides[1] = {cuuint64_t(K) * 2};
+  const cuuint32_t box[2] = {cuuint32_t(TC_BK), cuuint32_t(box_rows)};
+  const cuuint32_t es[2] = {1, 1};
+  const CUresult r = encode_tiled()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides,
+                                    box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) fail(WC_ERR_CUDA, "cuTensorMapEncodeTiled failed (" + std::to_string(int(r)) + ")");
+  return m;
+}
+
+bool tc_ready(wc_ctx* ctx) {
+  static std::set<int> done;
+  static std::mutex mu;
+  std::lock_guard<std::mutex> lock(mu);
+  if (done.count(ctx->device)) return true;
+  CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(gemm_tc_smem<128>())));
+  CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(gemm_tc_smem<256>())));
+  CUDA_TRY(cudaFuncSetAttribute(tree_attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(tree_attn_smem<128>())));
+  CUDA_TRY(cudaFuncSetAttribute(tree_attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(tree_attn_smem<64>())));
+  done.insert(ctx->device);
+  return true;
+}
+
+// C = A . B^T on the tensor cores; A [M][K] and B [N][K] bf16 row-major behind tensor maps.
+void launch_gemm_tc(wc_ctx* ctx, const CUtensorMap& ta, const CUtensorMap& tb, GemmTc p, int BN) {
+  tc_ready(ctx);
+  if (!p.err) p.err = ctx->d_err;
+  if (p.M < 1 || p.N < 1 || p.K < 1 || p.K % TC_BK) fail(WC_ERR_INVALID, "GEMM: K must be a multiple of 64");
+  if (p.epi == TC_SWIGLU && p.N % BN) fail(WC_ERR_INVALID, "GEMM SwiGLU: N must be a multiple of the tile");
+  const dim3 grid((p.M + TC_BM - 1) / TC_BM, (p.N + BN - 1) / BN);
+  if (BN == 256)
+    launch_ex(ctx, "gemm_tc", gemm_tc_kernel<256>, grid, dim3(TC_THREADS), gemm_tc_smem<256>(), true, 1, ta, tb, p);
+  else
+    launch_ex(ctx, "gemm_tc", gemm_tc_kernel<128>, grid, dim3(TC_THREADS), gemm_tc_smem<128>(), true, 1, ta, tb, p);
+}
+
+GemmTc gemm_tc_params(int M, int N, int K, int epi) {
+  GemmTc p;
+  std::memset(&p, 0, sizeof(p));
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.epi = epi;
+  return p;
+}
+
+// A GEMM weight: row-major bf16 copy of a projection, with its tensor map.
+struct TcWeight {
+  uint16_t* w = nullptr;
+  int rows = 0, K = 0, BN = 256;
+  CUtensorMap map;
+};
+
+TcWeight tc_weight_from(wc_ctx* ctx, const Lin& l, int BN) {
+  if (l.dtype != WC_BF16) fail(WC_ERR_UNSUPPORTED, "batched verification needs a bf16 target");
+  if (l.nseg != 1 || l.Kp % TC_BK) fail(WC_ERR_UNSUPPORTED, "GEMM weight: one input segment, K a multiple of 64");
+  TcWeight t;
+  t.rows = l.group == 2 ? 2 * l.N : l.N;
+  t.K = l.Kp;
+  t.BN = BN;
+  if (l.group == 2 && l.N % (BN / 2)) fail(WC_ERR_UNSUPPORTED, "SwiGLU GEMM weight: intermediate % (tile / 2) != 0");
+  t.w = static_cast<uint16_t*>(dalloc(size_t(t.rows) * t.K * 2));
+  detile_rows_kernel<<<grid_for(size_t(t.rows) * t.K), 256, 0, ctx->stream>>>(
+      static_cast<const uint16_t*>(l.w), l.Kp / 16, l.group, BN / 2, t.rows, t.K, t.w);
+  check_launch(ctx, "detile");
+  t.map = tmap_bf16(t.w, t.rows, t.K, BN);
+  return t;
+}
+
+}  // namespace
+
+struct wc_batch {
+  wc_ctx* ctx = nullptr;
+  wc_target* t = nullptr;
+  int B = 0, nodes_max = 0, cap = 0, M_max = 0;
+  int dl = 0, dHk = 0, dD = 0;  // drafter cache shape (compacted with the target's)
+  uint16_t *K = nullptr, *V = nullptr, *dK = nullptr, *dV = nullptr;
+  int* lens = nullptr;
+  std::vector<int> host_lens;
+  struct Layer {
+    TcWeight qkv, o, gu, down;
+  };
+  std::vector<Layer> lw;
+  TcWeight head;
+  float *h = nullptr, *qkv = nullptr, *logits = nullptr;
+  uint16_t *a = nullptr, *q = nullptr, *att = nullptr, *act = nullptr;
+  int *tok = nullptr, *par = nullptr, *dep = nullptr, *keep = nullptr, *nkeep = nullptr, *am = nullptr;
+  unsigned long long* keys = nullptr;
+  int maxkeep_alloc = 0;
+  size_t logits_rows = 0;
+};
+
+namespace {
+
+size_t batch_layer_elems(const wc_batch* b) { return size_t(b->B) * b->cap * b->t->cfg.kv_heads * b->t->cfg.head_dim; }
+
+__global__ void keys_to_ids_kernel(const unsigned long long* keys, int n, int* out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = int(argmax_key_index(keys[i]));
+}
+
+__global__ void fill_normal_bf16_kernel(uint16_t* x, size_t n, uint64_t seed) {
+  for (size_t i = blockIdx.x * size_t(blockDim.x) + threadIdx.x; i < n; i += size_t(gridDim.x) * blockDim.x) {
+    const uint4 r = philox4x32_10(i, seed);
+    // Box-Muller on two 24-bit uniforms in (0, 1)
+    const float u1 = (float(r.x >> 8) + 0.5f) * (1.0f / 16777216.0f), u2 = float(r.y >> 8) * (1.0f / 16777216.0f);
+    x[i] = f32_to_bf16_bits(sqrtf(-2.f * logf(u1)) * cospif(2.f * u2));
+  }
+}
+
+// The verify forward of rows M = nreq * nodes (tokens / parents / depths already on the
+// device): embeddings, every layer (GEMMs on the tensor cores, per-row q/k norm + RoPE +
+// K/V append at slots lens[r] + i, tree attention), final norm and head (argmax keys, and
+// fp32 logits when `logits` is set).
+void batch_forward(wc_batch* b, int nreq, int nodes, bool logits) {
+  wc_ctx* ctx = b->ctx;
+  wc_target* t = b->t;
+  const auto& c = t->cfg;
+  const int M = nreq * nodes, H = c.hidden, D = c.head_dim, Hq = c.heads, Hk = c.kv_heads, I = c.intermediate;
+  const int NQKV = (Hq + 2 * Hk) * D;
+  int* err = ctx->d_err;
+  const CUtensorMap ta_a = tmap_bf16(b->a, M, H, TC_BM);
+  const CUtensorMap ta_att = tmap_bf16(b->att, M, Hq * D, TC_BM);
+  const CUtensorMap ta_act = tmap_bf16(b->act, M, I, TC_BM);
+  for (int l = 0; l < c.layers; ++l) {
+    const TLayer& Ly = t->layers[l];
+    const wc_batch::Layer& W = b->lw[l];
+    RowNormParams rn;
+    std::memset(&rn, 0, sizeof(rn));
+    rn.x = l == 0 ? nullptr : b->h;
+    rn.tokens = l == 0 ? b->tok : nullptr;
+    rn.table = t->embed;
+    rn.vocab = c.vocab;
+    rn.h_copy = b->h;
+    rn.H = H;
+    rn.w = Ly.in_norm;
+    rn.eps = c.eps;
+    rn.out = b->a;
+    rn.M = M;
+    rn.err = err;
+    launch_ex(ctx, "row norm", row_norm_bf16_kernel, dim3(M), dim3(256), 0, true, 1, rn);
+    GemmTc g = gemm_tc_params(M, NQKV, H, TC_STORE);
+    g.c = b->qkv;
+    g.ldc = NQKV;
+    prof_begin(ctx, PK_QKV);
+    launch_gemm_tc(ctx, ta_a, W.qkv.map, g, W.qkv.BN);
+    prof_end(ctx, PK_QKV);
+    QkvPostParams qp;
+    std::memset(&qp, 0, sizeof(qp));
+    qp.qkv = b->qkv;
+    qp.nodes = nodes;
+    qp.Hq = Hq;
+    qp.Hk = Hk;
+    qp.D = D;
+    qp.lens = b->lens;
+    qp.depth = b->dep;
+    qp.q_norm = Ly.q_norm;
+    qp.k_norm = Ly.k_norm;
+    qp.eps = c.eps;
+    qp.rope = t->rope->ptr;
+    qp.max_pos = t->rope->max_pos;
+    qp.q = b->q;
+    qp.K = b->K + size_t(l) * batch_layer_elems(b);
+    qp.V = b->V + size_t(l) * batch_layer_elems(b);
+    qp.cap = b->cap;
+    qp.err = err;
+    launch_ex(ctx, "qkv post", qkv_post_kernel, dim3(M), dim3(128), 0, true, 1, qp);
+    TreeAttnParams ap;
+    std::memset(&ap, 0, sizeof(ap));
+    ap.q = b->q;
+    ap.K = qp.K;
+    ap.V = qp.V;
+    ap.cap = b->cap;
+    ap.lens = b->lens;
+    ap.parents = b->par;
+    ap.nodes = nodes;
+    ap.Hq = Hq;
+    ap.Hk = Hk;
+    ap.scale = 1.f / std::sqrt(float(D));
+    ap.out = b->att;
+    ap.err = err;
+    prof_begin(ctx, PK_ATTN);
+    if (D == 128)
+      launch_ex(ctx, "tree attention", tree_attention_kernel<128>, dim3(nreq, Hk), dim3(TA_THREADS),
+                tree_attn_smem<128>(), true, 1, ap);
+    else
+      launch_ex(ctx, "tree attention", tree_attention_kernel<64>, dim3(nreq, Hk), dim3(TA_THREADS),
+                tree_attn_smem<64>(), true, 1, ap);
+    prof_end(ctx, PK_ATTN);
+    g = gemm_tc_params(M, H, Hq * D, TC_ADD);
+    g.c = b->h;
+    g.ldc = H;
+    g.r = b->h;
+    g.ldr = H;
+    prof_begin(ctx, PK_O);
+    launch_gemm_tc(ctx, ta_att, W.o.map, g, W.o.BN);
+    prof_end(ctx, PK_O);
+    rn.x = b->h;
+    rn.tokens = nullptr;
+    rn.w = Ly.post_norm;
+    launch_ex(ctx, "row norm", row_norm_bf16_kernel, dim3(M), dim3(256), 0, true, 1, rn);
+    g = gemm_tc_params(M, 2 * I, H, TC_SWIGLU);
+    g.cb = b->act;
+    g.ldcb = I;
+    prof_begin(ctx, PK_GU);
+    launch_gemm_tc(ctx, ta_a, W.gu.map, g, W.gu.BN);
+    prof_end(ctx, PK_GU);
+    g = gemm_tc_params(M, H, I, TC_ADD);
+    g.c = b->h;
+    g.ldc = H;
+    g.r = b->h;
+    g.ldr = H;
+    prof_begin(ctx, PK_DOWN);
+    launch_gemm_tc(ctx, ta_act, W.down.map, g, W.down.BN);
+    prof_end(ctx, PK_DOWN);
+  }
+  RowNormParams rn;
+  std::memset(&rn, 0, sizeof(rn));
+  rn.x = b->h;
+  rn.H = H;
+  rn.w = t->final_norm;
+  rn.eps = c.eps;
+  rn.out = b->a;
+  rn.M = M;
+  rn.err = err;
+  launch_ex(ctx, "row norm", row_norm_bf16_kernel, dim3(M), dim3(256), 0, true, 1, rn);
+  CUDA_TRY(cudaMemsetAsync(b->keys, 0, sizeof(unsigned long long) * M, ctx->stream));
+  GemmTc g = gemm_tc_params(M, c.vocab, H, TC_ARGMAX);
+  g.keys = b->keys;
+  prof_begin(ctx, PK_HEAD);
+  launch_gemm_tc(ctx, ta_a, b->head.map, g, b->head.BN);
+  prof_end(ctx, PK_HEAD);
+  if (logits) {
+    g = gemm_tc_params(M, c.vocab, H, TC_STORE);
+    g.c = b->logits;
+    g.ldc = c.vocab;
+    launch_gemm_tc(ctx, ta_a, b->head.map, g, b->head.BN);
+  }
+  keys_to_ids_kernel<<<(M + 255) / 256, 256, 0, ctx->stream>>>(b->keys, M, b->am);
+  check_launch(ctx, "keys to ids");
+}
+
+void batch_check_tree(const int* parents, int nodes, int* depth) {
+  for (int i = 0; i < nodes; ++i) {
+    const int p = parents[i];
+    if (i == 0 ? p != -1 : (p < 0 || p >= i)) fail(WC_ERR_INVALID, "tree parents: parents[0] = -1, 0 <= parents[i] < i");
+    depth[i] = i == 0 ? 0 : depth[p] + 1;
+  }
+}
+
+}  // namespace
+
+extern "C" wc_status wc_gemm_bf16(wc_ctx* ctx, const void* A, const void* B, float* C, int M, int N, int K,
+                                  const float* residual) {
+  if (!ctx || !A || !B || !C || M < 1 || N < 1 || K < 1) return WC_ERR_INVALID;
+  return guard(ctx, [&] {
+    const CUtensorMap ta = tmap_bf16(A, M, K, TC_BM);
+    const int BN = N >= 2048 ? 256 : 128;
+    const CUtensorMap tb = tmap_bf16(B, N, K, BN);
+    GemmTc g = gemm_tc_params(M, N, K, residual ? TC_ADD : TC_STORE);
+    g.c = C;
+    g.ldc = N;
+    g.r = residual;
+    g.ldr = N;
+    launch_gemm_tc(ctx, ta, tb, g, BN);
+    check_launch(ctx, "gemm_tc");
+  });
+}
+
+extern "C" wc_status wc_batch_create(wc_target* t, int max_requests, int max_nodes, int capacity, int drafter_layers,
+                                     int drafter_kv_heads, int drafter_head_dim, wc_batch** out) {
+  if (!t || !out || max_requests < 1 || max_nodes < 1 || capacity < 2) return WC_ERR_INVALID;
+  return guard(t->ctx, [&] {
+    if (!t->finalized) fail(WC_ERR_INVALID, "target not finalized");
+    if (t->dtype != WC_BF16) fail(WC_ERR_UNSUPPORTED, "batched verification runs bf16 targets");
+    const auto& c = t->cfg;
+    if (max_nodes > TA_MAXN || max_nodes * (c.heads / c.kv_heads) > TA_MAXR)
+      fail(WC_ERR_UNSUPPORTED, "tree nodes x query heads per KV head must be <= 64");
+    if (c.head_dim != 128 && c.head_dim != 64) fail(WC_ERR_UNSUPPORTED, "batched verification: head_dim 64 or 128");
+    if (c.hidden % TC_BK || c.intermediate % 128 || (c.heads * c.head_dim) % TC_BK)
+      fail(WC_ERR_UNSUPPORTED, "batched verification: hidden, heads x head_dim multiples of 64, intermediate of 128");
+    wc_ctx* ctx = t->ctx;
+    auto b = std::make_unique<wc_batch>();
+    b->ctx = ctx;
+    b->t = t;
+    b->B = max_requests;
+    b->nodes_max = max_nodes;
+    b->cap = capacity;
+    b->M_max = max_requests * max_nodes;
+    b->dl = std::max(0, drafter_layers);
+    b->dHk = drafter_kv_heads;
+    b->dD = drafter_head_dim;
+    if (b->dl > 0 && (b->dHk < 1 || b->dD < 1 || (b->dHk * b->dD) % 8))
+      fail(WC_ERR_INVALID, "drafter cache shape");
+    struct Cleanup {
+      wc_batch* b;
+      bool armed = true;
+      ~Cleanup() {
+        if (armed) wc_batch_destroy(b);
+      }
+    } cleanup{b.get()};
+    const size_t le = batch_layer_elems(b.get());
+    b->K = static_cast<uint16_t*>(dalloc(size_t(c.layers) * le * 2));
+    b->V = static_cast<uint16_t*>(dalloc(size_t(c.layers) * le * 2));
+    if (b->dl) {
+      const size_t de = size_t(b->dl) * b->B * b->cap * b->dHk * b->dD;
+      b->dK = static_cast<uint16_t*>(dalloc(de * 2));
+      b->dV = static_cast<uint16_t*>(dalloc(de * 2));
+    }
+    b->lens = static_cast<int*>(dalloc(sizeof(int) * b->B));
+    CUDA_TRY(cudaMemset(b->lens, 0, sizeof(int) * b->B));
+    b->host_lens.assign(b->B, 0);
+    for (const TLayer& Ly : t->layers) {
+      wc_batch::Layer W;
+      W.qkv = tc_weight_from(ctx, Ly.qkv, 256);
+      W.o = tc_weight_from(ctx, Ly.o, 128);
+      W.gu = tc_weight_from(ctx, Ly.gu, 256);
+      W.down = tc_weight_from(ctx, Ly.down, 128);
+      b->lw.push_back(W);
+    }
+    b->head = tc_weight_from(ctx, t->head, 256);
+    const int M = b->M_max, H = c.hidden, NQKV = (c.heads + 2 * c.kv_heads) * c.head_dim;
+    b->h = static_cast<float*>(dalloc(sizeof(float) * size_t(M) * H));
+    b->qkv = static_cast<float*>(dalloc(sizeof(float) * size_t(M) * NQKV));
+    b->a = static_cast<uint16_t*>(dalloc(2 * size_t(M) * H));
+    b->q = static_cast<uint16_t*>(dalloc(2 * size_t(M) * c.heads * c.head_dim));
+    b->att = static_cast<uint16_t*>(dalloc(2 * size_t(M) * c.heads * c.head_dim));
+    b->act = static_cast<uint16_t*>(dalloc(2 * size_t(M) * c.intermediate));
+    for (int** pp : {&b->tok, &b->par, &b->dep, &b->am}) *pp = static_cast<int*>(dalloc(sizeof(int) * M));
+    b->keys = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * M));
+    b->maxkeep_alloc = max_nodes;
+    b->keep = static_cast<int*>(dalloc(sizeof(int) * size_t(b->B) * max_nodes));
+    b->nkeep = static_cast<int*>(dalloc(sizeof(int) * b->B));
+    CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    cleanup.armed = false;
+    *out = b.release();
+  });
+}
+
+extern "C" void wc_batch_destroy(wc_batch* b) {
+  if (!b) return;
+  cudaStreamSynchronize(b->ctx->stream);
+  for (auto& W : b->lw)
+    for (TcWeight* w : {&W.qkv, &W.o, &W.gu, &W.down}) dfree(w->w);
+  dfree(b->head.w);
+  for (void* p : {(void*)b->K, (void*)b->V, (void*)b->dK, (void*)b->dV, (void*)b->lens, (void*)b->h, (void*)b->qkv,
+                  (void*)b->logits, (void*)b->a, (void*)b->q, (void*)b->att, (void*)b->act, (void*)b->tok,
+                  (void*)b->par, (void*)b->dep, (void*)b->am, (void*)b->keys, (void*)b->keep, (void*)b->nkeep})
+    dfree(p);
+  delete b;
+}
+
+extern "C" wc_status wc_batch_set_prefix(wc_batch* b, int r, const wc_kv* src, int n) {
+  if (!b || !src || r < 0 || r >= b->B || n < 0) return WC_ERR_INVALID;
+  return guard(b->ctx, [&] {
+    const auto& c = b->t->cfg;
+    if (src->layers != c.layers || src->Hk != c.kv_heads || src->D != c.head_dim || src->dtype != WC_BF16)
+      fail(WC_ERR_INVALID, "source cache shape does not match the target");
+    if (n > src->cap || n + b->nodes_max > b->cap) fail(WC_ERR_CAPACITY, "prefix longer than the batch capacity");
+    const int D = c.head_dim, Hk = c.kv_heads;
+    for (int l = 0; l < c.layers; ++l)
+      for (int hk = 0; hk < Hk; ++hk) {  // both arenas are head-major: [Hk][capacity][D] per layer
+        const size_t dst = (size_t(l) * batch_layer_elems(b) + (size_t(r) * Hk + hk) * b->cap * D) * 2;
+        const size_t so = size_t(hk) * src->cap * D * 2;
+        CUDA_TRY(cudaMemcpyAsync(reinterpret_cast<char*>(b->K) + dst, static_cast<const char*>(src->Kl(l)) + so,
+                                 size_t(n) * D * 2, cudaMemcpyDeviceToDevice, b->ctx->stream));
+        CUDA_TRY(cudaMemcpyAsync(reinterpret_cast<char*>(b->V) + dst, static_cast<const char*>(src->Vl(l)) + so,
+                                 size_t(n) * D * 2, cudaMemcpyDeviceToDevice, b->ctx->stream));
+      }
+    b->host_lens[r] = n;
+    CUDA_TRY(cudaMemcpyAsync(b->lens + r, &b->host_lens[r], sizeof(int), cudaMemcpyHostToDevice, b->ctx->stream));
+    CUDA_TRY(cudaStreamSynchronize(b->ctx->stream));
+  });
+}
+
+extern "C" wc_status wc_batch_fill_synthetic(wc_batch* b, int nreq, int n, uint64_t seed) {
+  if (!b || nreq < 1 || nreq > b->B || n < 0) return WC_ERR_INVALID;
+  return guard(b->ctx, [&] {
+    if (n + b->nodes_max > b->cap) fail(WC_ERR_CAPACITY, "prefix longer than the batch capacity");
+    const auto& c = b->t->cfg;
+    const size_t le = batch_layer_elems(b);
+    fill_normal_bf16_kernel<<<148 * 8, 256, 0, b->ctx->stream>>>(b->K, size_t(c.layers) * le, seed);
+    fill_normal_bf16_kernel<<<148 * 8, 256, 0, b->ctx->stream>>>(b->V, size_t(c.layers) * le, seed + 1);
+    if (b->dl) {
+      const size_t de = size_t(b->dl) * b->B * b->cap * b->dHk * b->dD;
+      fill_normal_bf16_kernel<<<148 * 8, 256, 0, b->ctx->stream>>>(b->dK, de, seed + 2);
+      fill_normal_bf16_kernel<<<148 * 8, 256, 0, b->ctx->stream>>>(b->dV, de, seed + 3);
+    }
+    check_launch(b->ctx, "fill");
+    for (int r = 0; r < nreq; ++r) b->host_lens[r] = n;
+    CUDA_TRY(cudaMemcpyAsync(b->lens, b->host_lens.data(), sizeof(int) * nreq, cudaMemcpyHostToDevice, b->ctx->stream));
+    CUDA_TRY(cudaStreamSynchronize(b->ctx->stream));
+  });
+}
+
+namespace {
+void batch_verify_impl(wc_batch* b, int nreq, int nodes, const int* tokens, const int* parents, int* out_argmax,
+                       float* out_logits);
+}
+
+extern "C" wc_status wc_batch_verify(wc_batch* b, int nreq, int nodes, const int* tokens, const int* parents,
+                                     int* out_argmax, float* out_logits) {
+  if (!b || nreq < 1 || nreq > b->B || nodes < 1 || nodes > b->nodes_max || !tokens || !parents || !out_argmax)
+    return WC_ERR_INVALID;
+  return guard(b->ctx, [&] { batch_verify_impl(b, nreq, nodes, tokens, parents, out_argmax, out_logits); });
+}
+
+extern "C" wc_status wc_batch_verify_profiled(wc_batch* b, int nreq, int nodes, const int* tokens,
+                                              const int* parents, int* out_argmax, float* ms_sum, int* counts) {
+  if (!b || nreq < 1 || nreq > b->B || nodes < 1 || nodes > b->nodes_max || !tokens || !parents || !out_argmax ||
+      !ms_sum || !counts)
+    return WC_ERR_INVALID;
+  return guard(b->ctx, [&] {
+    Profiler pr;
+    b->ctx->prof = &pr;
+    try {
+      batch_verify_impl(b, nreq, nodes, tokens, parents, out_argmax, nullptr);
+    } catch (...) {
+      b->ctx->prof = nullptr;
+      throw;
+    }
+    b->ctx->prof = nullptr;
+    for (int i = 0; i < PK_SLOTS; ++i) {
+      ms_sum[i] = 0.f;
+      counts[i] = 0;
+    }
+    for (auto& m : pr.marks) {
+      float ms = 0.f;
+      CUDA_TRY(cudaEventElapsedTime(&ms, m.second.first, m.second.second));
+      ms_sum[m.first] += ms;
+      counts[m.first] += 1;
+    }
+  });
+}
+
+namespace {
+void batch_verify_impl(wc_batch* b, int nreq, int nodes, const int* tokens, const int* parents, int* out_argmax,
+                       float* out_logits) {
+  {
+    wc_ctx* ctx = b->ctx;
+    const auto& c = b->t->cfg;
+    const int M = nreq * nodes;
+    std::vector<int> depth(M);
+    for (int r = 0; r < nreq; ++r) {
+      batch_check_tree(parents + size_t(r) * nodes, nodes, depth.data() + size_t(r) * nodes);
+      if (b->host_lens[r] + nodes > b->cap) fail(WC_ERR_CAPACITY, "request context exhausted");
+      for (int i = 0; i < nodes; ++i) {
+        const int tok = tokens[size_t(r) * nodes + i];
+        if (tok < 0 || tok >= c.vocab) fail(WC_ERR_INVALID, "token id out of range");
+      }
+    }
+    if (out_logits && b->logits_rows < size_t(M)) {
+      CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+      dfree(b->logits);
+      b->logits = static_cast<float*>(dalloc(sizeof(float) * size_t(M) * c.vocab));
+      b->logits_rows = M;
+    }
+    CUDA_TRY(cudaMemcpyAsync(b->tok, tokens, sizeof(int) * M, cudaMemcpyHostToDevice, ctx->stream));
+    CUDA_TRY(cudaMemcpyAsync(b->par, parents, sizeof(int) * M, cudaMemcpyHostToDevice, ctx->stream));
+    CUDA_TRY(cudaMemcpyAsync(b->dep, depth.data(), sizeof(int) * M, cudaMemcpyHostToDevice, ctx->stream));
+    batch_forward(b, nreq, nodes, out_logits != nullptr);
+    CUDA_TRY(cudaMemcpyAsync(out_argmax, b->am, sizeof(int) * M, cudaMemcpyDeviceToHost, ctx->stream));
+    if (out_logits)
+      CUDA_TRY(cudaMemcpyAsync(out_logits, b->logits, sizeof(float) * size_t(M) * c.vocab, cudaMemcpyDeviceToHost,
+                               ctx->stream));
+    CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+    int e = 0;
+    CUDA_TRY(cudaMemcpy(&e, ctx->d_err, sizeof(int), cudaMemcpyDeviceToHost));
+    if (e) {
+      CUDA_TRY(cudaMemset(ctx->d_err, 0, sizeof(int)));
+      fail(WC_ERR_DEVICE, "device error flag " + std::to_string(e));
+    }
+  }
+}
+}  // namespace
+
+extern "C" wc_status wc_batch_commit(wc_batch* b, int nreq, const int* keep, const int* n_keep, int maxkeep) {
+  if (!b || nreq < 1 || nreq > b->B || !keep || !n_keep || maxkeep < 1) return WC_ERR_INVALID;
+  return guard(b->ctx, [&] {
+    wc_ctx* ctx = b->ctx;
+    if (maxkeep > b->maxkeep_alloc) fail(WC_ERR_INVALID, "keep lists longer than the tree size");
+    for (int r = 0; r < nreq; ++r) {
+      const int nk = n_keep[r];
+      const int* k = keep + size_t(r) * maxkeep;
+      if (nk < 1 || nk > maxkeep || k[0] != 0) fail(WC_ERR_INVALID, "keep lists start at the root (0)");
+      for (int i = 1; i < nk; ++i)
+        if (k[i] <= k[i - 1] || k[i] >= b->nodes_max) fail(WC_ERR_INVALID, "keep indices must increase within the tree");
+      if (b->host_lens[r] + k[nk - 1] >= b->cap) fail(WC_ERR_CAPACITY, "keep index beyond the capacity");
+    }
+    CUDA_TRY(cudaMemcpyAsync(b->keep, keep, sizeof(int) * size_t(nreq) * maxkeep, cudaMemcpyHostToDevice, ctx->stream));
+    CUDA_TRY(cudaMemcpyAsync(b->nkeep, n_keep, sizeof(int) * nreq, cudaMemcpyHostToDevice, ctx->stream));
+    const auto& c = b->t->cfg;
+    BatchCompactParams p;
+    p.K = b->K;
+    p.V = b->V;
+    p.layers = c.layers;
+    p.B = b->B;
+    p.cap = b->cap;
+    p.Hk = c.kv_heads;
+    p.D = c.head_dim;
+    p.lens = b->lens;
+    p.keep = b->keep;
+    p.n_keep = b->nkeep;
+    p.maxkeep = maxkeep;
+    p.err = ctx->d_err;
+    batch_compact_kernel<<<dim3(nreq, c.layers), 128, 0, ctx->stream>>>(p);
+    if (b->dl) {
+      p.K = b->dK;
+      p.V = b->dV;
+      p.layers = b->dl;
+      p.Hk = b->dHk;
+      p.D = b->dD;
+      batch_compact_kernel<<<dim3(nreq, b->dl), 128, 0, ctx->stream>>>(p);
+    }
+    batch_commit_lens_kernel<<<(nreq + 127) / 128, 128, 0, ctx->stream>>>(b->lens, b->nkeep, nreq);
+    check_launch(ctx, "batch compact");
+    for (int r = 0; r < nreq; ++r) b->host_lens[r] += n_keep[r];
+    CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  });
+}
+
+extern "C" wc_status wc_batch_lens(const wc_batch* b, int nreq, int* lens) {
+  if (!b || !lens || nreq < 1 || nreq > b->B) return WC_ERR_INVALID;
+  for (int r = 0; r < nreq; ++r) lens[r] = b->host_lens[r];
+  return WC_OK;
+}
+
+extern "C" wc_status wc_batch_read_kv(wc_batch* b, int r, int layer, int n, void* k_out, void* v_out) {
+  if (!b || r < 0 || r >= b->B || layer < 0 || layer >= b->t->cfg.layers || n < 0 || n > b->cap) return WC_ERR_INVALID;
+  return guard(b->ctx, [&] {
+    const auto& c = b->t->cfg;
+    const int D = c.head_dim, Hk = c.kv_heads;
+    CUDA_TRY(cudaStreamSynchronize(b->ctx->stream));
+    for (int hk = 0; hk < Hk && n > 0; ++hk) {  // head-major arena -> [n][Hk][D] rows
+      const size_t off = (size_t(layer) * batch_layer_elems(b) + (size_t(r) * Hk + hk) * b->cap * D) * 2;
+      for (int w = 0; w < 2; ++w) {
+        void* dst = w ? v_out : k_out;
+        if (!dst) continue;
+        CUDA_TRY(cudaMemcpy2D(static_cast<char*>(dst) + size_t(hk) * D * 2, size_t(Hk) * D * 2,
+                              reinterpret_cast<char*>(w ? b->V : b->K) + off, size_t(D) * 2, size_t(D) * 2, n,
+                              cudaMemcpyDeviceToHost));
+      }
+    }
   });
 }
