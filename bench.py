@@ -54,6 +54,9 @@ def parse():
     ap.add_argument("--workload", choices=["c3", "c4", "c5"], default="c3",
                     help="c3: the headline greedy round (default); c4: Qwen3-4B sampled round at T = 1.0; "
                          "c5: batched tree verification + compaction, 64 requests x 4096 context")
+    ap.add_argument("--c5-layers", type=int, default=0,
+                    help="c5: target layers (0 = the config's 28; fewer for profiler captures of the same launches)")
+    ap.add_argument("--c5-requests", type=int, default=64, help="c5: requests per GPU")
     ap.add_argument("--chi2", type=int, default=0,
                     help="c4: also draw this many first tokens from one replayed state and test their law")
     ap.add_argument("--profile-rounds", type=int, default=0,
@@ -644,12 +647,15 @@ def bench_c5(a):
 
         dist.init_process_group("gloo", timeout=timedelta(seconds=900))
     torch.cuda.set_device(local)
-    ts = syn.Q17_TARGET
-    nreq, ctx0, nodes = 64, 4096, sum(C5_LEVELS)
+    import dataclasses
+
+    ts = syn.Q17_TARGET if not a.c5_layers else dataclasses.replace(syn.Q17_TARGET, layers=a.c5_layers)
+    nreq, ctx0, nodes = a.c5_requests, 4096, sum(C5_LEVELS)
     t0 = time.time()
     dev = f"cuda:{local}"
+    taps = [2, 14, 26] if ts.layers == 28 else [0, ts.layers // 2, ts.layers - 1]
     t = Target.from_weights(ts.hf_config(), syn.device_weight_stream(syn.target_tensor_specs(ts), 0, dev),
-                            feature_layers=[2, 14, 26], dtype="bf16", device=local)
+                            feature_layers=taps, dtype="bf16", device=local)
     rounds_total = a.warmup + a.steps + 2
     cap = ctx0 + nodes + 8 * rounds_total
     bv = BatchVerifier(t, nreq, nodes, cap, drafter_cache=(1, ts.kv_heads, ts.head_dim))
@@ -738,8 +744,9 @@ def bench_c5(a):
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: seeded random-init Qwen3-1.7B-architecture weights, seeded N(0,1) K/V prefixes, "
                     "seeded trees and geometric accepted paths",
-            "config": {"workload": "C5: 64 requests x 4096 context, 32-node depth-6 trees, batched verify + "
-                                   "compaction (target and drafter caches)", "requests": nreq, "context": ctx0,
+            "config": {"workload": f"C5: {nreq} requests x 4096 context, 32-node depth-6 trees, batched verify + "
+                                   f"compaction (target and drafter caches), {ts.layers} layers",
+                       "requests": nreq, "context": ctx0,
                        "tree_nodes": nodes, "mean_path": 3, "tokens_per_round": toks / a.steps,
                        "l2": "inputs larger than L2: ~34 GB of weights + KV per round"},
             "round_ms": {"mean": statistics.mean(ms), "median": statistics.median(ms)},

@@ -403,22 +403,28 @@ struct TreeAttnParams {
   int nodes, Hq, Hk;
   float scale;
   uint16_t* out;  // [M][Hq D]
+  int nsplit;     // key-range slices per (request, KV head); > 1: partial states, then tree_attn_merge
+  float* part_o;  // [B][Hk][nsplit][MAXR][D] unnormalised outputs
+  float* part_ml; // [B][Hk][nsplit][MAXR][2] (running max in log2 units, sum)
   int* err;
 };
 
+// Queries are staged once in the second tile buffer (moved into registers before that
+// buffer's first fill): a block holds 70 KB of shared memory.
 template <int D>
 constexpr size_t tree_attn_smem() {
-  return size_t(TA_MAXR) * (D + 8) * 2 + 2 * 2 * size_t(TA_KT) * (D + 8) * 2 + TA_MAXN * 8 + 64;
+  return 2 * 2 * size_t(TA_KT) * (D + 8) * 2 + TA_MAXN * 8 + 64;
 }
 
 template <int D>
-__global__ void __launch_bounds__(TA_THREADS) tree_attention_kernel(__grid_constant__ const TreeAttnParams p) {
+__global__ void __launch_bounds__(TA_THREADS, 2) tree_attention_kernel(__grid_constant__ const TreeAttnParams p) {
   constexpr int LD = D + 8, NK = D / 16, ND = D / 8;
+  static_assert(TA_MAXR <= TA_KT, "queries are staged in a tile buffer");
   extern __shared__ __align__(16) unsigned char ta_smem[];
-  uint16_t* qs = reinterpret_cast<uint16_t*>(ta_smem);   // [MAXR][LD]
-  uint16_t* kv = qs + TA_MAXR * LD;                       // [2 buffers][K, V][KT][LD]
+  uint16_t* kv = reinterpret_cast<uint16_t*>(ta_smem);    // [2 buffers][K, V][KT][LD]
+  uint16_t* qs = kv + 2 * TA_KT * LD;                     // [MAXR][LD] = buffer 1's K tile, until tile 1 loads
   unsigned long long* anc = reinterpret_cast<unsigned long long*>(kv + 2 * 2 * TA_KT * LD);  // [MAXN]
-  const int r = blockIdx.x, hk = blockIdx.y;
+  const int r = blockIdx.x, hk = blockIdx.y, sp_i = blockIdx.z;
   const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp, g = lane >> 2, t = lane & 3;
   const int rep = p.Hq / p.Hk, R = p.nodes * rep;
   pdl_launch_dependents();
@@ -457,10 +463,13 @@ __global__ void __launch_bounds__(TA_THREADS) tree_attention_kernel(__grid_const
       cp_async16(vb + row * LD + col, Vr + off, ok ? 16 : 0);
     }
   };
-  const int ntiles = (total + TA_KT - 1) / TA_KT;
-  load_tile(0, 0);
+  const int ntiles_all = (total + TA_KT - 1) / TA_KT;
+  const int per = (ntiles_all + p.nsplit - 1) / p.nsplit;
+  const int tile0 = min(ntiles_all, sp_i * per), ntiles = min(ntiles_all, tile0 + per) - tile0;
+  load_tile(tile0, 0);
   cp_async_commit();
-  __syncthreads();  // anc visible
+  cp_async_wait<0>();
+  __syncthreads();  // queries, tile 0 and anc visible
 
   const bool active = warp * 16 < R;
   const int r0 = warp * 16;
@@ -471,6 +480,11 @@ __global__ void __launch_bounds__(TA_THREADS) tree_attention_kernel(__grid_const
     if (rb < R) anc_g8 = anc[rb / rep];
   }
   uint32_t qa[NK][4];
+  if (active) {
+#pragma unroll
+    for (int kk = 0; kk < NK; ++kk) ldsm_x4(qa[kk], qs + (r0 + (lane % 16)) * LD + kk * 16 + (lane / 16) * 8);
+  }
+  __syncthreads();  // buffer 1 is free for tile 1
   float o[ND][4];
 #pragma unroll
   for (int j = 0; j < ND; ++j)
@@ -481,14 +495,10 @@ __global__ void __launch_bounds__(TA_THREADS) tree_attention_kernel(__grid_const
 
   for (int tile = 0; tile < ntiles; ++tile) {
     const int buf = tile & 1;
-    if (tile + 1 < ntiles) load_tile(tile + 1, buf ^ 1);
+    if (tile + 1 < ntiles) load_tile(tile0 + tile + 1, buf ^ 1);
     cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
-    if (tile == 0 && active) {
-#pragma unroll
-      for (int kk = 0; kk < NK; ++kk) ldsm_x4(qa[kk], qs + (r0 + (lane % 16)) * LD + kk * 16 + (lane / 16) * 8);
-    }
     if (active) {
       const uint16_t* kb = kv + size_t(buf) * 2 * TA_KT * LD;
       const uint16_t* vb = kb + TA_KT * LD;
@@ -509,7 +519,7 @@ __global__ void __launch_bounds__(TA_THREADS) tree_attention_kernel(__grid_const
         }
       }
       // ---- visibility, scale, online softmax
-      const int p0 = tile * TA_KT;
+      const int p0 = (tile0 + tile) * TA_KT;
       const bool full_prefix = p0 + TA_KT <= n;
       float tmax[2] = {-INFINITY, -INFINITY};
 #pragma unroll
@@ -581,6 +591,20 @@ __global__ void __launch_bounds__(TA_THREADS) tree_attention_kernel(__grid_const
   }
   cp_async_wait<0>();
   if (!active) return;
+  if (p.nsplit > 1) {  // ---- this slice's partial state
+    const size_t base = ((size_t(r) * p.Hk + hk) * p.nsplit + sp_i) * TA_MAXR;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int rho = r0 + g + 8 * h;
+      if (rho >= R) continue;
+      float* po = p.part_o + (base + rho) * D;
+#pragma unroll
+      for (int dj = 0; dj < ND; ++dj)
+        *reinterpret_cast<float2*>(po + dj * 8 + 2 * t) = make_float2(o[dj][2 * h], o[dj][2 * h + 1]);
+      if (t == 0) *reinterpret_cast<float2*>(p.part_ml + (base + rho) * 2) = make_float2(mrow[h], lrow[h]);
+    }
+    return;
+  }
   // ---- normalise and store rows g / g+8 of this warp
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
@@ -593,6 +617,34 @@ __global__ void __launch_bounds__(TA_THREADS) tree_attention_kernel(__grid_const
       const uint32_t v = pack2(f32_to_bf16_bits(o[dj][2 * h] * inv), f32_to_bf16_bits(o[dj][2 * h + 1] * inv));
       *reinterpret_cast<uint32_t*>(dst + dj * 8 + 2 * t) = v;
     }
+  }
+}
+
+// Merges the slices' partial states of each (request, KV head) in slice order.
+template <int D>
+__global__ void __launch_bounds__(128) tree_attn_merge_kernel(__grid_constant__ const TreeAttnParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int r = blockIdx.x, hk = blockIdx.y;
+  const int rep = p.Hq / p.Hk, R = p.nodes * rep, S = p.nsplit;
+  const size_t base = (size_t(r) * p.Hk + hk) * S * TA_MAXR;
+  for (int idx = threadIdx.x; idx < R * (D / 2); idx += blockDim.x) {
+    const int rho = idx / (D / 2), d = (idx % (D / 2)) * 2;
+    float M = -INFINITY;
+    for (int s = 0; s < S; ++s) M = fmaxf(M, p.part_ml[(base + size_t(s) * TA_MAXR + rho) * 2]);
+    float L = 0.f, o0 = 0.f, o1 = 0.f;
+    for (int s = 0; s < S; ++s) {
+      const size_t row = base + size_t(s) * TA_MAXR + rho;
+      const float2 ml = *reinterpret_cast<const float2*>(p.part_ml + row * 2);
+      const float w = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);
+      const float2 ov = *reinterpret_cast<const float2*>(p.part_o + row * D + d);
+      L += w * ml.y;
+      o0 += w * ov.x;
+      o1 += w * ov.y;
+    }
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    uint16_t* dst = p.out + (size_t(r * p.nodes + rho / rep) * p.Hq + hk * rep + rho % rep) * D + d;
+    *reinterpret_cast<uint32_t*>(dst) = pack2(f32_to_bf16_bits(o0 * inv), f32_to_bf16_bits(o1 * inv));
   }
 }
 

@@ -147,14 +147,16 @@ void prof_begin(wc_ctx* ctx, int kind) {
   if (!ctx->prof) return;
   cudaEvent_t e = ctx->prof->take();
   // external event nodes: a plain record inside stream capture is only a dependency marker
-  cudaEventRecordWithFlags(e, ctx->stream, cudaEventRecordExternal);
+  if (ctx->capturing) cudaEventRecordWithFlags(e, ctx->stream, cudaEventRecordExternal);
+  else cudaEventRecord(e, ctx->stream);
   ctx->prof->open[kind] = e;
 }
 
 void prof_end(wc_ctx* ctx, int kind) {
   if (!ctx->prof || !ctx->prof->open[kind]) return;
   cudaEvent_t e = ctx->prof->take();
-  cudaEventRecordWithFlags(e, ctx->stream, cudaEventRecordExternal);
+  if (ctx->capturing) cudaEventRecordWithFlags(e, ctx->stream, cudaEventRecordExternal);
+  else cudaEventRecord(e, ctx->stream);
   ctx->prof->marks.push_back({kind, {ctx->prof->open[kind], e}});
   ctx->prof->open[kind] = nullptr;
 }
@@ -3457,6 +3459,8 @@ struct wc_batch {
   unsigned long long* keys = nullptr;
   int maxkeep_alloc = 0;
   size_t logits_rows = 0;
+  int nsplit = 1;  // attention key-range slices (WC_TA_SPLIT; one measured fastest at C5)
+  float *part_o = nullptr, *part_ml = nullptr;
 };
 
 namespace {
@@ -3547,14 +3551,25 @@ void batch_forward(wc_batch* b, int nreq, int nodes, bool logits) {
     ap.Hk = Hk;
     ap.scale = 1.f / std::sqrt(float(D));
     ap.out = b->att;
+    ap.nsplit = b->nsplit;
+    ap.part_o = b->part_o;
+    ap.part_ml = b->part_ml;
     ap.err = err;
     prof_begin(ctx, PK_ATTN);
     if (D == 128)
-      launch_ex(ctx, "tree attention", tree_attention_kernel<128>, dim3(nreq, Hk), dim3(TA_THREADS),
+      launch_ex(ctx, "tree attention", tree_attention_kernel<128>, dim3(nreq, Hk, b->nsplit), dim3(TA_THREADS),
                 tree_attn_smem<128>(), true, 1, ap);
     else
-      launch_ex(ctx, "tree attention", tree_attention_kernel<64>, dim3(nreq, Hk), dim3(TA_THREADS),
+      launch_ex(ctx, "tree attention", tree_attention_kernel<64>, dim3(nreq, Hk, b->nsplit), dim3(TA_THREADS),
                 tree_attn_smem<64>(), true, 1, ap);
+    if (b->nsplit > 1) {
+      if (D == 128)
+        launch_ex(ctx, "tree attention merge", tree_attn_merge_kernel<128>, dim3(nreq, Hk), dim3(128), 0, true, 1,
+                  ap);
+      else
+        launch_ex(ctx, "tree attention merge", tree_attn_merge_kernel<64>, dim3(nreq, Hk), dim3(128), 0, true, 1,
+                  ap);
+    }
     prof_end(ctx, PK_ATTN);
     g = gemm_tc_params(M, H, Hq * D, TC_ADD);
     g.c = b->h;
@@ -3697,6 +3712,12 @@ extern "C" wc_status wc_batch_create(wc_target* t, int max_requests, int max_nod
     b->act = static_cast<uint16_t*>(dalloc(2 * size_t(M) * c.intermediate));
     for (int** pp : {&b->tok, &b->par, &b->dep, &b->am}) *pp = static_cast<int*>(dalloc(sizeof(int) * M));
     b->keys = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * M));
+    if (const char* e = std::getenv("WC_TA_SPLIT")) b->nsplit = std::max(1, std::min(8, std::atoi(e)));
+    if (b->nsplit > 1) {
+      const size_t rows = size_t(b->B) * c.kv_heads * b->nsplit * TA_MAXR;
+      b->part_o = static_cast<float*>(dalloc(sizeof(float) * rows * c.head_dim));
+      b->part_ml = static_cast<float*>(dalloc(sizeof(float) * rows * 2));
+    }
     b->maxkeep_alloc = max_nodes;
     b->keep = static_cast<int*>(dalloc(sizeof(int) * size_t(b->B) * max_nodes));
     b->nkeep = static_cast<int*>(dalloc(sizeof(int) * b->B));
@@ -3714,7 +3735,8 @@ extern "C" void wc_batch_destroy(wc_batch* b) {
   dfree(b->head.w);
   for (void* p : {(void*)b->K, (void*)b->V, (void*)b->dK, (void*)b->dV, (void*)b->lens, (void*)b->h, (void*)b->qkv,
                   (void*)b->logits, (void*)b->a, (void*)b->q, (void*)b->att, (void*)b->act, (void*)b->tok,
-                  (void*)b->par, (void*)b->dep, (void*)b->am, (void*)b->keys, (void*)b->keep, (void*)b->nkeep})
+                  (void*)b->par, (void*)b->dep, (void*)b->am, (void*)b->keys, (void*)b->keep, (void*)b->nkeep,
+                  (void*)b->part_o, (void*)b->part_ml})
     dfree(p);
   delete b;
 }
