@@ -322,6 +322,19 @@ def bench_ours(a):
                 "achieved": kbytes / (kms / 1e3) / 1e9, "peak": pk["hbm_gbs"], "unit": "GB/s",
                 "frac": kbytes / (kms / 1e3) / 1e9 / pk["hbm_gbs"], "traffic": traffic,
                 "algorithmic_bytes_per_launch": kbytes, "mean_launch_ms": kms, "peak_source": pk["source"]}
+    # prefill (time to first token; excluded from the decode metric as in GenStats.decode_tps)
+    pf_ms = []
+    for i in range(3):
+        prompt, _ = streams[i % len(streams)]
+        torch.cuda.synchronize()
+        w0 = time.perf_counter()
+        dec.prefill(prompt)
+        pf_ms.append((time.perf_counter() - w0) * 1e3)
+    pf_flop = 2 * PROMPT_LEN * rl._target_params(ts)["layers"]
+    prefill = {"prompt_tokens": PROMPT_LEN, "ms": statistics.median(pf_ms),
+               "target_tflops": pf_flop / (statistics.median(pf_ms) / 1e3) / 1e12,
+               "path": "target layers as tcgen05 GEMMs over the 512 prompt rows, then the drafter prefill; "
+                       "wall time of SpeculativeDecoder.prefill"}
     # e2e: the public API (SpeculativeDecoder.generate) with host prompt and per-round host copies
     prompt, ar = streams[0]
     dec.forced = forced_from(ar, acc_len)
@@ -351,6 +364,7 @@ def bench_ours(a):
         "roofline": roofline,
         "kernel_profile_ms": kp,
         "draft_step": draft_step,
+        "prefill": prefill,
         "e2e": e2e,
         "gpu_launches": int(launches),
         "wall_s_timed": wall_s,

@@ -269,6 +269,16 @@ WC_API wc_kv* wc_decoder_drafter_cache(wc_decoder* dec);
  * state restored between them is NOT done: callers time real rounds). Returns ms of last round. */
 WC_API wc_status wc_decoder_last_round_ms(const wc_decoder* dec, float* ms);
 
+/* The prefill's target pass (spec.py:129-141; Qwen3::forward over the prompt) on the tensor
+ * cores: tokens_dev (device int32[n]) through every layer as tcgen05 GEMMs over all n rows,
+ * causal attention, K/V appended to `cache` after its current size; taps (device fp32
+ * [3][n][hidden], NULL = none) receive the tap layers' block outputs; last_hidden (device fp32
+ * [hidden], NULL = none) the last row's residual before the final norm. bf16 targets with
+ * head_dim 64 or 128 (WC_ERR_UNSUPPORTED otherwise). Decoder and autoregressive prefills take
+ * this path when it applies (environment WC_PREFILL_GEMM=0 keeps the decode kernels). */
+WC_API wc_status wc_target_prompt_forward(wc_target* t, wc_kv* cache, const int* tokens_dev, int n, float* taps,
+                                          float* last_hidden);
+
 /* ------------------------------------------------------------------ batched tree verification
  * BASELINE config C5 (no counterpart in the reference, whose decoder runs one request): B
  * independent requests, each verifying a draft token tree against its own KV arena, then

@@ -156,3 +156,29 @@ def test_batch_verify_and_compaction_match_single_requests(bf16_target):
                     np.testing.assert_array_equal(va[n + i], pre[r][l][1][n + src])
             singles[r].compact(n, k)  # the single-request cache follows the same compaction
             assert singles[r].size() == n + len(k)
+
+
+@pytest.mark.parametrize("n", [37, 300, 1100])
+def test_prompt_forward_matches_decode_path(bf16_target, n):
+    """The prefill's target pass on the tensor cores (chunks of 1024 rows, causal attention)
+    against wc_target_forward on the decode kernels: tap rows and K/V rows within the bf16
+    tolerance above; the cache grows by n."""
+    from woodcock_b200 import synthetic as syn
+    from woodcock_b200.target import prompt_forward
+
+    t = bf16_target
+    c = t.cfg
+    prompt = syn.prompt_ids(n, c.vocab, seed=n)
+    ca, cb = t.make_cache(n + 8), t.make_cache(n + 8)
+    ref = t(torch.tensor(prompt, dtype=torch.int32, device="cuda"), ca, capture=True, logits=False)
+    taps, last = prompt_forward(t, prompt, cb)
+    torch.cuda.synchronize()
+    assert cb.size() == n
+    for f in range(3):
+        r_ = ref.features[f][0].float()
+        g_ = taps[f]
+        assert (g_ - r_).abs().max().item() <= KV_TOL * r_.abs().max().item(), f
+    assert torch.isfinite(last).all()
+    for l in range(c.layers):
+        for a, b_ in zip(cb.read(l, n), ca.read(l, n)):
+            assert (a - b_).abs().max().item() <= KV_TOL * b_.abs().max().item(), l

@@ -118,6 +118,7 @@ SIGNATURES = {
     "wc_decoder_target_cache": (P, [P]),
     "wc_decoder_drafter_cache": (P, [P]),
     "wc_decoder_last_round_ms": (S, [P, C.POINTER(C.c_float)]),
+    "wc_target_prompt_forward": (S, [P, P, P, C.c_int, P, P]),
     "wc_batch_create": (S, [P, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(P)]),
     "wc_batch_destroy": (None, [P]),
     "wc_batch_set_prefix": (S, [P, C.c_int, P, C.c_int]),

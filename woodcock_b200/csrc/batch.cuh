@@ -404,6 +404,7 @@ struct TreeAttnParams {
   float scale;
   uint16_t* out;  // [M][Hq D]
   int nsplit;     // key-range slices per (request, KV head); > 1: partial states, then tree_attn_merge
+  int causal;     // chain (prompt) mode: node i sees new rows 0..i; blockIdx.z = tile of TA_MAXR / rep nodes
   float* part_o;  // [B][Hk][nsplit][MAXR][D] unnormalised outputs
   float* part_ml; // [B][Hk][nsplit][MAXR][2] (running max in log2 units, sum)
   int* err;
@@ -424,18 +425,24 @@ __global__ void __launch_bounds__(TA_THREADS, 2) tree_attention_kernel(__grid_co
   uint16_t* kv = reinterpret_cast<uint16_t*>(ta_smem);    // [2 buffers][K, V][KT][LD]
   uint16_t* qs = kv + 2 * TA_KT * LD;                     // [MAXR][LD] = buffer 1's K tile, until tile 1 loads
   unsigned long long* anc = reinterpret_cast<unsigned long long*>(kv + 2 * 2 * TA_KT * LD);  // [MAXN]
-  const int r = blockIdx.x, hk = blockIdx.y, sp_i = blockIdx.z;
+  const int r = blockIdx.x, hk = blockIdx.y;
+  const int sp_i = p.causal ? 0 : blockIdx.z;
   const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp, g = lane >> 2, t = lane & 3;
-  const int rep = p.Hq / p.Hk, R = p.nodes * rep;
+  const int rep = p.Hq / p.Hk;
+  // causal mode: this block's nodes [i0, i0 + nb); tree mode: all nodes
+  const int ntile = TA_MAXR / rep;
+  const int i0 = p.causal ? int(blockIdx.z) * ntile : 0;
+  const int nb = p.causal ? min(ntile, p.nodes - i0) : p.nodes;
+  const int R = nb * rep;
   pdl_launch_dependents();
   pdl_wait();
   const int n = p.lens[r];
-  const int total = n + p.nodes;
+  const int total = n + (p.causal ? i0 + nb : p.nodes);  // causal: later rows are invisible to every node here
   const uint16_t* Kr = p.K + (size_t(r) * p.Hk + hk) * p.cap * D;  // one contiguous [cap][D] stream
   const uint16_t* Vr = p.V + (size_t(r) * p.Hk + hk) * p.cap * D;
   constexpr size_t sp = D;  // position stride
   // ancestor sets of the tree nodes (node 0 is the root)
-  if (tid == 0) {
+  if (tid == 0 && !p.causal) {
     bool bad = false;
     for (int i = 0; i < p.nodes; ++i) {
       const int par = p.parents[size_t(r) * p.nodes + i];
@@ -448,7 +455,8 @@ __global__ void __launch_bounds__(TA_THREADS, 2) tree_attention_kernel(__grid_co
   for (int c = tid; c < TA_MAXR * (D / 8); c += TA_THREADS) {
     const int rho = c / (D / 8), col = (c % (D / 8)) * 8;
     const bool ok = rho < R;
-    const uint16_t* src = p.q + (size_t(r * p.nodes + (ok ? rho / rep : 0)) * p.Hq + hk * rep + (ok ? rho % rep : 0)) * D + col;
+    const uint16_t* src =
+        p.q + (size_t(r * p.nodes + i0 + (ok ? rho / rep : 0)) * p.Hq + hk * rep + (ok ? rho % rep : 0)) * D + col;
     cp_async16(qs + rho * LD + col, src, ok ? 16 : 0);
   }
   auto load_tile = [&](int tile, int buf) {
@@ -474,7 +482,8 @@ __global__ void __launch_bounds__(TA_THREADS, 2) tree_attention_kernel(__grid_co
   const bool active = warp * 16 < R;
   const int r0 = warp * 16;
   unsigned long long anc_g = 0ull, anc_g8 = 0ull;  // this thread's two rows' ancestor sets
-  if (active) {
+  const int node_g = i0 + (r0 + g) / rep, node_g8 = i0 + (r0 + g + 8) / rep;  // causal: last visible new row
+  if (active && !p.causal) {
     const int ra = r0 + g, rb = r0 + g + 8;
     if (ra < R) anc_g = anc[ra / rep];
     if (rb < R) anc_g8 = anc[rb / rep];
@@ -520,7 +529,7 @@ __global__ void __launch_bounds__(TA_THREADS, 2) tree_attention_kernel(__grid_co
       }
       // ---- visibility, scale, online softmax
       const int p0 = (tile0 + tile) * TA_KT;
-      const bool full_prefix = p0 + TA_KT <= n;
+      const bool full_prefix = p0 + TA_KT <= n + (p.causal ? i0 + 1 : 0);
       float tmax[2] = {-INFINITY, -INFINITY};
 #pragma unroll
       for (int j = 0; j < TA_KT / 8; ++j)
@@ -529,8 +538,13 @@ __global__ void __launch_bounds__(TA_THREADS, 2) tree_attention_kernel(__grid_co
           float v = s[j][e] * sl2;
           if (!full_prefix) {
             const int pos = p0 + j * 8 + 2 * t + (e & 1);
-            const unsigned long long a = (e & 2) ? anc_g8 : anc_g;
-            const bool vis = pos < n || (pos < total && ((a >> (pos - n)) & 1ull));
+            bool vis;
+            if (p.causal) {
+              vis = pos <= n + ((e & 2) ? node_g8 : node_g) && pos < total;
+            } else {
+              const unsigned long long a = (e & 2) ? anc_g8 : anc_g;
+              vis = pos < n || (pos < total && ((a >> (pos - n)) & 1ull));
+            }
             if (!vis) v = -INFINITY;
           }
           s[j][e] = v;
@@ -611,7 +625,7 @@ __global__ void __launch_bounds__(TA_THREADS, 2) tree_attention_kernel(__grid_co
     const int rho = r0 + g + 8 * h;
     if (rho >= R) continue;
     const float inv = lrow[h] > 0.f ? 1.f / lrow[h] : 0.f;
-    uint16_t* dst = p.out + (size_t(r * p.nodes + rho / rep) * p.Hq + hk * rep + rho % rep) * D;
+    uint16_t* dst = p.out + (size_t(r * p.nodes + i0 + rho / rep) * p.Hq + hk * rep + rho % rep) * D;
 #pragma unroll
     for (int dj = 0; dj < ND; ++dj) {
       const uint32_t v = pack2(f32_to_bf16_bits(o[dj][2 * h] * inv), f32_to_bf16_bits(o[dj][2 * h + 1] * inv));

@@ -634,6 +634,18 @@ void launch_attention(wc_ctx* ctx, AttnParams p) {
   // tensor-core paths: bf16 cache, rule-based visibility, new rows appended by the kernel
   const bool tc_ok = !p.q_ready && !p.mask_full && p.kv_dtype == WC_BF16 && p.write_cache &&
                      (p.D == 128 || p.D == 64) && p.L_max * rep <= AM_MAXR && p.stride_p == p.D;
+  if (tc_ok && ctx->attn_mode == 3 && p.D == SK_D && p.L_max <= SK_MAXL && p.L_max * rep <= SK_MAXR &&
+      p.Hk <= 16 && p.cap <= SK_MAXS * SK_NTILE * SK_BLK && !p.mask_full) {
+    AttnJob j;
+    std::memset(&j, 0, sizeof(j));
+    j.a = p;
+    j.part = ctx->sk_part;
+    j.counters = ctx->sk_counters;
+    j.S = SK_MAXS;
+    launch_ex(ctx, "attention_flat", attention_flat_kernel, dim3(p.Hk * SK_MAXS), dim3(SK_CTHREADS),
+              attention_flat_smem(), true, 1, j);
+    return;
+  }
   if (tc_ok && ctx->attn_mode == 2 && p.L_max <= AD_MAXL && p.L_max * rep <= AD_MAXR) {
     const bool mt2 = p.L_max * rep > 16;
     if (p.D == 128) {
@@ -709,6 +721,8 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
     ctx->sk_counters = static_cast<int*>(dalloc(sizeof(int) * 64));
     CUDA_TRY(cudaMemset(ctx->sk_counters, 0, sizeof(int) * 64));
     CUDA_TRY(cudaFuncSetAttribute(stack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(stack_smem())));
+    CUDA_TRY(cudaFuncSetAttribute(attention_flat_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  int(attention_flat_smem())));
     {
       int occ_s = 0;
       if (stack_smem() <= ctx->max_smem &&
@@ -1275,6 +1289,7 @@ struct wc_target {
   float *ss_pack = nullptr, *ss_tmp = nullptr;
   unsigned long long* ws_keys = nullptr;
   int* ws_tokens = nullptr;
+  wc_batch* pf = nullptr;  // tensor-core prompt forward (made at the first prefill)
 };
 
 namespace {
@@ -1871,6 +1886,7 @@ extern "C" wc_status wc_target_load(wc_ctx* ctx, const char* dir, const int* tap
 extern "C" void wc_target_destroy(wc_target* t) {
   if (!t) return;
   cudaStreamSynchronize(t->ctx->stream);
+  if (t->pf) wc_batch_destroy(t->pf);
   dfree(t->embed);
   free_lin(t->head);
   dfree(t->final_norm);
@@ -2557,6 +2573,17 @@ extern "C" wc_status wc_drafter_head_argmax(wc_drafter* d, const float* out, int
   });
 }
 
+// ============================================================================ prompt forward on the tensor cores
+
+namespace {
+// Rows [0, n) of tokens_dev (device) through every target layer as tcgen05 GEMMs over all
+// rows at once, their K/V appended to `kv` after its first `start` rows, tap rows into
+// `to->rows` (when set). Returns the fp32 residual row of the last token (before the final
+// norm), or nullptr when the target cannot take this path (the caller then runs the decode
+// kernels). Defined with the batched verification.
+const float* prefill_gemm_forward(wc_target* t, wc_kv* kv, const int* tokens_dev, int n, int start, const TapOut* to);
+}  // namespace
+
 // ============================================================================ sampled decoding
 
 namespace {
@@ -2964,7 +2991,12 @@ int decoder_prefill_impl(wc_decoder* dec, const int* prompt, int n, const wc_sam
   Pick pick;  // _sample_target (spec.py:143-147) of the first token
   pick.temperature = &dec->st->temperature;
   pick.rng = dec->st->rng;
-  for (int r0 = 0; r0 < n; r0 += GEMV_MAXL) {
+  TapOut tg;
+  tg.rows = dec->taps;
+  tg.stride = tstride;
+  const float* last = prefill_gemm_forward(t, dec->tkv, d_tok, n, 0, &tg);
+  if (last) target_head_rows(t, last, 1, dec->st->keys, nullptr, err, smp ? &pick : nullptr);
+  for (int r0 = 0; r0 < n && !last; r0 += GEMV_MAXL) {
     const int rows = std::min(GEMV_MAXL, n - r0);
     Rows r;
     r.L = rows;
@@ -3258,7 +3290,9 @@ extern "C" wc_status wc_generate_autoregressive(wc_target* t, const int* prompt,
     CUDA_TRY(cudaMemcpyAsync(d_tok, prompt, sizeof(int) * n, cudaMemcpyHostToDevice, ctx->stream));
     for (int i = 0; i < n; ++i)
       if (prompt[i] < 0 || prompt[i] >= t->cfg.vocab) fail(WC_ERR_INVALID, "prompt token id out of range");
-    for (int r0 = 0; r0 < n; r0 += GEMV_MAXL) {
+    const float* last = prefill_gemm_forward(t, kv.get(), d_tok, n, 0, nullptr);
+    if (last) target_head_rows(t, last, 1, st->keys, nullptr, &st->err, smp ? &pick : nullptr);
+    for (int r0 = 0; r0 < n && !last; r0 += GEMV_MAXL) {
       const int rows = std::min(GEMV_MAXL, n - r0);
       Rows r;
       r.L = rows;
@@ -3460,6 +3494,7 @@ struct wc_batch {
   int maxkeep_alloc = 0;
   size_t logits_rows = 0;
   int nsplit = 1;  // attention key-range slices (WC_TA_SPLIT; one measured fastest at C5)
+  bool own_kv = true;  // false: K / V belong to a single-request cache (prompt forward)
   float *part_o = nullptr, *part_ml = nullptr;
 };
 
@@ -3485,7 +3520,8 @@ __global__ void fill_normal_bf16_kernel(uint16_t* x, size_t n, uint64_t seed) {
 // device): embeddings, every layer (GEMMs on the tensor cores, per-row q/k norm + RoPE +
 // K/V append at slots lens[r] + i, tree attention), final norm and head (argmax keys, and
 // fp32 logits when `logits` is set).
-void batch_forward(wc_batch* b, int nreq, int nodes, bool logits) {
+void batch_forward(wc_batch* b, int nreq, int nodes, bool logits, bool causal = false, const TapOut* taps = nullptr,
+                   bool head = true) {
   wc_ctx* ctx = b->ctx;
   wc_target* t = b->t;
   const auto& c = t->cfg;
@@ -3551,18 +3587,20 @@ void batch_forward(wc_batch* b, int nreq, int nodes, bool logits) {
     ap.Hk = Hk;
     ap.scale = 1.f / std::sqrt(float(D));
     ap.out = b->att;
-    ap.nsplit = b->nsplit;
+    ap.nsplit = causal ? 1 : b->nsplit;
+    ap.causal = causal ? 1 : 0;
     ap.part_o = b->part_o;
     ap.part_ml = b->part_ml;
     ap.err = err;
+    const int gz = causal ? (nodes + TA_MAXR / (Hq / Hk) - 1) / (TA_MAXR / (Hq / Hk)) : ap.nsplit;
     prof_begin(ctx, PK_ATTN);
     if (D == 128)
-      launch_ex(ctx, "tree attention", tree_attention_kernel<128>, dim3(nreq, Hk, b->nsplit), dim3(TA_THREADS),
+      launch_ex(ctx, "tree attention", tree_attention_kernel<128>, dim3(nreq, Hk, gz), dim3(TA_THREADS),
                 tree_attn_smem<128>(), true, 1, ap);
     else
-      launch_ex(ctx, "tree attention", tree_attention_kernel<64>, dim3(nreq, Hk, b->nsplit), dim3(TA_THREADS),
+      launch_ex(ctx, "tree attention", tree_attention_kernel<64>, dim3(nreq, Hk, gz), dim3(TA_THREADS),
                 tree_attn_smem<64>(), true, 1, ap);
-    if (b->nsplit > 1) {
+    if (ap.nsplit > 1) {
       if (D == 128)
         launch_ex(ctx, "tree attention merge", tree_attn_merge_kernel<128>, dim3(nreq, Hk), dim3(128), 0, true, 1,
                   ap);
@@ -3597,7 +3635,13 @@ void batch_forward(wc_batch* b, int nreq, int nodes, bool logits) {
     prof_begin(ctx, PK_DOWN);
     launch_gemm_tc(ctx, ta_act, W.down.map, g, W.down.BN);
     prof_end(ctx, PK_DOWN);
+    if (taps && taps->rows)  // block outputs of the tap layers (qwen3.cpp:103-104)
+      for (int f = 0; f < 3; ++f)
+        if (t->taps[f] == l)
+          CUDA_TRY(cudaMemcpyAsync(taps->rows + f * taps->stride, b->h, sizeof(float) * size_t(M) * H,
+                                   cudaMemcpyDeviceToDevice, ctx->stream));
   }
+  if (!head) return;
   RowNormParams rn;
   std::memset(&rn, 0, sizeof(rn));
   rn.x = b->h;
@@ -3651,79 +3695,161 @@ extern "C" wc_status wc_gemm_bf16(wc_ctx* ctx, const void* A, const void* B, flo
   });
 }
 
+namespace {
+
+__global__ void iota_kernel(int* x, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) x[i] = i;
+}
+
+// A batch object: GEMM weight copies and activations for max_requests x max_nodes rows, and
+// (own_kv) KV arenas of `capacity` rows per request. Without own_kv it serves the prompt
+// forward: one request, chain mode, K / V bound per call to a single-request cache.
+wc_batch* batch_create_impl(wc_target* t, int max_requests, int max_nodes, int capacity, int drafter_layers,
+                            int drafter_kv_heads, int drafter_head_dim, bool own_kv) {
+  if (!t->finalized) fail(WC_ERR_INVALID, "target not finalized");
+  if (t->dtype != WC_BF16) fail(WC_ERR_UNSUPPORTED, "batched verification runs bf16 targets");
+  const auto& c = t->cfg;
+  if (own_kv && (max_nodes > TA_MAXN || max_nodes * (c.heads / c.kv_heads) > TA_MAXR))
+    fail(WC_ERR_UNSUPPORTED, "tree nodes x query heads per KV head must be <= 64");
+  if (c.heads / c.kv_heads > TA_MAXR) fail(WC_ERR_UNSUPPORTED, "too many query heads per KV head");
+  if (c.head_dim != 128 && c.head_dim != 64) fail(WC_ERR_UNSUPPORTED, "batched verification: head_dim 64 or 128");
+  if (c.hidden % TC_BK || c.intermediate % 128 || (c.heads * c.head_dim) % TC_BK)
+    fail(WC_ERR_UNSUPPORTED, "batched verification: hidden, heads x head_dim multiples of 64, intermediate of 128");
+  wc_ctx* ctx = t->ctx;
+  auto b = std::make_unique<wc_batch>();
+  b->ctx = ctx;
+  b->t = t;
+  b->B = max_requests;
+  b->nodes_max = max_nodes;
+  b->cap = capacity;
+  b->M_max = max_requests * max_nodes;
+  b->own_kv = own_kv;
+  b->dl = own_kv ? std::max(0, drafter_layers) : 0;
+  b->dHk = drafter_kv_heads;
+  b->dD = drafter_head_dim;
+  if (b->dl > 0 && (b->dHk < 1 || b->dD < 1 || (b->dHk * b->dD) % 8)) fail(WC_ERR_INVALID, "drafter cache shape");
+  struct Cleanup {
+    wc_batch* b;
+    bool armed = true;
+    ~Cleanup() {
+      if (armed) wc_batch_destroy(b);
+    }
+  } cleanup{b.get()};
+  if (own_kv) {
+    const size_t le = batch_layer_elems(b.get());
+    b->K = static_cast<uint16_t*>(dalloc(size_t(c.layers) * le * 2));
+    b->V = static_cast<uint16_t*>(dalloc(size_t(c.layers) * le * 2));
+  }
+  if (b->dl) {
+    const size_t de = size_t(b->dl) * b->B * b->cap * b->dHk * b->dD;
+    b->dK = static_cast<uint16_t*>(dalloc(de * 2));
+    b->dV = static_cast<uint16_t*>(dalloc(de * 2));
+  }
+  b->lens = static_cast<int*>(dalloc(sizeof(int) * b->B));
+  CUDA_TRY(cudaMemset(b->lens, 0, sizeof(int) * b->B));
+  b->host_lens.assign(b->B, 0);
+  for (const TLayer& Ly : t->layers) {
+    wc_batch::Layer W;
+    W.qkv = tc_weight_from(ctx, Ly.qkv, 256);
+    W.o = tc_weight_from(ctx, Ly.o, 128);
+    W.gu = tc_weight_from(ctx, Ly.gu, 256);
+    W.down = tc_weight_from(ctx, Ly.down, 128);
+    b->lw.push_back(W);
+  }
+  if (own_kv) b->head = tc_weight_from(ctx, t->head, 256);
+  const int M = b->M_max, H = c.hidden, NQKV = (c.heads + 2 * c.kv_heads) * c.head_dim;
+  b->h = static_cast<float*>(dalloc(sizeof(float) * size_t(M) * H));
+  b->qkv = static_cast<float*>(dalloc(sizeof(float) * size_t(M) * NQKV));
+  b->a = static_cast<uint16_t*>(dalloc(2 * size_t(M) * H));
+  b->q = static_cast<uint16_t*>(dalloc(2 * size_t(M) * c.heads * c.head_dim));
+  b->att = static_cast<uint16_t*>(dalloc(2 * size_t(M) * c.heads * c.head_dim));
+  b->act = static_cast<uint16_t*>(dalloc(2 * size_t(M) * c.intermediate));
+  for (int** pp : {&b->tok, &b->par, &b->dep, &b->am}) *pp = static_cast<int*>(dalloc(sizeof(int) * M));
+  b->keys = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * M));
+  if (!own_kv) {  // chain mode: node i sits at depth i
+    iota_kernel<<<(M + 255) / 256, 256, 0, ctx->stream>>>(b->dep, M);
+    check_launch(ctx, "iota");
+  }
+  if (const char* e = std::getenv("WC_TA_SPLIT")) b->nsplit = std::max(1, std::min(8, std::atoi(e)));
+  if (own_kv && b->nsplit > 1) {
+    const size_t rows = size_t(b->B) * c.kv_heads * b->nsplit * TA_MAXR;
+    b->part_o = static_cast<float*>(dalloc(sizeof(float) * rows * c.head_dim));
+    b->part_ml = static_cast<float*>(dalloc(sizeof(float) * rows * 2));
+  }
+  b->maxkeep_alloc = max_nodes;
+  b->keep = static_cast<int*>(dalloc(sizeof(int) * size_t(b->B) * max_nodes));
+  b->nkeep = static_cast<int*>(dalloc(sizeof(int) * b->B));
+  CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  cleanup.armed = false;
+  return b.release();
+}
+
+constexpr int kPrefillChunk = 1024;  // prompt rows per GEMM pass
+
+bool prefill_gemm_ok(const wc_target* t) {
+  static const bool on = [] {
+    const char* e = std::getenv("WC_PREFILL_GEMM");
+    return !e || std::atoi(e) != 0;
+  }();
+  const auto& c = t->cfg;
+  return on && t->dtype == WC_BF16 && (c.head_dim == 128 || c.head_dim == 64) && c.hidden % TC_BK == 0 &&
+         c.intermediate % 128 == 0 && (c.heads * c.head_dim) % TC_BK == 0 && c.heads / c.kv_heads <= TA_MAXR;
+}
+
+const float* prefill_gemm_forward(wc_target* t, wc_kv* kv, const int* tokens_dev, int n, int start, const TapOut* to) {
+  if (!prefill_gemm_ok(t) || kv->dtype != WC_BF16 || n < 1) return nullptr;
+  if (start + n > kv->cap) fail(WC_ERR_CAPACITY, "prompt longer than the cache");
+  wc_ctx* ctx = t->ctx;
+  if (!t->pf) t->pf = batch_create_impl(t, 1, kPrefillChunk, 0, 0, 0, 0, false);
+  wc_batch* b = t->pf;
+  b->K = static_cast<uint16_t*>(kv->K);  // [layer][kv_head][capacity][head_dim] = one request's arena
+  b->V = static_cast<uint16_t*>(kv->V);
+  b->cap = kv->cap;
+  const int H = t->cfg.hidden;
+  int rows = 0;
+  for (int r0 = 0; r0 < n; r0 += kPrefillChunk) {
+    rows = std::min(kPrefillChunk, n - r0);
+    const int len = start + r0;
+    CUDA_TRY(cudaMemcpyAsync(b->lens, &len, sizeof(int), cudaMemcpyHostToDevice, ctx->stream));
+    CUDA_TRY(cudaMemcpyAsync(b->tok, tokens_dev + r0, sizeof(int) * rows, cudaMemcpyDeviceToDevice, ctx->stream));
+    TapOut tc;
+    if (to && to->rows) {
+      tc.rows = to->rows + size_t(r0) * H;
+      tc.stride = to->stride;
+    }
+    batch_forward(b, 1, rows, false, true, &tc, false);
+  }
+  return b->h + size_t(rows - 1) * H;
+}
+
+}  // namespace
+
+extern "C" wc_status wc_target_prompt_forward(wc_target* t, wc_kv* cache, const int* tokens_dev, int n, float* taps,
+                                              float* last_hidden) {
+  if (!t || !cache || !tokens_dev || n < 1) return WC_ERR_INVALID;
+  return guard(t->ctx, [&] {
+    if (cache->layers != t->cfg.layers || cache->Hk != t->cfg.kv_heads || cache->D != t->cfg.head_dim)
+      fail(WC_ERR_INVALID, "cache shape does not match the target");
+    TapOut to;
+    to.rows = taps;
+    to.stride = size_t(n) * t->cfg.hidden;
+    const float* last = prefill_gemm_forward(t, cache, tokens_dev, n, cache->n, &to);
+    if (!last) fail(WC_ERR_UNSUPPORTED, "the tensor-core prompt forward needs a bf16 target (head_dim 64 / 128)");
+    if (last_hidden)
+      CUDA_TRY(cudaMemcpyAsync(last_hidden, last, sizeof(float) * t->cfg.hidden, cudaMemcpyDeviceToDevice,
+                               t->ctx->stream));
+    cache->n += n;
+    check_launch(t->ctx, "prompt forward");
+  });
+}
+
 extern "C" wc_status wc_batch_create(wc_target* t, int max_requests, int max_nodes, int capacity, int drafter_layers,
                                      int drafter_kv_heads, int drafter_head_dim, wc_batch** out) {
   if (!t || !out || max_requests < 1 || max_nodes < 1 || capacity < 2) return WC_ERR_INVALID;
   return guard(t->ctx, [&] {
-    if (!t->finalized) fail(WC_ERR_INVALID, "target not finalized");
-    if (t->dtype != WC_BF16) fail(WC_ERR_UNSUPPORTED, "batched verification runs bf16 targets");
-    const auto& c = t->cfg;
-    if (max_nodes > TA_MAXN || max_nodes * (c.heads / c.kv_heads) > TA_MAXR)
-      fail(WC_ERR_UNSUPPORTED, "tree nodes x query heads per KV head must be <= 64");
-    if (c.head_dim != 128 && c.head_dim != 64) fail(WC_ERR_UNSUPPORTED, "batched verification: head_dim 64 or 128");
-    if (c.hidden % TC_BK || c.intermediate % 128 || (c.heads * c.head_dim) % TC_BK)
-      fail(WC_ERR_UNSUPPORTED, "batched verification: hidden, heads x head_dim multiples of 64, intermediate of 128");
-    wc_ctx* ctx = t->ctx;
-    auto b = std::make_unique<wc_batch>();
-    b->ctx = ctx;
-    b->t = t;
-    b->B = max_requests;
-    b->nodes_max = max_nodes;
-    b->cap = capacity;
-    b->M_max = max_requests * max_nodes;
-    b->dl = std::max(0, drafter_layers);
-    b->dHk = drafter_kv_heads;
-    b->dD = drafter_head_dim;
-    if (b->dl > 0 && (b->dHk < 1 || b->dD < 1 || (b->dHk * b->dD) % 8))
-      fail(WC_ERR_INVALID, "drafter cache shape");
-    struct Cleanup {
-      wc_batch* b;
-      bool armed = true;
-      ~Cleanup() {
-        if (armed) wc_batch_destroy(b);
-      }
-    } cleanup{b.get()};
-    const size_t le = batch_layer_elems(b.get());
-    b->K = static_cast<uint16_t*>(dalloc(size_t(c.layers) * le * 2));
-    b->V = static_cast<uint16_t*>(dalloc(size_t(c.layers) * le * 2));
-    if (b->dl) {
-      const size_t de = size_t(b->dl) * b->B * b->cap * b->dHk * b->dD;
-      b->dK = static_cast<uint16_t*>(dalloc(de * 2));
-      b->dV = static_cast<uint16_t*>(dalloc(de * 2));
-    }
-    b->lens = static_cast<int*>(dalloc(sizeof(int) * b->B));
-    CUDA_TRY(cudaMemset(b->lens, 0, sizeof(int) * b->B));
-    b->host_lens.assign(b->B, 0);
-    for (const TLayer& Ly : t->layers) {
-      wc_batch::Layer W;
-      W.qkv = tc_weight_from(ctx, Ly.qkv, 256);
-      W.o = tc_weight_from(ctx, Ly.o, 128);
-      W.gu = tc_weight_from(ctx, Ly.gu, 256);
-      W.down = tc_weight_from(ctx, Ly.down, 128);
-      b->lw.push_back(W);
-    }
-    b->head = tc_weight_from(ctx, t->head, 256);
-    const int M = b->M_max, H = c.hidden, NQKV = (c.heads + 2 * c.kv_heads) * c.head_dim;
-    b->h = static_cast<float*>(dalloc(sizeof(float) * size_t(M) * H));
-    b->qkv = static_cast<float*>(dalloc(sizeof(float) * size_t(M) * NQKV));
-    b->a = static_cast<uint16_t*>(dalloc(2 * size_t(M) * H));
-    b->q = static_cast<uint16_t*>(dalloc(2 * size_t(M) * c.heads * c.head_dim));
-    b->att = static_cast<uint16_t*>(dalloc(2 * size_t(M) * c.heads * c.head_dim));
-    b->act = static_cast<uint16_t*>(dalloc(2 * size_t(M) * c.intermediate));
-    for (int** pp : {&b->tok, &b->par, &b->dep, &b->am}) *pp = static_cast<int*>(dalloc(sizeof(int) * M));
-    b->keys = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * M));
-    if (const char* e = std::getenv("WC_TA_SPLIT")) b->nsplit = std::max(1, std::min(8, std::atoi(e)));
-    if (b->nsplit > 1) {
-      const size_t rows = size_t(b->B) * c.kv_heads * b->nsplit * TA_MAXR;
-      b->part_o = static_cast<float*>(dalloc(sizeof(float) * rows * c.head_dim));
-      b->part_ml = static_cast<float*>(dalloc(sizeof(float) * rows * 2));
-    }
-    b->maxkeep_alloc = max_nodes;
-    b->keep = static_cast<int*>(dalloc(sizeof(int) * size_t(b->B) * max_nodes));
-    b->nkeep = static_cast<int*>(dalloc(sizeof(int) * b->B));
-    CUDA_TRY(cudaStreamSynchronize(ctx->stream));
-    cleanup.armed = false;
-    *out = b.release();
+    *out = batch_create_impl(t, max_requests, max_nodes, capacity, drafter_layers, drafter_kv_heads, drafter_head_dim,
+                             true);
   });
 }
 
@@ -3733,7 +3859,11 @@ extern "C" void wc_batch_destroy(wc_batch* b) {
   for (auto& W : b->lw)
     for (TcWeight* w : {&W.qkv, &W.o, &W.gu, &W.down}) dfree(w->w);
   dfree(b->head.w);
-  for (void* p : {(void*)b->K, (void*)b->V, (void*)b->dK, (void*)b->dV, (void*)b->lens, (void*)b->h, (void*)b->qkv,
+  if (b->own_kv) {
+    dfree(b->K);
+    dfree(b->V);
+  }
+  for (void* p : {(void*)b->dK, (void*)b->dV, (void*)b->lens, (void*)b->h, (void*)b->qkv,
                   (void*)b->logits, (void*)b->a, (void*)b->q, (void*)b->att, (void*)b->act, (void*)b->tok,
                   (void*)b->par, (void*)b->dep, (void*)b->am, (void*)b->keys, (void*)b->keep, (void*)b->nkeep,
                   (void*)b->part_o, (void*)b->part_ml})

@@ -500,6 +500,27 @@ __device__ void sk_attention(const AttnJob& J, unsigned char* U, float* mw, floa
   if (tid == 0) J.counters[hk] = 0;
 }
 
+// ---------------------------------------------------------------------------- standalone attention
+// The attention job as its own launch for the per-kernel round: S blocks per KV head and no
+// thread-block cluster (a cluster of large blocks waits for enough free SMs in one GPC);
+// the last block of a head merges the S partial states from global memory. Each block
+// covers at most SK_NTILE x 16 prefix rows, so the cache capacity must be <= S x 64.
+__global__ void __launch_bounds__(SK_CTHREADS) attention_flat_kernel(__grid_constant__ const AttnJob J) {
+  extern __shared__ __align__(128) unsigned char af_smem[];
+  unsigned char* U = af_smem;
+  float* mw = reinterpret_cast<float*>(U + SK_U_BYTES);  // [W][MAXR]
+  float* lw = mw + SK_CWARPS * SK_MAXR;                   // [W][MAXR]
+  float* cw = lw + SK_CWARPS * SK_MAXR;                   // [MAXR][MAXS]
+  int* s_flag = reinterpret_cast<int*>(cw + SK_MAXR * SK_MAXS);
+  pdl_launch_dependents();
+  pdl_wait();
+  sk_attention(J, U, mw, lw, cw, s_flag);
+}
+
+constexpr size_t attention_flat_smem() {
+  return size_t(SK_U_BYTES) + 2 * SK_CWARPS * SK_MAXR * 4 + SK_MAXR * SK_MAXS * 4 + 16;
+}
+
 // ---------------------------------------------------------------------------- the kernel
 __global__ void __launch_bounds__(SK_THREADS, 1) stack_kernel(__grid_constant__ const StackParams sp) {
   extern __shared__ __align__(128) unsigned char sk_smem[];

@@ -153,6 +153,19 @@ class Target:
         return TargetOutput(logits=z[None] if logits else None, features=feats, argmax=am)
 
 
+def prompt_forward(target: "Target", tokens, cache: KVCache) -> tuple[torch.Tensor, torch.Tensor]:
+    """The prefill's target pass on the tensor cores (wc_target_prompt_forward): appends the
+    prompt's K/V to `cache`; returns (taps [3][n][hidden], last row's residual [hidden])."""
+    dev = target.ctx.device
+    tok = device_ints(tokens, dev)
+    n = tok.numel()
+    taps = torch.empty((3, n, target.hidden_size), dtype=torch.float32, device=dev)
+    last = torch.empty((target.hidden_size,), dtype=torch.float32, device=dev)
+    with target.ctx.enter(tok, taps, last):
+        target.ctx.check(lib().wc_target_prompt_forward(target.h, cache.h, ptr(tok), n, ptr(taps), ptr(last)))
+    return taps, last
+
+
 def apply_rope_positions(x: torch.Tensor, positions, base: float) -> torch.Tensor:
     """Rotate-half RoPE of x[L][heads][D] at per-row positions (target.py:119-139) on the device."""
     from .ops import rope
