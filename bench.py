@@ -272,14 +272,12 @@ def bench_ours(a):
         torch.cuda.synchronize()
         wall_s = time.perf_counter() - tw0
     launches = t.ctx.launch_count() - launches0
-    timed_ms = float(sum(ms))
+    from woodcock_b200.replicas import aggregate
+
+    agg = aggregate(float(sum(ms)), float(a.steps * (acc_len + 1)), wall_s)
+    timed_ms, wall_s, tokens, value = agg["device_ms"], agg["wall_s"], agg["tokens"], agg["value"]
     if world > 1:
-        x = torch.tensor([timed_ms, wall_s], dtype=torch.float64)
-        dist.all_reduce(x, op=dist.ReduceOp.MAX)
-        timed_ms, wall_s = float(x[0]), float(x[1])
         dist.barrier()
-    tokens = world * a.steps * (acc_len + 1)
-    value = tokens / (timed_ms / 1e3)
     # algorithmic bytes of the timed rounds (weights + KV at each round's context)
     bytes_total = sum(rl.round_bytes(ts, ds, k, HEAD_ROWS, c)["total"] for c in ctxs)
     pk = peaks()
@@ -548,15 +546,10 @@ def bench_c4(a):
     with ClockSampler(local) as clk:
         ms, ctxs, toks = run(a.steps, 10_000 * rank)
         torch.cuda.synchronize()
-    timed_ms = float(sum(ms))
-    tok_total = float(toks)
-    if world > 1:
-        x = torch.tensor([timed_ms, tok_total], dtype=torch.float64)
-        dist.all_reduce(x, op=dist.ReduceOp.MAX)
-        timed_ms = float(x[0])
-        y = torch.tensor([tok_total], dtype=torch.float64)
-        dist.all_reduce(y, op=dist.ReduceOp.SUM)
-        tok_total = float(y[0])
+    from woodcock_b200.replicas import aggregate
+
+    agg = aggregate(float(sum(ms)), float(toks))
+    timed_ms, tok_total = agg["device_ms"], agg["tokens"]
     bytes_total = sum(rl.round_bytes(ts, ds, k, HEAD_ROWS, c)["total"] for c in ctxs)
     pk = peaks()
     gbs = bytes_total / (sum(ms) / 1e3) / 1e9
@@ -713,14 +706,10 @@ def bench_c5(a):
             toks += k_
             bytes_total += wbytes + sum(n + nodes for n in lens) * kvrow
         torch.cuda.synchronize()
-    timed_ms, wall_s, tok_total = float(sum(ms)), float(sum(walls)), float(toks)
-    if world > 1:
-        x = torch.tensor([timed_ms, wall_s], dtype=torch.float64)
-        dist.all_reduce(x, op=dist.ReduceOp.MAX)
-        timed_ms, wall_s = float(x[0]), float(x[1])
-        y = torch.tensor([tok_total], dtype=torch.float64)
-        dist.all_reduce(y, op=dist.ReduceOp.SUM)
-        tok_total = float(y[0])
+    from woodcock_b200.replicas import aggregate
+
+    agg = aggregate(float(sum(ms)), float(toks), float(sum(walls)))
+    timed_ms, wall_s, tok_total = agg["device_ms"], agg["wall_s"], agg["tokens"]
     # kernel classes of one more round, timed one by one
     trees = [c5_tree(rng, ts.vocab) for _ in range(nreq)]
     _, prof = bv.verify_profiled(np.array([x[0] for x in trees]), np.array([x[1] for x in trees]))
