@@ -14,6 +14,8 @@ Run in the build container (needs the reference tree and oracle/_ref built by
   functions used here are pure numpy) on seeded cases, driven by the Philox uniform
   tape of oracle/wc_oracle.py. Inputs and outputs are stored so the tests can
   replay them against the oracle and the CUDA acceptance kernel.
+* vocab.json: the reference's top_ids / coverage (python/woodcock/vocab.py:35-52) on
+  seeded counts with ties and forced ids (`python tests/golden/make_golden.py vocab`).
 """
 
 from __future__ import annotations
@@ -147,12 +149,36 @@ def sampling_fixture() -> dict:
     return cases
 
 
+def vocab_fixture() -> dict:
+    """python/woodcock/vocab.py:35-47 top_ids on seeded counts with many ties and forced ids."""
+    _reference_sampling()  # puts the reference package on the path (with the stand-in mlx)
+    from woodcock import vocab as ref_vocab  # noqa: E402
+
+    rs = np.random.default_rng(7)
+    cases = []
+    for i in range(30):
+        V = int(rs.integers(5, 400))
+        counts = rs.integers(0, 6 if i % 2 else 1000, V)
+        k = int(rs.integers(1, V + 1))
+        always = sorted({int(x) for x in rs.integers(0, V, int(rs.integers(0, min(k, 4) + 1)))})
+        ids = ref_vocab.top_ids(counts, k, set(always))
+        cases.append({"counts": counts.tolist(), "k": k, "always": always, "ids": ids.tolist(),
+                      "coverage": ref_vocab.coverage(counts, ids)})
+    return {"top_ids": cases}
+
+
 def main():
-    for name, tie in (("c1", True), ("c1u", False)):
-        (HERE / f"{name}.json").write_text(json.dumps(model_fixture(name, tie)))
-        print("wrote", name)
-    (HERE / "sampling.json").write_text(json.dumps(sampling_fixture()))
-    print("wrote sampling")
+    only = sys.argv[1:]
+    if not only or "models" in only:
+        for name, tie in (("c1", True), ("c1u", False)):
+            (HERE / f"{name}.json").write_text(json.dumps(model_fixture(name, tie)))
+            print("wrote", name)
+    if not only or "sampling" in only:
+        (HERE / "sampling.json").write_text(json.dumps(sampling_fixture()))
+        print("wrote sampling")
+    if not only or "vocab" in only:
+        (HERE / "vocab.json").write_text(json.dumps(vocab_fixture()))
+        print("wrote vocab")
 
 
 if __name__ == "__main__":

@@ -36,13 +36,24 @@ class Drafter:
         self.hidden_size, self.vocab_size = cfg.hidden, cfg.vocab
 
     @classmethod
-    def load(cls, path: str | Path, dtype=None, device=0) -> "Drafter":
+    def load(cls, path: str | Path, dtype=None, device=0, target=None, vocab=None) -> "Drafter":
+        """drafter.py:322-331. A v1 export (woodcock.json) is validated first (format, sha256,
+        and the target's hidden size / vocabulary when `target` is given); `vocab` =
+        '<counts.npz>:<K>' or an id list restricts the head at load (vocab.py:83-87)."""
+        from .export import check_manifest
+
+        check_manifest(path, target.cfg if target is not None else None)
         ctx = Context.get(device)
         if dtype is None:
             dtype = _file_dtype(Path(path))
         h = C.c_void_p()
         ctx.check(lib().wc_drafter_load(ctx.h, str(path).encode(), dtype_code(dtype), C.byref(h)))
-        return cls(h, ctx)
+        d = cls(h, ctx)
+        if vocab is not None:
+            from .vocab import load_ids
+
+            d.restrict_vocab(load_ids(vocab) if isinstance(vocab, (str, Path)) else vocab)
+        return d
 
     @classmethod
     def from_weights(cls, config: dict, weights: dict, dtype="bf16", device=0) -> "Drafter":
@@ -99,7 +110,8 @@ class Drafter:
     def save(self, path):
         if self._vocab_ids is not None:
             raise ValueError("a drafter with a restricted vocabulary cannot be saved")
-        raise NotImplementedError("drafter export is not part of the decode path")
+        raise NotImplementedError("weights live on the device in their streaming layout; export the source "
+                                  "directory with woodcock_b200.export.export_drafter")
 
     # ------------------------------------------------------------ compute
     def make_cache(self, capacity: int = 4096) -> KVCache:
