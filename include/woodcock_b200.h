@@ -231,7 +231,9 @@ WC_API wc_status wc_decoder_set_forced(wc_decoder* dec, const int* forced, int k
  * with verify_tree_stochastic's chain rule (sampling.py:143-187) and the next token is drawn
  * from the residual or from the bonus row. Random numbers: Philox4x32-10 keyed by sp->seed;
  * each round consumes one counter block of 2^26 (streams of 2^21: draft step i, the
- * acceptance uniforms, the residual's Gumbel noise). top_k / top_p: WC_ERR_UNSUPPORTED. */
+ * acceptance uniforms, the residual's Gumbel noise). top_k / top_p warp the target's p as
+ * probs_from_logits does (sampling.py:39-55), as one threshold per row on z / T; the draft
+ * distribution uses the temperature only (spec.py:113-125). */
 WC_API wc_status wc_decoder_round(wc_decoder* dec, int k, int* out_tokens, int* out_n);
 /* spec.py:151-212 generate with a static chain policy of depth k (trees: WC_ERR_UNSUPPORTED until built).
  * eos: host int32[n_eos]. out_tokens capacity max_new. */

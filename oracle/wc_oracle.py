@@ -126,8 +126,45 @@ def gumbel_draw(z: np.ndarray, T: float, seed: int, base: int, stream: int) -> i
     return int(np.argmax(key))  # first maximum, as the device's key packing breaks ties
 
 
+def warp_threshold(z: np.ndarray, T: float, top_k: int = 0, top_p: float = 1.0) -> float:
+    """The device's form of probs_from_logits' warping (sampling.py:39-55): with x = z / T
+    (float32), the kept tokens are x >= thr. top-k: thr = the k-th largest x; top-p: the
+    largest x at which the descending inclusive softmax mass of the top-k survivors reaches
+    top_p. Returns -inf when nothing is cut. Equal to the sort-based rule when no two kept
+    values tie at the cut."""
+    x = (np.asarray(z, F32) / F32(T)).astype(F32)
+    thr = -np.inf
+    if top_k and 0 < top_k < len(x):
+        thr = float(np.sort(x)[-top_k])
+    if top_p < 1.0:
+        kept = np.sort(x[x >= thr])[::-1].astype(np.float64)
+        e = np.exp(kept - kept[0])
+        cs = np.cumsum(e)
+        m = int(np.searchsorted(cs, top_p * cs[-1], side="left"))
+        if m < len(kept):
+            thr = max(thr, float(kept[m]))
+    return thr
+
+
+def warped_probs(z: np.ndarray, T: float, top_k: int = 0, top_p: float = 1.0) -> np.ndarray:
+    x = (np.asarray(z, F32) / F32(T)).astype(F32)
+    thr = warp_threshold(z, T, top_k, top_p)
+    e = np.where(x >= thr, np.exp(x.astype(np.float64) - float(x.max())), 0.0)
+    return e / e.sum()
+
+
+def gumbel_draw_warped(z: np.ndarray, T: float, top_k: int, top_p: float, seed: int, base: int, stream: int) -> int:
+    """Warped first-token / autoregressive draw: argmax over kept x of x + Gumbel (float32)."""
+    x = (np.asarray(z, F32) / F32(T)).astype(F32)
+    thr = warp_threshold(z, T, top_k, top_p)
+    g = philox_gumbel_f32(seed, base + stream * RNG_STREAM_LEN, len(x))
+    key = np.where(x >= thr, (x + g).astype(F32), -np.inf)
+    return int(np.argmax(key))
+
+
 def sampled_chain_accept(zt: np.ndarray, zd: np.ndarray, tokens: list[int], T: float, seed: int, base: int,
-                         vocab_ids: np.ndarray | None = None, skip_residual: bool = False) -> tuple[int, int]:
+                         vocab_ids: np.ndarray | None = None, skip_residual: bool = False, top_k: int = 0,
+                         top_p: float = 1.0) -> tuple[int, int]:
     """Acceptance of one sampled chain round from its logits: zt [K+1][V] target rows at
     [x_n, d_1..d_K], zd [K][Vd] draft rows (head row r is token vocab_ids[r]). p_i =
     softmax(zt_i / T), q_i = softmax(zd_i / T) scattered to token ids (spec.py:239-249);
@@ -140,6 +177,9 @@ def sampled_chain_accept(zt: np.ndarray, zd: np.ndarray, tokens: list[int], T: f
         x = (np.asarray(z, F32) / F32(T)).astype(np.float64)
         e = np.exp(x - x.max())
         return e / e.sum()
+
+    def target(z):  # the target rows carry the top-k / top-p warping, the draft rows only T
+        return warped_probs(z, T, top_k, top_p) if (top_k or top_p < 1.0) else probs(z)
 
     def q_full(i):
         qd = probs(zd[i])
@@ -157,12 +197,12 @@ def sampled_chain_accept(zt: np.ndarray, zd: np.ndarray, tokens: list[int], T: f
         qx = q[x]
         if not qx > 0:
             break
-        px = probs(zt[a])[x]
+        px = target(zt[a])[x]
         u = philox_uniforms(seed, base + RNG_ACCEPT_STREAM * RNG_STREAM_LEN + a, 1)[0]
         if not u < min(1.0, px / qx):
             break
         a += 1
-    p = probs(zt[a])
+    p = target(zt[a])
     if a < K and not skip_residual:
         r = np.maximum(p - q_full(a), 0.0)
         if not r.sum() > 1e-12:

@@ -12,6 +12,8 @@ chain; sampling.py:39-55, 69-82, 143-203) and the autoregressive baseline (spec.
     the residual.
 (c) The autoregressive baseline's sampled first token follows p over many seeds, and a seed
     reproduces its stream.
+(d) top-k / top-p warping of the target: tape parity of the first token and of the rounds
+    with the oracle's threshold rule, and the first-token law of the warped distribution.
 """
 
 from __future__ import annotations
@@ -159,12 +161,58 @@ def test_sampled_autoregressive_first_token_law(pair, prompt64):
     assert a == b
 
 
-def test_top_k_and_top_p_are_refused_on_the_device(pair, prompt64):
+WARPS = [(20, 1.0), (0, 0.8), (40, 0.9)]
+
+
+@pytest.mark.parametrize("top_k,top_p", WARPS)
+def test_warped_rounds_match_oracle_tape(pair, prompt64, top_k, top_p):
+    """top-k / top-p on the target distribution (sampling.py:39-55): the first token and every
+    round's decisions and draws equal the oracle's threshold rule on the same logits."""
+    from woodcock_b200 import SamplingParams
+
+    t, _, d = pair
+    ids = np.asarray(HEAD_IDS)
+    k = 4
+    dec = _decoder(t, d, k)
+    first = dec.prefill(prompt64, SamplingParams(temperature=T_TAPE, top_k=top_k, top_p=top_p, seed=77))
+    z = t(torch.tensor(prompt64, dtype=torch.int32, device="cuda"), t.make_cache(512),
+          logits_from=len(prompt64) - 1).logits.float().reshape(-1).cpu().numpy()
+    assert first == O.gumbel_draw_warped(z, T_TAPE, top_k, top_p, 77, 0, 0)
+    for r in range(25):
+        toks = dec.round(k)
+        g = dec.round_logits(k)
+        a, nxt = O.sampled_chain_accept(g["zt"], g["zd"], g["tokens"], T_TAPE, 77, g["base"], vocab_ids=ids,
+                                        top_k=top_k, top_p=top_p)
+        assert toks == g["tokens"][1:a + 1] + [nxt], (r, toks, a, nxt)
+
+
+def test_warped_first_token_law_chi_square(pair, prompt64):
+    from woodcock_b200 import SamplingParams
+
+    t, _, d = pair
+    k, n = 4, 20_000
+    top_k, top_p = 50, 0.9
+    dec = _decoder(t, d, k)
+    dec.prefill(prompt64, SamplingParams(temperature=T_LAW, top_k=top_k, top_p=top_p, seed=8))
+    dec.save_state()
+    counts = np.zeros(t.cfg.vocab)
+    for i in range(n):
+        dec.restore_state()
+        counts[dec.round(k)[0]] += 1
+        if i == 0:
+            z0 = dec.round_logits(k)["zt"][0].copy()
+    p = O.warped_probs(z0, T_LAW, top_k, top_p)
+    assert counts[p == 0].sum() == 0  # nothing outside the kept set is ever emitted
+    stat, dof, pval = O.chi2_equal_mass(counts, p, bins=1000)
+    assert dof >= 5 and pval > 1e-3, (stat, dof, pval)
+
+
+def test_invalid_warping_is_refused(pair, prompt64):
     from woodcock_b200 import SamplingParams
 
     t, _, d = pair
     dec = _decoder(t, d, 2)
-    with pytest.raises(Exception, match="top_k"):
-        dec.prefill(prompt64, SamplingParams(temperature=1.0, top_k=20))
     with pytest.raises(Exception, match="top_p"):
-        dec.prefill(prompt64, SamplingParams(temperature=1.0, top_p=0.9))
+        dec.prefill(prompt64, SamplingParams(temperature=1.0, top_p=0.0))
+    with pytest.raises(Exception, match="top_k"):
+        dec.prefill(prompt64, SamplingParams(temperature=1.0, top_k=-1))

@@ -312,3 +312,19 @@ def test_device_protocol_decisions_equal_the_reference_rule_on_its_uniforms():
         q = np.array([sm(r) for r in zd])
         ref_a, _ = O.verify_chain_stochastic(p, q, toks[1:], O.Tape(9, base + O.RNG_ACCEPT_STREAM * O.RNG_STREAM_LEN))
         assert a == ref_a, trial
+
+
+def test_device_warping_threshold_equals_reference_warping():
+    """The device's threshold form of top-k / top-p equals probs_from_logits (pinned to
+    sampling.py:39-55) on untied logits."""
+    rng = np.random.default_rng(21)
+    for trial in range(60):
+        V = int(rng.integers(20, 3000))
+        z = rng.normal(0, rng.uniform(0.5, 4.0), V).astype(np.float32)
+        T = float(rng.uniform(0.3, 1.5))
+        top_k = int(rng.integers(0, V)) if trial % 3 else 0
+        top_p = float(rng.uniform(0.05, 1.0)) if trial % 2 else 1.0
+        ref = O.probs_from_logits(z, O.SamplingParams(temperature=T, top_k=top_k, top_p=top_p))
+        got = O.warped_probs(z, T, top_k, top_p)
+        assert ((ref > 0) == (got > 0)).all(), trial
+        np.testing.assert_allclose(got, ref, rtol=2e-5, atol=1e-9)

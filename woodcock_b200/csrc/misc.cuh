@@ -28,6 +28,8 @@ struct RoundState {
   unsigned long long keys[MAXKEYS];  // argmax keys: draft steps [0, K), verify rows [K, 2K+1)
   unsigned long long rng[2];         // sampled decoding: Philox seed, counter base of the next round
   float temperature;                 // sampled decoding: T (0 = greedy)
+  int top_k;                         // sampled decoding: top-k warping of the target (0 = off)
+  float top_p;                       // sampled decoding: top-p warping of the target (1 = off)
   int pad2;
 };
 
@@ -534,6 +536,183 @@ __global__ void accept_chain_kernel(RoundState* st, int K, const int* vocab_map_
 }
 
 // ----------------------------------------------------------------------------- sampled rounds
+// probs_from_logits (sampling.py:39-55) as one threshold per row: with x = z / T, top-k keeps
+// x >= (k-th largest x) and top-p then keeps the largest x whose descending cumulative
+// softmax mass, counted before each of them, stays below top_p; both are "x >= thr", so the
+// warped distribution is p_j = [x_j >= thr] exp(x_j - M) / Z. Rows whose values tie exactly
+// at the threshold keep every tied token (the reference breaks such ties by sort position).
+struct RowWarp {
+  float M;    // max of x
+  float thr;  // -inf: no warping
+  double Z;   // sum of exp(x - M) over the kept tokens
+};
+
+__device__ __forceinline__ uint32_t order_key(float x) {
+  const uint32_t u = __float_as_uint(x);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ float order_key_value(uint32_t k) {
+  return __uint_as_float((k & 0x80000000u) ? (k & 0x7FFFFFFFu) : ~k);
+}
+
+struct WarpParams {
+  const float* z;  // [R][ld]
+  int V, ld;
+  const float* temperature;
+  const int* top_k;
+  const float* top_p;
+  RowWarp* out;                  // [R]
+  unsigned long long* zero_keys; // cleared here (the keys a later draw accumulates into)
+  int zero_n;
+};
+
+template <class T, class Op>
+__device__ __forceinline__ T block_reduce(T v, T* red, Op op) {
+  for (int o = 16; o > 0; o >>= 1) v = op(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if (threadIdx.x % 32 == 0) red[threadIdx.x / 32] = v;
+  __syncthreads();
+  T a = red[0];
+  for (int w = 1; w < int(blockDim.x / 32); ++w) a = op(a, red[w]);
+  return a;
+}
+
+// One block per row: max, then the top-k key by a count radix select (4 passes of 8 bits),
+// the kept mass, the top-p key by a mass radix select, the final normaliser.
+__global__ void __launch_bounds__(1024) warp_rows_kernel(__grid_constant__ const WarpParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
+  __shared__ unsigned cnt[256];
+  __shared__ double mass[256];
+  __shared__ float red_f[32];
+  __shared__ double red_d[32];
+  __shared__ uint32_t s_prefix;
+  __shared__ unsigned long long s_above;
+  __shared__ double s_above_m;
+  __shared__ int s_found;
+  const int row = blockIdx.x, tid = threadIdx.x;
+  if (row == 0 && p.zero_keys && tid < p.zero_n) p.zero_keys[tid] = 0ull;
+  const float* z = p.z + size_t(row) * p.ld;
+  const float T = *p.temperature;
+  const int k = p.top_k ? *p.top_k : 0;
+  const float tp = p.top_p ? *p.top_p : 1.f;
+  float m = -INFINITY;
+  for (int j = tid; j < p.V; j += blockDim.x) m = fmaxf(m, z[j] / T);
+  const float M = block_reduce(m, red_f, [](float a, float b) { return fmaxf(a, b); });
+  uint32_t keep_key = 0u;  // elements with order_key(x) >= keep_key stay
+  if (k > 0 && k < p.V) {  // the k-th largest x
+    uint32_t prefix = 0u;
+    unsigned long long above = 0ull;
+    for (int shift = 24; shift >= 0; shift -= 8) {
+      const uint32_t hi = shift == 24 ? 0u : (0xFFFFFFFFu << (shift + 8));
+      for (int b = tid; b < 256; b += blockDim.x) cnt[b] = 0u;
+      __syncthreads();
+      for (int j = tid; j < p.V; j += blockDim.x) {
+        const uint32_t key = order_key(z[j] / T);
+        if ((key & hi) == (prefix & hi)) atomicAdd(&cnt[(key >> shift) & 255u], 1u);
+      }
+      __syncthreads();
+      if (tid == 0) {
+        int b = 255;
+        for (; b > 0; --b) {
+          if (above + cnt[b] >= (unsigned long long)k) break;
+          above += cnt[b];
+        }
+        s_prefix = prefix | (uint32_t(b) << shift);
+        s_above = above;
+      }
+      __syncthreads();
+      prefix = s_prefix;
+      above = s_above;
+    }
+    keep_key = prefix;
+  }
+  double s1 = 0.0;
+  for (int j = tid; j < p.V; j += blockDim.x) {
+    const float x = z[j] / T;
+    if (order_key(x) >= keep_key) s1 += exp(double(x) - double(M));
+  }
+  const double S1 = block_reduce(s1, red_d, [](double a, double b) { return a + b; });
+  if (tp < 1.f) {  // the largest x at which the descending inclusive mass reaches top_p
+    const double target = double(tp) * S1;
+    uint32_t prefix = 0u;
+    double above_m = 0.0;
+    bool found = true;
+    for (int shift = 24; shift >= 0 && found; shift -= 8) {
+      const uint32_t hi = shift == 24 ? 0u : (0xFFFFFFFFu << (shift + 8));
+      for (int b = tid; b < 256; b += blockDim.x) mass[b] = 0.0;
+      __syncthreads();
+      for (int j = tid; j < p.V; j += blockDim.x) {
+        const float x = z[j] / T;
+        const uint32_t key = order_key(x);
+        if (key >= keep_key && (key & hi) == (prefix & hi)) atomicAdd(&mass[(key >> shift) & 255u], exp(double(x) - double(M)));
+      }
+      __syncthreads();
+      if (tid == 0) {
+        int b = 255;
+        bool hit = false;
+        for (; b >= 0; --b) {
+          if (above_m + mass[b] >= target) {
+            hit = true;
+            break;
+          }
+          above_m += mass[b];
+        }
+        s_found = hit ? 1 : 0;
+        s_prefix = prefix | (uint32_t(hit ? b : 0) << shift);
+        s_above_m = above_m;
+      }
+      __syncthreads();
+      found = s_found != 0;
+      prefix = s_prefix;
+      above_m = s_above_m;
+    }
+    if (found && prefix > keep_key) keep_key = prefix;
+  }
+  double zs = 0.0;
+  for (int j = tid; j < p.V; j += blockDim.x) {
+    const float x = z[j] / T;
+    if (order_key(x) >= keep_key) zs += exp(double(x) - double(M));
+  }
+  const double Z = block_reduce(zs, red_d, [](double a, double b) { return a + b; });
+  if (tid == 0) p.out[row] = RowWarp{M, keep_key ? order_key_value(keep_key) : -INFINITY, Z};
+}
+
+// Gumbel-max draws over the kept tokens of warped rows (the warped autoregressive step and
+// first token): keys[row] = argmax over x_j >= thr of (x_j + Gumbel), stream `stream` + row.
+struct SampleRowsParams {
+  const float* z;
+  int V, ld;
+  const float* temperature;
+  const RowWarp* warp;
+  const unsigned long long* rng;
+  int stream;
+  unsigned long long* keys;
+};
+
+__global__ void __launch_bounds__(256) sample_rows_kernel(__grid_constant__ const SampleRowsParams p) {
+  pdl_launch_dependents();
+  pdl_wait();
+  __shared__ unsigned long long s_best;
+  const int row = blockIdx.y;
+  const float* z = p.z + size_t(row) * p.ld;
+  const float T = *p.temperature, thr = p.warp[row].thr;
+  const uint64_t seed = p.rng[0], base = p.rng[1] + uint64_t(p.stream + row) * kRngStreamLen;
+  if (threadIdx.x == 0) s_best = 0ull;
+  __syncthreads();
+  const int chunk = (p.V + gridDim.x - 1) / gridDim.x;
+  const int j0 = min(p.V, int(blockIdx.x) * chunk), j1 = min(p.V, j0 + chunk);
+  unsigned long long best = 0ull;
+  for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x) {
+    const float x = z[j] / T;
+    if (!(x >= thr)) continue;
+    const unsigned long long key = argmax_key(x + philox_gumbel_f(seed, base + uint64_t(j)), uint32_t(j));
+    if (key > best) best = key;
+  }
+  if (best) atomicMax(&s_best, best);
+  __syncthreads();
+  if (threadIdx.x == 0 && s_best) atomicMax(&p.keys[row], s_best);
+}
 // Softmax statistics of logit rows at temperature T, in slices: block b of a row's nb blocks
 // writes (max of z / T, sum of exp(z / T - max)) over its slice. Rows [0, R1) are z1 (length
 // V1, row stride V1), then rows [R1, R1 + R2) are z2 (length V2).
@@ -606,8 +785,9 @@ struct SampleAcceptParams {
   const float* zd;
   int Vd;
   const int* vocab_inv;  // [V] or nullptr
-  const float2* stats;   // logit_stats_kernel: target rows (nbt each), then draft rows (nbd each)
+  const float2* stats;   // logit_stats_kernel: target rows (nbt each, unless warped), then draft rows (nbd each)
   int nbt, nbd;
+  const RowWarp* warp;   // warped target rows (top-k / top-p), or nullptr
   double* part;          // [gridDim][3]: residual mass, residual key, p key (bits)
   unsigned* counter;     // zero at launch; left at zero
   int* out_host_view;
@@ -623,6 +803,7 @@ __global__ void __launch_bounds__(256) accept_sampled_kernel(__grid_constant__ c
   pdl_launch_dependents();
   pdl_wait();
   __shared__ double sM[MAXK + 1], sS[MAXK + 1], dM[MAXK], dS[MAXK];
+  __shared__ float sThr[MAXK + 1];
   __shared__ int s_a;
   __shared__ double red_d[32];
   __shared__ unsigned long long s_kr, s_kp;
@@ -632,10 +813,16 @@ __global__ void __launch_bounds__(256) accept_sampled_kernel(__grid_constant__ c
   const float T = st->temperature;
   const uint64_t seed = st->rng[0], base = st->rng[1];
   // ---- per-row statistics from the slices, in slice order
-  if (tid < 2 * K + 1) {
+  if (tid < 2 * K + 1 && tid <= K && p.warp) {
+    sM[tid] = p.warp[tid].M;
+    sS[tid] = p.warp[tid].Z;
+    sThr[tid] = p.warp[tid].thr;
+  } else if (tid < 2 * K + 1) {
     const bool tgt = tid <= K;
     const int r = tgt ? tid : tid - K - 1, nb = tgt ? p.nbt : p.nbd;
-    const float2* s = p.stats + (tgt ? size_t(r) * p.nbt : size_t(K + 1) * p.nbt + size_t(r) * p.nbd);
+    const size_t tslices = p.warp ? 0 : size_t(K + 1) * p.nbt;
+    const float2* s = p.stats + (tgt ? size_t(r) * p.nbt : tslices + size_t(r) * p.nbd);
+    if (tgt) sThr[r] = -INFINITY;
     double M = -INFINITY;
     for (int b = 0; b < nb; ++b) M = fmax(M, double(s[b].x));
     double S = 0.0;
@@ -662,7 +849,8 @@ __global__ void __launch_bounds__(256) accept_sampled_kernel(__grid_constant__ c
       const int row = sample_row_of(p, x);
       const double qx = row >= 0 ? exp(double(p.zd[size_t(a) * p.Vd + row] / T) - dM[a]) / dS[a] : 0.0;
       if (!(qx > 0.0)) break;
-      const double px = exp(double(p.zt[size_t(a) * p.V + x] / T) - sM[a]) / sS[a];
+      const float xt = p.zt[size_t(a) * p.V + x] / T;
+      const double px = xt >= sThr[a] ? exp(double(xt) - sM[a]) / sS[a] : 0.0;
       const double u = philox_uniform(seed, base + uint64_t(kRngAcceptStream) * kRngStreamLen + uint64_t(a));
       const double ratio = px / qx;
       if (!(u < (ratio < 1.0 ? ratio : 1.0))) break;
@@ -679,7 +867,8 @@ __global__ void __launch_bounds__(256) accept_sampled_kernel(__grid_constant__ c
   double mass = 0.0;
   unsigned long long kr = 0ull, kp = 0ull;
   for (int j = j0 + tid; j < j1; j += blockDim.x) {
-    const double pj = exp(double(zr[j] / T) - sM[a]) / sS[a];
+    const float xj = zr[j] / T;
+    const double pj = xj >= sThr[a] ? exp(double(xj) - sM[a]) / sS[a] : 0.0;
     double rj = pj;
     if (qr) {
       const int row = sample_row_of(p, j);

@@ -2588,24 +2588,56 @@ const float* prefill_gemm_forward(wc_target* t, wc_kv* kv, const int* tokens_dev
 
 namespace {
 
-// probs_from_logits (sampling.py:39-55) on the device covers the temperature; top-k and
-// top-p warping are refused rather than silently ignored.
+// probs_from_logits (sampling.py:39-55) on the device: temperature, top-k, top-p.
 bool sampling_on(const wc_sampling_params* sp) {
   if (!sp || !(sp->temperature > 0.f)) return false;
-  if (sp->top_k > 0) fail(WC_ERR_UNSUPPORTED, "sampled decoding on the device: top_k is not supported yet");
-  if (sp->top_p < 1.f) fail(WC_ERR_UNSUPPORTED, "sampled decoding on the device: top_p is not supported yet");
+  if (sp->top_k < 0) fail(WC_ERR_INVALID, "top_k must be >= 0");
+  if (!(sp->top_p > 0.f) || sp->top_p > 1.f) fail(WC_ERR_INVALID, "top_p must be in (0, 1]");
   return true;
 }
+bool warping_on(const wc_sampling_params* sp) { return sp && (sp->top_k > 0 || sp->top_p < 1.f); }
 
-// RoundState's random state and temperature: seed, counter base 0 (the first token's draw)
+// RoundState's random state and warping: seed, counter base 0 (the first token's draw), T,
+// top-k, top-p
 void seed_rounds(wc_ctx* ctx, RoundState* st, const wc_sampling_params* sp, bool on) {
   struct {
     unsigned long long rng[2];
     float temperature;
+    int top_k;
+    float top_p;
     int pad;
-  } v{{on ? (unsigned long long)sp->seed : 0ull, 0ull}, on ? sp->temperature : 0.f, 0};
+  } v{{on ? (unsigned long long)sp->seed : 0ull, 0ull}, on ? sp->temperature : 0.f, on ? sp->top_k : 0,
+      on ? sp->top_p : 1.f, 0};
   static_assert(sizeof(v) == sizeof(RoundState) - offsetof(RoundState, rng), "RoundState tail layout");
   CUDA_TRY(cudaMemcpyAsync(st->rng, &v, sizeof(v), cudaMemcpyHostToDevice, ctx->stream));
+}
+
+// A warped draw from logits rows z [rows][V] into keys[0..rows) (first token / autoregressive
+// step): thresholds, then the Gumbel-max over the kept tokens (stream 0 + row).
+void warped_draw(wc_ctx* ctx, RoundState* st, const float* z, int rows, int V, RowWarp* warp,
+                 unsigned long long* keys) {
+  WarpParams w;
+  std::memset(&w, 0, sizeof(w));
+  w.z = z;
+  w.V = V;
+  w.ld = V;
+  w.temperature = &st->temperature;
+  w.top_k = &st->top_k;
+  w.top_p = &st->top_p;
+  w.out = warp;
+  w.zero_keys = keys;
+  w.zero_n = rows;
+  launch_ex(ctx, "warp rows", warp_rows_kernel, dim3(rows), dim3(1024), 0, true, 1, w);
+  SampleRowsParams sr;
+  sr.z = z;
+  sr.V = V;
+  sr.ld = V;
+  sr.temperature = &st->temperature;
+  sr.warp = warp;
+  sr.rng = st->rng;
+  sr.stream = 0;
+  sr.keys = keys;
+  launch_ex(ctx, "sample rows", sample_rows_kernel, dim3(148, rows), dim3(256), 0, true, 1, sr);
 }
 
 }  // namespace
@@ -2639,6 +2671,8 @@ struct wc_decoder {
   // sampled decoding (temperature > 0, set by the prefill): the round's logits, their softmax
   // slices and the acceptance kernel's partials
   bool sampled = false;
+  bool warped = false;       // top-k / top-p on the target distribution
+  RowWarp* rwarp = nullptr;  // [max_k + 1] warp thresholds of the verify rows
   float* zt = nullptr;       // [max_k + 1][V] target logits of the verify rows
   float* zd = nullptr;       // [max_k][head rows] draft logits
   float2* zstats = nullptr;  // logit_stats_kernel output
@@ -2755,9 +2789,21 @@ void build_round(wc_decoder* dec, int K) {
   // ---- acceptance + chain compaction (spec.py:357-362; sampled: spec.py:321-324 with
   // verify_tree_stochastic on the chain)
   if (smp) {
+    if (dec->warped) {  // top-k / top-p thresholds of the verify rows
+      WarpParams w;
+      std::memset(&w, 0, sizeof(w));
+      w.z = dec->zt;
+      w.V = t->cfg.vocab;
+      w.ld = t->cfg.vocab;
+      w.temperature = &st->temperature;
+      w.top_k = &st->top_k;
+      w.top_p = &st->top_p;
+      w.out = dec->rwarp;
+      launch_ex(ctx, "warp rows", warp_rows_kernel, dim3(K + 1), dim3(1024), 0, true, 1, w);
+    }
     StatsParams sp;
     sp.z1 = dec->zt;
-    sp.R1 = K + 1;
+    sp.R1 = dec->warped ? 0 : K + 1;
     sp.V1 = t->cfg.vocab;
     sp.nb1 = dec->nbt;
     sp.z2 = dec->zd;
@@ -2766,7 +2812,7 @@ void build_round(wc_decoder* dec, int K) {
     sp.nb2 = dec->nbd;
     sp.temperature = &st->temperature;
     sp.out = dec->zstats;
-    launch_ex(ctx, "logit stats", logit_stats_kernel, dim3((K + 1) * dec->nbt + K * dec->nbd), dim3(256), 0, true, 1,
+    launch_ex(ctx, "logit stats", logit_stats_kernel, dim3(sp.R1 * dec->nbt + K * dec->nbd), dim3(256), 0, true, 1,
               sp);
     SampleAcceptParams ap;
     ap.st = st;
@@ -2779,6 +2825,7 @@ void build_round(wc_decoder* dec, int K) {
     ap.stats = dec->zstats;
     ap.nbt = dec->nbt;
     ap.nbd = dec->nbd;
+    ap.warp = dec->warped ? dec->rwarp : nullptr;
     ap.part = dec->apart;
     ap.counter = dec->acount;
     ap.out_host_view = dec->out_dev;
@@ -2805,7 +2852,9 @@ void build_round(wc_decoder* dec, int K) {
   launch_finish(dec, &st->L_upd, K + 1, true);
 }
 
-int graph_key(const wc_decoder* dec, int K) { return K + (dec->sampled ? kSampledGraphKey : 0); }
+int graph_key(const wc_decoder* dec, int K) {
+  return K + (dec->sampled ? kSampledGraphKey : 0) + (dec->warped ? 2 * kSampledGraphKey : 0);
+}
 
 std::pair<cudaGraphExec_t, uint64_t>& round_graph(wc_decoder* dec, int K, bool profiled = false) {
   auto& store = profiled ? dec->prof_graphs : dec->graphs;
@@ -2925,6 +2974,7 @@ extern "C" wc_status wc_decoder_create(wc_target* t, wc_drafter* d, int max_cont
       dec->zd = static_cast<float*>(dalloc(sizeof(float) * size_t(max_k) * Vd));
       dec->zstats = static_cast<float2*>(dalloc(sizeof(float2) * size_t((max_k + 1) * dec->nbt + max_k * dec->nbd)));
       dec->apart = static_cast<double*>(dalloc(sizeof(double) * 3 * kAcceptBlocks));
+      dec->rwarp = static_cast<RowWarp*>(dalloc(sizeof(RowWarp) * (MAXK + 1)));
       dec->acount = static_cast<unsigned*>(dalloc(sizeof(unsigned)));
       CUDA_TRY(cudaMemset(dec->acount, 0, sizeof(unsigned)));
     }
@@ -2946,7 +2996,8 @@ extern "C" void wc_decoder_destroy(wc_decoder* dec) {
   if (dec->out_host) cudaFreeHost(dec->out_host);
   for (void* p : {(void*)dec->root_out, (void*)dec->root_fb, (void*)dec->xf_root, (void*)dec->xf_fb,
                   (void*)dec->ss_fb, (void*)dec->taps, (void*)dec->zt, (void*)dec->zd, (void*)dec->zstats,
-                  (void*)dec->apart, (void*)dec->acount, (void*)dec->saved_st, (void*)dec->saved_root})
+                  (void*)dec->apart, (void*)dec->acount, (void*)dec->saved_st, (void*)dec->saved_root,
+                  (void*)dec->rwarp})
     dfree(p);
   if (dec->ev0) cudaEventDestroy(dec->ev0);
   if (dec->ev1) cudaEventDestroy(dec->ev1);
@@ -2994,8 +3045,16 @@ int decoder_prefill_impl(wc_decoder* dec, const int* prompt, int n, const wc_sam
   TapOut tg;
   tg.rows = dec->taps;
   tg.stride = tstride;
+  const bool warp = smp && warping_on(sp);
   const float* last = prefill_gemm_forward(t, dec->tkv, d_tok, n, 0, &tg);
-  if (last) target_head_rows(t, last, 1, dec->st->keys, nullptr, err, smp ? &pick : nullptr);
+  if (last) {
+    if (warp) {  // logits of the last row, then the warped draw
+      target_head_rows(t, last, 1, dec->st->keys + 1, dec->zt, err);
+      warped_draw(ctx, dec->st, dec->zt, 1, t->cfg.vocab, dec->rwarp, dec->st->keys);
+    } else {
+      target_head_rows(t, last, 1, dec->st->keys, nullptr, err, smp ? &pick : nullptr);
+    }
+  }
   for (int r0 = 0; r0 < n && !last; r0 += GEMV_MAXL) {
     const int rows = std::min(GEMV_MAXL, n - r0);
     Rows r;
@@ -3007,8 +3066,14 @@ int decoder_prefill_impl(wc_decoder* dec, const int* prompt, int n, const wc_sam
     to.rows = dec->taps + size_t(r0) * Ht;
     to.stride = tstride;
     target_layers(t, dec->tkv, r, in0, t->ws_h, &to, err);
-    if (r0 + rows == n)
-      target_head_rows(t, t->ws_h + size_t(rows - 1) * Ht, 1, dec->st->keys, nullptr, err, smp ? &pick : nullptr);
+    if (r0 + rows == n) {
+      if (warp) {
+        target_head_rows(t, t->ws_h + size_t(rows - 1) * Ht, 1, dec->st->keys + 1, dec->zt, err);
+        warped_draw(ctx, dec->st, dec->zt, 1, t->cfg.vocab, dec->rwarp, dec->st->keys);
+      } else {
+        target_head_rows(t, t->ws_h + size_t(rows - 1) * Ht, 1, dec->st->keys, nullptr, err, smp ? &pick : nullptr);
+      }
+    }
   }
   int first = 0;
   {
@@ -3051,6 +3116,7 @@ int decoder_prefill_impl(wc_decoder* dec, const int* prompt, int n, const wc_sam
   dec->host_n = n;
   dec->prefilled = true;
   dec->sampled = smp;
+  dec->warped = warp;
   return first;
 }
 
@@ -3258,6 +3324,7 @@ extern "C" wc_status wc_generate_autoregressive(wc_target* t, const int* prompt,
                                                 int max_context, int* out_tokens, int* out_n, wc_gen_stats* stats) {
   if (!t || !prompt || !out_tokens || !out_n || n < 1 || max_new < 1) return WC_ERR_INVALID;
   return guard(t->ctx, [&] {
+    Pick pick_;
     const bool smp = sampling_on(sp);
     wc_ctx* ctx = t->ctx;
     const int Ht = t->cfg.hidden;
@@ -3273,6 +3340,27 @@ extern "C" wc_status wc_generate_autoregressive(wc_target* t, const int* prompt,
     int* d_tok = static_cast<int*>(dalloc(sizeof(int) * n));
     int* d_out = static_cast<int*>(dalloc(sizeof(int) * 4));
     float* h = static_cast<float*>(dalloc(sizeof(float) * GEMV_MAXL * Ht));
+    const bool warp = smp && warping_on(sp);
+    float* zw = warp ? static_cast<float*>(dalloc(sizeof(float) * t->cfg.vocab)) : nullptr;  // warped draws
+    RowWarp* rw = warp ? static_cast<RowWarp*>(dalloc(sizeof(RowWarp))) : nullptr;
+    struct FreeW {
+      void* a[2];
+      ~FreeW() {
+        for (void* p : a) dfree(p);
+      }
+    } frw{{zw, rw}};
+    // the step's draw: plain argmax, Gumbel-max in the head, or the warped draw from logits
+    auto head_draw = [&](const float* hrow, const XIn* hx) {
+      if (warp) {
+        if (hx) target_head(t, *hx, 1, nullptr, 1, st->keys + 1, zw, &st->err);
+        else target_head_rows(t, hrow, 1, st->keys + 1, zw, &st->err);
+        warped_draw(ctx, st, zw, 1, t->cfg.vocab, rw, st->keys);
+      } else if (hx) {
+        target_head(t, *hx, 1, nullptr, 1, st->keys, nullptr, &st->err, smp ? &pick_ : nullptr);
+      } else {
+        target_head_rows(t, hrow, 1, st->keys, nullptr, &st->err, smp ? &pick_ : nullptr);
+      }
+    };
     cudaGraphExec_t exec = nullptr;
     struct Free {
       void* a[4];
@@ -3284,14 +3372,13 @@ extern "C" wc_status wc_generate_autoregressive(wc_target* t, const int* prompt,
     } fr{{st, d_tok, d_out, h}, &exec};
     CUDA_TRY(cudaMemsetAsync(st, 0, sizeof(RoundState), ctx->stream));
     seed_rounds(ctx, st, sp, smp);
-    Pick pick;  // spec.py:377-397 samples each step from probs_from_logits
-    pick.temperature = &st->temperature;
-    pick.rng = st->rng;
+    pick_.temperature = &st->temperature;  // spec.py:377-397 samples each step from probs_from_logits
+    pick_.rng = st->rng;
     CUDA_TRY(cudaMemcpyAsync(d_tok, prompt, sizeof(int) * n, cudaMemcpyHostToDevice, ctx->stream));
     for (int i = 0; i < n; ++i)
       if (prompt[i] < 0 || prompt[i] >= t->cfg.vocab) fail(WC_ERR_INVALID, "prompt token id out of range");
     const float* last = prefill_gemm_forward(t, kv.get(), d_tok, n, 0, nullptr);
-    if (last) target_head_rows(t, last, 1, st->keys, nullptr, &st->err, smp ? &pick : nullptr);
+    if (last) head_draw(last, nullptr);
     for (int r0 = 0; r0 < n && !last; r0 += GEMV_MAXL) {
       const int rows = std::min(GEMV_MAXL, n - r0);
       Rows r;
@@ -3301,7 +3388,7 @@ extern "C" wc_status wc_generate_autoregressive(wc_target* t, const int* prompt,
       const XIn in0 = target_embed(t, r, d_tok + r0, nullptr, nullptr, h, &st->err);
       target_layers(t, kv.get(), r, in0, h, nullptr, &st->err);
       if (r0 + rows == n)
-        target_head_rows(t, h + size_t(rows - 1) * Ht, 1, st->keys, nullptr, &st->err, smp ? &pick : nullptr);
+        head_draw(h + size_t(rows - 1) * Ht, nullptr);
     }
     // st->n = n - 1 so that the first advance makes it n while emitting the first token
     RoundState init{};
@@ -3333,7 +3420,7 @@ extern "C" wc_status wc_generate_autoregressive(wc_target* t, const int* prompt,
           r.n_dev = &st->n;
           const XIn in0 = target_embed(t, r, nullptr, st, nullptr, h, &st->err);
           const XIn hx = target_layers(t, kv.get(), r, in0, h, nullptr, &st->err);
-          target_head(t, hx, 1, nullptr, 1, st->keys, nullptr, &st->err, smp ? &pick : nullptr);
+          head_draw(nullptr, &hx);
           ar_advance_kernel<<<1, 32, 0, ctx->stream>>>(st, d_out);
           check_launch(ctx, "ar advance");
         } catch (...) {
