@@ -197,6 +197,11 @@ WC_API wc_status wc_accept_stochastic_noalloc(wc_ctx* ctx, const double* p_dev, 
                                        uint64_t offset, int* out_path_dev, int* out_n_dev, int* out_next_dev,
                                        int* out_used_dev);
 /* fp64 uniforms of the Philox stream, for the host side of tests and for draft sampling */
+/* probs_from_logits (sampling.py:39-55): rows of device fp32 logits [rows][V] -> warped
+ * probabilities (temperature, top_k (0 = off), top_p (1 = off)) into out [rows][V]. Ties that
+ * fall exactly on the top-k / top-p cut are all kept. */
+WC_API wc_status wc_probs_from_logits(wc_ctx* ctx, const float* logits, int rows, int V, float temperature,
+                                      int top_k, float top_p, float* out);
 WC_API wc_status wc_philox_uniforms(wc_ctx* ctx, uint64_t seed, uint64_t offset, int n, double* out_dev);
 
 /* ------------------------------------------------------------------ speculative decoder

@@ -104,6 +104,7 @@ SIGNATURES = {
     "wc_accept_stochastic": (S, [P, P, P, C.c_int, P, P, C.c_int, C.c_uint64, C.c_uint64, P, P, P, P]),
     "wc_accept_stochastic_noalloc": (S, [P, P, P, C.c_int, P, P, C.c_int, C.c_uint64, C.c_uint64, P, P, P, P]),
     "wc_philox_uniforms": (S, [P, C.c_uint64, C.c_uint64, C.c_int, P]),
+    "wc_probs_from_logits": (S, [P, P, C.c_int, C.c_int, C.c_float, C.c_int, C.c_float, P]),
     "wc_decoder_create": (S, [P, P, C.c_int, C.c_int, C.POINTER(P)]),
     "wc_decoder_destroy": (None, [P]),
     "wc_decoder_prefill": (S, [P, I32P, C.c_int, C.POINTER(SamplingParamsC), I32P]),

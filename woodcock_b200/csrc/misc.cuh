@@ -678,6 +678,17 @@ __global__ void __launch_bounds__(1024) warp_rows_kernel(__grid_constant__ const
   if (tid == 0) p.out[row] = RowWarp{M, keep_key ? order_key_value(keep_key) : -INFINITY, Z};
 }
 
+// probs_from_logits (sampling.py:39-55) from the warp thresholds: p_j = [x_j >= thr] exp(x_j - M) / Z
+__global__ void warped_probs_kernel(const float* z, int V, const float* temperature, const RowWarp* warp, float* out) {
+  const int row = blockIdx.y;
+  const RowWarp w = warp[row];
+  const float T = *temperature;
+  for (int j = blockIdx.x * blockDim.x + threadIdx.x; j < V; j += gridDim.x * blockDim.x) {
+    const float x = z[size_t(row) * V + j] / T;
+    out[size_t(row) * V + j] = x >= w.thr ? float(exp(double(x) - double(w.M)) / w.Z) : 0.f;
+  }
+}
+
 // Gumbel-max draws over the kept tokens of warped rows (the warped autoregressive step and
 // first token): keys[row] = argmax over x_j >= thr of (x_j + Gumbel), stream `stream` + row.
 struct SampleRowsParams {

@@ -118,6 +118,8 @@ struct wc_ctx {
   bool stack = false;                    // persistent layer-stack kernel for the verify pass (opt-in: WC_STACK=1)
   int occ_stack = 0;                     // its blocks per SM (0: unavailable)
   float* sk_part = nullptr;              // its attention partial states
+  void* pw_scratch = nullptr;            // wc_probs_from_logits: parameters + row thresholds
+  int pw_rows = 0;
   int* sk_counters = nullptr;            // its per-head arrival counters (zero between launches)
   uint32_t* lin_xf = nullptr;  // input fragments of the ops-API linear
   int lin_xf_k = 0;
@@ -780,6 +782,7 @@ extern "C" void wc_ctx_destroy(wc_ctx* ctx) {
   dfree(ctx->gv_partial);
   dfree(ctx->gv_counters);
   dfree(ctx->sk_part);
+  dfree(ctx->pw_scratch);
   dfree(ctx->sk_counters);
   dfree(ctx->pw);
   dfree(ctx->qw);
@@ -960,6 +963,42 @@ extern "C" wc_status wc_philox_uniforms(wc_ctx* ctx, uint64_t seed, uint64_t off
     if (n == 0) return;
     philox_uniforms_kernel<<<(n + 255) / 256, 256, 0, ctx->stream>>>(seed, offset, n, out);
     check_launch(ctx, "philox");
+  });
+}
+
+extern "C" wc_status wc_probs_from_logits(wc_ctx* ctx, const float* logits, int rows, int V, float temperature,
+                                          int top_k, float top_p, float* out) {
+  if (!ctx || !logits || !out || rows < 1 || V < 1) return WC_ERR_INVALID;
+  return guard(ctx, [&] {
+    if (top_k < 0 || !(top_p > 0.f) || top_p > 1.f) fail(WC_ERR_INVALID, "top_k >= 0 and top_p in (0, 1]");
+    struct {
+      float T;
+      int k;
+      float p;
+      int pad;
+    } prm{std::max(temperature, 1e-6f), top_k, top_p, 0};
+    if (ctx->pw_rows < rows) {  // scratch: parameters + per-row thresholds
+      CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+      dfree(ctx->pw_scratch);
+      ctx->pw_scratch = dalloc(16 + sizeof(RowWarp) * size_t(rows));
+      ctx->pw_rows = rows;
+    }
+    char* sc = static_cast<char*>(ctx->pw_scratch);
+    CUDA_TRY(cudaMemcpyAsync(sc, &prm, sizeof(prm), cudaMemcpyHostToDevice, ctx->stream));
+    RowWarp* rw = reinterpret_cast<RowWarp*>(sc + 16);
+    WarpParams w;
+    std::memset(&w, 0, sizeof(w));
+    w.z = logits;
+    w.V = V;
+    w.ld = V;
+    w.temperature = reinterpret_cast<const float*>(sc);
+    w.top_k = reinterpret_cast<const int*>(sc + 4);
+    w.top_p = reinterpret_cast<const float*>(sc + 8);
+    w.out = rw;
+    launch_ex(ctx, "warp rows", warp_rows_kernel, dim3(rows), dim3(1024), 0, false, 1, w);
+    warped_probs_kernel<<<dim3(std::min(148, (V + 255) / 256), rows), 256, 0, ctx->stream>>>(
+        logits, V, reinterpret_cast<const float*>(sc), rw, out);
+    check_launch(ctx, "probs_from_logits");
   });
 }
 

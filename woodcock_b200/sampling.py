@@ -168,10 +168,12 @@ def verify_chain_stochastic(p, q, draft_tokens: list[int], rng: PhiloxStream) ->
 
 
 def probs_from_logits(logits: torch.Tensor, sp: SamplingParams) -> torch.Tensor:
-    """Temperature softmax on the device (sampling.py:39-55). top-k / top-p warping is not built."""
-    from .ops import softmax
-
-    if sp.top_k or sp.top_p < 1.0:
-        raise NotImplementedError("top-k / top-p warping is not built on the device yet")
-    x = (logits.float() / max(sp.temperature, 1e-6)).contiguous()
-    return softmax(x)
+    """sampling.py:39-55 on the device: temperature, top-k, top-p (wc_probs_from_logits)."""
+    ctx = Context.get(logits.device)
+    V = logits.shape[-1]
+    x = logits.float().reshape(-1, V).contiguous()
+    out = torch.empty_like(x)
+    with ctx.enter(x, out):
+        ctx.check(lib().wc_probs_from_logits(ctx.h, ptr(x), x.shape[0], V, float(sp.temperature), int(sp.top_k),
+                                             float(sp.top_p), ptr(out)))
+    return out.reshape(logits.shape)

@@ -180,8 +180,8 @@ class SpeculativeDecoder:
                  stop_on_eos: bool = True) -> tuple[list[int], GenStats]:
         """spec.py:151-212: returns (tokens, GenStats)."""
         chain = isinstance(self.policy, StaticPolicy) and self.policy.width == 1
-        if not chain:
-            raise WcValueError(WC_ERR_UNSUPPORTED, "only chain policies run on the device round so far")
+        if not chain or not self.fused:  # trees, and the synced path (spec.py:168-202)
+            return self._generate_host(prompt, max_new_tokens, sp, stop_on_eos)
         st = GenStats(prompt_tokens=len(prompt), fused=True)
         eos = self.t.eos_token_ids if stop_on_eos else set()
         t0 = time.perf_counter()
@@ -217,6 +217,35 @@ class SpeculativeDecoder:
             x_n = out[-1]
         if forced_active:
             self.set_forced(None)
+        st.t_total = time.perf_counter() - t0
+        st.new_tokens = len(out)
+        return out, st
+
+    def _generate_host(self, prompt: list[int], max_new_tokens: int, sp: SamplingParams,
+                       stop_on_eos: bool) -> tuple[list[int], GenStats]:
+        """Draft trees (any policy) and fused=False: host-driven rounds over the device API
+        (woodcock_b200.tree), one synchronisation per drafted level as in the reference."""
+        from .sampling import PhiloxStream
+        from .tree import HostRounds
+
+        st = GenStats(prompt_tokens=len(prompt), fused=False)
+        rng = PhiloxStream(sp.seed, device=self.ctx.device.index or 0)
+        eos = self.t.eos_token_ids if stop_on_eos else set()
+        t0 = time.perf_counter()
+        hr = HostRounds(self.t, self.d, self.policy, self.max_context + 256)
+        x_n = hr.prefill(prompt, sp, rng)
+        st.t_prefill = time.perf_counter() - t0
+        out = [x_n]
+        n = len(prompt)
+        self.policy.reset()
+        while len(out) < max_new_tokens and x_n not in eos:
+            acc = hr.round(x_n, n, sp, rng, st)
+            for tok in acc:
+                out.append(tok)
+                if tok in eos or len(out) >= max_new_tokens:
+                    break
+            n += len(acc)
+            x_n = out[-1]
         st.t_total = time.perf_counter() - t0
         st.new_tokens = len(out)
         return out, st
