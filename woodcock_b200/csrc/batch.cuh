@@ -261,6 +261,212 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
   }
 }
 
+// ---------------------------------------------------------------------------- persistent GEMM
+// One block per SM loops over the tiles (m fastest, so the blocks that run together share
+// weight tiles in L2). Two TMEM accumulators (2 x BN columns): while the four epilogue warps
+// drain tile i from one, the MMA thread fills the other with tile i + 1, and the TMA producer
+// runs ahead through the shared-memory ring across tile boundaries.
+template <int BN>
+__device__ __forceinline__ void tc_epilogue_tile(const GemmTc& p, uint32_t tl, int row, int n0) {
+  const bool rv = row < p.M;
+  if (p.epi == TC_SWIGLU) {
+    constexpr int H2 = BN / 2;
+#pragma unroll 1
+    for (int c0 = 0; c0 < H2; c0 += 16) {
+      float g[16], u[16];
+      tmem_ld16(tl + c0, g);
+      tmem_ld16(tl + H2 + c0, u);
+      const int f0 = n0 / 2 + c0;
+      if (rv && f0 < p.N / 2) {
+        uint32_t o[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const float a = g[2 * i] / (1.f + expf(-g[2 * i])) * u[2 * i];
+          const float b = g[2 * i + 1] / (1.f + expf(-g[2 * i + 1])) * u[2 * i + 1];
+          o[i] = pack2(f32_to_bf16_bits(a), f32_to_bf16_bits(b));
+        }
+        uint4* dst = reinterpret_cast<uint4*>(p.cb + size_t(row) * p.ldcb + f0);
+        dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+        dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+      }
+    }
+  } else if (p.epi == TC_ARGMAX) {
+    unsigned long long best = 0ull;
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+      float v[16];
+      tmem_ld16(tl + c0, v);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int col = n0 + c0 + i;
+        if (col < p.N) {
+          const unsigned long long k = argmax_key(v[i], uint32_t(col));
+          if (k > best) best = k;
+        }
+      }
+    }
+    if (rv && best) atomicMax(&p.keys[row], best);
+  } else {
+#pragma unroll 1
+    for (int c0 = 0; c0 < BN; c0 += 16) {
+      float v[16];
+      tmem_ld16(tl + c0, v);
+      if (!rv) continue;
+      const int col0 = n0 + c0;
+      if (p.epi == TC_BF16) {
+        if (col0 + 16 <= p.N) {
+          uint32_t o[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) o[i] = pack2(f32_to_bf16_bits(v[2 * i]), f32_to_bf16_bits(v[2 * i + 1]));
+          uint4* dst = reinterpret_cast<uint4*>(p.cb + size_t(row) * p.ldcb + col0);
+          dst[0] = make_uint4(o[0], o[1], o[2], o[3]);
+          dst[1] = make_uint4(o[4], o[5], o[6], o[7]);
+        } else {
+          for (int i = 0; i < 16; ++i)
+            if (col0 + i < p.N) p.cb[size_t(row) * p.ldcb + col0 + i] = f32_to_bf16_bits(v[i]);
+        }
+        continue;
+      }
+      float* dst = p.c + size_t(row) * p.ldc + col0;
+      const float* rs = p.epi == TC_ADD ? p.r + size_t(row) * p.ldr + col0 : nullptr;
+      if (col0 + 16 <= p.N) {
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+          float4 o = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+          if (rs) {
+            const float4 a = *reinterpret_cast<const float4*>(rs + i);
+            o.x += a.x;
+            o.y += a.y;
+            o.z += a.z;
+            o.w += a.w;
+          }
+          *reinterpret_cast<float4*>(dst + i) = o;
+        }
+      } else {
+        for (int i = 0; i < 16; ++i)
+          if (col0 + i < p.N) dst[i] = v[i] + (rs ? rs[i] : 0.f);
+      }
+    }
+  }
+}
+
+template <int BN>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    gemm_tcp_kernel(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+                    const __grid_constant__ GemmTc p) {
+  static_assert(BN == 128 || BN == 256, "tile width");
+  constexpr int SA = TC_BM * TC_BK * 2, SB = BN * TC_BK * 2, SS = SA + SB;
+  extern __shared__ unsigned char tcp_raw[];
+  unsigned char* sm = tcp_raw + ((1024u - (smem_addr(tcp_raw) & 1023u)) & 1023u);
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + TC_STAGES * SS);
+  uint64_t* empty = full + TC_STAGES;
+  uint64_t* acc_full = empty + TC_STAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;      // [2]
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  const int warp = threadIdx.x / kWarp, lane = threadIdx.x % kWarp;
+  const int KB = (p.K + TC_BK - 1) / TC_BK;
+  const int mt = (p.M + TC_BM - 1) / TC_BM, ntiles = mt * ((p.N + BN - 1) / BN);
+  const int my_tiles = int(blockIdx.x) < ntiles ? (ntiles - 1 - int(blockIdx.x)) / int(gridDim.x) + 1 : 0;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < TC_STAGES; ++s) {
+      mbar_init(full + s, 1);
+      mbar_init(empty + s, 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(acc_full + b, 1);
+      mbar_init(acc_empty + b, 4);  // one arrival per epilogue warp
+    }
+    mbar_fence_init();
+  }
+  if (warp == 1) {  // two accumulators of BN fp32 columns
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_addr(tslot)),
+                 "r"(uint32_t(2 * BN))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tslot;
+  pdl_launch_dependents();
+  pdl_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {  // ---- TMA producer, across tiles
+      int q = 0;
+      bool ok = true;
+      for (int i = 0; i < my_tiles && ok; ++i) {
+        const int t = int(blockIdx.x) + i * int(gridDim.x);
+        const int m0 = (t % mt) * TC_BM, n0 = (t / mt) * BN;
+        for (int kb = 0; kb < KB; ++kb, ++q) {
+          const int s = q % TC_STAGES;
+          if (q >= TC_STAGES && !mbar_wait(empty + s, ((q / TC_STAGES) - 1) & 1)) {
+            raise_error(p.err, kErrTimeout);
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(full + s, SS);
+          tma_load_2d(sm + s * SS, &ta, kb * TC_BK, m0, full + s);
+          tma_load_2d(sm + s * SS + SA, &tb, kb * TC_BK, n0, full + s);
+        }
+      }
+      for (int qq = max(0, q - TC_STAGES); qq < q; ++qq)
+        if (!mbar_wait(full + qq % TC_STAGES, (qq / TC_STAGES) & 1)) raise_error(p.err, kErrTimeout);
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {  // ---- MMA issuer
+      constexpr uint32_t idesc = umma_idesc_bf16<BN>();
+      int q = 0;
+      bool ok = true;
+      for (int i = 0; i < my_tiles; ++i) {
+        const int b = i & 1;
+        if (ok && i >= 2 && !mbar_wait(acc_empty + b, ((i / 2) - 1) & 1)) {
+          raise_error(p.err, kErrTimeout);
+          ok = false;
+        }
+        tc_fence_after();
+        const uint32_t acc = tmem + uint32_t(b * BN);
+        for (int kb = 0; kb < KB && ok; ++kb, ++q) {
+          const int s = q % TC_STAGES;
+          if (!mbar_wait(full + s, (q / TC_STAGES) & 1)) {
+            raise_error(p.err, kErrTimeout);
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = smem_addr(sm + s * SS), b0 = smem_addr(sm + s * SS + SA);
+#pragma unroll
+          for (int k = 0; k < TC_BK / 16; ++k)
+            umma_bf16(acc, umma_desc_sw128(a0 + 32 * k), umma_desc_sw128(b0 + 32 * k), idesc, (kb | k) != 0);
+          umma_commit(empty + s);
+        }
+        umma_commit(acc_full + b);  // arrives once this tile's MMAs (all issued above) are done
+      }
+    }
+  } else {  // ---- epilogue warps: TMEM lanes [32 (w % 4), +32)
+    const int qd = warp & 3;
+    for (int i = 0; i < my_tiles; ++i) {
+      const int b = i & 1;
+      const int t = int(blockIdx.x) + i * int(gridDim.x);
+      const int m0 = (t % mt) * TC_BM, n0 = (t / mt) * BN;
+      if (!mbar_wait(acc_full + b, (i / 2) & 1)) raise_error(p.err, kErrTimeout);
+      tc_fence_after();
+      tc_epilogue_tile<BN>(p, tmem + uint32_t(b * BN) + (uint32_t(qd * 32) << 16), m0 + qd * 32 + lane, n0);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(acc_empty + b);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(uint32_t(2 * BN))
+                 : "memory");
+  }
+}
+
 // ---------------------------------------------------------------------------- row kernels
 // RMSNorm of fp32 rows into bf16 GEMM operands: out[m] = bf16(x[m] / rms(x[m]) * w); rows
 // of the embedding table when `tokens` is set (x = the gathered row, also copied into h).

@@ -3544,6 +3544,10 @@ bool tc_ready(wc_ctx* ctx) {
                                 int(gemm_tc_smem<128>())));
   CUDA_TRY(cudaFuncSetAttribute(gemm_tc_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(gemm_tc_smem<256>())));
+  CUDA_TRY(cudaFuncSetAttribute(gemm_tcp_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(gemm_tc_smem<128>())));
+  CUDA_TRY(cudaFuncSetAttribute(gemm_tcp_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(gemm_tc_smem<256>())));
   CUDA_TRY(cudaFuncSetAttribute(tree_attention_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(tree_attn_smem<128>())));
   CUDA_TRY(cudaFuncSetAttribute(tree_attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -3559,10 +3563,23 @@ void launch_gemm_tc(wc_ctx* ctx, const CUtensorMap& ta, const CUtensorMap& tb, G
   if (p.M < 1 || p.N < 1 || p.K < 1 || p.K % TC_BK) fail(WC_ERR_INVALID, "GEMM: K must be a multiple of 64");
   if (p.epi == TC_SWIGLU && p.N % BN) fail(WC_ERR_INVALID, "GEMM SwiGLU: N must be a multiple of the tile");
   const dim3 grid((p.M + TC_BM - 1) / TC_BM, (p.N + BN - 1) / BN);
-  if (BN == 256)
+  static const bool persistent = [] {
+    const char* e = std::getenv("WC_GEMM_PERSIST");
+    return !e || std::atoi(e) != 0;
+  }();
+  if (persistent) {
+    const int tiles = int(grid.x * grid.y), blocks = std::min(tiles, ctx->num_sms);
+    if (BN == 256)
+      launch_ex(ctx, "gemm_tcp", gemm_tcp_kernel<256>, dim3(blocks), dim3(TC_THREADS), gemm_tc_smem<256>(), true, 1,
+                ta, tb, p);
+    else
+      launch_ex(ctx, "gemm_tcp", gemm_tcp_kernel<128>, dim3(blocks), dim3(TC_THREADS), gemm_tc_smem<128>(), true, 1,
+                ta, tb, p);
+  } else if (BN == 256) {
     launch_ex(ctx, "gemm_tc", gemm_tc_kernel<256>, grid, dim3(TC_THREADS), gemm_tc_smem<256>(), true, 1, ta, tb, p);
-  else
+  } else {
     launch_ex(ctx, "gemm_tc", gemm_tc_kernel<128>, grid, dim3(TC_THREADS), gemm_tc_smem<128>(), true, 1, ta, tb, p);
+  }
 }
 
 GemmTc gemm_tc_params(int M, int N, int K, int epi) {
