@@ -598,6 +598,7 @@ constexpr int TA_WARPS = TA_THREADS / kWarp;
 constexpr int TA_MAXR = 16 * TA_WARPS;  // 64 query rows
 constexpr int TA_KT = 64;               // keys per tile
 constexpr int TA_MAXN = 64;             // tree nodes
+constexpr int TA_NBUF = 3;              // K/V tile ring: two tiles in flight ahead of the one in use
 
 struct TreeAttnParams {
   const uint16_t* q;  // [M][Hq D]
@@ -616,11 +617,11 @@ struct TreeAttnParams {
   int* err;
 };
 
-// Queries are staged once in the second tile buffer (moved into registers before that
-// buffer's first fill): a block holds 70 KB of shared memory.
+// Queries are staged once in the last tile buffer (moved into registers before that
+// buffer's first fill): a block holds 105 KB of shared memory, two per SM.
 template <int D>
 constexpr size_t tree_attn_smem() {
-  return 2 * 2 * size_t(TA_KT) * (D + 8) * 2 + TA_MAXN * 8 + 64;
+  return size_t(TA_NBUF) * 2 * size_t(TA_KT) * (D + 8) * 2 + TA_MAXN * 8 + 64;
 }
 
 template <int D>
@@ -628,9 +629,9 @@ __global__ void __launch_bounds__(TA_THREADS, 2) tree_attention_kernel(__grid_co
   constexpr int LD = D + 8, NK = D / 16, ND = D / 8;
   static_assert(TA_MAXR <= TA_KT, "queries are staged in a tile buffer");
   extern __shared__ __align__(16) unsigned char ta_smem[];
-  uint16_t* kv = reinterpret_cast<uint16_t*>(ta_smem);    // [2 buffers][K, V][KT][LD]
-  uint16_t* qs = kv + 2 * TA_KT * LD;                     // [MAXR][LD] = buffer 1's K tile, until tile 1 loads
-  unsigned long long* anc = reinterpret_cast<unsigned long long*>(kv + 2 * 2 * TA_KT * LD);  // [MAXN]
+  uint16_t* kv = reinterpret_cast<uint16_t*>(ta_smem);    // [NBUF buffers][K, V][KT][LD]
+  uint16_t* qs = kv + size_t(TA_NBUF - 1) * 2 * TA_KT * LD;  // [MAXR][LD] = the last buffer's K tile
+  unsigned long long* anc = reinterpret_cast<unsigned long long*>(kv + size_t(TA_NBUF) * 2 * TA_KT * LD);
   const int r = blockIdx.x, hk = blockIdx.y;
   const int sp_i = p.causal ? 0 : blockIdx.z;
   const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp, g = lane >> 2, t = lane & 3;
@@ -681,8 +682,10 @@ __global__ void __launch_bounds__(TA_THREADS, 2) tree_attention_kernel(__grid_co
   const int per = (ntiles_all + p.nsplit - 1) / p.nsplit;
   const int tile0 = min(ntiles_all, sp_i * per), ntiles = min(ntiles_all, tile0 + per) - tile0;
   load_tile(tile0, 0);
-  cp_async_commit();
-  cp_async_wait<0>();
+  cp_async_commit();  // group: queries + tile 0
+  if (ntiles > 1) load_tile(tile0 + 1, 1);
+  cp_async_commit();  // group: tile 1
+  cp_async_wait<1>();
   __syncthreads();  // queries, tile 0 and anc visible
 
   const bool active = warp * 16 < R;
@@ -699,7 +702,7 @@ __global__ void __launch_bounds__(TA_THREADS, 2) tree_attention_kernel(__grid_co
 #pragma unroll
     for (int kk = 0; kk < NK; ++kk) ldsm_x4(qa[kk], qs + (r0 + (lane % 16)) * LD + kk * 16 + (lane / 16) * 8);
   }
-  __syncthreads();  // buffer 1 is free for tile 1
+  __syncthreads();  // the last buffer is free for its first tile
   float o[ND][4];
 #pragma unroll
   for (int j = 0; j < ND; ++j)
@@ -709,10 +712,10 @@ __global__ void __launch_bounds__(TA_THREADS, 2) tree_attention_kernel(__grid_co
   const float sl2 = p.scale * 1.4426950408889634f;  // scores in log2 units
 
   for (int tile = 0; tile < ntiles; ++tile) {
-    const int buf = tile & 1;
-    if (tile + 1 < ntiles) load_tile(tile0 + tile + 1, buf ^ 1);
+    const int buf = tile % TA_NBUF;
+    if (tile + 2 < ntiles) load_tile(tile0 + tile + 2, (tile + 2) % TA_NBUF);
     cp_async_commit();
-    cp_async_wait<1>();
+    cp_async_wait<2>();  // this tile's group is complete; the next two may be in flight
     __syncthreads();
     if (active) {
       const uint16_t* kb = kv + size_t(buf) * 2 * TA_KT * LD;
