@@ -3552,6 +3552,8 @@ bool tc_ready(wc_ctx* ctx) {
                                 int(tree_attn_smem<128>())));
   CUDA_TRY(cudaFuncSetAttribute(tree_attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(tree_attn_smem<64>())));
+  CUDA_TRY(cudaFuncSetAttribute(tree_attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                int(tree_attn_tc_smem())));
   done.insert(ctx->device);
   return true;
 }
@@ -3737,7 +3739,16 @@ void batch_forward(wc_batch* b, int nreq, int nodes, bool logits, bool causal = 
     ap.err = err;
     const int gz = causal ? (nodes + TA_MAXR / (Hq / Hk) - 1) / (TA_MAXR / (Hq / Hk)) : ap.nsplit;
     prof_begin(ctx, PK_ATTN);
-    if (D == 128)
+    static const bool tc_attn = [] {
+      const char* e = std::getenv("WC_TA_TC");
+      return e && std::atoi(e) != 0;
+    }();
+    if (tc_attn && D == 128 && !causal && ap.nsplit == 1 && nodes * (Hq / Hk) <= 128) {
+      const int rows = b->B * Hk * b->cap;  // the layer's arena as [rows][head_dim]
+      const CUtensorMap tk = tmap_bf16(ap.K, rows, D, TAT_KT), tv = tmap_bf16(ap.V, rows, D, TAT_KT);
+      launch_ex(ctx, "tree attention tc", tree_attention_tc_kernel, dim3(nreq, Hk), dim3(TAT_THREADS),
+                tree_attn_tc_smem(), true, 1, tk, tv, ap);
+    } else if (D == 128)
       launch_ex(ctx, "tree attention", tree_attention_kernel<128>, dim3(nreq, Hk, gz), dim3(TA_THREADS),
                 tree_attn_smem<128>(), true, 1, ap);
     else
