@@ -16,12 +16,14 @@
 // first stages are issued before the kernel waits on its predecessor (programmatic
 // dependent launch). After the wait the producer bulk-copies the activation fragments of
 // the block's K-chunk into shared memory once, so the MMA loop reads only shared memory.
-// Eight consumer warps split each slab's k-tiles and issue two MMAs per tile and n-tile
+// Eight MMA warps split each slab's k-tiles and issue two MMAs per tile and n-tile
 // (activation hi and lo bf16 terms, fp32-level accuracy), then release the slot through an
-// mbarrier. When K exceeds the activation buffer, K is split into chunks: the blocks of one
-// row range write fp32 partials and the last of them to arrive (one fence and one atomic
-// per block) adds them in chunk order and runs the epilogue, so results do not depend on
-// arrival order. Epilogues: store, residual add (linear(..., accumulate=true)), SwiGLU
+// mbarrier. At the end of each 16-feature unit they hand their per-warp sums to four
+// epilogue warps through two shared-memory buffers and continue with the next unit, so the
+// cross-warp reduction and the epilogue's global traffic overlap the weight stream. When K
+// exceeds the activation buffer, K is split into chunks: the blocks of one row range write
+// fp32 partials and the last of them to arrive (one fence and one atomic per block) adds them
+// in chunk order and runs the epilogue, so results do not depend on arrival order. Epilogues: store, residual add (linear(..., accumulate=true)), SwiGLU
 // (silu(gate)*up, cpu_ops.cpp:79-84, gate/up row blocks interleaved) and a fused argmax;
 // stored results can also be emitted as fragments for up to two consumers (times their norm
 // gains) and as per-unit sums of squares for their 1/rms. As its own stream ends, each block
@@ -39,18 +41,25 @@ enum Epilogue : int { EPI_STORE = 0, EPI_ADD = 1, EPI_SWIGLU = 2, EPI_ARGMAX = 3
 
 constexpr int GEMV_MAXL = 16;  // rows per launch (2 n-tiles)
 constexpr int GEMV_MAXSEG = 3;
-constexpr int GV_CWARPS = 8;                        // consumer warps
+constexpr int GV_CWARPS = 8;                        // MMA warps
 constexpr int GV_CTHREADS = GV_CWARPS * kWarp;      // 256
-constexpr int GV_THREADS = GV_CTHREADS + kWarp;     // + one producer warp
+constexpr int GV_EWARPS = 4;                        // epilogue warps
+constexpr int GV_ETHREADS = GV_EWARPS * kWarp;      // 128
+constexpr int GV_THREADS = GV_CTHREADS + kWarp + GV_ETHREADS;  // + one producer warp + the epilogue warps
 constexpr int GV_SLAB = 32;                         // k-tiles per ring stage: 512 columns
 constexpr int GV_COLS = GV_SLAB * 16;
 constexpr int GV_STAGE_BYTES = GV_SLAB * 512;       // 16 KB
-constexpr int GV_NSTAGE = 8;
+constexpr int GV_NSTAGE = 8;                        // ring stages at 8 rows (7 at 16 rows)
 constexpr int GV_ACT_BYTES = 64 * 1024;             // activation chunk buffer
 constexpr int GV_TPW = GV_SLAB / GV_CWARPS;         // k-tiles per warp per slab
 constexpr int GV_F32_THREADS = 256;
 constexpr int GV_F32_WARPS = GV_F32_THREADS / kWarp;
 constexpr int GV_SIDE_BLOCKS = 16;                  // blocks that run a head's side job
+
+__host__ __device__ constexpr int gv_nstage(int NT) { return NT == 1 ? GV_NSTAGE : GV_NSTAGE - 1; }
+
+// Host-computed properties of a launch's inputs (GemvParams::flags).
+enum GemvFlags : int { GV_F_TOK = 1, GV_F_SS = 2, GV_F_TABLE = 4 };
 
 // Slabs of K per activation chunk: 4 (2048 columns) for 8 rows, 2 for 16 rows.
 __host__ __device__ constexpr int gv_chunk_slabs(int NT) { return GV_ACT_BYTES / (GV_STAGE_BYTES * NT); }
@@ -97,6 +106,7 @@ struct GemvParams {
   XSeg seg[GEMV_MAXSEG];
   TokenSrc tok;
   int epi;
+  int flags;             // GemvFlags of the segments (set by the launcher)
   float* y;              // fp32 result rows (optional except for argmax logits)
   int ldy;
   const float* base;     // EPI_ADD: y = base + acc (base may equal y)
@@ -285,24 +295,113 @@ __device__ __forceinline__ float gemv_epilogue(const GemvParams& p, int n, int l
   return v * v;
 }
 
+// Tokens (GV_F_TOK) and s_inv[s * 16 + l] = the 1/rms of row l of segment s (0 for l >= L),
+// run by the MMA warps (named barrier 1). Every statistics load of every segment is issued
+// before the first is used, so the prologue costs one global round trip. The partial sums are
+// added in a fixed order: parts g, g + 16, g + 32, ... per row and part group, then the 16
+// groups. s_part holds GEMV_MAXSEG x 256 floats.
+__device__ void gemv_prologue_fast(const GemvParams& p, int L, int* s_tok, float* s_inv, float* s_part) {
+  const int tid = threadIdx.x;
+  if (p.flags & GV_F_TOK) {
+    if (tid < L) {
+      const int t = resolve_token(p.tok, tid, p.err);
+      s_tok[tid] = t;
+      if (p.tok.tok_out && blockIdx.x == 0) p.tok.tok_out[tid] = t;
+    }
+    named_sync(1, GV_CTHREADS);
+  }
+  if (p.flags & GV_F_SS) {
+    const int l = tid & 15, g = tid >> 4;
+    float v[GEMV_MAXSEG][8];
+#pragma unroll
+    for (int s = 0; s < GEMV_MAXSEG; ++s) {
+      const XSeg& sg = p.seg[s];
+      const bool on = s < p.nseg && sg.xf && sg.ss;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int q = g + 16 * i;
+        v[s][i] = (on && q < sg.nparts) ? __ldcg(sg.ss + q * 16 + l) : 0.f;
+      }
+    }
+#pragma unroll
+    for (int s = 0; s < GEMV_MAXSEG; ++s) {
+      const XSeg& sg = p.seg[s];
+      float a = 0.f;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) a += v[s][i];
+      if (s < p.nseg && sg.xf && sg.ss)
+        for (int q = g + 128; q < sg.nparts; q += 16) a += __ldcg(sg.ss + q * 16 + l);
+      s_part[s * 256 + g * 16 + l] = a;
+    }
+    named_sync(1, GV_CTHREADS);
+  }
+  if (tid < GEMV_MAXSEG * 16) {
+    const int s = tid >> 4, l = tid & 15;
+    float inv = 0.f;
+    if (s < p.nseg && l < L) {
+      const XSeg& sg = p.seg[s];
+      if (sg.xf && sg.ss) {
+        float t = 0.f;
+#pragma unroll
+        for (int q = 0; q < 16; ++q) t += s_part[s * 256 + q * 16 + l];
+        inv = 1.f / sqrtf(t / float(sg.len) + sg.eps);
+      } else {
+        inv = (!sg.xf && sg.row_inv) ? sg.row_inv[s_tok[l]] : 1.f;
+      }
+    }
+    s_inv[tid] = inv;
+  }
+  named_sync(1, GV_CTHREADS);
+}
+
+// Shared-memory carve-up of the bf16 kernel (byte offsets, every region 16-byte aligned).
+template <int NT>
+struct GvLayout {
+  static constexpr int NS = gv_nstage(NT);
+  static constexpr size_t ring = 0;                                        // NS x 16 KB weight slabs
+  static constexpr size_t act = ring + size_t(NS) * GV_STAGE_BYTES;        // [NT][CHS][32 kt][32 lanes] uint4
+  static constexpr size_t bars = act + GV_ACT_BYTES;                       // full[NS] empty[NS] act red_full[2] red_empty[2]
+  static constexpr size_t nbars = 2 * NS + 5;
+  static constexpr size_t red = bars + (nbars * 8 + 15) / 16 * 16;         // [2 buffers][2 row blocks][NT][W][32][4] floats
+  static constexpr size_t red_buf = size_t(2) * NT * GV_CWARPS * kWarp * 4;  // floats per buffer
+  static constexpr size_t inv = red + 2 * red_buf * 4;                     // [3][16] floats
+  static constexpr size_t part = inv + GEMV_MAXSEG * 16 * 4;               // [3][256] floats
+  static constexpr size_t sq = part + GEMV_MAXSEG * 256 * 4;               // [2][16 features][16 rows] floats
+  static constexpr size_t tok = sq + 2 * 256 * 4;                          // [16] ints
+  static constexpr size_t flag = tok + 16 * 4;                             // [4] ints
+  static constexpr size_t key = flag + 16;                                 // [16] u64
+  static constexpr size_t params = key + 16 * 8;
+  static constexpr size_t total = params + (sizeof(GemvParams) + 15) / 16 * 16;
+  static_assert(red_buf * 4 >= 8 * 256 * 4 || NT == 2, "split-K staging needs 8 KB of the reduction buffers");
+};
+
+// Warp roles: 0-7 MMA (named barrier 1), 8 the bulk-copy producer, 9-12 epilogue (named
+// barrier 2). The MMA warps hand each unit's per-warp sums to the epilogue warps through two
+// shared-memory buffers (mbarriers red_full / red_empty) and go straight on to the next
+// unit's slabs, so the cross-warp reduction, the epilogue's global traffic and the split-K
+// hand-off overlap the weight stream instead of stalling it.
 template <int NT>
 __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constant__ const GemvParams pk) {
+  using Lay = GvLayout<NT>;
+  constexpr int NS = Lay::NS;
   constexpr int CHS = gv_chunk_slabs(NT);
   extern __shared__ __align__(128) unsigned char gv_smem[];
-  unsigned char* ring = gv_smem;                                              // NSTAGE x 16 KB
-  unsigned char* act = ring + GV_NSTAGE * GV_STAGE_BYTES;                     // [NT][CHS][32 kt][32 lanes] uint4
-  uint64_t* full = reinterpret_cast<uint64_t*>(act + GV_ACT_BYTES);           // [NSTAGE]
-  uint64_t* empty = full + GV_NSTAGE;                                         // [NSTAGE]
-  uint64_t* act_bar = empty + GV_NSTAGE;                                      // [1]
-  float* red = reinterpret_cast<float*>(act_bar + 2);                         // [2][NT][W][32][4]
-  float* s_inv = red + 2 * NT * GV_CWARPS * kWarp * 4;                        // [3][16]
-  float* s_part = s_inv + GEMV_MAXSEG * 16;                                   // [256]
-  float* s_sq = s_part + 256;                                                 // [16 features][16 rows]
-  int* s_tok = reinterpret_cast<int*>(s_sq + 256);                            // [16]
-  int* s_flag = s_tok + 16;                                                   // [4]
-  unsigned long long* s_key = reinterpret_cast<unsigned long long*>(s_flag + 4);  // [16]
+  unsigned char* ring = gv_smem + Lay::ring;
+  unsigned char* act = gv_smem + Lay::act;
+  uint64_t* full = reinterpret_cast<uint64_t*>(gv_smem + Lay::bars);
+  uint64_t* empty = full + NS;
+  uint64_t* act_bar = empty + NS;
+  uint64_t* red_full = act_bar + 1;
+  uint64_t* red_empty = red_full + 2;
+  float* red = reinterpret_cast<float*>(gv_smem + Lay::red);
+  float* s_inv = reinterpret_cast<float*>(gv_smem + Lay::inv);
+  float* s_part = reinterpret_cast<float*>(gv_smem + Lay::part);
+  float* s_sq = reinterpret_cast<float*>(gv_smem + Lay::sq);
+  int* s_tok = reinterpret_cast<int*>(gv_smem + Lay::tok);
+  int* s_flag = reinterpret_cast<int*>(gv_smem + Lay::flag);
+  unsigned long long* s_key = reinterpret_cast<unsigned long long*>(gv_smem + Lay::key);
   const uint4* act4 = reinterpret_cast<const uint4*>(act);
-  GemvParams* s_params = reinterpret_cast<GemvParams*>(s_key + 16);
+  GemvParams* s_params = reinterpret_cast<GemvParams*>(gv_smem + Lay::params);
   params_to_smem(pk, s_params);
   __syncthreads();
   const GemvParams& p = *s_params;
@@ -317,11 +416,15 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
   const int s0 = kc * p.kc_slabs, s1 = min(nslab, s0 + p.kc_slabs), ns = s1 - s0;
   const int total = (u1 - u0) * G * ns;  // ring stages: unit, row block of the unit, slab
   if (tid == 0) {
-    for (int s = 0; s < GV_NSTAGE; ++s) {
+    for (int s = 0; s < NS; ++s) {
       mbar_init(full + s, 1);
       mbar_init(empty + s, GV_CWARPS);
     }
     mbar_init(act_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(red_full + b, GV_CTHREADS);
+      mbar_init(red_empty + b, GV_ETHREADS);
+    }
     mbar_fence_init();
   }
   __syncthreads();
@@ -332,7 +435,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
       const uint64_t pol = l2_evict_first_policy();
       const char* w = static_cast<const char*>(p.w);
       auto issue = [&](int q) {
-        const int st = q % GV_NSTAGE, rbl = q / ns, si = q % ns;
+        const int st = q % NS, rbl = q / ns, si = q % ns;
         const size_t rb = size_t(u0) * G + rbl;
         mbar_arrive_expect_tx(full + st, GV_STAGE_BYTES);
         bulk_g2s_hint(ring + st * GV_STAGE_BYTES, w + (rb * KT + size_t(s0 + si) * GV_SLAB) * 512, GV_STAGE_BYTES,
@@ -340,27 +443,34 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
       };
       int issued = 0;
       // weights do not depend on the previous kernel: fill the ring before waiting on it
-      for (; issued < min(total, GV_NSTAGE); ++issued) issue(issued);
+      for (; issued < min(total, NS); ++issued) issue(issued);
       pdl_wait();
+      // the activation fragments of this K-chunk (embedding segments are built by the MMA warps)
       uint32_t act_bytes = 0;
-      for (int sl = s0; sl < s1; ++sl) {
-        int f0;
-        if (p.seg[gemv_seg_of(p, sl, &f0)].xf) act_bytes += NT * GV_STAGE_BYTES;
+      {
+        int s = 0, f = 0;
+        for (int sl = s0; sl < s1; ++sl) {
+          while (s + 1 < p.nseg && sl >= f + p.seg[s].lenp / GV_COLS) f += p.seg[s++].lenp / GV_COLS;
+          if (p.seg[s].xf) act_bytes += NT * GV_STAGE_BYTES;
+        }
       }
       mbar_arrive_expect_tx(act_bar, act_bytes);
-      for (int sl = s0; sl < s1; ++sl) {
-        int f0;
-        const XSeg& sg = p.seg[gemv_seg_of(p, sl, &f0)];
-        if (!sg.xf) continue;
-        for (int nt = 0; nt < NT; ++nt)
-          bulk_g2s(act + (nt * CHS + (sl - s0)) * GV_STAGE_BYTES,
-                   reinterpret_cast<const char*>(sg.xf) + (size_t(nt) * (sg.lenp >> 4) + size_t(sl - f0) * GV_SLAB) * 512,
-                   GV_STAGE_BYTES, act_bar);
+      {
+        int s = 0, f = 0;
+        for (int sl = s0; sl < s1; ++sl) {
+          while (s + 1 < p.nseg && sl >= f + p.seg[s].lenp / GV_COLS) f += p.seg[s++].lenp / GV_COLS;
+          const XSeg& sg = p.seg[s];
+          if (!sg.xf) continue;
+          for (int nt = 0; nt < NT; ++nt)
+            bulk_g2s(act + (nt * CHS + (sl - s0)) * GV_STAGE_BYTES,
+                     reinterpret_cast<const char*>(sg.xf) + (size_t(nt) * (sg.lenp >> 4) + size_t(sl - f) * GV_SLAB) * 512,
+                     GV_STAGE_BYTES, act_bar);
+        }
       }
       bool ok = true;
       for (; issued < total; ++issued) {
-        const int st = issued % GV_NSTAGE;
-        if (!mbar_wait(empty + st, ((issued / GV_NSTAGE) - 1) & 1, 1u << 26)) {
+        const int st = issued % NS;
+        if (!mbar_wait(empty + st, ((issued / NS) - 1) & 1, 1u << 26)) {
           raise_error(p.err, kErrTimeout);
           ok = false;
           break;
@@ -378,32 +488,135 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
       }
       // the block's shared memory must outlive every copy issued into it, also when the
       // consumers gave up on a wait: wait (bounded) for the last copy of each slot
-      for (int q = max(0, issued - GV_NSTAGE); q < issued; ++q)
-        if (!mbar_wait(full + q % GV_NSTAGE, (q / GV_NSTAGE) & 1)) raise_error(p.err, kErrTimeout);
+      for (int q = max(0, issued - NS); q < issued; ++q)
+        if (!mbar_wait(full + q % NS, (q / NS) & 1)) raise_error(p.err, kErrTimeout);
       if (!mbar_wait(act_bar, 0)) raise_error(p.err, kErrTimeout);
     }
     return;
   }
 
-  // ---- consumers
+  if (warp > GV_CWARPS) {  // ---- epilogue warps
+    const int et = tid - (GV_CWARPS + 1) * kWarp;
+    pdl_wait();
+    const int L = gemv_rows(p.L_dev, p.L, p.L_max, nullptr);
+    if (et < 16) s_key[et] = 0ull;
+    named_sync(2, GV_ETHREADS);
+    bool ok = true;
+    for (int u = u0, j = 0; u < u1; ++u, ++j) {
+      const int b = j & 1;
+      if (ok && !mbar_wait(red_full + b, (j >> 1) & 1)) {
+        raise_error(p.err, kErrTimeout);
+        ok = false;
+      }
+      const float* rb = red + b * Lay::red_buf;
+      float* sq = s_sq + b * 256;
+#pragma unroll
+      for (int k = 0; k < NT; ++k) {
+        const int idx = et + k * GV_ETHREADS;
+        const int e = idx % 4, ln = (idx / 4) % kWarp, nt = idx / (4 * kWarp);
+        const int l = nt * 8 + 2 * (ln % 4) + (e & 1), r16 = ln / 4 + ((e & 2) ? 8 : 0);
+        float v[2] = {0.f, 0.f};
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+          if (r < G)
+#pragma unroll
+            for (int w = 0; w < GV_CWARPS; ++w) v[r] += rb[(((r * NT + nt) * GV_CWARPS + w) * kWarp + ln) * 4 + e];
+        if (p.nkc > 1) {  // this chunk's share, reduced below by the last block of the range
+#pragma unroll
+          for (int r = 0; r < 2; ++r)
+            if (r < G) p.partial[((size_t(kc) * (p.Np >> 4) + size_t(u) * G + r) * 16 + r16) * 16 + l] = v[r];
+        } else {
+          float s2 = 0.f;
+          if (l < L && u * 16 + r16 < p.N) s2 = gemv_epilogue(p, u * 16 + r16, l, v[0], v[1], s_key);
+          sq[r16 * 16 + l] = s2;
+        }
+      }
+      mbar_arrive(red_empty + b);  // this thread's reads of the buffer are done
+      if (p.nkc == 1 && p.ss_out) {  // fixed-order sum over the unit's 16 features
+        named_sync(2, GV_ETHREADS);
+        if (et < 16) {
+          float a = 0.f;
+          if (et < L)
+            for (int f = 0; f < 16; ++f) a += sq[f * 16 + et];
+          p.ss_out[size_t(u) * 16 + et] = a;
+        }
+      }
+    }
+    if (p.nkc > 1) {
+      // ---- split K: the last block of this unit range adds the chunks in order
+      __threadfence();
+      named_sync(2, GV_ETHREADS);
+      if (et == 0) s_flag[0] = atomicAdd(&p.counters[gi], 1) == p.nkc - 1;
+      named_sync(2, GV_ETHREADS);
+      if (s_flag[0]) {
+        __threadfence();
+        // up to 8 units at a time: every partial load of the group in flight together
+        constexpr int FU = 8, PER = FU * 256 / GV_ETHREADS;
+        float* s_sq8 = red;  // [FU][16 features][16 rows]; every unit of this block has been reduced
+        for (int ub = u0; ub < u1; ub += FU) {
+          const int nu = min(FU, u1 - ub), per = 16 * L, items = nu * per;
+          float v0[PER], v1[PER];
+#pragma unroll
+          for (int i = 0; i < PER; ++i) v0[i] = v1[i] = 0.f;
+          for (int c = 0; c < p.nkc; ++c) {
+#pragma unroll
+            for (int i = 0; i < PER; ++i) {
+              const int it = et + i * GV_ETHREADS;
+              if (it < items) {
+                const int uu = it / per, r16 = (it % per) / L, l = it % L;
+                const float* src = &p.partial[((size_t(c) * (p.Np >> 4) + size_t(ub + uu) * G) * 16 + r16) * 16 + l];
+                v0[i] += __ldcg(src);
+                if (G == 2) v1[i] += __ldcg(src + 256);
+              }
+            }
+          }
+#pragma unroll
+          for (int i = 0; i < PER; ++i) {
+            const int it = et + i * GV_ETHREADS;
+            if (it < items) {
+              const int uu = it / per, r16 = (it % per) / L, l = it % L;
+              const int n = (ub + uu) * 16 + r16;
+              s_sq8[(uu * 16 + r16) * 16 + l] = n < p.N ? gemv_epilogue(p, n, l, v0[i], v1[i], s_key) : 0.f;
+            }
+          }
+          named_sync(2, GV_ETHREADS);
+          if (p.ss_out && et < nu * 16) {  // fixed-order sum over each unit's 16 features
+            const int uu = et / 16, l = et % 16;
+            float a = 0.f;
+            if (l < L)
+              for (int f = 0; f < 16; ++f) a += s_sq8[(uu * 16 + f) * 16 + l];
+            p.ss_out[size_t(ub + uu) * 16 + l] = a;
+          }
+          named_sync(2, GV_ETHREADS);
+        }
+        if (et == 0) p.counters[gi] = 0;  // ready for the next launch
+      }
+    }
+    named_sync(2, GV_ETHREADS);
+    if (p.epi == EPI_ARGMAX && et < L && s_key[et] != 0ull) atomicMax(&p.keys[et], s_key[et]);
+    return;
+  }
+
+  // ---- MMA warps
   pdl_wait();
   const int L = gemv_rows(p.L_dev, p.L, p.L_max, p.err);
-  if (tid < 16) s_key[tid] = 0ull;
-  gemv_prologue(p, L, s_tok, s_inv, s_part);
-  // embedding segments of this chunk: built from the table straight into the buffer
-  bool table = false;
-  for (int sl = s0; sl < s1; ++sl) {
-    int f0;
-    const XSeg& sg = p.seg[gemv_seg_of(p, sl, &f0)];
-    if (sg.xf) continue;
-    table = true;
-    for (int idx = tid; idx < NT * GV_SLAB * kWarp; idx += GV_CTHREADS) {
-      const int nt = idx / (GV_SLAB * kWarp), kt = (idx / kWarp) % GV_SLAB, ln = idx % kWarp;
-      reinterpret_cast<uint4*>(act)[((nt * CHS + (sl - s0)) * GV_SLAB + kt) * kWarp + ln] =
-          xseg_table_b(sg, (sl - f0) * GV_SLAB + kt, nt, ln, L, s_tok);
+  gemv_prologue_fast(p, L, s_tok, s_inv, s_part);
+  if (p.flags & GV_F_TABLE) {  // embedding segments of this chunk: built from the table straight into the buffer
+    bool table = false;
+    int s = 0, f = 0;
+    for (int sl = s0; sl < s1; ++sl) {
+      while (s + 1 < p.nseg && sl >= f + p.seg[s].lenp / GV_COLS) f += p.seg[s++].lenp / GV_COLS;
+      const XSeg& sg = p.seg[s];
+      if (sg.xf) continue;
+      table = true;
+      for (int idx = tid; idx < NT * GV_SLAB * kWarp; idx += GV_CTHREADS) {
+        const int nt = idx / (GV_SLAB * kWarp), kt = (idx / kWarp) % GV_SLAB, ln = idx % kWarp;
+        reinterpret_cast<uint4*>(act)[((nt * CHS + (sl - s0)) * GV_SLAB + kt) * kWarp + ln] =
+            xseg_table_b(sg, (sl - f) * GV_SLAB + kt, nt, ln, L, s_tok);
+      }
     }
+    if (table) named_sync(1, GV_CTHREADS);
   }
-  if (table) named_sync(1, GV_CTHREADS);
   bool ok = true;
   if (!mbar_wait(act_bar, 0)) {
     raise_error(p.err, kErrTimeout);
@@ -413,7 +626,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
   const int seg0 = gemv_seg_of(p, s0, &seg_first0);
   const int seg_end0 = seg_first0 + p.seg[seg0].lenp / GV_COLS;
   int q = 0;
-  for (int u = u0; u < u1; ++u) {
+  for (int u = u0, j = 0; u < u1; ++u, ++j) {
     float tot[2][NT][4];
 #pragma unroll
     for (int r = 0; r < 2; ++r)
@@ -436,8 +649,8 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
           for (int e = 0; e < 4; ++e) acc[nt][c][e] = 0.f;
       int seg = seg0, seg_end = seg_end0;
       for (int si = 0; si < ns; ++si, ++q) {
-        const int st = q % GV_NSTAGE;
-        if (ok && !mbar_wait(full + st, (q / GV_NSTAGE) & 1)) {
+        const int st = q % NS;
+        if (ok && !mbar_wait(full + st, (q / NS) & 1)) {
           raise_error(p.err, kErrTimeout);
           ok = false;
         }
@@ -479,103 +692,28 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
         }
       }
     }
-    // ---- cross-warp reduction of the unit
+    // ---- hand the unit's per-warp sums to the epilogue warps
+    const int b = j & 1;
+    if (j >= 2 && ok && !mbar_wait(red_empty + b, ((j >> 1) - 1) & 1)) {
+      raise_error(p.err, kErrTimeout);
+      ok = false;
+    }
+    float* rb = red + b * Lay::red_buf;
 #pragma unroll
     for (int r = 0; r < 2; ++r)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
         if (r < G)
-          *reinterpret_cast<float4*>(&red[(((r * NT + nt) * GV_CWARPS + warp) * kWarp + lane) * 4]) =
+          *reinterpret_cast<float4*>(&rb[(((r * NT + nt) * GV_CWARPS + warp) * kWarp + lane) * 4]) =
               make_float4(tot[r][nt][0], tot[r][nt][1], tot[r][nt][2], tot[r][nt][3]);
-    named_sync(1, GV_CTHREADS);
-    if (tid < NT * kWarp * 4) {
-      const int e = tid % 4, ln = (tid / 4) % kWarp, nt = tid / (4 * kWarp);
-      const int l = nt * 8 + 2 * (ln % 4) + (e & 1), r16 = ln / 4 + ((e & 2) ? 8 : 0);
-      float v[2] = {0.f, 0.f};
-#pragma unroll
-      for (int r = 0; r < 2; ++r)
-        if (r < G)
-#pragma unroll
-          for (int w = 0; w < GV_CWARPS; ++w) v[r] += red[(((r * NT + nt) * GV_CWARPS + w) * kWarp + ln) * 4 + e];
-      if (p.nkc > 1) {  // this chunk's share, reduced below by the last block of the range
-#pragma unroll
-        for (int r = 0; r < 2; ++r)
-          if (r < G) p.partial[((size_t(kc) * (p.Np >> 4) + size_t(u) * G + r) * 16 + r16) * 16 + l] = v[r];
-      } else {
-        float sq = 0.f;
-        if (l < L && u * 16 + r16 < p.N)
-          sq = gemv_epilogue(p, u * 16 + r16, l, v[0], v[1], s_key);
-        s_sq[r16 * 16 + l] = sq;
-      }
-    }
-    named_sync(1, GV_CTHREADS);
-    if (p.nkc == 1 && p.ss_out && tid < 16) {  // fixed-order sum over the unit's 16 features
-      float a = 0.f;
-      if (tid < L)
-        for (int f = 0; f < 16; ++f) a += s_sq[f * 16 + tid];
-      p.ss_out[size_t(u) * 16 + tid] = a;
-    }
+    mbar_arrive(red_full + b);
   }
-  if (p.nkc > 1) {
-    // ---- split K: the last block of this unit range adds the chunks in order
-    __threadfence();
-    named_sync(1, GV_CTHREADS);
-    if (tid == 0) s_flag[0] = atomicAdd(&p.counters[gi], 1) == p.nkc - 1;
-    named_sync(1, GV_CTHREADS);
-    if (s_flag[0]) {
-      __threadfence();
-      // up to 8 units at a time: every partial load of the group in flight together
-      constexpr int FU = 8;
-      float* s_sq8 = red;  // [FU][16 features][16 rows]
-      for (int ub = u0; ub < u1; ub += FU) {
-        const int nu = min(FU, u1 - ub), per = 16 * L, items = nu * per;
-        float v0[FU], v1[FU];
-#pragma unroll
-        for (int i = 0; i < FU; ++i) v0[i] = v1[i] = 0.f;
-        for (int c = 0; c < p.nkc; ++c) {
-#pragma unroll
-          for (int i = 0; i < FU; ++i) {
-            const int it = tid + i * GV_CTHREADS;
-            if (it < items) {
-              const int uu = it / per, r16 = (it % per) / L, l = it % L;
-              const float* src = &p.partial[((size_t(c) * (p.Np >> 4) + size_t(ub + uu) * G) * 16 + r16) * 16 + l];
-              v0[i] += __ldcg(src);
-              if (G == 2) v1[i] += __ldcg(src + 256);
-            }
-          }
-        }
-#pragma unroll
-        for (int i = 0; i < FU; ++i) {
-          const int it = tid + i * GV_CTHREADS;
-          if (it < items) {
-            const int uu = it / per, r16 = (it % per) / L, l = it % L;
-            const int n = (ub + uu) * 16 + r16;
-            s_sq8[(uu * 16 + r16) * 16 + l] = n < p.N ? gemv_epilogue(p, n, l, v0[i], v1[i], s_key) : 0.f;
-          }
-        }
-        named_sync(1, GV_CTHREADS);
-        if (p.ss_out && tid < nu * 16) {  // fixed-order sum over each unit's 16 features
-          const int uu = tid / 16, l = tid % 16;
-          float a = 0.f;
-          if (l < L)
-            for (int f = 0; f < 16; ++f) a += s_sq8[(uu * 16 + f) * 16 + l];
-          p.ss_out[size_t(ub + uu) * 16 + l] = a;
-        }
-        named_sync(1, GV_CTHREADS);
-      }
-      if (tid == 0) p.counters[gi] = 0;  // ready for the next launch
-    }
-  }
-  named_sync(1, GV_CTHREADS);
-  if (p.epi == EPI_ARGMAX && tid < L && s_key[tid] != 0ull) atomicMax(&p.keys[tid], s_key[tid]);
   if (p.side_src && int(blockIdx.x) < p.side_blocks) gemv_side_job(p, L, s_inv, s_part, GV_CTHREADS, true);
 }
 
 template <int NT>
 constexpr size_t gemv_bf16_smem() {
-  return size_t(GV_NSTAGE) * GV_STAGE_BYTES + GV_ACT_BYTES + (2 * GV_NSTAGE + 2) * 8 +
-         size_t(2) * NT * GV_CWARPS * kWarp * 4 * 4 + GEMV_MAXSEG * 16 * 4 + 256 * 4 + 256 * 4 + 16 * 4 + 4 * 4 +
-         16 * 8 + sizeof(GemvParams) + 128;
+  return GvLayout<NT>::total + 128;
 }
 
 // ----------------------------------------------------------------------------- fp32 models

@@ -573,6 +573,11 @@ void launch_gemv(wc_ctx* ctx, const Lin& W, GemvParams p) {
     if (!sg.xf && (!sg.table || !sg.norm_w || (bf16 && sg.len % 16)))
       fail(WC_ERR_INVALID, "embedding segments need a table, a gain and a width that is a multiple of 16");
   }
+  p.flags = 0;
+  for (int s = 0; s < p.nseg; ++s) {
+    if (!p.seg[s].xf) p.flags |= GV_F_TOK | GV_F_TABLE;
+    if (p.seg[s].xf && p.seg[s].ss) p.flags |= GV_F_SS;
+  }
   if (p.L_max < 1 || p.L_max > GEMV_MAXL) fail(WC_ERR_INVALID, "GEMV rows outside 1..16");
   if (p.nout > 2 || (p.nout > 0 && p.epi == EPI_ARGMAX)) fail(WC_ERR_INVALID, "bad GEMV outputs");
   p.out_width = xf_width(bf16, W.N);
