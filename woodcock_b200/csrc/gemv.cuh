@@ -279,8 +279,24 @@ __device__ __forceinline__ float gemv_pick_value(const GemvParams& p, int l, int
          philox_gumbel_f(p.rng[0], p.rng[1] + uint64_t(p.rng_stream + l) * kRngStreamLen + uint64_t(n));
 }
 
-__device__ __forceinline__ float gemv_epilogue(const GemvParams& p, int n, int l, float v0, float v1,
-                                               unsigned long long* s_key) {
+// The global inputs of one element's epilogue: the residual (which may be the output buffer
+// itself) and the consumers' norm gains. Callers load them for all of a thread's elements
+// before storing any result, so the loads are one round trip instead of one per element.
+struct EpiIn {
+  float base;
+  float w[2];
+};
+
+__device__ __forceinline__ EpiIn gemv_epi_load(const GemvParams& p, int n, int l) {
+  EpiIn e;
+  e.base = p.epi == EPI_ADD ? p.base[size_t(l) * p.ldb + n] : 0.f;
+  e.w[0] = (p.nout > 0 && p.out[0].w) ? __ldg(p.out[0].w + n) : 1.f;
+  e.w[1] = (p.nout > 1 && p.out[1].w) ? __ldg(p.out[1].w + n) : 1.f;
+  return e;
+}
+
+__device__ __forceinline__ float gemv_epilogue_in(const GemvParams& p, int n, int l, float v0, float v1,
+                                                  EpiIn e, unsigned long long* s_key) {
   float v = v0;
   if (p.epi == EPI_ARGMAX) {
     if (p.y) p.y[size_t(l) * p.ldy + n] = v;
@@ -288,11 +304,18 @@ __device__ __forceinline__ float gemv_epilogue(const GemvParams& p, int n, int l
     return 0.f;
   }
   if (p.epi == EPI_SWIGLU) v = v0 / (1.f + expf(-v0)) * v1;
-  if (p.epi == EPI_ADD) v += p.base[size_t(l) * p.ldb + n];
+  if (p.epi == EPI_ADD) v += e.base;
   if (p.y) p.y[size_t(l) * p.ldy + n] = v;
   if (p.y2) p.y2[size_t(l) * p.ldy2 + n] = v;
-  for (int o = 0; o < p.nout; ++o) xf_store(p.out[o].xf, p.out_width, l, n, p.out[o].w ? v * p.out[o].w[n] : v);
+#pragma unroll
+  for (int o = 0; o < 2; ++o)
+    if (o < p.nout) xf_store(p.out[o].xf, p.out_width, l, n, p.out[o].w ? v * e.w[o] : v);
   return v * v;
+}
+
+__device__ __forceinline__ float gemv_epilogue(const GemvParams& p, int n, int l, float v0, float v1,
+                                               unsigned long long* s_key) {
+  return gemv_epilogue_in(p, n, l, v0, v1, gemv_epi_load(p, n, l), s_key);
 }
 
 // Tokens (GV_F_TOK) and s_inv[s * 16 + l] = the 1/rms of row l of segment s (0 for l >= L),
@@ -300,7 +323,26 @@ __device__ __forceinline__ float gemv_epilogue(const GemvParams& p, int n, int l
 // before the first is used, so the prologue costs one global round trip. The partial sums are
 // added in a fixed order: parts g, g + 16, g + 32, ... per row and part group, then the 16
 // groups. s_part holds GEMV_MAXSEG x 256 floats.
-__device__ void gemv_prologue_fast(const GemvParams& p, int L, int* s_tok, float* s_inv, float* s_part) {
+// Byte offsets (or -1) at which the producer stages each normalised segment's statistics in
+// a shared buffer of `cap` bytes: in segment order, while they fit and are 16-byte aligned.
+// Producer and MMA warps evaluate the same rule.
+__device__ __forceinline__ void gemv_ss_plan(const GemvParams& p, size_t cap, int (&stg)[GEMV_MAXSEG]) {
+  size_t off = 0;
+#pragma unroll
+  for (int s = 0; s < GEMV_MAXSEG; ++s) {
+    stg[s] = -1;
+    if (s < p.nseg && p.seg[s].xf && p.seg[s].ss) {
+      const size_t bytes = size_t(p.seg[s].nparts) * 64;
+      if ((reinterpret_cast<uintptr_t>(p.seg[s].ss) & 15) == 0 && off + bytes <= cap) {
+        stg[s] = int(off);
+        off += bytes;
+      }
+    }
+  }
+}
+
+__device__ void gemv_prologue_fast(const GemvParams& p, int L, int* s_tok, float* s_inv, float* s_part,
+                                   const unsigned char* stage, const int (&stg)[GEMV_MAXSEG], uint64_t* ss_bar) {
   const int tid = threadIdx.x;
   if (p.flags & GV_F_TOK) {
     if (tid < L) {
@@ -313,24 +355,32 @@ __device__ void gemv_prologue_fast(const GemvParams& p, int L, int* s_tok, float
   if (p.flags & GV_F_SS) {
     const int l = tid & 15, g = tid >> 4;
     float v[GEMV_MAXSEG][8];
+    bool staged = false;
 #pragma unroll
-    for (int s = 0; s < GEMV_MAXSEG; ++s) {
+    for (int s = 0; s < GEMV_MAXSEG; ++s) {  // global statistics first: their loads are in flight below
       const XSeg& sg = p.seg[s];
-      const bool on = s < p.nseg && sg.xf && sg.ss;
+      const bool on = s < p.nseg && sg.xf && sg.ss && stg[s] < 0;
+      staged |= stg[s] >= 0;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int q = g + 16 * i;
         v[s][i] = (on && q < sg.nparts) ? __ldcg(sg.ss + q * 16 + l) : 0.f;
       }
     }
+    if (staged && !mbar_wait(ss_bar, 0)) raise_error(p.err, kErrTimeout);
 #pragma unroll
     for (int s = 0; s < GEMV_MAXSEG; ++s) {
       const XSeg& sg = p.seg[s];
       float a = 0.f;
+      if (stg[s] >= 0) {
+        const float* st = reinterpret_cast<const float*>(stage + stg[s]);
+        for (int q = g; q < sg.nparts; q += 16) a += st[q * 16 + l];
+      } else {
 #pragma unroll
-      for (int i = 0; i < 8; ++i) a += v[s][i];
-      if (s < p.nseg && sg.xf && sg.ss)
-        for (int q = g + 128; q < sg.nparts; q += 16) a += __ldcg(sg.ss + q * 16 + l);
+        for (int i = 0; i < 8; ++i) a += v[s][i];
+        if (s < p.nseg && sg.xf && sg.ss)
+          for (int q = g + 128; q < sg.nparts; q += 16) a += __ldcg(sg.ss + q * 16 + l);
+      }
       s_part[s * 256 + g * 16 + l] = a;
     }
     named_sync(1, GV_CTHREADS);
@@ -360,8 +410,8 @@ struct GvLayout {
   static constexpr int NS = gv_nstage(NT);
   static constexpr size_t ring = 0;                                        // NS x 16 KB weight slabs
   static constexpr size_t act = ring + size_t(NS) * GV_STAGE_BYTES;        // [NT][CHS][32 kt][32 lanes] uint4
-  static constexpr size_t bars = act + GV_ACT_BYTES;                       // full[NS] empty[NS] act red_full[2] red_empty[2]
-  static constexpr size_t nbars = 2 * NS + 5;
+  static constexpr size_t bars = act + GV_ACT_BYTES;                       // full[NS] empty[NS] act red_full[2] red_empty[2] ss
+  static constexpr size_t nbars = 2 * NS + 6;
   static constexpr size_t red = bars + (nbars * 8 + 15) / 16 * 16;         // [2 buffers][2 row blocks][NT][W][32][4] floats
   static constexpr size_t red_buf = size_t(2) * NT * GV_CWARPS * kWarp * 4;  // floats per buffer
   static constexpr size_t inv = red + 2 * red_buf * 4;                     // [3][16] floats
@@ -393,6 +443,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
   uint64_t* act_bar = empty + NS;
   uint64_t* red_full = act_bar + 1;
   uint64_t* red_empty = red_full + 2;
+  uint64_t* ss_bar = red_empty + 2;
   float* red = reinterpret_cast<float*>(gv_smem + Lay::red);
   float* s_inv = reinterpret_cast<float*>(gv_smem + Lay::inv);
   float* s_part = reinterpret_cast<float*>(gv_smem + Lay::part);
@@ -421,6 +472,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
       mbar_init(empty + s, GV_CWARPS);
     }
     mbar_init(act_bar, 1);
+    mbar_init(ss_bar, 1);
     for (int b = 0; b < 2; ++b) {
       mbar_init(red_full + b, GV_CTHREADS);
       mbar_init(red_empty + b, GV_ETHREADS);
@@ -445,6 +497,21 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
       // weights do not depend on the previous kernel: fill the ring before waiting on it
       for (; issued < min(total, NS); ++issued) issue(issued);
       pdl_wait();
+      // statistics of the normalised segments, into the reduction buffers (unused until the
+      // first unit is handed over), ahead of the larger activation copy
+      int stg[GEMV_MAXSEG];
+      gemv_ss_plan(p, 2 * Lay::red_buf * 4, stg);
+      uint32_t ss_bytes = 0;
+#pragma unroll
+      for (int s = 0; s < GEMV_MAXSEG; ++s)
+        if (stg[s] >= 0) ss_bytes += uint32_t(p.seg[s].nparts) * 64;
+      if (ss_bytes) {
+        mbar_arrive_expect_tx(ss_bar, ss_bytes);
+#pragma unroll
+        for (int s = 0; s < GEMV_MAXSEG; ++s)
+          if (stg[s] >= 0)
+            bulk_g2s(reinterpret_cast<unsigned char*>(red) + stg[s], p.seg[s].ss, uint32_t(p.seg[s].nparts) * 64, ss_bar);
+      }
       // the activation fragments of this K-chunk (embedding segments are built by the MMA warps)
       uint32_t act_bytes = 0;
       {
@@ -491,6 +558,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
       for (int q = max(0, issued - NS); q < issued; ++q)
         if (!mbar_wait(full + q % NS, (q / NS) & 1)) raise_error(p.err, kErrTimeout);
       if (!mbar_wait(act_bar, 0)) raise_error(p.err, kErrTimeout);
+      if (ss_bytes && !mbar_wait(ss_bar, 0)) raise_error(p.err, kErrTimeout);
     }
     return;
   }
@@ -504,34 +572,51 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
     bool ok = true;
     for (int u = u0, j = 0; u < u1; ++u, ++j) {
       const int b = j & 1;
+      // this thread's elements of the unit; their epilogue inputs load while the MMAs run
+      int ln_[NT], e_[NT], nt_[NT], l_[NT], r16_[NT];
+      bool live[NT];
+      EpiIn ein[NT];
+#pragma unroll
+      for (int k = 0; k < NT; ++k) {
+        const int idx = et + k * GV_ETHREADS;
+        e_[k] = idx % 4;
+        ln_[k] = (idx / 4) % kWarp;
+        nt_[k] = idx / (4 * kWarp);
+        l_[k] = nt_[k] * 8 + 2 * (ln_[k] % 4) + (e_[k] & 1);
+        r16_[k] = ln_[k] / 4 + ((e_[k] & 2) ? 8 : 0);
+        live[k] = p.nkc == 1 && l_[k] < L && u * 16 + r16_[k] < p.N;
+        if (live[k]) ein[k] = gemv_epi_load(p, u * 16 + r16_[k], l_[k]);
+      }
       if (ok && !mbar_wait(red_full + b, (j >> 1) & 1)) {
         raise_error(p.err, kErrTimeout);
         ok = false;
       }
       const float* rb = red + b * Lay::red_buf;
       float* sq = s_sq + b * 256;
+      float v[NT][2];
 #pragma unroll
       for (int k = 0; k < NT; ++k) {
-        const int idx = et + k * GV_ETHREADS;
-        const int e = idx % 4, ln = (idx / 4) % kWarp, nt = idx / (4 * kWarp);
-        const int l = nt * 8 + 2 * (ln % 4) + (e & 1), r16 = ln / 4 + ((e & 2) ? 8 : 0);
-        float v[2] = {0.f, 0.f};
+        v[k][0] = v[k][1] = 0.f;
 #pragma unroll
         for (int r = 0; r < 2; ++r)
           if (r < G)
 #pragma unroll
-            for (int w = 0; w < GV_CWARPS; ++w) v[r] += rb[(((r * NT + nt) * GV_CWARPS + w) * kWarp + ln) * 4 + e];
+            for (int w = 0; w < GV_CWARPS; ++w)
+              v[k][r] += rb[(((r * NT + nt_[k]) * GV_CWARPS + w) * kWarp + ln_[k]) * 4 + e_[k]];
+      }
+      mbar_arrive(red_empty + b);  // this thread's reads of the buffer are done
+#pragma unroll
+      for (int k = 0; k < NT; ++k) {
         if (p.nkc > 1) {  // this chunk's share, reduced below by the last block of the range
 #pragma unroll
           for (int r = 0; r < 2; ++r)
-            if (r < G) p.partial[((size_t(kc) * (p.Np >> 4) + size_t(u) * G + r) * 16 + r16) * 16 + l] = v[r];
+            if (r < G)
+              p.partial[((size_t(kc) * (p.Np >> 4) + size_t(u) * G + r) * 16 + r16_[k]) * 16 + l_[k]] = v[k][r];
         } else {
-          float s2 = 0.f;
-          if (l < L && u * 16 + r16 < p.N) s2 = gemv_epilogue(p, u * 16 + r16, l, v[0], v[1], s_key);
-          sq[r16 * 16 + l] = s2;
+          sq[r16_[k] * 16 + l_[k]] =
+              live[k] ? gemv_epilogue_in(p, u * 16 + r16_[k], l_[k], v[k][0], v[k][1], ein[k], s_key) : 0.f;
         }
       }
-      mbar_arrive(red_empty + b);  // this thread's reads of the buffer are done
       if (p.nkc == 1 && p.ss_out) {  // fixed-order sum over the unit's 16 features
         named_sync(2, GV_ETHREADS);
         if (et < 16) {
@@ -550,14 +635,23 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
       named_sync(2, GV_ETHREADS);
       if (s_flag[0]) {
         __threadfence();
-        // up to 8 units at a time: every partial load of the group in flight together
-        constexpr int FU = 8, PER = FU * 256 / GV_ETHREADS;
+        // up to 4 units at a time: every partial load of the group in flight together
+        constexpr int FU = 4, PER = FU * 256 / GV_ETHREADS;
         float* s_sq8 = red;  // [FU][16 features][16 rows]; every unit of this block has been reduced
         for (int ub = u0; ub < u1; ub += FU) {
           const int nu = min(FU, u1 - ub), per = 16 * L, items = nu * per;
           float v0[PER], v1[PER];
+          EpiIn ein[PER];
 #pragma unroll
-          for (int i = 0; i < PER; ++i) v0[i] = v1[i] = 0.f;
+          for (int i = 0; i < PER; ++i) {  // every global input of the group before any store
+            v0[i] = v1[i] = 0.f;
+            const int it = et + i * GV_ETHREADS;
+            if (it < items) {
+              const int uu = it / per, r16 = (it % per) / L, l = it % L;
+              const int n = (ub + uu) * 16 + r16;
+              if (n < p.N) ein[i] = gemv_epi_load(p, n, l);
+            }
+          }
           for (int c = 0; c < p.nkc; ++c) {
 #pragma unroll
             for (int i = 0; i < PER; ++i) {
@@ -576,7 +670,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
             if (it < items) {
               const int uu = it / per, r16 = (it % per) / L, l = it % L;
               const int n = (ub + uu) * 16 + r16;
-              s_sq8[(uu * 16 + r16) * 16 + l] = n < p.N ? gemv_epilogue(p, n, l, v0[i], v1[i], s_key) : 0.f;
+              s_sq8[(uu * 16 + r16) * 16 + l] = n < p.N ? gemv_epilogue_in(p, n, l, v0[i], v1[i], ein[i], s_key) : 0.f;
             }
           }
           named_sync(2, GV_ETHREADS);
@@ -600,7 +694,11 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
   // ---- MMA warps
   pdl_wait();
   const int L = gemv_rows(p.L_dev, p.L, p.L_max, p.err);
-  gemv_prologue_fast(p, L, s_tok, s_inv, s_part);
+  {
+    int stg[GEMV_MAXSEG];
+    gemv_ss_plan(p, 2 * Lay::red_buf * 4, stg);
+    gemv_prologue_fast(p, L, s_tok, s_inv, s_part, reinterpret_cast<const unsigned char*>(red), stg, ss_bar);
+  }
   if (p.flags & GV_F_TABLE) {  // embedding segments of this chunk: built from the table straight into the buffer
     bool table = false;
     int s = 0, f = 0;
