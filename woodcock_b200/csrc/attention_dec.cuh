@@ -256,61 +256,80 @@ __global__ void __launch_bounds__(AD_THREADS, 1) attention_dec_kernel(__grid_con
   }
   __syncthreads();
 
-  // ---- per-head RMSNorm + RoPE: q -> bf16 hi / lo tiles; new k / v -> bf16, tail tile + cache
+  // ---- per-head RMSNorm + RoPE, eight lanes per row (lane j of the eight holds elements
+  // [j * EPQ, (j + 1) * EPQ); the rotate-half partner of element d < D/2 sits in lane j ^ 4):
+  // q -> bf16 hi / lo tiles; new k / v -> bf16, tail tile + cache. Every row of a block is in
+  // flight in one pass; only the blocks that store k / v (the tail owner, rank 0 for the
+  // cache) process those rows.
   const bool cache_ok = n + L <= p.cap;
   if (!cache_ok && tid == 0) raise_error(p.err, kErrCapacity);
-  constexpr int EPL = D / kWarp;
-  const int nraw = R + 2 * L;
-  for (int it = warp; it < nraw; it += AD_WARPS) {
+  constexpr int EPQ = D / 8;
+  const bool need_kv = owns_tail || (rank == 0 && p.write_cache && cache_ok);
+  const int nrows = R + (need_kv ? 2 * L : 0);
+  const int sub = lane & 7;
+  for (int base = 0; base < nrows; base += AD_THREADS / 8) {  // uniform across the block
+    const int it = base + warp * 4 + (lane >> 3);
+    const bool valid = it < nrows;
     const bool is_q = it < R;
     const int j = it - R;
     const bool is_k = !is_q && j < L;
-    const int l = is_q ? it / rep : j % L;
-    const int rrow = is_q ? (l * rep + it % rep) : Lm * rep + (is_k ? 0 : Lm) + l;  // row in raw
-    float v[EPL];
+    const int l = valid ? (is_q ? it / rep : j % L) : 0;
+    const int rrow = is_q ? (l * rep + it % rep) : Lm * rep + (is_k ? 0 : Lm) + l;
+    float v[EPQ];
 #pragma unroll
-    for (int e = 0; e < EPL; ++e) v[e] = raw[rrow * D + lane * EPL + e];
-    if ((is_q && p.q_norm) || (is_k && p.k_norm)) {
+    for (int e = 0; e < EPQ; e += 4) {
+      const float4 x4 = valid ? *reinterpret_cast<const float4*>(&raw[rrow * D + sub * EPQ + e])
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[e] = x4.x;
+      v[e + 1] = x4.y;
+      v[e + 2] = x4.z;
+      v[e + 3] = x4.w;
+    }
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < EPQ; ++e) ss = fmaf(v[e], v[e], ss);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 1);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+    ss += __shfl_xor_sync(0xffffffffu, ss, 4);
+    if (valid && ((is_q && p.q_norm) || (is_k && p.k_norm))) {
       const float* w = is_q ? wq : wk;
-      float ss = 0.f;
-#pragma unroll
-      for (int e = 0; e < EPL; ++e) ss = fmaf(v[e], v[e], ss);
-      ss = warp_sum(ss);
       const float inv = 1.f / sqrtf(ss / float(D) + p.eps);
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) v[e] = v[e] * inv * w[lane * EPL + e];
+      for (int e = 0; e < EPQ; ++e) v[e] = v[e] * inv * w[sub * EPQ + e];
     }
-    if (is_q || is_k) {  // rotate-half: dims d and d + D/2 sit in lanes lane and lane ^ 16
+    const bool rot = valid && (is_q || is_k);
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) {
-        const float partner = __shfl_xor_sync(0xffffffffu, v[e], 16);
-        const int d = lane * EPL + e;
+    for (int e = 0; e < EPQ; ++e) {  // rotate-half
+      const float partner = __shfl_xor_sync(0xffffffffu, v[e], 4);
+      const int d = sub * EPQ + e;
+      if (rot) {
         const float2 cs = rp[l * (D / 2) + d % (D / 2)];
         v[e] = (d < D / 2) ? (v[e] * cs.x - partner * cs.y) : (v[e] * cs.x + partner * cs.y);
       }
     }
+    if (!valid) continue;
     if (is_q) {
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) {
+      for (int e = 0; e < EPQ; ++e) {
         uint16_t h, lo;
         split_bf16(v[e], h, lo);
-        qh[it * LD + lane * EPL + e] = h;
-        ql[it * LD + lane * EPL + e] = lo;
+        qh[it * LD + sub * EPQ + e] = h;
+        ql[it * LD + sub * EPQ + e] = lo;
       }
     } else {
-      uint16_t bv[EPL];
+      uint16_t bv[EPQ];
 #pragma unroll
-      for (int e = 0; e < EPL; ++e) bv[e] = f32_to_bf16_bits(v[e]);
+      for (int e = 0; e < EPQ; ++e) bv[e] = f32_to_bf16_bits(v[e]);
       if (owns_tail) {
         const int ti = n + l - npre;
         uint16_t* dst = tail + (ti / AD_BLK) * 2 * AD_BLK * LD + (is_k ? 0 : AD_BLK * LD) + (ti % AD_BLK) * LD;
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) dst[lane * EPL + e] = bv[e];
+        for (int e = 0; e < EPQ; ++e) dst[sub * EPQ + e] = bv[e];
       }
       if (rank == 0 && p.write_cache && cache_ok) {
         uint16_t* dst = static_cast<uint16_t*>(is_k ? p.Kc : p.Vc) + hk * p.stride_h + (long long)(n + l) * p.stride_p;
 #pragma unroll
-        for (int e = 0; e < EPL; ++e) dst[lane * EPL + e] = bv[e];
+        for (int e = 0; e < EPQ; ++e) dst[sub * EPQ + e] = bv[e];
       }
     }
   }
@@ -429,6 +448,7 @@ __global__ void __launch_bounds__(AD_THREADS, 1) attention_dec_kernel(__grid_con
       }
     }
   };
+  bool worked = false;  // this warp ran at least one tile (idle warps skip the merge traffic)
   const int nbatch = (ntiles + AD_WARPS * AD_TPW - 1) / (AD_WARPS * AD_TPW);
   for (int b = 0; b < nbatch; ++b) {
     if (b > 0) {  // longer prefixes: refill this warp's buffers (one more round trip per batch)
@@ -443,6 +463,7 @@ __global__ void __launch_bounds__(AD_THREADS, 1) attention_dec_kernel(__grid_con
       if (tl_idx >= ntiles) continue;
       const uint16_t* kb = reinterpret_cast<const uint16_t*>(reg_a + (size_t(warp) * AD_TPW + i) * Lay::tile_bytes);
       tile(kb, kb + AD_BLK * LD, q0 + tl_idx * AD_BLK, q1);
+      worked = true;
     }
   }
   if (owns_tail) {
@@ -451,6 +472,7 @@ __global__ void __launch_bounds__(AD_THREADS, 1) attention_dec_kernel(__grid_con
     if (j < ntail) {
       const uint16_t* kb = tail + j * 2 * AD_BLK * LD;
       tile(kb, kb + AD_BLK * LD, npre + j * AD_BLK, n + L);
+      worked = true;
     }
   }
   __syncthreads();  // every warp is done with its tiles: region A now holds warp outputs
@@ -462,10 +484,12 @@ __global__ void __launch_bounds__(AD_THREADS, 1) attention_dec_kernel(__grid_con
     for (int h = 0; h < 2; ++h) {
       const int r = mt * 16 + g + 8 * h;
       if (r < R) {
+        if (worked) {
 #pragma unroll
-        for (int dt = 0; dt < NDT; ++dt) {
-          *reinterpret_cast<float2*>(&ow[(warp * AD_MAXR + r) * D + dt * 8 + 2 * t]) =
-              make_float2(o[mt][dt][2 * h], o[mt][dt][2 * h + 1]);
+          for (int dt = 0; dt < NDT; ++dt) {
+            *reinterpret_cast<float2*>(&ow[(warp * AD_MAXR + r) * D + dt * 8 + 2 * t]) =
+                make_float2(o[mt][dt][2 * h], o[mt][dt][2 * h + 1]);
+          }
         }
         if (t == 0) {
           mw[warp * AD_MAXR + r] = mrow[mt][h];
@@ -501,7 +525,10 @@ __global__ void __launch_bounds__(AD_THREADS, 1) attention_dec_kernel(__grid_con
     const int r = idx / D, d = idx % D;
     float acc = 0.f;
 #pragma unroll
-    for (int w = 0; w < AD_WARPS; ++w) acc = fmaf(mw[w * AD_MAXR + r], ow[(w * AD_MAXR + r) * D + d], acc);
+    for (int w = 0; w < AD_WARPS; ++w) {
+      const float wt = mw[w * AD_MAXR + r];
+      if (wt != 0.f) acc = fmaf(wt, ow[(w * AD_MAXR + r) * D + d], acc);  // idle warps have weight 0
+    }
     pacc[r * D + d] = acc;
   }
   cluster.sync();
