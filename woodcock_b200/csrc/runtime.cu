@@ -109,7 +109,9 @@ struct wc_ctx {
   bool pdl = true;           // programmatic dependent launch between round kernels
   int attn_mode = 2;         // bf16 caches: 2 decode kernel, 1 split-KV mma kernel, 0 CUDA cores
   int gemv_blocks_per_sm = 1;
-  bool gemv_prefetch = true;             // L2 prefetch of the next GEMV's weights
+  bool gemv_prefetch = false;            // L2 prefetch of the next GEMV's weights (WC_GEMV_PREFETCH=1;
+                                         // measured 1.6% slower on the C3 round: it competes with the
+                                         // dependent loads of the kernels in between)
   size_t gemv_prefetch_cap = 64u << 20;  // bytes prefetched at most
   float* gv_partial = nullptr;           // split-K partial sums
   size_t gv_partial_n = 0;               // floats
@@ -716,6 +718,7 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
     if (const char* e = std::getenv("WC_GEMV_BLOCKS_PER_SM")) ctx->gemv_blocks_per_sm = std::max(1, std::atoi(e));
     if (const char* e = std::getenv("WC_ATTN")) ctx->attn_mode = std::atoi(e);
     if (const char* e = std::getenv("WC_GEMV_PREFETCH")) ctx->gemv_prefetch = std::atoi(e) != 0;
+    if (const char* e = std::getenv("WC_GEMV_PREFETCH_MB")) ctx->gemv_prefetch_cap = size_t(std::max(0, std::atoi(e))) << 20;
     ctx->d_err = static_cast<int*>(dalloc(sizeof(int)));
     CUDA_TRY(cudaMemset(ctx->d_err, 0, sizeof(int)));
     ctx->gv_partial_n = size_t(8) << 20;  // 32 MB of split-K partials
