@@ -55,6 +55,7 @@ constexpr int GV_TPW = GV_SLAB / GV_CWARPS;         // k-tiles per warp per slab
 constexpr int GV_F32_THREADS = 256;
 constexpr int GV_F32_WARPS = GV_F32_THREADS / kWarp;
 constexpr int GV_SIDE_BLOCKS = 16;                  // blocks that run a head's side job
+constexpr int GV_ACS_DEPTH = GV_ACT_BYTES / GV_STAGE_BYTES;  // streamed activation pieces in flight (4)
 
 __host__ __device__ constexpr int gv_nstage(int NT) { return NT == 1 ? GV_NSTAGE : GV_NSTAGE - 1; }
 
@@ -107,6 +108,10 @@ struct GemvParams {
   TokenSrc tok;
   int epi;
   int flags;             // GemvFlags of the segments (set by the launcher)
+  // acs = 1 (8 rows, group 1, one unit per block, no embedding segment): the whole K in one
+  // block, the activation streamed beside the weights in 16 KB pieces through a 4-deep ring
+  // in the activation buffer instead of split K
+  int acs;
   float* y;              // fp32 result rows (optional except for argmax logits)
   int ldy;
   const float* base;     // EPI_ADD: y = base + acc (base may equal y)
@@ -410,8 +415,8 @@ struct GvLayout {
   static constexpr int NS = gv_nstage(NT);
   static constexpr size_t ring = 0;                                        // NS x 16 KB weight slabs
   static constexpr size_t act = ring + size_t(NS) * GV_STAGE_BYTES;        // [NT][CHS][32 kt][32 lanes] uint4
-  static constexpr size_t bars = act + GV_ACT_BYTES;                       // full[NS] empty[NS] act red_full[2] red_empty[2] ss
-  static constexpr size_t nbars = 2 * NS + 6;
+  static constexpr size_t bars = act + GV_ACT_BYTES;  // full[NS] empty[NS] act red_full[2] red_empty[2] ss act_full[4] act_empty[4]
+  static constexpr size_t nbars = 2 * NS + 6 + 2 * GV_ACS_DEPTH;
   static constexpr size_t red = bars + (nbars * 8 + 15) / 16 * 16;         // [2 buffers][2 row blocks][NT][W][32][4] floats
   static constexpr size_t red_buf = size_t(2) * NT * GV_CWARPS * kWarp * 4;  // floats per buffer
   static constexpr size_t inv = red + 2 * red_buf * 4;                     // [3][16] floats
@@ -444,6 +449,8 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
   uint64_t* red_full = act_bar + 1;
   uint64_t* red_empty = red_full + 2;
   uint64_t* ss_bar = red_empty + 2;
+  uint64_t* act_full = ss_bar + 1;                 // [GV_ACS_DEPTH] (acs)
+  uint64_t* act_empty = act_full + GV_ACS_DEPTH;   // [GV_ACS_DEPTH]
   float* red = reinterpret_cast<float*>(gv_smem + Lay::red);
   float* s_inv = reinterpret_cast<float*>(gv_smem + Lay::inv);
   float* s_part = reinterpret_cast<float*>(gv_smem + Lay::part);
@@ -473,6 +480,10 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
     }
     mbar_init(act_bar, 1);
     mbar_init(ss_bar, 1);
+    for (int b = 0; b < GV_ACS_DEPTH; ++b) {
+      mbar_init(act_full + b, 1);
+      mbar_init(act_empty + b, GV_CWARPS);
+    }
     for (int b = 0; b < 2; ++b) {
       mbar_init(red_full + b, GV_CTHREADS);
       mbar_init(red_empty + b, GV_ETHREADS);
@@ -513,36 +524,76 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
             bulk_g2s(reinterpret_cast<unsigned char*>(red) + stg[s], p.seg[s].ss, uint32_t(p.seg[s].nparts) * 64, ss_bar);
       }
       // the activation fragments of this K-chunk (embedding segments are built by the MMA warps)
-      uint32_t act_bytes = 0;
-      {
-        int s = 0, f = 0;
-        for (int sl = s0; sl < s1; ++sl) {
-          while (s + 1 < p.nseg && sl >= f + p.seg[s].lenp / GV_COLS) f += p.seg[s++].lenp / GV_COLS;
-          if (p.seg[s].xf) act_bytes += NT * GV_STAGE_BYTES;
-        }
-      }
-      mbar_arrive_expect_tx(act_bar, act_bytes);
-      {
-        int s = 0, f = 0;
-        for (int sl = s0; sl < s1; ++sl) {
-          while (s + 1 < p.nseg && sl >= f + p.seg[s].lenp / GV_COLS) f += p.seg[s++].lenp / GV_COLS;
-          const XSeg& sg = p.seg[s];
-          if (!sg.xf) continue;
-          for (int nt = 0; nt < NT; ++nt)
-            bulk_g2s(act + (nt * CHS + (sl - s0)) * GV_STAGE_BYTES,
-                     reinterpret_cast<const char*>(sg.xf) + (size_t(nt) * (sg.lenp >> 4) + size_t(sl - f) * GV_SLAB) * 512,
-                     GV_STAGE_BYTES, act_bar);
-        }
-      }
       bool ok = true;
-      for (; issued < total; ++issued) {
-        const int st = issued % NS;
-        if (!mbar_wait(empty + st, ((issued / NS) - 1) & 1, 1u << 26)) {
-          raise_error(p.err, kErrTimeout);
-          ok = false;
-          break;
+      int as = 0, af = 0;  // acs: segment of the next activation piece and its first slab
+      auto issue_act = [&](int j) {  // acs: activation piece j (slab s0 + j) into ring slot j % depth
+        const int sl = s0 + j;
+        while (as + 1 < p.nseg && sl >= af + p.seg[as].lenp / GV_COLS) af += p.seg[as++].lenp / GV_COLS;
+        const XSeg& sg = p.seg[as];
+        uint64_t* bar = act_full + j % GV_ACS_DEPTH;
+        mbar_arrive_expect_tx(bar, GV_STAGE_BYTES);
+        bulk_g2s(act + (j % GV_ACS_DEPTH) * GV_STAGE_BYTES,
+                 reinterpret_cast<const char*>(sg.xf) + size_t(sl - af) * GV_SLAB * 512, GV_STAGE_BYTES, bar);
+      };
+      if (p.acs) {
+        // pieces j and weight slabs j are consumed together; slot j % depth frees after step
+        // j - depth and weight slot j % NS after step j - NS: issue in the order they free
+        int aiss = 0;
+        for (; aiss < min(ns, GV_ACS_DEPTH); ++aiss) issue_act(aiss);
+        for (int k = 0; ok && (issued < total || aiss < ns); ++k) {
+          if (issued < total && issued == k + NS) {
+            const int st = issued % NS;
+            if (!mbar_wait(empty + st, ((issued / NS) - 1) & 1, 1u << 26)) {
+              raise_error(p.err, kErrTimeout);
+              ok = false;
+              break;
+            }
+            issue(issued++);
+          }
+          if (aiss < ns && aiss == k + GV_ACS_DEPTH) {
+            const int sa = aiss % GV_ACS_DEPTH;
+            if (!mbar_wait(act_empty + sa, ((aiss / GV_ACS_DEPTH) - 1) & 1, 1u << 26)) {
+              raise_error(p.err, kErrTimeout);
+              ok = false;
+              break;
+            }
+            issue_act(aiss++);
+          }
         }
-        issue(issued);
+        // the block's shared memory must outlive every activation copy issued into it
+        for (int j = max(0, aiss - GV_ACS_DEPTH); j < aiss; ++j)
+          if (!mbar_wait(act_full + j % GV_ACS_DEPTH, (j / GV_ACS_DEPTH) & 1)) raise_error(p.err, kErrTimeout);
+      } else {
+        uint32_t act_bytes = 0;
+        {
+          int s = 0, f = 0;
+          for (int sl = s0; sl < s1; ++sl) {
+            while (s + 1 < p.nseg && sl >= f + p.seg[s].lenp / GV_COLS) f += p.seg[s++].lenp / GV_COLS;
+            if (p.seg[s].xf) act_bytes += NT * GV_STAGE_BYTES;
+          }
+        }
+        mbar_arrive_expect_tx(act_bar, act_bytes);
+        {
+          int s = 0, f = 0;
+          for (int sl = s0; sl < s1; ++sl) {
+            while (s + 1 < p.nseg && sl >= f + p.seg[s].lenp / GV_COLS) f += p.seg[s++].lenp / GV_COLS;
+            const XSeg& sg = p.seg[s];
+            if (!sg.xf) continue;
+            for (int nt = 0; nt < NT; ++nt)
+              bulk_g2s(act + (nt * CHS + (sl - s0)) * GV_STAGE_BYTES,
+                       reinterpret_cast<const char*>(sg.xf) + (size_t(nt) * (sg.lenp >> 4) + size_t(sl - f) * GV_SLAB) * 512,
+                       GV_STAGE_BYTES, act_bar);
+          }
+        }
+        for (; issued < total; ++issued) {
+          const int st = issued % NS;
+          if (!mbar_wait(empty + st, ((issued / NS) - 1) & 1, 1u << 26)) {
+            raise_error(p.err, kErrTimeout);
+            ok = false;
+            break;
+          }
+          issue(issued);
+        }
       }
       // the HBM stream of this block is issued: fetch our share of the next GEMV's weights
       for (int rgn = 0; rgn < 2 && ok; ++rgn) {
@@ -557,7 +608,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
       // consumers gave up on a wait: wait (bounded) for the last copy of each slot
       for (int q = max(0, issued - NS); q < issued; ++q)
         if (!mbar_wait(full + q % NS, (q / NS) & 1)) raise_error(p.err, kErrTimeout);
-      if (!mbar_wait(act_bar, 0)) raise_error(p.err, kErrTimeout);
+      if (!p.acs && !mbar_wait(act_bar, 0)) raise_error(p.err, kErrTimeout);
       if (ss_bytes && !mbar_wait(ss_bar, 0)) raise_error(p.err, kErrTimeout);
     }
     return;
@@ -716,7 +767,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
     if (table) named_sync(1, GV_CTHREADS);
   }
   bool ok = true;
-  if (!mbar_wait(act_bar, 0)) {
+  if (!p.acs && !mbar_wait(act_bar, 0)) {
     raise_error(p.err, kErrTimeout);
     ok = false;
   }
@@ -752,6 +803,12 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
           raise_error(p.err, kErrTimeout);
           ok = false;
         }
+        if (p.acs && ok && !mbar_wait(act_full + si % GV_ACS_DEPTH, (si / GV_ACS_DEPTH) & 1)) {
+          raise_error(p.err, kErrTimeout);
+          ok = false;
+        }
+        // acs: this slab's activation piece sits in ring slot si % depth (8 rows: NT == 1)
+        const int abase = p.acs ? (si % GV_ACS_DEPTH) * GV_SLAB : si * GV_SLAB;
         if (ok) {
           const uint4* A = reinterpret_cast<const uint4*>(ring + st * GV_STAGE_BYTES);
 #pragma unroll
@@ -760,14 +817,17 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
             const uint4 a = A[kl * kWarp + lane];
 #pragma unroll
             for (int nt = 0; nt < NT; ++nt) {
-              const uint4 b = act4[((nt * CHS + si) * GV_SLAB + kl) * kWarp + lane];
+              const uint4 b = act4[(nt * CHS * GV_SLAB + abase + kl) * kWarp + lane];
               mma_bf16_16816(acc[nt][2 * i], a, b.x, b.y);
               mma_bf16_16816(acc[nt][2 * i + 1], a, b.z, b.w);
             }
           }
         }
         __syncwarp();
-        if (lane == 0) mbar_arrive(empty + st);
+        if (lane == 0) {
+          mbar_arrive(empty + st);
+          if (p.acs) mbar_arrive(act_empty + si % GV_ACS_DEPTH);
+        }
         const int gs = s0 + si;
         if (gs + 1 == seg_end || si + 1 == ns) {  // fold with the segment's 1/rms per activation row
 #pragma unroll

@@ -109,6 +109,7 @@ struct wc_ctx {
   bool pdl = true;           // programmatic dependent launch between round kernels
   int attn_mode = 2;         // bf16 caches: 2 decode kernel, 1 split-KV mma kernel, 0 CUDA cores
   int gemv_blocks_per_sm = 1;
+  bool gemv_acs = true;                  // whole-K blocks with streamed activation pieces (WC_GEMV_ACS=0: split K)
   bool gemv_prefetch = false;            // L2 prefetch of the next GEMV's weights (WC_GEMV_PREFETCH=1;
                                          // measured 1.6% slower on the C3 round: it competes with the
                                          // dependent loads of the kernels in between)
@@ -583,7 +584,18 @@ void launch_gemv(wc_ctx* ctx, const Lin& W, GemvParams p) {
   if (p.L_max < 1 || p.L_max > GEMV_MAXL) fail(WC_ERR_INVALID, "GEMV rows outside 1..16");
   if (p.nout > 2 || (p.nout > 0 && p.epi == EPI_ARGMAX)) fail(WC_ERR_INVALID, "bad GEMV outputs");
   p.out_width = xf_width(bf16, W.N);
-  const GemvPlan g = gemv_plan(ctx, W, p.L_max);
+  GemvPlan g = gemv_plan(ctx, W, p.L_max);
+  // a projection that would split K but has at most one unit per SM runs whole-K blocks,
+  // streaming the activation beside the weights (no partials, no last-block hand-off)
+  p.acs = 0;
+  if (bf16 && ctx->gemv_acs && g.nkc > 1 && p.L_max <= 8 && W.group == 1 && !(p.flags & GV_F_TABLE) &&
+      W.Np / 16 <= ctx->num_sms) {
+    p.acs = 1;
+    g.nkc = 1;
+    g.kc_slabs = W.Kp / GV_COLS;
+    g.gpk = W.Np / 16;
+    g.grid = g.gpk;
+  }
   if (p.ss_out && gemv_parts(ctx, W, p.L_max) > max_parts(ctx))
     fail(WC_ERR_INVALID, "GEMV output statistics above the buffer size");
   if (p.side_src) {
@@ -594,7 +606,7 @@ void launch_gemv(wc_ctx* ctx, const Lin& W, GemvParams p) {
     p.nkc = g.nkc;
     p.kc_slabs = g.kc_slabs;
     p.gpk = g.gpk;
-    if (g.kc_slabs > gv_chunk_slabs(p.L_max <= 8 ? 1 : 2)) fail(WC_ERR_INVALID, "GEMV chunk above the buffer");
+    if (!p.acs && g.kc_slabs > gv_chunk_slabs(p.L_max <= 8 ? 1 : 2)) fail(WC_ERR_INVALID, "GEMV chunk above the buffer");
     if (g.nkc > 1) {
       if (size_t(g.nkc) * (W.Np / 16) * 256 > ctx->gv_partial_n || g.gpk > ctx->gv_counters_n)
         fail(WC_ERR_UNSUPPORTED, "GEMV split-K scratch too small for this projection");
@@ -718,6 +730,7 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
     if (const char* e = std::getenv("WC_GEMV_BLOCKS_PER_SM")) ctx->gemv_blocks_per_sm = std::max(1, std::atoi(e));
     if (const char* e = std::getenv("WC_ATTN")) ctx->attn_mode = std::atoi(e);
     if (const char* e = std::getenv("WC_GEMV_PREFETCH")) ctx->gemv_prefetch = std::atoi(e) != 0;
+    if (const char* e = std::getenv("WC_GEMV_ACS")) ctx->gemv_acs = std::atoi(e) != 0;
     if (const char* e = std::getenv("WC_GEMV_PREFETCH_MB")) ctx->gemv_prefetch_cap = size_t(std::max(0, std::atoi(e))) << 20;
     ctx->d_err = static_cast<int*>(dalloc(sizeof(int)));
     CUDA_TRY(cudaMemset(ctx->d_err, 0, sizeof(int)));
