@@ -108,9 +108,9 @@ struct GemvParams {
   TokenSrc tok;
   int epi;
   int flags;             // GemvFlags of the segments (set by the launcher)
-  // acs = 1 (8 rows, group 1, one unit per block, no embedding segment): the whole K in one
-  // block, the activation streamed beside the weights in 16 KB pieces through a 4-deep ring
-  // in the activation buffer instead of split K
+  // acs = 1 (8 rows, group 1, one unit per block, no embedding segment; launched as the
+  // kernel's ACS instance): the whole K in one block, the activation streamed beside the
+  // weights in 16 KB pieces through a 4-deep ring in the activation buffer instead of split K
   int acs;
   float* y;              // fp32 result rows (optional except for argmax logits)
   int ldy;
@@ -300,6 +300,14 @@ __device__ __forceinline__ EpiIn gemv_epi_load(const GemvParams& p, int n, int l
   return e;
 }
 
+// EPI_ARGMAX element: stores the logit and returns its ranking key; callers keep the best key
+// of each row in registers and fold it into the block's key once (a shared atomic per element
+// serialises the 128 epilogue threads on a handful of row addresses).
+__device__ __forceinline__ unsigned long long gemv_argmax_item(const GemvParams& p, int n, int l, float v) {
+  if (p.y) p.y[size_t(l) * p.ldy + n] = v;
+  return argmax_key(gemv_pick_value(p, l, n, v), uint32_t(n));
+}
+
 __device__ __forceinline__ float gemv_epilogue_in(const GemvParams& p, int n, int l, float v0, float v1,
                                                   EpiIn e, unsigned long long* s_key) {
   float v = v0;
@@ -435,7 +443,7 @@ struct GvLayout {
 // shared-memory buffers (mbarriers red_full / red_empty) and go straight on to the next
 // unit's slabs, so the cross-warp reduction, the epilogue's global traffic and the split-K
 // hand-off overlap the weight stream instead of stalling it.
-template <int NT>
+template <int NT, bool ACS = false>
 __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constant__ const GemvParams pk) {
   using Lay = GvLayout<NT>;
   constexpr int NS = Lay::NS;
@@ -535,7 +543,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
         bulk_g2s(act + (j % GV_ACS_DEPTH) * GV_STAGE_BYTES,
                  reinterpret_cast<const char*>(sg.xf) + size_t(sl - af) * GV_SLAB * 512, GV_STAGE_BYTES, bar);
       };
-      if (p.acs) {
+      if (ACS) {
         // pieces j and weight slabs j are consumed together; slot j % depth frees after step
         // j - depth and weight slot j % NS after step j - NS: issue in the order they free
         int aiss = 0;
@@ -608,7 +616,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
       // consumers gave up on a wait: wait (bounded) for the last copy of each slot
       for (int q = max(0, issued - NS); q < issued; ++q)
         if (!mbar_wait(full + q % NS, (q / NS) & 1)) raise_error(p.err, kErrTimeout);
-      if (!p.acs && !mbar_wait(act_bar, 0)) raise_error(p.err, kErrTimeout);
+      if (!ACS && !mbar_wait(act_bar, 0)) raise_error(p.err, kErrTimeout);
       if (ss_bytes && !mbar_wait(ss_bar, 0)) raise_error(p.err, kErrTimeout);
     }
     return;
@@ -621,6 +629,14 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
     if (et < 16) s_key[et] = 0ull;
     named_sync(2, GV_ETHREADS);
     bool ok = true;
+    unsigned long long kbest[NT];  // EPI_ARGMAX: best key of this thread's row(s) (fixed per k)
+    int krow[NT];
+#pragma unroll
+    for (int k = 0; k < NT; ++k) {
+      const int idx = et + k * GV_ETHREADS;
+      kbest[k] = 0ull;
+      krow[k] = (idx / (4 * kWarp)) * 8 + 2 * (((idx / 4) % kWarp) % 4) + ((idx % 4) & 1);
+    }
     for (int u = u0, j = 0; u < u1; ++u, ++j) {
       const int b = j & 1;
       // this thread's elements of the unit; their epilogue inputs load while the MMAs run
@@ -663,6 +679,11 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
           for (int r = 0; r < 2; ++r)
             if (r < G)
               p.partial[((size_t(kc) * (p.Np >> 4) + size_t(u) * G + r) * 16 + r16_[k]) * 16 + l_[k]] = v[k][r];
+        } else if (p.epi == EPI_ARGMAX) {
+          if (live[k]) {
+            const unsigned long long key = gemv_argmax_item(p, u * 16 + r16_[k], l_[k], v[k][0]);
+            kbest[k] = key > kbest[k] ? key : kbest[k];
+          }
         } else {
           sq[r16_[k] * 16 + l_[k]] =
               live[k] ? gemv_epilogue_in(p, u * 16 + r16_[k], l_[k], v[k][0], v[k][1], ein[k], s_key) : 0.f;
@@ -678,6 +699,9 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
         }
       }
     }
+#pragma unroll
+    for (int k = 0; k < NT; ++k)
+      if (kbest[k]) atomicMax(&s_key[krow[k]], kbest[k]);
     if (p.nkc > 1) {
       // ---- split K: the last block of this unit range adds the chunks in order
       __threadfence();
@@ -686,53 +710,95 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
       named_sync(2, GV_ETHREADS);
       if (s_flag[0]) {
         __threadfence();
-        // up to 4 units at a time: every partial load of the group in flight together
-        constexpr int FU = 4, PER = FU * 256 / GV_ETHREADS;
-        float* s_sq8 = red;  // [FU][16 features][16 rows]; every unit of this block has been reduced
-        for (int ub = u0; ub < u1; ub += FU) {
-          const int nu = min(FU, u1 - ub), per = 16 * L, items = nu * per;
-          float v0[PER], v1[PER];
-          EpiIn ein[PER];
+        if (p.epi == EPI_ARGMAX) {
+          // heads: many units per range and no epilogue inputs; 16 units at a time, every
+          // partial load of a group in flight together, the best key per row in registers
+          constexpr int FU = 16, PER = FU * 256 / GV_ETHREADS;
+          unsigned long long fbest[NT * 8];
 #pragma unroll
-          for (int i = 0; i < PER; ++i) {  // every global input of the group before any store
-            v0[i] = v1[i] = 0.f;
-            const int it = et + i * GV_ETHREADS;
-            if (it < items) {
-              const int uu = it / per, r16 = (it % per) / L, l = it % L;
-              const int n = (ub + uu) * 16 + r16;
-              if (n < p.N) ein[i] = gemv_epi_load(p, n, l);
+          for (int r = 0; r < NT * 8; ++r) fbest[r] = 0ull;
+          for (int ub = u0; ub < u1; ub += FU) {
+            const int nu = min(FU, u1 - ub), per = 16 * L, items = nu * per;
+            float v0[PER];
+#pragma unroll
+            for (int i = 0; i < PER; ++i) v0[i] = 0.f;
+            for (int c = 0; c < p.nkc; ++c) {
+#pragma unroll
+              for (int i = 0; i < PER; ++i) {
+                const int it = et + i * GV_ETHREADS;
+                if (it < items) {
+                  const int uu = it / per, r16 = (it % per) / L, l = it % L;
+                  v0[i] += __ldcg(&p.partial[((size_t(c) * (p.Np >> 4) + size_t(ub + uu)) * 16 + r16) * 16 + l]);
+                }
+              }
             }
-          }
-          for (int c = 0; c < p.nkc; ++c) {
 #pragma unroll
             for (int i = 0; i < PER; ++i) {
               const int it = et + i * GV_ETHREADS;
               if (it < items) {
                 const int uu = it / per, r16 = (it % per) / L, l = it % L;
-                const float* src = &p.partial[((size_t(c) * (p.Np >> 4) + size_t(ub + uu) * G) * 16 + r16) * 16 + l];
-                v0[i] += __ldcg(src);
-                if (G == 2) v1[i] += __ldcg(src + 256);
+                const int n = (ub + uu) * 16 + r16;
+                if (n < p.N) {
+                  const unsigned long long key = gemv_argmax_item(p, n, l, v0[i]);
+#pragma unroll
+                  for (int r = 0; r < NT * 8; ++r)
+                    if (r == l && key > fbest[r]) fbest[r] = key;
+                }
               }
             }
           }
 #pragma unroll
-          for (int i = 0; i < PER; ++i) {
-            const int it = et + i * GV_ETHREADS;
-            if (it < items) {
-              const int uu = it / per, r16 = (it % per) / L, l = it % L;
-              const int n = (ub + uu) * 16 + r16;
-              s_sq8[(uu * 16 + r16) * 16 + l] = n < p.N ? gemv_epilogue_in(p, n, l, v0[i], v1[i], ein[i], s_key) : 0.f;
+          for (int r = 0; r < NT * 8; ++r)
+            if (fbest[r]) atomicMax(&s_key[r], fbest[r]);
+        } else {
+          // up to 4 units at a time: every global input of the group before any store
+          constexpr int FU = 4, PER = FU * 256 / GV_ETHREADS;
+          float* s_sq8 = red;  // [FU][16 features][16 rows]; every unit of this block has been reduced
+          for (int ub = u0; ub < u1; ub += FU) {
+            const int nu = min(FU, u1 - ub), per = 16 * L, items = nu * per;
+            float v0[PER], v1[PER];
+            EpiIn ein[PER];
+#pragma unroll
+            for (int i = 0; i < PER; ++i) {
+              v0[i] = v1[i] = 0.f;
+              const int it = et + i * GV_ETHREADS;
+              if (it < items) {
+                const int uu = it / per, r16 = (it % per) / L, l = it % L;
+                const int n = (ub + uu) * 16 + r16;
+                if (n < p.N) ein[i] = gemv_epi_load(p, n, l);
+              }
             }
+            for (int c = 0; c < p.nkc; ++c) {
+#pragma unroll
+              for (int i = 0; i < PER; ++i) {
+                const int it = et + i * GV_ETHREADS;
+                if (it < items) {
+                  const int uu = it / per, r16 = (it % per) / L, l = it % L;
+                  const float* src = &p.partial[((size_t(c) * (p.Np >> 4) + size_t(ub + uu) * G) * 16 + r16) * 16 + l];
+                  v0[i] += __ldcg(src);
+                  if (G == 2) v1[i] += __ldcg(src + 256);
+                }
+              }
+            }
+#pragma unroll
+            for (int i = 0; i < PER; ++i) {
+              const int it = et + i * GV_ETHREADS;
+              if (it < items) {
+                const int uu = it / per, r16 = (it % per) / L, l = it % L;
+                const int n = (ub + uu) * 16 + r16;
+                s_sq8[(uu * 16 + r16) * 16 + l] = n < p.N ? gemv_epilogue_in(p, n, l, v0[i], v1[i], ein[i], s_key) : 0.f;
+              }
+            }
+            named_sync(2, GV_ETHREADS);
+            if (p.ss_out && et < nu * 16) {  // fixed-order sum over each unit's 16 features
+              const int uu = et / 16, l = et % 16;
+              float a = 0.f;
+              if (l < L)
+                for (int f = 0; f < 16; ++f) a += s_sq8[(uu * 16 + f) * 16 + l];
+              p.ss_out[size_t(ub + uu) * 16 + l] = a;
+            }
+            named_sync(2, GV_ETHREADS);
           }
-          named_sync(2, GV_ETHREADS);
-          if (p.ss_out && et < nu * 16) {  // fixed-order sum over each unit's 16 features
-            const int uu = et / 16, l = et % 16;
-            float a = 0.f;
-            if (l < L)
-              for (int f = 0; f < 16; ++f) a += s_sq8[(uu * 16 + f) * 16 + l];
-            p.ss_out[size_t(ub + uu) * 16 + l] = a;
-          }
-          named_sync(2, GV_ETHREADS);
         }
         if (et == 0) p.counters[gi] = 0;  // ready for the next launch
       }
@@ -767,7 +833,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
     if (table) named_sync(1, GV_CTHREADS);
   }
   bool ok = true;
-  if (!p.acs && !mbar_wait(act_bar, 0)) {
+  if (!ACS && !mbar_wait(act_bar, 0)) {
     raise_error(p.err, kErrTimeout);
     ok = false;
   }
@@ -803,12 +869,12 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
           raise_error(p.err, kErrTimeout);
           ok = false;
         }
-        if (p.acs && ok && !mbar_wait(act_full + si % GV_ACS_DEPTH, (si / GV_ACS_DEPTH) & 1)) {
+        if (ACS && ok && !mbar_wait(act_full + si % GV_ACS_DEPTH, (si / GV_ACS_DEPTH) & 1)) {
           raise_error(p.err, kErrTimeout);
           ok = false;
         }
         // acs: this slab's activation piece sits in ring slot si % depth (8 rows: NT == 1)
-        const int abase = p.acs ? (si % GV_ACS_DEPTH) * GV_SLAB : si * GV_SLAB;
+        const int abase = ACS ? (si % GV_ACS_DEPTH) * GV_SLAB : si * GV_SLAB;
         if (ok) {
           const uint4* A = reinterpret_cast<const uint4*>(ring + st * GV_STAGE_BYTES);
 #pragma unroll
@@ -826,7 +892,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
         __syncwarp();
         if (lane == 0) {
           mbar_arrive(empty + st);
-          if (p.acs) mbar_arrive(act_empty + si % GV_ACS_DEPTH);
+          if (ACS) mbar_arrive(act_empty + si % GV_ACS_DEPTH);
         }
         const int gs = s0 + si;
         if (gs + 1 == seg_end || si + 1 == ns) {  // fold with the segment's 1/rms per activation row

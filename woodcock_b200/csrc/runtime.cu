@@ -582,7 +582,7 @@ void launch_gemv(wc_ctx* ctx, const Lin& W, GemvParams p) {
     if (p.seg[s].xf && p.seg[s].ss) p.flags |= GV_F_SS;
   }
   if (p.L_max < 1 || p.L_max > GEMV_MAXL) fail(WC_ERR_INVALID, "GEMV rows outside 1..16");
-  if (p.nout > 2 || (p.nout > 0 && p.epi == EPI_ARGMAX)) fail(WC_ERR_INVALID, "bad GEMV outputs");
+  if (p.nout > 2 || ((p.nout > 0 || p.ss_out) && p.epi == EPI_ARGMAX)) fail(WC_ERR_INVALID, "bad GEMV outputs");
   p.out_width = xf_width(bf16, W.N);
   GemvPlan g = gemv_plan(ctx, W, p.L_max);
   // a projection that would split K but has at most one unit per SM runs whole-K blocks,
@@ -613,7 +613,10 @@ void launch_gemv(wc_ctx* ctx, const Lin& W, GemvParams p) {
       p.partial = ctx->gv_partial;
       p.counters = ctx->gv_counters;
     }
-    if (p.L_max <= 8)
+    if (p.acs)
+      launch_ex(ctx, "gemv", gemv_bf16_kernel<1, true>, dim3(g.grid), dim3(GV_THREADS), gemv_bf16_smem<1>(), true, 1,
+                p);
+    else if (p.L_max <= 8)
       launch_ex(ctx, "gemv", gemv_bf16_kernel<1>, dim3(g.grid), dim3(GV_THREADS), gemv_bf16_smem<1>(), true, 1, p);
     else
       launch_ex(ctx, "gemv", gemv_bf16_kernel<2>, dim3(g.grid), dim3(GV_THREADS), gemv_bf16_smem<2>(), true, 1, p);
@@ -756,6 +759,7 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
     const int smax = int(ctx->max_smem);
     CUDA_TRY(cudaFuncSetAttribute(gemv_bf16_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(gemv_bf16_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
+    CUDA_TRY(cudaFuncSetAttribute(gemv_bf16_kernel<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(gemv_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(attention_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
