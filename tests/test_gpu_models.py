@@ -184,3 +184,29 @@ def test_bf16_target_logits_within_tolerance(tmp_path):
     zf, _ = ot.forward(prompt, ot.make_cache(), logits_from=20)
     assert np.abs(z - zf).max() <= 1e-2 * np.abs(zf).max()
     assert (z.argmax(-1) == zf.argmax(-1)).all()
+
+
+def test_bf16_target_logits_at_4b_widths(tmp_path):
+    """The same tolerances at Qwen3-4B widths (hidden 2560, 32 query heads, SwiGLU 9728): the
+    projections with K = 2560 run the 80 KB activation-chunk GEMV instance without splitting
+    K, the O projection (K = 4096) and down (K = 9728) split K; a 32,768-row head keeps the
+    oracle's fp32 pass short."""
+    import dataclasses
+
+    from woodcock_b200 import Target
+    from woodcock_b200 import synthetic as syn
+
+    ts = dataclasses.replace(syn.Q4_TARGET, layers=3, vocab=32768, tie_embeddings=True)
+    w = syn.round_to_bf16(syn.generate_weights(syn.target_tensor_specs(ts), seed=2))
+    t = Target.from_weights(ts.hf_config(), {k: torch.from_numpy(v).to(torch.bfloat16) for k, v in w.items()},
+                            feature_layers=[0, 1, 2], dtype="bf16")
+    prompt = syn.prompt_ids(24, ts.vocab, seed=3)
+    z = t(prompt, t.make_cache(64), logits_from=20).logits[0].cpu().numpy()
+    ot = O.Qwen3(ts.hf_config(), w, taps=[0, 1, 2])
+    ot.kv_bf16 = True
+    zb, _ = ot.forward(prompt, ot.make_cache(), logits_from=20)
+    assert np.abs(z - zb).max() <= 2e-3 * np.abs(zb).max() + 2e-3
+    ot.kv_bf16 = False
+    zf, _ = ot.forward(prompt, ot.make_cache(), logits_from=20)
+    assert np.abs(z - zf).max() <= 1e-2 * np.abs(zf).max()
+    assert (z.argmax(-1) == zf.argmax(-1)).all()

@@ -64,6 +64,10 @@ enum GemvFlags : int { GV_F_TOK = 1, GV_F_SS = 2, GV_F_TABLE = 4 };
 
 // Slabs of K per activation chunk: 4 (2048 columns) for 8 rows, 2 for 16 rows.
 __host__ __device__ constexpr int gv_chunk_slabs(int NT) { return GV_ACT_BYTES / (GV_STAGE_BYTES * NT); }
+// The wide instance (8 rows): a 5-slab activation chunk (K up to 2560, e.g. Qwen3-4B's hidden
+// width) in 80 KB, with a 7-stage weight ring, so those projections need not split K.
+constexpr int GV_WIDE_ACT_BYTES = 80 * 1024;
+constexpr int GV_WIDE_SLABS = GV_WIDE_ACT_BYTES / GV_STAGE_BYTES;
 
 // Fragment width of an input of K columns: bf16 models pad to whole ring slabs.
 __host__ __device__ inline int xf_width(bool bf16, int K) { return bf16 ? (K + GV_COLS - 1) / GV_COLS * GV_COLS : K; }
@@ -418,12 +422,14 @@ __device__ void gemv_prologue_fast(const GemvParams& p, int L, int* s_tok, float
 }
 
 // Shared-memory carve-up of the bf16 kernel (byte offsets, every region 16-byte aligned).
-template <int NT>
+template <int NT, bool WIDE = false>
 struct GvLayout {
-  static constexpr int NS = gv_nstage(NT);
+  static constexpr int NS = WIDE ? gv_nstage(NT) - 1 : gv_nstage(NT);
+  static constexpr int ACT_BYTES = WIDE ? GV_WIDE_ACT_BYTES : GV_ACT_BYTES;
+  static constexpr int CHS = ACT_BYTES / (GV_STAGE_BYTES * NT);            // slabs per activation chunk
   static constexpr size_t ring = 0;                                        // NS x 16 KB weight slabs
   static constexpr size_t act = ring + size_t(NS) * GV_STAGE_BYTES;        // [NT][CHS][32 kt][32 lanes] uint4
-  static constexpr size_t bars = act + GV_ACT_BYTES;  // full[NS] empty[NS] act red_full[2] red_empty[2] ss act_full[4] act_empty[4]
+  static constexpr size_t bars = act + ACT_BYTES;  // full[NS] empty[NS] act red_full[2] red_empty[2] ss act_full[4] act_empty[4]
   static constexpr size_t nbars = 2 * NS + 6 + 2 * GV_ACS_DEPTH;
   static constexpr size_t red = bars + (nbars * 8 + 15) / 16 * 16;         // [2 buffers][2 row blocks][NT][W][32][4] floats
   static constexpr size_t red_buf = size_t(2) * NT * GV_CWARPS * kWarp * 4;  // floats per buffer
@@ -443,11 +449,12 @@ struct GvLayout {
 // shared-memory buffers (mbarriers red_full / red_empty) and go straight on to the next
 // unit's slabs, so the cross-warp reduction, the epilogue's global traffic and the split-K
 // hand-off overlap the weight stream instead of stalling it.
-template <int NT, bool ACS = false>
+template <int NT, bool ACS = false, bool WIDE = false>
 __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constant__ const GemvParams pk) {
-  using Lay = GvLayout<NT>;
+  static_assert(!(ACS && WIDE) && (!WIDE || NT == 1), "kernel instances: ACS and WIDE are 8-row, exclusive");
+  using Lay = GvLayout<NT, WIDE>;
   constexpr int NS = Lay::NS;
-  constexpr int CHS = gv_chunk_slabs(NT);
+  constexpr int CHS = Lay::CHS;
   extern __shared__ __align__(128) unsigned char gv_smem[];
   unsigned char* ring = gv_smem + Lay::ring;
   unsigned char* act = gv_smem + Lay::act;
@@ -935,9 +942,9 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
   if (p.side_src && int(blockIdx.x) < p.side_blocks) gemv_side_job(p, L, s_inv, s_part, GV_CTHREADS, true);
 }
 
-template <int NT>
+template <int NT, bool WIDE = false>
 constexpr size_t gemv_bf16_smem() {
-  return GvLayout<NT>::total + 128;
+  return GvLayout<NT, WIDE>::total + 128;
 }
 
 // ----------------------------------------------------------------------------- fp32 models

@@ -109,6 +109,7 @@ struct wc_ctx {
   bool pdl = true;           // programmatic dependent launch between round kernels
   int attn_mode = 2;         // bf16 caches: 2 decode kernel, 1 split-KV mma kernel, 0 CUDA cores
   int gemv_blocks_per_sm = 1;
+  bool gemv_wide = true;                 // 80 KB activation chunks for K up to 2560 (WC_GEMV_WIDE=0: split K)
   bool gemv_acs = true;                  // whole-K blocks with streamed activation pieces (WC_GEMV_ACS=0: split K)
   bool gemv_prefetch = false;            // L2 prefetch of the next GEMV's weights (WC_GEMV_PREFETCH=1;
                                          // measured 1.6% slower on the C3 round: it competes with the
@@ -514,6 +515,7 @@ XSeg xs_embed(const void* table, int len, bool bf16, const float* norm_w, const 
 // per chunk so that one block runs per SM.
 struct GemvPlan {
   int grid = 1, nkc = 1, kc_slabs = 1, gpk = 1;
+  bool wide = false;  // the 80 KB activation-chunk instance
 };
 
 GemvPlan gemv_plan(const wc_ctx* ctx, const Lin& W, int L_max) {
@@ -527,6 +529,10 @@ GemvPlan gemv_plan(const wc_ctx* ctx, const Lin& W, int L_max) {
   const int nslab = W.Kp / GV_COLS;
   const int nunits = W.Np / (16 * W.group);
   g.nkc = (nslab + chs - 1) / chs;
+  if (NT == 1 && g.nkc > 1 && nslab <= GV_WIDE_SLABS && ctx->gemv_wide) {  // K up to 2560: no split
+    g.nkc = 1;
+    g.wide = true;
+  }
   g.kc_slabs = (nslab + g.nkc - 1) / g.nkc;
   const int target = ctx->num_sms * std::min(ctx->gemv_blocks_per_sm, ctx->occ_gemv[NT]);
   g.gpk = std::max(1, std::min(nunits, target / g.nkc));
@@ -606,7 +612,8 @@ void launch_gemv(wc_ctx* ctx, const Lin& W, GemvParams p) {
     p.nkc = g.nkc;
     p.kc_slabs = g.kc_slabs;
     p.gpk = g.gpk;
-    if (!p.acs && g.kc_slabs > gv_chunk_slabs(p.L_max <= 8 ? 1 : 2)) fail(WC_ERR_INVALID, "GEMV chunk above the buffer");
+    if (!p.acs && g.kc_slabs > (g.wide ? GV_WIDE_SLABS : gv_chunk_slabs(p.L_max <= 8 ? 1 : 2)))
+      fail(WC_ERR_INVALID, "GEMV chunk above the buffer");
     if (g.nkc > 1) {
       if (size_t(g.nkc) * (W.Np / 16) * 256 > ctx->gv_partial_n || g.gpk > ctx->gv_counters_n)
         fail(WC_ERR_UNSUPPORTED, "GEMV split-K scratch too small for this projection");
@@ -616,6 +623,9 @@ void launch_gemv(wc_ctx* ctx, const Lin& W, GemvParams p) {
     if (p.acs)
       launch_ex(ctx, "gemv", gemv_bf16_kernel<1, true>, dim3(g.grid), dim3(GV_THREADS), gemv_bf16_smem<1>(), true, 1,
                 p);
+    else if (g.wide)
+      launch_ex(ctx, "gemv", gemv_bf16_kernel<1, false, true>, dim3(g.grid), dim3(GV_THREADS),
+                gemv_bf16_smem<1, true>(), true, 1, p);
     else if (p.L_max <= 8)
       launch_ex(ctx, "gemv", gemv_bf16_kernel<1>, dim3(g.grid), dim3(GV_THREADS), gemv_bf16_smem<1>(), true, 1, p);
     else
@@ -734,6 +744,7 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
     if (const char* e = std::getenv("WC_ATTN")) ctx->attn_mode = std::atoi(e);
     if (const char* e = std::getenv("WC_GEMV_PREFETCH")) ctx->gemv_prefetch = std::atoi(e) != 0;
     if (const char* e = std::getenv("WC_GEMV_ACS")) ctx->gemv_acs = std::atoi(e) != 0;
+    if (const char* e = std::getenv("WC_GEMV_WIDE")) ctx->gemv_wide = std::atoi(e) != 0;
     if (const char* e = std::getenv("WC_GEMV_PREFETCH_MB")) ctx->gemv_prefetch_cap = size_t(std::max(0, std::atoi(e))) << 20;
     ctx->d_err = static_cast<int*>(dalloc(sizeof(int)));
     CUDA_TRY(cudaMemset(ctx->d_err, 0, sizeof(int)));
@@ -760,6 +771,8 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
     CUDA_TRY(cudaFuncSetAttribute(gemv_bf16_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(gemv_bf16_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(gemv_bf16_kernel<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
+    CUDA_TRY(cudaFuncSetAttribute(gemv_bf16_kernel<1, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  smax));
     CUDA_TRY(cudaFuncSetAttribute(gemv_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(attention_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
