@@ -11,23 +11,30 @@
 // 1/rms table built at load time.
 //
 // bf16 weights are pre-tiled in mma.m16n8k16 A-fragment order (16x16 tile = 512 contiguous
-// bytes). One block per SM: a producer warp streams the block's weights through a 4-stage
+// bytes). One block per SM: a producer warp streams the block's weights through an 8-stage
 // ring of 16 KB shared-memory slabs with 1-D bulk (TMA) copies marked L2 evict-first; the
 // first stages are issued before the kernel waits on its predecessor (programmatic
-// dependent launch). After the wait the producer bulk-copies the activation fragments of
-// the block's K-chunk into shared memory once, so the MMA loop reads only shared memory.
-// Eight MMA warps split each slab's k-tiles and issue two MMAs per tile and n-tile
-// (activation hi and lo bf16 terms, fp32-level accuracy), then release the slot through an
-// mbarrier. At the end of each 16-feature unit they hand their per-warp sums to four
-// epilogue warps through two shared-memory buffers and continue with the next unit, so the
-// cross-warp reduction and the epilogue's global traffic overlap the weight stream. When K
-// exceeds the activation buffer, K is split into chunks: the blocks of one row range write
-// fp32 partials and the last of them to arrive (one fence and one atomic per block) adds them
-// in chunk order and runs the epilogue, so results do not depend on arrival order. Epilogues: store, residual add (linear(..., accumulate=true)), SwiGLU
+// dependent launch). After the wait the producer bulk-copies the input rows' RMSNorm
+// statistics and the activation fragments of the block's K-chunk into shared memory once,
+// so the MMA loop reads only shared memory. Eight MMA warps split each slab's k-tiles and
+// issue two MMAs per tile and n-tile (activation hi and lo bf16 terms, fp32-level
+// accuracy), then release the slot through an mbarrier. At the end of each 16-feature unit
+// they hand their per-warp sums to four epilogue warps through two shared-memory buffers
+// and continue with the next unit, so the cross-warp reduction and the epilogue's global
+// traffic overlap the weight stream.
+//
+// Three instances: the default (64 KB activation chunk, up to 2048 columns at 8 rows); the
+// wide one (80 KB chunk, 7-stage ring: K up to 2560 without splitting); and the streamed
+// one (ACS: whole K in one block for projections with at most one unit per SM, the
+// activation streamed in 16 KB pieces through a 4-deep ring beside the weight slab each
+// piece multiplies). Otherwise, when K exceeds the chunk, K is split: the blocks of one row
+// range write fp32 partials and the last of them to arrive (one fence and one atomic per
+// block) adds them in chunk order and runs the epilogue, so results do not depend on
+// arrival order. Epilogues: store, residual add (linear(..., accumulate=true)), SwiGLU
 // (silu(gate)*up, cpu_ops.cpp:79-84, gate/up row blocks interleaved) and a fused argmax;
 // stored results can also be emitted as fragments for up to two consumers (times their norm
-// gains) and as per-unit sums of squares for their 1/rms. As its own stream ends, each block
-// prefetches its share of the next GEMV's weights into L2.
+// gains) and as per-unit sums of squares for their 1/rms. Optionally, as its own stream
+// ends, each block prefetches its share of the next GEMV's weights into L2.
 //
 // fp32 weights (row-major [N][Kp]) run the same interface on CUDA cores: fragments are
 // then plain fp32 rows [16][len].
