@@ -88,7 +88,7 @@ class ClockSampler:
          "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu: int):
-        self.gpu, self.rows, self.proc = gpu, [], None
+        self.gpu, self.rows, self.proc, self.n_before = gpu, [], None, 0
 
     def __enter__(self):
         try:
@@ -96,6 +96,11 @@ class ClockSampler:
                                           "-i", str(self.gpu), "-lms", "50"], stdout=subprocess.PIPE,
                                          stderr=subprocess.DEVNULL, text=True)
             threading.Thread(target=self._read, daemon=True).start()
+            # nvidia-smi needs a moment to start: the timed region begins after its first sample
+            t0 = time.time()
+            while not self.rows and time.time() - t0 < 5.0 and self.proc.poll() is None:
+                time.sleep(0.01)
+            self.n_before = len(self.rows)
         except OSError:
             self.proc = None
         return self
@@ -106,7 +111,10 @@ class ClockSampler:
 
     def __exit__(self, *a):
         if self.proc:
-            time.sleep(0.12)
+            # one more sample after the timed region, so the samples bracket it
+            n, t0 = len(self.rows), time.time()
+            while len(self.rows) <= n and time.time() - t0 < 2.0 and self.proc.poll() is None:
+                time.sleep(0.01)
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
@@ -147,41 +155,43 @@ def build_models(device: int):
 def write_reference_files(root: Path, device: int) -> tuple[Path, Path]:
     """The same seeded C3 weights as safetensors (bf16) for the reference C++ core; the drafter
     keeps its full 151,936-row head (the reference's C++ drafter has no trimmed head)."""
-    import torch
-
-    from woodcock_b200 import safetensors_io as st
     from woodcock_b200 import synthetic as syn
 
     ts, ds = syn.Q17_TARGET, syn.Q17_DRAFTER
     td, dd = root / "target", root / "drafter"
     if (root / "complete").exists():
         return td, dd
-    for d_, cfg, specs, seed in ((td, ts.hf_config(), syn.target_tensor_specs(ts), 0),
-                                 (dd, ds.config(), syn.drafter_tensor_specs(ds), 1)):
-        d_.mkdir(parents=True, exist_ok=True)
-        (d_ / "config.json").write_text(json.dumps(cfg))
-        stream = syn.device_weight_stream(specs, seed=seed, device=f"cuda:{device}")
-
-        def produce(name, _s=stream):
-            n, w = next(_s)
-            assert n == name
-            return w.view(torch.int16).cpu().numpy().view("uint16")
-
-        st.save_streaming(d_ / "model.safetensors", [(n, "BF16", s) for n, s, _ in specs], produce)
+    syn.write_device_model(td, ts.hf_config(), syn.target_tensor_specs(ts), 0, f"cuda:{device}")
+    syn.write_device_model(dd, ds.config(), syn.drafter_tensor_specs(ds), 1, f"cuda:{device}")
     (root / "complete").write_text("ok")
     return td, dd
 
 
-def run_reference_round(td: Path, dd: Path, rounds: int, prompt_len: int = 2, k: int = 4) -> dict:
+def run_reference_round(td: Path, dd: Path, rounds: int, prompt_len: int = 2, k: int = 4, accept: int = 2) -> dict:
+    """The reference C++ core in oracle-drafter mode (`wc_ref_driver forced`): it first computes
+    its own greedy continuation, then runs `rounds` chain-k rounds whose drafts are that
+    continuation with draft accept+1 corrupted, so each round really accepts `accept` drafts and
+    emits accept + 1 tokens while every draft, verify and update step of the reference runs.
+    Returns the reference's own timing of the rounds (prefill and the continuation excluded)."""
     from woodcock_b200 import synthetic as syn
 
     prompt = syn.prompt_ids(prompt_len, syn.Q17_TARGET.vocab, seed=0)
-    cmd = [str(REF_DRIVER), "gen", "--target", str(td), "--drafter", str(dd), "--ids", ",".join(map(str, prompt)),
-           "--max", str(1 + rounds), "--policy", f"chain:{k}", "--taps", "2,14,26", "--no-eos"]
-    r = subprocess.run(cmd, capture_output=True, text=True, check=True)
+    tpl = " ".join(f"{j}:{j}:{1 if j == accept else 0}" for j in range(k))
+    with tempfile.NamedTemporaryFile("w", suffix=".txt", delete=False) as f:
+        f.write(tpl + "\n")
+        tpl_path = f.name
+    try:
+        cmd = [str(REF_DRIVER), "forced", "--target", str(td), "--drafter", str(dd), "--ids",
+               ",".join(map(str, prompt)), "--max", str(1 + rounds * (accept + 1)), "--taps", "2,14,26",
+               "--trees", tpl_path]
+        r = subprocess.run(cmd, capture_output=True, text=True, check=True)
+    finally:
+        os.unlink(tpl_path)
     out = json.loads(r.stdout)
-    out["round_s"] = (out["t_total"] - out["t_prefill"]) / max(1, out["rounds"])
-    return out
+    emitted = [len(x["path"]) + 1 for x in out["rounds"]]
+    secs = [float(x) for x in out["round_s"]]
+    return {"rounds": len(secs), "tokens": sum(emitted), "seconds": sum(secs), "round_s": sum(secs) / len(secs),
+            "accepted_per_round": [len(x["path"]) for x in out["rounds"]], "t_prefill": out["t_prefill"]}
 
 
 # ----------------------------------------------------------------------------- our arm
@@ -297,17 +307,10 @@ def bench_ours(a):
     traffic = None
     tp = REPO / "profiles" / "ncu_traffic.json"
     tdata = json.loads(tp.read_text()) if tp.exists() else {}
-    if kp.get("target_stack", {}).get("launches_per_round", 0) > 0:
-        # the dominant kernel is the persistent layer stack (all target layers of the verify)
-        kbytes = rl.target_stack_bytes(ts, PROMPT_LEN + 1)
-        kms = kp["target_stack"]["mean_ms"]
-        kname = "stack_kernel (target layer stack: QKV, attention, O, gate/up, down of every layer)"
-        traffic = tdata.get("stack_kernel_bytes_per_launch")
-    else:
-        kbytes = 2 * ts.intermediate * ts.hidden * 2 + L * ts.hidden * 4 + L * ts.intermediate * 4
-        kms = kp["target_gate_up"]["mean_ms"]
-        kname = "gemv_bf16_kernel (target gate/up projection, SwiGLU epilogue)"
-        traffic = tdata.get("target_gate_up_bytes_per_launch")
+    kbytes = 2 * ts.intermediate * ts.hidden * 2 + L * ts.hidden * 4 + L * ts.intermediate * 4
+    kms = kp["target_gate_up"]["mean_ms"]
+    kname = "gemv_bf16_kernel (target gate/up projection, SwiGLU epilogue)"
+    traffic = tdata.get("target_gate_up_bytes_per_launch")
     # one chain step (time_draft_step.py:51-56): trimmed head + one drafter layer pass
     step_ms = kp["drafter_head"]["mean_ms"] + kp["drafter_layer"]["mean_ms"]
     step_bytes = rl.draft_step_bytes(ds, HEAD_ROWS, PROMPT_LEN + 1)
@@ -334,12 +337,17 @@ def bench_ours(a):
                "path": "target layers as tcgen05 GEMMs over the 512 prompt rows, then the drafter prefill; "
                        "wall time of SpeculativeDecoder.prefill"}
     # e2e: the public API (SpeculativeDecoder.generate) with host prompt and per-round host copies
+    # every rank runs its own generation at the same time; the job's figure is all ranks' decode
+    # tokens over the slowest rank's decode time (the same reduction as `value`)
     prompt, ar = streams[0]
     dec.forced = forced_from(ar, acc_len)
+    if world > 1:
+        dist.barrier()
     out_e2e, st = dec.generate(prompt, NEW_TOKENS, stop_on_eos=False)
     dec.forced = None
     assert out_e2e == ar[:NEW_TOKENS]
-    e2e = {"value": st.decode_tps * world, "unit": "tok/s", "h2d_bytes_per_step": 16 * 4,
+    e2e_agg = aggregate((st.t_total - st.t_prefill) * 1e3, float(st.new_tokens - 1))
+    e2e = {"value": e2e_agg["value"], "unit": "tok/s", "h2d_bytes_per_step": 16 * 4,
            "d2h_bytes_per_step": (k + 2) * 4 + 4, "rounds": st.rounds,
            "note": "SpeculativeDecoder.generate over a 256-token generation: per round the forced drafts go "
                    "host->device and the emitted tokens come back; prefill excluded as in GenStats.decode_tps"}
@@ -348,8 +356,7 @@ def bench_ours(a):
         "ms_per_step": timed_ms / a.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic: seeded random-init Qwen3-1.7B-architecture weights, uniform-random prompt ids",
-        "config": {"workload": "C3: Qwen3-1.7B arch bf16 greedy chain round, k=4, batch 1, 512-token prompts, "
-                               "256-token generations, EAGLE-3 drafter with a 16,384-row head (taps 2,14,26)",
+        "config": {"workload": C3_WORKLOAD,
                    "k": k, "accept_len": acc_len, "tokens_per_round": acc_len + 1, "prompt_tokens": PROMPT_LEN,
                    "new_tokens": NEW_TOKENS, "drafter_head_rows": HEAD_ROWS,
                    "mode": "oracle drafter: drafts = greedy continuation except draft a+1",
@@ -383,16 +390,28 @@ def bench_ours(a):
             Path(a.out).write_text(s + "\n")
 
 
+C3_WORKLOAD = ("C3: Qwen3-1.7B arch bf16 greedy chain round, k=4, batch 1, 512-token prompts, 256-token "
+               "generations, EAGLE-3 drafter with a 16,384-row head (taps 2,14,26)")
+REF_DIFFERENCES = {
+    "prompt_tokens": "2 instead of 512: a 512-token fp32 prefill takes ~10 min on one core; attention over 512 "
+                     "more rows would add ~2% to a round, whose cost is the 1.7B-parameter weight loops",
+    "drafter_head": "full 151,936 rows: the reference's C++ drafter has no trimmed head (README.md:180)",
+    "dtype": "fp32 compute on the same bf16-rounded weights (the reference's C++ core has no bf16 path)",
+    "acceptance": "oracle-drafter mode as ours: drafts = the reference's own greedy continuation with draft "
+                  "a+1 corrupted, so every round accepts a drafts and emits a+1 tokens",
+}
+
+
 def cpu_baseline(device: int, acc_len: int, k: int) -> dict:
     root = Path(tempfile.gettempdir()) / "wc_bench_c3_ref"
     td, dd = write_reference_files(root, device)
-    r = run_reference_round(td, dd, rounds=1, k=k)
-    return {"value": (acc_len + 1) / r["round_s"], "unit": "tok/s", "cores": 1, "kind": "reference",
-            "round_s": r["round_s"],
-            "sample": f"the reference C++ core (oracle/_ref/wc_ref_driver, built from its sources, fp32 loops, "
-                      f"single-threaded) on the same seeded C3 weights: 1 chain-{k} round after a 2-token prompt; "
-                      f"its C++ drafter has no trimmed head, so the full 151,936-row head runs; value = "
-                      f"{acc_len + 1} tokens per round (this arm's accept length) / measured round time"}
+    r = run_reference_round(td, dd, rounds=1, k=k, accept=acc_len)
+    return {"value": r["tokens"] / r["seconds"], "unit": "tok/s", "cores": 1, "kind": "reference",
+            "round_s": r["round_s"], "accepted_per_round": r["accepted_per_round"],
+            "sample": f"the reference C++ core (oracle/_ref/wc_ref_driver forced, built from its sources, fp32 "
+                      f"loops, single-threaded) on the same seeded C3 weights: 1 chain-{k} round accepting "
+                      f"{acc_len} drafts (oracle-drafter mode) after a 2-token prompt, full 151,936-row drafter "
+                      f"head; value = tokens emitted / the reference's own time of the round"}
 
 
 # ----------------------------------------------------------------------------- reference arm
@@ -414,25 +433,37 @@ def bench_reference(a):
         avail_gb = int(open("/proc/meminfo").read().split("MemAvailable:")[1].split()[0]) / 1e6
     except Exception:
         avail_gb = 32.0
-    procs = max(1, min(ncores, int(avail_gb // 16)))  # ~10 GB of fp32 weights per process
+    # the reference is single-threaded: one process per core, as many as ~16 GB each allows
+    # (fp32 copies of the target and of the full-head drafter, plus the file cache)
+    procs = max(1, min(ncores, int(avail_gb // 16)))
     rounds = max(1, min(3, math.ceil((a.warmup + a.steps) / procs)))
     t0 = time.perf_counter()
     from concurrent.futures import ThreadPoolExecutor
 
     with ThreadPoolExecutor(procs) as ex:
-        res = list(ex.map(lambda i: run_reference_round(td, dd, rounds=rounds, k=a.k), range(procs)))
+        res = list(ex.map(lambda i: run_reference_round(td, dd, rounds=rounds, k=a.k, accept=a.accept),
+                          range(procs)))
     wall = time.perf_counter() - t0
-    rate = sum((a.accept + 1) / r["round_s"] for r in res)
+    rate = sum(r["tokens"] / r["seconds"] for r in res)  # processes run concurrently
+    round_ms = statistics.mean(r["round_s"] for r in res) * 1e3
     line = {"impl": "reference", "metric": METRIC, "value": rate, "unit": "tok/s", "n_gpus": world,
-            "steps": a.steps, "warmup": a.warmup, "ms_per_step": statistics.mean(r["round_s"] for r in res) * 1e3,
+            "steps": rounds, "warmup": 0, "ms_per_step": round_ms,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic: the same seeded Qwen3-1.7B-architecture weights (bf16 files, fp32 compute)",
-            "config": {"workload": "C3 chain-4 round on the reference C++ core (full 151,936-row drafter head)",
-                       "k": a.k, "accept_len": a.accept, "processes": procs, "rounds_per_process": rounds},
-            "cpu_baseline": {"value": rate, "unit": "tok/s", "cores": procs, "kind": "reference",
-                             "sample": f"{procs} independent single-threaded reference processes x {rounds} "
-                                       f"round(s) each after a 2-token prompt; rate = sum over processes of "
-                                       f"{a.accept + 1} tokens / round time"},
+            "config": {"workload": C3_WORKLOAD, "k": a.k, "accept_len": a.accept, "tokens_per_round": a.accept + 1,
+                       "prompt_tokens": 2, "drafter_head_rows": 151936, "processes": procs,
+                       "rounds_per_process": rounds, "host_cores": ncores,
+                       "differences_from_ours": REF_DIFFERENCES,
+                       "steps_note": f"steps = rounds each process ran ({procs} processes in parallel); the "
+                                     f"--steps {a.steps} --warmup {a.warmup} request is bounded to keep the CPU "
+                                     f"run to a few minutes"},
+            "accepted_per_round": sorted({x for r in res for x in r["accepted_per_round"]}),
+            "cpu_baseline": {"value": rate, "unit": "tok/s", "cores": procs, "host_cores": ncores,
+                             "kind": "reference",
+                             "sample": f"{procs} independent single-threaded reference processes (of {ncores} host "
+                                       f"cores) x {rounds} chain-{a.k} round(s) each, accepting {a.accept} drafts "
+                                       f"per round, after a 2-token prompt; rate = sum over processes of tokens "
+                                       f"emitted / the reference's own round time"},
             "e2e": {"value": rate, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
             "wall_s": wall}
     print(json.dumps(line), flush=True)

@@ -176,7 +176,7 @@ WC_API wc_status wc_accept_stochastic(wc_ctx* ctx, const double* p_dev, const do
                                int* out_n_dev, int* out_next_dev, int* out_used_dev);
 /* The same decision as wc_accept_stochastic (same arguments, same results), for callers that must
  * not allocate device memory while they verify. No counterpart in the reference, whose sampling
- * runs on the host (python/woodcock/sampling.py, src/core/sampling.cpp).
+ * runs on the host (python/woodcock/sampling.py, src/sampling/sampling.cpp).
  * wc_accept_stochastic keeps two scratch rows of V doubles per context and grows them with
  * cudaMalloc / cudaFree on its first call and whenever V grows. cudaFree waits for the whole
  * device, which a caller that keeps other streams busy cannot accept, and a caller that runs
@@ -240,7 +240,8 @@ WC_API wc_status wc_decoder_set_forced(wc_decoder* dec, const int* forced, int k
  * probs_from_logits does (sampling.py:39-55), as one threshold per row on z / T; the draft
  * distribution uses the temperature only (spec.py:113-125). */
 WC_API wc_status wc_decoder_round(wc_decoder* dec, int k, int* out_tokens, int* out_n);
-/* spec.py:151-212 generate with a static chain policy of depth k (trees: WC_ERR_UNSUPPORTED until built).
+/* spec.py:151-212 generate with a static chain policy of depth k (draft trees go through
+ * wc_decoder_tree_round; per-round chain lengths through wc_decoder_round).
  * eos: host int32[n_eos]. out_tokens capacity max_new. */
 WC_API wc_status wc_decoder_generate(wc_decoder* dec, const int* prompt, int n, int max_new, int k,
                               const wc_sampling_params* sp, const int* eos, int n_eos, int* out_tokens, int* out_n,
@@ -260,11 +261,14 @@ WC_API wc_status wc_decoder_restore_state(wc_decoder* dec);
  * of that round}. Host buffers; any may be NULL. */
 WC_API wc_status wc_decoder_round_logits(wc_decoder* dec, int k, float* zt, float* zd, int* tokens,
                                          unsigned long long* rng);
+/* Test support, no counterpart in the reference: the drafter's own choice at each of the last
+ * greedy round's k chain steps (head argmax mapped to a token id, and its logit), also when
+ * wc_decoder_set_forced replaced the drafts. Host buffers; either may be NULL. */
+WC_API wc_status wc_decoder_draft_proposals(wc_decoder* dec, int k, int* tokens, float* logits);
 /* A real round (as wc_decoder_round) replayed from a second graph that records CUDA events
  * around kernels: ms_sum[i] / counts[i] is the mean device time of kernel class i, for
  * i = 0 target QKV GEMV, 1 attention, 2 o-proj, 3 gate/up, 4 down-proj, 5 target head,
- * 6 drafter head, 7 drafter layer pass (whole), 8 target layer stack (the persistent kernel
- * that replaces classes 0-4 in the verify pass when it is used). Arrays of 16. */
+ * 6 drafter head, 7 drafter layer pass (whole). Arrays of 16. */
 WC_API wc_status wc_decoder_profile_round(wc_decoder* dec, int k, int* out_tokens, int* out_n, float* ms_sum,
                                           int* counts);
 /* device-side state after the last round: committed length n (target cache size) and drafter cache size */

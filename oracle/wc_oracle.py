@@ -105,10 +105,9 @@ def _philox_words(seed: int, start: int, n: int):
 
 
 def philox_gumbel_f32(seed: int, start: int, n: int) -> np.ndarray:
-    """float32 Gumbel noise, u = (24 bits of word 0 + 1/2) / 2^24 on (0, 1)."""
-    r0, _, _, _ = _philox_words(seed, start, n)
-    u = ((r0 >> np.uint32(8)).astype(F32) + F32(0.5)) * F32(1.0 / 16777216.0)
-    return (-np.log(-np.log(u))).astype(F32)
+    """The float64 noise of philox_gumbel_f64 rounded to float32 (the device's head-epilogue and
+    first-token draws)."""
+    return philox_gumbel_f64(seed, start, n).astype(F32)
 
 
 def philox_gumbel_f64(seed: int, start: int, n: int) -> np.ndarray:
@@ -215,12 +214,20 @@ def sampled_chain_accept(zt: np.ndarray, zd: np.ndarray, tokens: list[int], T: f
     return a, int(np.argmax(key))
 
 
-def chi2_equal_mass(counts: np.ndarray, p: np.ndarray, bins: int = 1000) -> tuple[float, int, float]:
-    """Pearson chi-square of token counts against the law p, on `bins` groups of consecutive
-    token ids with (near) equal expected mass (the binning the reference's test uses where one
-    token per cell would leave expected counts under 5, tests/test_sampling.py:73-76).
-    Returns (statistic, degrees of freedom, p-value)."""
+def chi2_equal_mass(counts: np.ndarray, p: np.ndarray, bins: int = 1000, order: str = "id") -> tuple[float, int, float]:
+    """Pearson chi-square of token counts against the law p, on `bins` groups of tokens with
+    (near) equal expected mass (the binning the reference's test uses where one token per cell
+    would leave expected counts under 5, tests/test_sampling.py:73-76). order="id" groups
+    consecutive token ids; order="rank" groups tokens in decreasing order of p, so a bias that
+    grows or shrinks with the logit concentrates in the first or last bins instead of averaging
+    out. Returns (statistic, degrees of freedom, p-value)."""
     from scipy.stats import chi2
+    counts, p = np.asarray(counts, np.float64), np.asarray(p, np.float64)
+    if order == "rank":
+        perm = np.argsort(-p, kind="stable")
+        counts, p = counts[perm], p[perm]
+    elif order != "id":
+        raise ValueError("order must be 'id' or 'rank'")
     n = counts.sum()
     c = np.cumsum(p) / p.sum()
     edges = np.searchsorted(c, np.arange(1, bins) / bins, side="left")
@@ -973,3 +980,101 @@ def generate_autoregressive(t: Qwen3, prompt, max_new_tokens, sp=SamplingParams(
         tok = pick(z[-1])
         out.append(tok)
     return out
+
+
+# ----------------------------------------------------------------------------- forced draft trees
+
+
+def parse_template(line: str) -> list[tuple[int, int, int]]:
+    """One draft-tree template: nodes 1..N-1 as "parent:offset:delta" (see forced_tree_run)."""
+    nodes = []
+    for item in line.split():
+        p, o, d = (int(x) for x in item.split(":"))
+        if not 0 <= p <= len(nodes):
+            raise ValueError(f"template node parent {p} must precede the node")
+        nodes.append((p, o, d))
+    return nodes
+
+
+def forced_tree_run(t: Qwen3, d: Drafter, prompt, max_new: int, templates: list[str]) -> dict:
+    """Oracle-drafter rounds over given draft trees, restating the `forced` mode of
+    oracle/ref_driver.cpp, which runs the reference's own draft / verify / update
+    (src/core/spec.cpp:86-233) with the drafts taken from templates.
+
+    A = the greedy continuation (generate_autoregressive). Round r instantiates template
+    r mod len(templates) at e = tokens emitted so far: node i gets token A[e + offset_i] plus
+    delta_i (mod vocab) under its parent. The drafter runs over every internal node level by level
+    (positions n-1+depth, committed entries + drafted ancestors + itself visible,
+    spec.cpp:158-171); the root's and every drafted node's head argmax and its logit are
+    recorded. The target verifies with positions n+depth and the tree mask (a chain: causal),
+    verify_tree_greedy picks the path, the cache keeps it and the drafter is updated on the
+    accepted rows."""
+    tpl = [parse_template(x) for x in templates]
+    max_off = max(o for tp in tpl for _, o, _ in tp)
+    A = generate_autoregressive(t, prompt, max_new + max_off + 2, stop_on_eos=False)
+    tc, dc = t.make_cache(), d.make_cache()
+    z, feats = t.forward(prompt, tc, logits_from=len(prompt) - 1)
+    first = argmax(z[-1])
+    hid, out = d.forward(list(prompt[1:]) + [first], d.fuse(feats), dc)
+    root_out, root_fb = out[-1:].copy(), d.feedback(hid[-1:], out[-1:]).copy()
+    emitted, rounds, accepted = [first], [], 0
+    r = 0
+    while len(emitted) < max_new:
+        n, e = tc.size(), len(emitted)
+        tokens, parents, depth = [emitted[-1]], [-1], [0]
+        for p, o, dl in tpl[r % len(tpl)]:
+            tokens.append((A[e + o] + dl) % t.vocab)
+            parents.append(p)
+            depth.append(depth[p] + 1)
+        N = len(tokens)
+        children = [[v for v in range(N) if parents[v] == u] for u in range(N)]
+        outs, fbs, cidx = {0: root_out}, {0: root_fb}, {0: n - 1}
+        prop, pz = [-1] * N, [0.0] * N
+
+        def propose(v):
+            zz = d.logits(outs[v])[0]
+            prop[v] = d.token_ids(argmax(zz))
+            pz[v] = float(zz[argmax(zz)])
+
+        propose(0)
+        base, drafted = dc.size(), 0
+        for dep in range(1, max(depth)):
+            level = [v for v in range(1, N) if depth[v] == dep and children[v]]
+            if not level:
+                break
+            m = len(level)
+            mask = np.zeros((m, base + drafted + m), np.uint8)
+            lo = 0 if not d.window else max(0, base - 1 + dep - d.window + 1)
+            for i, v in enumerate(level):
+                mask[i, lo:base] = 1
+                u = parents[v]
+                while u > 0:
+                    mask[i, cidx[u]] = 1
+                    u = parents[u]
+                mask[i, base + drafted + i] = 1
+            fb = np.concatenate([fbs[parents[v]] for v in level], axis=0)
+            h2, o2 = d.forward([tokens[v] for v in level], fb, dc, positions=[n - 1 + dep] * m, mask=mask)
+            f2 = d.feedback(h2, o2)
+            for i, v in enumerate(level):
+                outs[v], fbs[v], cidx[v] = o2[i : i + 1], f2[i : i + 1], base + drafted + i
+                propose(v)
+            drafted += m
+        dc.trim_to(base)
+        tree = DraftTree(tokens, parents, depth)
+        if tree.is_chain():
+            zt, feats = t.forward(tokens, tc)
+        else:
+            zt, feats = t.forward(tokens, tc, positions=[n + x for x in depth],
+                                  mask=tree_attention_mask(tree, n).astype(np.uint8))
+        path, nxt = verify_tree_greedy([argmax(row) for row in zt], tree)
+        keep = [0] + path
+        tc.compact(n, keep)
+        acc = [tokens[v] for v in path] + [nxt]
+        hid, out = d.forward(acc, d.fuse([f[keep] for f in feats]), dc)
+        root_out, root_fb = out[-1:].copy(), d.feedback(hid[-1:], out[-1:]).copy()
+        accepted += len(path)
+        rounds.append({"tokens": tokens, "parents": parents, "path": path, "next": nxt, "proposals": prop,
+                       "proposal_logits": pz, "n": tc.size(), "drafter_len": dc.size()})
+        emitted.extend(acc[: max_new - len(emitted)])
+        r += 1
+    return {"first": first, "ar": A, "rounds": rounds, "tokens": emitted, "accepted": accepted}

@@ -14,6 +14,16 @@ Run in the build container (needs the reference tree and oracle/_ref built by
   functions used here are pure numpy) on seeded cases, driven by the Philox uniform
   tape of oracle/wc_oracle.py. Inputs and outputs are stored so the tests can
   replay them against the oracle and the CUDA acceptance kernel.
+* c1u_forced.json: the reference C++ core in oracle-drafter mode (`wc_ref_driver forced`) on
+  the C1u pair: chains of 4 and 6 with seeded accept lengths and draft trees whose accepted
+  paths branch, per round the tree, accepted path, next token, the drafter's own head
+  proposals (root and every drafted node) and the cache lengths
+  (`python tests/golden/make_golden.py forced`).
+* c3_reference.json: the reference C++ core on the full 28-layer C3 target (Qwen3-1.7B
+  architecture; the bench's seeded bf16 weights, read by the reference in fp32): its greedy
+  continuation of an 8-token prompt and, teacher-forced on it, every row's argmax, top-8
+  logits and the logits at 256 seeded ids (`python tests/golden/make_golden.py c3`; needs a
+  CUDA device, because the weights are the bench's seeded device stream, and oracle/_ref).
 * vocab.json: the reference's top_ids / coverage (python/woodcock/vocab.py:35-52) on
   seeded counts with ties and forced ids (`python tests/golden/make_golden.py vocab`).
 """
@@ -22,6 +32,7 @@ from __future__ import annotations
 
 import dataclasses
 import json
+import os
 import subprocess
 import sys
 import tempfile
@@ -32,7 +43,7 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parents[1]
-REF = Path("/root/reference")
+REF = Path(os.environ.get("WC_REFERENCE_DIR", "/root/reference"))
 sys.path.insert(0, str(REPO))
 sys.path.insert(0, str(REPO / "oracle"))
 
@@ -69,6 +80,61 @@ def model_fixture(name: str, tie: bool) -> dict:
             sd = _run("gen", *common, "--drafter", str(dd), "--max", str(N_NEW), "--policy", pol)
             out[f"spec_{pol}"] = {"tokens": sd["tokens"], "rounds": sd["rounds"], "accepted": sd["accepted"]}
     return out
+
+
+def chain_template(K: int, accept: int) -> str:
+    """K chained drafts; draft accept+1 is corrupted (none when accept == K)."""
+    return " ".join(f"{j}:{j}:{1 if j == accept else 0}" for j in range(K))
+
+
+# Forced draft trees (parent:offset:delta per node, node 0 = the root): the second root child
+# accepted with a matching node under the rejected first child; both children of an accepted
+# node rejected; nothing accepted; a depth-3 path with a side branch.
+FORCED_TREES = ["0:0:1 0:0:0 2:1:0 1:1:0 3:2:1 3:2:0", "0:0:0 1:1:1 1:1:2 3:2:0", "0:0:2 0:0:1 1:1:0",
+                "0:0:0 1:1:0 2:2:0 3:3:1 2:2:3"]
+FORCED_SETS = {"chain4": [chain_template(4, a) for a in (2, 4, 0, 3, 1)],
+               "chain6": [chain_template(6, a) for a in (6, 1, 3, 5, 0)],
+               "tree": FORCED_TREES}
+FORCED_NEW = 96
+
+
+def forced_fixture() -> dict:
+    ts = dataclasses.replace(syn.TINY_TARGET, tie_embeddings=False)
+    out = {"config": "c1u", "taps": [1, 2, 3], "max_new": FORCED_NEW}
+    with tempfile.TemporaryDirectory() as tmp:
+        td, dd, _, _ = syn.make_pair(tmp, "c1", seed=0, dtype="F32", target_spec=ts)
+        prompt = syn.prompt_ids(64, ts.vocab, seed=0)
+        out["prompt"] = prompt
+        for name, tpl in FORCED_SETS.items():
+            f = Path(tmp) / f"{name}.txt"
+            f.write_text("\n".join(tpl) + "\n")
+            r = _run("forced", "--target", str(td), "--drafter", str(dd), "--ids", ",".join(map(str, prompt)),
+                     "--taps", "1,2,3", "--max", str(FORCED_NEW), "--trees", str(f))
+            r["templates"] = tpl
+            for key in ("round_s", "t_prefill"):  # timings: not part of the fixture
+                r.pop(key, None)
+            out[name] = r
+    return out
+
+
+C3_PROMPT, C3_NEW, C3_SAMPLE = 8, 16, 256
+
+
+def c3_fixture() -> dict:
+    from woodcock_b200 import synthetic as syn
+
+    ts = syn.Q17_TARGET
+    prompt = syn.prompt_ids(C3_PROMPT, ts.vocab, seed=3)
+    sample = np.sort(np.random.default_rng(4).choice(ts.vocab, C3_SAMPLE, replace=False)).tolist()
+    with tempfile.TemporaryDirectory() as tmp:
+        td = syn.write_device_model(Path(tmp) / "target", ts.hf_config(), syn.target_tensor_specs(ts), 0)
+        common = ["--target", str(td), "--taps", "2,14,26"]
+        ar = _run("gen", "--ar", *common, "--ids", ",".join(map(str, prompt)), "--max", str(C3_NEW), "--no-eos")
+        seq = prompt + ar["tokens"][: C3_NEW - 1]
+        fw = _run("forward", *common, "--ids", ",".join(map(str, seq)), "--rows-from", str(C3_PROMPT - 1),
+                  "--top", "8", "--sample-ids", ",".join(map(str, sample)))
+    return {"config": "c3 target (Qwen3-1.7B architecture, 28 layers), device weight stream seed 0",
+            "prompt": prompt, "ar_tokens": ar["tokens"], "sample_ids": sample, "rows": fw["rows"]}
 
 
 def _reference_sampling():
@@ -176,6 +242,12 @@ def main():
     if not only or "sampling" in only:
         (HERE / "sampling.json").write_text(json.dumps(sampling_fixture()))
         print("wrote sampling")
+    if not only or "forced" in only:
+        (HERE / "c1u_forced.json").write_text(json.dumps(forced_fixture()))
+        print("wrote c1u_forced")
+    if "c3" in only:  # needs a CUDA device: not part of the default run
+        (HERE / "c3_reference.json").write_text(json.dumps(c3_fixture()))
+        print("wrote c3_reference")
     if not only or "vocab" in only:
         (HERE / "vocab.json").write_text(json.dumps(vocab_fixture()))
         print("wrote vocab")

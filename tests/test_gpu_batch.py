@@ -183,18 +183,3 @@ def test_prompt_forward_matches_decode_path(bf16_target, n):
         for a, b_ in zip(cb.read(l, n), ca.read(l, n)):
             assert (a - b_).abs().max().item() <= KV_TOL * b_.abs().max().item(), l
 
-
-def test_tcgen05_tree_attention_in_a_child_process():
-    """The opt-in tcgen05 tree attention (WC_TA_TC=1: S and O in TMEM, V as the MN-major
-    operand) passes the same single-request parity; contexts read the switch at first use."""
-    import os
-    import subprocess
-    import sys
-
-    from conftest import REPO
-
-    env = dict(os.environ, WC_TA_TC="1")
-    r = subprocess.run([sys.executable, "-m", "pytest", "-q", "-x", "-m", "gpu", str(REPO / "tests" / "test_gpu_batch.py"),
-                        "-k", "verify_and_compaction"], env=env, capture_output=True, text=True, timeout=600,
-                       cwd=str(REPO))
-    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]

@@ -5,9 +5,11 @@ chain; sampling.py:39-55, 69-82, 143-203) and the autoregressive baseline (spec.
     oracle's (wc_oracle.gumbel_draw / sampled_chain_accept) on that round's own logits with
     the same Philox counters; the prefill's first token likewise.
 (b) Law: the first emitted token of rounds replayed from one state follows
-    p_0 = softmax(z_0 / T): Pearson chi-square of 1e5 draws in 1000 equal-mass bins must not
-    reject (p > 1e-3), while the oracle with a planted mistake (rejections drawn from p
-    instead of the residual) on the same p and q must be rejected (p < 1e-6). The draft
+    p_0 = softmax(z_0 / T): Pearson chi-square of 1e5 draws in 1000 equal-mass bins, the bins
+    taken over consecutive token ids and, separately, over tokens in decreasing order of p (a
+    bias that follows the logit collects in the first or last rank bins), must not reject
+    (p > 1e-3), while the oracle with a planted mistake (rejections drawn from p instead of the
+    residual) on the same p and q must be rejected under both binnings (p < 1e-6). The draft
     vocabulary is restricted, so q is zero on most tokens and those are reached only through
     the residual.
 (c) The autoregressive baseline's sampled first token follows p over many seeds, and a seed
@@ -102,8 +104,9 @@ def test_sampled_first_token_law_chi_square(pair, prompt64):
     x = (z0 / np.float32(T_LAW)).astype(np.float64)
     p = np.exp(x - x.max())
     p /= p.sum()
-    stat, dof, pval = O.chi2_equal_mass(counts, p)
-    assert pval > 1e-3, (stat, dof, pval)
+    for order in ("id", "rank"):
+        stat, dof, pval = O.chi2_equal_mass(counts, p, order=order)
+        assert pval > 1e-3, (order, stat, dof, pval)
 
     # the same test on the oracle's draws from this p and q: correct rule passes, the planted
     # mistake (no residual) fails
@@ -118,8 +121,9 @@ def test_sampled_first_token_law_chi_square(pair, prompt64):
     r = np.maximum(p - q, 0.0)
     good = np.where(accept, drafts, rng.choice(V, N_LAW, p=r / r.sum()))
     bad = np.where(accept, drafts, rng.choice(V, N_LAW, p=p))
-    assert O.chi2_equal_mass(np.bincount(good, minlength=V).astype(float), p)[2] > 1e-3
-    assert O.chi2_equal_mass(np.bincount(bad, minlength=V).astype(float), p)[2] < 1e-6
+    for order in ("id", "rank"):
+        assert O.chi2_equal_mass(np.bincount(good, minlength=V).astype(float), p, order=order)[2] > 1e-3
+        assert O.chi2_equal_mass(np.bincount(bad, minlength=V).astype(float), p, order=order)[2] < 1e-6
 
 
 def test_sampled_generate_runs_and_reproduces(pair, prompt64):
@@ -155,7 +159,8 @@ def test_sampled_autoregressive_first_token_law(pair, prompt64):
         if seed < 4:
             assert out[0] == O.gumbel_draw(z, T_LAW, seed, 0, 0)
         counts[out[0]] += 1
-    assert O.chi2_equal_mass(counts, p, bins=60)[2] > 1e-3
+    for order in ("id", "rank"):
+        assert O.chi2_equal_mass(counts, p, bins=60, order=order)[2] > 1e-3
     a, _ = generate_autoregressive(t, prompt, 24, SamplingParams(temperature=T_LAW, seed=5), stop_on_eos=False)
     b, _ = generate_autoregressive(t, prompt, 24, SamplingParams(temperature=T_LAW, seed=5), stop_on_eos=False)
     assert a == b
@@ -203,8 +208,9 @@ def test_warped_first_token_law_chi_square(pair, prompt64):
             z0 = dec.round_logits(k)["zt"][0].copy()
     p = O.warped_probs(z0, T_LAW, top_k, top_p)
     assert counts[p == 0].sum() == 0  # nothing outside the kept set is ever emitted
-    stat, dof, pval = O.chi2_equal_mass(counts, p, bins=1000)
-    assert dof >= 5 and pval > 1e-3, (stat, dof, pval)
+    for order in ("id", "rank"):
+        stat, dof, pval = O.chi2_equal_mass(counts, p, bins=1000, order=order)
+        assert dof >= 5 and pval > 1e-3, (order, stat, dof, pval)
 
 
 def test_invalid_warping_is_refused(pair, prompt64):

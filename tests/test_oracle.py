@@ -64,6 +64,28 @@ def test_oracle_forced_drafts_accept_and_stay_exact(tiny_models, prompt64):
 
 # ------------------------------------------------------------------ acceptance vs the reference's Python functions
 
+@pytest.mark.parametrize("name", ["chain4", "chain6", "tree"])
+def test_oracle_forced_rounds_match_reference(name, golden, tiny_models, prompt64):
+    """tests/golden/c1u_forced.json was made by the reference's C++ core in oracle-drafter mode
+    (drafts forced from its own greedy continuation, partially accepted; trees with branching
+    accepted paths). The oracle restatement reproduces every round: tree, accepted path, next
+    token, the drafter's own proposals and their logits, and both cache lengths."""
+    g = golden("c1u_forced")
+    ref = g[name]
+    assert g["prompt"] == prompt64
+    td, dd, _, _ = tiny_models["c1u"]
+    t, d = O.Qwen3.load(td, taps=g["taps"]), O.Drafter.load(dd)
+    r = O.forced_tree_run(t, d, prompt64, g["max_new"], ref["templates"])
+    assert r["tokens"] == ref["tokens"] == ref["ar"][: g["max_new"]]
+    assert r["accepted"] == ref["accepted"] and ref["accepted"] >= 50
+    assert len(r["rounds"]) == len(ref["rounds"])
+    for a, b in zip(r["rounds"], ref["rounds"]):
+        for key in ("tokens", "parents", "path", "next", "proposals", "n", "drafter_len"):
+            assert a[key] == b[key], key
+        np.testing.assert_allclose(a["proposal_logits"], b["proposal_logits"], rtol=0, atol=2e-5)
+    assert any(len(x["path"]) not in (0, len(x["tokens"]) - 1) for x in ref["rounds"])  # partial acceptance
+
+
 def test_oracle_chain_stochastic_matches_reference(golden):
     for c in golden("sampling")["chain"]:
         tape = O.Tape(c["seed"])

@@ -133,6 +133,7 @@ SIGNATURES = {
     "wc_decoder_save_state": (S, [P]),
     "wc_decoder_restore_state": (S, [P]),
     "wc_decoder_round_logits": (S, [P, C.c_int, P, P, I32P, C.POINTER(C.c_uint64)]),
+    "wc_decoder_draft_proposals": (S, [P, C.c_int, I32P, P]),
 }
 
 _lib = None

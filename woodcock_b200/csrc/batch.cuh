@@ -843,299 +843,6 @@ __global__ void __launch_bounds__(TA_THREADS, 2) tree_attention_kernel(__grid_co
   }
 }
 
-// ---------------------------------------------------------------------------- tree attention, tcgen05
-// The same contract as tree_attention_kernel (tree mode), with both products on the 5th-gen
-// tensor cores: S = Q K^T (M 128 query rows, the 64 real ones padded with zeros; N 64 keys;
-// K 128 dims) into one of two 64-column TMEM buffers, one softmax row per thread read with
-// tcgen05.ld, P written as a bf16 K-major 128B-swizzled tile, O += P V (N 128 dims) into a
-// 128-column TMEM accumulator with V as the MN-major operand straight from its TMA tile. A
-// row's O is rescaled only when its running max grows by more than 2^8 (otherwise P uses the
-// stale max; the final 1 / l uses the same one, so the result is exact). Warp 0: TMA, warp
-// 1: MMA issue + TMEM owner, warps 2-5: softmax and the output.
-constexpr int TAT_THREADS = 192;
-constexpr int TAT_STAGES = 4;
-constexpr int TAT_KT = 64;                                  // keys per tile
-constexpr int TAT_Q_BYTES = 2 * 128 * 128;                   // 2 atom blocks of [128 rows x 64 dims]
-constexpr int TAT_KV_BYTES = 2 * 2 * TAT_KT * 128;           // K, V: 2 atom blocks of [64 keys x 64 dims]
-constexpr int TAT_P_BYTES = 2 * 128 * 128;                   // 2 buffers of [128 rows x 64 keys]
-constexpr size_t tree_attn_tc_smem() {
-  return 1024 + TAT_Q_BYTES + TAT_P_BYTES + size_t(TAT_STAGES) * TAT_KV_BYTES + 256 + TA_MAXN * 8;
-}
-
-// MN-major 128B-swizzled operand: rows of 128 bytes are K indices (8-row groups 1024 bytes
-// apart = stride byte offset), 64-element MN blocks `mn_block` bytes apart (leading byte offset).
-__device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t saddr, uint32_t mn_block) {
-  return uint64_t((saddr & 0x3FFFFu) >> 4) | (uint64_t(mn_block >> 4) << 16) | (uint64_t(1024 >> 4) << 32) |
-         (uint64_t(1) << 46) | (uint64_t(2) << 61);
-}
-// kind::f16 instruction descriptor, fp32 accumulator, bf16 operands, M 128, N, B major
-__host__ __device__ constexpr uint32_t umma_idesc_bf16_mn(int N, int b_mn_major) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | (uint32_t(b_mn_major) << 16) | (uint32_t(N >> 3) << 17) |
-         (uint32_t(128 >> 4) << 24);
-}
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float (&v)[16]) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};\n" ::"r"(
-          taddr),
-      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
-      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
-      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
-      "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
-      "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
-      : "memory");
-}
-__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory"); }
-
-__global__ void __launch_bounds__(TAT_THREADS, 1)
-    tree_attention_tc_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
-                             const __grid_constant__ TreeAttnParams p) {
-  constexpr int D = 128;
-  extern __shared__ unsigned char tat_raw[];
-  unsigned char* sm = tat_raw + ((1024u - (smem_addr(tat_raw) & 1023u)) & 1023u);
-  unsigned char* qs = sm;                                    // [2 blocks][128 rows][128 B]
-  unsigned char* ps = qs + TAT_Q_BYTES;                      // [2][128 rows][128 B]
-  unsigned char* kvs = ps + TAT_P_BYTES;                     // [stage][K blocks 2 | V blocks 2][64][128 B]
-  uint64_t* kv_full = reinterpret_cast<uint64_t*>(kvs + TAT_STAGES * TAT_KV_BYTES);
-  uint64_t* kv_empty = kv_full + TAT_STAGES;
-  uint64_t* s_full = kv_empty + TAT_STAGES;  // [2]
-  uint64_t* s_free = s_full + 2;             // [2]
-  uint64_t* p_full = s_free + 2;  // [2]
-  uint64_t* o_done = p_full + 2;  // [2]: P V of tile t done (buffer t & 1 free, O updated)
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(o_done + 2);
-  unsigned long long* anc = reinterpret_cast<unsigned long long*>(kvs + TAT_STAGES * TAT_KV_BYTES + 256);
-  const int r = blockIdx.x, hk = blockIdx.y;
-  const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
-  const int rep = p.Hq / p.Hk, R = p.nodes * rep;
-
-  if (tid == 0) {
-    for (int s = 0; s < TAT_STAGES; ++s) {
-      mbar_init(kv_full + s, 1);
-      mbar_init(kv_empty + s, 1);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(s_full + b, 1);
-      mbar_init(s_free + b, 4);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(p_full + b, 4);
-      mbar_init(o_done + b, 1);
-    }
-    mbar_fence_init();
-  }
-  if (warp == 1) {  // S buffers at columns 0 / 64, O at 128
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_addr(tslot)),
-                 "r"(256u)
-                 : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::: "memory");
-  }
-  pdl_launch_dependents();
-  pdl_wait();
-  const int n = p.lens[r];
-  const int total = n + p.nodes;
-  const int ntiles = (total + TAT_KT - 1) / TAT_KT;
-  // queries: 128-row K-major tile (rows >= R zero); row rho = node * rep + j
-  for (int c = tid; c < 128 * 16; c += TAT_THREADS) {
-    const int row = c / 16, chunk = c % 16, blk = chunk / 8, cc = chunk % 8;
-    unsigned char* dst = qs + blk * 128 * 128 + row * 128 + ((cc ^ (row & 7)) * 16);
-    if (row < R) {
-      const uint16_t* src = p.q + (size_t(r * p.nodes + row / rep) * p.Hq + hk * rep + row % rep) * D + chunk * 8;
-      cp_async16(dst, src, 16);
-    } else {
-      *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
-    }
-  }
-  cp_async_commit();
-  if (tid == 0) {
-    bool bad = false;
-    for (int i = 0; i < p.nodes; ++i) {
-      const int par = p.parents[size_t(r) * p.nodes + i];
-      if (i == 0 ? par >= 0 : (par < 0 || par >= i)) bad = true;
-      anc[i] = (1ull << i) | ((i > 0 && par >= 0 && par < i) ? anc[par] : 0ull);
-    }
-    if (bad) raise_error(p.err, kErrTree);
-  }
-  cp_async_wait<0>();
-  fence_proxy_async_smem();  // queries written by the generic proxy, read by tcgen05.mma
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tslot;
-  const int row0 = (r * p.Hk + hk) * p.cap;  // first arena row of this (request, head)
-
-  if (warp == 0) {
-    if (lane == 0) {  // ---- TMA: K and V tiles (two 64-dim blocks each)
-      for (int t = 0; t < ntiles; ++t) {
-        const int s = t % TAT_STAGES;
-        if (t >= TAT_STAGES && !mbar_wait(kv_empty + s, ((t / TAT_STAGES) - 1) & 1)) {
-          raise_error(p.err, kErrTimeout);
-          break;
-        }
-        unsigned char* st = kvs + s * TAT_KV_BYTES;
-        mbar_arrive_expect_tx(kv_full + s, TAT_KV_BYTES);
-        const int y = row0 + t * TAT_KT;
-        tma_load_2d(st, &tk, 0, y, kv_full + s);
-        tma_load_2d(st + TAT_KT * 128, &tk, 64, y, kv_full + s);
-        tma_load_2d(st + 2 * TAT_KT * 128, &tv, 0, y, kv_full + s);
-        tma_load_2d(st + 3 * TAT_KT * 128, &tv, 64, y, kv_full + s);
-      }
-    }
-  } else if (warp == 1) {
-    if (lane == 0) {  // ---- MMA issuer
-      constexpr uint32_t id_s = umma_idesc_bf16_mn(TAT_KT, 0), id_o = umma_idesc_bf16_mn(D, 1);
-      const uint32_t qa = smem_addr(qs), pa = smem_addr(ps);
-      bool ok = true;
-      auto issue_s = [&](int t) {  // S(t) = Q K(t)^T into buffer t & 1
-        const int s = t % TAT_STAGES, b = t & 1;
-        if (!mbar_wait(kv_full + s, (t / TAT_STAGES) & 1)) {
-          raise_error(p.err, kErrTimeout);
-          ok = false;
-          return;
-        }
-        if (t >= 2 && !mbar_wait(s_free + b, ((t - 2) / 2) & 1)) {
-          raise_error(p.err, kErrTimeout);
-          ok = false;
-          return;
-        }
-        tc_fence_after();
-        const uint32_t ka = smem_addr(kvs + s * TAT_KV_BYTES);
-#pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t off = (kk % 4) * 32;  // 16 dims inside the 64-dim swizzle row
-          const uint32_t adesc_a = qa + (kk / 4) * (128 * 128) + off;
-          const uint32_t adesc_b = ka + (kk / 4) * (TAT_KT * 128) + off;
-          umma_bf16(tmem + uint32_t(b * 64), umma_desc_sw128(adesc_a), umma_desc_sw128(adesc_b), id_s, kk != 0);
-        }
-        umma_commit(s_full + b);
-      };
-      issue_s(0);
-      for (int t = 0; t < ntiles && ok; ++t) {
-        if (t + 1 < ntiles) issue_s(t + 1);
-        if (!ok) break;
-        if (!mbar_wait(p_full + (t & 1), (t / 2) & 1)) {  // P(t) written, O rescaled if needed
-          raise_error(p.err, kErrTimeout);
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const int s = t % TAT_STAGES;
-        const uint32_t va = smem_addr(kvs + s * TAT_KV_BYTES + 2 * TAT_KT * 128);
-        const uint32_t pb = pa + uint32_t((t & 1) * 128 * 128);
-#pragma unroll
-        for (int kk = 0; kk < TAT_KT / 16; ++kk)  // 16 keys per step: K-major P, MN-major V
-          umma_bf16(tmem + 128u, umma_desc_sw128(pb + kk * 32), umma_desc_sw128_mn(va + kk * 16 * 128, TAT_KT * 128),
-                    id_o, (t | kk) != 0);
-        umma_commit(o_done + (t & 1));
-        umma_commit(kv_empty + s);
-      }
-      if (!ok) {  // let every waiter finish: the remaining phases complete once prior MMAs are done
-        umma_commit(s_full + 0);
-        umma_commit(s_full + 1);
-        umma_commit(o_done + 0);
-        umma_commit(o_done + 1);
-      }
-    }
-  } else {  // ---- softmax warps: thread = row 32 (w % 4) + lane
-    const int qd = warp & 3, row = qd * 32 + lane;
-    const uint32_t lane_base = tmem + (uint32_t(qd * 32) << 16);
-    const bool valid = row < R;
-    const unsigned long long my_anc = valid ? anc[row / rep] : 0ull;
-    const float sl2 = p.scale * 1.4426950408889634f;
-    float m_used = -INFINITY, l = 0.f;
-    for (int t = 0; t < ntiles; ++t) {
-      const int b = t & 1;
-      if (!mbar_wait(s_full + b, (t / 2) & 1)) raise_error(p.err, kErrTimeout);
-      tc_fence_after();
-      float sv[TAT_KT];
-#pragma unroll
-      for (int c = 0; c < TAT_KT; c += 16) {
-        float v[16];
-        tmem_ld16(lane_base + uint32_t(b * 64 + c), v);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) sv[c + i] = v[i];
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(s_free + b);
-      // visibility and the running max
-      const int p0 = t * TAT_KT;
-      float mt = -INFINITY;
-#pragma unroll
-      for (int j = 0; j < TAT_KT; ++j) {
-        const int pos = p0 + j;
-        const bool vis = valid && (pos < n || (pos < total && ((my_anc >> (pos - n)) & 1ull)));
-        sv[j] = vis ? sv[j] * sl2 : -INFINITY;
-        mt = fmaxf(mt, sv[j]);
-      }
-      // buffer t & 1 was read by P V(t - 2): wait for it before overwriting
-      if (t >= 2 && !mbar_wait(o_done + (t & 1), ((t - 2) / 2) & 1)) raise_error(p.err, kErrTimeout);
-      const bool rescale = mt > m_used + 8.f;
-      if (rescale && t >= 1) {  // O is read below: every earlier P V must be done (P V(t - 1))
-        if (!mbar_wait(o_done + ((t - 1) & 1), ((t - 1) / 2) & 1)) raise_error(p.err, kErrTimeout);
-      }
-      tc_fence_after();
-      if (rescale) {  // rescale O (and l) to the new max
-        const float alpha = m_used == -INFINITY ? 0.f : exp2f(m_used - mt);
-        if (t > 0) {
-#pragma unroll 1
-          for (int c = 0; c < D; c += 16) {
-            float v[16];
-            tmem_ld16(lane_base + 128u + uint32_t(c), v);
-#pragma unroll
-            for (int i = 0; i < 16; ++i) v[i] *= alpha;
-            tmem_st16(lane_base + 128u + uint32_t(c), v);
-          }
-          asm volatile("tcgen05.wait::st.sync.aligned;\n" ::: "memory");
-        }
-        l *= alpha;
-        m_used = mt;
-      }
-      // P = exp2(S - m_used) as bf16, one 128-byte row of 8 swizzled chunks
-      float ls = 0.f;
-      unsigned char* prow = ps + (t & 1) * 128 * 128 + row * 128;
-#pragma unroll
-      for (int cc = 0; cc < 8; ++cc) {
-        uint32_t w[4];
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          const float a = sv[cc * 8 + 2 * h] == -INFINITY ? 0.f : exp2f(sv[cc * 8 + 2 * h] - m_used);
-          const float b2 = sv[cc * 8 + 2 * h + 1] == -INFINITY ? 0.f : exp2f(sv[cc * 8 + 2 * h + 1] - m_used);
-          ls += a + b2;
-          w[h] = pack2(f32_to_bf16_bits(a), f32_to_bf16_bits(b2));
-        }
-        *reinterpret_cast<uint4*>(prow + ((cc ^ (row & 7)) * 16)) = make_uint4(w[0], w[1], w[2], w[3]);
-      }
-      l += ls;
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(p_full + (t & 1));
-    }
-    if (ntiles > 0 && !mbar_wait(o_done + ((ntiles - 1) & 1), ((ntiles - 1) / 2) & 1)) raise_error(p.err, kErrTimeout);
-    tc_fence_after();
-    const float inv = l > 0.f ? 1.f / l : 0.f;
-    uint16_t* dst = valid ? p.out + (size_t(r * p.nodes + row / rep) * p.Hq + hk * rep + row % rep) * D : nullptr;
-#pragma unroll 1
-    for (int c = 0; c < D; c += 16) {
-      float v[16];
-      tmem_ld16(lane_base + 128u + uint32_t(c), v);
-      if (dst) {
-        uint32_t o[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) o[i] = pack2(f32_to_bf16_bits(v[2 * i] * inv), f32_to_bf16_bits(v[2 * i + 1] * inv));
-        uint4* d4 = reinterpret_cast<uint4*>(dst + c);
-        d4[0] = make_uint4(o[0], o[1], o[2], o[3]);
-        d4[1] = make_uint4(o[4], o[5], o[6], o[7]);
-      }
-    }
-  }
-  tc_fence_before();
-  __syncthreads();
-  if (warp == 1) {
-    tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(256u) : "memory");
-  }
-}
-
 // Merges the slices' partial states of each (request, KV head) in slice order.
 template <int D>
 __global__ void __launch_bounds__(128) tree_attn_merge_kernel(__grid_constant__ const TreeAttnParams p) {

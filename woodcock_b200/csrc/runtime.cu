@@ -31,7 +31,6 @@
 #include "gemv.cuh"
 #include "host_io.h"
 #include "misc.cuh"
-#include "stack.cuh"
 
 using namespace wc;
 namespace fs = std::filesystem;
@@ -68,7 +67,7 @@ struct RopeTable {
 };
 
 // CUDA-event marks around kernels of a profiled round (a separate graph from the timed one).
-enum ProfKind { PK_QKV, PK_ATTN, PK_O, PK_GU, PK_DOWN, PK_HEAD, PK_DRAFT_HEAD, PK_DRAFT_LAYER, PK_STACK, PK_COUNT };
+enum ProfKind { PK_QKV, PK_ATTN, PK_O, PK_GU, PK_DOWN, PK_HEAD, PK_DRAFT_HEAD, PK_DRAFT_LAYER, PK_COUNT };
 constexpr int PK_SLOTS = 16;  // entries of the profile arrays in the C ABI
 
 struct Profiler {
@@ -119,12 +118,8 @@ struct wc_ctx {
   size_t gv_partial_n = 0;               // floats
   int* gv_counters = nullptr;            // split-K arrival counters (zero between launches)
   int gv_counters_n = 0;
-  bool stack = false;                    // persistent layer-stack kernel for the verify pass (opt-in: WC_STACK=1)
-  int occ_stack = 0;                     // its blocks per SM (0: unavailable)
-  float* sk_part = nullptr;              // its attention partial states
   void* pw_scratch = nullptr;            // wc_probs_from_logits: parameters + row thresholds
   int pw_rows = 0;
-  int* sk_counters = nullptr;            // its per-head arrival counters (zero between launches)
   uint32_t* lin_xf = nullptr;  // input fragments of the ops-API linear
   int lin_xf_k = 0;
   bool lin_xf_bf16 = false;
@@ -668,18 +663,6 @@ void launch_attention(wc_ctx* ctx, AttnParams p) {
   // tensor-core paths: bf16 cache, rule-based visibility, new rows appended by the kernel
   const bool tc_ok = !p.q_ready && !p.mask_full && p.kv_dtype == WC_BF16 && p.write_cache &&
                      (p.D == 128 || p.D == 64) && p.L_max * rep <= AM_MAXR && p.stride_p == p.D;
-  if (tc_ok && ctx->attn_mode == 3 && p.D == SK_D && p.L_max <= SK_MAXL && p.L_max * rep <= SK_MAXR &&
-      p.Hk <= 16 && p.cap <= SK_MAXS * SK_NTILE * SK_BLK && !p.mask_full) {
-    AttnJob j;
-    std::memset(&j, 0, sizeof(j));
-    j.a = p;
-    j.part = ctx->sk_part;
-    j.counters = ctx->sk_counters;
-    j.S = SK_MAXS;
-    launch_ex(ctx, "attention_flat", attention_flat_kernel, dim3(p.Hk * SK_MAXS), dim3(SK_CTHREADS),
-              attention_flat_smem(), true, 1, j);
-    return;
-  }
   if (tc_ok && ctx->attn_mode == 2 && p.L_max <= AD_MAXL && p.L_max * rep <= AD_MAXR) {
     const bool mt2 = p.L_max * rep > 16;
     if (p.D == 128) {
@@ -753,20 +736,6 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
     ctx->gv_counters_n = 8192;
     ctx->gv_counters = static_cast<int*>(dalloc(sizeof(int) * ctx->gv_counters_n));
     CUDA_TRY(cudaMemset(ctx->gv_counters, 0, sizeof(int) * ctx->gv_counters_n));
-    if (const char* e = std::getenv("WC_STACK")) ctx->stack = std::atoi(e) != 0;
-    ctx->sk_part = static_cast<float*>(dalloc(sizeof(float) * 16 * SK_MAXS * SK_MAXR * (SK_D + 2)));
-    ctx->sk_counters = static_cast<int*>(dalloc(sizeof(int) * 64));
-    CUDA_TRY(cudaMemset(ctx->sk_counters, 0, sizeof(int) * 64));
-    CUDA_TRY(cudaFuncSetAttribute(stack_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(stack_smem())));
-    CUDA_TRY(cudaFuncSetAttribute(attention_flat_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                  int(attention_flat_smem())));
-    {
-      int occ_s = 0;
-      if (stack_smem() <= ctx->max_smem &&
-          cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ_s, stack_kernel, SK_THREADS, stack_smem()) == cudaSuccess)
-        ctx->occ_stack = occ_s;
-      cudaGetLastError();
-    }
     const int smax = int(ctx->max_smem);
     CUDA_TRY(cudaFuncSetAttribute(gemv_bf16_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(gemv_bf16_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
@@ -819,9 +788,7 @@ extern "C" void wc_ctx_destroy(wc_ctx* ctx) {
   dfree(ctx->d_err);
   dfree(ctx->gv_partial);
   dfree(ctx->gv_counters);
-  dfree(ctx->sk_part);
   dfree(ctx->pw_scratch);
-  dfree(ctx->sk_counters);
   dfree(ctx->pw);
   dfree(ctx->qw);
   dfree(ctx->lin_xf);
@@ -840,7 +807,6 @@ extern "C" wc_status wc_ctx_synchronize(wc_ctx* ctx) {
     if (e) {
       CUDA_TRY(cudaMemset(ctx->d_err, 0, sizeof(int)));
       CUDA_TRY(cudaMemset(ctx->gv_counters, 0, sizeof(int) * ctx->gv_counters_n));
-      CUDA_TRY(cudaMemset(ctx->sk_counters, 0, sizeof(int) * 64));
       fail(WC_ERR_DEVICE, "device error flag " + std::to_string(e));
     }
   });
@@ -1626,228 +1592,6 @@ XIn target_layers(wc_target* t, wc_kv* kv, const Rows& r, XIn in0, float* h, con
 XIn target_tap_stats(const wc_target* t, int f, const uint32_t* xf, int L_max) {
   const TLayer& Ly = t->layers[t->taps[f]];
   return XIn{xf, Ly.ss_d, gemv_parts(t->ctx, Ly.down, L_max)};
-}
-
-// ---- persistent layer stack (stack.cuh): the same layer program as target_layers, as jobs
-
-struct StackPlan {
-  bool ready = false;
-  Job* dev = nullptr;
-  int njobs = 0;
-  unsigned* bar = nullptr;
-  int last_down_parts = 0;
-  ~StackPlan() {
-    dfree(dev);
-    dfree(bar);
-  }
-};
-
-bool target_stack_ok(const wc_target* t, const Rows& r) {
-  const wc_ctx* ctx = t->ctx;
-  const auto& c = t->cfg;
-  return ctx->stack && ctx->occ_stack >= 1 && t->dtype == WC_BF16 && c.head_dim == SK_D && c.kv_heads <= 16 &&
-         r.L_max <= SK_MAXL && r.L_max * (c.heads / c.kv_heads) <= SK_MAXR && !r.mask_full && !r.positions &&
-         r.stable;
-}
-
-// GEMV job parameters for the stack grid (one CTA per SM, 8-row fragments)
-GemvParams stack_gemv(wc_ctx* ctx, const Lin& W, GemvParams p) {
-  const bool bf16 = W.dtype == WC_BF16;
-  if (!bf16 || p.L_max > 8) fail(WC_ERR_INVALID, "stack GEMV needs bf16 weights and <= 8 rows");
-  p.w = W.w;
-  p.N = W.N;
-  p.Np = W.Np;
-  p.Kp = W.Kp;
-  p.group = W.group;
-  if (!p.err) p.err = ctx->d_err;
-  if (p.nseg != W.nseg) fail(WC_ERR_INVALID, "GEMV input segments do not match the weight");
-  for (int i = 0; i < p.nseg; ++i)
-    if (p.seg[i].len != W.seg_len[i] || p.seg[i].lenp != xf_width(true, p.seg[i].len))
-      fail(WC_ERR_INVALID, "GEMV input width does not match the weight");
-  p.out_width = xf_width(true, W.N);
-  const int chs = SK_ACT_BYTES / GV_STAGE_BYTES;
-  const int nslab = W.Kp / GV_COLS, nunits = W.Np / (16 * W.group);
-  p.nkc = (nslab + chs - 1) / chs;
-  p.kc_slabs = (nslab + p.nkc - 1) / p.nkc;
-  p.gpk = std::max(1, std::min(nunits, ctx->num_sms / p.nkc));
-  if (p.nkc > 1) {
-    if (size_t(p.nkc) * (W.Np / 16) * 256 > ctx->gv_partial_n) fail(WC_ERR_UNSUPPORTED, "stack split-K scratch");
-    p.partial = ctx->gv_partial;
-  }
-  if (p.ss_out && nunits > max_parts(ctx)) fail(WC_ERR_INVALID, "GEMV output statistics above the buffer size");
-  return p;
-}
-
-// Builds and uploads the verify's job list (outside stream capture).
-void target_stack_build(wc_target* t, wc_kv* kv, const Rows& r, XIn in0, float* h, const TapOut* taps, int* err,
-                        StackPlan& plan) {
-  wc_ctx* ctx = t->ctx;
-  const auto& c = t->cfg;
-  const int H = c.hidden, D = c.head_dim, Hq = c.heads * D, Hkv = c.kv_heads * D, I = c.intermediate;
-  const int ld_qkv = Hq + 2 * Hkv;
-  std::vector<Job> jobs;
-  auto gemv_job = [&](const Lin& W, const GemvParams& p) {
-    Job j;
-    std::memset(&j, 0, sizeof(j));
-    j.type = JOB_GEMV;
-    j.g = stack_gemv(ctx, W, p);
-    jobs.push_back(j);
-    if (j.g.nkc > 1) {  // partials only; the finalize job runs the epilogue
-      jobs.back().g.ss_out = nullptr;
-      Job f = j;
-      f.type = JOB_FIN;
-      jobs.push_back(f);
-    }
-  };
-  const int S = std::max(1, std::min(SK_MAXS, ctx->num_sms / c.kv_heads));
-  XIn x = in0;
-  for (int li = 0; li < c.layers; ++li) {
-    const TLayer& Ly = t->layers[li];
-    {
-      GemvParams p = gemv_params();
-      p.L = r.L;
-      p.L_dev = r.L_dev;
-      p.L_max = r.L_max;
-      p.nseg = 1;
-      p.seg[0] = xs_frag(x, H, true, c.eps);
-      p.epi = EPI_STORE;
-      p.y = t->ws_qkv;
-      p.ldy = ld_qkv;
-      p.err = err;
-      gemv_job(Ly.qkv, p);
-    }
-    {
-      Job j;
-      std::memset(&j, 0, sizeof(j));
-      j.type = JOB_ATTN;
-      AttnParams& a = j.at.a;
-      a.qkv = t->ws_qkv;
-      a.ld_qkv = ld_qkv;
-      a.q_norm = Ly.q_norm;
-      a.k_norm = Ly.k_norm;
-      a.eps = c.eps;
-      a.rope = t->rope->ptr;
-      a.max_pos = t->rope->max_pos;
-      a.n_dev = r.n_dev;
-      a.n_add = r.n_add;
-      a.L = r.L;
-      a.L_dev = r.L_dev;
-      a.L_max = r.L_max;
-      a.Kc = kv->Kl(li);
-      a.Vc = kv->Vl(li);
-      a.kv_dtype = kv->dtype;
-      a.stride_h = (long long)kv->cap * D;
-      a.stride_p = D;
-      a.cap = kv->cap;
-      a.H = c.heads;
-      a.Hk = c.kv_heads;
-      a.D = D;
-      a.newmask = r.newmask;
-      a.scale = 1.f / std::sqrt(float(D));
-      a.xf_out = t->xf_att;
-      a.xf_width = xf_width(true, Hq);
-      a.write_cache = 1;
-      a.err = err;
-      j.at.part = ctx->sk_part;
-      j.at.counters = ctx->sk_counters;
-      j.at.S = S;
-      jobs.push_back(j);
-    }
-    {
-      GemvParams p = gemv_params();
-      p.L = r.L;
-      p.L_dev = r.L_dev;
-      p.L_max = r.L_max;
-      p.nseg = 1;
-      p.seg[0] = xs_frag(XIn{t->xf_att, nullptr, 0}, Hq, true);
-      p.epi = EPI_ADD;
-      p.y = h;
-      p.ldy = H;
-      p.base = h;
-      p.ldb = H;
-      p.nout = 1;
-      p.out[0] = XOut{t->xf_post, Ly.post_norm};
-      p.ss_out = Ly.ss_o;
-      p.err = err;
-      gemv_job(Ly.o, p);
-    }
-    {
-      GemvParams p = gemv_params();
-      p.L = r.L;
-      p.L_dev = r.L_dev;
-      p.L_max = r.L_max;
-      p.nseg = 1;
-      p.seg[0] = xs_frag(XIn{t->xf_post, Ly.ss_o, gemv_parts(ctx, Ly.o, r.L_max)}, H, true, c.eps);
-      p.epi = EPI_SWIGLU;
-      p.nout = 1;
-      p.out[0] = XOut{t->xf_act, nullptr};
-      p.err = err;
-      gemv_job(Ly.gu, p);
-    }
-    {
-      GemvParams p = gemv_params();
-      p.L = r.L;
-      p.L_dev = r.L_dev;
-      p.L_max = r.L_max;
-      p.nseg = 1;
-      p.seg[0] = xs_frag(XIn{t->xf_act, nullptr, 0}, I, true);
-      p.epi = EPI_ADD;
-      p.y = h;
-      p.ldy = H;
-      p.base = h;
-      p.ldb = H;
-      p.nout = 1;
-      p.out[0] = XOut{t->xf_in, li + 1 < c.layers ? t->layers[li + 1].in_norm : t->final_norm};
-      p.ss_out = Ly.ss_d;
-      for (int f = 0; f < 3; ++f)
-        if (taps && t->taps[f] == li) {
-          if (taps->rows) {
-            p.y2 = taps->rows + size_t(f) * taps->stride;
-            p.ldy2 = H;
-          }
-          if (taps->xf[f]) p.out[p.nout++] = XOut{taps->xf[f], taps->w[f]};
-        }
-      p.err = err;
-      gemv_job(Ly.down, p);
-    }
-    x = XIn{t->xf_in, Ly.ss_d, gemv_parts(ctx, Ly.down, r.L_max)};
-  }
-  plan.last_down_parts = x.nparts;
-  dfree(plan.dev);
-  plan.dev = static_cast<Job*>(dalloc(sizeof(Job) * jobs.size()));
-  CUDA_TRY(cudaMemcpy(plan.dev, jobs.data(), sizeof(Job) * jobs.size(), cudaMemcpyHostToDevice));
-  if (!plan.bar) plan.bar = static_cast<unsigned*>(dalloc(sizeof(unsigned) * 4));
-  plan.njobs = int(jobs.size());
-  plan.ready = true;
-}
-
-// Runs a built stack; returns the head input (fragments times the final norm gain).
-XIn target_stack_launch(wc_target* t, StackPlan& plan, int* err) {
-  wc_ctx* ctx = t->ctx;
-  if (!plan.ready) fail(WC_ERR_INVALID, "layer stack not built");
-  CUDA_TRY(cudaMemsetAsync(plan.bar, 0, sizeof(unsigned) * 4, ctx->stream));
-  StackParams sp;
-  std::memset(&sp, 0, sizeof(sp));
-  sp.jobs = plan.dev;
-  sp.njobs = plan.njobs;
-  sp.bar = plan.bar;
-  sp.err = err;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(ctx->num_sms);
-  cfg.blockDim = dim3(SK_THREADS);
-  cfg.dynamicSmemBytes = stack_smem();
-  cfg.stream = ctx->stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeCooperative;
-  attr[0].val.cooperative = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  prof_begin(ctx, PK_STACK);
-  const cudaError_t e = cudaLaunchKernelEx(&cfg, stack_kernel, sp);
-  if (e != cudaSuccess) fail(WC_ERR_CUDA, std::string("launch of stack_kernel: ") + cudaGetErrorString(e));
-  count_launch(ctx);
-  prof_end(ctx, PK_STACK);
-  return XIn{t->xf_in, t->layers.back().ss_d, plan.last_down_parts};
 }
 
 // Head over `rows` rows given as fragments (times the final norm): argmax keys and,
@@ -2744,7 +2488,6 @@ struct wc_decoder {
   bool prefilled = false;
   cudaEvent_t ev0 = nullptr, ev1 = nullptr;
   float last_ms = 0.f;
-  std::map<int, std::unique_ptr<StackPlan>> stack_plans;  // verify layer stacks per chain length
   // sampled decoding (temperature > 0, set by the prefill): the round's logits, their softmax
   // slices and the acceptance kernel's partials
   bool sampled = false;
@@ -2858,10 +2601,7 @@ void build_round(wc_decoder* dec, int K) {
     to.xf[f] = d->xf_tap[f];
     to.w[f] = d->cfg.feature_norm ? d->feature_norms[f] : nullptr;
   }
-  auto sp_it = dec->stack_plans.find(K);
-  const XIn hx = (sp_it != dec->stack_plans.end() && sp_it->second->ready)
-                     ? target_stack_launch(t, *sp_it->second, err)
-                     : target_layers(t, dec->tkv, rv, in0, t->ws_h, &to, err);
+  const XIn hx = target_layers(t, dec->tkv, rv, in0, t->ws_h, &to, err);
   target_head(t, hx, K + 1, nullptr, K + 1, st->keys + K, smp ? dec->zt : nullptr, err);
   // ---- acceptance + chain compaction (spec.py:357-362; sampled: spec.py:321-324 with
   // verify_tree_stochastic on the chain)
@@ -2944,25 +2684,6 @@ std::pair<cudaGraphExec_t, uint64_t>& round_graph(wc_decoder* dec, int K, bool p
     dec->profilers[gk] = std::make_unique<Profiler>();
     ctx->prof = dec->profilers[gk].get();
   }
-  {  // the verify's layer stack is built and uploaded before capture
-    wc_target* t = dec->t;
-    wc_drafter* d = dec->d;
-    Rows rv;
-    rv.stable = true;
-    rv.L = K + 1;
-    rv.L_max = K + 1;
-    rv.n_dev = &dec->st->n;
-    if (!dec->stack_plans.count(K) && target_stack_ok(t, rv)) {
-      TapOut to;
-      for (int f = 0; f < 3; ++f) {
-        to.xf[f] = d->xf_tap[f];
-        to.w[f] = d->cfg.feature_norm ? d->feature_norms[f] : nullptr;
-      }
-      auto plan = std::make_unique<StackPlan>();
-      target_stack_build(t, dec->tkv, rv, XIn{t->xf_in, t->ss_pack, 1}, t->ws_h, &to, &dec->st->err, *plan);
-      dec->stack_plans[K] = std::move(plan);
-    }
-  }
   cudaGraph_t g = nullptr;
   CUDA_TRY(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
   ctx->capturing = true;
@@ -2997,7 +2718,6 @@ void check_state_error(wc_decoder* dec) {
     CUDA_TRY(cudaMemset(&dec->st->err, 0, sizeof(int)));
     CUDA_TRY(cudaMemset(dec->ctx->d_err, 0, sizeof(int)));
     CUDA_TRY(cudaMemset(dec->ctx->gv_counters, 0, sizeof(int) * dec->ctx->gv_counters_n));
-    CUDA_TRY(cudaMemset(dec->ctx->sk_counters, 0, sizeof(int) * 64));
     fail(WC_ERR_DEVICE, "device error flag " + std::to_string(e | ce));
   }
 }
@@ -3382,6 +3102,27 @@ extern "C" wc_status wc_decoder_round_logits(wc_decoder* dec, int k, float* zt, 
   });
 }
 
+extern "C" wc_status wc_decoder_draft_proposals(wc_decoder* dec, int k, int* tokens, float* logits) {
+  if (!dec) return WC_ERR_INVALID;
+  return guard(dec->ctx, [&] {
+    if (k < 1 || k > dec->max_k) fail(WC_ERR_INVALID, "chain length outside 1..max_k");
+    if (dec->sampled) fail(WC_ERR_INVALID, "sampled rounds rank perturbed logits; read wc_decoder_round_logits");
+    CUDA_TRY(cudaStreamSynchronize(dec->ctx->stream));
+    unsigned long long keys[MAXK];
+    CUDA_TRY(cudaMemcpy(keys, dec->st->keys, sizeof(unsigned long long) * k, cudaMemcpyDeviceToHost));
+    for (int i = 0; i < k; ++i) {
+      // argmax_key layout (common.cuh): order-preserving float bits above the inverted row index
+      const uint32_t row = 0xFFFFFFFFu - uint32_t(keys[i] & 0xFFFFFFFFull);
+      uint32_t u = uint32_t(keys[i] >> 32);
+      u = (u & 0x80000000u) ? (u & 0x7FFFFFFFu) : ~u;
+      int tok = int(row);
+      if (dec->d->vocab_map) CUDA_TRY(cudaMemcpy(&tok, dec->d->vocab_map + row, sizeof(int), cudaMemcpyDeviceToHost));
+      if (tokens) tokens[i] = tok;
+      if (logits) std::memcpy(logits + i, &u, sizeof(float));
+    }
+  });
+}
+
 // ============================================================================ autoregressive baseline
 
 namespace {
@@ -3590,8 +3331,6 @@ bool tc_ready(wc_ctx* ctx) {
                                 int(tree_attn_smem<128>())));
   CUDA_TRY(cudaFuncSetAttribute(tree_attention_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                 int(tree_attn_smem<64>())));
-  CUDA_TRY(cudaFuncSetAttribute(tree_attention_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                int(tree_attn_tc_smem())));
   done.insert(ctx->device);
   return true;
 }
@@ -3777,16 +3516,7 @@ void batch_forward(wc_batch* b, int nreq, int nodes, bool logits, bool causal = 
     ap.err = err;
     const int gz = causal ? (nodes + TA_MAXR / (Hq / Hk) - 1) / (TA_MAXR / (Hq / Hk)) : ap.nsplit;
     prof_begin(ctx, PK_ATTN);
-    static const bool tc_attn = [] {
-      const char* e = std::getenv("WC_TA_TC");
-      return e && std::atoi(e) != 0;
-    }();
-    if (tc_attn && D == 128 && !causal && ap.nsplit == 1 && nodes * (Hq / Hk) <= 128) {
-      const int rows = b->B * Hk * b->cap;  // the layer's arena as [rows][head_dim]
-      const CUtensorMap tk = tmap_bf16(ap.K, rows, D, TAT_KT), tv = tmap_bf16(ap.V, rows, D, TAT_KT);
-      launch_ex(ctx, "tree attention tc", tree_attention_tc_kernel, dim3(nreq, Hk), dim3(TAT_THREADS),
-                tree_attn_tc_smem(), true, 1, tk, tv, ap);
-    } else if (D == 128)
+    if (D == 128)
       launch_ex(ctx, "tree attention", tree_attention_kernel<128>, dim3(nreq, Hk, gz), dim3(TA_THREADS),
                 tree_attn_smem<128>(), true, 1, ap);
     else

@@ -51,10 +51,3 @@ def draft_step_bytes(drafter, head_rows: int, ctx: int, wbytes: int = 2, kvbytes
     dl = _drafter_layer_params(drafter) * drafter.layers
     return (head_rows * drafter.hidden + dl) * wbytes + ctx * drafter.layers * 2 * drafter.kv_heads * \
         drafter.head_dim * kvbytes
-
-
-def target_stack_bytes(target, ctx: int, wbytes: int = 2, kvbytes: int = 2) -> int:
-    """The verify's layer stack (all target layers, no head): weights once + the KV rows of `ctx`
-    positions of every layer."""
-    tp = _target_params(target)
-    return tp["layers"] * wbytes + ctx * target.layers * 2 * target.kv_heads * target.head_dim * kvbytes

@@ -136,7 +136,7 @@ class SpeculativeDecoder:
         return list(out[: n.value])
 
     PROFILE_KINDS = ("target_qkv", "attention", "target_o", "target_gate_up", "target_down", "target_head",
-                     "drafter_head", "drafter_layer", "target_stack")
+                     "drafter_head", "drafter_layer")
 
     def profile_round(self, k: int) -> tuple[list[int], dict]:
         """A real round replayed from an instrumented graph: mean device ms per kernel class."""
@@ -169,6 +169,14 @@ class SpeculativeDecoder:
         rng = (C.c_uint64 * 2)()
         self.ctx.check(lib().wc_decoder_round_logits(self.h, k, zt.ctypes.data, zd.ctypes.data, toks, rng))
         return {"zt": zt, "zd": zd, "tokens": list(toks), "seed": int(rng[0]), "base": int(rng[1])}
+
+    def draft_proposals(self, k: int) -> tuple[list[int], list[float]]:
+        """The drafter's own head choice (token id, logit) at each of the last greedy round's k
+        chain steps, also when forced drafts replaced them (test support)."""
+        toks = (C.c_int * k)()
+        z = np.empty(k, dtype=np.float32)
+        self.ctx.check(lib().wc_decoder_draft_proposals(self.h, k, toks, z.ctypes.data))
+        return list(toks), [float(x) for x in z]
 
     def last_round_ms(self) -> float:
         ms = C.c_float()

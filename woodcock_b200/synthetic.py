@@ -247,3 +247,23 @@ def device_weight_stream(specs, seed: int, device="cuda", std: float = 0.02):
             yield name, torch.ones(shape, dtype=torch.bfloat16, device=device)
         else:
             yield name, (torch.randn(shape, generator=g, device=device, dtype=torch.float32) * std).to(torch.bfloat16)
+
+
+def write_device_model(dir_: str | Path, config: dict, specs, seed: int, device="cuda") -> Path:
+    """config.json + model.safetensors (bf16) holding the tensors of device_weight_stream(specs,
+    seed, device): the same seeded weights the device-built models use, as files the
+    reference's C++ core loads."""
+    import torch
+
+    d = Path(dir_)
+    d.mkdir(parents=True, exist_ok=True)
+    (d / "config.json").write_text(json.dumps(config))
+    stream = device_weight_stream(specs, seed=seed, device=device)
+
+    def produce(name):
+        n, w = next(stream)
+        assert n == name
+        return w.view(torch.int16).cpu().numpy().view("uint16")
+
+    st.save_streaming(d / "model.safetensors", [(n, "BF16", s) for n, s, _ in specs], produce)
+    return d
