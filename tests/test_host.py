@@ -34,18 +34,35 @@ def test_cost_aware_chain_monotonic():
 
 
 def test_cost_aware_chain_alpha_estimate_and_limits():
-    pol = CostAwareChain(1.0, 0.5, {n: 10.0 for n in range(1, 10)}, alpha0=0.5, prior=2.0, window=3)
+    """Successes and first failures with exponential forgetting over a prior."""
+    pol = CostAwareChain(1.0, 0.5, {n: 10.0 for n in range(1, 10)}, alpha0=0.5, prior=2.0, window=4)
     assert pol.alpha() == pytest.approx(0.5)
-    pol.observe(4, 4, 4, 0, 0)
-    pol.observe(1, 4, 4, 0, 0)
-    assert pol.alpha() == pytest.approx((5 + 1) / (5 + 1 + 2))
-    for _ in range(3):
+    pol.observe(4, 4, 4, 0, 0)  # all accepted: 4 successes, no failure
+    assert pol.alpha() == pytest.approx(4.75 / 5.5)
+    pol.observe(1, 4, 4, 0, 0)  # one success, then the first rejection
+    assert pol.alpha() == pytest.approx(4.5625 / (4.5625 + 1.5625))
+    for _ in range(60):
         pol.observe(0, 2, 2, 0, 0)
-    assert pol.alpha() == pytest.approx(1 / (3 + 2))
+    assert pol.alpha() == pytest.approx(0.01)  # clamped
     pol.reset()
     assert pol.alpha() == pytest.approx(0.5)
     lim = CostAwareChain(0.1, 0.05, {n: 1.0 for n in range(1, 5)}, k_max=8)
     assert lim.k_max == 3 and lim.best_depth(0.99) == 3
+
+
+def test_cost_aware_chain_from_measured_round_times():
+    """A cost file with this package's measured round times: T(k) = round_ms[k] directly."""
+    rm = {1: 1.0, 2: 1.1, 3: 1.2, 4: 1.3, 5: 1.4, 6: 1.5}
+    costs = {"ctx": 512, "drafter": {"16384": {"head_ms": 0.02, "step_ms": 0.09}},
+             "verify_ms": {str(n): 1.0 for n in range(1, 10)}, "round_ms": {"16384": {str(k): v for k, v in rm.items()}}}
+    pol = CostAwareChain.from_costs(costs, "16384")
+    assert pol.k_max == 6
+    for a in (0.2, 0.5, 0.8, 0.95):
+        want = max(rm, key=lambda k: ((1 - a ** (k + 1)) / (1 - a) / rm[k], -k))
+        assert pol.best_depth(a) == want
+    assert pol.best_depth(0.05) == 1 and pol.best_depth(0.99) == 6
+    with pytest.raises(ValueError):
+        CostAwareChain()
 
 
 def test_static_policy_budget_and_plan():

@@ -26,6 +26,7 @@ struct RoundState {
   int acc[MAXK + 1];      // accepted tokens d_1..d_a, next
   int forced[MAXK];       // oracle-drafter tokens (-1 = drafter's own)
   unsigned long long keys[MAXKEYS];  // argmax keys: draft steps [0, K), verify rows [K, 2K+1)
+  unsigned long long draft_keys[MAXK];  // the last round's draft-step keys, kept when keys reset
   unsigned long long rng[2];         // sampled decoding: Philox seed, counter base of the next round
   float temperature;                 // sampled decoding: T (0 = greedy)
   int top_k;                         // sampled decoding: top-k warping of the target (0 = off)
@@ -527,6 +528,7 @@ __global__ void accept_chain_kernel(RoundState* st, int K, const int* vocab_map_
   st->L_upd = a + 1;
   st->n += a + 1;
   st->x_n = next;
+  for (int i = 0; i < K; ++i) st->draft_keys[i] = st->keys[i];
   for (int i = 0; i < MAXKEYS; ++i) st->keys[i] = 0ull;
   if (out_host_view) {
     out_host_view[0] = a + 1;

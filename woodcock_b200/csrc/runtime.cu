@@ -25,6 +25,7 @@
 #include "../../include/woodcock_b200.h"
 #include "attention.cuh"
 #include "attention_dec.cuh"
+#include "attention_split.cuh"
 #include "attention_mma.cuh"
 #include "batch.cuh"
 #include "common.cuh"
@@ -106,7 +107,11 @@ struct wc_ctx {
   size_t max_smem = 0;
   Profiler* prof = nullptr;  // set while a profiled round is being captured
   bool pdl = true;           // programmatic dependent launch between round kernels
-  int attn_mode = 2;         // bf16 caches: 2 decode kernel, 1 split-KV mma kernel, 0 CUDA cores
+  int attn_mode = 2;         // bf16 caches: 2 split-sequence kernel (attention_split.cuh), 4 the
+                             // cluster kernel (attention_dec.cuh), 1 split-KV mma kernel, 0 CUDA cores
+  float* as_part_o = nullptr;   // attention_split partial states: [16 KV heads][AS_MAXS + 1][AS_MAXR][128]
+  float* as_part_ml = nullptr;  //   and their (m, l): [16][AS_MAXS + 1][AS_MAXR][2]
+  int* as_counters = nullptr;   //   per-KV-head arrivals (zero between launches)
   int gemv_blocks_per_sm = 1;
   bool gemv_wide = true;                 // 80 KB activation chunks for K up to 2560 (WC_GEMV_WIDE=0: split K)
   bool gemv_acs = true;                  // whole-K blocks with streamed activation pieces (WC_GEMV_ACS=0: split K)
@@ -663,7 +668,36 @@ void launch_attention(wc_ctx* ctx, AttnParams p) {
   // tensor-core paths: bf16 cache, rule-based visibility, new rows appended by the kernel
   const bool tc_ok = !p.q_ready && !p.mask_full && p.kv_dtype == WC_BF16 && p.write_cache &&
                      (p.D == 128 || p.D == 64) && p.L_max * rep <= AM_MAXR && p.stride_p == p.D;
-  if (tc_ok && ctx->attn_mode == 2 && p.L_max <= AD_MAXL && p.L_max * rep <= AD_MAXR) {
+  if (tc_ok && ctx->attn_mode == 2 && p.L_max <= AS_MAXL && p.L_max * rep <= AS_MAXR && p.Hk <= 16) {
+    AttnSplitParams sp;
+    std::memset(&sp, 0, sizeof(sp));
+    sp.a = p;
+    sp.part_o = ctx->as_part_o;
+    sp.part_ml = ctx->as_part_ml;
+    sp.counters = ctx->as_counters;
+    // prefix blocks per KV head: the capacity in 128-position chunks, so that a block holds its
+    // whole slice in shared memory at any context the cache can reach
+    sp.S = std::max(1, std::min(AS_MAXS, (p.cap + AS_CHUNK - 1) / AS_CHUNK));
+    const bool mt2 = p.L_max * rep > 16;
+    const dim3 grid(sp.S + 1, p.Hk);
+    if (p.D == 128) {
+      if (mt2)
+        launch_ex(ctx, "attention_split", attention_split_kernel<128, 2>, grid, dim3(AS_THREADS),
+                  attention_split_smem<128>(), true, 1, sp);
+      else
+        launch_ex(ctx, "attention_split", attention_split_kernel<128, 1>, grid, dim3(AS_THREADS),
+                  attention_split_smem<128>(), true, 1, sp);
+    } else {
+      if (mt2)
+        launch_ex(ctx, "attention_split", attention_split_kernel<64, 2>, grid, dim3(AS_THREADS),
+                  attention_split_smem<64>(), true, 1, sp);
+      else
+        launch_ex(ctx, "attention_split", attention_split_kernel<64, 1>, grid, dim3(AS_THREADS),
+                  attention_split_smem<64>(), true, 1, sp);
+    }
+    return;
+  }
+  if (tc_ok && ctx->attn_mode == 4 && p.L_max <= AD_MAXL && p.L_max * rep <= AD_MAXR) {
     const bool mt2 = p.L_max * rep > 16;
     if (p.D == 128) {
       if (mt2)
@@ -733,6 +767,10 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
     CUDA_TRY(cudaMemset(ctx->d_err, 0, sizeof(int)));
     ctx->gv_partial_n = size_t(8) << 20;  // 32 MB of split-K partials
     ctx->gv_partial = static_cast<float*>(dalloc(sizeof(float) * ctx->gv_partial_n));
+    ctx->as_part_o = static_cast<float*>(dalloc(sizeof(float) * 16 * (AS_MAXS + 1) * AS_MAXR * 128));
+    ctx->as_part_ml = static_cast<float*>(dalloc(sizeof(float) * 16 * (AS_MAXS + 1) * AS_MAXR * 2));
+    ctx->as_counters = static_cast<int*>(dalloc(sizeof(int) * AS_MAXHK));
+    CUDA_TRY(cudaMemset(ctx->as_counters, 0, sizeof(int) * AS_MAXHK));
     ctx->gv_counters_n = 8192;
     ctx->gv_counters = static_cast<int*>(dalloc(sizeof(int) * ctx->gv_counters_n));
     CUDA_TRY(cudaMemset(ctx->gv_counters, 0, sizeof(int) * ctx->gv_counters_n));
@@ -746,6 +784,10 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
     CUDA_TRY(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(attention_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(attention_mma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
+    CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<128, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
+    CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<128, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
+    CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<64, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
+    CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<64, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(attention_dec_kernel<128, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(attention_dec_kernel<128, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(attention_dec_kernel<64, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
@@ -788,6 +830,9 @@ extern "C" void wc_ctx_destroy(wc_ctx* ctx) {
   dfree(ctx->d_err);
   dfree(ctx->gv_partial);
   dfree(ctx->gv_counters);
+  dfree(ctx->as_part_o);
+  dfree(ctx->as_part_ml);
+  dfree(ctx->as_counters);
   dfree(ctx->pw_scratch);
   dfree(ctx->pw);
   dfree(ctx->qw);
@@ -807,6 +852,7 @@ extern "C" wc_status wc_ctx_synchronize(wc_ctx* ctx) {
     if (e) {
       CUDA_TRY(cudaMemset(ctx->d_err, 0, sizeof(int)));
       CUDA_TRY(cudaMemset(ctx->gv_counters, 0, sizeof(int) * ctx->gv_counters_n));
+      CUDA_TRY(cudaMemset(ctx->as_counters, 0, sizeof(int) * AS_MAXHK));
       fail(WC_ERR_DEVICE, "device error flag " + std::to_string(e));
     }
   });
@@ -2718,6 +2764,7 @@ void check_state_error(wc_decoder* dec) {
     CUDA_TRY(cudaMemset(&dec->st->err, 0, sizeof(int)));
     CUDA_TRY(cudaMemset(dec->ctx->d_err, 0, sizeof(int)));
     CUDA_TRY(cudaMemset(dec->ctx->gv_counters, 0, sizeof(int) * dec->ctx->gv_counters_n));
+    CUDA_TRY(cudaMemset(dec->ctx->as_counters, 0, sizeof(int) * AS_MAXHK));
     fail(WC_ERR_DEVICE, "device error flag " + std::to_string(e | ce));
   }
 }
@@ -3109,7 +3156,7 @@ extern "C" wc_status wc_decoder_draft_proposals(wc_decoder* dec, int k, int* tok
     if (dec->sampled) fail(WC_ERR_INVALID, "sampled rounds rank perturbed logits; read wc_decoder_round_logits");
     CUDA_TRY(cudaStreamSynchronize(dec->ctx->stream));
     unsigned long long keys[MAXK];
-    CUDA_TRY(cudaMemcpy(keys, dec->st->keys, sizeof(unsigned long long) * k, cudaMemcpyDeviceToHost));
+    CUDA_TRY(cudaMemcpy(keys, dec->st->draft_keys, sizeof(unsigned long long) * k, cudaMemcpyDeviceToHost));
     for (int i = 0; i < k; ++i) {
       // argmax_key layout (common.cuh): order-preserving float bits above the inverted row index
       const uint32_t row = 0xFFFFFFFFu - uint32_t(keys[i] & 0xFFFFFFFFull);
@@ -3261,6 +3308,7 @@ extern "C" wc_status wc_generate_autoregressive(wc_target* t, const int* prompt,
       CUDA_TRY(cudaStreamSynchronize(ctx->stream));
       if (hout[1]) {
         CUDA_TRY(cudaMemset(ctx->gv_counters, 0, sizeof(int) * ctx->gv_counters_n));
+        CUDA_TRY(cudaMemset(ctx->as_counters, 0, sizeof(int) * AS_MAXHK));
         fail(WC_ERR_DEVICE, "device error flag " + std::to_string(hout[1]));
       }
       x = hout[0];
