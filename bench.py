@@ -51,9 +51,11 @@ def parse():
     ap.add_argument("--accept", type=int, default=2, help="drafts accepted per round (oracle-drafter mode)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--out", default=None, help="also write the JSON line here")
-    ap.add_argument("--workload", choices=["c3", "c4", "c5"], default="c3",
-                    help="c3: the headline greedy round (default); c4: Qwen3-4B sampled round at T = 1.0; "
-                         "c5: batched tree verification + compaction, 64 requests x 4096 context")
+    ap.add_argument("--workload", choices=["c2", "c3", "c4", "c5"], default="c3",
+                    help="c3: the headline greedy round (default); c2: drafter micro-bench at 1.7B sizes, "
+                         "ctx 2048, k = 1..8, 16k and full heads (writes the cost file with --costs-out); "
+                         "c4: Qwen3-4B sampled round at T = 1.0; c5: batched tree verification + compaction")
+    ap.add_argument("--costs-out", default=None, help="c2: write the measured cost file (CostAwareChain.from_costs)")
     ap.add_argument("--c5-layers", type=int, default=0,
                     help="c5: target layers (0 = the config's 28; fewer for profiler captures of the same launches)")
     ap.add_argument("--c5-requests", type=int, default=64, help="c5: requests per GPU")
@@ -494,6 +496,96 @@ def profile_mode(a):
     print(json.dumps({"profile_rounds": a.profile_rounds, "last_round_ms": dec.last_round_ms()}), flush=True)
 
 
+# ----------------------------------------------------------------------------- C2: drafter micro-bench
+
+def bench_c2(a):
+    """the EAGLE-3 drafter at Qwen3-1.7B sizes (fuse 6144 -> 2048, one layer
+    with 16 / 8 heads of 128 and SwiGLU 6144) with the 16,384-row trimmed head and, for comparison,
+    the full 151,936-row head; drafter KV context 2048; chains of k = 1..8 at batch 1. The drafter
+    runs inside the device round (C3 target, bf16, a 2048-token prompt so the drafter cache holds
+    2048 entries); every round is replayed from the same saved state, so the context stays at 2048.
+    Definitions follow scripts/time_draft_step.py:48-57: head = drafter head + argmax on one row,
+    step = head + one drafter layer pass; chain(k) = k heads + (k - 1) layer passes, the draft phase
+    of a chain round. Kernel times come from CUDA events around each kernel inside a real round
+    (the instrumented copy of the round graph); round_ms[k] is the whole round from its graph.
+    With --costs-out the measured table is written for CostAwareChain.from_costs."""
+    import torch
+
+    from woodcock_b200 import Drafter, SpeculativeDecoder, StaticPolicy
+    from woodcock_b200 import roofline as rl
+    from woodcock_b200 import synthetic as syn
+
+    torch.cuda.set_device(0)
+    ts, ds = syn.Q17_TARGET, syn.Q17_DRAFTER
+    ctx_len = 2048
+    t, d16 = build_models(0)
+    dfull = Drafter.from_weights(ds.config(), syn.device_weight_stream(syn.drafter_tensor_specs(ds), 1, "cuda:0"),
+                                 dtype="bf16", device=0)
+    prompt = syn.prompt_ids(ctx_len, ts.vocab, seed=11)
+    pk = peaks()
+    heads, costs_round, verify_ms = {}, {}, {}
+    for name, d, rows in (("16384", d16, HEAD_ROWS), ("full", dfull, ds.vocab)):
+        dec = SpeculativeDecoder(t, d, StaticPolicy(8), max_context=ctx_len + 64, max_k=8)
+        dec.prefill(prompt)
+        dec.save_state()
+        per_k = {}
+        for k in range(1, 9):
+            for _ in range(max(3, a.warmup)):
+                dec.restore_state()
+                dec.round(k)
+            ms = []
+            for _ in range(max(1, a.steps)):
+                dec.restore_state()
+                dec.round(k)
+                ms.append(dec.last_round_ms())
+            profs = []
+            for _ in range(3):
+                dec.restore_state()
+                profs.append(dec.profile_round(k)[1])
+            mean = {c: statistics.mean(p[c]["mean_ms"] for p in profs) for c in profs[0]}
+            launches = {c: profs[0][c]["launches"] for c in profs[0]}
+            head_ms, layer_ms = mean["drafter_head"], mean["drafter_layer"]
+            target_ms = sum(mean[c] * launches[c] for c in ("target_qkv", "attention", "target_o", "target_gate_up",
+                                                             "target_down", "target_head"))
+            per_k[k] = {"round_ms": statistics.median(ms), "head_ms": head_ms, "layer_ms": layer_ms,
+                        "step_ms": head_ms + layer_ms, "chain_ms": k * head_ms + (k - 1) * layer_ms,
+                        "verify_ms_kernels": target_ms}
+            if name == "16384":
+                verify_ms[k + 1] = target_ms
+        step = statistics.median(per_k[k]["step_ms"] for k in per_k)
+        head = statistics.median(per_k[k]["head_ms"] for k in per_k)
+        sb = rl.draft_step_bytes(ds, rows, ctx_len)
+        heads[name] = {"head_rows": rows, "head_ms": head, "step_ms": step, "per_k": per_k,
+                       "step_bytes": sb, "step_gbs": sb / (step / 1e3) / 1e9, "step_frac": sb / (step / 1e3) / 1e9 / pk["hbm_gbs"]}
+        costs_round[name] = {k: per_k[k]["round_ms"] for k in per_k}
+        del dec
+    # verify(1) from the k = 1 round has two rows; a one-row verify is the autoregressive step
+    verify_ms.setdefault(1, verify_ms[2])
+    h16 = heads["16384"]
+    line = {"metric": "C2 draft step latency (ms): drafter head + argmax + one drafter layer, Qwen3-1.7B-size "
+                      "drafter, ctx 2048, batch 1", "value": h16["step_ms"], "unit": "ms", "n_gpus": 1,
+            "steps": a.steps, "warmup": a.warmup, "higher_is_better": False, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic: seeded random-init weights, uniform-random prompt ids",
+            "config": {"workload": "C2: drafter micro-bench at Qwen3-1.7B sizes, 16,384-row head vs the full "
+                                   "151,936-row head, drafter KV context 2048, chains k = 1..8, batch 1",
+                       "ctx": ctx_len, "k": list(range(1, 9)),
+                       "l2": "each step streams 117 MB of drafter layer + 67 MB (16k) / 622 MB (full) of head"},
+            "heads": heads,
+            "roofline": {"bound": "hbm", "kernel": "draft step (drafter head GEMV + drafter layer GEMVs + attention)",
+                         "achieved": h16["step_gbs"], "peak": pk["hbm_gbs"], "unit": "GB/s",
+                         "frac": h16["step_frac"], "traffic": None,
+                         "algorithmic_bytes_per_launch": h16["step_bytes"], "peak_source": pk["source"]}}
+    print(json.dumps(line), flush=True)
+    if a.out:
+        Path(a.out).write_text(json.dumps(line) + "\n")
+    if a.costs_out:
+        costs = {"ctx": ctx_len, "measured_on": "B200, bench.py --workload c2",
+                 "drafter": {n: {"head_ms": h["head_ms"], "step_ms": h["step_ms"]} for n, h in heads.items()},
+                 "verify_ms": {str(n): v for n, v in sorted(verify_ms.items())},
+                 "round_ms": {n: {str(k): v for k, v in r.items()} for n, r in costs_round.items()}}
+        Path(a.costs_out).write_text(json.dumps(costs, indent=1) + "\n")
+
+
 # ----------------------------------------------------------------------------- C4: sampled 4B round
 
 def chi2_equal_mass(counts, p, bins=1000):
@@ -809,6 +901,8 @@ def main():
         profile_mode(a)
     elif a.impl == "reference":
         bench_reference(a)
+    elif a.workload == "c2":
+        bench_c2(a)
     elif a.workload == "c4":
         bench_c4(a)
     elif a.workload == "c5":

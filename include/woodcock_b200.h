@@ -246,6 +246,26 @@ WC_API wc_status wc_decoder_round(wc_decoder* dec, int k, int* out_tokens, int* 
 WC_API wc_status wc_decoder_generate(wc_decoder* dec, const int* prompt, int n, int max_new, int k,
                               const wc_sampling_params* sp, const int* eos, int n_eos, int* out_tokens, int* out_n,
                               wc_gen_stats* stats);
+/* A greedy draft-tree round (spec.py:216-329; src/core/spec.cpp:86-233 with StaticPolicy(depth,
+ * width, budget)) on the device from one CUDA graph per shape, one host synchronisation: the
+ * drafter expands the tree level by level (top-width children of the `width` most probable nodes of
+ * each level, by path probability), the `budget` most probable nodes are verified in one target
+ * pass with the tree mask and positions n + depth, verify_tree_greedy picks the path, the target
+ * cache is compacted to it and the drafter is updated on the accepted rows. Writes d_1..d_a, next
+ * to out_tokens (host, capacity depth + 1). Limits: width <= 16, (depth - 1) * width <= 32,
+ * at most 128 drafted nodes and 16 verify rows; greedy decoding only (WC_ERR_UNSUPPORTED). */
+WC_API wc_status wc_decoder_tree_round(wc_decoder* dec, int depth, int width, int budget, int* out_tokens,
+                                       int* out_n);
+/* Test support (oracle-drafter mode for trees, tests/test_spec_model.py:59-92 pattern): while set,
+ * tree rounds verify this tree (host int32 tokens[n], parents[n]; node 0 is the round's root and
+ * its token is ignored; parents precede their nodes) instead of the drafted one; the drafter still
+ * runs over every node that has children. NULL clears it. */
+WC_API wc_status wc_decoder_set_forced_tree(wc_decoder* dec, const int* tokens, const int* parents, int n);
+/* Test support: the last tree round's nodes (tokens, parents, the drafter head's own argmax token
+ * and logit at every node it ran on, -1 elsewhere) and the node id of each verify row. Host
+ * buffers of `cap` entries; any may be NULL. */
+WC_API wc_status wc_decoder_tree_nodes(wc_decoder* dec, int cap, int* n_nodes, int* tokens, int* parents,
+                                       int* proposals, float* proposal_logits, int* verified, int* n_verified);
 /* spec.py:377-397 / spec.cpp:282-311 autoregressive baseline through the same target kernels */
 WC_API wc_status wc_generate_autoregressive(wc_target* t, const int* prompt, int n, int max_new,
                                      const wc_sampling_params* sp, const int* eos, int n_eos, int max_context,

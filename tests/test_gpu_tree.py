@@ -1,10 +1,15 @@
-"""Draft trees and the synced path (host-driven rounds over the device API; spec.py:216-374).
+"""Draft trees (spec.py:216-374; src/core/spec.cpp:86-233).
 
-(a) Greedy top-k trees (StaticPolicy(3, 3, 8)) on C1 fp32: tokens equal the reference C++
-    core's tree:3,3,8 run and autoregressive decoding, and the accepted total equals the
-    reference's (tests/golden/c1*.json), so the tree shapes agree round by round.
-(b) fused=False on a chain: the synced path gives the autoregressive tokens.
-(c) Sampled trees: the same Philox stream drives the oracle's restatement of the reference
+(a) Greedy top-k trees (StaticPolicy(3, 3, 8)) on C1 fp32, as device tree rounds: tokens equal
+    the reference C++ core's tree:3,3,8 run and autoregressive decoding, and the accepted total
+    equals the reference's (tests/golden/c1*.json).
+(b) fused=False on a chain (a width-1 device tree round): the autoregressive tokens.
+(c) Forced trees with branching accepted paths (tests/golden/c1u_forced.json, made by the
+    reference C++ core in oracle-drafter mode): every round's accepted path and next token,
+    the drafter's own proposals and logits at the root and every drafted node (these depend on
+    the tree-masked drafter passes and on the previous round's multi-row update), and both
+    cache lengths equal the reference's.
+(d) Sampled trees: the same Philox stream drives the oracle's restatement of the reference
     (wc_oracle.SpeculativeDecoder with Tape(seed)) and this path; the token streams agree.
 """
 
@@ -34,7 +39,7 @@ def test_greedy_tree_matches_reference(name, golden, c1_models, prompt64):
     out, st = SpeculativeDecoder(t, d, StaticPolicy(3, 3, 8), max_context=512).generate(prompt64, 128)
     assert out == g["spec_tree:3,3,8"]["tokens"] == g["ar_tokens"]
     assert sum(st.accepted) == g["spec_tree:3,3,8"]["accepted"]
-    assert not st.fused and st.rounds == len(st.accepted) and max(st.depths) <= 3
+    assert st.fused and st.rounds == len(st.accepted) and max(st.depths) <= 3
 
 
 def test_synced_chain_equals_autoregressive(golden, c1_models, prompt64):
@@ -43,7 +48,44 @@ def test_synced_chain_equals_autoregressive(golden, c1_models, prompt64):
     t, d = c1_models["c1u"]
     out, st = SpeculativeDecoder(t, d, StaticPolicy(4), fused=False, max_context=512).generate(prompt64, 64)
     assert out == golden("c1u")["ar_tokens"][:64]
-    assert not st.fused
+
+
+def test_forced_tree_rounds_match_reference(golden, c1_models, prompt64):
+    import numpy as np
+
+    from woodcock_b200 import SpeculativeDecoder, StaticPolicy
+
+    g = golden("c1u_forced")
+    ref = g["tree"]
+    t, d = c1_models["c1u"]
+    V, A = t.cfg.vocab, ref["ar"]
+    templates = [O.parse_template(x) for x in ref["templates"]]
+    dec = SpeculativeDecoder(t, d, StaticPolicy(4, 2, 8), max_context=512)
+    emitted = [dec.prefill(prompt64)]
+    assert emitted[0] == ref["first"]
+    branched = 0
+    for r, rr in enumerate(ref["rounds"]):
+        e = len(emitted)
+        tpl = templates[r % len(templates)]
+        toks = [emitted[-1]] + [(A[e + o] + dl) % V for _, o, dl in tpl]
+        pars = [-1] + [p for p, _, _ in tpl]
+        assert toks == rr["tokens"] and pars == rr["parents"]
+        dec.set_forced_tree(toks, pars)
+        acc = dec.tree_round(4, 2, 8)
+        assert acc[:-1] == [rr["tokens"][v] for v in rr["path"]], r
+        assert acc[-1] == rr["next"], r
+        nodes = dec.tree_nodes()
+        assert nodes["tokens"][1:] == toks[1:] and nodes["parents"] == pars
+        assert nodes["proposals"] == rr["proposals"], r
+        drafted = [i for i, x in enumerate(rr["proposals"]) if x >= 0]
+        np.testing.assert_allclose([nodes["proposal_logits"][i] for i in drafted],
+                                   [rr["proposal_logits"][i] for i in drafted], rtol=0, atol=1e-4)
+        assert dec.state() == (rr["n"], rr["drafter_len"]), r
+        branched += any(p not in (-1, i - 1) for i, p in enumerate(rr["parents"])) and len(rr["path"]) > 1
+        emitted.extend(acc[: g["max_new"] - len(emitted)])
+    dec.set_forced_tree(None)
+    assert emitted == ref["tokens"]
+    assert branched >= 4
 
 
 def test_sampled_tree_follows_the_oracle_on_one_philox_stream(tiny_models, c1_models, prompt64):

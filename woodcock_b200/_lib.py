@@ -110,6 +110,9 @@ SIGNATURES = {
     "wc_decoder_prefill": (S, [P, I32P, C.c_int, C.POINTER(SamplingParamsC), I32P]),
     "wc_decoder_set_forced": (S, [P, I32P, C.c_int]),
     "wc_decoder_round": (S, [P, C.c_int, I32P, I32P]),
+    "wc_decoder_tree_round": (S, [P, C.c_int, C.c_int, C.c_int, I32P, I32P]),
+    "wc_decoder_set_forced_tree": (S, [P, I32P, I32P, C.c_int]),
+    "wc_decoder_tree_nodes": (S, [P, C.c_int, I32P, I32P, I32P, I32P, P, I32P, I32P]),
     "wc_decoder_generate": (S, [P, I32P, C.c_int, C.c_int, C.c_int, C.POINTER(SamplingParamsC), I32P, C.c_int,
                                 I32P, I32P, C.POINTER(GenStatsC)]),
     "wc_generate_autoregressive": (S, [P, I32P, C.c_int, C.c_int, C.POINTER(SamplingParamsC), I32P, C.c_int,

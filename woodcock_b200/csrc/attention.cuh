@@ -11,6 +11,9 @@
 // Visibility of cache position p for new row l (prefix n = cache size before the rows):
 //   p <  n : lo_l <= p, with lo_l = max(0, n + l - window + 1) under a sliding window, else 0;
 //   p >= n : bit (p - n) of newmask[l] (nullptr = causal: p - n <= l).
+// With mask_from_prefix, n above is the committed length *n_dev instead, so the bits also
+// cover rows appended earlier in the same round (drafted tree levels: a drafted node sees the
+// committed entries, its drafted ancestors and itself, src/core/spec.cpp:158-171).
 // This covers the causal chain, tree masks (prefix + ancestors + self,
 // src/sampling/sampling.cpp:85-93) and the drafter window (src/core/qwen3.cpp:44-53).
 // A full uint8 mask [L][T] (ops::attention, include/woodcock/ops.h:20) is also accepted.
@@ -68,6 +71,7 @@ struct AttnParams {
   int xf_width;      // their (padded) width, >= H*D
   int xf_fp32;       // fp32 models: xf_out holds plain fp32 rows [16][H*D]
   int write_cache;
+  int mask_from_prefix;  // newmask bits count from *n_dev (the committed length), not from n
   int stable_prefix;  // n_dev and the cache rows below it were written by completed work
                       // (not by a kernel that may still run): they may be read before the
                       // dependency wait
@@ -120,13 +124,15 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(__grid_constant_
 
   pdl_launch_dependents();
   pdl_wait();
-  int L, n;
+  int L, n, mlo;
   if (p.q_ready) {
     L = p.L;
     n = p.T_full;
+    mlo = n;
   } else {
     L = p.L_dev ? *p.L_dev : p.L;
     n = (p.n_dev ? *p.n_dev : 0) + p.n_add;
+    mlo = p.mask_from_prefix ? (p.n_dev ? *p.n_dev : 0) : n;
     if (L < 0 || L > p.L_max) {
       raise_error(p.err, kErrRows);
       L = L < 0 ? 0 : p.L_max;
@@ -330,10 +336,10 @@ __global__ void __launch_bounds__(ATT_THREADS) attention_kernel(__grid_constant_
       if (vis) {
         if (p.mask_full) {
           vis = p.mask_full[size_t(l) * p.mask_ld + pos] != 0;
-        } else if (pos < n) {
+        } else if (pos < mlo) {
           vis = p.window <= 0 || pos >= n + l - p.window + 1;
         } else {
-          const int j = pos - n;
+          const int j = pos - mlo;
           vis = p.newmask ? ((p.newmask[l] >> j) & 1ull) != 0 : j <= l;
           if (vis && p.window > 0) vis = pos >= n + l - p.window + 1;
         }

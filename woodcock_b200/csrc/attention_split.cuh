@@ -4,6 +4,9 @@
 // optional window); the reference computation is ops::attention (src/backends/cpu_ops.cpp)
 // after the per-head q/k RMSNorm and RoPE of qwen3.cpp:86-101 / drafter.cpp:106-128.
 //
+// With mask_from_prefix the newmask bits count from the committed length (*n_dev) and cover the
+// rows appended earlier in the round too (drafted tree levels).
+//
 // Grid (S + 1, Hk), 128 threads, no clusters. Blocks 0..S-1 of KV head hk each own a slice of
 // the committed prefix [0, npre); block S owns the tail [npre, n + L): rows appended earlier in
 // the same round, then the new rows, which it normalises, rotates, rounds to bf16 and appends
@@ -58,7 +61,8 @@ struct AsLayout {
   static constexpr size_t ml_off = w_off + 2 * D * 4;                            // [WARPS][MAXR] m, l
   static constexpr size_t pos_off = ml_off + 2 * AS_WARPS * AS_MAXR * 4;         // [MAXL] ints
   static constexpr size_t wt_off = pos_off + AS_MAXL * 4;                       // [MAXR][WARPS] weights, [MAXR] M
-  static constexpr size_t flag_off = wt_off + size_t(AS_MAXR) * (AS_WARPS + 1) * 4;
+  static constexpr size_t mlall_off = wt_off + size_t(AS_MAXR) * (AS_WARPS + 1) * 4;  // [MAXS + 1][MAXR][2]
+  static constexpr size_t flag_off = mlall_off + size_t(AS_MAXS + 1) * AS_MAXR * 2 * 4;
   static constexpr size_t total = flag_off + 16;
 };
 
@@ -168,6 +172,7 @@ __global__ void __launch_bounds__(AS_THREADS) attention_split_kernel(__grid_cons
   int L = p.L_dev ? *p.L_dev : p.L;
   const int nd = p.n_dev ? *p.n_dev : 0;
   const int n = nd + p.n_add;
+  const int mlo = p.mask_from_prefix ? nd : n;  // first position whose visibility the bits decide
   if (L < 0 || L > Lm) {
     if (tid == 0 && split == 0 && hk == 0) raise_error(p.err, kErrRows);
     L = L < 0 ? 0 : Lm;
@@ -378,10 +383,10 @@ __global__ void __launch_bounds__(AS_THREADS) attention_split_kernel(__grid_cons
             const int pos = pos_base + nt * 8 + 2 * t + c;
             bool vis = r < R && pos < end;
             if (vis) {
-              if (pos < n) {
+              if (pos < mlo) {
                 vis = p.window <= 0 || pos >= n + l - p.window + 1;
               } else {
-                const int jj = pos - n;
+                const int jj = pos - mlo;
                 vis = p.newmask ? ((p.newmask[l] >> jj) & 1ull) != 0 : jj <= l;
                 if (vis && p.window > 0) vis = pos >= n + l - p.window + 1;
               }
@@ -517,57 +522,83 @@ __global__ void __launch_bounds__(AS_THREADS) attention_split_kernel(__grid_cons
     *reinterpret_cast<float4*>(po + size_t(r) * D + c) = acc;
   }
   // ---- arrival; the last block of this KV head combines the S + 1 partial states in order
-  __threadfence();
-  __syncthreads();
-  if (tid == 0) s_flag[0] = atomicAdd(&sp.counters[hk], 1) == S;
+  __syncthreads();  // every partial store of this block has been issued
+  if (tid == 0) {
+    __threadfence();
+    s_flag[0] = atomicAdd(&sp.counters[hk], 1) == S;
+  }
   __syncthreads();
   if (!s_flag[0]) return;
   __threadfence();
+  // the partials arrive by cp.async through L2 in as few batches as shared memory allows: every
+  // (m, l) pair and as many splits' o rows as the tile region holds (all of them at C3 sizes)
   const float* hml = sp.part_ml + size_t(hk) * (S + 1) * AS_MAXR * 2;
   const float* ho = sp.part_o + size_t(hk) * (S + 1) * AS_MAXR * D;
-  for (int r = warp; r < R; r += AS_WARPS) {  // per-row block weights exp(m_s - M) / sum_s exp(m_s - M) l_s
-    float M = -INFINITY;
-    for (int s2 = lane; s2 <= S; s2 += kWarp) M = fmaxf(M, __ldcg(hml + (size_t(s2) * AS_MAXR + r) * 2));
-    for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
-    float lt = 0.f;
-    for (int s2 = lane; s2 <= S; s2 += kWarp) {
-      const float2 e = __ldcg(reinterpret_cast<const float2*>(hml + (size_t(s2) * AS_MAXR + r) * 2));
-      const float wv = e.x == -INFINITY ? 0.f : expf(e.x - M);
-      cw[r * (AS_MAXS + 1) + s2] = wv;
-      lt = fmaf(wv, e.y, lt);
+  float* sml = reinterpret_cast<float*>(as_smem + Lay::mlall_off);  // [S + 1][MAXR][2]
+  float* so = reinterpret_cast<float*>(as_smem);                    // [batch][R][D]
+  const int split_floats = R * D;                                   // one split's o rows, contiguous
+  const int fit = max(1, int(Lay::region_a / (size_t(split_floats) * 4)));
+  for (int c = tid; c < (S + 1) * AS_MAXR * 2 / 4; c += AS_THREADS) cp_async16(sml + 4 * c, hml + 4 * c, 16);
+  constexpr int IT = (AS_MAXR * (D / 4) + AS_THREADS - 1) / AS_THREADS;  // o items (row, 4 dims) per thread
+  float4 acc[IT];
+#pragma unroll
+  for (int k = 0; k < IT; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int b0 = 0; b0 <= S; b0 += fit) {
+    const int nb = min(S + 1 - b0, fit);
+    if (b0 > 0) __syncthreads();  // the previous batch has been consumed
+    for (int c = tid; c < nb * split_floats / 4; c += AS_THREADS) {
+      const int sb = c / (split_floats / 4), off = (c % (split_floats / 4)) * 4;
+      cp_async16(so + size_t(sb) * split_floats + off, ho + size_t(b0 + sb) * AS_MAXR * D + off, 16);
     }
-    for (int o2 = 16; o2 > 0; o2 >>= 1) lt += __shfl_xor_sync(0xffffffffu, lt, o2);
-    __syncwarp();
-    const float inv = lt > 0.f ? 1.f / lt : 0.f;
-    for (int s2 = lane; s2 <= S; s2 += kWarp) cw[r * (AS_MAXS + 1) + s2] *= inv;
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    if (b0 == 0) {  // per-row split weights exp(m_s - M) / sum_s exp(m_s - M) l_s
+      for (int r = warp; r < R; r += AS_WARPS) {
+        float M = -INFINITY;
+        for (int s2 = lane; s2 <= S; s2 += kWarp) M = fmaxf(M, sml[(s2 * AS_MAXR + r) * 2]);
+        for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
+        float lt = 0.f;
+        for (int s2 = lane; s2 <= S; s2 += kWarp) {
+          const float mv = sml[(s2 * AS_MAXR + r) * 2];
+          const float wv = mv == -INFINITY ? 0.f : expf(mv - M);
+          cw[r * (AS_MAXS + 1) + s2] = wv;
+          lt = fmaf(wv, sml[(s2 * AS_MAXR + r) * 2 + 1], lt);
+        }
+        for (int o2 = 16; o2 > 0; o2 >>= 1) lt += __shfl_xor_sync(0xffffffffu, lt, o2);
+        __syncwarp();
+        const float inv = lt > 0.f ? 1.f / lt : 0.f;
+        for (int s2 = lane; s2 <= S; s2 += kWarp) cw[r * (AS_MAXS + 1) + s2] *= inv;
+      }
+      __syncthreads();
+    }
+#pragma unroll
+    for (int k = 0; k < IT; ++k) {
+      const int it = tid + k * AS_THREADS;
+      if (it < R * (D / 4)) {
+        const int r = it / (D / 4), c = (it % (D / 4)) * 4;
+        for (int sb = 0; sb < nb; ++sb) {
+          const float wv = cw[r * (AS_MAXS + 1) + b0 + sb];
+          const float4 v = *reinterpret_cast<const float4*>(so + size_t(sb) * split_floats + r * D + c);
+          acc[k].x = fmaf(wv, v.x, acc[k].x);
+          acc[k].y = fmaf(wv, v.y, acc[k].y);
+          acc[k].z = fmaf(wv, v.z, acc[k].z);
+          acc[k].w = fmaf(wv, v.w, acc[k].w);
+        }
+      }
+    }
   }
-  __syncthreads();
-  for (int it = tid; it < R * (D / 4); it += AS_THREADS) {
-    const int r = it / (D / 4), c = (it % (D / 4)) * 4;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int s0 = 0; s0 <= S; s0 += 8) {  // eight splits' loads in flight at a time
-      float4 v[8];
-      float wv[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        const int s2 = s0 + u;
-        wv[u] = s2 <= S ? cw[r * (AS_MAXS + 1) + s2] : 0.f;
-        v[u] = wv[u] != 0.f ? __ldcg(reinterpret_cast<const float4*>(ho + (size_t(s2) * AS_MAXR + r) * D + c))
-                            : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-#pragma unroll
-      for (int u = 0; u < 8; ++u) {
-        acc.x = fmaf(wv[u], v[u].x, acc.x);
-        acc.y = fmaf(wv[u], v[u].y, acc.y);
-        acc.z = fmaf(wv[u], v[u].z, acc.z);
-        acc.w = fmaf(wv[u], v[u].w, acc.w);
-      }
+  for (int k = 0; k < IT; ++k) {
+    const int it = tid + k * AS_THREADS;
+    if (it < R * (D / 4)) {
+      const int r = it / (D / 4), c = (it % (D / 4)) * 4;
+      const int l = r / rep, h = hk * rep + r % rep;
+      attn_emit(p, l, h * D + c, acc[k].x);
+      attn_emit(p, l, h * D + c + 1, acc[k].y);
+      attn_emit(p, l, h * D + c + 2, acc[k].z);
+      attn_emit(p, l, h * D + c + 3, acc[k].w);
     }
-    const int l = r / rep, h = hk * rep + r % rep;
-    attn_emit(p, l, h * D + c, acc.x);
-    attn_emit(p, l, h * D + c + 1, acc.y);
-    attn_emit(p, l, h * D + c + 2, acc.z);
-    attn_emit(p, l, h * D + c + 3, acc.w);
   }
   if (tid == 0) sp.counters[hk] = 0;  // ready for the next launch
 }

@@ -43,6 +43,7 @@ struct RoundState {
 // verify input the tokens are [x_n, d_1..d_K] resolved from the round state.
 struct PackParams {
   const float* src;
+  const int* row_map;  // source row of output row l: src + row_map[l] * ld (nullptr = l)
   int ld;
   const void* table;   // [vocab][K] of table_dtype (when src == nullptr)
   int table_dtype;
@@ -95,7 +96,7 @@ __global__ void pack_rows_kernel(__grid_constant__ const PackParams p) {
   float ss = 0.f;
   for (int k = threadIdx.x; k < p.K; k += blockDim.x) {
     float v;
-    if (p.src) v = p.src[size_t(l) * p.ld + k];
+    if (p.src) v = p.src[size_t(p.row_map ? p.row_map[l] : l) * p.ld + k];
     else {
       const size_t o = size_t(s_tok) * p.K + k;
       v = p.table_dtype == 1 ? bf16_bits_to_f32(static_cast<const uint16_t*>(p.table)[o])

@@ -32,6 +32,7 @@
 #include "gemv.cuh"
 #include "host_io.h"
 #include "misc.cuh"
+#include "tree.cuh"
 
 using namespace wc;
 namespace fs = std::filesystem;
@@ -112,6 +113,7 @@ struct wc_ctx {
   float* as_part_o = nullptr;   // attention_split partial states: [16 KV heads][AS_MAXS + 1][AS_MAXR][128]
   float* as_part_ml = nullptr;  //   and their (m, l): [16][AS_MAXS + 1][AS_MAXR][2]
   int* as_counters = nullptr;   //   per-KV-head arrivals (zero between launches)
+  int attn_split_pos = 64;      // capacity positions per prefix block (WC_ATTN_SPLIT_POS)
   int gemv_blocks_per_sm = 1;
   bool gemv_wide = true;                 // 80 KB activation chunks for K up to 2560 (WC_GEMV_WIDE=0: split K)
   bool gemv_acs = true;                  // whole-K blocks with streamed activation pieces (WC_GEMV_ACS=0: split K)
@@ -666,6 +668,8 @@ void launch_attention(wc_ctx* ctx, AttnParams p) {
     fail(WC_ERR_INVALID, "attention inputs must be 16-byte aligned with 16-byte row strides");
   if (p.xf_out) p.xf_width = xf_width(!p.xf_fp32, p.H * p.D);
   // tensor-core paths: bf16 cache, rule-based visibility, new rows appended by the kernel
+  if (p.mask_from_prefix && p.kv_dtype == WC_BF16 && ctx->attn_mode != 2)
+    fail(WC_ERR_UNSUPPORTED, "tree-level masks need the split decode attention (WC_ATTN=2)");
   const bool tc_ok = !p.q_ready && !p.mask_full && p.kv_dtype == WC_BF16 && p.write_cache &&
                      (p.D == 128 || p.D == 64) && p.L_max * rep <= AM_MAXR && p.stride_p == p.D;
   if (tc_ok && ctx->attn_mode == 2 && p.L_max <= AS_MAXL && p.L_max * rep <= AS_MAXR && p.Hk <= 16) {
@@ -675,9 +679,9 @@ void launch_attention(wc_ctx* ctx, AttnParams p) {
     sp.part_o = ctx->as_part_o;
     sp.part_ml = ctx->as_part_ml;
     sp.counters = ctx->as_counters;
-    // prefix blocks per KV head: the capacity in 128-position chunks, so that a block holds its
-    // whole slice in shared memory at any context the cache can reach
-    sp.S = std::max(1, std::min(AS_MAXS, (p.cap + AS_CHUNK - 1) / AS_CHUNK));
+    // prefix blocks per KV head: the capacity in slices of attn_split_pos positions (a block holds
+    // up to 128 at once), fixed when the round graph is captured
+    sp.S = std::max(1, std::min(AS_MAXS, (p.cap + ctx->attn_split_pos - 1) / ctx->attn_split_pos));
     const bool mt2 = p.L_max * rep > 16;
     const dim3 grid(sp.S + 1, p.Hk);
     if (p.D == 128) {
@@ -759,6 +763,7 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
     if (const char* e = std::getenv("WC_PDL")) ctx->pdl = std::atoi(e) != 0;
     if (const char* e = std::getenv("WC_GEMV_BLOCKS_PER_SM")) ctx->gemv_blocks_per_sm = std::max(1, std::atoi(e));
     if (const char* e = std::getenv("WC_ATTN")) ctx->attn_mode = std::atoi(e);
+    if (const char* e = std::getenv("WC_ATTN_SPLIT_POS")) ctx->attn_split_pos = std::max(16, std::atoi(e));
     if (const char* e = std::getenv("WC_GEMV_PREFETCH")) ctx->gemv_prefetch = std::atoi(e) != 0;
     if (const char* e = std::getenv("WC_GEMV_ACS")) ctx->gemv_acs = std::atoi(e) != 0;
     if (const char* e = std::getenv("WC_GEMV_WIDE")) ctx->gemv_wide = std::atoi(e) != 0;
@@ -784,6 +789,11 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
     CUDA_TRY(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(attention_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(attention_mma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
+    if (std::getenv("WC_ATTN_CARVEOUT")) {  // A/B switch: the shared-memory carveout of the decode kernels
+      const int cv = std::atoi(std::getenv("WC_ATTN_CARVEOUT"));
+      CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<128, 1>, cudaFuncAttributePreferredSharedMemoryCarveout, cv));
+      CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<128, 2>, cudaFuncAttributePreferredSharedMemoryCarveout, cv));
+    }
     CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<128, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<128, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<64, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
@@ -1248,6 +1258,7 @@ struct Rows {
   int n_add = 0;
   const int* positions = nullptr;
   const unsigned long long* newmask = nullptr;
+  bool mask_from_prefix = false;  // newmask bits count from *n_dev (drafted tree levels)
   const uint8_t* mask_full = nullptr;
   int mask_ld = 0;
 };
@@ -2038,6 +2049,7 @@ XIn drafter_layers(wc_drafter* d, wc_kv* kv, const Rows& r, XIn feat_in, const f
       a.Hk = c.kv_heads;
       a.D = D;
       a.newmask = r.newmask;
+      a.mask_from_prefix = r.mask_from_prefix ? 1 : 0;
       a.window = c.window;
       a.mask_full = r.mask_full;
       a.mask_ld = r.mask_ld;
@@ -2546,6 +2558,12 @@ struct wc_decoder {
   unsigned* acount = nullptr;
   int nbt = 0, nbd = 0;      // softmax slices per target / draft row
   int zd_rows = 0;           // draft head rows zd was sized for
+  // device draft trees (tree.cuh): node state, node features, head logits, taps of the verify rows
+  TreeState* ts = nullptr;
+  float* tree_fb = nullptr;     // [1 + 32][H]
+  float* tree_z = nullptr;      // [TR_MAXW][head rows], allocated at the first tree round
+  int tree_z_rows = 0;
+  float* tree_taps = nullptr;   // [2][3][TR_MAXV][Ht]: the verify rows', then the kept rows'
   // wc_decoder_save_state snapshot
   RoundState* saved_st = nullptr;
   unsigned char* saved_root = nullptr;
@@ -2715,6 +2733,204 @@ void build_round(wc_decoder* dec, int K) {
   launch_finish(dec, &st->L_upd, K + 1, true);
 }
 
+// ---- device draft trees (tree.cuh)
+
+struct TreeShape {
+  int depth, width, budget, rows;  // rows: verify rows the graph is built for
+};
+
+// Checks a greedy tree shape against the device limits and returns its verify row count.
+TreeShape tree_shape(int depth, int width, int budget) {
+  if (depth < 1 || width < 1 || budget < 1) fail(WC_ERR_INVALID, "tree depth, width and budget must be >= 1");
+  if (width > TR_MAXW) fail(WC_ERR_UNSUPPORTED, "tree width above 16");
+  if ((depth - 1) * width > 32) fail(WC_ERR_UNSUPPORTED, "(depth - 1) * width above 32 drafted rows");
+  long long nodes = 1 + width;
+  for (int dd = 2; dd <= depth; ++dd) nodes += (long long)width * width;
+  if (nodes > TR_MAXN) fail(WC_ERR_UNSUPPORTED, "tree of more than 128 drafted nodes");
+  const int rows = int(std::min<long long>(nodes - 1, budget)) + 1;
+  if (rows > TR_MAXV) fail(WC_ERR_UNSUPPORTED, "verify budget above 15 nodes (16 rows per target pass)");
+  return {depth, width, budget, rows};
+}
+
+TreeStepParams tree_params(wc_decoder* dec, const TreeShape& sh) {
+  wc_drafter* d = dec->d;
+  TreeStepParams p;
+  std::memset(&p, 0, sizeof(p));
+  p.ts = dec->ts;
+  p.st = dec->st;
+  p.W = sh.width;
+  p.budget = sh.budget;
+  p.max_rows = sh.rows;
+  p.z = dec->tree_z;
+  p.Vh = d->head_rows;
+  p.vocab_map = d->vocab_map;
+  p.vocab = dec->t->cfg.vocab;
+  p.root_fb = dec->root_fb;
+  p.fb_store = dec->tree_fb;
+  p.H = d->cfg.hidden;
+  p.h = d->ws_h;
+  p.norm_w = d->norm;
+  p.eps = d->cfg.eps;
+  p.post_norm = d->cfg.post_norm;
+  p.out_host_view = dec->out_dev;
+  return p;
+}
+
+// One greedy tree round: draft the tree level by level, verify it in one target pass, accept,
+// compact and update the drafter on the accepted rows.
+void build_tree_round(wc_decoder* dec, const TreeShape& sh) {
+  wc_ctx* ctx = dec->ctx;
+  wc_target* t = dec->t;
+  wc_drafter* d = dec->d;
+  RoundState* st = dec->st;
+  TreeState* ts = dec->ts;
+  int* err = &st->err;
+  const int W = sh.width, N = sh.rows, H = d->cfg.hidden, Ht = t->cfg.hidden;
+  TreeStepParams tp = tree_params(dec, sh);
+  launch_ex(ctx, "tree begin", tree_begin_kernel, dim3(1), dim3(256), 0, true, 1, tp);
+  // depth 1: the root's children from its head row
+  drafter_head(d, XIn{dec->xf_root, nullptr, 0}, 1, ts->hkeys, dec->tree_z, nullptr, nullptr, err);
+  tp.level = 1;
+  launch_ex(ctx, "tree expand", tree_expand_kernel, dim3(1), dim3(256), 0, true, 1, tp);
+  for (int lvl = 1; lvl < sh.depth; ++lvl) {
+    tp.level = lvl;
+    launch_ex(ctx, "tree frontier", tree_frontier_kernel, dim3(1), dim3(32), 0, true, 1, tp);
+    PackParams pk = pack_params();  // the frontier's parent features: fragments x layer-0 gain, fp32 rows
+    pk.src = dec->tree_fb;
+    pk.row_map = ts->fr_fbrow;
+    pk.ld = H;
+    pk.K = H;
+    pk.L = W;
+    pk.L_dev = &ts->n_frontier;
+    pk.w = d->layers[0].in_norm;
+    pk.xf = d->xf_feat;
+    pk.ss = d->ss_feat;
+    pk.copy = d->ws_feat;
+    pk.err = err;
+    launch_pack(ctx, pk, is_bf16(d->dtype), W);
+    Rows r;
+    r.stable = true;
+    r.L = W;
+    r.L_dev = &ts->n_frontier;
+    r.L_max = W;
+    r.n_dev = &st->dc_len;
+    r.n_add = (lvl - 1) * W;
+    r.positions = ts->fr_pos;
+    r.newmask = ts->fr_mask;
+    r.mask_from_prefix = true;
+    TokenSrc tok;
+    std::memset(&tok, 0, sizeof(tok));
+    tok.tokens = ts->fr_tok;
+    tok.vocab = d->cfg.vocab;
+    const XIn head_in = drafter_layers(d, dec->dkv, r, XIn{d->xf_feat, d->ss_feat, 1}, d->ws_feat, tok, d->ws_h,
+                                       nullptr, err);
+    launch_ex(ctx, "tree store fb", tree_store_fb_kernel, dim3(W), dim3(256), 0, true, 1, tp);
+    drafter_head(d, head_in, W, ts->hkeys, dec->tree_z, nullptr, nullptr, err);
+    tp.level = lvl + 1;
+    launch_ex(ctx, "tree expand", tree_expand_kernel, dim3(W), dim3(256), 0, true, 1, tp);
+  }
+  launch_ex(ctx, "tree select", tree_select_kernel, dim3(1), dim3(32), 0, true, 1, tp);
+  // verification of the tree in one target pass (positions n + depth, tree-mask bits)
+  Rows rv;
+  rv.stable = true;
+  rv.L = N;
+  rv.L_dev = &ts->N;
+  rv.L_max = N;
+  rv.n_dev = &st->n;
+  rv.positions = ts->vpos;
+  rv.newmask = ts->vmask;
+  const XIn in0 = target_embed(t, rv, ts->vtok, nullptr, nullptr, t->ws_h, err);
+  TapOut to;
+  to.rows = dec->tree_taps;
+  to.stride = size_t(TR_MAXV) * Ht;
+  const XIn hx = target_layers(t, dec->tkv, rv, in0, t->ws_h, &to, err);
+  target_head(t, hx, N, &ts->N, N, ts->vkeys, nullptr, err);
+  launch_ex(ctx, "tree accept", tree_accept_kernel, dim3(1), dim3(32), 0, true, 1, tp);
+  TreeCompactParams cp;
+  cp.ts = ts;
+  cp.st = st;
+  cp.K = dec->tkv->K;
+  cp.V = dec->tkv->V;
+  cp.layer_elems = (long long)dec->tkv->layer_elems();
+  cp.stride_h = (long long)dec->tkv->cap * dec->tkv->D;
+  cp.D = dec->tkv->D;
+  cp.esize = int(dtype_size(dec->tkv->dtype));
+  cp.cap = dec->tkv->cap;
+  launch_ex(ctx, "tree compact", tree_compact_kernel, dim3(t->cfg.layers, t->cfg.kv_heads), dim3(128), 0, true, 1,
+            cp);
+  TreeTapsParams tq;
+  tq.ts = ts;
+  tq.st = st;
+  tq.in = dec->tree_taps;
+  tq.out = dec->tree_taps + size_t(3) * TR_MAXV * Ht;
+  tq.rows = TR_MAXV;
+  tq.Ht = Ht;
+  launch_ex(ctx, "tree taps", tree_taps_kernel, dim3(3, N), dim3(256), 0, true, 1, tq);
+  // drafter update on the accepted rows (spec.cpp:226-233)
+  XIn tx[3];
+  for (int f = 0; f < 3; ++f) {
+    PackParams pt = pack_params();
+    pt.src = tq.out + size_t(f) * TR_MAXV * Ht;
+    pt.ld = Ht;
+    pt.K = Ht;
+    pt.L = N;
+    pt.L_dev = &st->L_upd;
+    pt.w = d->cfg.feature_norm ? d->feature_norms[f] : nullptr;
+    pt.xf = d->xf_tap[f];
+    pt.ss = d->ss_tap[f];
+    pt.err = err;
+    launch_pack(ctx, pt, is_bf16(d->dtype), N);
+    tx[f] = XIn{d->xf_tap[f], d->ss_tap[f], 1};
+  }
+  const XIn gin = drafter_fuse_impl(d, tx, N, &st->L_upd, N, d->ws_g, err);
+  Rows ru;
+  ru.stable = true;
+  ru.L = N;
+  ru.L_dev = &st->L_upd;
+  ru.L_max = N;
+  ru.n_dev = &st->dc_len;
+  TokenSrc tok;
+  std::memset(&tok, 0, sizeof(tok));
+  tok.tokens = st->acc;
+  tok.vocab = d->cfg.vocab;
+  drafter_layers(d, dec->dkv, ru, gin, d->ws_g, tok, d->ws_h, nullptr, err);
+  launch_finish(dec, &st->L_upd, N, true);
+}
+
+std::pair<cudaGraphExec_t, uint64_t>& tree_graph(wc_decoder* dec, const TreeShape& sh) {
+  const int key = 1 << 20 | sh.depth << 12 | sh.width << 6 | sh.budget;
+  auto it = dec->graphs.find(key);
+  if (it != dec->graphs.end()) return it->second;
+  wc_ctx* ctx = dec->ctx;
+  if (!dec->tree_z || dec->tree_z_rows != dec->d->head_rows) {  // outside the capture
+    dfree(dec->tree_z);
+    dec->tree_z = static_cast<float*>(dalloc(sizeof(float) * size_t(TR_MAXW) * dec->d->head_rows));
+    dec->tree_z_rows = dec->d->head_rows;
+  }
+  CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  cudaGraph_t g = nullptr;
+  CUDA_TRY(cudaStreamBeginCapture(ctx->stream, cudaStreamCaptureModeThreadLocal));
+  ctx->capturing = true;
+  ctx->capture_launches = 0;
+  try {
+    build_tree_round(dec, sh);
+  } catch (...) {
+    ctx->capturing = false;
+    cudaStreamEndCapture(ctx->stream, &g);
+    if (g) cudaGraphDestroy(g);
+    cudaGetLastError();
+    throw;
+  }
+  ctx->capturing = false;
+  CUDA_TRY(cudaStreamEndCapture(ctx->stream, &g));
+  cudaGraphExec_t exec = nullptr;
+  const cudaError_t e = cudaGraphInstantiate(&exec, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) fail(WC_ERR_CUDA, std::string("graph instantiate: ") + cudaGetErrorString(e));
+  dec->graphs[key] = {exec, ctx->capture_launches};
+  return dec->graphs[key];
+}
+
 int graph_key(const wc_decoder* dec, int K) {
   return K + (dec->sampled ? kSampledGraphKey : 0) + (dec->warped ? 2 * kSampledGraphKey : 0);
 }
@@ -2788,7 +3004,7 @@ extern "C" wc_status wc_decoder_create(wc_target* t, wc_drafter* d, int max_cont
     dec->d = d;
     dec->max_k = max_k;
     dec->max_ctx = max_context;
-    const int cap = max_context + max_k + 1;
+    const int cap = max_context + std::max(max_k + 1, 33);  // room for a round's chain or tree rows
     dec->tkv = kv_new(ctx, t->cfg.layers, t->cfg.kv_heads, t->cfg.head_dim, cap, t->dtype);
     dec->dkv = kv_new(ctx, d->cfg.layers, d->cfg.kv_heads, d->cfg.head_dim, cap, d->dtype);
     dec->st = static_cast<RoundState*>(dalloc(sizeof(RoundState)));
@@ -2822,6 +3038,10 @@ extern "C" wc_status wc_decoder_create(wc_target* t, wc_drafter* d, int max_cont
       dec->acount = static_cast<unsigned*>(dalloc(sizeof(unsigned)));
       CUDA_TRY(cudaMemset(dec->acount, 0, sizeof(unsigned)));
     }
+    dec->ts = static_cast<TreeState*>(dalloc(sizeof(TreeState)));
+    CUDA_TRY(cudaMemset(dec->ts, 0, sizeof(TreeState)));
+    dec->tree_fb = static_cast<float*>(dalloc(sizeof(float) * 33 * H));
+    dec->tree_taps = static_cast<float*>(dalloc(sizeof(float) * 2 * 3 * TR_MAXV * t->cfg.hidden));
     CUDA_TRY(cudaEventCreate(&dec->ev0));
     CUDA_TRY(cudaEventCreate(&dec->ev1));
     *out = dec.release();
@@ -2841,7 +3061,8 @@ extern "C" void wc_decoder_destroy(wc_decoder* dec) {
   for (void* p : {(void*)dec->root_out, (void*)dec->root_fb, (void*)dec->xf_root, (void*)dec->xf_fb,
                   (void*)dec->ss_fb, (void*)dec->taps, (void*)dec->zt, (void*)dec->zd, (void*)dec->zstats,
                   (void*)dec->apart, (void*)dec->acount, (void*)dec->saved_st, (void*)dec->saved_root,
-                  (void*)dec->rwarp})
+                  (void*)dec->rwarp, (void*)dec->ts, (void*)dec->tree_fb, (void*)dec->tree_z,
+                  (void*)dec->tree_taps})
     dfree(p);
   if (dec->ev0) cudaEventDestroy(dec->ev0);
   if (dec->ev1) cudaEventDestroy(dec->ev1);
@@ -2987,6 +3208,82 @@ int decoder_round_impl(wc_decoder* dec, int K, int* out_tokens, bool profiled = 
 }
 
 }  // namespace
+
+namespace {
+int decoder_tree_round_impl(wc_decoder* dec, int depth, int width, int budget, int* out_tokens) {
+  if (!dec->prefilled) fail(WC_ERR_INVALID, "prefill before the first round");
+  if (dec->sampled) fail(WC_ERR_UNSUPPORTED, "device draft trees are greedy; sampled trees are not built");
+  const TreeShape sh = tree_shape(depth, width, budget);
+  if (dec->host_n + std::max(sh.rows, (depth - 1) * width + width) > dec->tkv->cap)
+    fail(WC_ERR_CAPACITY, "decoder context exhausted");
+  wc_ctx* ctx = dec->ctx;
+  auto& g = tree_graph(dec, sh);
+  CUDA_TRY(cudaEventRecord(dec->ev0, ctx->stream));
+  CUDA_TRY(cudaGraphLaunch(g.first, ctx->stream));
+  CUDA_TRY(cudaEventRecord(dec->ev1, ctx->stream));
+  ctx->launches += g.second;
+  const int cnt = std::min(depth, MAXK) + 2;
+  CUDA_TRY(cudaMemcpyAsync(dec->out_host, dec->out_dev, sizeof(int) * cnt, cudaMemcpyDeviceToHost, ctx->stream));
+  CUDA_TRY(cudaMemcpyAsync(dec->out_host + cnt, &dec->st->err, sizeof(int), cudaMemcpyDeviceToHost, ctx->stream));
+  CUDA_TRY(cudaStreamSynchronize(ctx->stream));  // the round's single host synchronisation
+  cudaEventElapsedTime(&dec->last_ms, dec->ev0, dec->ev1);
+  if (dec->out_host[cnt]) check_state_error(dec);
+  const int m = dec->out_host[0];
+  if (m < 1 || m > depth + 1) fail(WC_ERR_DEVICE, "tree round produced an invalid token count");
+  for (int i = 0; i < m; ++i) out_tokens[i] = dec->out_host[1 + i];
+  dec->host_n += m;
+  return m;
+}
+}  // namespace
+
+extern "C" wc_status wc_decoder_tree_round(wc_decoder* dec, int depth, int width, int budget, int* out_tokens,
+                                           int* out_n) {
+  if (!dec || !out_tokens || !out_n) return WC_ERR_INVALID;
+  return guard(dec->ctx, [&] { *out_n = decoder_tree_round_impl(dec, depth, width, budget, out_tokens); });
+}
+
+extern "C" wc_status wc_decoder_set_forced_tree(wc_decoder* dec, const int* tokens, const int* parents, int n) {
+  if (!dec) return WC_ERR_INVALID;
+  return guard(dec->ctx, [&] {
+    TreeState* ts = dec->ts;
+    int on = 0;
+    if (tokens && parents && n > 0) {
+      if (n > TR_MAXN) fail(WC_ERR_UNSUPPORTED, "forced tree of more than 128 nodes");
+      if (parents[0] != -1) fail(WC_ERR_INVALID, "forced tree: node 0 is the root (parent -1)");
+      for (int v = 1; v < n; ++v) {
+        if (parents[v] < 0 || parents[v] >= v) fail(WC_ERR_INVALID, "forced tree: parents must precede their nodes");
+        if (tokens[v] < 0 || tokens[v] >= dec->t->cfg.vocab) fail(WC_ERR_INVALID, "forced tree: token id out of range");
+      }
+      CUDA_TRY(cudaMemcpy(ts->f_tok, tokens, sizeof(int) * n, cudaMemcpyHostToDevice));
+      CUDA_TRY(cudaMemcpy(ts->f_par, parents, sizeof(int) * n, cudaMemcpyHostToDevice));
+      CUDA_TRY(cudaMemcpy(&ts->f_n, &n, sizeof(int), cudaMemcpyHostToDevice));
+      on = 1;
+    }
+    CUDA_TRY(cudaMemcpy(&ts->forced_on, &on, sizeof(int), cudaMemcpyHostToDevice));
+  });
+}
+
+extern "C" wc_status wc_decoder_tree_nodes(wc_decoder* dec, int cap, int* n_nodes, int* tokens, int* parents,
+                                           int* proposals, float* proposal_logits, int* verified, int* n_verified) {
+  if (!dec || cap < 0) return WC_ERR_INVALID;
+  return guard(dec->ctx, [&] {
+    CUDA_TRY(cudaStreamSynchronize(dec->ctx->stream));
+    TreeState* ts = dec->ts;
+    int n = 0, N = 0;
+    CUDA_TRY(cudaMemcpy(&n, &ts->n, sizeof(int), cudaMemcpyDeviceToHost));
+    CUDA_TRY(cudaMemcpy(&N, &ts->N, sizeof(int), cudaMemcpyDeviceToHost));
+    n = std::max(0, std::min(n, TR_MAXN));
+    N = std::max(0, std::min(N, TR_MAXV));
+    if (n_nodes) *n_nodes = n;
+    if (n_verified) *n_verified = N;
+    const int k = std::min(n, cap);
+    if (tokens) CUDA_TRY(cudaMemcpy(tokens, ts->token, sizeof(int) * k, cudaMemcpyDeviceToHost));
+    if (parents) CUDA_TRY(cudaMemcpy(parents, ts->parent, sizeof(int) * k, cudaMemcpyDeviceToHost));
+    if (proposals) CUDA_TRY(cudaMemcpy(proposals, ts->prop_tok, sizeof(int) * k, cudaMemcpyDeviceToHost));
+    if (proposal_logits) CUDA_TRY(cudaMemcpy(proposal_logits, ts->prop_z, sizeof(float) * k, cudaMemcpyDeviceToHost));
+    if (verified) CUDA_TRY(cudaMemcpy(verified, ts->vnode, sizeof(int) * std::min(N, cap), cudaMemcpyDeviceToHost));
+  });
+}
 
 extern "C" wc_status wc_decoder_prefill(wc_decoder* dec, const int* prompt, int n, const wc_sampling_params* sp,
                                         int* first) {

@@ -98,6 +98,8 @@ class SpeculativeDecoder:
         # oracle-drafter hook: forced(round, k, emitted) -> k tokens that replace d_1..d_k after
         # the drafter computed them (the OracleDecoder pattern of tests/test_spec_model.py:59-92)
         self.forced = None
+        # the same for tree rounds: forced_tree(round, emitted) -> (tokens, parents)
+        self.forced_tree = None
 
     def __del__(self):
         if getattr(self, "h", None):
@@ -134,6 +136,35 @@ class SpeculativeDecoder:
         n = C.c_int()
         self.ctx.check(lib().wc_decoder_round(self.h, k, out, C.byref(n)))
         return list(out[: n.value])
+
+    def tree_round(self, depth: int, width: int, budget: int) -> list[int]:
+        """One greedy draft-tree round on the device (StaticPolicy(depth, width, budget) shape);
+        returns d_1..d_a, next."""
+        out = (C.c_int * (depth + 1))()
+        n = C.c_int()
+        self.ctx.check(lib().wc_decoder_tree_round(self.h, depth, width, budget, out, C.byref(n)))
+        return list(out[: n.value])
+
+    def set_forced_tree(self, tokens: list[int] | None, parents: list[int] | None = None) -> None:
+        """Oracle-drafter mode for trees: the next tree rounds verify this tree (node 0 = the round's
+        root, its token ignored) instead of the drafted one. None clears it."""
+        if tokens is None:
+            self.ctx.check(lib().wc_decoder_set_forced_tree(self.h, None, None, 0))
+            return
+        self.ctx.check(lib().wc_decoder_set_forced_tree(self.h, int_array(tokens), int_array(parents), len(tokens)))
+
+    def tree_nodes(self) -> dict:
+        """The last tree round's nodes (test support): tokens, parents, the drafter's own proposal
+        and its logit at each node it ran on (-1 elsewhere), and the node of each verify row."""
+        cap = 128
+        n, nv = C.c_int(), C.c_int()
+        tok, par, prop, ver = ((C.c_int * cap)() for _ in range(4))
+        z = np.zeros(cap, dtype=np.float32)
+        self.ctx.check(lib().wc_decoder_tree_nodes(self.h, cap, C.byref(n), tok, par, prop, z.ctypes.data, ver,
+                                                   C.byref(nv)))
+        k = n.value
+        return {"tokens": list(tok[:k]), "parents": list(par[:k]), "proposals": list(prop[:k]),
+                "proposal_logits": [float(x) for x in z[:k]], "verified": list(ver[: nv.value])}
 
     PROFILE_KINDS = ("target_qkv", "attention", "target_o", "target_gate_up", "target_down", "target_head",
                      "drafter_head", "drafter_layer")
@@ -188,7 +219,9 @@ class SpeculativeDecoder:
                  stop_on_eos: bool = True) -> tuple[list[int], GenStats]:
         """spec.py:151-212: returns (tokens, GenStats)."""
         chain = isinstance(self.policy, StaticPolicy) and self.policy.width == 1
-        if not chain or not self.fused:  # trees, and the synced path (spec.py:168-202)
+        if sp.greedy and isinstance(self.policy, StaticPolicy) and (not chain or not self.fused):
+            return self._generate_tree(prompt, max_new_tokens, stop_on_eos)
+        if not chain or not self.fused:  # sampled trees (spec.py:168-202)
             return self._generate_host(prompt, max_new_tokens, sp, stop_on_eos)
         st = GenStats(prompt_tokens=len(prompt), fused=True)
         eos = self.t.eos_token_ids if stop_on_eos else set()
@@ -225,6 +258,50 @@ class SpeculativeDecoder:
             x_n = out[-1]
         if forced_active:
             self.set_forced(None)
+        st.t_total = time.perf_counter() - t0
+        st.new_tokens = len(out)
+        return out, st
+
+    def _generate_tree(self, prompt: list[int], max_new_tokens: int, stop_on_eos: bool) -> tuple[list[int], GenStats]:
+        """Greedy draft trees (and the synced path on a chain) as device tree rounds, one graph per
+        (depth, width, budget) and one synchronisation per round. `forced_tree(round, emitted) ->
+        (tokens, parents)` replaces the drafted tree (oracle-drafter mode)."""
+        st = GenStats(prompt_tokens=len(prompt), fused=True)
+        eos = self.t.eos_token_ids if stop_on_eos else set()
+        t0 = time.perf_counter()
+        x_n = self.prefill(prompt)
+        st.t_prefill = time.perf_counter() - t0
+        out = [x_n]
+        n = len(prompt)
+        self.policy.reset()
+        forced_active = False
+        while len(out) < max_new_tokens and x_n not in eos:
+            ta = time.perf_counter()
+            plan = self.policy.plan(context_len=n, stochastic=False)
+            nodes = 1 + plan.width + (plan.max_depth - 1) * plan.width * plan.width
+            verified = min(nodes - 1, plan.budget)
+            if self.forced_tree is not None:
+                toks, pars = self.forced_tree(st.rounds, len(out))
+                self.set_forced_tree(toks, pars)
+                forced_active = True
+                verified = len(toks) - 1
+            acc = self.tree_round(plan.max_depth, plan.width, plan.budget)
+            dt = time.perf_counter() - ta
+            st.t_verify += dt
+            st.round_ms_device.append(self.last_round_ms())
+            st.rounds += 1
+            st.accepted.append(len(acc) - 1)
+            st.drafted.append(verified)
+            st.depths.append(plan.max_depth)
+            self.policy.observe(len(acc) - 1, verified, plan.max_depth, 0.0, dt)
+            for tok in acc:
+                out.append(tok)
+                if tok in eos or len(out) >= max_new_tokens:
+                    break
+            n += len(acc)
+            x_n = out[-1]
+        if forced_active:
+            self.set_forced_tree(None)
         st.t_total = time.perf_counter() - t0
         st.new_tokens = len(out)
         return out, st
