@@ -56,6 +56,8 @@ def parse():
                          "ctx 2048, k = 1..8, 16k and full heads (writes the cost file with --costs-out); "
                          "c4: Qwen3-4B sampled round at T = 1.0; c5: batched tree verification + compaction")
     ap.add_argument("--costs-out", default=None, help="c2: write the measured cost file (CostAwareChain.from_costs)")
+    ap.add_argument("--tree", default=None, help="c3: time device tree rounds of shape D,W,B (e.g. 3,3,8) on forced "
+                                                 "trees accepting 2 drafts per round instead of chain rounds")
     ap.add_argument("--c5-layers", type=int, default=0,
                     help="c5: target layers (0 = the config's 28; fewer for profiler captures of the same launches)")
     ap.add_argument("--c5-requests", type=int, default=64, help="c5: requests per GPU")
@@ -496,6 +498,77 @@ def profile_mode(a):
     print(json.dumps({"profile_rounds": a.profile_rounds, "last_round_ms": dec.last_round_ms()}), flush=True)
 
 
+# ----------------------------------------------------------------------------- C3 with draft trees
+
+def forced_tree(ar, e, vocab):
+    """An 8-node depth-3 draft tree over the greedy continuation A = ar[e:]: root children
+    [A0+1, A0, A0+2], under A0 [A1+1, A1], under A0+1 [A1], under A1 [A2+1, A2+2]. The
+    second child of the root and of A0 match, so the round accepts A0, A1 and emits A2."""
+    A = [ar[min(e + j, len(ar) - 1)] for j in range(3)]
+    toks = [0, (A[0] + 1) % vocab, A[0], (A[0] + 2) % vocab, (A[1] + 1) % vocab, A[1], A[1],
+            (A[2] + 1) % vocab, (A[2] + 2) % vocab]
+    pars = [-1, 0, 0, 0, 2, 2, 1, 5, 5]
+    return toks, pars
+
+
+def bench_tree(a):
+    """C3 shapes with draft trees: device tree rounds (one graph per shape, one sync per round) of
+    StaticPolicy(D, W, B) verifying forced 8-node trees (accept 2, emit 3 per round, as the chain
+    line's oracle-drafter mode); the drafter runs over every internal node of the tree."""
+    import torch
+
+    from woodcock_b200 import SpeculativeDecoder, StaticPolicy, generate_autoregressive
+    from woodcock_b200 import synthetic as syn
+
+    D, W, B = (int(x) for x in a.tree.split(","))
+    torch.cuda.set_device(0)
+    t, d = build_models(0)
+    ts = syn.Q17_TARGET
+    dec = SpeculativeDecoder(t, d, StaticPolicy(D, W, B), max_context=PROMPT_LEN + NEW_TOKENS + 64)
+    streams = []
+    for seed in range(3):
+        prompt = syn.prompt_ids(PROMPT_LEN, ts.vocab, seed=2000 + seed)
+        ar, _ = generate_autoregressive(t, prompt, NEW_TOKENS + 8, stop_on_eos=False,
+                                        max_context=PROMPT_LEN + NEW_TOKENS + 64)
+        streams.append((prompt, ar))
+
+    def run(n_rounds, g0):
+        ms, g, done, ok = [], g0, 0, 0
+        while done < n_rounds:
+            prompt, ar = streams[g % len(streams)]
+            dec.prefill(prompt)
+            e = 1
+            while e + 3 <= NEW_TOKENS and done < n_rounds:
+                dec.set_forced_tree(*forced_tree(ar, e, ts.vocab))
+                toks = dec.tree_round(D, W, B)
+                ms.append(dec.last_round_ms())
+                ok += toks == ar[e : e + len(toks)]
+                e += len(toks)
+                done += 1
+            g += 1
+        return ms, g, ok
+
+    _, g, _ = run(a.warmup, 0)
+    torch.cuda.synchronize()
+    with ClockSampler(0) as clk:
+        ms, _, ok = run(a.steps, g)
+        torch.cuda.synchronize()
+    dec.set_forced_tree(None)
+    line = {"metric": METRIC + " (draft-tree rounds)", "value": 3 * len(ms) / (sum(ms) / 1e3), "unit": "tok/s",
+            "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": statistics.mean(ms),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded random-init Qwen3-1.7B-architecture weights, uniform-random prompt ids",
+            "config": {"workload": f"C3 shapes, device tree rounds StaticPolicy({D},{W},{B}), forced 8-node "
+                                   f"depth-3 trees accepting 2 drafts (9 verify rows)", "tree": [D, W, B],
+                       "tokens_per_round": 3, "prompt_tokens": PROMPT_LEN},
+            "round_ms": {"mean": statistics.mean(ms), "median": statistics.median(ms)},
+            "greedy_check": {"rounds_equal_to_autoregressive": ok, "rounds": len(ms)},
+            "clocks": clk.summary()}
+    print(json.dumps(line), flush=True)
+    if a.out:
+        Path(a.out).write_text(json.dumps(line) + "\n")
+
+
 # ----------------------------------------------------------------------------- C2: drafter micro-bench
 
 def bench_c2(a):
@@ -901,6 +974,8 @@ def main():
         profile_mode(a)
     elif a.impl == "reference":
         bench_reference(a)
+    elif a.tree:
+        bench_tree(a)
     elif a.workload == "c2":
         bench_c2(a)
     elif a.workload == "c4":

@@ -102,3 +102,28 @@ def test_sampled_tree_follows_the_oracle_on_one_philox_stream(tiny_models, c1_mo
         prompt64, 24, O.SamplingParams(temperature=0.8, seed=5), stop_on_eos=False, rng=O.Tape(5))
     assert out == ref
     assert st.accepted == rst.accepted
+
+
+def test_policy_with_host_hooks_runs_synced_rounds(golden, c1_models, prompt64):
+    """A policy that is not a StaticPolicy (its hooks may need the host between levels) takes the
+    host-driven rounds; with the static tree:3,3,8 rules it reproduces the reference's run."""
+    from woodcock_b200 import Policy, SpeculativeDecoder, StaticPolicy
+
+    class HookedTree(Policy):
+        def __init__(self):
+            self.inner = StaticPolicy(3, 3, 8)
+            self.seen = 0
+
+        def plan(self, context_len, stochastic):
+            return self.inner.plan(context_len, stochastic)
+
+        def select_verify(self, nodes, context_len, stochastic):
+            self.seen += 1
+            return self.inner.select_verify(nodes, context_len, stochastic)
+
+    g = golden("c1u")
+    t, d = c1_models["c1u"]
+    pol = HookedTree()
+    out, st = SpeculativeDecoder(t, d, pol, max_context=512).generate(prompt64, 64)
+    assert out == g["spec_tree:3,3,8"]["tokens"][:64]
+    assert not st.fused and pol.seen == st.rounds

@@ -480,6 +480,7 @@ struct RowNormParams {
   const float* w;
   float eps;
   uint16_t* out;
+  int ld_out;         // row stride of out (0 = H); lets several normalised blocks share one row
   int M;
   int* err;
 };
@@ -519,7 +520,7 @@ __global__ void __launch_bounds__(256) row_norm_bf16_kernel(__grid_constant__ co
   const float inv = s_inv;
   for (int k = threadIdx.x; k < p.H; k += blockDim.x) {
     const float v = trow ? bf16_bits_to_f32(trow[k]) : x[k];
-    p.out[size_t(m) * p.H + k] = f32_to_bf16_bits(v * inv * (p.w ? p.w[k] : 1.f));
+    p.out[size_t(m) * (p.ld_out ? p.ld_out : p.H) + k] = f32_to_bf16_bits(v * inv * (p.w ? p.w[k] : 1.f));
   }
 }
 

@@ -23,8 +23,9 @@
 // and continue with the next unit, so the cross-warp reduction and the epilogue's global
 // traffic overlap the weight stream.
 //
-// Three instances: the default (64 KB activation chunk, up to 2048 columns at 8 rows); the
-// wide one (80 KB chunk, 7-stage ring: K up to 2560 without splitting); and the streamed
+// Four instances: the default (64 KB activation chunk, up to 2048 columns at 8 rows); the
+// wide one (80 KB chunk, 7-stage ring: K up to 2560 without splitting) and its 16-row form
+// (128 KB chunk, 3-stage ring: K up to 2048 at 9-16 rows); and the streamed
 // one (ACS: whole K in one block for projections with at most one unit per SM, the
 // activation streamed in 16 KB pieces through a 4-deep ring beside the weight slab each
 // piece multiplies). Otherwise, when K exceeds the chunk, K is split: the blocks of one row
@@ -75,6 +76,11 @@ __host__ __device__ constexpr int gv_chunk_slabs(int NT) { return GV_ACT_BYTES /
 // width) in 80 KB, with a 7-stage weight ring, so those projections need not split K.
 constexpr int GV_WIDE_ACT_BYTES = 80 * 1024;
 constexpr int GV_WIDE_SLABS = GV_WIDE_ACT_BYTES / GV_STAGE_BYTES;
+// The wide instance at 16 rows: a 4-slab chunk (K up to 2048 for both n-tiles) in 128 KB beside a
+// 3-stage weight ring, so the 9-16-row verifies (chains of 8 and more, draft trees) do not split
+// the hidden-width projections and split the 6144-wide ones in 3 instead of 6.
+constexpr int GV_WIDE2_ACT_BYTES = 128 * 1024;
+constexpr int GV_WIDE2_SLABS = GV_WIDE2_ACT_BYTES / (2 * GV_STAGE_BYTES);
 
 // Fragment width of an input of K columns: bf16 models pad to whole ring slabs.
 __host__ __device__ inline int xf_width(bool bf16, int K) { return bf16 ? (K + GV_COLS - 1) / GV_COLS * GV_COLS : K; }
@@ -431,8 +437,8 @@ __device__ void gemv_prologue_fast(const GemvParams& p, int L, int* s_tok, float
 // Shared-memory carve-up of the bf16 kernel (byte offsets, every region 16-byte aligned).
 template <int NT, bool WIDE = false>
 struct GvLayout {
-  static constexpr int NS = WIDE ? gv_nstage(NT) - 1 : gv_nstage(NT);
-  static constexpr int ACT_BYTES = WIDE ? GV_WIDE_ACT_BYTES : GV_ACT_BYTES;
+  static constexpr int NS = WIDE ? (NT == 1 ? gv_nstage(NT) - 1 : 3) : gv_nstage(NT);
+  static constexpr int ACT_BYTES = WIDE ? (NT == 1 ? GV_WIDE_ACT_BYTES : GV_WIDE2_ACT_BYTES) : GV_ACT_BYTES;
   static constexpr int CHS = ACT_BYTES / (GV_STAGE_BYTES * NT);            // slabs per activation chunk
   static constexpr size_t ring = 0;                                        // NS x 16 KB weight slabs
   static constexpr size_t act = ring + size_t(NS) * GV_STAGE_BYTES;        // [NT][CHS][32 kt][32 lanes] uint4
@@ -458,7 +464,7 @@ struct GvLayout {
 // hand-off overlap the weight stream instead of stalling it.
 template <int NT, bool ACS = false, bool WIDE = false>
 __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constant__ const GemvParams pk) {
-  static_assert(!(ACS && WIDE) && (!WIDE || NT == 1), "kernel instances: ACS and WIDE are 8-row, exclusive");
+  static_assert(!(ACS && WIDE) && (!ACS || NT == 1), "kernel instances: ACS is 8-row, ACS and WIDE exclusive");
   using Lay = GvLayout<NT, WIDE>;
   constexpr int NS = Lay::NS;
   constexpr int CHS = Lay::CHS;

@@ -108,8 +108,9 @@ struct wc_ctx {
   size_t max_smem = 0;
   Profiler* prof = nullptr;  // set while a profiled round is being captured
   bool pdl = true;           // programmatic dependent launch between round kernels
-  int attn_mode = 2;         // bf16 caches: 2 split-sequence kernel (attention_split.cuh), 4 the
-                             // cluster kernel (attention_dec.cuh), 1 split-KV mma kernel, 0 CUDA cores
+  int attn_mode = 4;         // bf16 caches: 4 the cluster kernel (attention_dec.cuh), 2 the
+                             // split-sequence kernel (attention_split.cuh; always used for drafted
+                             // tree levels), 1 split-KV mma kernel, 0 CUDA cores
   float* as_part_o = nullptr;   // attention_split partial states: [16 KV heads][AS_MAXS + 1][AS_MAXR][128]
   float* as_part_ml = nullptr;  //   and their (m, l): [16][AS_MAXS + 1][AS_MAXR][2]
   int* as_counters = nullptr;   //   per-KV-head arrivals (zero between launches)
@@ -527,10 +528,12 @@ GemvPlan gemv_plan(const wc_ctx* ctx, const Lin& W, int L_max) {
     return g;
   }
   const int NT = L_max <= 8 ? 1 : 2;
-  const int chs = gv_chunk_slabs(NT);
+  const bool wide2 = NT == 2 && ctx->gemv_wide;  // 16 rows: the 128 KB chunk (K to 2048 unsplit)
+  const int chs = wide2 ? GV_WIDE2_SLABS : gv_chunk_slabs(NT);
   const int nslab = W.Kp / GV_COLS;
   const int nunits = W.Np / (16 * W.group);
   g.nkc = (nslab + chs - 1) / chs;
+  g.wide = wide2;
   if (NT == 1 && g.nkc > 1 && nslab <= GV_WIDE_SLABS && ctx->gemv_wide) {  // K up to 2560: no split
     g.nkc = 1;
     g.wide = true;
@@ -614,7 +617,8 @@ void launch_gemv(wc_ctx* ctx, const Lin& W, GemvParams p) {
     p.nkc = g.nkc;
     p.kc_slabs = g.kc_slabs;
     p.gpk = g.gpk;
-    if (!p.acs && g.kc_slabs > (g.wide ? GV_WIDE_SLABS : gv_chunk_slabs(p.L_max <= 8 ? 1 : 2)))
+    const bool nt2 = p.L_max > 8;
+    if (!p.acs && g.kc_slabs > (g.wide ? (nt2 ? GV_WIDE2_SLABS : GV_WIDE_SLABS) : gv_chunk_slabs(nt2 ? 2 : 1)))
       fail(WC_ERR_INVALID, "GEMV chunk above the buffer");
     if (g.nkc > 1) {
       if (size_t(g.nkc) * (W.Np / 16) * 256 > ctx->gv_partial_n || g.gpk > ctx->gv_counters_n)
@@ -625,6 +629,9 @@ void launch_gemv(wc_ctx* ctx, const Lin& W, GemvParams p) {
     if (p.acs)
       launch_ex(ctx, "gemv", gemv_bf16_kernel<1, true>, dim3(g.grid), dim3(GV_THREADS), gemv_bf16_smem<1>(), true, 1,
                 p);
+    else if (g.wide && nt2)
+      launch_ex(ctx, "gemv", gemv_bf16_kernel<2, false, true>, dim3(g.grid), dim3(GV_THREADS),
+                gemv_bf16_smem<2, true>(), true, 1, p);
     else if (g.wide)
       launch_ex(ctx, "gemv", gemv_bf16_kernel<1, false, true>, dim3(g.grid), dim3(GV_THREADS),
                 gemv_bf16_smem<1, true>(), true, 1, p);
@@ -668,11 +675,12 @@ void launch_attention(wc_ctx* ctx, AttnParams p) {
     fail(WC_ERR_INVALID, "attention inputs must be 16-byte aligned with 16-byte row strides");
   if (p.xf_out) p.xf_width = xf_width(!p.xf_fp32, p.H * p.D);
   // tensor-core paths: bf16 cache, rule-based visibility, new rows appended by the kernel
-  if (p.mask_from_prefix && p.kv_dtype == WC_BF16 && ctx->attn_mode != 2)
-    fail(WC_ERR_UNSUPPORTED, "tree-level masks need the split decode attention (WC_ATTN=2)");
   const bool tc_ok = !p.q_ready && !p.mask_full && p.kv_dtype == WC_BF16 && p.write_cache &&
                      (p.D == 128 || p.D == 64) && p.L_max * rep <= AM_MAXR && p.stride_p == p.D;
-  if (tc_ok && ctx->attn_mode == 2 && p.L_max <= AS_MAXL && p.L_max * rep <= AS_MAXR && p.Hk <= 16) {
+  // drafted tree levels (mask bits from the committed length) take the split kernel in every mode
+  const bool split_ok = tc_ok && p.L_max <= AS_MAXL && p.L_max * rep <= AS_MAXR && p.Hk <= 16;
+  if (p.mask_from_prefix && tc_ok && !split_ok) fail(WC_ERR_UNSUPPORTED, "tree level too wide for the decode attention");
+  if (split_ok && (ctx->attn_mode == 2 || p.mask_from_prefix)) {
     AttnSplitParams sp;
     std::memset(&sp, 0, sizeof(sp));
     sp.a = p;
@@ -784,6 +792,8 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
     CUDA_TRY(cudaFuncSetAttribute(gemv_bf16_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(gemv_bf16_kernel<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(gemv_bf16_kernel<1, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  smax));
+    CUDA_TRY(cudaFuncSetAttribute(gemv_bf16_kernel<2, false, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                   smax));
     CUDA_TRY(cudaFuncSetAttribute(gemv_f32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
@@ -1860,6 +1870,8 @@ struct DLayer {
 };
 }  // namespace
 
+struct DrafterGemm;
+
 struct wc_drafter {
   wc_ctx* ctx;
   wc_drafter_config cfg;
@@ -1884,6 +1896,7 @@ struct wc_drafter {
   float *ss_feat = nullptr, *ss_g = nullptr, *ss_pack = nullptr;
   float* ss_tap[3] = {nullptr, nullptr, nullptr};
   unsigned long long* ws_keys = nullptr;
+  DrafterGemm* pg = nullptr;  // tensor-core prompt pass (row-major weight copies), made on first use
 };
 
 namespace {
@@ -2288,9 +2301,14 @@ extern "C" wc_status wc_drafter_load(wc_ctx* ctx, const char* dir, int dtype, wc
   });
 }
 
+namespace {
+void drafter_gemm_free(wc_drafter* d);
+}  // namespace
+
 extern "C" void wc_drafter_destroy(wc_drafter* d) {
   if (!d) return;
   cudaStreamSynchronize(d->ctx->stream);
+  drafter_gemm_free(d);
   dfree(d->embed);
   dfree(d->aux_inv);
   free_lin(d->fc);
@@ -2461,6 +2479,12 @@ namespace {
 // norm), or nullptr when the target cannot take this path (the caller then runs the decode
 // kernels). Defined with the batched verification.
 const float* prefill_gemm_forward(wc_target* t, wc_kv* kv, const int* tokens_dev, int n, int start, const TapOut* to);
+// The drafter's prompt pass the same way (fuse, then every layer as tcgen05 GEMMs over all rows,
+// causal attention, K/V appended to `kv` after `start`): tokens_dev[n] are the entries' tokens,
+// taps [3][n][target hidden] (tap f at + f * tstride) their features. Returns the last row's
+// residual before the final norm, or nullptr when the drafter cannot take this path.
+const float* drafter_prefill_gemm(wc_drafter* d, wc_kv* kv, const int* tokens_dev, int n, int start,
+                                  const float* taps, size_t tstride);
 }  // namespace
 
 // ============================================================================ sampled decoding
@@ -2577,14 +2601,14 @@ constexpr int kAcceptBlocks = 148;      // acceptance draw: one slice of the voc
 constexpr int kStatsSlice = 4096;       // logits per softmax slice
 constexpr int kSampledGraphKey = 1000;  // graph key offset of sampled rounds
 
-void launch_finish(wc_decoder* dec, const int* L_dev, int L_static, bool advance) {
+void launch_finish(wc_decoder* dec, const int* L_dev, int L_static, bool advance, const float* h = nullptr) {
   wc_drafter* d = dec->d;
   FinishParams f;
   std::memset(&f, 0, sizeof(f));
   f.st = dec->st;
   f.L_dev = L_dev;
   f.L_static = L_static;
-  f.h = d->ws_h;
+  f.h = h ? h : d->ws_h;
   f.d = d->cfg.hidden;
   f.norm_w = d->norm;
   f.eps = d->cfg.eps;
@@ -3150,7 +3174,9 @@ int decoder_prefill_impl(wc_decoder* dec, const int* prompt, int n, const wc_sam
   // drafter entries e = (token x_{e+1}, feature at e) for e = 0..n-1
   CUDA_TRY(cudaMemcpyAsync(d_tok, prompt + 1, sizeof(int) * (n - 1), cudaMemcpyHostToDevice, ctx->stream));
   CUDA_TRY(cudaMemcpyAsync(d_tok + n - 1, &first, sizeof(int), cudaMemcpyHostToDevice, ctx->stream));
-  for (int r0 = 0; r0 < n; r0 += GEMV_MAXL) {
+  const float* dlast = drafter_prefill_gemm(d, dec->dkv, d_tok, n, 0, dec->taps, tstride);
+  if (dlast) launch_finish(dec, nullptr, 1, false, dlast);
+  for (int r0 = 0; r0 < n && !dlast; r0 += GEMV_MAXL) {
     const int rows = std::min(GEMV_MAXL, n - r0);
     XIn tx[3];
     drafter_pack_taps(d, dec->taps + size_t(r0) * Ht, tstride, Ht, rows, tx, err);
@@ -3725,7 +3751,11 @@ struct TcWeight {
 
 TcWeight tc_weight_from(wc_ctx* ctx, const Lin& l, int BN) {
   if (l.dtype != WC_BF16) fail(WC_ERR_UNSUPPORTED, "batched verification needs a bf16 target");
-  if (l.nseg != 1 || l.Kp % TC_BK) fail(WC_ERR_UNSUPPORTED, "GEMM weight: one input segment, K a multiple of 64");
+  // several input segments read as one K when none of them is padded (the tiled layout is then
+  // the same as one segment's)
+  for (int sg = 0; sg < l.nseg; ++sg)
+    if (l.seg_len[sg] % GV_COLS) fail(WC_ERR_UNSUPPORTED, "GEMM weight: a padded input segment");
+  if (l.Kp % TC_BK) fail(WC_ERR_UNSUPPORTED, "GEMM weight: K a multiple of 64");
   TcWeight t;
   t.rows = l.group == 2 ? 2 * l.N : l.N;
   t.K = l.Kp;
@@ -4088,6 +4118,205 @@ const float* prefill_gemm_forward(wc_target* t, wc_kv* kv, const int* tokens_dev
     batch_forward(b, 1, rows, false, true, &tc, false);
   }
   return b->h + size_t(rows - 1) * H;
+}
+
+}  // namespace
+
+struct DrafterGemm {
+  std::vector<TcWeight> qkv, o, gu, down;
+  TcWeight fc;
+  int M = 0;
+  float *h = nullptr, *qkv_out = nullptr;
+  uint16_t *ab = nullptr, *a = nullptr, *q = nullptr, *att = nullptr, *act = nullptr;
+  int *lens = nullptr, *dep = nullptr;
+};
+
+namespace {
+
+void drafter_gemm_free(wc_drafter* d) {
+  DrafterGemm* g = d->pg;
+  if (!g) return;
+  auto drop = [](TcWeight& w) { dfree(w.w); };
+  drop(g->fc);
+  for (auto* v : {&g->qkv, &g->o, &g->gu, &g->down})
+    for (auto& w : *v) drop(w);
+  for (void* p : {(void*)g->h, (void*)g->qkv_out, (void*)g->ab, (void*)g->a, (void*)g->q, (void*)g->att,
+                  (void*)g->act, (void*)g->lens, (void*)g->dep})
+    dfree(p);
+  delete g;
+  d->pg = nullptr;
+}
+
+bool drafter_gemm_ok(const wc_drafter* d) {
+  static const bool on = [] {
+    const char* e = std::getenv("WC_PREFILL_GEMM");
+    return !e || std::atoi(e) != 0;
+  }();
+  const auto& c = d->cfg;
+  return on && d->dtype == WC_BF16 && (c.head_dim == 128 || c.head_dim == 64) && c.window == 0 &&
+         c.num_features == 3 && c.hidden % GV_COLS == 0 && c.target_hidden % GV_COLS == 0 &&
+         c.intermediate % 128 == 0 && (c.heads * c.head_dim) % TC_BK == 0 && c.heads / c.kv_heads <= TA_MAXR;
+}
+
+const float* drafter_prefill_gemm(wc_drafter* d, wc_kv* kv, const int* tokens_dev, int n, int start,
+                                  const float* taps, size_t tstride) {
+  if (!drafter_gemm_ok(d) || kv->dtype != WC_BF16 || n < 1) return nullptr;
+  wc_ctx* ctx = d->ctx;
+  if (!tc_ready(ctx)) return nullptr;
+  if (start + n > kv->cap) fail(WC_ERR_CAPACITY, "prompt longer than the drafter cache");
+  const auto& c = d->cfg;
+  const int H = c.hidden, Ht = c.target_hidden, D = c.head_dim, Hq = c.heads, Hk = c.kv_heads, I = c.intermediate;
+  const int NQKV = (Hq + 2 * Hk) * D, rep = Hq / Hk;
+  if (!d->pg) {  // row-major weight copies (made from the GEMV tiles) and activations for 1024 rows
+    auto g = new DrafterGemm();
+    d->pg = g;
+    g->fc = tc_weight_from(ctx, d->fc, 128);
+    for (const DLayer& Ly : d->layers) {
+      g->qkv.push_back(tc_weight_from(ctx, Ly.qkv, 256));
+      g->o.push_back(tc_weight_from(ctx, Ly.o, 128));
+      g->gu.push_back(tc_weight_from(ctx, Ly.gu, 256));
+      g->down.push_back(tc_weight_from(ctx, Ly.down, 128));
+    }
+    const int M = kPrefillChunk;
+    g->M = M;
+    g->h = static_cast<float*>(dalloc(sizeof(float) * size_t(M) * H));
+    g->qkv_out = static_cast<float*>(dalloc(sizeof(float) * size_t(M) * NQKV));
+    g->ab = static_cast<uint16_t*>(dalloc(2 * size_t(M) * 3 * Ht));
+    g->a = static_cast<uint16_t*>(dalloc(2 * size_t(M) * 2 * H));
+    g->q = static_cast<uint16_t*>(dalloc(2 * size_t(M) * Hq * D));
+    g->att = static_cast<uint16_t*>(dalloc(2 * size_t(M) * Hq * D));
+    g->act = static_cast<uint16_t*>(dalloc(2 * size_t(M) * I));
+    g->lens = static_cast<int*>(dalloc(sizeof(int)));
+    g->dep = static_cast<int*>(dalloc(sizeof(int) * M));
+    iota_kernel<<<(M + 255) / 256, 256, 0, ctx->stream>>>(g->dep, M);
+    check_launch(ctx, "iota");
+  }
+  DrafterGemm* g = d->pg;
+  int* err = ctx->d_err;
+  const size_t kv_layer = kv->layer_elems();
+  int rows = 0;
+  for (int r0 = 0; r0 < n; r0 += g->M) {
+    rows = std::min(g->M, n - r0);
+    const int M = rows;
+    const int len = start + r0;
+    CUDA_TRY(cudaMemcpyAsync(g->lens, &len, sizeof(int), cudaMemcpyHostToDevice, ctx->stream));
+    // fuse (drafter.cpp:75-89): per-tap RMSNorm into one [M][3 Ht] row block, then fc
+    RowNormParams rn;
+    std::memset(&rn, 0, sizeof(rn));
+    rn.H = Ht;
+    rn.eps = c.eps;
+    rn.M = M;
+    rn.ld_out = 3 * Ht;
+    rn.err = err;
+    for (int f = 0; f < 3; ++f) {
+      rn.x = taps + f * tstride + size_t(r0) * Ht;
+      rn.w = c.feature_norm ? d->feature_norms[f] : nullptr;
+      rn.out = g->ab + size_t(f) * Ht;
+      if (!c.feature_norm) fail(WC_ERR_UNSUPPORTED, "tensor-core drafter prefill needs the feature norms");
+      launch_ex(ctx, "row norm", row_norm_bf16_kernel, dim3(M), dim3(256), 0, true, 1, rn);
+    }
+    GemmTc gm = gemm_tc_params(M, H, 3 * Ht, TC_STORE);
+    gm.c = g->h;
+    gm.ldc = H;
+    launch_gemm_tc(ctx, tmap_bf16(g->ab, M, 3 * Ht, TC_BM), g->fc.map, gm, g->fc.BN);
+    for (size_t li = 0; li < d->layers.size(); ++li) {
+      const DLayer& Ly = d->layers[li];
+      const bool aux = Ly.aux_norm != nullptr;
+      const int Kq = aux ? 2 * H : H;
+      std::memset(&rn, 0, sizeof(rn));
+      rn.x = g->h;
+      rn.H = H;
+      rn.w = Ly.in_norm;
+      rn.eps = c.eps;
+      rn.out = g->a;
+      rn.ld_out = Kq;
+      rn.M = M;
+      rn.err = err;
+      launch_ex(ctx, "row norm", row_norm_bf16_kernel, dim3(M), dim3(256), 0, true, 1, rn);
+      if (aux) {  // the token embedding's auxiliary term beside it (drafter.cpp:110-116)
+        rn.x = nullptr;
+        rn.tokens = tokens_dev + r0;
+        rn.table = d->embed;
+        rn.vocab = c.vocab;
+        rn.w = Ly.aux_norm;
+        rn.out = g->a + H;
+        launch_ex(ctx, "row norm", row_norm_bf16_kernel, dim3(M), dim3(256), 0, true, 1, rn);
+      }
+      gm = gemm_tc_params(M, NQKV, Kq, TC_STORE);
+      gm.c = g->qkv_out;
+      gm.ldc = NQKV;
+      launch_gemm_tc(ctx, tmap_bf16(g->a, M, Kq, TC_BM), g->qkv[li].map, gm, g->qkv[li].BN);
+      QkvPostParams qp;
+      std::memset(&qp, 0, sizeof(qp));
+      qp.qkv = g->qkv_out;
+      qp.nodes = M;
+      qp.Hq = Hq;
+      qp.Hk = Hk;
+      qp.D = D;
+      qp.lens = g->lens;
+      qp.depth = g->dep;
+      qp.q_norm = Ly.q_norm;
+      qp.k_norm = Ly.k_norm;
+      qp.eps = c.eps;
+      qp.rope = d->rope->ptr;
+      qp.max_pos = d->rope->max_pos;
+      qp.q = g->q;
+      qp.K = static_cast<uint16_t*>(kv->K) + li * kv_layer;
+      qp.V = static_cast<uint16_t*>(kv->V) + li * kv_layer;
+      qp.cap = kv->cap;
+      qp.err = err;
+      launch_ex(ctx, "qkv post", qkv_post_kernel, dim3(M), dim3(128), 0, true, 1, qp);
+      TreeAttnParams ap;
+      std::memset(&ap, 0, sizeof(ap));
+      ap.q = g->q;
+      ap.K = qp.K;
+      ap.V = qp.V;
+      ap.cap = kv->cap;
+      ap.lens = g->lens;
+      ap.parents = g->dep;  // unused in causal mode
+      ap.nodes = M;
+      ap.Hq = Hq;
+      ap.Hk = Hk;
+      ap.scale = 1.f / std::sqrt(float(D));
+      ap.out = g->att;
+      ap.nsplit = 1;
+      ap.causal = 1;
+      ap.err = err;
+      const int gz = (M + TA_MAXR / rep - 1) / (TA_MAXR / rep);
+      if (D == 128)
+        launch_ex(ctx, "tree attention", tree_attention_kernel<128>, dim3(1, Hk, gz), dim3(TA_THREADS),
+                  tree_attn_smem<128>(), true, 1, ap);
+      else
+        launch_ex(ctx, "tree attention", tree_attention_kernel<64>, dim3(1, Hk, gz), dim3(TA_THREADS),
+                  tree_attn_smem<64>(), true, 1, ap);
+      gm = gemm_tc_params(M, H, Hq * D, TC_ADD);
+      gm.c = g->h;
+      gm.ldc = H;
+      gm.r = g->h;
+      gm.ldr = H;
+      launch_gemm_tc(ctx, tmap_bf16(g->att, M, Hq * D, TC_BM), g->o[li].map, gm, g->o[li].BN);
+      std::memset(&rn, 0, sizeof(rn));
+      rn.x = g->h;
+      rn.H = H;
+      rn.w = Ly.post_norm;
+      rn.eps = c.eps;
+      rn.out = g->a;
+      rn.M = M;
+      rn.err = err;
+      launch_ex(ctx, "row norm", row_norm_bf16_kernel, dim3(M), dim3(256), 0, true, 1, rn);
+      gm = gemm_tc_params(M, 2 * I, H, TC_SWIGLU);
+      gm.cb = g->act;
+      gm.ldcb = I;
+      launch_gemm_tc(ctx, tmap_bf16(g->a, M, H, TC_BM), g->gu[li].map, gm, g->gu[li].BN);
+      gm = gemm_tc_params(M, H, I, TC_ADD);
+      gm.c = g->h;
+      gm.ldc = H;
+      gm.r = g->h;
+      gm.ldr = H;
+      launch_gemm_tc(ctx, tmap_bf16(g->act, M, I, TC_BM), g->down[li].map, gm, g->down[li].BN);
+    }
+  }
+  return g->h + size_t(rows - 1) * H;
 }
 
 }  // namespace

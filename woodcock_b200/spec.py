@@ -308,16 +308,16 @@ class SpeculativeDecoder:
 
     def _generate_host(self, prompt: list[int], max_new_tokens: int, sp: SamplingParams,
                        stop_on_eos: bool) -> tuple[list[int], GenStats]:
-        """Draft trees (any policy) and fused=False: host-driven rounds over the device API
-        (woodcock_b200.tree), one synchronisation per drafted level as in the reference."""
+        """Sampled trees and policies with host-side hooks: host-driven rounds over the device API
+        (woodcock_b200.synced), one synchronisation per drafted level as in the reference."""
         from .sampling import PhiloxStream
-        from .tree import HostRounds
+        from .synced import SyncedRounds
 
         st = GenStats(prompt_tokens=len(prompt), fused=False)
         rng = PhiloxStream(sp.seed, device=self.ctx.device.index or 0)
         eos = self.t.eos_token_ids if stop_on_eos else set()
         t0 = time.perf_counter()
-        hr = HostRounds(self.t, self.d, self.policy, self.max_context + 256)
+        hr = SyncedRounds(self.t, self.d, self.policy, self.max_context + 256)
         x_n = hr.prefill(prompt, sp, rng)
         st.t_prefill = time.perf_counter() - t0
         out = [x_n]
