@@ -61,6 +61,11 @@ WC_API const char* wc_last_error(const wc_ctx* ctx);
 WC_API wc_status wc_ctx_synchronize(wc_ctx* ctx);
 /* number of kernels this context launched since creation (graph replays count each kernel) */
 WC_API uint64_t wc_ctx_launch_count(const wc_ctx* ctx);
+/* Test support, no counterpart in the reference: launches a kernel whose bounded wait (the helper
+ * every pipelined kernel uses) can never be satisfied and gives up after `iterations` tries
+ * (1..2^20), raising the timeout bit of the device error word; the next wc_ctx_synchronize then
+ * returns WC_ERR_DEVICE and clears the word, and the context stays usable. */
+WC_API wc_status wc_ctx_wait_selftest(wc_ctx* ctx, int iterations);
 
 /* ------------------------------------------------------------------ backend ops
  * Device-pointer counterparts of woodcock::ops (include/woodcock/ops.h:11-22,

@@ -217,6 +217,26 @@ class SafetensorsFile {
     void* m = mmap(nullptr, size_, PROT_READ, MAP_PRIVATE, fd_, 0);
     if (m == MAP_FAILED) throw std::runtime_error("mmap failed for " + path);
     base_ = static_cast<const uint8_t*>(m);
+    try {
+      parse(path);
+    } catch (...) {  // the destructor does not run for a throwing constructor
+      munmap(const_cast<uint8_t*>(base_), size_);
+      ::close(fd_);
+      base_ = nullptr;
+      fd_ = -1;
+      throw;
+    }
+  }
+  ~SafetensorsFile() {
+    if (base_) munmap(const_cast<uint8_t*>(base_), size_);
+    if (fd_ >= 0) ::close(fd_);
+  }
+  SafetensorsFile(const SafetensorsFile&) = delete;
+  SafetensorsFile& operator=(const SafetensorsFile&) = delete;
+  const std::map<std::string, TensorView>& tensors() const { return tensors_; }
+
+ private:
+  void parse(const std::string& path) {
     uint64_t hlen = 0;
     std::memcpy(&hlen, base_, 8);
     if (hlen > size_ - 8) throw std::runtime_error("corrupt safetensors header length in " + path);
@@ -239,15 +259,7 @@ class SafetensorsFile {
       tensors_[kv.first] = t;
     }
   }
-  ~SafetensorsFile() {
-    if (base_) munmap(const_cast<uint8_t*>(base_), size_);
-    if (fd_ >= 0) ::close(fd_);
-  }
-  SafetensorsFile(const SafetensorsFile&) = delete;
-  SafetensorsFile& operator=(const SafetensorsFile&) = delete;
-  const std::map<std::string, TensorView>& tensors() const { return tensors_; }
 
- private:
   int fd_ = -1;
   size_t size_ = 0;
   const uint8_t* base_ = nullptr;

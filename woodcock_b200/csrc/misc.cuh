@@ -507,6 +507,20 @@ __global__ void philox_uniforms_kernel(uint64_t seed, uint64_t offset, int n, do
   if (i < n) out[i] = philox_uniform(seed, offset + uint64_t(i));
 }
 
+// ----------------------------------------------------------------------------- bounded-wait self test
+// Waits, with the same bounded helper every pipelined kernel uses, on an mbarrier phase that
+// nothing completes: after `iters` tries the wait gives up and the kernel raises kErrTimeout in
+// the error word and returns, which the host reads at its next synchronisation.
+__global__ void wait_selftest_kernel(int* err, uint32_t iters) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    mbar_fence_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && !mbar_wait(&bar, 0, iters)) raise_error(err, kErrTimeout);
+}
+
 // ----------------------------------------------------------------------------- round bookkeeping
 
 // Greedy chain acceptance (python/woodcock/spec.py:357-362): longest prefix of drafts

@@ -879,6 +879,13 @@ extern "C" wc_status wc_ctx_synchronize(wc_ctx* ctx) {
 }
 
 extern "C" uint64_t wc_ctx_launch_count(const wc_ctx* ctx) { return ctx ? ctx->launches : 0; }
+extern "C" wc_status wc_ctx_wait_selftest(wc_ctx* ctx, int iterations) {
+  if (!ctx || iterations < 1 || iterations > (1 << 20)) return WC_ERR_INVALID;
+  return guard(ctx, [&] {
+    wait_selftest_kernel<<<1, 32, 0, ctx->stream>>>(ctx->d_err, uint32_t(iterations));
+    check_launch(ctx, "wait self test");
+  });
+}
 
 // ============================================================================ C ABI: ops
 

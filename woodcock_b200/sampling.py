@@ -97,7 +97,13 @@ def tree_attention_mask(tree: DraftTree, prefix_len: int) -> np.ndarray:
 
 
 def _tree_args(tree: DraftTree, dev):
-    return device_ints(tree.tokens, dev), device_ints(tree.parents, dev)
+    """Device copies of a flattened tree, after checking it: node 0 is the root (parent -1) and
+    every other node's parent precedes it."""
+    par = list(tree.parents)
+    if not par or par[0] != -1 or any(not 0 <= p < v for v, p in enumerate(par) if v > 0) or \
+            len(tree.tokens) != len(par):
+        raise ValueError("malformed draft tree: node 0 must be the root and parents must precede their nodes")
+    return device_ints(tree.tokens, dev), device_ints(par, dev)
 
 
 def verify_tree_greedy(target_argmax, tree: DraftTree, device=0) -> tuple[list[int], int]:

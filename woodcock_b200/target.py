@@ -25,6 +25,16 @@ from .context import Context, device_ints, ptr
 QWEN3_EOS = frozenset({151643, 151645})
 
 
+def _taps_arg(feature_layers):
+    """Three tap layer indices for the C ABI (None = the reference default, target.py:26-33)."""
+    if feature_layers is None:
+        return None
+    taps = [int(x) for x in feature_layers]
+    if len(taps) != 3:
+        raise ValueError(f"the drafter fuses exactly three target layers, got {len(taps)}")
+    return int_array(taps)
+
+
 def default_feature_layers(num_layers: int) -> tuple[int, int, int]:
     """python/woodcock/target.py:26-33."""
     return (2, num_layers // 2, num_layers - 3)
@@ -85,7 +95,7 @@ class Target:
         if dtype is None:
             dtype = _file_dtype(Path(path))
         h = C.c_void_p()
-        taps = int_array(feature_layers) if feature_layers is not None else None
+        taps = _taps_arg(feature_layers)
         ctx.check(lib().wc_target_load(ctx.h, str(path).encode(), taps, dtype_code(dtype), C.byref(h)))
         return cls(h, ctx)
 
@@ -101,7 +111,7 @@ class Target:
                         eps=float(config.get("rms_norm_eps", 1e-6)), rope_theta=float(config.get("rope_theta", 1e6)),
                         tie_embeddings=int(bool(config.get("tie_word_embeddings", False))))
         h = C.c_void_p()
-        taps = int_array(feature_layers) if feature_layers is not None else None
+        taps = _taps_arg(feature_layers)
         ctx.check(lib().wc_target_create(ctx.h, C.byref(c), taps, dtype_code(dtype), C.byref(h)))
         t = cls.__new__(cls)
         try:
