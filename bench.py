@@ -63,6 +63,7 @@ def parse():
     ap.add_argument("--c5-requests", type=int, default=64, help="c5: requests per GPU")
     ap.add_argument("--chi2", type=int, default=0,
                     help="c4: also draw this many first tokens from one replayed state and test their law")
+    ap.add_argument("--chi2-seeds", type=int, default=1, help="c4: independent states (prompts, seeds) to test")
     ap.add_argument("--profile-rounds", type=int, default=0,
                     help="profiling mode for ncu: short prompt, then N rounds inside the NVTX range 'timed'")
     return ap.parse_args()
@@ -661,12 +662,16 @@ def bench_c2(a):
 
 # ----------------------------------------------------------------------------- C4: sampled 4B round
 
-def chi2_equal_mass(counts, p, bins=1000):
-    """Pearson chi-square of token counts against p over `bins` runs of consecutive ids with
-    (near) equal expected mass; returns (statistic, dof, p-value)."""
+def chi2_equal_mass(counts, p, bins=1000, order="id"):
+    """Pearson chi-square of token counts against p over `bins` groups of (near) equal expected
+    mass: consecutive ids (order "id") or tokens in decreasing order of p (order "rank", where a
+    bias that follows the logit collects in the first or last bins); (statistic, dof, p-value)."""
     import numpy as np
     from scipy.stats import chi2
 
+    if order == "rank":
+        perm = np.argsort(-p, kind="stable")
+        counts, p = counts[perm], p[perm]
     n = counts.sum()
     c = np.cumsum(p) / p.sum()
     b = np.unique(np.clip(np.concatenate([[0], np.searchsorted(c, np.arange(1, bins) / bins) + 1, [len(p)]]), 0,
@@ -766,24 +771,33 @@ def bench_c4(a):
     if rank == 0:
         line["clocks"] = clk.summary()
     if a.chi2 and rank == 0:
-        prompt = syn.prompt_ids(prompt_len, ts.vocab, seed=77)
-        dec.prefill(prompt, SamplingParams(temperature=T, seed=77))
-        dec.save_state()
-        counts = np.zeros(ts.vocab)
-        tc0 = time.perf_counter()
-        z0 = None
-        for i in range(a.chi2):
-            dec.restore_state()
-            counts[dec.round(k)[0]] += 1
-            if i == 0:
-                z0 = dec.round_logits(k)["zt"][0].copy()
-        x = (z0 / np.float32(T)).astype(np.float64)
-        pz = np.exp(x - x.max())
-        pz /= pz.sum()
-        stat, dof, pval = chi2_equal_mass(counts, pz)
-        line["chi2_first_token"] = {"samples": a.chi2, "bins": dof + 1, "statistic": stat, "dof": dof,
-                                    "p_value": pval, "pass": pval > 1e-3, "seconds": time.perf_counter() - tc0,
-                                    "law": "softmax(z_0 / T) of the replayed state's target row"}
+        tests = []
+        for j in range(max(1, a.chi2_seeds)):
+            seed = 77 + j
+            prompt = syn.prompt_ids(prompt_len, ts.vocab, seed=seed)
+            dec.prefill(prompt, SamplingParams(temperature=T, seed=seed))
+            dec.save_state()
+            counts = np.zeros(ts.vocab)
+            tc0 = time.perf_counter()
+            z0 = None
+            for i in range(a.chi2):
+                dec.restore_state()
+                counts[dec.round(k)[0]] += 1
+                if i == 0:
+                    z0 = dec.round_logits(k)["zt"][0].copy()
+            x = (z0 / np.float32(T)).astype(np.float64)
+            pz = np.exp(x - x.max())
+            pz /= pz.sum()
+            res = {"seed": seed, "samples": a.chi2, "seconds": time.perf_counter() - tc0}
+            for order in ("id", "rank"):
+                stat, dof, pval = chi2_equal_mass(counts, pz, order=order)
+                res[order] = {"statistic": stat, "dof": dof, "p_value": pval, "pass": pval > 1e-3}
+            tests.append(res)
+            print(json.dumps({"chi2": res}), file=sys.stderr, flush=True)
+        line["chi2_first_token"] = {"law": "softmax(z_0 / T) of each replayed state's target row; 1000 equal-mass "
+                                           "bins over consecutive ids (id) and over tokens ranked by p (rank)",
+                                    "tests": tests,
+                                    "all_pass": all(t[o]["pass"] for t in tests for o in ("id", "rank"))}
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
