@@ -162,6 +162,11 @@ WC_API wc_status wc_drafter_forward(wc_drafter* d, wc_kv* cache, const int* toke
                              const int* positions_dev, const uint8_t* mask_dev, float* hidden_dev, float* out_dev);
 /* drafter.h:49 logits over the head rows (full vocabulary or the restricted rows) for `rows` rows */
 WC_API wc_status wc_drafter_logits(wc_drafter* d, const float* out_dev, int rows, float* z_dev);
+/* The draft distribution (spec.py:113-125 _draft_dist; drafter.py:204-207 logits): softmax(z / T) over the
+ * head rows (the full vocabulary or the restricted rows, in row order) for `rows` rows of drafter output,
+ * into probs [rows][head rows] (device fp32). T > 0; the reference drafts greedily with T = 1. */
+WC_API wc_status wc_drafter_head_softmax(wc_drafter* d, const float* out_dev, int rows, float temperature,
+                                         float* probs_dev);
 /* fused head + argmax; token ids are mapped back through the restricted vocabulary (drafter.py:213-215) */
 WC_API wc_status wc_drafter_head_argmax(wc_drafter* d, const float* out_dev, int rows, int* token_dev);
 
@@ -192,7 +197,8 @@ WC_API wc_status wc_accept_stochastic(wc_ctx* ctx, const double* p_dev, const do
  *  - Nothing in the scratch has to start at zero: each call writes the rows before it reads them.
  *  - The first call on a device looks up the array's device address (cudaGetSymbolAddress), with
  *    the context's device current (otherwise WC_ERR_INVALID). Make that first call before any
- *    stream capture begins.
+ *    stream capture begins (a first call on a capturing stream returns WC_ERR_INVALID). The
+ *    address is kept for the life of the process: a cudaDeviceReset between calls is not supported.
  *  - Every call on one device uses the same array. Two calls that can run at the same time
  *    (different streams, or different contexts on that device) race on it: order them on one
  *    stream, or use wc_accept_stochastic. */

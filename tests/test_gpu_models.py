@@ -125,6 +125,25 @@ def test_drafter_pieces_match_oracle(tiny_models, gpu_models):
     assert d.head_argmax(out).cpu().tolist() == [O.argmax(r) for r in od.logits(out_ref)]
 
 
+@pytest.mark.parametrize("T", [1.0, 0.7])
+def test_drafter_head_softmax_is_the_draft_distribution(tiny_models, T):
+    """wc_drafter_head_softmax: softmax(z / T) of the head rows, full and restricted heads."""
+    from woodcock_b200 import Drafter
+
+    td, dd, _, _ = tiny_models["c1u"]
+    d = Drafter.load(dd, dtype="fp32")
+    out = torch.randn((5, 256), device="cuda")
+    for restrict in (False, True):
+        if restrict:
+            d.restrict_vocab([1, 5, 9, 300, 2048, 4095])
+        q = d.head_softmax(out, T)
+        ref = torch.softmax(d.logits(out).double() / T, dim=-1)
+        torch.testing.assert_close(q.double(), ref, rtol=1e-5, atol=1e-7)
+        torch.testing.assert_close(q.sum(-1).double(), torch.ones(5, dtype=torch.float64), rtol=0, atol=1e-5)
+    with pytest.raises(ValueError):
+        d.head_softmax(out, 0.0)
+
+
 def test_restricted_head_equals_gathered_full_logits(tiny_models):
     """tests/test_vocab.py:37-51 restated: restricted logits == full logits at the kept ids and
     the argmax row maps back to its token id; a second restriction is refused."""

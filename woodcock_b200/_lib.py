@@ -109,6 +109,7 @@ SIGNATURES = {
     "wc_decoder_destroy": (None, [P]),
     "wc_decoder_prefill": (S, [P, I32P, C.c_int, C.POINTER(SamplingParamsC), I32P]),
     "wc_ctx_wait_selftest": (S, [P, C.c_int]),
+    "wc_drafter_head_softmax": (S, [P, P, C.c_int, C.c_float, P]),
     "wc_decoder_set_forced": (S, [P, I32P, C.c_int]),
     "wc_decoder_round": (S, [P, C.c_int, I32P, I32P]),
     "wc_decoder_tree_round": (S, [P, C.c_int, C.c_int, C.c_int, I32P, I32P]),

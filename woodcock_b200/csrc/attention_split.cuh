@@ -7,7 +7,7 @@
 // With mask_from_prefix the newmask bits count from the committed length (*n_dev) and cover the
 // rows appended earlier in the round too (drafted tree levels).
 //
-// Grid (S + 1, Hk), 128 threads, no clusters. Blocks 0..S-1 of KV head hk each own a slice of
+// Grid (S + 1, Hk), 16 warps (8 when a block holds two m-tiles of query rows), no clusters. Blocks 0..S-1 of KV head hk each own a slice of
 // the committed prefix [0, npre); block S owns the tail [npre, n + L): rows appended earlier in
 // the same round, then the new rows, which it normalises, rotates, rounds to bf16 and appends
 // to the cache. When the caller marks the prefix stable (its rows were written by completed
@@ -15,7 +15,7 @@
 // rows before the programmatic-dependent wait, so that traffic overlaps the QKV projection.
 // After the wait every block loads its head's q rows (one round trip), normalises and rotates
 // them into bf16 hi / lo tiles, runs S = Q K^T, online softmax and O += P V on m16n8k16 MMAs
-// (two 16-position tiles per warp), merges its four warps in shared memory and stores
+// (16 tiles of 16 positions per block and pass), merges its warps pairwise in shared memory and stores
 // its partial state (unnormalised o, running max m, sum l per query row) to global scratch.
 // The last block of the head to arrive (one fence and one atomic per block) combines the S + 1
 // partial states in block order, so the result does not depend on arrival order, and writes
@@ -27,11 +27,8 @@
 
 namespace wc {
 
-constexpr int AS_THREADS = 128;
-constexpr int AS_WARPS = AS_THREADS / kWarp;
 constexpr int AS_BLK = 16;                    // positions per tile
-constexpr int AS_TPW = 2;                     // tiles per warp and chunk
-constexpr int AS_CHUNK = AS_WARPS * AS_TPW * AS_BLK;  // positions in shared memory at once (128)
+constexpr int AS_CHUNK = 16 * AS_BLK;         // positions in shared memory at once (16 tiles)
 constexpr int AS_MAXR = 32;                   // query rows per KV head
 constexpr int AS_MAXL = 16;                   // new rows per launch
 constexpr int AS_MAXS = 64;                   // prefix blocks per KV head
@@ -46,34 +43,37 @@ struct AttnSplitParams {
   int pad;
 };
 
-template <int D>
+template <int D, int NW>
 struct AsLayout {
   static constexpr int LD = D + 8;  // padded bf16 row stride: conflict-free ldmatrix rows
   static constexpr size_t kv_bytes = size_t(2) * AS_CHUNK * LD * 2;              // K | V tiles
   static constexpr size_t raw_bytes = size_t(AS_MAXR + 2 * AS_MAXL) * D * 4;     // raw q | k | v rows
-  static constexpr size_t ow_bytes = size_t(AS_WARPS) * AS_MAXR * D * 4;         // warp outputs (after the tiles)
-  static constexpr size_t region_a = kv_bytes + raw_bytes > ow_bytes ? kv_bytes + raw_bytes : ow_bytes;
+  static constexpr size_t mg_bytes = size_t(NW / 2) * AS_MAXR * D * 4;           // pairwise warp merge (after the tiles)
+  static constexpr size_t region_a = kv_bytes + raw_bytes > mg_bytes ? kv_bytes + raw_bytes : mg_bytes;
   static constexpr size_t q_bytes = size_t(AS_MAXR) * LD * 2;                    // per hi / lo
   static constexpr size_t cw_bytes = size_t(AS_MAXR) * (AS_MAXS + 1) * 4;        // merge weights
   static constexpr size_t region_q = 2 * q_bytes > cw_bytes ? 2 * q_bytes : cw_bytes;
   static constexpr size_t rope_off = region_a + region_q;                        // [MAXL][D/2] float2
   static constexpr size_t w_off = rope_off + size_t(AS_MAXL) * (D / 2) * 8;      // q_norm, k_norm
-  static constexpr size_t ml_off = w_off + 2 * D * 4;                            // [WARPS][MAXR] m, l
-  static constexpr size_t pos_off = ml_off + 2 * AS_WARPS * AS_MAXR * 4;         // [MAXL] ints
-  static constexpr size_t wt_off = pos_off + AS_MAXL * 4;                       // [MAXR][WARPS] weights, [MAXR] M
-  static constexpr size_t mlall_off = wt_off + size_t(AS_MAXR) * (AS_WARPS + 1) * 4;  // [MAXS + 1][MAXR][2]
+  static constexpr size_t ml_off = w_off + 2 * D * 4;                            // [NW/2][MAXR] m, l
+  static constexpr size_t pos_off = ml_off + size_t(NW) * AS_MAXR * 4;           // [MAXL] ints
+  static constexpr size_t mlall_off = pos_off + AS_MAXL * 4;                     // [MAXS + 1][MAXR][2]
   static constexpr size_t flag_off = mlall_off + size_t(AS_MAXS + 1) * AS_MAXR * 2 * 4;
   static constexpr size_t total = flag_off + 16;
 };
 
-template <int D>
+template <int D, int NW>
 constexpr size_t attention_split_smem() {
-  return AsLayout<D>::total;
+  return AsLayout<D, NW>::total;
 }
 
-template <int D, int MT>
-__global__ void __launch_bounds__(AS_THREADS) attention_split_kernel(__grid_constant__ const AttnSplitParams sp) {
-  using Lay = AsLayout<D>;
+template <int D, int MT, int NW>
+__global__ void __launch_bounds__(NW * 32) attention_split_kernel(__grid_constant__ const AttnSplitParams sp) {
+  static_assert(16 % NW == 0 || NW == 16, "16 tiles per chunk over NW warps");
+  constexpr int AS_THREADS = NW * kWarp;
+  constexpr int AS_WARPS = NW;
+  constexpr int AS_TPW = 16 / NW;  // tiles per warp and chunk
+  using Lay = AsLayout<D, NW>;
   constexpr int LD = Lay::LD;
   constexpr int NDT = D / 8;
   constexpr int d4 = D / 4;
@@ -82,17 +82,16 @@ __global__ void __launch_bounds__(AS_THREADS) attention_split_kernel(__grid_cons
   uint16_t* kbuf = reinterpret_cast<uint16_t*>(as_smem);                       // [CHUNK][LD]
   uint16_t* vbuf = kbuf + AS_CHUNK * LD;                                         // [CHUNK][LD]
   float* raw = reinterpret_cast<float*>(as_smem + Lay::kv_bytes);                // [MAXR + 2 MAXL][D]
-  float* ow = reinterpret_cast<float*>(as_smem);                                 // [WARPS][MAXR][D]
+  float* mg = reinterpret_cast<float*>(as_smem);                                 // [NW/2][MAXR][D]
   uint16_t* qh = reinterpret_cast<uint16_t*>(as_smem + Lay::region_a);           // [MAXR][LD]
   uint16_t* ql = qh + AS_MAXR * LD;
   float* cw = reinterpret_cast<float*>(as_smem + Lay::region_a);                 // [MAXR][S + 1]
   float2* rp = reinterpret_cast<float2*>(as_smem + Lay::rope_off);               // [MAXL][D/2]
   float* wq = reinterpret_cast<float*>(as_smem + Lay::w_off);
   float* wk = wq + D;
-  float* mw = reinterpret_cast<float*>(as_smem + Lay::ml_off);                   // [WARPS][MAXR]
-  float* lw = mw + AS_WARPS * AS_MAXR;
+  float* mw = reinterpret_cast<float*>(as_smem + Lay::ml_off);                   // [NW/2][MAXR]
+  float* lw = mw + (AS_WARPS / 2) * AS_MAXR;
   int* spos = reinterpret_cast<int*>(as_smem + Lay::pos_off);
-  float* s_wt = reinterpret_cast<float*>(as_smem + Lay::wt_off);                // [MAXR][WARPS]
   int* s_flag = reinterpret_cast<int*>(as_smem + Lay::flag_off);
 
   const int S = sp.S, split = blockIdx.x, hk = blockIdx.y;
@@ -463,63 +462,76 @@ __global__ void __launch_bounds__(AS_THREADS) attention_split_kernel(__grid_cons
       }
     }
   }
-  __syncthreads();  // the tile buffers now hold the warp outputs
+  __syncthreads();  // the tile buffers are free: they hold the pairwise warp merge from here
 
-  // ---- the block's partial state: merge the four warps
+  // ---- the block's partial state: warps merge pairwise in a fixed order (w += w + half), so
+  // warp 0 ends with the block's (m, l, o) in registers
+  if (!worked) {  // an idle warp contributes nothing
 #pragma unroll
-  for (int mt = 0; mt < MT; ++mt) {
+    for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const int r = mt * 16 + g + 8 * h;
-      if (r < R) {
-        if (worked) {
+      for (int h = 0; h < 2; ++h) {
+        mrow[mt][h] = -INFINITY;
+        lrow[mt][h] = 0.f;
+      }
+  }
+#pragma unroll
+  for (int half = AS_WARPS / 2; half >= 1; half >>= 1) {
+    if (warp >= half && warp < 2 * half) {  // the upper half writes its state
+      const int slot = warp - half;
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int r = mt * 16 + g + 8 * h;
 #pragma unroll
           for (int dt = 0; dt < NDT; ++dt)
-            *reinterpret_cast<float2*>(&ow[(warp * AS_MAXR + r) * D + dt * 8 + 2 * t]) =
+            *reinterpret_cast<float2*>(&mg[(slot * AS_MAXR + r) * D + dt * 8 + 2 * t]) =
                 make_float2(o[mt][dt][2 * h], o[mt][dt][2 * h + 1]);
+          if (t == 0) {
+            mw[slot * AS_MAXR + r] = mrow[mt][h];
+            lw[slot * AS_MAXR + r] = lrow[mt][h];
+          }
         }
-        if (t == 0) {
-          mw[warp * AS_MAXR + r] = worked ? mrow[mt][h] : -INFINITY;
-          lw[warp * AS_MAXR + r] = worked ? lrow[mt][h] : 0.f;
+    }
+    __syncthreads();
+    if (warp < half) {  // the lower half folds its partner in
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int r = mt * 16 + g + 8 * h;
+          const float m2 = mw[warp * AS_MAXR + r], l2 = lw[warp * AS_MAXR + r];
+          const float M = fmaxf(mrow[mt][h], m2);
+          const float a1 = mrow[mt][h] == -INFINITY ? 0.f : expf(mrow[mt][h] - M);
+          const float a2 = m2 == -INFINITY ? 0.f : expf(m2 - M);
+          lrow[mt][h] = a1 * lrow[mt][h] + a2 * l2;
+          mrow[mt][h] = M;
+#pragma unroll
+          for (int dt = 0; dt < NDT; ++dt) {
+            const float2 v = *reinterpret_cast<const float2*>(&mg[(warp * AS_MAXR + r) * D + dt * 8 + 2 * t]);
+            o[mt][dt][2 * h] = a1 * o[mt][dt][2 * h] + a2 * v.x;
+            o[mt][dt][2 * h + 1] = a1 * o[mt][dt][2 * h + 1] + a2 * v.y;
+          }
         }
-      }
     }
+    __syncthreads();
   }
-  __syncthreads();
-  // per row: the warps' weights exp(m_w - M) and the block's M, l
-  if (tid < R) {
-    float M = -INFINITY;
+  if (warp == 0) {  // the block's partial state, straight from warp 0's registers
+    float* po = sp.part_o + (size_t(hk) * (S + 1) + split) * AS_MAXR * D;
+    float* ml = sp.part_ml + (size_t(hk) * (S + 1) + split) * AS_MAXR * 2;
 #pragma unroll
-    for (int w = 0; w < AS_WARPS; ++w) M = fmaxf(M, mw[w * AS_MAXR + tid]);
-    float lt = 0.f;
+    for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-    for (int w = 0; w < AS_WARPS; ++w) {
-      const float mv = mw[w * AS_MAXR + tid];
-      const float wv = mv == -INFINITY ? 0.f : expf(mv - M);
-      s_wt[tid * AS_WARPS + w] = wv;
-      lt = fmaf(wv, lw[w * AS_MAXR + tid], lt);
-    }
-    float* ml = sp.part_ml + ((size_t(hk) * (S + 1) + split) * AS_MAXR + tid) * 2;
-    ml[0] = M;
-    ml[1] = lt;
-  }
-  __syncthreads();
-  float* po = sp.part_o + (size_t(hk) * (S + 1) + split) * AS_MAXR * D;
-  for (int it = tid; it < R * (D / 4); it += AS_THREADS) {
-    const int r = it / (D / 4), c = (it % (D / 4)) * 4;
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int h = 0; h < 2; ++h) {
+        const int r = mt * 16 + g + 8 * h;
+        if (r >= R) continue;
 #pragma unroll
-    for (int w = 0; w < AS_WARPS; ++w) {
-      const float wv = s_wt[r * AS_WARPS + w];
-      if (wv != 0.f) {  // idle warps (weight 0) left their output slots unwritten
-        const float4 v = *reinterpret_cast<const float4*>(&ow[(w * AS_MAXR + r) * D + c]);
-        acc.x = fmaf(wv, v.x, acc.x);
-        acc.y = fmaf(wv, v.y, acc.y);
-        acc.z = fmaf(wv, v.z, acc.z);
-        acc.w = fmaf(wv, v.w, acc.w);
+        for (int dt = 0; dt < NDT; ++dt)
+          *reinterpret_cast<float2*>(&po[size_t(r) * D + dt * 8 + 2 * t]) =
+              make_float2(o[mt][dt][2 * h], o[mt][dt][2 * h + 1]);
+        if (t == 0) *reinterpret_cast<float2*>(&ml[r * 2]) = make_float2(mrow[mt][h], lrow[mt][h]);
       }
-    }
-    *reinterpret_cast<float4*>(po + size_t(r) * D + c) = acc;
   }
   // ---- arrival; the last block of this KV head combines the S + 1 partial states in order
   __syncthreads();  // every partial store of this block has been issued
@@ -530,75 +542,55 @@ __global__ void __launch_bounds__(AS_THREADS) attention_split_kernel(__grid_cons
   __syncthreads();
   if (!s_flag[0]) return;
   __threadfence();
-  // the partials arrive by cp.async through L2 in as few batches as shared memory allows: every
-  // (m, l) pair and as many splits' o rows as the tile region holds (all of them at C3 sizes)
   const float* hml = sp.part_ml + size_t(hk) * (S + 1) * AS_MAXR * 2;
   const float* ho = sp.part_o + size_t(hk) * (S + 1) * AS_MAXR * D;
   float* sml = reinterpret_cast<float*>(as_smem + Lay::mlall_off);  // [S + 1][MAXR][2]
-  float* so = reinterpret_cast<float*>(as_smem);                    // [batch][R][D]
-  const int split_floats = R * D;                                   // one split's o rows, contiguous
-  const int fit = max(1, int(Lay::region_a / (size_t(split_floats) * 4)));
-  for (int c = tid; c < (S + 1) * AS_MAXR * 2 / 4; c += AS_THREADS) cp_async16(sml + 4 * c, hml + 4 * c, 16);
-  constexpr int IT = (AS_MAXR * (D / 4) + AS_THREADS - 1) / AS_THREADS;  // o items (row, 4 dims) per thread
-  float4 acc[IT];
-#pragma unroll
-  for (int k = 0; k < IT; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int b0 = 0; b0 <= S; b0 += fit) {
-    const int nb = min(S + 1 - b0, fit);
-    if (b0 > 0) __syncthreads();  // the previous batch has been consumed
-    for (int c = tid; c < nb * split_floats / 4; c += AS_THREADS) {
-      const int sb = c / (split_floats / 4), off = (c % (split_floats / 4)) * 4;
-      cp_async16(so + size_t(sb) * split_floats + off, ho + size_t(b0 + sb) * AS_MAXR * D + off, 16);
+  for (int c = tid; c < (S + 1) * AS_MAXR * 2 / 4; c += AS_THREADS)
+    *reinterpret_cast<float4*>(sml + 4 * c) = __ldcg(reinterpret_cast<const float4*>(hml) + c);
+  __syncthreads();
+  for (int r = warp; r < R; r += AS_WARPS) {  // per-row split weights exp(m_s - M) / sum_s exp(m_s - M) l_s
+    float M = -INFINITY;
+    for (int s2 = lane; s2 <= S; s2 += kWarp) M = fmaxf(M, sml[(s2 * AS_MAXR + r) * 2]);
+    for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
+    float lt = 0.f;
+    for (int s2 = lane; s2 <= S; s2 += kWarp) {
+      const float mv = sml[(s2 * AS_MAXR + r) * 2];
+      const float wv = mv == -INFINITY ? 0.f : expf(mv - M);
+      cw[r * (AS_MAXS + 1) + s2] = wv;
+      lt = fmaf(wv, sml[(s2 * AS_MAXR + r) * 2 + 1], lt);
     }
-    cp_async_commit();
-    cp_async_wait<0>();
-    __syncthreads();
-    if (b0 == 0) {  // per-row split weights exp(m_s - M) / sum_s exp(m_s - M) l_s
-      for (int r = warp; r < R; r += AS_WARPS) {
-        float M = -INFINITY;
-        for (int s2 = lane; s2 <= S; s2 += kWarp) M = fmaxf(M, sml[(s2 * AS_MAXR + r) * 2]);
-        for (int o2 = 16; o2 > 0; o2 >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
-        float lt = 0.f;
-        for (int s2 = lane; s2 <= S; s2 += kWarp) {
-          const float mv = sml[(s2 * AS_MAXR + r) * 2];
-          const float wv = mv == -INFINITY ? 0.f : expf(mv - M);
-          cw[r * (AS_MAXS + 1) + s2] = wv;
-          lt = fmaf(wv, sml[(s2 * AS_MAXR + r) * 2 + 1], lt);
-        }
-        for (int o2 = 16; o2 > 0; o2 >>= 1) lt += __shfl_xor_sync(0xffffffffu, lt, o2);
-        __syncwarp();
-        const float inv = lt > 0.f ? 1.f / lt : 0.f;
-        for (int s2 = lane; s2 <= S; s2 += kWarp) cw[r * (AS_MAXS + 1) + s2] *= inv;
-      }
-      __syncthreads();
-    }
-#pragma unroll
-    for (int k = 0; k < IT; ++k) {
-      const int it = tid + k * AS_THREADS;
-      if (it < R * (D / 4)) {
-        const int r = it / (D / 4), c = (it % (D / 4)) * 4;
-        for (int sb = 0; sb < nb; ++sb) {
-          const float wv = cw[r * (AS_MAXS + 1) + b0 + sb];
-          const float4 v = *reinterpret_cast<const float4*>(so + size_t(sb) * split_floats + r * D + c);
-          acc[k].x = fmaf(wv, v.x, acc[k].x);
-          acc[k].y = fmaf(wv, v.y, acc[k].y);
-          acc[k].z = fmaf(wv, v.z, acc[k].z);
-          acc[k].w = fmaf(wv, v.w, acc[k].w);
-        }
-      }
-    }
+    for (int o2 = 16; o2 > 0; o2 >>= 1) lt += __shfl_xor_sync(0xffffffffu, lt, o2);
+    __syncwarp();
+    const float inv = lt > 0.f ? 1.f / lt : 0.f;
+    for (int s2 = lane; s2 <= S; s2 += kWarp) cw[r * (AS_MAXS + 1) + s2] *= inv;
   }
+  __syncthreads();
+  for (int it = tid; it < R * (D / 4); it += AS_THREADS) {
+    const int r = it / (D / 4), c = (it % (D / 4)) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int s0 = 0; s0 <= S; s0 += 8) {  // eight splits' loads in flight at a time
+      float4 v[8];
+      float wv[8];
 #pragma unroll
-  for (int k = 0; k < IT; ++k) {
-    const int it = tid + k * AS_THREADS;
-    if (it < R * (D / 4)) {
-      const int r = it / (D / 4), c = (it % (D / 4)) * 4;
-      const int l = r / rep, h = hk * rep + r % rep;
-      attn_emit(p, l, h * D + c, acc[k].x);
-      attn_emit(p, l, h * D + c + 1, acc[k].y);
-      attn_emit(p, l, h * D + c + 2, acc[k].z);
-      attn_emit(p, l, h * D + c + 3, acc[k].w);
+      for (int u = 0; u < 8; ++u) {
+        const int s2 = s0 + u;
+        wv[u] = s2 <= S ? cw[r * (AS_MAXS + 1) + s2] : 0.f;
+        v[u] = wv[u] != 0.f ? __ldcg(reinterpret_cast<const float4*>(ho + (size_t(s2) * AS_MAXR + r) * D + c))
+                            : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        acc.x = fmaf(wv[u], v[u].x, acc.x);
+        acc.y = fmaf(wv[u], v[u].y, acc.y);
+        acc.z = fmaf(wv[u], v[u].z, acc.z);
+        acc.w = fmaf(wv[u], v[u].w, acc.w);
+      }
     }
+    const int l = r / rep, h = hk * rep + r % rep;
+    attn_emit(p, l, h * D + c, acc.x);
+    attn_emit(p, l, h * D + c + 1, acc.y);
+    attn_emit(p, l, h * D + c + 2, acc.z);
+    attn_emit(p, l, h * D + c + 3, acc.w);
   }
   if (tid == 0) sp.counters[hk] = 0;  // ready for the next launch
 }

@@ -114,7 +114,7 @@ struct wc_ctx {
   float* as_part_o = nullptr;   // attention_split partial states: [16 KV heads][AS_MAXS + 1][AS_MAXR][128]
   float* as_part_ml = nullptr;  //   and their (m, l): [16][AS_MAXS + 1][AS_MAXR][2]
   int* as_counters = nullptr;   //   per-KV-head arrivals (zero between launches)
-  int attn_split_pos = 64;      // capacity positions per prefix block (WC_ATTN_SPLIT_POS)
+  int attn_split_pos = 256;     // capacity positions per prefix block (WC_ATTN_SPLIT_POS)
   int gemv_blocks_per_sm = 1;
   bool gemv_wide = true;                 // 80 KB activation chunks for K up to 2560 (WC_GEMV_WIDE=0: split K)
   bool gemv_acs = true;                  // whole-K blocks with streamed activation pieces (WC_GEMV_ACS=0: split K)
@@ -688,24 +688,24 @@ void launch_attention(wc_ctx* ctx, AttnParams p) {
     sp.part_ml = ctx->as_part_ml;
     sp.counters = ctx->as_counters;
     // prefix blocks per KV head: the capacity in slices of attn_split_pos positions (a block holds
-    // up to 128 at once), fixed when the round graph is captured
+    // 256 at once), fixed when the round graph is captured
     sp.S = std::max(1, std::min(AS_MAXS, (p.cap + ctx->attn_split_pos - 1) / ctx->attn_split_pos));
     const bool mt2 = p.L_max * rep > 16;
     const dim3 grid(sp.S + 1, p.Hk);
     if (p.D == 128) {
       if (mt2)
-        launch_ex(ctx, "attention_split", attention_split_kernel<128, 2>, grid, dim3(AS_THREADS),
-                  attention_split_smem<128>(), true, 1, sp);
+        launch_ex(ctx, "attention_split", attention_split_kernel<128, 2, 8>, grid, dim3(8 * kWarp),
+                  attention_split_smem<128, 8>(), true, 1, sp);
       else
-        launch_ex(ctx, "attention_split", attention_split_kernel<128, 1>, grid, dim3(AS_THREADS),
-                  attention_split_smem<128>(), true, 1, sp);
+        launch_ex(ctx, "attention_split", attention_split_kernel<128, 1, 16>, grid, dim3(16 * kWarp),
+                  attention_split_smem<128, 16>(), true, 1, sp);
     } else {
       if (mt2)
-        launch_ex(ctx, "attention_split", attention_split_kernel<64, 2>, grid, dim3(AS_THREADS),
-                  attention_split_smem<64>(), true, 1, sp);
+        launch_ex(ctx, "attention_split", attention_split_kernel<64, 2, 8>, grid, dim3(8 * kWarp),
+                  attention_split_smem<64, 8>(), true, 1, sp);
       else
-        launch_ex(ctx, "attention_split", attention_split_kernel<64, 1>, grid, dim3(AS_THREADS),
-                  attention_split_smem<64>(), true, 1, sp);
+        launch_ex(ctx, "attention_split", attention_split_kernel<64, 1, 16>, grid, dim3(16 * kWarp),
+                  attention_split_smem<64, 16>(), true, 1, sp);
     }
     return;
   }
@@ -801,13 +801,15 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
     CUDA_TRY(cudaFuncSetAttribute(attention_mma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     if (std::getenv("WC_ATTN_CARVEOUT")) {  // A/B switch: the shared-memory carveout of the decode kernels
       const int cv = std::atoi(std::getenv("WC_ATTN_CARVEOUT"));
-      CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<128, 1>, cudaFuncAttributePreferredSharedMemoryCarveout, cv));
-      CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<128, 2>, cudaFuncAttributePreferredSharedMemoryCarveout, cv));
+      CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<128, 1, 16>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                    cv));
+      CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<128, 2, 8>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                    cv));
     }
-    CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<128, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
-    CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<128, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
-    CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<64, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
-    CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<64, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
+    CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<128, 1, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
+    CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<128, 2, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
+    CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<64, 1, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
+    CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<64, 2, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(attention_dec_kernel<128, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(attention_dec_kernel<128, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(attention_dec_kernel<64, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
@@ -1141,6 +1143,11 @@ extern "C" wc_status wc_accept_stochastic_noalloc(wc_ctx* ctx, const double* p, 
       // one-time set-up per device, with that device current
       std::lock_guard<std::mutex> lock(g_scratch_mu);
       if (!g_scratch_addr[cur]) {
+        // the look-up may load the module; that must not happen inside a stream capture
+        cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+        CUDA_TRY(cudaStreamIsCapturing(ctx->stream, &cs));
+        if (cs != cudaStreamCaptureStatusNone)
+          fail(WC_ERR_INVALID, "wc_accept_stochastic_noalloc: make the first call on a device before any capture");
         void* a = nullptr;
         const cudaError_t e = cudaGetSymbolAddress(&a, g_accept_scratch);
         if (e != cudaSuccess || !a)
@@ -2460,6 +2467,18 @@ extern "C" wc_status wc_drafter_logits(wc_drafter* d, const float* out, int rows
       drafter_head(d, x, n, d->ws_keys, z + size_t(r0) * d->head_rows, nullptr, nullptr, d->ctx->d_err);
     }
   });
+}
+
+extern "C" wc_status wc_drafter_head_softmax(wc_drafter* d, const float* out, int rows, float temperature,
+                                             float* probs) {
+  if (!d || !out || !probs || rows <= 0) return WC_ERR_INVALID;
+  if (!(temperature > 0.f)) {
+    d->ctx->err = "the draft distribution needs a temperature > 0 (greedy drafting uses 1)";
+    return WC_ERR_INVALID;
+  }
+  const wc_status st = wc_drafter_logits(d, out, rows, probs);  // logits into the output, then in place
+  if (st != WC_OK) return st;
+  return wc_probs_from_logits(d->ctx, probs, rows, d->head_rows, temperature, 0, 1.f, probs);
 }
 
 extern "C" wc_status wc_drafter_head_argmax(wc_drafter* d, const float* out, int rows, int* token) {

@@ -158,6 +158,15 @@ class Drafter:
             self.ctx.check(lib().wc_drafter_logits(self.h, ptr(x), x.shape[0], ptr(z)))
         return z.reshape(*shape, self.head_rows)
 
+    def head_softmax(self, out: torch.Tensor, temperature: float = 1.0) -> torch.Tensor:
+        """The draft distribution softmax(logits / T) over the head rows (spec.py:113-125)."""
+        shape = out.shape[:-1]
+        x = out.reshape(-1, self.hidden_size).float().contiguous()
+        with self.ctx.enter(x):
+            q = torch.empty((x.shape[0], self.head_rows), dtype=torch.float32, device=self.ctx.device)
+            self.ctx.check(lib().wc_drafter_head_softmax(self.h, ptr(x), x.shape[0], float(temperature), ptr(q)))
+        return q.reshape(*shape, self.head_rows)
+
     def head_argmax(self, out: torch.Tensor) -> torch.Tensor:
         """Fused head + argmax, mapped to token ids."""
         x = out.reshape(-1, self.hidden_size).float().contiguous()
