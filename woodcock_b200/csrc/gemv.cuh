@@ -133,6 +133,8 @@ struct GemvParams {
   int ldy;
   const float* base;     // EPI_ADD: y = base + acc (base may equal y)
   int ldb;
+  int base_tok;          // EPI_ADD: base row of row l = the row of l's token (tok), not l
+                         // (the drafter's per-token auxiliary Q/K/V table)
   float* y2;             // optional second copy of the stored result (tap capture)
   int ldy2;
   unsigned long long* keys;  // EPI_ARGMAX: per-row max keys (atomicMax)
@@ -309,9 +311,9 @@ struct EpiIn {
   float w[2];
 };
 
-__device__ __forceinline__ EpiIn gemv_epi_load(const GemvParams& p, int n, int l) {
+__device__ __forceinline__ EpiIn gemv_epi_load(const GemvParams& p, int n, int l, const int* btok) {
   EpiIn e;
-  e.base = p.epi == EPI_ADD ? p.base[size_t(l) * p.ldb + n] : 0.f;
+  e.base = p.epi == EPI_ADD ? p.base[size_t(p.base_tok ? btok[l] : l) * p.ldb + n] : 0.f;
   e.w[0] = (p.nout > 0 && p.out[0].w) ? __ldg(p.out[0].w + n) : 1.f;
   e.w[1] = (p.nout > 1 && p.out[1].w) ? __ldg(p.out[1].w + n) : 1.f;
   return e;
@@ -345,7 +347,7 @@ __device__ __forceinline__ float gemv_epilogue_in(const GemvParams& p, int n, in
 
 __device__ __forceinline__ float gemv_epilogue(const GemvParams& p, int n, int l, float v0, float v1,
                                                unsigned long long* s_key) {
-  return gemv_epilogue_in(p, n, l, v0, v1, gemv_epi_load(p, n, l), s_key);
+  return gemv_epilogue_in(p, n, l, v0, v1, gemv_epi_load(p, n, l, nullptr), s_key);
 }
 
 // Tokens (GV_F_TOK) and s_inv[s * 16 + l] = the 1/rms of row l of segment s (0 for l >= L),
@@ -450,7 +452,8 @@ struct GvLayout {
   static constexpr size_t part = inv + GEMV_MAXSEG * 16 * 4;               // [3][256] floats
   static constexpr size_t sq = part + GEMV_MAXSEG * 256 * 4;               // [2][16 features][16 rows] floats
   static constexpr size_t tok = sq + 2 * 256 * 4;                          // [16] ints
-  static constexpr size_t flag = tok + 16 * 4;                             // [4] ints
+  static constexpr size_t btok = tok + 16 * 4;                             // [16] ints (epilogue's tokens)
+  static constexpr size_t flag = btok + 16 * 4;                            // [4] ints
   static constexpr size_t key = flag + 16;                                 // [16] u64
   static constexpr size_t params = key + 16 * 8;
   static constexpr size_t total = params + (sizeof(GemvParams) + 15) / 16 * 16;
@@ -484,6 +487,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
   float* s_part = reinterpret_cast<float*>(gv_smem + Lay::part);
   float* s_sq = reinterpret_cast<float*>(gv_smem + Lay::sq);
   int* s_tok = reinterpret_cast<int*>(gv_smem + Lay::tok);
+  int* s_btok = reinterpret_cast<int*>(gv_smem + Lay::btok);
   int* s_flag = reinterpret_cast<int*>(gv_smem + Lay::flag);
   unsigned long long* s_key = reinterpret_cast<unsigned long long*>(gv_smem + Lay::key);
   const uint4* act4 = reinterpret_cast<const uint4*>(act);
@@ -646,7 +650,10 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
     const int et = tid - (GV_CWARPS + 1) * kWarp;
     pdl_wait();
     const int L = gemv_rows(p.L_dev, p.L, p.L_max, nullptr);
-    if (et < 16) s_key[et] = 0ull;
+    if (et < 16) {
+      s_key[et] = 0ull;
+      s_btok[et] = (p.base_tok && et < L) ? resolve_token(p.tok, et, nullptr) : 0;
+    }
     named_sync(2, GV_ETHREADS);
     bool ok = true;
     unsigned long long kbest[NT];  // EPI_ARGMAX: best key of this thread's row(s) (fixed per k)
@@ -672,7 +679,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
         l_[k] = nt_[k] * 8 + 2 * (ln_[k] % 4) + (e_[k] & 1);
         r16_[k] = ln_[k] / 4 + ((e_[k] & 2) ? 8 : 0);
         live[k] = p.nkc == 1 && l_[k] < L && u * 16 + r16_[k] < p.N;
-        if (live[k]) ein[k] = gemv_epi_load(p, u * 16 + r16_[k], l_[k]);
+        if (live[k]) ein[k] = gemv_epi_load(p, u * 16 + r16_[k], l_[k], s_btok);
       }
       if (ok && !mbar_wait(red_full + b, (j >> 1) & 1)) {
         raise_error(p.err, kErrTimeout);
@@ -785,7 +792,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
               if (it < items) {
                 const int uu = it / per, r16 = (it % per) / L, l = it % L;
                 const int n = (ub + uu) * 16 + r16;
-                if (n < p.N) ein[i] = gemv_epi_load(p, n, l);
+                if (n < p.N) ein[i] = gemv_epi_load(p, n, l, s_btok);
               }
             }
             for (int c = 0; c < p.nkc; ++c) {

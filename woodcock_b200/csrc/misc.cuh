@@ -507,6 +507,24 @@ __global__ void philox_uniforms_kernel(uint64_t seed, uint64_t offset, int n, do
   if (i < n) out[i] = philox_uniform(seed, offset + uint64_t(i));
 }
 
+// ----------------------------------------------------------------------------- drafter auxiliary table
+// GEMM operand rows for the per-token auxiliary term: row i = token r0 + i, columns [0, H) zero
+// (the feature half of the layer-0 Q/K/V weight), columns [H, 2H) the bf16 high (lo = 0) or low
+// (lo = 1) part of embed[t] * (1/rms of the row) * aux_norm, so two GEMMs add up to the fp32 value.
+__global__ void aux_rows_kernel(const uint16_t* embed, const float* row_inv, const float* aux_norm, int r0, int H,
+                                int lo, uint16_t* out) {
+  const int i = blockIdx.x, t = r0 + i;
+  const uint16_t* e = embed + size_t(t) * H;
+  uint16_t* o = out + size_t(i) * 2 * H;
+  const float inv = row_inv[t];
+  for (int k = threadIdx.x; k < H; k += blockDim.x) {
+    const float x = bf16_bits_to_f32(e[k]) * inv * aux_norm[k];
+    const uint16_t hi = f32_to_bf16_bits(x);
+    o[k] = 0;
+    o[H + k] = lo ? f32_to_bf16_bits(x - bf16_bits_to_f32(hi)) : hi;
+  }
+}
+
 // ----------------------------------------------------------------------------- bounded-wait self test
 // Waits, with the same bounded helper every pipelined kernel uses, on an mbarrier phase that
 // nothing completes: after `iters` tries the wait gives up and the kernel raises kErrTimeout in

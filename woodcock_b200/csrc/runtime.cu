@@ -1879,6 +1879,7 @@ extern "C" wc_status wc_target_forward(wc_target* t, wc_kv* cache, const int* to
 namespace {
 struct DLayer {
   Lin qkv, o, gu, down;
+  Lin qkv_main;  // layer 0 with the auxiliary table: the Q/K/V weights of the feature input alone
   float *in_norm = nullptr, *post_norm = nullptr, *q_norm = nullptr, *k_norm = nullptr, *aux_norm = nullptr;
   float *ss_o = nullptr, *ss_d = nullptr;
 };
@@ -1894,6 +1895,7 @@ struct wc_drafter {
   Stage stage;
   void* embed = nullptr;
   float* aux_inv = nullptr;  // [vocab]: 1/rms of each embedding row with the drafter eps (aux_norm)
+  float* aux_table = nullptr;  // [vocab][Q+K+V]: W_aux . aux_norm(embed(t)) per token (bf16 drafters)
   Lin fc;
   float* feature_norms[GEMV_MAXSEG] = {nullptr, nullptr, nullptr};
   std::vector<DLayer> layers;
@@ -1914,6 +1916,7 @@ struct wc_drafter {
 };
 
 namespace {
+void drafter_build_aux_table(wc_drafter* d);
 
 void drafter_check_cfg(const wc_drafter_config& c) {
   if (c.hidden <= 0 || c.layers <= 0 || c.heads <= 0 || c.kv_heads <= 0 || c.head_dim <= 0 || c.intermediate <= 0 ||
@@ -2011,6 +2014,7 @@ void drafter_finalize_impl(wc_drafter* d) {
   d->ss_g = ss_alloc(ctx);
   d->ss_pack = ss_alloc(ctx);
   d->ws_keys = static_cast<unsigned long long*>(dalloc(sizeof(unsigned long long) * M));
+  drafter_build_aux_table(d);
   CUDA_TRY(cudaStreamSynchronize(ctx->stream));
   d->stage.clear();
   d->finalized = true;
@@ -2038,18 +2042,26 @@ XIn drafter_layers(wc_drafter* d, wc_kv* kv, const Rows& r, XIn feat_in, const f
       p.L_max = r.L_max;
       p.nseg = 1;
       p.seg[0] = xs_frag(x, H, bf16, c.eps);
-      if (Ly.aux_norm) {
+      const bool table = Ly.aux_norm && d->aux_table && Ly.qkv_main.w;
+      p.epi = EPI_STORE;
+      if (table) {  // the token's row of the precomputed auxiliary term, added in the epilogue
+        p.epi = EPI_ADD;
+        p.base = d->aux_table;
+        p.ldb = ld_qkv;
+        p.base_tok = 1;
+        p.tok = tok;
+        p.tok.vocab = c.vocab;
+      } else if (Ly.aux_norm) {
         p.nseg = 2;
         p.seg[1] = xs_embed(d->embed, H, bf16, Ly.aux_norm, d->aux_inv);
         p.tok = tok;
         p.tok.vocab = c.vocab;
       }
-      p.epi = EPI_STORE;
       p.y = d->ws_qkv;
       p.ldy = ld_qkv;
       p.err = err;
       gemv_prefetch(ctx, p, &Ly.o, &Ly.gu);  // both land while attention runs
-      launch_gemv(ctx, Ly.qkv, p);
+      launch_gemv(ctx, table ? Ly.qkv_main : Ly.qkv, p);
     }
     {
       AttnParams a = attn_params();
@@ -2323,12 +2335,14 @@ extern "C" void wc_drafter_destroy(wc_drafter* d) {
   if (!d) return;
   cudaStreamSynchronize(d->ctx->stream);
   drafter_gemm_free(d);
+  dfree(d->aux_table);
   dfree(d->embed);
   dfree(d->aux_inv);
   free_lin(d->fc);
   for (auto* f : d->feature_norms) dfree(f);
   for (auto& L : d->layers) {
     free_lin(L.qkv);
+    free_lin(L.qkv_main);
     free_lin(L.o);
     free_lin(L.gu);
     free_lin(L.down);
@@ -4343,6 +4357,56 @@ const float* drafter_prefill_gemm(wc_drafter* d, wc_kv* kv, const int* tokens_de
     }
   }
   return g->h + size_t(rows - 1) * H;
+}
+
+// The drafter's auxiliary Q/K/V term per vocabulary token, W_aux . aux_norm(embed(t)), as an fp32
+// table [vocab][Q+K+V] (two tcgen05 GEMMs over the bf16 high and low parts of the normalised
+// embeddings), and the layer-0 Q/K/V weight of the feature input alone: the decode passes then
+// stream half the layer-0 Q/K/V weights, without splitting K, and add the token's table row in the
+// GEMV epilogue. bf16 drafters with a hidden size that is a multiple of 512; WC_AUX_TABLE=0 keeps
+// the two-segment projection.
+void drafter_build_aux_table(wc_drafter* d) {
+  static const bool on = [] {
+    const char* e = std::getenv("WC_AUX_TABLE");
+    return !e || std::atoi(e) != 0;
+  }();
+  const auto& c = d->cfg;
+  if (!on || d->aux_table || d->dtype != WC_BF16 || c.hidden % GV_COLS || d->layers.empty() ||
+      !d->layers[0].aux_norm)
+    return;
+  wc_ctx* ctx = d->ctx;
+  if (!tc_ready(ctx)) return;
+  DLayer& L0 = d->layers[0];
+  const int H = c.hidden, NQKV = L0.qkv.N;
+  if (L0.qkv.Np != NQKV || NQKV % 256) return;
+  Lin m = make_lin(WC_BF16, NQKV, {H}, 1);
+  CUDA_TRY(cudaMemcpy2DAsync(m.w, size_t(H / 16) * 512, L0.qkv.w, size_t(L0.qkv.Kp / 16) * 512, size_t(H / 16) * 512,
+                             size_t(L0.qkv.Np / 16), cudaMemcpyDeviceToDevice, ctx->stream));
+  TcWeight B = tc_weight_from(ctx, L0.qkv, 256);  // [NQKV][2H] row-major
+  float* table = static_cast<float*>(dalloc(sizeof(float) * size_t(c.vocab) * NQKV));
+  constexpr int kRows = 4096;
+  uint16_t* A = static_cast<uint16_t*>(dalloc(2 * size_t(kRows) * 2 * H));
+  for (int r0 = 0; r0 < c.vocab; r0 += kRows) {
+    const int M = std::min(kRows, c.vocab - r0);
+    for (int lo = 0; lo < 2; ++lo) {
+      aux_rows_kernel<<<M, 256, 0, ctx->stream>>>(static_cast<const uint16_t*>(d->embed), d->aux_inv, L0.aux_norm,
+                                                  r0, H, lo, A);
+      check_launch(ctx, "aux rows");
+      GemmTc g = gemm_tc_params(M, NQKV, 2 * H, lo ? TC_ADD : TC_STORE);
+      g.c = table + size_t(r0) * NQKV;
+      g.ldc = NQKV;
+      if (lo) {
+        g.r = g.c;
+        g.ldr = NQKV;
+      }
+      launch_gemm_tc(ctx, tmap_bf16(A, M, 2 * H, TC_BM), B.map, g, B.BN);
+    }
+  }
+  CUDA_TRY(cudaStreamSynchronize(ctx->stream));
+  dfree(A);
+  dfree(B.w);
+  L0.qkv_main = m;
+  d->aux_table = table;
 }
 
 }  // namespace

@@ -8,9 +8,15 @@ over (BASELINE's definition: weight bytes + KV bytes read per round):
   + fuse FC + 1 drafter layer pass                       (the drafter update)
   + target KV over the context (once)
   + drafter KV over the context (once per drafter pass: K - 1 chain steps + the update).
+
+With the drafter's auxiliary table (bf16 drafters whose hidden size is a multiple of 512), a
+drafter pass reads the layer-0 Q/K/V weights of the feature input only, plus one fp32 table row
+of Q+K+V values per row it processes, instead of the auxiliary Q/K/V weights.
 """
 
 from __future__ import annotations
+
+import os
 
 
 def _target_params(t) -> dict:
@@ -19,10 +25,21 @@ def _target_params(t) -> dict:
     return {"layers": per_layer * t.layers, "head": t.vocab * H, "per_layer": per_layer}
 
 
+def aux_table_on(d) -> bool:
+    """Whether the library precomputes the drafter's auxiliary term per token (WC_AUX_TABLE)."""
+    return os.environ.get("WC_AUX_TABLE", "1") != "0" and d.hidden % 512 == 0
+
+
 def _drafter_layer_params(d) -> int:
     H, D = d.hidden, d.head_dim
     qkv = (d.heads + 2 * d.kv_heads) * D * H
-    return 2 * qkv + H * d.heads * D + 3 * d.intermediate * H  # layer 0 carries the auxiliary Q/K/V
+    aux = 0 if aux_table_on(d) else qkv  # layer 0 carries the auxiliary Q/K/V
+    return qkv + aux + H * d.heads * D + 3 * d.intermediate * H
+
+
+def _aux_row_bytes(d) -> int:
+    """Table bytes one row of a drafter pass reads (fp32 Q+K+V), when the table is on."""
+    return (d.heads + 2 * d.kv_heads) * d.head_dim * 4 if aux_table_on(d) else 0
 
 
 def round_bytes(target, drafter, k: int, head_rows: int, ctx: int, wbytes: int = 2, kvbytes: int = 2) -> dict:
@@ -34,9 +51,9 @@ def round_bytes(target, drafter, k: int, head_rows: int, ctx: int, wbytes: int =
     d_kv_per_tok = drafter.layers * 2 * drafter.kv_heads * drafter.head_dim * kvbytes
     out = {
         "draft_heads": k * head * wbytes,
-        "draft_layers": (k - 1) * dl * wbytes,
+        "draft_layers": (k - 1) * (dl * wbytes + _aux_row_bytes(drafter)),
         "target_weights": (tp["layers"] + tp["head"]) * wbytes,
-        "update": (fc + dl) * wbytes,
+        "update": (fc + dl) * wbytes + (k + 1) * _aux_row_bytes(drafter),
         "target_kv": ctx * t_kv_per_tok,
         "drafter_kv": k * ctx * d_kv_per_tok,
     }
@@ -49,5 +66,5 @@ def round_bytes(target, drafter, k: int, head_rows: int, ctx: int, wbytes: int =
 def draft_step_bytes(drafter, head_rows: int, ctx: int, wbytes: int = 2, kvbytes: int = 2) -> int:
     """One chain step: head + one drafter layer pass + its KV reads (scripts/time_draft_step.py `step`)."""
     dl = _drafter_layer_params(drafter) * drafter.layers
-    return (head_rows * drafter.hidden + dl) * wbytes + ctx * drafter.layers * 2 * drafter.kv_heads * \
-        drafter.head_dim * kvbytes
+    return (head_rows * drafter.hidden + dl) * wbytes + _aux_row_bytes(drafter) + \
+        ctx * drafter.layers * 2 * drafter.kv_heads * drafter.head_dim * kvbytes
