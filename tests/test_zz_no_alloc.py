@@ -70,3 +70,33 @@ def test_noalloc_rejects_vocabulary_above_its_scratch():
                                             ptr(out[0:1]), ptr(out[1:2]), ptr(out[2:3]))
     assert st == WC_ERR_CAPACITY
     assert b"WC_ACCEPT_NOALLOC_MAX_V" in lib().wc_last_error(ctx.h)
+
+
+def test_noalloc_call_records_into_a_global_mode_capture():
+    """The property the entry point exists for: after one warm call, a second call records into
+    a CUDA graph captured in global mode, which refuses cudaMalloc, cudaFree and any device or
+    stream synchronisation made during the capture. Replays give the eager result."""
+    from woodcock_b200._lib import lib
+    from woodcock_b200.context import Context, ptr
+
+    ctx = Context.get(0)
+    torch.cuda.set_device(ctx.device)
+    rng = np.random.default_rng(77)
+    P, Q, tok, par = _case(rng, 32000, 4, ctx.device)
+    N, V = P.shape
+    ref = _run("wc_accept_stochastic", ctx, P, Q, tok, par, 31, 9)
+    assert _run("wc_accept_stochastic_noalloc", ctx, P, Q, tok, par, 31, 9) == ref  # warm call
+    out = torch.full((N + 3,), -7, dtype=torch.int32, device=ctx.device)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g, stream=ctx.stream, capture_error_mode="global"):
+        st = lib().wc_accept_stochastic_noalloc(ctx.h, ptr(P), ptr(Q), V, ptr(tok), ptr(par), N, 31, 9,
+                                                ptr(out[3:]), ptr(out[0:1]), ptr(out[1:2]), ptr(out[2:3]))
+    assert st == 0, lib().wc_last_error(ctx.h)
+    for _ in range(2):
+        out.fill_(-7)
+        g.replay()
+        torch.cuda.synchronize()
+        o = out.cpu().tolist()
+        assert (o[3 : 3 + o[0]], o[1], o[2]) == ref
+    del g

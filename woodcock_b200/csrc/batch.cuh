@@ -874,8 +874,11 @@ __global__ void __launch_bounds__(128) tree_attn_merge_kernel(__grid_constant__ 
 
 // ---------------------------------------------------------------------------- compaction
 // KVCache::compact (src/cache/kv_cache.cpp:21-31) for every request and layer: rows
-// lens[r] + keep[r][i] -> lens[r] + i, then lens[r] += n_keep[r]. keep is strictly increasing
-// with keep[0] = 0, so no destination row is another row's source: every row moves at once.
+// lens[r] + keep[r][i] -> lens[r] + i, then lens[r] += n_keep[r]. keep must be strictly
+// increasing with keep[0] = 0 (checked; kErrTree otherwise), hence keep[i] >= i. Rows are moved
+// in increasing i, and one thread moves the same 16-byte chunk c of every row. Row m is written
+// only at step m and read only at steps i <= m (keep[i] = m), the read at i = m being skipped, so
+// each chunk is read as a source before that thread overwrites it as a destination.
 struct BatchCompactParams {
   uint16_t* K;  // [layers][B][Hk][cap][D]
   uint16_t* V;
@@ -891,7 +894,7 @@ __global__ void batch_compact_kernel(__grid_constant__ const BatchCompactParams 
   const int r = blockIdx.x, layer = blockIdx.y;
   const int n = p.lens[r], nk = p.n_keep[r];
   const int* keep = p.keep + size_t(r) * p.maxkeep;
-  if (nk < 1 || nk > p.maxkeep) {
+  if (nk < 1 || nk > p.maxkeep || keep[0] != 0) {
     if (threadIdx.x == 0) raise_error(p.err, kErrTree);
     return;
   }

@@ -1170,7 +1170,8 @@ struct wc_kv {
   int layers, Hk, D, cap, dtype;
   void* K;
   void* V;
-  int n;  // host-side size for the ops / forward API
+  int n;               // host-side size for the ops / forward API
+  int* keep = nullptr;  // MAXTREE ints: the compaction keep list on the device
   size_t layer_elems() const { return size_t(Hk) * cap * D; }
   void* Kl(int l) const { return static_cast<char*>(K) + size_t(l) * layer_elems() * dtype_size(dtype); }
   void* Vl(int l) const { return static_cast<char*>(V) + size_t(l) * layer_elems() * dtype_size(dtype); }
@@ -1179,13 +1180,15 @@ struct wc_kv {
 namespace {
 wc_kv* kv_new(wc_ctx* ctx, int layers, int Hk, int D, int cap, int dtype) {
   if (layers <= 0 || Hk <= 0 || D <= 0 || cap <= 0) fail(WC_ERR_INVALID, "bad KV cache shape");
-  auto* kv = new wc_kv{ctx, layers, Hk, D, cap, dtype, nullptr, nullptr, 0};
+  std::unique_ptr<wc_kv, void (*)(wc_kv*)> kv(new wc_kv{ctx, layers, Hk, D, cap, dtype, nullptr, nullptr, 0},
+                                              wc_kv_destroy);
   const size_t bytes = size_t(layers) * kv->layer_elems() * dtype_size(dtype);
   kv->K = dalloc(bytes);
   kv->V = dalloc(bytes);
+  kv->keep = static_cast<int*>(dalloc(sizeof(int) * MAXTREE));
   CUDA_TRY(cudaMemset(kv->K, 0, bytes));
   CUDA_TRY(cudaMemset(kv->V, 0, bytes));
-  return kv;
+  return kv.release();
 }
 }  // namespace
 
@@ -1199,6 +1202,7 @@ extern "C" void wc_kv_destroy(wc_kv* kv) {
   if (!kv) return;
   dfree(kv->K);
   dfree(kv->V);
+  dfree(kv->keep);
   delete kv;
 }
 
@@ -1241,14 +1245,13 @@ void kv_compact_impl(wc_kv* kv, int start, const int* keep_host, int n_keep) {
   for (int i = 0; i < n_keep; ++i) identity &= keep_host[i] == i;
   if (!identity && n_keep > 0) {
     if (n_keep > MAXTREE) fail(WC_ERR_UNSUPPORTED, "keep list longer than 64");
-    int* d_keep = static_cast<int*>(dalloc(sizeof(int) * n_keep));
-    CUDA_TRY(cudaMemcpyAsync(d_keep, keep_host, sizeof(int) * n_keep, cudaMemcpyHostToDevice, kv->ctx->stream));
+    // stream-ordered: a later compaction's copy into kv->keep waits for this kernel; a pageable
+    // source is staged by the copy call, so keep_host may be reused when it returns
+    CUDA_TRY(cudaMemcpyAsync(kv->keep, keep_host, sizeof(int) * n_keep, cudaMemcpyHostToDevice, kv->ctx->stream));
     const int slabs = kv->layers * kv->Hk;
     kv_compact_kernel<<<2 * slabs, 256, size_t(n_keep) * kv->D * sizeof(float), kv->ctx->stream>>>(
-        kv->K, kv->V, kv->dtype, kv->D, kv->cap, slabs, d_keep, n_keep, start);
+        kv->K, kv->V, kv->dtype, kv->D, kv->cap, slabs, kv->keep, n_keep, start);
     check_launch(kv->ctx, "kv_compact");
-    CUDA_TRY(cudaStreamSynchronize(kv->ctx->stream));
-    dfree(d_keep);
   }
   kv->n = start + n_keep;
 }
