@@ -66,6 +66,8 @@ def parse():
     ap.add_argument("--chi2-seeds", type=int, default=1, help="c4: independent states (prompts, seeds) to test")
     ap.add_argument("--profile-rounds", type=int, default=0,
                     help="profiling mode for ncu: short prompt, then N rounds inside the NVTX range 'timed'")
+    ap.add_argument("--profile-prompt", type=int, default=16,
+                    help="profiling mode: prompt tokens before the rounds (512: the bench's context)")
     return ap.parse_args()
 
 
@@ -477,8 +479,9 @@ def bench_reference(a):
 
 
 def profile_mode(a):
-    """Builds the C3 models, prefills a 16-token prompt and runs W + N rounds (random drafter); the
-    last N rounds run inside the NVTX range 'timed' (ncu --nvtx --nvtx-include timed/)."""
+    """Builds the C3 models, prefills a --profile-prompt-token prompt (16 by default; 512 gives the
+    bench's context) and runs W + N rounds (random drafter); the last N rounds run inside the NVTX
+    range 'timed' (ncu --nvtx --nvtx-include timed/)."""
     import torch
 
     from woodcock_b200 import SpeculativeDecoder, StaticPolicy
@@ -487,7 +490,7 @@ def profile_mode(a):
     torch.cuda.set_device(0)
     t, d = build_models(0)
     dec = SpeculativeDecoder(t, d, StaticPolicy(a.k), max_context=PROMPT_LEN + NEW_TOKENS + 64, max_k=max(8, a.k))
-    dec.prefill(syn.prompt_ids(16, syn.Q17_TARGET.vocab, seed=0))
+    dec.prefill(syn.prompt_ids(a.profile_prompt, syn.Q17_TARGET.vocab, seed=0))
     for _ in range(max(3, a.warmup)):
         dec.round(a.k)
     torch.cuda.synchronize()
