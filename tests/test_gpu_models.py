@@ -139,7 +139,7 @@ def test_drafter_head_softmax_is_the_draft_distribution(tiny_models, T):
         q = d.head_softmax(out, T)
         ref = torch.softmax(d.logits(out).double() / T, dim=-1)
         torch.testing.assert_close(q.double(), ref, rtol=1e-5, atol=1e-7)
-        torch.testing.assert_close(q.sum(-1).double(), torch.ones(5, dtype=torch.float64), rtol=0, atol=1e-5)
+        torch.testing.assert_close(q.sum(-1).double().cpu(), torch.ones(5, dtype=torch.float64), rtol=0, atol=1e-5)
     with pytest.raises(ValueError):
         d.head_softmax(out, 0.0)
 

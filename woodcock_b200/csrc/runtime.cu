@@ -118,9 +118,12 @@ struct wc_ctx {
   int gemv_blocks_per_sm = 1;
   bool gemv_wide = true;                 // 80 KB activation chunks for K up to 2560 (WC_GEMV_WIDE=0: split K)
   bool gemv_acs = true;                  // whole-K blocks with streamed activation pieces (WC_GEMV_ACS=0: split K)
-  bool gemv_prefetch = false;            // L2 prefetch of the next GEMV's weights (WC_GEMV_PREFETCH=1;
+  int gemv_prefetch = 0;                 // L2 prefetch of the next GEMV's weights (WC_GEMV_PREFETCH=1;
                                          // measured 1.6% slower on the C3 round: it competes with the
-                                         // dependent loads of the kernels in between)
+                                         // dependent loads of the kernels in between); 2: only the
+                                         // QKV projection's prefetch of O and gate/up
+  int attn_prefetch = 0;                 // the decode attention prefetches the gate/up weights (1) or
+                                         // gate/up and down (2) into L2 while it computes (WC_ATTN_PF)
   size_t gemv_prefetch_cap = 64u << 20;  // bytes prefetched at most
   bool gemv_act_rot = false;             // activation chunks in block-rotated 4 KB pieces (WC_GEMV_ACT_ROT=1)
   int gemv_prefill = 0;                  // weight stages issued before the dependency wait (WC_GEMV_PREFILL; 0: all)
@@ -559,8 +562,9 @@ int gemv_parts(const wc_ctx* ctx, const Lin& W, int L_max) {
 int side_parts(const wc_ctx* ctx, const Lin& W, int L_max) { return std::min(GV_SIDE_BLOCKS, gemv_grid(ctx, W, L_max)); }
 
 // Bytes of `next` to prefetch into L2 while the current GEMV ends (0 = off).
-void gemv_prefetch(const wc_ctx* ctx, GemvParams& p, const Lin* next, const Lin* next2 = nullptr) {
-  if (!ctx->gemv_prefetch) return;
+void gemv_prefetch(const wc_ctx* ctx, GemvParams& p, const Lin* next, const Lin* next2 = nullptr,
+                   bool over_attention = false) {
+  if (!ctx->gemv_prefetch || (ctx->gemv_prefetch == 2 && !over_attention)) return;
   if (next && next->dtype == WC_BF16) {
     p.pf = next->w;
     p.pf_bytes = std::min(next->bytes, ctx->gemv_prefetch_cap);
@@ -568,6 +572,22 @@ void gemv_prefetch(const wc_ctx* ctx, GemvParams& p, const Lin* next, const Lin*
   if (next2 && next2->dtype == WC_BF16) {
     p.pf2 = next2->w;
     p.pf2_bytes = std::min(next2->bytes, ctx->gemv_prefetch_cap);
+  }
+}
+
+// The decode attention's L2 prefetch of the MLP weights (bf16; WC_ATTN_PF=1: gate/up, 2: and down).
+// The O projection is not among them: its blocks on the SMs the attention leaves free fill their
+// weight rings while the attention runs.
+void attn_prefetch(const wc_ctx* ctx, AttnParams& a, const Lin* next, const Lin* next2) {
+  if (!ctx->attn_prefetch) return;
+  if (ctx->attn_prefetch < 2) next2 = nullptr;
+  if (next && next->dtype == WC_BF16) {
+    a.pf = next->w;
+    a.pf_bytes = std::min(next->bytes, ctx->gemv_prefetch_cap);
+  }
+  if (next2 && next2->dtype == WC_BF16) {
+    a.pf2 = next2->w;
+    a.pf2_bytes = std::min(next2->bytes, ctx->gemv_prefetch_cap);
   }
 }
 
@@ -776,7 +796,8 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
     if (const char* e = std::getenv("WC_GEMV_BLOCKS_PER_SM")) ctx->gemv_blocks_per_sm = std::max(1, std::atoi(e));
     if (const char* e = std::getenv("WC_ATTN")) ctx->attn_mode = std::atoi(e);
     if (const char* e = std::getenv("WC_ATTN_SPLIT_POS")) ctx->attn_split_pos = std::max(16, std::atoi(e));
-    if (const char* e = std::getenv("WC_GEMV_PREFETCH")) ctx->gemv_prefetch = std::atoi(e) != 0;
+    if (const char* e = std::getenv("WC_GEMV_PREFETCH")) ctx->gemv_prefetch = std::max(0, std::atoi(e));
+    if (const char* e = std::getenv("WC_ATTN_PF")) ctx->attn_prefetch = std::max(0, std::atoi(e));
     if (const char* e = std::getenv("WC_GEMV_ACS")) ctx->gemv_acs = std::atoi(e) != 0;
     if (const char* e = std::getenv("WC_GEMV_WIDE")) ctx->gemv_wide = std::atoi(e) != 0;
     if (const char* e = std::getenv("WC_GEMV_PREFETCH_MB")) ctx->gemv_prefetch_cap = size_t(std::max(0, std::atoi(e))) << 20;
@@ -1566,7 +1587,7 @@ XIn target_layers(wc_target* t, wc_kv* kv, const Rows& r, XIn in0, float* h, con
       p.y = t->ws_qkv;
       p.ldy = ld_qkv;
       p.err = err;
-      gemv_prefetch(ctx, p, &Ly.o, &Ly.gu);  // both land while attention runs
+      gemv_prefetch(ctx, p, &Ly.o, &Ly.gu, true);  // both land while attention runs
       prof_begin(ctx, PK_QKV);
       launch_gemv(ctx, Ly.qkv, p);
       prof_end(ctx, PK_QKV);
@@ -1604,6 +1625,7 @@ XIn target_layers(wc_target* t, wc_kv* kv, const Rows& r, XIn in0, float* h, con
       a.write_cache = 1;
       a.stable_prefix = r.stable ? 1 : 0;
       a.err = err;
+      attn_prefetch(ctx, a, &Ly.gu, &Ly.down);
       prof_begin(ctx, PK_ATTN);
       launch_attention(ctx, a);
       prof_end(ctx, PK_ATTN);
@@ -2069,7 +2091,7 @@ XIn drafter_layers(wc_drafter* d, wc_kv* kv, const Rows& r, XIn feat_in, const f
       p.y = d->ws_qkv;
       p.ldy = ld_qkv;
       p.err = err;
-      gemv_prefetch(ctx, p, &Ly.o, &Ly.gu);  // both land while attention runs
+      gemv_prefetch(ctx, p, &Ly.o, &Ly.gu, true);  // both land while attention runs
       launch_gemv(ctx, table ? Ly.qkv_main : Ly.qkv, p);
     }
     {
@@ -2107,6 +2129,7 @@ XIn drafter_layers(wc_drafter* d, wc_kv* kv, const Rows& r, XIn feat_in, const f
       a.write_cache = 1;
       a.stable_prefix = r.stable ? 1 : 0;
       a.err = err;
+      attn_prefetch(ctx, a, &Ly.gu, &Ly.down);
       launch_attention(ctx, a);
     }
     {
