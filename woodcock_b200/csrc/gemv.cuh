@@ -167,8 +167,6 @@ struct GemvParams {
   float* side_y;
   XOut side_out;
   float* side_ss;        // [side_blocks][16]
-  int act_rot;           // activation chunk copied in 4 KB pieces from a block-dependent first piece
-  int prefill;           // weight stages issued before the dependency wait (0: the whole ring)
   int* err;
 };
 
@@ -539,10 +537,8 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
                       full + st, pol);
       };
       int issued = 0;
-      // weights do not depend on the previous kernel: fill the ring (or its first p.prefill
-      // stages) before waiting on it
-      const int pre = min(total, p.prefill > 0 ? min(p.prefill, NS) : NS);
-      for (; issued < pre; ++issued) issue(issued);
+      // weights do not depend on the previous kernel: fill the ring before waiting on it
+      for (; issued < min(total, NS); ++issued) issue(issued);
       pdl_wait();
       // statistics of the normalised segments, into the reduction buffers (unused until the
       // first unit is handed over), ahead of the larger activation copy
@@ -576,7 +572,6 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
         // j - depth and weight slot j % NS after step j - NS: issue in the order they free
         int aiss = 0;
         for (; aiss < min(ns, GV_ACS_DEPTH); ++aiss) issue_act(aiss);
-        for (; issued < min(total, NS); ++issued) issue(issued);  // the ring's first use: slots free
         for (int k = 0; ok && (issued < total || aiss < ns); ++k) {
           if (issued < total && issued == k + NS) {
             const int st = issued % NS;
@@ -610,7 +605,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
           }
         }
         mbar_arrive_expect_tx(act_bar, act_bytes);
-        if (!p.act_rot) {
+        {
           int s = 0, f = 0;
           for (int sl = s0; sl < s1; ++sl) {
             while (s + 1 < p.nseg && sl >= f + p.seg[s].lenp / GV_COLS) f += p.seg[s++].lenp / GV_COLS;
@@ -620,28 +615,6 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
               bulk_g2s(act + (nt * CHS + (sl - s0)) * GV_STAGE_BYTES,
                        reinterpret_cast<const char*>(sg.xf) + (size_t(nt) * (sg.lenp >> 4) + size_t(sl - f) * GV_SLAB) * 512,
                        GV_STAGE_BYTES, act_bar);
-          }
-        } else {
-          // every block reads the same rows: 4 KB pieces from a block-dependent first piece
-          constexpr int PC = 4, PB = GV_STAGE_BYTES / PC;
-          const int npc = int(act_bytes / PB);
-          const int first = npc ? int((blockIdx.x * 5u) % unsigned(npc)) : 0;
-          for (int i = 0; i < npc; ++i) {
-            int q = (first + i) % npc;
-            const int pc = q % PC;
-            q /= PC;
-            const int nt = q % NT;
-            q /= NT;  // q-th slab of [s0, s1) that has fragments
-            int s = 0, f = 0, sl = s0;
-            for (;; ++sl) {
-              while (s + 1 < p.nseg && sl >= f + p.seg[s].lenp / GV_COLS) f += p.seg[s++].lenp / GV_COLS;
-              if (p.seg[s].xf && q-- == 0) break;
-            }
-            const XSeg& sg = p.seg[s];
-            bulk_g2s(act + (nt * CHS + (sl - s0)) * GV_STAGE_BYTES + pc * PB,
-                     reinterpret_cast<const char*>(sg.xf) + (size_t(nt) * (sg.lenp >> 4) + size_t(sl - f) * GV_SLAB) * 512 +
-                         pc * PB,
-                     PB, act_bar);
           }
         }
         for (; issued < total; ++issued) {

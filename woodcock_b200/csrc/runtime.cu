@@ -125,8 +125,6 @@ struct wc_ctx {
   int attn_prefetch = 0;                 // the decode attention prefetches the gate/up weights (1) or
                                          // gate/up and down (2) into L2 while it computes (WC_ATTN_PF)
   size_t gemv_prefetch_cap = 64u << 20;  // bytes prefetched at most
-  bool gemv_act_rot = false;             // activation chunks in block-rotated 4 KB pieces (WC_GEMV_ACT_ROT=1)
-  int gemv_prefill = 0;                  // weight stages issued before the dependency wait (WC_GEMV_PREFILL; 0: all)
   float* gv_partial = nullptr;           // split-K partial sums
   size_t gv_partial_n = 0;               // floats
   int* gv_counters = nullptr;            // split-K arrival counters (zero between launches)
@@ -639,8 +637,6 @@ void launch_gemv(wc_ctx* ctx, const Lin& W, GemvParams p) {
     p.nkc = g.nkc;
     p.kc_slabs = g.kc_slabs;
     p.gpk = g.gpk;
-    p.act_rot = ctx->gemv_act_rot;
-    p.prefill = ctx->gemv_prefill;
     const bool nt2 = p.L_max > 8;
     if (!p.acs && g.kc_slabs > (g.wide ? (nt2 ? GV_WIDE2_SLABS : GV_WIDE_SLABS) : gv_chunk_slabs(nt2 ? 2 : 1)))
       fail(WC_ERR_INVALID, "GEMV chunk above the buffer");
@@ -801,8 +797,6 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
     if (const char* e = std::getenv("WC_GEMV_ACS")) ctx->gemv_acs = std::atoi(e) != 0;
     if (const char* e = std::getenv("WC_GEMV_WIDE")) ctx->gemv_wide = std::atoi(e) != 0;
     if (const char* e = std::getenv("WC_GEMV_PREFETCH_MB")) ctx->gemv_prefetch_cap = size_t(std::max(0, std::atoi(e))) << 20;
-    if (const char* e = std::getenv("WC_GEMV_ACT_ROT")) ctx->gemv_act_rot = std::atoi(e) != 0;
-    if (const char* e = std::getenv("WC_GEMV_PREFILL")) ctx->gemv_prefill = std::max(0, std::atoi(e));
     ctx->d_err = static_cast<int*>(dalloc(sizeof(int)));
     CUDA_TRY(cudaMemset(ctx->d_err, 0, sizeof(int)));
     ctx->gv_partial_n = size_t(8) << 20;  // 32 MB of split-K partials
