@@ -86,6 +86,10 @@ __device__ __forceinline__ float4 ldg_stream_f4(const float4* p) {
 }
 
 // Bulk prefetch of [p, p+bytes) into L2 (bytes multiple of 16, p 16-byte aligned).
+__device__ __forceinline__ void prefetch_l2_line(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];\n" ::"l"(p));
+}
+
 __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"(bytes) : "memory");
 }

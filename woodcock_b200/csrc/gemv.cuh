@@ -167,6 +167,8 @@ struct GemvParams {
   float* side_y;
   XOut side_out;
   float* side_ss;        // [side_blocks][16]
+  int self_pf;           // bytes of this block's own weights past the ring to prefetch into L2
+                         // before the dependency wait (multiple of 16 KB; 0: none)
   int* err;
 };
 
@@ -648,6 +650,18 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
 
   if (warp > GV_CWARPS) {  // ---- epilogue warps
     const int et = tid - (GV_CWARPS + 1) * kWarp;
+    if (p.self_pf > 0 && total > NS) {
+      // idle until the first unit: pull this block's weight stages past the ring into L2 with
+      // plain line prefetches (the bulk-copy queue stays free for the activation copy)
+      const char* w = static_cast<const char*>(p.w);
+      const int q1 = min(total, NS + p.self_pf / GV_STAGE_BYTES);
+      constexpr int LPS = GV_STAGE_BYTES / 128;  // 128-byte lines per stage
+      for (int i = et; i < (q1 - NS) * LPS; i += GV_ETHREADS) {
+        const int q = NS + i / LPS, rbl = q / ns, si = q % ns;
+        const size_t rb = size_t(u0) * G + rbl;
+        prefetch_l2_line(w + (rb * KT + size_t(s0 + si) * GV_SLAB) * 512 + size_t(i % LPS) * 128);
+      }
+    }
     pdl_wait();
     const int L = gemv_rows(p.L_dev, p.L, p.L_max, nullptr);
     if (et < 16) {

@@ -122,6 +122,8 @@ struct wc_ctx {
                                          // measured 1.6% slower on the C3 round: it competes with the
                                          // dependent loads of the kernels in between); 2: only the
                                          // QKV projection's prefetch of O and gate/up
+  int gemv_self_pf = 0;                  // KB of a GEMV block's own weights past its ring prefetched
+                                         // into L2 before the dependency wait (WC_GEMV_SELF_PF)
   int attn_prefetch = 0;                 // the decode attention prefetches the gate/up weights (1) or
                                          // gate/up and down (2) into L2 while it computes (WC_ATTN_PF)
   size_t gemv_prefetch_cap = 64u << 20;  // bytes prefetched at most
@@ -637,6 +639,7 @@ void launch_gemv(wc_ctx* ctx, const Lin& W, GemvParams p) {
     p.nkc = g.nkc;
     p.kc_slabs = g.kc_slabs;
     p.gpk = g.gpk;
+    p.self_pf = ctx->gemv_self_pf * 1024;
     const bool nt2 = p.L_max > 8;
     if (!p.acs && g.kc_slabs > (g.wide ? (nt2 ? GV_WIDE2_SLABS : GV_WIDE_SLABS) : gv_chunk_slabs(nt2 ? 2 : 1)))
       fail(WC_ERR_INVALID, "GEMV chunk above the buffer");
@@ -794,6 +797,7 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
     if (const char* e = std::getenv("WC_ATTN_SPLIT_POS")) ctx->attn_split_pos = std::max(16, std::atoi(e));
     if (const char* e = std::getenv("WC_GEMV_PREFETCH")) ctx->gemv_prefetch = std::max(0, std::atoi(e));
     if (const char* e = std::getenv("WC_ATTN_PF")) ctx->attn_prefetch = std::max(0, std::atoi(e));
+    if (const char* e = std::getenv("WC_GEMV_SELF_PF")) ctx->gemv_self_pf = std::max(0, std::atoi(e)) / 16 * 16;
     if (const char* e = std::getenv("WC_GEMV_ACS")) ctx->gemv_acs = std::atoi(e) != 0;
     if (const char* e = std::getenv("WC_GEMV_WIDE")) ctx->gemv_wide = std::atoi(e) != 0;
     if (const char* e = std::getenv("WC_GEMV_PREFETCH_MB")) ctx->gemv_prefetch_cap = size_t(std::max(0, std::atoi(e))) << 20;
