@@ -75,12 +75,6 @@ struct AttnParams {
   int stable_prefix;  // n_dev and the cache rows below it were written by completed work
                       // (not by a kernel that may still run): they may be read before the
                       // dependency wait
-  // optional L2 prefetch of the next projections' weights (up to two regions), split over the
-  // blocks and issued once the kernel's own dependent loads have landed (decode kernel)
-  const void* pf;
-  size_t pf_bytes;
-  const void* pf2;
-  size_t pf2_bytes;
   int* err;
 };
 

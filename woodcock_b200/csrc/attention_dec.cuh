@@ -234,17 +234,6 @@ __global__ void __launch_bounds__(AD_THREADS, 1) attention_dec_kernel(__grid_con
   }
   cp_async_commit();
   __syncthreads();
-  if (tid == 0) {  // HBM is idle for the rest of this kernel: stream the next weights into L2
-    const int nb = int(gridDim.x * gridDim.y), b = int(blockIdx.y * gridDim.x + blockIdx.x);
-    for (int rgn = 0; rgn < 2; ++rgn) {
-      const char* pfp = static_cast<const char*>(rgn ? p.pf2 : p.pf);
-      const size_t pfb = rgn ? p.pf2_bytes : p.pf_bytes;
-      if (!pfp || pfb < 16) continue;
-      const size_t per = ((pfb / nb) + 15) & ~size_t(15);
-      const size_t b0 = per * b, b1 = min(pfb & ~size_t(15), b0 + per);
-      for (size_t o = b0; o < b1; o += (1u << 20)) prefetch_l2_bulk(pfp + o, uint32_t(min(size_t(1u << 20), b1 - o)));
-    }
-  }
 
   // ---- round trip 2: RoPE rows (unless fetched before the wait)
   if (!rope_ready || n != npre + p.n_add) {

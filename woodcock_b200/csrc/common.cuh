@@ -86,10 +86,6 @@ __device__ __forceinline__ float4 ldg_stream_f4(const float4* p) {
 }
 
 // Bulk prefetch of [p, p+bytes) into L2 (bytes multiple of 16, p 16-byte aligned).
-__device__ __forceinline__ void prefetch_l2_line(const void* p) {
-  asm volatile("prefetch.global.L2 [%0];\n" ::"l"(p));
-}
-
 __device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;\n" ::"l"(p), "r"(bytes) : "memory");
 }
@@ -101,20 +97,6 @@ __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory");
 }
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
-
-// Kernel parameters live in a per-launch constant buffer, so the first use of each of its
-// lines misses, and spread along a kernel those misses add up one after another. A kernel
-// with a large parameter block copies it into shared memory at entry (one parallel load,
-// before the dependency wait) and reads every field from there. The parameter must be
-// declared __grid_constant__ so that its address refers to it; call from all threads,
-// followed by a barrier.
-template <typename P>
-__device__ __forceinline__ void params_to_smem(const P& p, P* dst) {
-  static_assert(sizeof(P) % 4 == 0, "parameter block size");
-  const uint32_t* src = reinterpret_cast<const uint32_t*>(&p);
-  uint32_t* d = reinterpret_cast<uint32_t*>(dst);
-  for (unsigned i = threadIdx.x; i < sizeof(P) / 4; i += blockDim.x) d[i] = src[i];
-}
 
 // Orderable argmax key: larger value first, then the smaller index (first maximum,
 // like std::max_element / np.argmax). atomicMax over keys is order-independent.

@@ -167,8 +167,6 @@ struct GemvParams {
   float* side_y;
   XOut side_out;
   float* side_ss;        // [side_blocks][16]
-  int self_pf;           // bytes of this block's own weights past the ring to prefetch into L2
-                         // before the dependency wait (multiple of 16 KB; 0: none)
   int* err;
 };
 
@@ -457,8 +455,7 @@ struct GvLayout {
   static constexpr size_t btok = tok + 16 * 4;                             // [16] ints (epilogue's tokens)
   static constexpr size_t flag = btok + 16 * 4;                            // [4] ints
   static constexpr size_t key = flag + 16;                                 // [16] u64
-  static constexpr size_t params = key + 16 * 8;
-  static constexpr size_t total = params + (sizeof(GemvParams) + 15) / 16 * 16;
+  static constexpr size_t total = key + 16 * 8;
   static_assert(red_buf * 4 >= 8 * 256 * 4 || NT == 2, "split-K staging needs 8 KB of the reduction buffers");
 };
 
@@ -493,35 +490,32 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
   int* s_flag = reinterpret_cast<int*>(gv_smem + Lay::flag);
   unsigned long long* s_key = reinterpret_cast<unsigned long long*>(gv_smem + Lay::key);
   const uint4* act4 = reinterpret_cast<const uint4*>(act);
-  GemvParams* s_params = reinterpret_cast<GemvParams*>(gv_smem + Lay::params);
-  params_to_smem(pk, s_params);
-  __syncthreads();
-  const GemvParams& p = *s_params;
+  // parameters are read in place (a copy to shared memory cost ~0.4 us per launch: the
+  // threads' distinct words serialise in the constant cache)
+  const GemvParams& p = pk;
 
   const int tid = threadIdx.x, warp = tid / kWarp, lane = tid % kWarp;
   const int G = p.group;
   const int nunits = p.Np / (16 * G);
   const int KT = p.Kp >> 4;
   const int nslab = KT / GV_SLAB;
-  const int kc = int(blockIdx.x) % p.nkc, gi = int(blockIdx.x) / p.nkc;
-  const int u0 = int((long long)gi * nunits / p.gpk), u1 = int((long long)(gi + 1) * nunits / p.gpk);
+  // 32-bit work split (gi < grid <= a few hundred, nunits < 2^14): no 64-bit divisions
+  const unsigned nkc = unsigned(p.nkc), gpk = unsigned(p.gpk);
+  const int kc = int(blockIdx.x % nkc), gi = int(blockIdx.x / nkc);
+  const int u0 = int(unsigned(gi) * unsigned(nunits) / gpk), u1 = int(unsigned(gi + 1) * unsigned(nunits) / gpk);
   const int s0 = kc * p.kc_slabs, s1 = min(nslab, s0 + p.kc_slabs), ns = s1 - s0;
   const int total = (u1 - u0) * G * ns;  // ring stages: unit, row block of the unit, slab
-  if (tid == 0) {
-    for (int s = 0; s < NS; ++s) {
-      mbar_init(full + s, 1);
-      mbar_init(empty + s, GV_CWARPS);
-    }
-    mbar_init(act_bar, 1);
-    mbar_init(ss_bar, 1);
-    for (int b = 0; b < GV_ACS_DEPTH; ++b) {
-      mbar_init(act_full + b, 1);
-      mbar_init(act_empty + b, GV_CWARPS);
-    }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(red_full + b, GV_CTHREADS);
-      mbar_init(red_empty + b, GV_ETHREADS);
-    }
+  if (tid < int(Lay::nbars)) {  // one barrier per thread, in the order of the layout above
+    uint32_t cnt;
+    if (tid < NS) cnt = 1;                                          // full
+    else if (tid < 2 * NS) cnt = GV_CWARPS;                         // empty
+    else if (tid == 2 * NS) cnt = 1;                                // act_bar
+    else if (tid < 2 * NS + 3) cnt = GV_CTHREADS;                   // red_full
+    else if (tid < 2 * NS + 5) cnt = GV_ETHREADS;                   // red_empty
+    else if (tid == 2 * NS + 5) cnt = 1;                            // ss_bar
+    else if (tid < 2 * NS + 6 + GV_ACS_DEPTH) cnt = 1;              // act_full
+    else cnt = GV_CWARPS;                                           // act_empty
+    mbar_init(full + tid, cnt);
     mbar_fence_init();
   }
   __syncthreads();
@@ -650,18 +644,6 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
 
   if (warp > GV_CWARPS) {  // ---- epilogue warps
     const int et = tid - (GV_CWARPS + 1) * kWarp;
-    if (p.self_pf > 0 && total > NS) {
-      // idle until the first unit: pull this block's weight stages past the ring into L2 with
-      // plain line prefetches (the bulk-copy queue stays free for the activation copy)
-      const char* w = static_cast<const char*>(p.w);
-      const int q1 = min(total, NS + p.self_pf / GV_STAGE_BYTES);
-      constexpr int LPS = GV_STAGE_BYTES / 128;  // 128-byte lines per stage
-      for (int i = et; i < (q1 - NS) * LPS; i += GV_ETHREADS) {
-        const int q = NS + i / LPS, rbl = q / ns, si = q % ns;
-        const size_t rb = size_t(u0) * G + rbl;
-        prefetch_l2_line(w + (rb * KT + size_t(s0 + si) * GV_SLAB) * 512 + size_t(i % LPS) * 128);
-      }
-    }
     pdl_wait();
     const int L = gemv_rows(p.L_dev, p.L, p.L_max, nullptr);
     if (et < 16) {

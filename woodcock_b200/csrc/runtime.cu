@@ -121,11 +121,7 @@ struct wc_ctx {
   int gemv_prefetch = 0;                 // L2 prefetch of the next GEMV's weights (WC_GEMV_PREFETCH=1;
                                          // measured 1.6% slower on the C3 round: it competes with the
                                          // dependent loads of the kernels in between); 2: only the
-                                         // QKV projection's prefetch of O and gate/up
-  int gemv_self_pf = 0;                  // KB of a GEMV block's own weights past its ring prefetched
-                                         // into L2 before the dependency wait (WC_GEMV_SELF_PF)
-  int attn_prefetch = 0;                 // the decode attention prefetches the gate/up weights (1) or
-                                         // gate/up and down (2) into L2 while it computes (WC_ATTN_PF)
+                                         // QKV projection's prefetch of O and gate/up (1.4% slower)
   size_t gemv_prefetch_cap = 64u << 20;  // bytes prefetched at most
   float* gv_partial = nullptr;           // split-K partial sums
   size_t gv_partial_n = 0;               // floats
@@ -575,22 +571,6 @@ void gemv_prefetch(const wc_ctx* ctx, GemvParams& p, const Lin* next, const Lin*
   }
 }
 
-// The decode attention's L2 prefetch of the MLP weights (bf16; WC_ATTN_PF=1: gate/up, 2: and down).
-// The O projection is not among them: its blocks on the SMs the attention leaves free fill their
-// weight rings while the attention runs.
-void attn_prefetch(const wc_ctx* ctx, AttnParams& a, const Lin* next, const Lin* next2) {
-  if (!ctx->attn_prefetch) return;
-  if (ctx->attn_prefetch < 2) next2 = nullptr;
-  if (next && next->dtype == WC_BF16) {
-    a.pf = next->w;
-    a.pf_bytes = std::min(next->bytes, ctx->gemv_prefetch_cap);
-  }
-  if (next2 && next2->dtype == WC_BF16) {
-    a.pf2 = next2->w;
-    a.pf2_bytes = std::min(next2->bytes, ctx->gemv_prefetch_cap);
-  }
-}
-
 void launch_gemv(wc_ctx* ctx, const Lin& W, GemvParams p) {
   const bool bf16 = W.dtype == WC_BF16;
   p.w = W.w;
@@ -639,7 +619,6 @@ void launch_gemv(wc_ctx* ctx, const Lin& W, GemvParams p) {
     p.nkc = g.nkc;
     p.kc_slabs = g.kc_slabs;
     p.gpk = g.gpk;
-    p.self_pf = ctx->gemv_self_pf * 1024;
     const bool nt2 = p.L_max > 8;
     if (!p.acs && g.kc_slabs > (g.wide ? (nt2 ? GV_WIDE2_SLABS : GV_WIDE_SLABS) : gv_chunk_slabs(nt2 ? 2 : 1)))
       fail(WC_ERR_INVALID, "GEMV chunk above the buffer");
@@ -796,8 +775,6 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
     if (const char* e = std::getenv("WC_ATTN")) ctx->attn_mode = std::atoi(e);
     if (const char* e = std::getenv("WC_ATTN_SPLIT_POS")) ctx->attn_split_pos = std::max(16, std::atoi(e));
     if (const char* e = std::getenv("WC_GEMV_PREFETCH")) ctx->gemv_prefetch = std::max(0, std::atoi(e));
-    if (const char* e = std::getenv("WC_ATTN_PF")) ctx->attn_prefetch = std::max(0, std::atoi(e));
-    if (const char* e = std::getenv("WC_GEMV_SELF_PF")) ctx->gemv_self_pf = std::max(0, std::atoi(e)) / 16 * 16;
     if (const char* e = std::getenv("WC_GEMV_ACS")) ctx->gemv_acs = std::atoi(e) != 0;
     if (const char* e = std::getenv("WC_GEMV_WIDE")) ctx->gemv_wide = std::atoi(e) != 0;
     if (const char* e = std::getenv("WC_GEMV_PREFETCH_MB")) ctx->gemv_prefetch_cap = size_t(std::max(0, std::atoi(e))) << 20;
@@ -1623,7 +1600,6 @@ XIn target_layers(wc_target* t, wc_kv* kv, const Rows& r, XIn in0, float* h, con
       a.write_cache = 1;
       a.stable_prefix = r.stable ? 1 : 0;
       a.err = err;
-      attn_prefetch(ctx, a, &Ly.gu, &Ly.down);
       prof_begin(ctx, PK_ATTN);
       launch_attention(ctx, a);
       prof_end(ctx, PK_ATTN);
@@ -2127,7 +2103,6 @@ XIn drafter_layers(wc_drafter* d, wc_kv* kv, const Rows& r, XIn feat_in, const f
       a.write_cache = 1;
       a.stable_prefix = r.stable ? 1 : 0;
       a.err = err;
-      attn_prefetch(ctx, a, &Ly.gu, &Ly.down);
       launch_attention(ctx, a);
     }
     {
