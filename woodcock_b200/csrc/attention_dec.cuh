@@ -15,6 +15,10 @@
 // last CTA, and CTA 0 appends them to the cache. S = Q K^T and O += P V run on m16n8k16
 // MMAs with Q and P split into bf16 hi + lo terms; warps merge in shared memory, CTAs through
 // distributed shared memory, and the result is emitted as the O projection's input fragments.
+// With one m-tile (at most 16 query rows per KV head) every CTA pushes the column slices of its
+// merged partial state into the CTA that owns those columns, so one cluster barrier suffices
+// and each CTA merges and emits from its own shared memory (no final barrier); two m-tiles
+// merge by reading the peers' partial states between two barriers.
 #pragma once
 
 #include <cooperative_groups.h>
@@ -44,9 +48,13 @@ struct AdLayout {
   static constexpr size_t raw_bytes = size_t(AD_MAXR + 2 * AD_MAXL) * D * 4;
   static constexpr size_t pacc_bytes = size_t(AD_MAXR) * D * 4;
   static constexpr size_t region_b = raw_bytes > pacc_bytes ? raw_bytes : pacc_bytes;
-  static constexpr size_t total = 2 * q_bytes + region_a + tail_bytes + region_b + 2 * D * 4 +
-                                  size_t(AD_MAXL) * (D / 2) * 8 + AD_MAXL * 4 + 2 * AD_WARPS * AD_MAXR * 4 +
-                                  2 * AD_MAXR * 4 + 64;
+  static constexpr size_t base_total = 2 * q_bytes + region_a + tail_bytes + region_b + 2 * D * 4 +
+                                       size_t(AD_MAXL) * (D / 2) * 8 + AD_MAXL * 4 + 2 * AD_WARPS * AD_MAXR * 4 +
+                                       2 * AD_MAXR * 4 + 64;
+  // one-m-tile merge: partial column slices pushed by every CTA of the cluster
+  static constexpr size_t rx_off = (base_total + 15) / 16 * 16;
+  static constexpr size_t rx_bytes = size_t(AD_CLUSTER) * 16 * (D / AD_CLUSTER) * 4 + size_t(AD_CLUSTER) * 16 * 2 * 4;
+  static constexpr size_t total = rx_off + rx_bytes;
 };
 
 template <int D>
@@ -530,6 +538,48 @@ __global__ void __launch_bounds__(AD_THREADS, 1) attention_dec_kernel(__grid_con
       if (wt != 0.f) acc = fmaf(wt, ow[(w * AD_MAXR + r) * D + d], acc);  // idle warps have weight 0
     }
     pacc[r * D + d] = acc;
+  }
+  if constexpr (MT == 1) {
+    constexpr int CW = D / AD_CLUSTER;  // output columns this CTA merges and emits
+    float* rx = reinterpret_cast<float*>(ad_smem + Lay::rx_off);  // [source CTA][16 rows][CW]
+    float* rml = rx + AD_CLUSTER * 16 * CW;                         // [source CTA][16 rows][m, l]
+    __syncthreads();  // pacc complete
+    for (int idx = tid; idx < R * D; idx += AD_THREADS) {
+      const int r = idx / D, d = idx % D;
+      cluster.map_shared_rank(rx, d / CW)[(rank * 16 + r) * CW + d % CW] = pacc[r * D + d];
+    }
+    if (tid < R * AD_CLUSTER) {
+      const int r = tid / AD_CLUSTER, j = tid % AD_CLUSTER;
+      float* dst = cluster.map_shared_rank(rml, j) + (rank * 16 + r) * 2;
+      dst[0] = pm[r];
+      dst[1] = pl[r];
+    }
+    cluster.sync();  // every CTA's slices have landed; only local shared memory is read below
+    float* cw = lw;  // [MAXR][CLUSTER] weights / l
+    if (warp * kWarp < R * AD_CLUSTER) {  // whole warps take part in the shuffles
+      const bool act = tid < R * AD_CLUSTER;
+      const int r = act ? tid / AD_CLUSTER : 0, s2 = tid % AD_CLUSTER;
+      const float mv = act ? rml[(s2 * 16 + r) * 2] : -INFINITY;
+      const float lv = act ? rml[(s2 * 16 + r) * 2 + 1] : 0.f;
+      float M = mv;
+#pragma unroll
+      for (int o2 = 1; o2 < AD_CLUSTER; o2 <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
+      const float wt = (mv == -INFINITY) ? 0.f : expf(mv - M);
+      float lt = wt * lv;
+#pragma unroll
+      for (int o2 = 1; o2 < AD_CLUSTER; o2 <<= 1) lt += __shfl_xor_sync(0xffffffffu, lt, o2);
+      if (act) cw[r * AD_CLUSTER + s2] = wt / lt;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < R * CW; idx += AD_THREADS) {
+      const int r = idx / CW, c = idx % CW;
+      float acc = 0.f;
+#pragma unroll
+      for (int s2 = 0; s2 < AD_CLUSTER; ++s2) acc = fmaf(cw[r * AD_CLUSTER + s2], rx[(s2 * 16 + r) * CW + c], acc);
+      const int l = r / rep, h = hk * rep + r % rep;
+      attn_emit(p, l, h * D + rank * CW + c, acc);
+    }
+    return;  // no peer reads this CTA's shared memory after the barrier
   }
   cluster.sync();
   // ---- merge the cluster's CTAs through distributed shared memory. This CTA emits elements
