@@ -505,18 +505,20 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
   const int u0 = int(unsigned(gi) * unsigned(nunits) / gpk), u1 = int(unsigned(gi + 1) * unsigned(nunits) / gpk);
   const int s0 = kc * p.kc_slabs, s1 = min(nslab, s0 + p.kc_slabs), ns = s1 - s0;
   const int total = (u1 - u0) * G * ns;  // ring stages: unit, row block of the unit, slab
-  if (tid < int(Lay::nbars)) {  // one barrier per thread, in the order of the layout above
-    uint32_t cnt;
-    if (tid < NS) cnt = 1;                                          // full
-    else if (tid < 2 * NS) cnt = GV_CWARPS;                         // empty
-    else if (tid == 2 * NS) cnt = 1;                                // act_bar
-    else if (tid < 2 * NS + 3) cnt = GV_CTHREADS;                   // red_full
-    else if (tid < 2 * NS + 5) cnt = GV_ETHREADS;                   // red_empty
-    else if (tid == 2 * NS + 5) cnt = 1;                            // ss_bar
-    else if (tid < 2 * NS + 6 + GV_ACS_DEPTH) cnt = 1;              // act_full
-    else cnt = GV_CWARPS;                                           // act_empty
-    mbar_init(full + tid, cnt);
+  if (tid == GV_CWARPS * kWarp) {  // the producer lane: every barrier a bulk copy completes, one fence
+    for (int s = 0; s < NS; ++s) mbar_init(full + s, 1);
+    mbar_init(act_bar, 1);
+    mbar_init(ss_bar, 1);
+    for (int b = 0; b < GV_ACS_DEPTH; ++b) mbar_init(act_full + b, 1);
     mbar_fence_init();
+  } else if (tid < NS) {  // arrivals from threads only: ordered by the barrier below
+    mbar_init(empty + tid, GV_CWARPS);
+  } else if (tid >= 32 && tid < 32 + GV_ACS_DEPTH) {
+    mbar_init(act_empty + (tid - 32), GV_CWARPS);
+  } else if (tid >= 64 && tid < 66) {
+    mbar_init(red_full + (tid - 64), GV_CTHREADS);
+  } else if (tid >= 96 && tid < 98) {
+    mbar_init(red_empty + (tid - 96), GV_ETHREADS);
   }
   __syncthreads();
   pdl_launch_dependents();
