@@ -88,6 +88,14 @@ __global__ void __launch_bounds__(AD_THREADS, 1) attention_dec_kernel(__grid_con
   float* ow = reinterpret_cast<float*>(reg_a);                             // [WARPS][MAXR][D]
 
   cg::cluster_group cluster = cg::this_cluster();
+  // scalar parameters used in the dependent phases, read before the dependency wait and held in
+  // registers (a parameter-space read there costs a constant-cache miss on the critical path)
+  float pv_eps = p.eps, pv_scale = p.scale;
+  int pv_window = p.window;
+  const float* pv_qn = p.q_norm;
+  const float* pv_kn = p.k_norm;
+  const unsigned long long* pv_nm = p.newmask;
+  asm volatile("" : "+f"(pv_eps), "+f"(pv_scale), "+r"(pv_window), "+l"(pv_qn), "+l"(pv_kn), "+l"(pv_nm));
   const int S = int(cluster.num_blocks());
   const int rank = int(cluster.block_rank());
   const int hk = blockIdx.y;
@@ -101,8 +109,8 @@ __global__ void __launch_bounds__(AD_THREADS, 1) attention_dec_kernel(__grid_con
   // committed prefix length (stable: written by completed work) and the norm gains, together
   const int npre_stable = (p.stable_prefix && p.n_dev) ? *p.n_dev : 0;
   for (int i = tid; i < D; i += AD_THREADS) {  // weights: independent of the previous kernel
-    wq[i] = p.q_norm ? p.q_norm[i] : 1.f;
-    wk[i] = p.k_norm ? p.k_norm[i] : 1.f;
+    wq[i] = pv_qn ? pv_qn[i] : 1.f;
+    wk[i] = pv_kn ? pv_kn[i] : 1.f;
   }
   // this CTA's slice of the committed prefix [0, npre), in 16-position tiles
   int q0 = 0, q1 = 0, ntiles = 0;
@@ -299,9 +307,9 @@ __global__ void __launch_bounds__(AD_THREADS, 1) attention_dec_kernel(__grid_con
     ss += __shfl_xor_sync(0xffffffffu, ss, 1);
     ss += __shfl_xor_sync(0xffffffffu, ss, 2);
     ss += __shfl_xor_sync(0xffffffffu, ss, 4);
-    if (valid && ((is_q && p.q_norm) || (is_k && p.k_norm))) {
+    if (valid && ((is_q && pv_qn) || (is_k && pv_kn))) {
       const float* w = is_q ? wq : wk;
-      const float inv = 1.f / sqrtf(ss / float(D) + p.eps);
+      const float inv = 1.f / sqrtf(ss / float(D) + pv_eps);
 #pragma unroll
       for (int e = 0; e < EPQ; ++e) v[e] = v[e] * inv * w[sub * EPQ + e];
     }
@@ -400,14 +408,14 @@ __global__ void __launch_bounds__(AD_THREADS, 1) attention_dec_kernel(__grid_con
             bool vis = r < R && pos < end;
             if (vis) {
               if (pos < n) {
-                vis = p.window <= 0 || pos >= n + l - p.window + 1;
+                vis = pv_window <= 0 || pos >= n + l - pv_window + 1;
               } else {
                 const int jj = pos - n;
-                vis = p.newmask ? ((p.newmask[l] >> jj) & 1ull) != 0 : jj <= l;
-                if (vis && p.window > 0) vis = pos >= n + l - p.window + 1;
+                vis = pv_nm ? ((pv_nm[l] >> jj) & 1ull) != 0 : jj <= l;
+                if (vis && pv_window > 0) vis = pos >= n + l - pv_window + 1;
               }
             }
-            const float sv = vis ? p.scale * s[mt][nt][2 * h + c] : -INFINITY;
+            const float sv = vis ? pv_scale * s[mt][nt][2 * h + c] : -INFINITY;
             s[mt][nt][2 * h + c] = sv;
             mx = fmaxf(mx, sv);
           }
