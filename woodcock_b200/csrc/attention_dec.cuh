@@ -90,7 +90,7 @@ __global__ void __launch_bounds__(AD_THREADS, 1) attention_dec_kernel(__grid_con
   cg::cluster_group cluster = cg::this_cluster();
   // scalar parameters used in the dependent phases, read before the dependency wait and held in
   // registers (a parameter-space read there costs a constant-cache miss on the critical path)
-  float pv_eps = p.eps, pv_scale = p.scale;
+  float pv_eps = p.eps, pv_scale = p.scale * kLog2e;  // scores in log2 units
   int pv_window = p.window;
   const float* pv_qn = p.q_norm;
   const float* pv_kn = p.k_norm;
@@ -423,14 +423,14 @@ __global__ void __launch_bounds__(AD_THREADS, 1) attention_dec_kernel(__grid_con
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
         const float mn = fmaxf(mrow[mt][h], mx);
         const float alpha = (mn == -INFINITY || mrow[mt][h] == -INFINITY) ? (mn == -INFINITY ? 1.f : 0.f)
-                                                                          : expf(mrow[mt][h] - mn);
+                                                                          : ex2_approx(mrow[mt][h] - mn);
         float sum = 0.f;
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             const float sv = s[mt][nt][2 * h + c];
-            const float e = (sv == -INFINITY) ? 0.f : expf(sv - mn);
+            const float e = (sv == -INFINITY) ? 0.f : ex2_approx(sv - mn);
             s[mt][nt][2 * h + c] = e;
             sum += e;
           }
@@ -523,7 +523,7 @@ __global__ void __launch_bounds__(AD_THREADS, 1) attention_dec_kernel(__grid_con
     float M = mv;
 #pragma unroll
     for (int o2 = 1; o2 < AD_WARPS; o2 <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
-    const float wt = (mv == -INFINITY) ? 0.f : expf(mv - M);
+    const float wt = (mv == -INFINITY) ? 0.f : ex2_approx(mv - M);
     float lt = act ? wt * lw[w * AD_MAXR + r] : 0.f;
 #pragma unroll
     for (int o2 = 1; o2 < AD_WARPS; o2 <<= 1) lt += __shfl_xor_sync(0xffffffffu, lt, o2);
@@ -572,7 +572,7 @@ __global__ void __launch_bounds__(AD_THREADS, 1) attention_dec_kernel(__grid_con
       float M = mv;
 #pragma unroll
       for (int o2 = 1; o2 < AD_CLUSTER; o2 <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
-      const float wt = (mv == -INFINITY) ? 0.f : expf(mv - M);
+      const float wt = (mv == -INFINITY) ? 0.f : ex2_approx(mv - M);
       float lt = wt * lv;
 #pragma unroll
       for (int o2 = 1; o2 < AD_CLUSTER; o2 <<= 1) lt += __shfl_xor_sync(0xffffffffu, lt, o2);
@@ -603,7 +603,7 @@ __global__ void __launch_bounds__(AD_THREADS, 1) attention_dec_kernel(__grid_con
     float M = mv;
 #pragma unroll
     for (int o2 = 1; o2 < AD_CLUSTER; o2 <<= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o2));
-    const float wt = (mv == -INFINITY) ? 0.f : expf(mv - M);
+    const float wt = (mv == -INFINITY) ? 0.f : ex2_approx(mv - M);
     float lt = wt * lv;
 #pragma unroll
     for (int o2 = 1; o2 < AD_CLUSTER; o2 <<= 1) lt += __shfl_xor_sync(0xffffffffu, lt, o2);

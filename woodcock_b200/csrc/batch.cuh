@@ -766,7 +766,7 @@ __global__ void __launch_bounds__(TA_THREADS, 2) tree_attention_kernel(__grid_co
         tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 1));
         tmax[h] = fmaxf(tmax[h], __shfl_xor_sync(0xffffffffu, tmax[h], 2));
         const float mn = fmaxf(mrow[h], tmax[h]);
-        alpha[h] = (mn == -INFINITY) ? 1.f : exp2f(mrow[h] - mn);
+        alpha[h] = (mn == -INFINITY) ? 1.f : ex2_approx(mrow[h] - mn);
         mrow[h] = mn;
       }
       float lt[2] = {0.f, 0.f};
@@ -777,7 +777,7 @@ __global__ void __launch_bounds__(TA_THREADS, 2) tree_attention_kernel(__grid_co
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           const float m = mrow[e >> 1];
-          e4[e] = (s[j][e] == -INFINITY) ? 0.f : exp2f(s[j][e] - m);
+          e4[e] = (s[j][e] == -INFINITY) ? 0.f : ex2_approx(s[j][e] - m);
           lt[e >> 1] += e4[e];
         }
         const int kk = j / 2, hi = j & 1;
@@ -860,7 +860,7 @@ __global__ void __launch_bounds__(128) tree_attn_merge_kernel(__grid_constant__ 
     for (int s = 0; s < S; ++s) {
       const size_t row = base + size_t(s) * TA_MAXR + rho;
       const float2 ml = *reinterpret_cast<const float2*>(p.part_ml + row * 2);
-      const float w = ml.x == -INFINITY ? 0.f : exp2f(ml.x - M);
+      const float w = ml.x == -INFINITY ? 0.f : ex2_approx(ml.x - M);
       const float2 ov = *reinterpret_cast<const float2*>(p.part_o + row * D + d);
       L += w * ml.y;
       o0 += w * ov.x;

@@ -55,6 +55,17 @@ __device__ __forceinline__ void split_bf16(float v, uint16_t& hi, uint16_t& lo) 
   lo = f32_to_bf16_bits(v - bf16_bits_to_f32(hi));
 }
 
+// 2^x with the PTX ex2.approx.ftz.f32 instruction (relative error about 2^-22 per the PTX ISA;
+// subnormal results flush to zero, 2^-inf = +0). The attention kernels keep scores and running
+// maxima in log2 units (e^x = 2^(x log2 e)) and use it for the softmax weights, which they round
+// to bf16 or use to weigh fp32 partial states.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+constexpr float kLog2e = 1.4426950408889634f;
+
 __device__ __forceinline__ uint32_t pack2(uint16_t lo_half, uint16_t hi_half) {
   return uint32_t(lo_half) | (uint32_t(hi_half) << 16);
 }
