@@ -309,7 +309,7 @@ __global__ void __launch_bounds__(AD_THREADS, 1) attention_dec_kernel(__grid_con
     ss += __shfl_xor_sync(0xffffffffu, ss, 4);
     if (valid && ((is_q && pv_qn) || (is_k && pv_kn))) {
       const float* w = is_q ? wq : wk;
-      const float inv = 1.f / sqrtf(ss / float(D) + pv_eps);
+      const float inv = rsqrtf(ss / float(D) + pv_eps);
 #pragma unroll
       for (int e = 0; e < EPQ; ++e) v[e] = v[e] * inv * w[sub * EPQ + e];
     }

@@ -287,7 +287,7 @@ __global__ void __launch_bounds__(NW * 32) attention_split_kernel(__grid_constan
     ss += __shfl_xor_sync(0xffffffffu, ss, 4);
     if (valid && ((is_q && p.q_norm) || (is_k && p.k_norm))) {
       const float* w = is_q ? wq : wk;
-      const float inv = 1.f / sqrtf(ss / float(D) + p.eps);
+      const float inv = rsqrtf(ss / float(D) + p.eps);
 #pragma unroll
       for (int e = 0; e < EPQ; ++e) v[e] = v[e] * inv * w[sub * EPQ + e];
     }
@@ -390,7 +390,7 @@ __global__ void __launch_bounds__(NW * 32) attention_split_kernel(__grid_constan
                 if (vis && p.window > 0) vis = pos >= n + l - p.window + 1;
               }
             }
-            const float sv = vis ? p.scale * s[mt][nt][2 * h + c] : -INFINITY;
+            const float sv = vis ? (p.scale * kLog2e) * s[mt][nt][2 * h + c] : -INFINITY;  // log2 units
             s[mt][nt][2 * h + c] = sv;
             mx = fmaxf(mx, sv);
           }
@@ -398,14 +398,14 @@ __global__ void __launch_bounds__(NW * 32) attention_split_kernel(__grid_constan
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
         const float mn = fmaxf(mrow[mt][h], mx);
         const float alpha = (mn == -INFINITY || mrow[mt][h] == -INFINITY) ? (mn == -INFINITY ? 1.f : 0.f)
-                                                                          : expf(mrow[mt][h] - mn);
+                                                                          : ex2_approx(mrow[mt][h] - mn);
         float sum = 0.f;
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
           for (int c = 0; c < 2; ++c) {
             const float sv = s[mt][nt][2 * h + c];
-            const float e = (sv == -INFINITY) ? 0.f : expf(sv - mn);
+            const float e = (sv == -INFINITY) ? 0.f : ex2_approx(sv - mn);
             s[mt][nt][2 * h + c] = e;
             sum += e;
           }
@@ -503,8 +503,8 @@ __global__ void __launch_bounds__(NW * 32) attention_split_kernel(__grid_constan
           const int r = mt * 16 + g + 8 * h;
           const float m2 = mw[warp * AS_MAXR + r], l2 = lw[warp * AS_MAXR + r];
           const float M = fmaxf(mrow[mt][h], m2);
-          const float a1 = mrow[mt][h] == -INFINITY ? 0.f : expf(mrow[mt][h] - M);
-          const float a2 = m2 == -INFINITY ? 0.f : expf(m2 - M);
+          const float a1 = mrow[mt][h] == -INFINITY ? 0.f : ex2_approx(mrow[mt][h] - M);
+          const float a2 = m2 == -INFINITY ? 0.f : ex2_approx(m2 - M);
           lrow[mt][h] = a1 * lrow[mt][h] + a2 * l2;
           mrow[mt][h] = M;
 #pragma unroll
@@ -555,7 +555,7 @@ __global__ void __launch_bounds__(NW * 32) attention_split_kernel(__grid_constan
     float lt = 0.f;
     for (int s2 = lane; s2 <= S; s2 += kWarp) {
       const float mv = sml[(s2 * AS_MAXR + r) * 2];
-      const float wv = mv == -INFINITY ? 0.f : expf(mv - M);
+      const float wv = mv == -INFINITY ? 0.f : ex2_approx(mv - M);
       cw[r * (AS_MAXS + 1) + s2] = wv;
       lt = fmaf(wv, sml[(s2 * AS_MAXR + r) * 2 + 1], lt);
     }
