@@ -771,13 +771,14 @@ __global__ void __launch_bounds__(TA_THREADS, 2) tree_attention_kernel(__grid_co
       }
       float lt[2] = {0.f, 0.f};
       uint32_t pa[TA_KT / 16][4];
+      // a row with no visible key so far keeps m = -inf: subtract 0 instead (2^-inf = 0)
+      const float mg[2] = {mrow[0] == -INFINITY ? 0.f : mrow[0], mrow[1] == -INFINITY ? 0.f : mrow[1]};
 #pragma unroll
       for (int j = 0; j < TA_KT / 8; ++j) {
         float e4[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          const float m = mrow[e >> 1];
-          e4[e] = (s[j][e] == -INFINITY) ? 0.f : ex2_approx(s[j][e] - m);
+          e4[e] = ex2_approx(s[j][e] - mg[e >> 1]);
           lt[e >> 1] += e4[e];
         }
         const int kk = j / 2, hi = j & 1;
@@ -790,12 +791,14 @@ __global__ void __launch_bounds__(TA_THREADS, 2) tree_attention_kernel(__grid_co
         lt[h] += __shfl_xor_sync(0xffffffffu, lt[h], 2);
         lrow[h] = lrow[h] * alpha[h] + lt[h];
       }
+      if (__any_sync(0xffffffffu, alpha[0] != 1.f || alpha[1] != 1.f)) {  // a running maximum moved
 #pragma unroll
-      for (int dj = 0; dj < ND; ++dj) {
-        o[dj][0] *= alpha[0];
-        o[dj][1] *= alpha[0];
-        o[dj][2] *= alpha[1];
-        o[dj][3] *= alpha[1];
+        for (int dj = 0; dj < ND; ++dj) {
+          o[dj][0] *= alpha[0];
+          o[dj][1] *= alpha[0];
+          o[dj][2] *= alpha[1];
+          o[dj][3] *= alpha[1];
+        }
       }
       // ---- O += P V: 4 k-steps of 16 keys, 16 n-tiles of 8 dims
 #pragma unroll
