@@ -873,6 +873,8 @@ def bench_c5(a):
     nreq, ctx0, nodes = a.c5_requests, 4096, sum(C5_LEVELS)
     t0 = time.time()
     dev = f"cuda:{local}"
+    if ts.layers < 3:
+        raise SystemExit("--c5-layers: at least 3 (the three tap layers must be distinct)")
     taps = [2, 14, 26] if ts.layers == 28 else [0, ts.layers // 2, ts.layers - 1]
     t = Target.from_weights(ts.hf_config(), syn.device_weight_stream(syn.target_tensor_specs(ts), 0, dev),
                             feature_layers=taps, dtype="bf16", device=local)

@@ -450,9 +450,37 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
       const int b = i & 1;
       const int t = int(blockIdx.x) + i * int(gridDim.x);
       const int m0 = (t % mt) * TC_BM, n0 = (t / mt) * BN;
+      const int row = m0 + qd * 32 + lane;
+      const uint32_t tl = tmem + uint32_t(b * BN) + (uint32_t(qd * 32) << 16);
+      // residual epilogue on 128-wide tiles: this row's residual is loaded while the MMAs run
+      // (one round trip instead of one per 16 columns); the branch is warp-uniform because the
+      // TMEM loads below are warp-collective
+      const bool pre = BN == 128 && p.epi == TC_ADD && n0 + BN <= p.N;
+      float4 rres[BN == 128 ? BN / 4 : 1];
+      if (pre && row < p.M) {
+        const float4* rs = reinterpret_cast<const float4*>(p.r + size_t(row) * p.ldr + n0);
+#pragma unroll
+        for (int q = 0; q < (BN == 128 ? BN / 4 : 1); ++q) rres[q] = rs[q];
+      }
       if (!mbar_wait(acc_full + b, (i / 2) & 1)) raise_error(p.err, kErrTimeout);
       tc_fence_after();
-      tc_epilogue_tile<BN>(p, tmem + uint32_t(b * BN) + (uint32_t(qd * 32) << 16), m0 + qd * 32 + lane, n0);
+      if (pre) {
+#pragma unroll
+        for (int c0 = 0; c0 < (BN == 128 ? BN : 0); c0 += 16) {
+          float v[16];
+          tmem_ld16(tl + c0, v);
+          if (row < p.M) {
+            float* dst = p.c + size_t(row) * p.ldc + n0 + c0;
+#pragma unroll
+            for (int k = 0; k < 16; k += 4) {
+              const float4 a = rres[(c0 + k) / 4];
+              *reinterpret_cast<float4*>(dst + k) = make_float4(v[k] + a.x, v[k + 1] + a.y, v[k + 2] + a.z, v[k + 3] + a.w);
+            }
+          }
+        }
+      } else {
+        tc_epilogue_tile<BN>(p, tl, row, n0);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(acc_empty + b);
