@@ -78,6 +78,16 @@ struct AttnParams {
   int* err;
 };
 
+// Shared-memory RoPE table of the new rows, [row][D/2] (cos, sin) pairs stored in groups of 16
+// pairs padded to 18: the norm loop's lanes read 16 consecutive pairs of one group per row, and
+// with unpadded power-of-two strides every group and row fell into the same banks.
+template <int D>
+struct RopeSmem {
+  static constexpr int kGroups = D / 32;       // 16-pair groups per row
+  static constexpr int kRow = kGroups * 18;    // pairs per padded row
+  __device__ __forceinline__ static int at(int l, int pair) { return l * kRow + (pair >> 4) * 18 + (pair & 15); }
+};
+
 __device__ __forceinline__ void attn_emit(const AttnParams& p, int l, int col, float v) {
   if (p.out) p.out[size_t(l) * p.ld_out + col] = v;
   if (p.xf_out) {

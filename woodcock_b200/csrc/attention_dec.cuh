@@ -49,7 +49,7 @@ struct AdLayout {
   static constexpr size_t pacc_bytes = size_t(AD_MAXR) * D * 4;
   static constexpr size_t region_b = raw_bytes > pacc_bytes ? raw_bytes : pacc_bytes;
   static constexpr size_t base_total = 2 * q_bytes + region_a + tail_bytes + region_b + 2 * D * 4 +
-                                       size_t(AD_MAXL) * (D / 2) * 8 + AD_MAXL * 4 + 2 * AD_WARPS * AD_MAXR * 4 +
+                                       size_t(AD_MAXL) * RopeSmem<D>::kRow * 8 + AD_MAXL * 4 + 2 * AD_WARPS * AD_MAXR * 4 +
                                        2 * AD_MAXR * 4 + 64;
   // one-m-tile merge: partial column slices pushed by every CTA of the cluster
   static constexpr size_t rx_off = (base_total + 15) / 16 * 16;
@@ -79,8 +79,8 @@ __global__ void __launch_bounds__(AD_THREADS, 1) attention_dec_kernel(__grid_con
   float* pacc = reinterpret_cast<float*>(reg_b);                           // [MAXR][D]
   float* wq = reinterpret_cast<float*>(reg_b + Lay::region_b);             // [D]
   float* wk = wq + D;                                                      // [D]
-  float2* rp = reinterpret_cast<float2*>(wk + D);                          // [MAXL][D/2]
-  int* spos = reinterpret_cast<int*>(rp + AD_MAXL * (D / 2));              // [MAXL]
+  float2* rp = reinterpret_cast<float2*>(wk + D);                          // [MAXL][padded D/2]
+  int* spos = reinterpret_cast<int*>(rp + AD_MAXL * RopeSmem<D>::kRow);   // [MAXL]
   float* mw = reinterpret_cast<float*>(spos + AD_MAXL);                    // [WARPS][MAXR]
   float* lw = mw + AD_WARPS * AD_MAXR;                                     // [WARPS][MAXR]
   float* pm = lw + AD_WARPS * AD_MAXR;                                     // [MAXR]
@@ -160,7 +160,7 @@ __global__ void __launch_bounds__(AD_THREADS, 1) attention_dec_kernel(__grid_con
 #pragma unroll
       for (int i = 0; i < ROPEV; ++i) {
         const int idx = tid + i * AD_THREADS;
-        if (idx < Lm * (D / 2)) rp[idx] = rr[i];
+        if (idx < Lm * (D / 2)) rp[RopeSmem<D>::at(idx / (D / 2), idx % (D / 2))] = rr[i];
       }
       rope_ready = true;
     }
@@ -262,7 +262,7 @@ __global__ void __launch_bounds__(AD_THREADS, 1) attention_dec_kernel(__grid_con
 #pragma unroll
     for (int i = 0; i < ROPEV; ++i) {
       const int idx = tid + i * AD_THREADS;
-      if (idx < L * (D / 2)) rp[idx] = rr[i];
+      if (idx < L * (D / 2)) rp[RopeSmem<D>::at(idx / (D / 2), idx % (D / 2))] = rr[i];
     }
   }
   // zero the padding query rows (they only feed output rows that are never stored)
@@ -319,7 +319,7 @@ __global__ void __launch_bounds__(AD_THREADS, 1) attention_dec_kernel(__grid_con
       const float partner = __shfl_xor_sync(0xffffffffu, v[e], 4);
       const int d = sub * EPQ + e;
       if (rot) {
-        const float2 cs = rp[l * (D / 2) + d % (D / 2)];
+        const float2 cs = rp[RopeSmem<D>::at(l, d % (D / 2))];
         v[e] = (d < D / 2) ? (v[e] * cs.x - partner * cs.y) : (v[e] * cs.x + partner * cs.y);
       }
     }

@@ -54,7 +54,7 @@ struct AsLayout {
   static constexpr size_t cw_bytes = size_t(AS_MAXR) * (AS_MAXS + 1) * 4;        // merge weights
   static constexpr size_t region_q = 2 * q_bytes > cw_bytes ? 2 * q_bytes : cw_bytes;
   static constexpr size_t rope_off = region_a + region_q;                        // [MAXL][D/2] float2
-  static constexpr size_t w_off = rope_off + size_t(AS_MAXL) * (D / 2) * 8;      // q_norm, k_norm
+  static constexpr size_t w_off = rope_off + size_t(AS_MAXL) * RopeSmem<D>::kRow * 8;      // q_norm, k_norm
   static constexpr size_t ml_off = w_off + 2 * D * 4;                            // [NW/2][MAXR] m, l
   static constexpr size_t pos_off = ml_off + size_t(NW) * AS_MAXR * 4;           // [MAXL] ints
   static constexpr size_t mlall_off = pos_off + AS_MAXL * 4;                     // [MAXS + 1][MAXR][2]
@@ -145,7 +145,7 @@ __global__ void __launch_bounds__(NW * 32) attention_split_kernel(__grid_constan
 #pragma unroll
     for (int i = 0; i < ROPEV; ++i) {
       const int idx = tid + i * AS_THREADS;
-      if (idx < Lm * (D / 2)) rp[idx] = rr[i];
+      if (idx < Lm * (D / 2)) rp[RopeSmem<D>::at(idx / (D / 2), idx % (D / 2))] = rr[i];
     }
   };
 
@@ -297,7 +297,7 @@ __global__ void __launch_bounds__(NW * 32) attention_split_kernel(__grid_constan
       const float partner = __shfl_xor_sync(0xffffffffu, v[e], 4);
       const int d = sub * EPQ + e;
       if (rot) {
-        const float2 cs = rp[l * (D / 2) + d % (D / 2)];
+        const float2 cs = rp[RopeSmem<D>::at(l, d % (D / 2))];
         v[e] = (d < D / 2) ? (v[e] * cs.x - partner * cs.y) : (v[e] * cs.x + partner * cs.y);
       }
     }
