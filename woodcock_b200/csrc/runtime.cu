@@ -118,10 +118,9 @@ struct wc_ctx {
   int gemv_blocks_per_sm = 1;
   bool gemv_wide = true;                 // 80 KB activation chunks for K up to 2560 (WC_GEMV_WIDE=0: split K)
   bool gemv_acs = true;                  // whole-K blocks with streamed activation pieces (WC_GEMV_ACS=0: split K)
-  int gemv_prefetch = 0;                 // L2 prefetch of the next GEMV's weights (WC_GEMV_PREFETCH=1;
+  bool gemv_prefetch = false;            // L2 prefetch of the next GEMV's weights (WC_GEMV_PREFETCH=1;
                                          // measured 1.6% slower on the C3 round: it competes with the
-                                         // dependent loads of the kernels in between); 2: only the
-                                         // QKV projection's prefetch of O and gate/up (1.4% slower)
+                                         // dependent loads of the kernels in between)
   size_t gemv_prefetch_cap = 64u << 20;  // bytes prefetched at most
   float* gv_partial = nullptr;           // split-K partial sums
   size_t gv_partial_n = 0;               // floats
@@ -558,9 +557,8 @@ int gemv_parts(const wc_ctx* ctx, const Lin& W, int L_max) {
 int side_parts(const wc_ctx* ctx, const Lin& W, int L_max) { return std::min(GV_SIDE_BLOCKS, gemv_grid(ctx, W, L_max)); }
 
 // Bytes of `next` to prefetch into L2 while the current GEMV ends (0 = off).
-void gemv_prefetch(const wc_ctx* ctx, GemvParams& p, const Lin* next, const Lin* next2 = nullptr,
-                   bool over_attention = false) {
-  if (!ctx->gemv_prefetch || (ctx->gemv_prefetch == 2 && !over_attention)) return;
+void gemv_prefetch(const wc_ctx* ctx, GemvParams& p, const Lin* next, const Lin* next2 = nullptr) {
+  if (!ctx->gemv_prefetch) return;
   if (next && next->dtype == WC_BF16) {
     p.pf = next->w;
     p.pf_bytes = std::min(next->bytes, ctx->gemv_prefetch_cap);
@@ -774,7 +772,7 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
     if (const char* e = std::getenv("WC_GEMV_BLOCKS_PER_SM")) ctx->gemv_blocks_per_sm = std::max(1, std::atoi(e));
     if (const char* e = std::getenv("WC_ATTN")) ctx->attn_mode = std::atoi(e);
     if (const char* e = std::getenv("WC_ATTN_SPLIT_POS")) ctx->attn_split_pos = std::max(16, std::atoi(e));
-    if (const char* e = std::getenv("WC_GEMV_PREFETCH")) ctx->gemv_prefetch = std::max(0, std::atoi(e));
+    if (const char* e = std::getenv("WC_GEMV_PREFETCH")) ctx->gemv_prefetch = std::atoi(e) != 0;
     if (const char* e = std::getenv("WC_GEMV_ACS")) ctx->gemv_acs = std::atoi(e) != 0;
     if (const char* e = std::getenv("WC_GEMV_WIDE")) ctx->gemv_wide = std::atoi(e) != 0;
     if (const char* e = std::getenv("WC_GEMV_PREFETCH_MB")) ctx->gemv_prefetch_cap = size_t(std::max(0, std::atoi(e))) << 20;
@@ -801,13 +799,6 @@ extern "C" wc_status wc_ctx_create(int device, void* stream, wc_ctx** out) {
     CUDA_TRY(cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(attention_mma_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(attention_mma_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
-    if (std::getenv("WC_ATTN_CARVEOUT")) {  // A/B switch: the shared-memory carveout of the decode kernels
-      const int cv = std::atoi(std::getenv("WC_ATTN_CARVEOUT"));
-      CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<128, 1, 16>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                    cv));
-      CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<128, 2, 8>, cudaFuncAttributePreferredSharedMemoryCarveout,
-                                    cv));
-    }
     CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<128, 1, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<128, 2, 8>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
     CUDA_TRY(cudaFuncSetAttribute(attention_split_kernel<64, 1, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smax));
@@ -1562,7 +1553,7 @@ XIn target_layers(wc_target* t, wc_kv* kv, const Rows& r, XIn in0, float* h, con
       p.y = t->ws_qkv;
       p.ldy = ld_qkv;
       p.err = err;
-      gemv_prefetch(ctx, p, &Ly.o, &Ly.gu, true);  // both land while attention runs
+      gemv_prefetch(ctx, p, &Ly.o, &Ly.gu);  // both land while attention runs
       prof_begin(ctx, PK_QKV);
       launch_gemv(ctx, Ly.qkv, p);
       prof_end(ctx, PK_QKV);
@@ -2065,7 +2056,7 @@ XIn drafter_layers(wc_drafter* d, wc_kv* kv, const Rows& r, XIn feat_in, const f
       p.y = d->ws_qkv;
       p.ldy = ld_qkv;
       p.err = err;
-      gemv_prefetch(ctx, p, &Ly.o, &Ly.gu, true);  // both land while attention runs
+      gemv_prefetch(ctx, p, &Ly.o, &Ly.gu);  // both land while attention runs
       launch_gemv(ctx, table ? Ly.qkv_main : Ly.qkv, p);
     }
     {
