@@ -77,8 +77,11 @@ __host__ __device__ constexpr int gv_chunk_slabs(int NT) { return GV_ACT_BYTES /
 constexpr int GV_WIDE_ACT_BYTES = 80 * 1024;
 constexpr int GV_WIDE_SLABS = GV_WIDE_ACT_BYTES / GV_STAGE_BYTES;
 // The wide instance at 16 rows: a 4-slab chunk (K up to 2048 for both n-tiles) in 128 KB beside a
-// 3-stage weight ring, so the 9-16-row verifies (chains of 8 and more, draft trees) do not split
-// the hidden-width projections and split the 6144-wide ones in 3 instead of 6.
+// 4-stage weight ring, so the 9-16-row verifies (chains of 8 and more, draft trees) do not split
+// the hidden-width projections and split the 6144-wide ones in 3 instead of 6. It keeps one
+// reduction buffer instead of two to make room for the 4th stage: a unit's partial sums are
+// written only after all of its slabs, so the epilogue drains the buffer while the MMA warps
+// run the next unit, and the ring depth bounds the weight stream (bytes in flight per SM).
 constexpr int GV_WIDE2_ACT_BYTES = 128 * 1024;
 constexpr int GV_WIDE2_SLABS = GV_WIDE2_ACT_BYTES / (2 * GV_STAGE_BYTES);
 
@@ -439,16 +442,18 @@ __device__ void gemv_prologue_fast(const GemvParams& p, int L, int* s_tok, float
 // Shared-memory carve-up of the bf16 kernel (byte offsets, every region 16-byte aligned).
 template <int NT, bool WIDE = false>
 struct GvLayout {
-  static constexpr int NS = WIDE ? (NT == 1 ? gv_nstage(NT) - 1 : 3) : gv_nstage(NT);
+  static constexpr int NS = WIDE ? (NT == 1 ? gv_nstage(NT) - 1 : 4) : gv_nstage(NT);
+  static constexpr int NRB = WIDE && NT == 2 ? 1 : 2;  // reduction buffers
   static constexpr int ACT_BYTES = WIDE ? (NT == 1 ? GV_WIDE_ACT_BYTES : GV_WIDE2_ACT_BYTES) : GV_ACT_BYTES;
   static constexpr int CHS = ACT_BYTES / (GV_STAGE_BYTES * NT);            // slabs per activation chunk
   static constexpr size_t ring = 0;                                        // NS x 16 KB weight slabs
   static constexpr size_t act = ring + size_t(NS) * GV_STAGE_BYTES;        // [NT][CHS][32 kt][32 lanes] uint4
   static constexpr size_t bars = act + ACT_BYTES;  // full[NS] empty[NS] act red_full[2] red_empty[2] ss act_full[4] act_empty[4]
   static constexpr size_t nbars = 2 * NS + 6 + 2 * GV_ACS_DEPTH;
-  static constexpr size_t red = bars + (nbars * 8 + 15) / 16 * 16;         // [2 buffers][2 row blocks][NT][W][32][4] floats
+  static constexpr size_t red = bars + (nbars * 8 + 15) / 16 * 16;         // [NRB buffers][2 row blocks][NT][W][32][4] floats
   static constexpr size_t red_buf = size_t(2) * NT * GV_CWARPS * kWarp * 4;  // floats per buffer
-  static constexpr size_t inv = red + 2 * red_buf * 4;                     // [3][16] floats
+  static constexpr size_t red_bytes = NRB * red_buf * 4;
+  static constexpr size_t inv = red + red_bytes;                           // [3][16] floats
   static constexpr size_t part = inv + GEMV_MAXSEG * 16 * 4;               // [3][256] floats
   static constexpr size_t sq = part + GEMV_MAXSEG * 256 * 4;               // [2][16 features][16 rows] floats
   static constexpr size_t tok = sq + 2 * 256 * 4;                          // [16] ints
@@ -460,8 +465,8 @@ struct GvLayout {
 };
 
 // Warp roles: 0-7 MMA (named barrier 1), 8 the bulk-copy producer, 9-12 epilogue (named
-// barrier 2). The MMA warps hand each unit's per-warp sums to the epilogue warps through two
-// shared-memory buffers (mbarriers red_full / red_empty) and go straight on to the next
+// barrier 2). The MMA warps hand each unit's per-warp sums to the epilogue warps through
+// shared-memory buffers (NRB of them; mbarriers red_full / red_empty) and go straight on to the next
 // unit's slabs, so the cross-warp reduction, the epilogue's global traffic and the split-K
 // hand-off overlap the weight stream instead of stalling it.
 template <int NT, bool ACS = false, bool WIDE = false>
@@ -541,7 +546,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
       // statistics of the normalised segments, into the reduction buffers (unused until the
       // first unit is handed over), ahead of the larger activation copy
       int stg[GEMV_MAXSEG];
-      gemv_ss_plan(p, 2 * Lay::red_buf * 4, stg);
+      gemv_ss_plan(p, Lay::red_bytes, stg);
       uint32_t ss_bytes = 0;
 #pragma unroll
       for (int s = 0; s < GEMV_MAXSEG; ++s)
@@ -679,11 +684,12 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
         live[k] = p.nkc == 1 && l_[k] < L && u * 16 + r16_[k] < p.N;
         if (live[k]) ein[k] = gemv_epi_load(p, u * 16 + r16_[k], l_[k], s_btok);
       }
-      if (ok && !mbar_wait(red_full + b, (j >> 1) & 1)) {
+      const int rbi = j % Lay::NRB;
+      if (ok && !mbar_wait(red_full + rbi, (j / Lay::NRB) & 1)) {
         raise_error(p.err, kErrTimeout);
         ok = false;
       }
-      const float* rb = red + b * Lay::red_buf;
+      const float* rb = red + rbi * Lay::red_buf;
       float* sq = s_sq + b * 256;
       float v[NT][2];
 #pragma unroll
@@ -696,7 +702,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
             for (int w = 0; w < GV_CWARPS; ++w)
               v[k][r] += rb[(((r * NT + nt_[k]) * GV_CWARPS + w) * kWarp + ln_[k]) * 4 + e_[k]];
       }
-      mbar_arrive(red_empty + b);  // this thread's reads of the buffer are done
+      mbar_arrive(red_empty + rbi);  // this thread's reads of the buffer are done
 #pragma unroll
       for (int k = 0; k < NT; ++k) {
         if (p.nkc > 1) {  // this chunk's share, reduced below by the last block of the range
@@ -838,7 +844,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
   const int L = gemv_rows(p.L_dev, p.L, p.L_max, p.err);
   {
     int stg[GEMV_MAXSEG];
-    gemv_ss_plan(p, 2 * Lay::red_buf * 4, stg);
+    gemv_ss_plan(p, Lay::red_bytes, stg);
     gemv_prologue_fast(p, L, s_tok, s_inv, s_part, reinterpret_cast<const unsigned char*>(red), stg, ss_bar);
   }
   if (p.flags & GV_F_TABLE) {  // embedding segments of this chunk: built from the table straight into the buffer
@@ -942,12 +948,12 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
       }
     }
     // ---- hand the unit's per-warp sums to the epilogue warps
-    const int b = j & 1;
-    if (j >= 2 && ok && !mbar_wait(red_empty + b, ((j >> 1) - 1) & 1)) {
+    const int rbi = j % Lay::NRB;
+    if (j >= Lay::NRB && ok && !mbar_wait(red_empty + rbi, ((j / Lay::NRB) - 1) & 1)) {
       raise_error(p.err, kErrTimeout);
       ok = false;
     }
-    float* rb = red + b * Lay::red_buf;
+    float* rb = red + rbi * Lay::red_buf;
 #pragma unroll
     for (int r = 0; r < 2; ++r)
 #pragma unroll
@@ -955,7 +961,7 @@ __global__ void __launch_bounds__(GV_THREADS, 1) gemv_bf16_kernel(__grid_constan
         if (r < G)
           *reinterpret_cast<float4*>(&rb[(((r * NT + nt) * GV_CWARPS + warp) * kWarp + lane) * 4]) =
               make_float4(tot[r][nt][0], tot[r][nt][1], tot[r][nt][2], tot[r][nt][3]);
-    mbar_arrive(red_full + b);
+    mbar_arrive(red_full + rbi);
   }
   if (p.side_src && int(blockIdx.x) < p.side_blocks) gemv_side_job(p, L, s_inv, s_part, GV_CTHREADS, true);
 }
