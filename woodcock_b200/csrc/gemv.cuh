@@ -25,7 +25,7 @@
 //
 // Four instances: the default (64 KB activation chunk, up to 2048 columns at 8 rows); the
 // wide one (80 KB chunk, 7-stage ring: K up to 2560 without splitting) and its 16-row form
-// (128 KB chunk, 3-stage ring: K up to 2048 at 9-16 rows); and the streamed
+// (128 KB chunk, 4-stage ring, one reduction buffer: K up to 2048 at 9-16 rows); and the streamed
 // one (ACS: whole K in one block for projections with at most one unit per SM, the
 // activation streamed in 16 KB pieces through a 4-deep ring beside the weight slab each
 // piece multiplies). Otherwise, when K exceeds the chunk, K is split: the blocks of one row
