@@ -61,6 +61,8 @@ template <int D>
 constexpr size_t attention_dec_smem() {
   return AdLayout<D>::total;
 }
+static_assert(attention_dec_smem<128>() <= kSmemOptinBytes && attention_dec_smem<64>() <= kSmemOptinBytes,
+              "the decode attention layout exceeds the per-block shared memory");
 
 template <int D, int MT>
 __global__ void __launch_bounds__(AD_THREADS, 1) attention_dec_kernel(__grid_constant__ const AttnParams p) {

@@ -8,6 +8,9 @@
 namespace wc {
 
 constexpr int kWarp = 32;
+// Dynamic shared memory one block may opt into on sm_100 (227 KB); the kernels' layouts are
+// checked against it at compile time.
+constexpr size_t kSmemOptinBytes = 232448;
 
 // Device error word bits (raised with atomicOr, read by the host at the round's sync).
 enum DeviceError : int {

@@ -970,6 +970,9 @@ template <int NT, bool WIDE = false>
 constexpr size_t gemv_bf16_smem() {
   return GvLayout<NT, WIDE>::total + 128;
 }
+static_assert(gemv_bf16_smem<1>() <= kSmemOptinBytes && gemv_bf16_smem<2>() <= kSmemOptinBytes &&
+                  gemv_bf16_smem<1, true>() <= kSmemOptinBytes && gemv_bf16_smem<2, true>() <= kSmemOptinBytes,
+              "a GEMV layout exceeds the per-block shared memory");
 
 // ----------------------------------------------------------------------------- fp32 models
 // Inputs are staged in shared memory with their 1/rms applied, then one warp per output
