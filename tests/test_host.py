@@ -1,5 +1,6 @@
 """Host-side logic without a GPU: policies (restating tests/test_policies.py), draft trees and
-masks, safetensors I/O, and the seeded synthetic configs."""
+masks, the host-driven sampled tree's draws, safetensors I/O, and the seeded synthetic
+configs."""
 
 from __future__ import annotations
 
@@ -80,6 +81,31 @@ def test_draft_tree_and_mask_known_answer():
     assert list(m[3, 2:]) == [True, False, True, True]
     assert list(m[1, 2:]) == [True, True, False, False]
     assert SamplingParams().greedy and not SamplingParams(temperature=0.7).greedy
+
+
+def test_synced_tree_draws_match_the_reference_rules(golden):
+    """The host-driven sampled tree's two draws read the Philox stream exactly as the reference
+    reads its Generator: a node's children by Gumbel-top-k (synced.gumbel_top_k) against the
+    reference's own sample_without_replacement outputs (python/woodcock/sampling.py:196-203,
+    fixture made from it), and the inverse-CDF draw (synced.inverse_cdf_draw) against the
+    reference's _sample rule (sampling.py:190-193, as the oracle restates it)."""
+    import wc_oracle as O
+    from woodcock_b200.synced import gumbel_top_k, inverse_cdf_draw
+
+    cases = golden("sampling")["gumbel"]
+    assert cases
+    for c in cases:
+        tape = O.Tape(c["seed"])
+        assert gumbel_top_k(np.array(c["q"]), c["k"], tape) == c["out"]
+        assert tape.pos == c["uniforms_used"]
+    rng = np.random.default_rng(3)
+    for trial in range(64):
+        p = rng.random(40) * (rng.random(40) < 0.6)
+        p[trial % 40] += 0.01  # at least one positive entry
+        a, b = O.Tape(trial, 5), O.Tape(trial, 5)
+        assert inverse_cdf_draw(p, a) == O.sample(p, b)
+        assert a.pos == b.pos == 6
+    assert gumbel_top_k(np.zeros(8), 3, O.Tape(0)) == []  # nothing to draw from
 
 
 def test_safetensors_roundtrip_and_bf16_rounding(tmp_path):
